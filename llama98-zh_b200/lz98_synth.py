@@ -1,0 +1,303 @@
+"""Synthetic KunMoe model writer: random-init weights in the "L98Z" model.bin
+format that the reference engine's loader reads.
+
+The reference ships no exporter (its tools/export_q8.py is cited but absent),
+so this module writes the file from the loader's side of the contract:
+
+* header words in the exact order ``lz_open_bin`` reads them
+  (src/model.c:3993-4340: 28 fixed words, layer_types[128], the 13-word
+  KDA/MoE tail, then the v5 tail up to csa2_compress_m_layer[128]);
+* tensors in ``model_walk`` order (src/model.c:2240-2630): embed_tokens,
+  final norm, then per layer the LAYER_SPECS rows that apply to a KDA +
+  latent-MoE layer (src/model.c:1496-1665), then every expert's w1/w2/w3,
+  then the MTP block (attention rows of LAYER_SPECS, its dense FFN, then
+  fc/norm/pre_fc_norm_hidden/pre_fc_norm_embedding);
+* each tensor as ``{dtype u8, n u32, [gs u32], data, [f32 scales]}``
+  (src/model.c:3567-3804, scale_layout 0).
+
+Weights are N(0, 0.02), rounded to bf16, then quantised to Q8_0 with the
+activation quantiser's rule (scale = amax * (1/127), q = rne(x * 127/amax)
+clamped to +-127; src/ops_quant.c:1633-1666 and 2152-2282).  1-D and 3-D
+tensors are written as F32 holding bf16-rounded values.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import json
+import os
+import struct
+
+import numpy as np
+
+LZ_MAX_LAYERS = 128
+LT_KDA = 2
+FMT_F32 = 0
+FMT_Q8_0 = 1
+
+
+@dataclasses.dataclass(frozen=True)
+class KunMoeConfig:
+    """Architecture of one synthetic KunMoe model (all layers KDA + latent MoE,
+    one MTP block with gated full attention and a dense SwiGLU FFN)."""
+    name: str
+    hidden: int
+    n_layers: int
+    kda_heads: int
+    vocab: int
+    n_experts: int
+    top_k: int
+    latent: int
+    moe_ffn: int
+    shared_width: int
+    seq_len: int
+    gs_mode: str = "row"          # "row": one scale per weight row; "32": Q8_0 gs=32
+    head_dim: int = 64
+    kda_head_dim: int = 64
+    conv_kernel: int = 4
+    gate_rank: int = 64
+    gate_lower_bound: float = -5.0
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000000.0
+    partial_rotary: float = 0.25
+    seed: int = 0
+
+    @property
+    def n_heads(self) -> int:
+        return self.hidden // self.head_dim
+
+    @property
+    def n_kv_heads(self) -> int:
+        return max(1, self.n_heads // 4)
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary)
+
+    @property
+    def key_dim(self) -> int:
+        return self.kda_heads * self.kda_head_dim
+
+    @property
+    def mtp_ffn(self) -> int:
+        return self.moe_ffn
+
+    def gs(self, in_dim: int) -> int:
+        return in_dim if self.gs_mode == "row" else 32
+
+    def to_json(self) -> dict:
+        d = dataclasses.asdict(self)
+        d["n_heads"] = self.n_heads
+        d["n_kv_heads"] = self.n_kv_heads
+        d["rotary_dim"] = self.rotary_dim
+        return d
+
+
+# The BASELINE configurations this path is measured on (weights seed = config
+# index).  "tiny" is the reference's CPU-runnable case; "0p5b" is the ~0.5B
+# model of the batch-1 and batch-32 workloads.
+CONFIGS = {
+    "tiny": KunMoeConfig(name="tiny", hidden=256, n_layers=4, kda_heads=4,
+                         vocab=8192, n_experts=8, top_k=2, latent=128,
+                         moe_ffn=512, shared_width=0, seq_len=512,
+                         gs_mode="32", seed=0),
+    "0p5b": KunMoeConfig(name="0p5b", hidden=1024, n_layers=24, kda_heads=16,
+                         vocab=64000, n_experts=64, top_k=4, latent=512,
+                         moe_ffn=1024, shared_width=1024, seq_len=2048,
+                         gs_mode="row", seed=1),
+    # Small shapes of the 0p5b family for fast parity tests.
+    "mini": KunMoeConfig(name="mini", hidden=128, n_layers=2, kda_heads=2,
+                         vocab=1024, n_experts=8, top_k=4, latent=64,
+                         moe_ffn=128, shared_width=128, seq_len=256,
+                         gs_mode="row", seed=7),
+}
+
+
+def _bf16_round(x: np.ndarray) -> np.ndarray:
+    u = x.astype(np.float32).view(np.uint32)
+    u = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return u.view(np.float32)
+
+
+def quantize_q8_rows(w: np.ndarray, gs: int):
+    """Q8_0 with the engine's absmax/127 rule; returns (int8 data, f32 scales)."""
+    flat = w.astype(np.float32).reshape(-1, gs)
+    amax = np.abs(flat).max(axis=1)
+    inv127 = np.float32(1.0) / np.float32(127.0)
+    scale = (amax * inv127).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(amax > 0, np.float32(127.0) / amax, np.float32(0.0)).astype(np.float32)
+    small = scale < np.float32(1e-30)
+    scale = np.where(small | (amax <= 0), np.float32(1.0), scale).astype(np.float32)
+    inv = np.where(small, np.float32(0.0), inv).astype(np.float32)
+    q = np.rint(flat * inv[:, None]).clip(-127, 127).astype(np.int8)
+    return q.reshape(-1), scale
+
+
+class _Writer:
+    def __init__(self, f, cfg: KunMoeConfig):
+        self.f = f
+        self.cfg = cfg
+        self.idx = 0
+        self.digest = hashlib.sha256()
+
+    def _rng(self):
+        self.idx += 1
+        return np.random.default_rng([self.cfg.seed, self.idx])
+
+    def _put(self, b: bytes):
+        self.f.write(b)
+        self.digest.update(b)
+
+    def normal(self, shape, std=0.02, offset=0.0):
+        x = self._rng().standard_normal(int(np.prod(shape)), dtype=np.float32)
+        x = x * np.float32(std)
+        if offset:
+            x = x + np.float32(offset)
+        return _bf16_round(x)
+
+    def f32(self, arr: np.ndarray):
+        arr = np.ascontiguousarray(arr, dtype=np.float32).reshape(-1)
+        self._put(struct.pack("<BI", FMT_F32, arr.size))
+        self._put(arr.tobytes())
+
+    def q8(self, out_dim: int, in_dim: int):
+        gs = self.cfg.gs(in_dim)
+        w = self.normal((out_dim, in_dim))
+        q, s = quantize_q8_rows(w, gs)
+        self._put(struct.pack("<BII", FMT_Q8_0, q.size, gs))
+        self._put(q.tobytes())
+        self._put(s.astype("<f4").tobytes())
+
+
+def header_words(cfg: KunMoeConfig) -> bytes:
+    c = cfg
+    w = []
+    i32 = lambda v: w.append(struct.pack("<i", int(v)))
+    f32 = lambda v: w.append(struct.pack("<f", float(v)))
+    q_dim = c.n_heads * c.head_dim
+    kv_dim = c.n_kv_heads * c.head_dim
+    kdim = c.key_dim
+    # 28 fixed words (src/model.c:4022-4040)
+    i32(c.vocab); i32(c.hidden); i32(c.n_layers); i32(c.seq_len)
+    i32(c.n_heads); i32(c.n_kv_heads); i32(c.head_dim); i32(c.moe_ffn)
+    i32(c.kda_heads); i32(c.kda_heads); i32(c.kda_head_dim); i32(c.kda_head_dim)
+    i32(c.conv_kernel); i32(c.n_layers); i32(0); i32(0)
+    i32(1); i32(1)
+    f32(c.rms_eps); f32(c.rope_theta); f32(c.partial_rotary)
+    i32(q_dim); i32(2 * q_dim); i32(kv_dim)
+    i32(kdim); i32(kdim); i32(3 * kdim)
+    i32(c.rotary_dim)
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS,
+                         *([LT_KDA] * c.n_layers + [0] * (LZ_MAX_LAYERS - c.n_layers))))
+    # KDA / MoE tail (src/model.c:4082-4094)
+    i32(c.gate_rank); i32(1); f32(c.gate_lower_bound)
+    i32(c.n_experts); i32(c.top_k); i32(1 if c.shared_width else 0)
+    i32(c.moe_ffn); i32(c.latent); i32(0)
+    i32(1); i32(1); i32(0); i32(c.shared_width)
+    # v5 tail (src/model.c:4106-4301)
+    i32(1); i32(c.mtp_ffn)                      # mtp_n_layers, mtp_intermediate_size
+    i32(0); f32(1.0); f32(4096.0); f32(32.0); f32(1.0)   # rope scaling off
+    i32(0); i32(0); i32(0)                      # use_subn, hadamard_o, hadamard_down
+    i32(0); i32(0); i32(0)                      # mla q/o rank, attn_kv_share
+    i32(0); i32(0); i32(0); i32(0)              # sink, gated_residual, ced_split, ced_kv
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([0] * LZ_MAX_LAYERS)))      # csa2_on
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([0] * LZ_MAX_LAYERS)))      # csa2_mode
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([-1] * LZ_MAX_LAYERS)))     # csa2_source
+    i32(0); i32(4); i32(64); i32(1); i32(64); i32(64)  # replay_w, compress_m, topk, idx heads/dim/rank
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([0] * LZ_MAX_LAYERS)))      # csa2_compress_m_layer
+    return b"L98Z" + struct.pack("<I", 5) + b"".join(w)
+
+
+def write_model(cfg: KunMoeConfig, out_dir: str) -> str:
+    """Write ``out_dir/model.bin`` (and a config.json describing it); returns
+    the sha256 of the tensor stream.  Idempotent: an existing file whose
+    recorded config matches is kept."""
+    os.makedirs(out_dir, exist_ok=True)
+    meta_path = os.path.join(out_dir, "lz98_synth.json")
+    bin_path = os.path.join(out_dir, "model.bin")
+    want = cfg.to_json()
+    if os.path.exists(meta_path) and os.path.exists(bin_path):
+        try:
+            with open(meta_path) as f:
+                have = json.load(f)
+            if have.get("config") == want:
+                return have["sha256"]
+        except (OSError, ValueError, KeyError):
+            pass
+    c = cfg
+    kdim = c.key_dim
+    q_dim = c.n_heads * c.head_dim
+    kv_dim = c.n_kv_heads * c.head_dim
+    tmp = bin_path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(header_words(cfg))
+        w = _Writer(f, cfg)
+        w.q8(c.vocab, c.hidden)                       # embed_tokens (tied lm_head)
+        w.f32(w.normal((c.hidden,)))                  # final norm
+        for _ in range(c.n_layers):
+            w.f32(w.normal((c.hidden,)))              # input_layernorm
+            w.f32(w.normal((c.hidden,)))              # post_attention_layernorm
+            w.q8(kdim, c.hidden)                      # q_proj
+            w.q8(kdim, c.hidden)                      # k_proj
+            w.q8(kdim, c.hidden)                      # v_proj
+            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # q_conv1d
+            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # k_conv1d
+            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # v_conv1d
+            w.f32(w.normal((c.kda_heads,)))           # A_log
+            w.q8(c.gate_rank, c.hidden)               # f_a_proj
+            w.q8(kdim, c.gate_rank)                   # f_b_proj
+            w.f32(w.normal((kdim,)))                  # dt_bias
+            w.q8(c.kda_heads, c.hidden)               # b_proj
+            w.q8(kdim, c.hidden)                      # g_proj
+            w.f32(w.normal((c.kda_head_dim,), offset=1.0))   # o_norm (multiplies directly)
+            w.q8(c.hidden, kdim)                      # o_proj
+            w.q8(c.n_experts, c.hidden)               # router
+            w.f32(w.normal((c.n_experts,)))           # e_score_correction_bias
+            w.q8(c.latent, c.hidden)                  # routed_expert_down_proj
+            w.q8(c.hidden, c.latent)                  # routed_expert_up_proj
+            if c.shared_width:
+                w.q8(c.shared_width, c.hidden)        # shared gate
+                w.q8(c.shared_width, c.hidden)        # shared up
+                w.q8(c.hidden, c.shared_width)        # shared down
+            for _e in range(c.n_experts):
+                w.q8(c.moe_ffn, c.latent)             # w1
+                w.q8(c.latent, c.moe_ffn)             # w2
+                w.q8(c.moe_ffn, c.latent)             # w3
+        # MTP block: attention rows of LAYER_SPECS, dense FFN, then the head.
+        w.f32(w.normal((c.hidden,)))                  # input_layernorm
+        w.f32(w.normal((c.hidden,)))                  # post_attention_layernorm
+        w.q8(2 * q_dim, c.hidden)                     # q_proj (q | gate interleaved per head)
+        w.q8(kv_dim, c.hidden)                        # k_proj
+        w.q8(kv_dim, c.hidden)                        # v_proj
+        w.q8(c.hidden, q_dim)                         # o_proj
+        w.f32(w.normal((c.head_dim,)))                # q_norm
+        w.f32(w.normal((c.head_dim,)))                # k_norm
+        w.q8(c.mtp_ffn, c.hidden)                     # mlp.gate_proj
+        w.q8(c.mtp_ffn, c.hidden)                     # mlp.up_proj
+        w.q8(c.hidden, c.mtp_ffn)                     # mlp.down_proj
+        w.q8(c.hidden, 2 * c.hidden)                  # fc
+        w.f32(w.normal((c.hidden,)))                  # norm
+        w.f32(w.normal((c.hidden,)))                  # pre_fc_norm_hidden
+        w.f32(w.normal((c.hidden,)))                  # pre_fc_norm_embedding
+        sha = w.digest.hexdigest()
+    os.replace(tmp, bin_path)
+    with open(meta_path, "w") as f:
+        json.dump({"config": want, "sha256": sha}, f, indent=1)
+    return sha
+
+
+def workload_prompts(cfg: KunMoeConfig, n_seq: int, lo: int, hi: int,
+                     zipf: float | None, seed: int = 0):
+    """Seeded synthetic prompts: lengths U[lo, hi], ids uniform or Zipf(s)
+    over the vocabulary (per-sequence seed = 1000 + seq for Zipf)."""
+    prompts = []
+    for s in range(n_seq):
+        rng = np.random.default_rng([seed, 1000 + s])
+        n = int(rng.integers(lo, hi + 1)) if hi > lo else lo
+        if zipf is None:
+            ids = rng.integers(0, cfg.vocab, size=n)
+        else:
+            ids = (rng.zipf(zipf, size=n) - 1) % cfg.vocab
+        prompts.append([int(x) for x in ids])
+    return prompts
