@@ -1,0 +1,153 @@
+/* C ABI of the B200-native MTP speculative-decoding step for KunMoe.
+ *
+ * Drop-in boundary for the reference engine's exports on this path
+ * (llama98.def:6-66; prototypes in the reference's src/llama_zh.h and
+ * src/forward.h).  Plain pointers and sizes only.  Differences from the
+ * reference surface, all forced by the model and the run state living in
+ * GPU memory:
+ *   - LZModel / LZRunState are opaque handles (the reference's are
+ *     by-value structs the caller allocates); lz_open and lz_state_alloc
+ *     return them through an out pointer;
+ *   - the fields generate.c pokes directly (ssm_slot, mtp_pos, mtp_chain,
+ *     mtp_logits, mtp_verify_hidden) are reached through accessors;
+ *   - returned float* point into host mirrors owned by the state, valid
+ *     until the next call on that state (as in the reference).
+ * Error convention as in the reference: round functions return a negative
+ * LZErr and fill errbuf; forward functions return NULL or nonzero.
+ * One caller per state at a time (src/llama_zh.h:140-143). */
+#ifndef LZ98_GPU_H
+#define LZ98_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct LZModel LZModel;
+typedef struct LZRunState LZRunState;
+
+/* Sampler state of the temperature round: the subset of LZSampler
+   (src/sampler.h:145-187) that the acceptance path reads. */
+typedef struct {
+    float temperature;
+    float topp;
+    uint64_t rng_state;
+} LZSampler;
+
+/* LZErr codes used on this path (values of the reference's err.h). */
+enum {
+    LZ98_ERR_OK = 0,
+    LZ98_ERR_NULL_ARG = 1,
+    LZ98_ERR_FORWARD = 2,
+    LZ98_ERR_SPEC_NO_HEAD = 3,
+    LZ98_ERR_SPEC_K_RANGE = 4,
+    LZ98_ERR_CUDA = 5,
+    LZ98_ERR_ALLOC = 6,
+    LZ98_ERR_MODEL = 7
+};
+
+/* ---- model: replaces lz_open + lz_read_weights + lz_free
+   (src/model.h:1333-1339).  Reads DIR/model.bin ("L98Z" v5) and uploads
+   every tensor to device memory of the current CUDA device. */
+int  lz_open(LZModel **out, const char *dir, char *errbuf, int errlen);
+void lz_free(LZModel *m);
+/* vocab, hidden, n_layers, kda_heads, key_dim, latent, n_experts, top_k,
+   shared_width, head_dim, n_heads, n_kv_heads, rotary_dim, seq_len,
+   mtp_ffn, moe_ffn */
+void lz_model_info(const LZModel *m, int *out16);
+/* Bytes of weights resident in HBM. */
+size_t lz_model_weight_bytes(const LZModel *m);
+
+/* ---- run state: replaces lz_state_alloc / lz_state_reset /
+   lz_state_free (src/forward.h:1847-1933).  n_seq independent sequences
+   share one allocation (n_seq = 1 is the reference's LZRunState). */
+int  lz_state_alloc(LZRunState **out, const LZModel *m, int seq_len,
+                    int spec_k_max, char *errbuf, int errlen);
+int  lz_state_alloc_batch(LZRunState **out, const LZModel *m, int n_seq,
+                          int seq_len, int spec_k_max, char *errbuf, int errlen);
+void lz_state_reset(LZRunState *s, const LZModel *m);
+void lz_state_free(LZRunState *s);
+/* Host mirrors of LZRunState fields for sequence `seq`. */
+int  lz_state_get(const LZRunState *s, int seq, int *mtp_pos, int *ssm_slot,
+                  int *ring_depth);
+int  lz_state_set(LZRunState *s, int seq, int mtp_pos, int ssm_slot);
+int  lz_state_get_chain(const LZRunState *s, int seq, float *chain);
+int  lz_state_set_chain(LZRunState *s, int seq, const float *chain);
+
+/* ---- forwards of sequence 0 (src/forward.c:1619-1837). */
+float *lz_forward(const LZModel *m, LZRunState *s, int token, int pos);
+float *lz_forward_capture(const LZModel *m, LZRunState *s, int token, int pos);
+float *lz_forward_batch_capture(const LZModel *m, LZRunState *s,
+                                const int *tokens, int n, int pos0,
+                                float *hidden_out);
+/* Verify forward: logits of every row into the state's mtp_logits mirror,
+   captured hidden rows into mtp_verify_hidden. */
+int    lz_forward_verify(const LZModel *m, LZRunState *s, const int *tokens,
+                         int n, int pos0);
+const float *lz_state_mtp_logits(const LZRunState *s);
+const float *lz_state_mtp_verify_hidden(const LZRunState *s);
+
+/* ---- MTP draft head of sequence 0 (src/forward_mtp.c:32-144,
+   561-642). */
+float *lz_mtp_draft_step(const LZModel *m, LZRunState *s, int next_token, int pos);
+int    lz_mtp_prefill(const LZModel *m, LZRunState *s, const float *h_body_all,
+                      const int *next_tokens, int n, int pos0);
+int    lz_mtp_catchup(const LZModel *m, LZRunState *s, const float *h_body_all,
+                      const int *next_tokens, int n, int pos0);
+
+/* ---- rounds of sequence 0 (src/llama_zh.h:470-593,
+   src/generate.c:694-994 and 1234-1377).  p_min and n_min must be 0 and
+   samp must be NULL or carry identity penalties (the only settings the
+   benchmark workloads use). */
+int lz_spec_round(const LZModel *m, LZRunState *s, int anchor, int anchor_pos,
+                  int k, float p_min, int n_min, const LZSampler *samp,
+                  int debug_break_rollback, int debug_skip_catchup,
+                  int *out, int *out_n_accept, int *out_new_pos, int *out_k_eff,
+                  char *errbuf, int errlen);
+int lz_spec_round_temp(const LZModel *m, LZRunState *s, int anchor, int anchor_pos,
+                       int k, float p_min, int n_min, LZSampler *samp,
+                       int debug_break_rollback, int debug_skip_catchup,
+                       int *out, int *out_n_accept, int *out_new_pos, int *out_k_eff,
+                       char *errbuf, int errlen);
+
+/* ---- model-free acceptance (src/generate.c:232-349). */
+int lz_spec_accept(const int *draft, const int *targ, int n_draft, int bonus, int *out);
+int lz_spec_accept_temp(const float *p, const float *q, int x, int vocab, float u,
+                        uint64_t *residual_rng, int *out_accepted);
+
+/* ---- batched extension (appended surface, no reference counterpart
+   beyond lz_spec_round itself): all n_seq sequences of the state advance
+   one greedy round together on the device. */
+/* Per-sequence prefill of sequence `seq`: capture-prefill of the prompt,
+   MTP prompt prefill, first anchor (greedy) from the forward of the last
+   prompt token.  Leaves the sequence ready for rounds; returns the anchor. */
+int lz_seq_prefill(const LZModel *m, LZRunState *s, int seq, const int *prompt,
+                   int n_prompt, int *out_anchor, char *errbuf, int errlen);
+/* One greedy round of every sequence with draft depth k (device resident:
+   draft k steps, one (k+1)-row verify per sequence, acceptance, ring
+   rollback, chain reseed, catch-up).  out_tokens (n_seq x (k+1)) and
+   out_counts (n_seq) may be NULL, which skips the device-to-host copy. */
+int lz_spec_round_batch(const LZModel *m, LZRunState *s, int k,
+                        int *out_tokens, int *out_counts, char *errbuf, int errlen);
+/* Capture the round of depth k into a CUDA graph (replayed by later
+   lz_spec_round_batch calls of the same k); 0 disables graphs. */
+int lz_set_graphs(LZRunState *s, int enable);
+/* Whole generation on token ids (the reference's lz_generate_call spec
+   loop, src/generate.c:2781-3091, without EOS/stop strings): greedy when
+   temp <= 1e-3, else the coupled temperature rounds with top-p `topp`. */
+int lz_generate(const LZModel *m, LZRunState *s, const int *prompt, int n_prompt,
+                int max_new, int spec_k, float temp, float topp, uint64_t seed,
+                int *out_tok, int out_cap, int *out_n, int *rounds, int round_cap,
+                int *n_rounds, char *errbuf, int errlen);
+
+/* Stream the library launches on (cudaStream_t, NULL = a private stream). */
+void *lz_state_stream(LZRunState *s);
+/* Kernels this library launched since the state was created. */
+long long lz_state_launches(const LZRunState *s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

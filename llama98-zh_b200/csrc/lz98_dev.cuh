@@ -1,0 +1,127 @@
+// Device numerics of the MTP speculative-decoding path, op for op the
+// reference engine's float tier (--fixed off, --fastfp off): IEEE binary32,
+// round-to-nearest, no fused multiply-add (this translation unit is built
+// with -fmad=false), no flush-to-zero, IEEE-rounded division.
+// Every helper names the reference file:line whose operation order it keeps.
+#pragma once
+#include <cstdint>
+#include <cfloat>
+
+#define LZ_HD __device__ __forceinline__
+
+namespace lz98 {
+
+constexpr float kLoScale = 256.0f;   // two-plane state, src/ops.h:1922
+constexpr float kL2Eps = 1e-6f;      // src/forward.h:23
+
+// src/ops_quant.c:126-135: magic seed, two Newton steps.
+LZ_HD float rsqrt_body(float x) {
+  float h = __fmul_rn(0.5f, x);
+  float y = __uint_as_float(0x5f375a86u - (__float_as_uint(x) >> 1));
+  y = __fmul_rn(y, __fsub_rn(1.5f, __fmul_rn(__fmul_rn(h, y), y)));
+  y = __fmul_rn(y, __fsub_rn(1.5f, __fmul_rn(__fmul_rn(h, y), y)));
+  return y;
+}
+
+// 2^(i/32), the reference's own table (src/ops_quant.c:244-253).
+__constant__ float kExpTab32[32] = {
+    1.000000000f, 1.021897149f, 1.044273782f, 1.067140401f,
+    1.090507733f, 1.114386743f, 1.138788635f, 1.163724859f,
+    1.189207115f, 1.215247360f, 1.241857812f, 1.269050957f,
+    1.296839555f, 1.325236643f, 1.354255547f, 1.383909882f,
+    1.414213562f, 1.445180807f, 1.476826146f, 1.509164428f,
+    1.542210825f, 1.575980845f, 1.610490332f, 1.645755478f,
+    1.681792831f, 1.718619298f, 1.756252160f, 1.794709075f,
+    1.834008086f, 1.874167634f, 1.915206561f, 1.957144124f,
+};
+
+// src/ops_quant.c:300-349: exponent/32-step split by the 1.5*2^23 magic
+// add, quadratic in w = 1 + r/32, table times polynomial times 2^n.
+LZ_HD float exp_body(float x) {
+  if (x > 88.0f) return FLT_MAX;
+  if (x < -87.3f) return 0.0f;
+  const float log2e32 = 1.44269504f * 32.0f;
+  float y32 = __fmul_rn(x, log2e32);
+  float u = __fadd_rn(__fsub_rn(y32, 0.5f), 12582912.0f);
+  int t = (__float_as_int(u) & 0x007FFFFF) - 0x00400000;
+  int n = t >> 5;
+  int idx = t & 31;
+  float r = __fsub_rn(y32, (float)t);
+  float w = __fadd_rn(1.0f, __fmul_rn(r, 0.03125f));
+  float p2n = __int_as_float((n + 127) << 23);
+  float c = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(0.242844437f, w), 0.207425515f), w), 0.549730133f);
+  return __fmul_rn(p2n, __fmul_rn(kExpTab32[idx], c));
+}
+
+// src/ops_quant.c:1836-1842 (float arm).
+LZ_HD float sigmoid(float x) {
+  if (x >= 0.0f) {
+    float z = exp_body(-x);
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, z));
+  }
+  float z = exp_body(x);
+  return __fdiv_rn(z, __fadd_rn(1.0f, z));
+}
+
+LZ_HD float silu(float x) { return __fmul_rn(x, sigmoid(x)); }
+
+// src/ops_quant.h:181-186 under round-to-nearest: half-to-even rounding
+// of |v| < 2^22 through the magic add.
+LZ_HD int q8_round(float v) {
+  return (__float_as_int(__fadd_rn(v, 12582912.0f)) & 0x007FFFFF) - 0x00400000;
+}
+LZ_HD int q8_clamp(int q) { return q > 127 ? 127 : (q < -127 ? -127 : q); }
+
+// src/ops_quant.c:1633-1666 given the group's magnitude bits.
+LZ_HD void q8_scale_from_amax(uint32_t am_bits, float* sg, float* inv) {
+  float amax = __uint_as_float(am_bits);
+  if (amax > 0.0f) {
+    *sg = __fmul_rn(amax, 1.0f / 127.0f);
+    *inv = __fdiv_rn(127.0f, amax);
+    if (*sg < 1.0e-30f) { *sg = 1.0f; *inv = 0.0f; }
+  } else {
+    *sg = 1.0f;
+    *inv = 0.0f;
+  }
+}
+
+LZ_HD uint32_t abs_bits(float x) { return __float_as_uint(x) & 0x7FFFFFFFu; }
+
+// Max of the magnitude bits over the 32 lanes of a warp (the group).
+LZ_HD uint32_t warp_max_u32(uint32_t v) {
+  for (int o = 16; o > 0; o >>= 1) {
+    uint32_t w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = v > w ? v : w;
+  }
+  return v;
+}
+
+// One 32-element activation group held one element per lane: the
+// reference quantiser (src/ops_quant.c:2152-2282). Returns the code; the
+// group scale is written by lane 0 when `scale_out` is non-null.
+LZ_HD int8_t warp_quant32(float x, float* scale_out) {
+  uint32_t am = warp_max_u32(abs_bits(x));
+  float sg, inv;
+  q8_scale_from_amax(am, &sg, &inv);
+  if (scale_out && (threadIdx.x & 31) == 0) *scale_out = sg;
+  return (int8_t)q8_clamp(q8_round(__fmul_rn(x, inv)));
+}
+
+// Total-order key of src/sampler.c:224: larger float -> larger key.
+LZ_HD uint32_t fkey(float f) {
+  uint32_t u = __float_as_uint(f);
+  return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
+}
+
+// xorshift64*, top 24 bits over 2^24 (src/sampler.c:185-203).
+LZ_HD float random_f32(unsigned long long* st) {
+  unsigned long long x = *st;
+  x ^= x >> 12;
+  x ^= x << 25;
+  x ^= x >> 27;
+  *st = x;
+  unsigned int r = (unsigned int)((x * 0x2545F4914F6CDD1DULL) >> 32);
+  return __fdiv_rn((float)(r >> 8), 16777216.0f);
+}
+
+}  // namespace lz98

@@ -1,0 +1,1156 @@
+// Host side of the B200-native MTP speculative-decoding step: model.bin
+// ("L98Z" v5) reader and HBM upload, the device run state (KDA state
+// ring, conv ring, MTP KV cache, draft chain), the forward orchestration
+// (body verify forward, MTP draft step, MTP prefill/catch-up) and the C ABI
+// declared in include/lz98_gpu.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <algorithm>
+#include <initializer_list>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/lz98_gpu.h"
+#include "lz98_kernels.cuh"
+
+using namespace lz98;
+
+namespace {
+
+void set_err(char* buf, int len, const char* fmt, const char* a = "") {
+  if (buf && len > 0) snprintf(buf, (size_t)len, fmt, a);
+}
+
+#define CK(call)                                                              \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess) {                                                  \
+      fprintf(stderr, "lz98: CUDA error %s at %s:%d\n", cudaGetErrorString(e_), \
+              __FILE__, __LINE__);                                            \
+      return LZ98_ERR_CUDA;                                                   \
+    }                                                                         \
+  } while (0)
+
+struct QW {                       // Q8_0 weight resident in HBM
+  int out = 0, in = 0, gs = 0;
+  int8_t* q = nullptr;
+  float* s = nullptr;
+};
+
+struct HQ {                       // host copy while reading
+  int out = 0, in = 0, gs = 0;
+  std::vector<int8_t> q;
+  std::vector<float> s;
+};
+
+struct Cfg {
+  int vocab, d, nl, seq_len, nh, nkv, hd, inter, nk, nv, kd, vd, conv_k;
+  float eps, theta, prf;
+  int q_dim, qg_dim, kv_dim, key_dim, val_dim, conv_dim, rot;
+  int rank, has_lb;
+  float lb;
+  int ne, topk, n_shared, moe_ffn, latent, fkdr, renorm, sigm, lat_norm, shared_w, mtp_layers, mtp_ffn;
+};
+
+struct DLayer {
+  float *in_ln, *post_ln, *conv_w, *a_log, *dt_bias, *o_norm, *router_bias;
+  QW inproj, fb, o, moein, up, sh_down;
+  int8_t *w13q, *w2q;
+  float *w13s, *w2s;
+  int w13_gs, w2_gs;
+};
+
+struct DMtp {
+  float *in_ln, *post_ln, *q_norm, *k_norm, *norm, *pre_h, *pre_e;
+  QW fc, qkv, o, gu, down;
+};
+
+}  // namespace
+
+struct LZModel {
+  Cfg c;
+  QW embed;
+  float* final_norm = nullptr;
+  std::vector<DLayer> L;
+  DMtp mtp;
+  size_t wbytes = 0;
+  std::vector<void*> allocs;
+  // column offsets inside the fused projection groups
+  int off_q, off_k, off_v, off_g, off_fa, off_b, n_in;
+  int off_router, off_down, off_shg, off_shu, n_moe;
+  int off_mq, off_mk, off_mv, n_qkv;
+};
+
+namespace {
+
+struct Reader {
+  FILE* f = nullptr;
+  bool bad = false;
+  void bytes(void* p, size_t n) {
+    if (!bad && fread(p, 1, n, f) != n) bad = true;
+  }
+  int i32() { int32_t v = 0; bytes(&v, 4); return v; }
+  float f32() { float v = 0; bytes(&v, 4); return v; }
+  std::vector<float> ften(size_t n) {
+    uint8_t dt = 0; uint32_t cnt = 0;
+    bytes(&dt, 1); bytes(&cnt, 4);
+    std::vector<float> v;
+    if (bad || dt != 0 || cnt != n) { bad = true; return v; }
+    v.resize(n);
+    bytes(v.data(), n * 4);
+    return v;
+  }
+  HQ qten(int out, int in) {
+    HQ t;
+    uint8_t dt = 0; uint32_t cnt = 0, gs = 0;
+    bytes(&dt, 1); bytes(&cnt, 4); bytes(&gs, 4);
+    if (bad || dt != 1 || (long long)cnt != (long long)out * in || gs == 0 || cnt % gs || gs % 32 ||
+        in % gs) {
+      bad = true;
+      return t;
+    }
+    t.out = out; t.in = in; t.gs = (int)gs;
+    t.q.resize(cnt);
+    t.s.resize(cnt / gs);
+    bytes(t.q.data(), cnt);
+    bytes(t.s.data(), (cnt / gs) * 4);
+    return t;
+  }
+};
+
+template <typename T>
+T* dev_upload(LZModel* m, const T* src, size_t n) {
+  T* p = nullptr;
+  if (cudaMalloc(&p, n * sizeof(T) + 16) != cudaSuccess) return nullptr;
+  cudaMemcpy(p, src, n * sizeof(T), cudaMemcpyHostToDevice);
+  m->allocs.push_back(p);
+  m->wbytes += n * sizeof(T);
+  return p;
+}
+
+float* up_f(LZModel* m, const std::vector<float>& v) { return dev_upload(m, v.data(), v.size()); }
+
+// Concatenate tensors of equal in-dim and group size along the output
+// dimension into one fused weight (rows stay whole, so every output row's
+// arithmetic is exactly that of its own tensor).
+bool up_group(LZModel* m, const std::vector<const HQ*>& parts, QW* out) {
+  int in = parts[0]->in, gs = parts[0]->gs, rows = 0;
+  for (auto* p : parts) {
+    if (p->in != in || p->gs != gs) return false;
+    rows += p->out;
+  }
+  std::vector<int8_t> q((size_t)rows * in);
+  std::vector<float> s((size_t)rows * (in / gs));
+  size_t oq = 0, os = 0;
+  for (auto* p : parts) {
+    memcpy(q.data() + oq, p->q.data(), p->q.size());
+    memcpy(s.data() + os, p->s.data(), p->s.size() * 4);
+    oq += p->q.size();
+    os += p->s.size();
+  }
+  out->out = rows; out->in = in; out->gs = gs;
+  out->q = dev_upload(m, q.data(), q.size());
+  out->s = dev_upload(m, s.data(), s.size());
+  return out->q && out->s;
+}
+
+bool up_one(LZModel* m, const HQ& h, QW* out) { return up_group(m, {&h}, out); }
+
+}  // namespace
+
+// ====================================================================== model
+
+extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen) {
+  if (!out || !dir) { set_err(errbuf, errlen, "null argument"); return LZ98_ERR_NULL_ARG; }
+  *out = nullptr;
+  std::string path = std::string(dir) + "/model.bin";
+  Reader r;
+  r.f = fopen(path.c_str(), "rb");
+  if (!r.f) { set_err(errbuf, errlen, "cannot open %s", path.c_str()); return LZ98_ERR_MODEL; }
+  LZModel* m = new LZModel();
+  Cfg& c = m->c;
+  char magic[4];
+  r.bytes(magic, 4);
+  int ver = r.i32();
+  if (memcmp(magic, "L98Z", 4) != 0 || ver != 5) {
+    set_err(errbuf, errlen, "not an L98Z v5 model.bin");
+    fclose(r.f); delete m; return LZ98_ERR_MODEL;
+  }
+  // Header words in the order of src/model.c:3993-4301.
+  c.vocab = r.i32(); c.d = r.i32(); c.nl = r.i32(); c.seq_len = r.i32();
+  c.nh = r.i32(); c.nkv = r.i32(); c.hd = r.i32(); c.inter = r.i32();
+  c.nk = r.i32(); c.nv = r.i32(); c.kd = r.i32(); c.vd = r.i32();
+  c.conv_k = r.i32(); r.i32(); r.i32(); r.i32(); r.i32(); r.i32();
+  c.eps = r.f32(); c.theta = r.f32(); c.prf = r.f32();
+  c.q_dim = r.i32(); c.qg_dim = r.i32(); c.kv_dim = r.i32();
+  c.key_dim = r.i32(); c.val_dim = r.i32(); c.conv_dim = r.i32(); c.rot = r.i32();
+  int lt[128];
+  for (int i = 0; i < 128; i++) lt[i] = r.i32();
+  c.rank = r.i32(); c.has_lb = r.i32(); c.lb = r.f32();
+  c.ne = r.i32(); c.topk = r.i32(); c.n_shared = r.i32(); c.moe_ffn = r.i32();
+  c.latent = r.i32(); c.fkdr = r.i32(); c.renorm = r.i32(); c.sigm = r.i32();
+  c.lat_norm = r.i32(); c.shared_w = r.i32();
+  c.mtp_layers = r.i32(); c.mtp_ffn = r.i32();
+  for (int i = 0; i < 15; i++) r.i32();
+  for (int i = 0; i < 3 * 128; i++) r.i32();
+  for (int i = 0; i < 6; i++) r.i32();
+  for (int i = 0; i < 128; i++) r.i32();
+  bool ok = !r.bad;
+  for (int l = 0; l < c.nl && ok; l++) ok = lt[l] == 2;
+  ok = ok && c.fkdr == 0 && c.ne > 0 && c.ne <= 256 && c.topk <= 16 && c.mtp_layers == 1 &&
+       !c.lat_norm && c.has_lb && c.sigm && c.renorm && c.kd == 64 && c.vd == 64 &&
+       c.nk == c.nv && c.hd == 64 && c.conv_k == 4 && c.d % 32 == 0 && c.rank % 32 == 0 &&
+       c.rank <= 256 && c.latent <= 1024 && c.latent % 32 == 0 && c.moe_ffn % 32 == 0 &&
+       c.shared_w % 32 == 0 && 2 * c.d <= 8192;
+  if (!ok) {
+    set_err(errbuf, errlen, "unsupported KunMoe configuration (needs all-KDA layers, latent MoE with "
+                            "sigmoid router, one MTP layer, head dims 64)");
+    fclose(r.f); delete m; return LZ98_ERR_MODEL;
+  }
+  HQ embed = r.qten(c.vocab, c.d);
+  std::vector<float> fnorm = r.ften(c.d);
+  if (!r.bad) {
+    up_one(m, embed, &m->embed);
+    m->final_norm = up_f(m, fnorm);
+  }
+  const int kdim = c.key_dim, vdim = c.val_dim, nvk = c.nv * c.kd;
+  m->off_q = 0; m->off_k = kdim; m->off_v = 2 * kdim; m->off_g = 2 * kdim + vdim;
+  m->off_fa = 2 * kdim + 2 * vdim; m->off_b = m->off_fa + c.rank; m->n_in = m->off_b + c.nv;
+  m->off_router = 0; m->off_down = c.ne; m->off_shg = c.ne + c.latent;
+  m->off_shu = m->off_shg + c.shared_w; m->n_moe = m->off_shu + c.shared_w;
+  m->off_mq = 0; m->off_mk = c.qg_dim; m->off_mv = c.qg_dim + c.kv_dim;
+  m->n_qkv = c.qg_dim + 2 * c.kv_dim;
+  m->L.resize(c.nl);
+  for (int l = 0; l < c.nl && !r.bad; l++) {
+    DLayer& L = m->L[l];
+    auto in_ln = r.ften(c.d), post_ln = r.ften(c.d);
+    HQ q = r.qten(kdim, c.d), k = r.qten(kdim, c.d), v = r.qten(vdim, c.d);
+    auto qc = r.ften((size_t)kdim * c.conv_k), kc = r.ften((size_t)kdim * c.conv_k),
+         vc = r.ften((size_t)vdim * c.conv_k);
+    auto a_log = r.ften(c.nv);
+    HQ fa = r.qten(c.rank, c.d), fb = r.qten(nvk, c.rank);
+    auto dt_bias = r.ften(nvk);
+    HQ b = r.qten(c.nv, c.d), g = r.qten(vdim, c.d);
+    auto o_norm = r.ften(c.vd);
+    HQ o = r.qten(c.d, vdim);
+    HQ router = r.qten(c.ne, c.d);
+    auto rbias = r.ften(c.ne);
+    HQ down = r.qten(c.latent, c.d), up = r.qten(c.d, c.latent);
+    HQ shg, shu, shd;
+    if (c.shared_w) {
+      shg = r.qten(c.shared_w, c.d); shu = r.qten(c.shared_w, c.d); shd = r.qten(c.d, c.shared_w);
+    }
+    std::vector<int8_t> w13q, w2q;
+    std::vector<float> w13s, w2s;
+    int gs1 = 0, gs2 = 0;
+    for (int e = 0; e < c.ne && !r.bad; e++) {
+      HQ w1 = r.qten(c.moe_ffn, c.latent), w2 = r.qten(c.latent, c.moe_ffn), w3 = r.qten(c.moe_ffn, c.latent);
+      if (r.bad) break;
+      if (e == 0) { gs1 = w1.gs; gs2 = w2.gs; }
+      if (w1.gs != gs1 || w3.gs != gs1 || w2.gs != gs2) { r.bad = true; break; }
+      w13q.insert(w13q.end(), w1.q.begin(), w1.q.end());
+      w13q.insert(w13q.end(), w3.q.begin(), w3.q.end());
+      w13s.insert(w13s.end(), w1.s.begin(), w1.s.end());
+      w13s.insert(w13s.end(), w3.s.begin(), w3.s.end());
+      w2q.insert(w2q.end(), w2.q.begin(), w2.q.end());
+      w2s.insert(w2s.end(), w2.s.begin(), w2.s.end());
+    }
+    if (r.bad) break;
+    std::vector<float> conv_w;
+    conv_w.insert(conv_w.end(), qc.begin(), qc.end());
+    conv_w.insert(conv_w.end(), kc.begin(), kc.end());
+    conv_w.insert(conv_w.end(), vc.begin(), vc.end());
+    L.in_ln = up_f(m, in_ln); L.post_ln = up_f(m, post_ln); L.conv_w = up_f(m, conv_w);
+    L.a_log = up_f(m, a_log); L.dt_bias = up_f(m, dt_bias); L.o_norm = up_f(m, o_norm);
+    L.router_bias = up_f(m, rbias);
+    bool g_ok = up_group(m, {&q, &k, &v, &g, &fa, &b}, &L.inproj) && up_one(m, fb, &L.fb) &&
+                up_one(m, o, &L.o) && up_one(m, up, &L.up);
+    if (c.shared_w) {
+      g_ok = g_ok && up_group(m, {&router, &down, &shg, &shu}, &L.moein) && up_one(m, shd, &L.sh_down);
+    } else {
+      g_ok = g_ok && up_group(m, {&router, &down}, &L.moein);
+    }
+    L.w13q = dev_upload(m, w13q.data(), w13q.size());
+    L.w13s = dev_upload(m, w13s.data(), w13s.size());
+    L.w2q = dev_upload(m, w2q.data(), w2q.size());
+    L.w2s = dev_upload(m, w2s.data(), w2s.size());
+    L.w13_gs = gs1; L.w2_gs = gs2;
+    if (!g_ok) { r.bad = true; break; }
+  }
+  if (!r.bad) {
+    DMtp& M = m->mtp;
+    auto in_ln = r.ften(c.d), post_ln = r.ften(c.d);
+    HQ qp = r.qten(c.qg_dim, c.d), kp = r.qten(c.kv_dim, c.d), vp = r.qten(c.kv_dim, c.d);
+    HQ op = r.qten(c.d, c.q_dim);
+    auto qn = r.ften(c.hd), kn = r.ften(c.hd);
+    HQ gate = r.qten(c.mtp_ffn, c.d), up = r.qten(c.mtp_ffn, c.d), down = r.qten(c.d, c.mtp_ffn);
+    HQ fc = r.qten(c.d, 2 * c.d);
+    auto norm = r.ften(c.d), pre_h = r.ften(c.d), pre_e = r.ften(c.d);
+    if (!r.bad) {
+      M.in_ln = up_f(m, in_ln); M.post_ln = up_f(m, post_ln); M.q_norm = up_f(m, qn);
+      M.k_norm = up_f(m, kn); M.norm = up_f(m, norm); M.pre_h = up_f(m, pre_h); M.pre_e = up_f(m, pre_e);
+      bool g_ok = up_group(m, {&qp, &kp, &vp}, &M.qkv) && up_one(m, op, &M.o) &&
+                  up_group(m, {&gate, &up}, &M.gu) && up_one(m, down, &M.down) && up_one(m, fc, &M.fc);
+      if (!g_ok) r.bad = true;
+    }
+  }
+  fclose(r.f);
+  if (r.bad) {
+    set_err(errbuf, errlen, "truncated or malformed model.bin (or mixed group sizes in a fused group)");
+    lz_free(m);
+    return LZ98_ERR_MODEL;
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure while uploading weights");
+    lz_free(m);
+    return LZ98_ERR_CUDA;
+  }
+  *out = m;
+  return 0;
+}
+
+extern "C" void lz_free(LZModel* m) {
+  if (!m) return;
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+}
+
+extern "C" void lz_model_info(const LZModel* m, int* o) {
+  const Cfg& c = m->c;
+  int v[16] = {c.vocab, c.d, c.nl, c.nv, c.key_dim, c.latent, c.ne, c.topk, c.shared_w,
+               c.hd, c.nh, c.nkv, c.rot, c.seq_len, c.mtp_ffn, c.moe_ffn};
+  memcpy(o, v, sizeof v);
+}
+
+extern "C" size_t lz_model_weight_bytes(const LZModel* m) { return m ? m->wbytes : 0; }
+
+// ====================================================================== state
+
+struct LZRunState {
+  const LZModel* m = nullptr;
+  int B = 1, seq_len = 0, depth = 1, kmax = 1, Rmax = 64;
+  cudaStream_t st = nullptr;
+  // recurrent state and caches
+  int8_t *hi = nullptr, *lo = nullptr;
+  float *sc = nullptr, *conv = nullptr;
+  int8_t *kq = nullptr, *vq = nullptr;
+  float *ks = nullptr, *vs = nullptr, *chain = nullptr, *rope = nullptr;
+  size_t q_slot = 0, q_seq = 0, conv_slot = 0, conv_seq = 0, cache_seq = 0;
+  float attn_scale = 0, ssm_scale = 0;
+  // scratch
+  float *x, *inproj, *conv_out, *gate, *moein, *h2, *shout, *hidden, *logits, *qkv, *mtpx, *hb;
+  int8_t *xq, *oq, *latq, *hq, *yq, *shq, *aq;
+  float *xs, *os, *lats, *hs, *ys, *shs, *as;
+  int *pair_e, *tok, *vmax, *catch_tok, *catch_hidx;
+  float* pair_w;
+  KdaSeq* seqs;
+  MtpRow *mrows, *crows;
+  SeqRound* sr;
+  size_t hb_rows = 0;
+  // host mirrors
+  std::vector<SeqRound> h_sr;
+  std::vector<float> h_logits, h_hidden, h_draft;
+  long long launches = 0;
+  bool graphs = true;
+  std::map<int, cudaGraphExec_t> graph;
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+template <typename T>
+bool dmalloc(LZRunState* s, T** p, size_t n) {
+  if (cudaMalloc((void**)p, n * sizeof(T) + 64) != cudaSuccess) return false;
+  cudaMemset(*p, 0, n * sizeof(T) + 64);
+  s->allocs.push_back(*p);
+  return true;
+}
+
+// RoPE table (src/forward_rope.c:178-187, no scaling): freq_i =
+// theta^(-2i/rot), angle = l * freq_i; cos/sin/pow evaluated in double
+// and rounded once.
+void build_rope(const Cfg& c, int seq_len, std::vector<float>& t) {
+  int half = c.rot / 2;
+  t.assign((size_t)seq_len * c.rot, 0.0f);
+  for (int i = 0; i < half; i++) {
+    float ex = -2.0f * (float)i / (float)c.rot;
+    float freq = (float)pow((double)c.theta, (double)ex);
+    for (int l = 0; l < seq_len; l++) {
+      float ang = (float)l * freq;
+      t[((size_t)l * half + i) * 2] = (float)cos((double)ang);
+      t[((size_t)l * half + i) * 2 + 1] = (float)sin((double)ang);
+    }
+  }
+}
+
+float host_rsqrt_body(float x) {         // src/ops_quant.c:126-135
+  union { float f; uint32_t u; } t;
+  volatile float h = 0.5f * x;
+  float y;
+  t.f = x;
+  t.u = 0x5f375a86u - (t.u >> 1);
+  y = t.f;
+  volatile float a = h * y;
+  volatile float b = a * y;
+  volatile float cc = 1.5f - b;
+  y = y * cc;
+  a = h * y; b = a * y; cc = 1.5f - b;
+  y = y * cc;
+  return y;
+}
+
+}  // namespace
+
+static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_len, int spec_k_max,
+                       char* errbuf, int errlen) {
+  if (!out || !m || n_seq < 1 || seq_len < 2 || spec_k_max < 1 || spec_k_max > 6) {
+    set_err(errbuf, errlen, "bad state arguments");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const Cfg& c = m->c;
+  LZRunState* s = new LZRunState();
+  s->m = m;
+  s->B = n_seq;
+  s->seq_len = seq_len;
+  s->depth = spec_k_max + 1;              // src/forward_state.c:738-744
+  s->kmax = spec_k_max;
+  s->Rmax = std::max(64, n_seq * (spec_k_max + 1));
+  if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+    delete s;
+    set_err(errbuf, errlen, "cudaStreamCreate failed");
+    return LZ98_ERR_CUDA;
+  }
+  s->q_slot = (size_t)c.nl * c.nv * c.kd * c.vd;
+  s->q_seq = s->q_slot * s->depth;
+  s->conv_slot = (size_t)c.nl * c.conv_dim * 3;
+  s->conv_seq = s->conv_slot * s->depth;
+  s->cache_seq = (size_t)seq_len * c.kv_dim;
+  const size_t B = n_seq, R = s->Rmax, P = R * c.topk;
+  const int kmaxw = std::max({2 * c.d, c.key_dim, c.val_dim, c.moe_ffn, c.shared_w, c.latent, c.q_dim,
+                              c.mtp_ffn, c.rank});
+  const int nwide = std::max({m->n_in, m->n_moe, m->n_qkv, 2 * c.mtp_ffn});
+  bool ok = dmalloc(s, &s->hi, s->q_seq * B) && dmalloc(s, &s->lo, s->q_seq * B) &&
+            dmalloc(s, &s->sc, s->q_seq * B / 32) && dmalloc(s, &s->conv, s->conv_seq * B) &&
+            dmalloc(s, &s->kq, s->cache_seq * B) && dmalloc(s, &s->vq, s->cache_seq * B) &&
+            dmalloc(s, &s->ks, s->cache_seq * B / 32) && dmalloc(s, &s->vs, s->cache_seq * B / 32) &&
+            dmalloc(s, &s->chain, B * c.d) && dmalloc(s, &s->rope, (size_t)seq_len * c.rot) &&
+            dmalloc(s, &s->x, R * c.d) && dmalloc(s, &s->inproj, R * nwide) &&
+            dmalloc(s, &s->conv_out, R * c.conv_dim) && dmalloc(s, &s->gate, R * c.nv * c.kd) &&
+            dmalloc(s, &s->moein, R * m->n_moe) && dmalloc(s, &s->h2, P * c.latent) &&
+            dmalloc(s, &s->shout, R * c.d) && dmalloc(s, &s->hidden, R * c.d) &&
+            dmalloc(s, &s->logits, R * (size_t)c.vocab) && dmalloc(s, &s->qkv, R * m->n_qkv) &&
+            dmalloc(s, &s->mtpx, R * c.d) && dmalloc(s, &s->xq, R * kmaxw) &&
+            dmalloc(s, &s->xs, R * kmaxw / 32) && dmalloc(s, &s->oq, R * c.val_dim) &&
+            dmalloc(s, &s->os, R * c.val_dim / 32) && dmalloc(s, &s->latq, R * c.latent) &&
+            dmalloc(s, &s->lats, R * c.latent / 32) && dmalloc(s, &s->hq, P * c.moe_ffn) &&
+            dmalloc(s, &s->hs, P * c.moe_ffn / 32) && dmalloc(s, &s->yq, R * c.latent) &&
+            dmalloc(s, &s->ys, R * c.latent / 32) &&
+            dmalloc(s, &s->shq, R * std::max(c.shared_w, c.mtp_ffn)) &&
+            dmalloc(s, &s->shs, R * std::max(c.shared_w, c.mtp_ffn) / 32) &&
+            dmalloc(s, &s->aq, R * c.q_dim) && dmalloc(s, &s->as, R * c.q_dim / 32) &&
+            dmalloc(s, &s->pair_e, P) && dmalloc(s, &s->pair_w, P) && dmalloc(s, &s->tok, R) &&
+            dmalloc(s, &s->vmax, R) && dmalloc(s, &s->catch_tok, R) && dmalloc(s, &s->catch_hidx, R) &&
+            dmalloc(s, &s->seqs, R) && dmalloc(s, &s->mrows, R) && dmalloc(s, &s->crows, R) &&
+            dmalloc(s, &s->sr, B);
+  if (!ok) {
+    set_err(errbuf, errlen, "device allocation failed");
+    lz_state_free(s);
+    return LZ98_ERR_ALLOC;
+  }
+  std::vector<float> rope;
+  build_rope(c, seq_len, rope);
+  cudaMemcpy(s->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice);
+  s->attn_scale = host_rsqrt_body((float)c.hd);     // src/forward_state.c:1408-1409
+  s->ssm_scale = host_rsqrt_body((float)c.kd);
+  s->h_sr.assign(B, SeqRound{});
+  s->h_logits.resize((size_t)R * c.vocab);
+  s->h_hidden.resize((size_t)R * c.d);
+  s->h_draft.resize(c.vocab);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure in state allocation");
+    lz_state_free(s);
+    return LZ98_ERR_CUDA;
+  }
+  *out = s;
+  return 0;
+}
+
+extern "C" int lz_state_alloc(LZRunState** out, const LZModel* m, int seq_len, int spec_k_max,
+                              char* errbuf, int errlen) {
+  return state_alloc(out, m, 1, seq_len, spec_k_max, errbuf, errlen);
+}
+
+extern "C" int lz_state_alloc_batch(LZRunState** out, const LZModel* m, int n_seq, int seq_len,
+                                    int spec_k_max, char* errbuf, int errlen) {
+  return state_alloc(out, m, n_seq, seq_len, spec_k_max, errbuf, errlen);
+}
+
+extern "C" void lz_state_free(LZRunState* s) {
+  if (!s) return;
+  for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->st) cudaStreamDestroy(s->st);
+  delete s;
+}
+
+static void clear_state(LZRunState* s) {
+  const Cfg& c = s->m->c;
+  const size_t B = s->B;
+  cudaMemsetAsync(s->hi, 0, s->q_seq * B, s->st);
+  cudaMemsetAsync(s->lo, 0, s->q_seq * B, s->st);
+  cudaMemsetAsync(s->sc, 0, s->q_seq * B / 32 * 4, s->st);
+  cudaMemsetAsync(s->conv, 0, s->conv_seq * B * 4, s->st);
+  cudaMemsetAsync(s->kq, 0, s->cache_seq * B, s->st);
+  cudaMemsetAsync(s->vq, 0, s->cache_seq * B, s->st);
+  cudaMemsetAsync(s->ks, 0, s->cache_seq * B / 32 * 4, s->st);
+  cudaMemsetAsync(s->vs, 0, s->cache_seq * B / 32 * 4, s->st);
+  cudaMemsetAsync(s->chain, 0, B * c.d * 4, s->st);
+  for (auto& r : s->h_sr) r = SeqRound{};
+  cudaMemcpyAsync(s->sr, s->h_sr.data(), B * sizeof(SeqRound), cudaMemcpyHostToDevice, s->st);
+  cudaStreamSynchronize(s->st);
+}
+
+extern "C" void lz_state_reset(LZRunState* s, const LZModel*) {
+  if (s) clear_state(s);
+}
+
+static void sr_down(LZRunState* s) {
+  cudaMemcpyAsync(s->h_sr.data(), s->sr, s->B * sizeof(SeqRound), cudaMemcpyDeviceToHost, s->st);
+  cudaStreamSynchronize(s->st);
+}
+static void sr_up(LZRunState* s) {
+  cudaMemcpyAsync(s->sr, s->h_sr.data(), s->B * sizeof(SeqRound), cudaMemcpyHostToDevice, s->st);
+}
+
+extern "C" int lz_state_get(const LZRunState* cs, int seq, int* mtp_pos, int* ssm_slot, int* depth) {
+  LZRunState* s = const_cast<LZRunState*>(cs);
+  if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  sr_down(s);
+  if (mtp_pos) *mtp_pos = s->h_sr[seq].mtp_pos;
+  if (ssm_slot) *ssm_slot = s->h_sr[seq].ssm_slot;
+  if (depth) *depth = s->depth;
+  return 0;
+}
+
+extern "C" int lz_state_set(LZRunState* s, int seq, int mtp_pos, int ssm_slot) {
+  if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  sr_down(s);
+  if (mtp_pos >= 0) s->h_sr[seq].mtp_pos = mtp_pos;
+  if (ssm_slot >= 0) s->h_sr[seq].ssm_slot = ssm_slot % s->depth;
+  sr_up(s);
+  cudaStreamSynchronize(s->st);
+  return 0;
+}
+
+extern "C" int lz_state_get_chain(const LZRunState* s, int seq, float* chain) {
+  if (!s || !chain || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  const int d = s->m->c.d;
+  cudaMemcpyAsync(chain, s->chain + (size_t)seq * d, d * 4, cudaMemcpyDeviceToHost, s->st);
+  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+}
+
+extern "C" int lz_state_set_chain(LZRunState* s, int seq, const float* chain) {
+  if (!s || !chain || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  const int d = s->m->c.d;
+  cudaMemcpyAsync(s->chain + (size_t)seq * d, chain, d * 4, cudaMemcpyHostToDevice, s->st);
+  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+}
+
+extern "C" void* lz_state_stream(LZRunState* s) { return s ? (void*)s->st : nullptr; }
+extern "C" long long lz_state_launches(const LZRunState* s) { return s ? s->launches : 0; }
+extern "C" int lz_set_graphs(LZRunState* s, int enable) {
+  if (!s) return LZ98_ERR_NULL_ARG;
+  s->graphs = enable != 0;
+  return 0;
+}
+
+// ================================================================== launches
+
+namespace {
+
+void gemv(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, float* y, int ldy,
+          int mode = 0, const float* z = nullptr, int ldz = 0) {
+  const int nsb = w.in / 32;
+  const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
+  if (nsb <= 32)
+    gemv_q8_kernel<1><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
+  else if (nsb <= 64)
+    gemv_q8_kernel<2><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
+  else if (nsb <= 128)
+    gemv_q8_kernel<4><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
+  else
+    gemv_q8_kernel<8><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
+  s->launches++;
+}
+
+void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
+                   int ldo, int8_t* xq, float* xs) {
+  rmsnorm_quant_kernel<<<R, 256, n * sizeof(float), s->st>>>(x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs);
+  s->launches++;
+}
+
+// Body forward of R rows (src/forward.c:1210-1617): embed, per layer
+// pre-norm -> KDA -> residual -> post-norm -> latent MoE -> residual, then
+// final norm (hidden capture) and the tied lm_head over every row.
+void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
+  const LZModel* m = s->m;
+  const Cfg& c = m->c;
+  const int d = c.d, kdim = c.key_dim, vdim = c.val_dim, nvk = c.nv * c.kd;
+  embed_kernel<<<R, 256, 0, s->st>>>(m->embed.q, m->embed.s, m->embed.gs, d, s->tok, s->x);
+  s->launches++;
+  for (int l = 0; l < c.nl; l++) {
+    const DLayer& L = m->L[l];
+    rmsnorm_quant(s, s->x, d, L.in_ln, d, R, nullptr, 0, s->xq, s->xs);
+    gemv(s, L.inproj, s->xq, s->xs, R, s->inproj, m->n_in);
+    kda_fb_gate_kernel<<<dim3((nvk + 255) / 256, R), 256, 0, s->st>>>(
+        s->inproj, m->n_in, m->off_fa, c.rank, L.fb.q, L.fb.s, L.fb.gs, L.a_log, L.dt_bias, c.lb, nvk,
+        c.kd, s->gate);
+    kda_conv_kernel<<<dim3((c.conv_dim + 127) / 128, nseq), 128, 0, s->st>>>(
+        s->inproj, m->n_in, c.conv_dim, L.conv_w, s->seqs, s->conv + (size_t)l * c.conv_dim * 3,
+        s->conv_seq, s->conv_slot, s->depth, adv, s->conv_out, c.conv_dim);
+    kda_recur_kernel<<<dim3(c.nv, nseq), kRecurThreads, 0, s->st>>>(
+        s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
+        s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
+        s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
+    s->launches += 3;
+    gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);
+    rmsnorm_quant(s, s->x, d, L.post_ln, d, R, nullptr, 0, s->xq, s->xs);
+    gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe);
+    moe_route_kernel<<<R, 32, 0, s->st>>>(s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
+                                          c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats);
+    s->launches++;
+    if (c.shared_w) {
+      swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->moein, m->n_moe, m->off_shg, m->off_shu, c.shared_w,
+                                                s->shq, s->shs);
+      s->launches++;
+      gemv(s, L.sh_down, s->shq, s->shs, R, s->shout, d);
+    }
+    moe_w13_kernel<<<dim3(c.moe_ffn / 32, R * c.topk), 256, 0, s->st>>>(
+        L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
+    moe_w2_kernel<<<dim3((c.latent + 7) / 8, R * c.topk), 256, 0, s->st>>>(
+        L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->hq, s->hs, s->h2);
+    moe_combine_kernel<<<R, 256, 0, s->st>>>(s->h2, s->pair_w, s->pair_e, c.topk, c.latent, s->yq, s->ys);
+    s->launches += 3;
+    gemv(s, L.up, s->yq, s->ys, R, s->x, d, c.shared_w ? 2 : 1, s->shout, d);
+  }
+  rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs);
+  if (want_logits) gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
+}
+
+// MTP block over R rows (src/forward_mtp.c:32-144, 561-624): fc front,
+// input norm, q|k|v projection, cache write; when `full`, the gated
+// attention, o_proj, dense SwiGLU FFN, final norm into chain_out and the
+// tied lm_head into s->logits.
+void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const int* hid_idx,
+                 const MtpRow* rows, bool full, float* chain_out) {
+  const LZModel* m = s->m;
+  const Cfg& c = m->c;
+  const DMtp& M = m->mtp;
+  const int d = c.d;
+  mtp_front_kernel<<<R, 256, 2 * d * sizeof(float), s->st>>>(m->embed.q, m->embed.s, m->embed.gs, d, tok,
+                                                             hid, hid_idx, M.pre_e, M.pre_h, c.eps, s->xq,
+                                                             s->xs);
+  s->launches++;
+  gemv(s, M.fc, s->xq, s->xs, R, s->mtpx, d);
+  rmsnorm_quant(s, s->mtpx, d, M.in_ln, d, R, nullptr, 0, s->xq, s->xs);
+  gemv(s, M.qkv, s->xq, s->xs, R, s->qkv, m->n_qkv);
+  mtp_kv_write_kernel<<<dim3(c.nkv, R), 64, 0, s->st>>>(s->qkv, m->n_qkv, m->off_mk, m->off_mv, rows, M.k_norm,
+                                                        c.eps, c.hd, c.rot, c.kv_dim, s->rope, s->kq, s->ks,
+                                                        s->vq, s->vs, s->cache_seq);
+  s->launches++;
+  if (!full) return;
+  const size_t smem = (size_t)s->seq_len * sizeof(float);
+  mtp_attn_kernel<<<dim3(c.nh, R), 128, smem, s->st>>>(s->qkv, m->n_qkv, c.q_dim, rows, M.q_norm, c.eps, c.hd,
+                                                       c.rot, c.kv_dim, c.nh / c.nkv, s->rope, s->attn_scale,
+                                                       s->kq, s->ks, s->vq, s->vs, s->cache_seq, s->aq, s->as);
+  s->launches++;
+  gemv(s, M.o, s->aq, s->as, R, s->mtpx, d, 1);
+  rmsnorm_quant(s, s->mtpx, d, M.post_ln, d, R, nullptr, 0, s->xq, s->xs);
+  gemv(s, M.gu, s->xq, s->xs, R, s->inproj, 2 * c.mtp_ffn);
+  swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->inproj, 2 * c.mtp_ffn, 0, c.mtp_ffn, c.mtp_ffn, s->shq, s->shs);
+  s->launches++;
+  gemv(s, M.down, s->shq, s->shs, R, s->mtpx, d, 1);
+  rmsnorm_quant(s, s->mtpx, d, M.norm, d, R, chain_out, d, s->xq, s->xs);
+  gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
+}
+
+__global__ void set_rows_kernel(MtpRow* rows, int n, int seq, int pos0, int seq_len) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) rows[i] = MtpRow{seq, pos0 + i, pos0 + i >= 0 && pos0 + i < seq_len};
+}
+
+// Rows whose MTP position would fall outside the cache are marked
+// inactive (no cache write, no attention): the memory stays in bounds and
+// the host's budget check (max_pos) keeps such rounds from being asked for.
+__global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_len, int* tok, MtpRow* rows) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nseq) return;
+  tok[b] = i == 0 ? sr[b].anchor : sr[b].draft[i - 1];
+  const int pos = sr[b].mtp_pos + i;
+  rows[b] = MtpRow{b, pos, pos >= 0 && pos < seq_len};
+}
+
+__global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const int* amax) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nseq) return;
+  sr[b].draft[i] = amax[b];
+  sr[b].k = k;
+}
+
+__global__ void verify_setup_kernel(const SeqRound* sr, int nseq, int k, int* tok, KdaSeq* seqs) {
+  int b = blockIdx.x;
+  if (b >= nseq) return;
+  if (threadIdx.x == 0) seqs[b] = KdaSeq{b * (k + 1), k + 1, sr[b].ssm_slot, b};
+  for (int j = threadIdx.x; j <= k; j += blockDim.x)
+    tok[b * (k + 1) + j] = j == 0 ? sr[b].anchor : sr[b].draft[j - 1];
+}
+
+int upload_seqs(LZRunState* s, const std::vector<KdaSeq>& v) {
+  CK(cudaMemcpyAsync(s->seqs, v.data(), v.size() * sizeof(KdaSeq), cudaMemcpyHostToDevice, s->st));
+  return 0;
+}
+
+// One greedy round of every sequence, all on the device.
+void round_greedy(LZRunState* s, int k) {
+  const LZModel* m = s->m;
+  const Cfg& c = m->c;
+  const int B = s->B;
+  const int tb = (B + 127) / 128;
+  for (int i = 0; i < k; i++) {
+    draft_setup_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, s->seq_len, s->tok, s->mrows);
+    mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
+    argmax_kernel<<<B, 1024, 0, s->st>>>(s->logits, c.vocab, 1, s->vmax);
+    draft_store_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, k, s->vmax);
+    s->launches += 3;
+  }
+  const int R = B * (k + 1);
+  verify_setup_kernel<<<B, 32, 0, s->st>>>(s->sr, B, k, s->tok, s->seqs);
+  body_forward(s, R, B, 1, true);
+  argmax_kernel<<<R, 1024, 0, s->st>>>(s->logits, c.vocab, 0, s->vmax);
+  spec_accept_greedy_kernel<<<B, 256, 0, s->st>>>(s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
+                                                  s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  s->launches += 3;
+  if (k > 1)
+    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+}
+
+}  // namespace
+
+// ================================================================== forwards
+
+static float* forward_one(const LZModel* m, LZRunState* s, const int* tokens, int n, int pos0, bool capture,
+                          float* hidden_out, bool all_logits) {
+  const Cfg& c = m->c;
+  if (!m || !s || !tokens || n < 1) return nullptr;
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab || pos0 + i < 0 || pos0 + i >= s->seq_len) return nullptr;
+  sr_down(s);
+  const int slot = s->h_sr[0].ssm_slot;
+  float* last = nullptr;
+  for (int done = 0; done < n;) {
+    const int R = std::min(s->Rmax, n - done);
+    cudaMemcpyAsync(s->tok, tokens + done, R * sizeof(int), cudaMemcpyHostToDevice, s->st);
+    upload_seqs(s, {KdaSeq{0, R, slot, 0}});
+    const bool logits_here = all_logits || done + R == n;
+    body_forward(s, R, 1, 0, logits_here);
+    if (hidden_out)
+      cudaMemcpyAsync(hidden_out + (size_t)done * c.d, s->hidden, (size_t)R * c.d * 4, cudaMemcpyDeviceToHost,
+                      s->st);
+    if (logits_here) {
+      const int r0 = all_logits ? 0 : R - 1;
+      const int nr = all_logits ? R : 1;
+      cudaMemcpyAsync(s->h_logits.data() + (all_logits ? (size_t)done * c.vocab : 0),
+                      s->logits + (size_t)r0 * c.vocab, (size_t)nr * c.vocab * 4, cudaMemcpyDeviceToHost,
+                      s->st);
+      last = s->h_logits.data();
+    }
+    if (capture && done + R == n)
+      cudaMemcpyAsync(s->chain, s->hidden + (size_t)(R - 1) * c.d, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
+    done += R;
+  }
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) return nullptr;
+  return last;
+}
+
+extern "C" float* lz_forward(const LZModel* m, LZRunState* s, int token, int pos) {
+  return forward_one(m, s, &token, 1, pos, false, nullptr, false);
+}
+
+extern "C" float* lz_forward_capture(const LZModel* m, LZRunState* s, int token, int pos) {
+  return forward_one(m, s, &token, 1, pos, true, nullptr, false);
+}
+
+extern "C" float* lz_forward_batch_capture(const LZModel* m, LZRunState* s, const int* tokens, int n, int pos0,
+                                           float* hidden_out) {
+  if (!hidden_out) return nullptr;
+  return forward_one(m, s, tokens, n, pos0, false, hidden_out, false);
+}
+
+extern "C" int lz_forward_verify(const LZModel* m, LZRunState* s, const int* tokens, int n, int pos0) {
+  if (!m || !s || !tokens || n < 1 || n > s->kmax + 1) return 1;
+  const Cfg& c = m->c;
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab || pos0 + i < 0 || pos0 + i >= s->seq_len) return 1;
+  sr_down(s);
+  const int slot = s->h_sr[0].ssm_slot;
+  cudaMemcpyAsync(s->tok, tokens, n * sizeof(int), cudaMemcpyHostToDevice, s->st);
+  upload_seqs(s, {KdaSeq{0, n, slot, 0}});
+  body_forward(s, n, 1, 1, true);
+  cudaMemcpyAsync(s->h_logits.data(), s->logits, (size_t)n * c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
+  cudaMemcpyAsync(s->h_hidden.data(), s->hidden, (size_t)n * c.d * 4, cudaMemcpyDeviceToHost, s->st);
+  s->h_sr[0].ssm_slot = (slot + n) % s->depth;
+  sr_up(s);
+  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : 1;
+}
+
+extern "C" const float* lz_state_mtp_logits(const LZRunState* s) { return s ? s->h_logits.data() : nullptr; }
+extern "C" const float* lz_state_mtp_verify_hidden(const LZRunState* s) {
+  return s ? s->h_hidden.data() : nullptr;
+}
+
+extern "C" float* lz_mtp_draft_step(const LZModel* m, LZRunState* s, int next_token, int pos) {
+  if (!m || !s) return nullptr;
+  const Cfg& c = m->c;
+  if (next_token < 0 || next_token >= c.vocab || pos < 0 || pos >= s->seq_len) return nullptr;
+  cudaMemcpyAsync(s->tok, &next_token, sizeof(int), cudaMemcpyHostToDevice, s->st);
+  set_rows_kernel<<<1, 32, 0, s->st>>>(s->mrows, 1, 0, pos, s->seq_len);
+  s->launches++;
+  mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
+  cudaMemcpyAsync(s->h_draft.data(), s->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) return nullptr;
+  return s->h_draft.data();
+}
+
+static int mtp_prefill_seq(LZRunState* s, int seq, const float* h_host, const float* h_dev, const int* next,
+                           int n, int pos0) {
+  const Cfg& c = s->m->c;
+  for (int done = 0; done < n;) {
+    const int R = std::min(s->Rmax, n - done);
+    cudaMemcpyAsync(s->catch_tok, next + done, R * sizeof(int), cudaMemcpyHostToDevice, s->st);
+    const float* hid = h_dev ? h_dev + (size_t)done * c.d : s->mtpx;
+    if (h_host) {
+      cudaMemcpyAsync(s->hidden, h_host + (size_t)done * c.d, (size_t)R * c.d * 4, cudaMemcpyHostToDevice, s->st);
+      hid = s->hidden;
+    }
+    set_rows_kernel<<<(R + 127) / 128, 128, 0, s->st>>>(s->crows, R, seq, pos0 + done, s->seq_len);
+    s->launches++;
+    mtp_forward(s, R, s->catch_tok, hid, nullptr, s->crows, false, nullptr);
+    done += R;
+  }
+  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : 1;
+}
+
+extern "C" int lz_mtp_prefill(const LZModel* m, LZRunState* s, const float* h_body_all, const int* next_tokens,
+                              int n, int pos0) {
+  if (!m || !s || !h_body_all || !next_tokens || n < 1) return 1;
+  return mtp_prefill_seq(s, 0, h_body_all, nullptr, next_tokens, n, pos0);
+}
+
+extern "C" int lz_mtp_catchup(const LZModel* m, LZRunState* s, const float* h_body_all, const int* next_tokens,
+                              int n, int pos0) {
+  return lz_mtp_prefill(m, s, h_body_all, next_tokens, n, pos0);
+}
+
+// ================================================================== rounds
+
+extern "C" int lz_spec_accept(const int* draft, const int* targ, int n_draft, int bonus, int* out) {
+  if (!draft || !targ || !out || n_draft < 0) return 0;     // src/generate.c:232-243
+  for (int i = 0; i < n_draft; i++) {
+    out[i] = targ[i];
+    if (draft[i] != targ[i]) return i;
+  }
+  out[n_draft] = bonus;
+  return n_draft;
+}
+
+static float host_random_f32(uint64_t* st) {               // src/sampler.c:185-203
+  uint64_t x = *st;
+  x ^= x >> 12; x ^= x << 25; x ^= x >> 27;
+  *st = x;
+  return (float)((unsigned)((x * 0x2545F4914F6CDD1DULL) >> 32) >> 8) / 16777216.0f;
+}
+
+static uint32_t host_fkey(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
+}
+
+extern "C" int lz_spec_accept_temp(const float* p, const float* q, int x, int vocab, float u, uint64_t* rng,
+                                   int* acc) {
+  // src/generate.c:264-349
+  if (!p || !q || !rng || vocab <= 0 || x < 0 || x >= vocab) {
+    if (acc) *acc = 0;
+    return -1;
+  }
+  volatile float qx = q[x], ratio;
+  if (qx <= 0.0f) ratio = 0.0f;
+  else {
+    ratio = p[x] / qx;
+    if (ratio > 1.0f) ratio = 1.0f;
+  }
+  if (u < ratio) {
+    if (acc) *acc = 1;
+    return x;
+  }
+  if (acc) *acc = 0;
+  volatile float total = 0.0f, cdf = 0.0f;
+  int last_pos = -1;
+  for (int i = 0; i < vocab; i++) {
+    volatile float d = p[i] - q[i];
+    if (d > 0.0f) { total = total + d; last_pos = i; }
+  }
+  if (total <= 0.0f) {
+    int mi = 0;
+    uint32_t best = host_fkey(p[0]);
+    for (int i = 1; i < vocab; i++) {
+      uint32_t k = host_fkey(p[i]);
+      if (k > best) { best = k; mi = i; }
+    }
+    return mi;
+  }
+  volatile float coin = host_random_f32(rng) * total;
+  for (int i = 0; i < vocab; i++) {
+    volatile float d = p[i] - q[i];
+    if (d > 0.0f) {
+      cdf = cdf + d;
+      if (coin < cdf) return i;
+    }
+  }
+  return last_pos;
+}
+
+static int run_round(LZRunState* s, int k) {
+  if (s->graphs) {
+    auto it = s->graph.find(k);
+    if (it == s->graph.end()) {
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+      round_greedy(s, k);
+      CK(cudaStreamEndCapture(s->st, &g));
+      cudaGraphExec_t ge;
+      CK(cudaGraphInstantiate(&ge, g, 0));
+      cudaGraphDestroy(g);
+      it = s->graph.emplace(k, ge).first;
+    }
+    CK(cudaGraphLaunch(it->second, s->st));
+  } else {
+    round_greedy(s, k);
+  }
+  return 0;
+}
+
+extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
+                             int n_min, const LZSampler* samp, int debug_break_rollback, int debug_skip_catchup,
+                             int* out, int* out_n_accept, int* out_new_pos, int* out_k_eff, char* errbuf,
+                             int errlen) {
+  if (!m || !s || !out || !out_n_accept || !out_new_pos || !out_k_eff) {
+    set_err(errbuf, errlen, "null argument");
+    return -LZ98_ERR_NULL_ARG;
+  }
+  if (k < 1 || k > 6 || k > s->depth - 1) {
+    set_err(errbuf, errlen, "draft depth out of range");
+    return -LZ98_ERR_SPEC_K_RANGE;
+  }
+  if (p_min != 0.0f || n_min != 0 || debug_break_rollback || debug_skip_catchup ||
+      (samp && samp->temperature > 1e-3f) || s->B != 1) {
+    set_err(errbuf, errlen, "unsupported round options on the device path");
+    return -LZ98_ERR_FORWARD;
+  }
+  sr_down(s);
+  SeqRound& r = s->h_sr[0];
+  r.anchor = anchor;
+  r.anchor_pos = anchor_pos;
+  r.k = k;
+  sr_up(s);
+  if (run_round(s, k)) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return -LZ98_ERR_CUDA;
+  }
+  sr_down(s);
+  if (cudaGetLastError() != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return -LZ98_ERR_CUDA;
+  }
+  const SeqRound& o = s->h_sr[0];
+  for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
+  *out_n_accept = o.n_accept;
+  *out_new_pos = anchor_pos + 1 + o.n_accept;
+  *out_k_eff = k;
+  return o.n_accept + 1;
+}
+
+extern "C" int lz_spec_round_temp(const LZModel*, LZRunState*, int, int, int, float, int, LZSampler*, int, int,
+                                  int*, int*, int*, int*, char* errbuf, int errlen) {
+  set_err(errbuf, errlen, "temperature rounds are not built yet on the device path");
+  return -LZ98_ERR_FORWARD;
+}
+
+extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const int* prompt, int n_prompt,
+                              int* out_anchor, char* errbuf, int errlen) {
+  if (!m || !s || !prompt || n_prompt < 1 || seq < 0 || seq >= s->B || n_prompt >= s->seq_len) {
+    set_err(errbuf, errlen, "bad prefill arguments");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const Cfg& c = m->c;
+  sr_down(s);
+  const int slot = s->h_sr[seq].ssm_slot;
+  int mtp_pos = s->h_sr[seq].mtp_pos;
+  const int n = n_prompt - 1;
+  if (n > 0) {
+    if ((size_t)n > s->hb_rows) {
+      if (s->hb) cudaFree(s->hb);
+      s->hb = nullptr;
+      if (cudaMalloc(&s->hb, (size_t)n * c.d * 4) != cudaSuccess) {
+        set_err(errbuf, errlen, "device allocation failed");
+        return LZ98_ERR_ALLOC;
+      }
+      s->hb_rows = n;
+    }
+    for (int done = 0; done < n;) {
+      const int R = std::min(s->Rmax, n - done);
+      cudaMemcpyAsync(s->tok, prompt + done, R * sizeof(int), cudaMemcpyHostToDevice, s->st);
+      upload_seqs(s, {KdaSeq{0, R, slot, seq}});
+      body_forward(s, R, 1, 0, false);
+      cudaMemcpyAsync(s->hb + (size_t)done * c.d, s->hidden, (size_t)R * c.d * 4, cudaMemcpyDeviceToDevice,
+                      s->st);
+      done += R;
+    }
+    if (mtp_prefill_seq(s, seq, nullptr, s->hb, prompt + 1, n, mtp_pos)) {
+      set_err(errbuf, errlen, "CUDA failure in prefill");
+      return LZ98_ERR_CUDA;
+    }
+    mtp_pos += n;
+  }
+  const int last = prompt[n_prompt - 1];
+  cudaMemcpyAsync(s->tok, &last, sizeof(int), cudaMemcpyHostToDevice, s->st);
+  upload_seqs(s, {KdaSeq{0, 1, slot, seq}});
+  body_forward(s, 1, 1, 0, true);
+  cudaMemcpyAsync(s->chain + (size_t)seq * c.d, s->hidden, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
+  argmax_kernel<<<1, 1024, 0, s->st>>>(s->logits, c.vocab, 0, s->vmax);
+  s->launches++;
+  int anchor = 0;
+  cudaMemcpyAsync(&anchor, s->vmax, sizeof(int), cudaMemcpyDeviceToHost, s->st);
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure in prefill");
+    return LZ98_ERR_CUDA;
+  }
+  SeqRound& r = s->h_sr[seq];
+  r.anchor = anchor;
+  r.anchor_pos = n_prompt - 1;
+  r.mtp_pos = mtp_pos;
+  r.ssm_slot = slot;
+  sr_up(s);
+  cudaStreamSynchronize(s->st);
+  if (out_anchor) *out_anchor = anchor;
+  return 0;
+}
+
+extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* out_tokens, int* out_counts,
+                                   char* errbuf, int errlen) {
+  if (!m || !s) return LZ98_ERR_NULL_ARG;
+  if (k < 1 || k > s->kmax) {
+    set_err(errbuf, errlen, "draft depth out of range");
+    return LZ98_ERR_SPEC_K_RANGE;
+  }
+  if (run_round(s, k)) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return LZ98_ERR_CUDA;
+  }
+  if (out_tokens || out_counts) {
+    sr_down(s);
+    for (int b = 0; b < s->B; b++) {
+      const SeqRound& o = s->h_sr[b];
+      if (out_counts) out_counts[b] = o.n_emit;
+      if (out_tokens)
+        for (int i = 0; i <= k; i++) out_tokens[b * (k + 1) + i] = i <= o.n_accept ? o.out[i] : -1;
+    }
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return LZ98_ERR_CUDA;
+  }
+  return 0;
+}
+
+// The generation loop of src/generate.c:2781-3091 on token ids, greedy,
+// sequence 0.
+extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
+                           int spec_k, float temp, float topp, uint64_t seed, int* out_tok, int out_cap,
+                           int* out_n, int* rounds, int round_cap, int* n_rounds, char* errbuf, int errlen) {
+  (void)topp; (void)seed;
+  if (!m || !s || !prompt || n_prompt < 1 || !out_n || !n_rounds) return LZ98_ERR_NULL_ARG;
+  if (temp > 1e-3f) {
+    set_err(errbuf, errlen, "temperature generation is not built yet on the device path");
+    return LZ98_ERR_FORWARD;
+  }
+  const Cfg& c = m->c;
+  clear_state(s);
+  int max_pos = n_prompt + max_new;
+  if (max_pos > s->seq_len) max_pos = s->seq_len;
+  if (max_pos < n_prompt + 1) max_pos = n_prompt + 1;
+  int n_out = 0, nr = 0;
+  auto emit = [&](int t) { if (n_out < out_cap) out_tok[n_out] = t; n_out++; };
+  int pos = n_prompt - 1, token = prompt[n_prompt - 1];
+  bool have_seed = false;
+  if (spec_k > 0) {
+    int anchor;
+    int rc = lz_seq_prefill(m, s, 0, prompt, n_prompt, &anchor, errbuf, errlen);
+    if (rc) return rc;
+    // lz_seq_prefill already forwarded the last prompt token (the first
+    // round's capture) and picked the anchor.
+    int round_k = spec_k;
+    if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
+    if (round_k > 0) {
+      emit(anchor);
+      token = anchor;
+      pos = pos + 1;
+      have_seed = true;
+    } else {
+      token = anchor;
+      emit(anchor);
+      pos = pos + 1;
+    }
+  } else if (n_prompt > 1) {
+    std::vector<float> hb((size_t)(n_prompt - 1) * c.d);
+    if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, 0, hb.data())) return LZ98_ERR_FORWARD;
+  }
+  while (pos < max_pos - 1) {
+    int round_k = 0;
+    if (spec_k > 0) {
+      round_k = spec_k;
+      if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
+    }
+    if (round_k > 0 && have_seed) {
+      int out[8], n_acc = 0, new_pos = 0, k_eff = 0;
+      int ne = lz_spec_round(m, s, token, pos - 1, round_k, 0.0f, 0, nullptr, 0, 0, out, &n_acc, &new_pos, &k_eff,
+                             errbuf, errlen);
+      if (ne < 0) return -ne;
+      if (rounds && nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_acc; }
+      nr++;
+      for (int ei = 0; ei <= n_acc; ei++) emit(out[ei]);
+      pos = new_pos + 1;
+      token = out[n_acc];
+      continue;
+    }
+    const float* lg = lz_forward(m, s, token, pos);
+    if (!lg) return LZ98_ERR_FORWARD;
+    int mi = 0;
+    uint32_t best = host_fkey(lg[0]);
+    for (int i = 1; i < c.vocab; i++) {
+      uint32_t kk = host_fkey(lg[i]);
+      if (kk > best) { best = kk; mi = i; }
+    }
+    token = mi;
+    emit(token);
+    pos++;
+  }
+  *out_n = n_out;
+  *n_rounds = nr;
+  return 0;
+}

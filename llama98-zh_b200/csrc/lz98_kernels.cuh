@@ -1,0 +1,788 @@
+// CUDA kernels of the MTP speculative-decoding step (sm_100a).
+//
+// Layout in HBM (all row-major):
+//   activations  x  f32 [R][d]           one row per (sequence, position)
+//   quantised    xq i8  [R][K], xs f32 [R][K/32]   (per-32 absmax/127)
+//   Q8_0 weight  W  i8  [N][K], ws f32 [N][K/gs]    (gs = 32 or K)
+//   KDA state    hi/lo i8 [seq][ring][layer][head][64][64],
+//                scale f32 [seq][ring][layer][head][64][2]
+//   conv state   f32 [seq][ring][layer][3*H*64][3]
+//   MTP KV cache kq/vq i8 [seq][pos][kv_dim], ks/vs f32 [seq][pos][kv_dim/32]
+//
+// Every float reduction keeps the reference's order: where the reference
+// sums sequentially the kernel sums sequentially (one lane per chain, the
+// chains of different rows/columns in parallel); integer sums (int8 dot
+// products per 32-element sub-block) are order-free and run as __dp4a.
+#pragma once
+#include "lz98_dev.cuh"
+
+namespace lz98 {
+
+constexpr int kGemvWarps = 4;
+constexpr int kGemvRB = 8;        // token rows per reduction pass
+constexpr int kNsbMax = 256;      // K <= 8192
+
+// ------------------------------------------------------------------ GEMV
+
+// The float reduction of one output element from its per-32 products,
+// src/ops_matmul.c:590-629 / src/ops_epi.c:983-1023:
+//   rb = gs/32 > 1: p[s] = acc[s]*xs[s]; sum over groups of (sum of p in the
+//                   group) * ws[g], both sequential;
+//   rb == 1:        p[s] = acc[s]*(xs[s]*ws[s]); four interleaved
+//                   accumulators combined (a0+a2)+(a1+a3), tail into a0.
+LZ_HD float q8_reduce(const float* p, const float* wsr, int rb, int ng) {
+  if (rb > 1) {
+    float sum = 0.0f;
+    for (int g = 0; g < ng; g++) {
+      float dot = 0.0f;
+      for (int s = 0; s < rb; s++) dot = __fadd_rn(dot, p[g * rb + s]);
+      sum = __fadd_rn(sum, __fmul_rn(dot, wsr[g]));
+    }
+    return sum;
+  }
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  int g = 0;
+  for (; g + 3 < ng; g += 4) {
+    a0 = __fadd_rn(a0, p[g]);
+    a1 = __fadd_rn(a1, p[g + 1]);
+    a2 = __fadd_rn(a2, p[g + 2]);
+    a3 = __fadd_rn(a3, p[g + 3]);
+  }
+  for (; g < ng; g++) a0 = __fadd_rn(a0, p[g]);
+  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+}
+
+LZ_HD int dot32(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
+  int acc = 0;
+  acc = __dp4a(wa.x, xa.x, acc); acc = __dp4a(wa.y, xa.y, acc);
+  acc = __dp4a(wa.z, xa.z, acc); acc = __dp4a(wa.w, xa.w, acc);
+  acc = __dp4a(wb.x, xb.x, acc); acc = __dp4a(wb.y, xb.y, acc);
+  acc = __dp4a(wb.z, xb.z, acc); acc = __dp4a(wb.w, xb.w, acc);
+  return acc;
+}
+
+// Weight-streaming int8 GEMV/skinny GEMM: one warp per output row, each
+// lane owning 32-byte sub-blocks of that row (loaded once, reused for
+// every token row), per-sub-block int32 sums by __dp4a, then one lane per
+// token row runs the reference reduction.
+// mode 0: y = v;  mode 1: y = y + v;  mode 2: y = y + (v + z).
+template <int JM>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv_q8_kernel(const int8_t* __restrict__ W, const float* __restrict__ ws,
+               int N, int K, int gs,
+               const int8_t* __restrict__ xq, const float* __restrict__ xs, int R,
+               float* y, int ldy, int mode, const float* __restrict__ z, int ldz) {
+  __shared__ float P[kGemvWarps][kGemvRB][JM * 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kGemvWarps + warp;
+  if (n >= N) return;
+  const int nsb = K >> 5, rb = gs >> 5, ng = K / gs;
+  const int8_t* wr = W + (size_t)n * K;
+  const float* wsr = ws + (size_t)n * ng;
+  int4 wa[JM], wb[JM];
+#pragma unroll
+  for (int j = 0; j < JM; j++) {
+    int s = lane + 32 * j;
+    if (s < nsb) {
+      wa[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+      wb[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+    }
+  }
+  for (int r0 = 0; r0 < R; r0 += kGemvRB) {
+    const int nr = min(kGemvRB, R - r0);
+    for (int rr = 0; rr < nr; rr++) {
+      const int8_t* xr = xq + (size_t)(r0 + rr) * K;
+      const float* xsr = xs + (size_t)(r0 + rr) * nsb;
+#pragma unroll
+      for (int j = 0; j < JM; j++) {
+        int s = lane + 32 * j;
+        if (s < nsb) {
+          int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+          int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+          float a = (float)dot32(wa[j], wb[j], xa, xb);
+          P[warp][rr][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane < nr) {
+      float v = q8_reduce(P[warp][lane], wsr, rb, ng);
+      const int r = r0 + lane;
+      float* yp = y + (size_t)r * ldy + n;
+      if (mode == 0) *yp = v;
+      else if (mode == 1) *yp = __fadd_rn(*yp, v);
+      else *yp = __fadd_rn(*yp, __fadd_rn(v, z[(size_t)r * ldz + n]));
+    }
+    __syncwarp();
+  }
+}
+
+// --------------------------------------------------------- row kernels
+
+// Serial sum of squares by one thread (src/ops_norm.c:718).
+LZ_HD float seq_sumsq(const float* v, int n) {
+  float ss = 0.0f;
+  for (int i = 0; i < n; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  return ss;
+}
+
+// rmsnorm (1+w) of one row, then per-32 quantisation of the result; the
+// float result is stored too when `out` is non-null.  One block per row.
+// src/ops_norm.c:690-747 and src/ops_quant.c:2152-2282.
+__global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
+                                     const float* __restrict__ w, int n, float eps,
+                                     float* out, int ldo, int8_t* xq, float* xs) {
+  extern __shared__ float sm[];
+  __shared__ float s_inv;
+  const int r = blockIdx.x;
+  const float* xr = x + (size_t)r * ldx;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = xr[i];
+  __syncthreads();
+  if (threadIdx.x == 0) s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, n), (float)n), eps));
+  __syncthreads();
+  const float inv = s_inv;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < n / 32; g += nw) {
+    int i = g * 32 + lane;
+    float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, w[i]));
+    if (out) out[(size_t)r * ldo + i] = o;
+    xq[(size_t)r * n + i] = warp_quant32(o, &xs[(size_t)r * (n / 32) + g]);
+  }
+}
+
+// Embedding rows: x[i] = q[i] * scale[group]  (src/ops_epi.c:1276-1280).
+__global__ void embed_kernel(const int8_t* __restrict__ eq, const float* __restrict__ es,
+                             int gs, int d, const int* __restrict__ tok, float* x) {
+  const int r = blockIdx.x;
+  const size_t base = (size_t)tok[r] * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    x[(size_t)r * d + i] = __fmul_rn((float)eq[base + i], es[(base + i) / gs]);
+}
+
+// silu(gate)*up then per-32 quantisation (src/forward_kda.c:1082-1085
+// followed by lz_quantize_q8).  gate at column g0, up at column u0.
+__global__ void swiglu_quant_kernel(const float* __restrict__ src, int lds, int g0, int u0,
+                                    int n, int8_t* xq, float* xs) {
+  const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const float* row = src + (size_t)r * lds;
+  for (int g = warp; g < n / 32; g += nw) {
+    int i = g * 32 + lane;
+    float a = __fmul_rn(silu(row[g0 + i]), row[u0 + i]);
+    xq[(size_t)r * n + i] = warp_quant32(a, &xs[(size_t)r * (n / 32) + g]);
+  }
+}
+
+// ArgMax with the first index on ties.  p1_mode = 0 compares by the total
+// key of src/sampler.c:224-240; p1_mode = 1 by float `>` (lz_argmax_p1,
+// src/sampler.c:279-295), i.e. -0 and +0 compare equal.
+__global__ void argmax_kernel(const float* __restrict__ logits, int V, int p1_mode, int* out) {
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * V;
+  uint32_t bk = 0;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = row[i];
+    if (p1_mode && v == 0.0f) v = 0.0f;
+    uint32_t k = fkey(v);
+    if (bi == 0x7fffffff || k > bk) { bk = k; bi = i; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
+    int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (k2 > bk || (k2 == bk && i2 < bi)) { bk = k2; bi = i2; }
+  }
+  __shared__ uint32_t sk[32];
+  __shared__ int si[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { sk[warp] = bk; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    int nw = blockDim.x >> 5;
+    bk = lane < nw ? sk[lane] : 0;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (k2 > bk || (k2 == bk && i2 < bi)) { bk = k2; bi = i2; }
+    }
+    if (lane == 0) out[r] = bi;
+  }
+}
+
+// ---------------------------------------------------------------- KDA
+
+struct KdaSeq {            // one sequence's rows inside a forward batch
+  int row0, nrows, base_slot, seq;
+};
+
+// f_b_proj of every token (quantised f_a latent, src/forward_kda.c:773-819)
+// then the per-channel decay gate gt = exp(lb * sigmoid(exp(A_log[h]) *
+// (pre + dt_bias))) (src/forward_kda.c:277-297, 847-851).
+__global__ void kda_fb_gate_kernel(const float* __restrict__ inproj, int ldi, int off_fa, int rank,
+                                   const int8_t* __restrict__ fbq, const float* __restrict__ fbs, int fb_gs,
+                                   const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                   float lb, int nvk, int kd, float* gate) {
+  __shared__ __align__(16) int8_t lq[256];
+  __shared__ float ls[8];
+  const int r = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < rank / 32; g += nw) {
+    float v = inproj[(size_t)r * ldi + off_fa + g * 32 + lane];
+    lq[g * 32 + lane] = warp_quant32(v, &ls[g]);
+  }
+  __syncthreads();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= nvk) return;
+  const int nsb = rank / 32, rb = fb_gs / 32, ng = rank / fb_gs;
+  float p[8];
+  const int8_t* wr = fbq + (size_t)j * rank;
+  const float* wsr = fbs + (size_t)j * ng;
+  for (int s = 0; s < nsb; s++) {
+    int4 wa = *reinterpret_cast<const int4*>(wr + s * 32);
+    int4 wb = *reinterpret_cast<const int4*>(wr + s * 32 + 16);
+    int4 xa = *reinterpret_cast<const int4*>(lq + s * 32);
+    int4 xb = *reinterpret_cast<const int4*>(lq + s * 32 + 16);
+    float a = (float)dot32(wa, wb, xa, xb);
+    p[s] = rb > 1 ? __fmul_rn(a, ls[s]) : __fmul_rn(a, __fmul_rn(ls[s], wsr[s]));
+  }
+  float pre = __fadd_rn(q8_reduce(p, wsr, rb, ng), dt_bias[j]);
+  float decay = exp_body(a_log[j / kd]);
+  float g = __fmul_rn(lb, sigmoid(__fmul_rn(decay, pre)));
+  gate[(size_t)r * nvk + j] = exp_body(g);
+}
+
+// Depthwise causal conv1d (kernel 4) + SiLU over q, k and v channels,
+// token-serial per sequence through the state ring (src/ops_conv1d.c:26-53,
+// src/forward_kda.c:680-749).  adv = 1: token t reads slot base+t and
+// writes slot base+t+1; adv = 0: one slot, updated in place.
+__global__ void kda_conv_kernel(const float* __restrict__ inproj, int ldi, int conv_dim,
+                                const float* __restrict__ cw, const KdaSeq* __restrict__ seqs,
+                                float* conv_state, size_t seq_stride, size_t slot_stride,
+                                int depth, int adv, float* out, int ldo) {
+  const KdaSeq sq = seqs[blockIdx.y];
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= conv_dim) return;
+  float* st0 = conv_state + (size_t)sq.seq * seq_stride + (size_t)c * 3;
+  const float* st = st0 + (size_t)sq.base_slot * slot_stride;
+  float h0 = st[0], h1 = st[1], h2 = st[2];
+  const float w0 = cw[c * 4], w1 = cw[c * 4 + 1], w2 = cw[c * 4 + 2], w3 = cw[c * 4 + 3];
+  for (int t = 0; t < sq.nrows; t++) {
+    const int r = sq.row0 + t;
+    const float xv = inproj[(size_t)r * ldi + c];
+    float sum = 0.0f;
+    sum = __fadd_rn(sum, __fmul_rn(w0, h0));
+    sum = __fadd_rn(sum, __fmul_rn(w1, h1));
+    sum = __fadd_rn(sum, __fmul_rn(w2, h2));
+    sum = __fadd_rn(sum, __fmul_rn(w3, xv));
+    out[(size_t)r * ldo + c] = silu(sum);
+    h0 = h1; h1 = h2; h2 = xv;
+    if (adv) {
+      int so = (sq.base_slot + t + 1) % depth;
+      float* d = st0 + (size_t)so * slot_stride;
+      d[0] = h0; d[1] = h1; d[2] = h2;
+    }
+  }
+  if (!adv) {
+    float* d = st0 + (size_t)sq.base_slot * slot_stride;
+    d[0] = h0; d[1] = h1; d[2] = h2;
+  }
+}
+
+// The KDA recurrence of one (sequence, head), token-serial, with the 64x64
+// two-plane int8 state resident in shared memory: l2norm(q)*kd^-1/2,
+// l2norm(k), beta = sigmoid(b), pass 1 (u = S^T(g.k), w = S^T(g.q),
+// kq = k.q, all sequential over the 64 state rows), pass 2 (each state row
+// g*S + k*u requantised in two planes), then the gated RMSNorm of the head
+// output and its per-32 quantisation for o_proj.
+// src/forward_kda.c:856-936 and 1029-1040, src/ops_gdn.c:2488-2778,
+// src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
+constexpr int kRecurThreads = 512;
+__global__ void __launch_bounds__(kRecurThreads)
+kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
+                 const float* __restrict__ inproj, int ldi, int off_b, int off_g,
+                 const float* __restrict__ gate, int nvk,
+                 const KdaSeq* __restrict__ seqs,
+                 int8_t* st_hi, int8_t* st_lo, float* st_sc,
+                 size_t seq_stride_q, size_t slot_stride_q, int layer_off_q,
+                 int depth, int adv, float ssm_scale,
+                 const float* __restrict__ o_norm, float eps, int vdim,
+                 int8_t* oq, float* os) {
+  constexpr int KD = 64, VD = 64;
+  __shared__ __align__(16) int8_t hi[KD][VD];
+  __shared__ __align__(16) int8_t lo[KD][VD];
+  __shared__ float sc[KD][2];
+  __shared__ float qn[KD], kn[KD], gv[KD], U[VD], OUT[VD], s_misc[4];
+  const KdaSeq sq = seqs[blockIdx.y];
+  const int h = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t head_off = (size_t)layer_off_q + (size_t)h * KD * VD;
+  const size_t seq_off = (size_t)sq.seq * seq_stride_q;
+  {
+    const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
+    const int4* sh = reinterpret_cast<const int4*>(st_hi + off);
+    const int4* sl = reinterpret_cast<const int4*>(st_lo + off);
+    for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
+      reinterpret_cast<int4*>(&hi[0][0])[i] = sh[i];
+      reinterpret_cast<int4*>(&lo[0][0])[i] = sl[i];
+    }
+    const float* ss = st_sc + off / 32;
+    for (int i = tid; i < KD * 2; i += blockDim.x) (&sc[0][0])[i] = ss[i];
+  }
+  __syncthreads();
+  for (int t = 0; t < sq.nrows; t++) {
+    const int r = sq.row0 + t;
+    const float* qc = conv_out + (size_t)r * ldc + h * KD;
+    const float* kc = conv_out + (size_t)r * ldc + kdim + h * KD;
+    if (tid == 0) s_misc[0] = rsqrt_body(__fadd_rn(seq_sumsq(qc, KD), kL2Eps));
+    if (tid == 32) s_misc[1] = rsqrt_body(__fadd_rn(seq_sumsq(kc, KD), kL2Eps));
+    if (tid == 64) s_misc[2] = sigmoid(inproj[(size_t)r * ldi + off_b + h]);
+    __syncthreads();
+    if (tid < KD) {
+      qn[tid] = __fmul_rn(__fmul_rn(qc[tid], s_misc[0]), ssm_scale);
+      kn[tid] = __fmul_rn(kc[tid], s_misc[1]);
+      gv[tid] = gate[(size_t)r * nvk + h * KD + tid];
+    }
+    __syncthreads();
+    if (tid < VD) {
+      const int vv = tid, grp = vv >> 5;
+      float u = 0.0f, w = 0.0f, kq = 0.0f;
+      for (int kk = 0; kk < KD; kk++) {
+        const float kcv = kn[kk], qcv = qn[kk];
+        const float kcw = __fmul_rn(kcv, gv[kk]), qcw = __fmul_rn(qcv, gv[kk]);
+        kq = __fadd_rn(kq, __fmul_rn(kcv, qcv));
+        const float sck = __fmul_rn(sc[kk][grp], kcw), scq = __fmul_rn(sc[kk][grp], qcw);
+        const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+        u = __fadd_rn(u, __fmul_rn(e, sck));
+        w = __fadd_rn(w, __fmul_rn(e, scq));
+      }
+      const float vval = conv_out[(size_t)r * ldc + 2 * kdim + h * VD + vv];
+      u = __fmul_rn(__fsub_rn(vval, u), s_misc[2]);
+      U[vv] = u;
+      OUT[vv] = __fadd_rn(w, __fmul_rn(u, kq));
+    }
+    __syncthreads();
+    for (int unit = warp; unit < KD * 2; unit += blockDim.x >> 5) {
+      const int kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
+      const float scg = __fmul_rn(sc[kk][grp], gv[kk]);
+      const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+      const float buf = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[kk], U[vv]));
+      const uint32_t am = warp_max_u32(abs_bits(buf));
+      float sg, inv;
+      q8_scale_from_amax(am, &sg, &inv);
+      const float f = __fmul_rn(buf, inv);
+      int hq = q8_clamp(q8_round(f));
+      float res = __fsub_rn(f, (float)hq);
+      if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
+      else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
+      __syncwarp();
+      hi[kk][vv] = (int8_t)hq;
+      lo[kk][vv] = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
+      if (lane == 0) sc[kk][grp] = sg;
+    }
+    __syncthreads();
+    if (adv) {
+      const int so = (sq.base_slot + t + 1) % depth;
+      const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
+      int4* dh = reinterpret_cast<int4*>(st_hi + off);
+      int4* dl = reinterpret_cast<int4*>(st_lo + off);
+      for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
+        dh[i] = reinterpret_cast<const int4*>(&hi[0][0])[i];
+        dl[i] = reinterpret_cast<const int4*>(&lo[0][0])[i];
+      }
+      float* ds = st_sc + off / 32;
+      for (int i = tid; i < KD * 2; i += blockDim.x) ds[i] = (&sc[0][0])[i];
+    }
+    // gated RMSNorm of the head output, then per-32 quantisation.
+    if (tid == 0) s_misc[3] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT, VD), (float)VD), eps));
+    __syncthreads();
+    if (tid < VD) {
+      const float zg = inproj[(size_t)r * ldi + off_g + h * VD + tid];
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[tid], s_misc[3]), o_norm[tid]), silu(zg));
+      oq[(size_t)r * vdim + h * VD + tid] =
+          warp_quant32(o, &os[(size_t)r * (vdim / 32) + (h * VD) / 32 + (tid >> 5)]);
+    }
+    __syncthreads();
+  }
+  if (!adv) {
+    const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
+    int4* dh = reinterpret_cast<int4*>(st_hi + off);
+    int4* dl = reinterpret_cast<int4*>(st_lo + off);
+    for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
+      dh[i] = reinterpret_cast<const int4*>(&hi[0][0])[i];
+      dl[i] = reinterpret_cast<const int4*>(&lo[0][0])[i];
+    }
+    float* ds = st_sc + off / 32;
+    for (int i = tid; i < KD * 2; i += blockDim.x) ds[i] = (&sc[0][0])[i];
+  }
+}
+
+// ---------------------------------------------------------------- MoE
+
+// Router of one token row per warp: sigmoid scores, key = score + bias,
+// top-k by key (first index on ties), weights = scores renormalised by
+// their sequential sum in selection order (src/ops_moe.c:12-163); then
+// the per-32 quantisation of the row's latent (src/forward_moe.c:150).
+__global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
+                                 const float* __restrict__ bias, int E, int topk, int latent,
+                                 int* pair_expert, float* pair_w, int8_t* latq, float* lats) {
+  const int r = blockIdx.x, lane = threadIdx.x;
+  float score[8], key[8];
+  const int nj = (E + 31) / 32;
+  for (int j = 0; j < nj; j++) {
+    int e = lane + 32 * j;
+    if (e < E) {
+      score[j] = sigmoid(moein[(size_t)r * ldm + off_router + e]);
+      key[j] = __fadd_rn(score[j], bias[e]);
+    } else {
+      score[j] = 0.0f;
+      key[j] = -1e30f;
+    }
+  }
+  float wsel[16];
+  int isel[16];
+  float wsum = 0.0f;
+  for (int t = 0; t < topk; t++) {
+    uint32_t bk = 0;
+    int bi = 0x7fffffff;
+    for (int j = 0; j < nj; j++) {
+      int e = lane + 32 * j;
+      if (e < E && key[j] > -1e30f) {
+        uint32_t k = fkey(key[j]);
+        if (bi == 0x7fffffff || k > bk) { bk = k; bi = e; }
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (i2 != 0x7fffffff && (bi == 0x7fffffff || k2 > bk || (k2 == bk && i2 < bi))) { bk = k2; bi = i2; }
+    }
+    float sw = 0.0f;
+    if (bi != 0x7fffffff && (bi & 31) == lane) {
+      sw = score[bi >> 5];
+      key[bi >> 5] = -1e30f;
+    }
+    sw = __shfl_sync(0xffffffffu, sw, bi == 0x7fffffff ? 0 : (bi & 31));
+    isel[t] = bi == 0x7fffffff ? -1 : bi;
+    wsel[t] = bi == 0x7fffffff ? 0.0f : sw;
+    wsum = __fadd_rn(wsum, wsel[t]);
+  }
+  if (lane == 0) {
+    for (int t = 0; t < topk; t++) {
+      pair_expert[r * topk + t] = isel[t];
+      pair_w[r * topk + t] = (wsum > 0.0f && isel[t] >= 0) ? __fdiv_rn(wsel[t], wsum) : wsel[t];
+    }
+  }
+  for (int g = 0; g < latent / 32; g++) {
+    float v = moein[(size_t)r * ldm + off_lat + g * 32 + lane];
+    latq[(size_t)r * latent + g * 32 + lane] = warp_quant32(v, &lats[(size_t)r * (latent / 32) + g]);
+  }
+}
+
+// One (token, expert) pair, 32 consecutive FFN outputs of w1 and of w3:
+// int8 GEMV over the pair's quantised latent, silu(w1.x)*(w3.x), and the
+// per-32 quantisation of that group (src/forward_moe.c:189-196).
+// w13 is the expert's [w1 rows; w3 rows] ([2*ffn][latent]).
+__global__ void __launch_bounds__(256)
+moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent, int gs,
+               const int* __restrict__ pair_expert, int topk,
+               const int8_t* __restrict__ latq, const float* __restrict__ lats,
+               int8_t* hq, float* hs) {
+  __shared__ float P[8][32];
+  __shared__ float H[64];
+  const int p = blockIdx.y, r = p / topk;
+  const int e = pair_expert[p];
+  if (e < 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsb = latent / 32, rb = gs / 32, ng = latent / gs;
+  const int8_t* xr = latq + (size_t)r * latent;
+  const float* xsr = lats + (size_t)r * nsb;
+  const size_t wbase = (size_t)e * 2 * ffn * latent;
+  const size_t sbase = (size_t)e * 2 * ffn * ng;
+  for (int k = 0; k < 8; k++) {
+    const int lr = warp * 8 + k;                     // 0..63 within the block
+    const int orow = (lr < 32) ? blockIdx.x * 32 + lr : ffn + blockIdx.x * 32 + (lr - 32);
+    const int8_t* wr = w13q + wbase + (size_t)orow * latent;
+    const float* wsr = w13s + sbase + (size_t)orow * ng;
+    for (int s = lane; s < nsb; s += 32) {
+      int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+      int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+      int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+      int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+      float a = (float)dot32(wa, wb, xa, xb);
+      P[warp][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+    }
+    __syncwarp();
+    if (lane == 0) H[lr] = q8_reduce(P[warp], wsr, rb, ng);
+    __syncwarp();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float a = __fmul_rn(silu(H[lane]), H[32 + lane]);
+    const int i = blockIdx.x * 32 + lane;
+    hq[(size_t)p * ffn + i] = warp_quant32(a, &hs[(size_t)p * (ffn / 32) + blockIdx.x]);
+  }
+}
+
+// w2 (latent x ffn) of every pair, one warp per output row.
+__global__ void __launch_bounds__(256)
+moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int ffn, int latent, int gs,
+              const int* __restrict__ pair_expert,
+              const int8_t* __restrict__ hq, const float* __restrict__ hs, float* h2) {
+  __shared__ float P[8][kNsbMax];
+  const int p = blockIdx.y;
+  const int e = pair_expert[p];
+  if (e < 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  if (n >= latent) return;
+  const int nsb = ffn / 32, rb = gs / 32, ng = ffn / gs;
+  const int8_t* wr = w2q + ((size_t)e * latent + n) * ffn;
+  const float* wsr = w2s + ((size_t)e * latent + n) * ng;
+  const int8_t* xr = hq + (size_t)p * ffn;
+  const float* xsr = hs + (size_t)p * nsb;
+  for (int s = lane; s < nsb; s += 32) {
+    int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+    int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+    int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+    int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+    float a = (float)dot32(wa, wb, xa, xb);
+    P[warp][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+  }
+  __syncwarp();
+  if (lane == 0) h2[(size_t)p * latent + n] = q8_reduce(P[warp], wsr, rb, ng);
+}
+
+// lat_y = sum over the row's selected experts, in selection order, of
+// w * h2 (src/forward_moe.c:198-199), then its per-32 quantisation.
+__global__ void moe_combine_kernel(const float* __restrict__ h2, const float* __restrict__ pair_w,
+                                   const int* __restrict__ pair_expert, int topk, int latent,
+                                   int8_t* yq, float* ys) {
+  const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < latent / 32; g += nw) {
+    const int i = g * 32 + lane;
+    float acc = 0.0f;
+    for (int t = 0; t < topk; t++) {
+      const int p = r * topk + t;
+      if (pair_expert[p] < 0) continue;
+      acc = __fadd_rn(acc, __fmul_rn(pair_w[p], h2[(size_t)p * latent + i]));
+    }
+    yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
+  }
+}
+
+// ---------------------------------------------------------------- MTP
+
+// fc input of the draft head for one row: [rmsnorm_e(embed(tok)) |
+// rmsnorm_h(hidden)] quantised per 32 (src/forward_mtp.c:53-67, 580-597).
+__global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __restrict__ es, int egs,
+                                 int d, const int* __restrict__ tok,
+                                 const float* __restrict__ hid, const int* __restrict__ hid_idx,
+                                 const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
+                                 int8_t* xq, float* xs) {
+  extern __shared__ float sm[];           // [2][d]
+  __shared__ float s_inv[2];
+  const int r = blockIdx.x;
+  const int hr = hid_idx ? hid_idx[r] : r;
+  const size_t base = (size_t)tok[r] * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    sm[i] = __fmul_rn((float)eq[base + i], es[(base + i) / egs]);
+    sm[d + i] = hid[(size_t)hr * d + i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_inv[0] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, d), (float)d), eps));
+  if (threadIdx.x == 32) s_inv[1] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm + d, d), (float)d), eps));
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < 2 * d / 32; g += nw) {
+    const int i = g * 32 + lane;
+    const int half = i >= d;
+    const int ii = half ? i - d : i;
+    const float wv = half ? w_h[ii] : w_e[ii];
+    const float o = __fmul_rn(__fmul_rn(sm[i], s_inv[half]), __fadd_rn(1.0f, wv));
+    xq[(size_t)r * 2 * d + i] = warp_quant32(o, &xs[(size_t)r * (2 * d / 32) + g]);
+  }
+}
+
+// Per-head RMSNorm (1+w) then RoPE of the first rot dims, in place on a
+// 64-wide shared vector; called by one warp pair (64 threads).
+LZ_HD void head_norm_rope(float* v, const float* w, float eps, int hd, int rot,
+                          const float* cs_row, float* s_inv) {
+  const int i = threadIdx.x;
+  if (i == 0) *s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(v, hd), (float)hd), eps));
+  __syncthreads();
+  float o = 0.0f;
+  if (i < hd) o = __fmul_rn(__fmul_rn(v[i], *s_inv), __fadd_rn(1.0f, w[i]));
+  __syncthreads();
+  if (i < hd) v[i] = o;
+  __syncthreads();
+  const int half = rot / 2;
+  float nv = 0.0f;
+  if (i < half) {
+    const float c = cs_row[2 * i], sn = cs_row[2 * i + 1];
+    nv = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + half], sn));
+  } else if (i < rot) {
+    const int j = i - half;
+    const float c = cs_row[2 * j], sn = cs_row[2 * j + 1];
+    nv = __fadd_rn(__fmul_rn(v[i], c), __fmul_rn(v[j], sn));
+  }
+  __syncthreads();
+  if (i < rot) v[i] = nv;
+  __syncthreads();
+}
+
+struct MtpRow {            // one draft / prefill row of the MTP block
+  int seq, pos, active;
+};
+
+// K/V side of the MTP attention for one (row, kv head): k RMSNorm, RoPE,
+// Q8 write of k and v into the row's sequence cache at `pos`
+// (src/forward_attn.c:909-965).
+__global__ void mtp_kv_write_kernel(const float* __restrict__ qkv, int ldq, int off_k, int off_v,
+                                    const MtpRow* __restrict__ rows, const float* __restrict__ k_norm,
+                                    float eps, int hd, int rot, int kvd, const float* __restrict__ rope_cs,
+                                    int8_t* kq, float* ks, int8_t* vq, float* vs,
+                                    size_t cache_seq_stride) {
+  __shared__ float v[64];
+  __shared__ float s_inv;
+  const int h = blockIdx.x, r = blockIdx.y;
+  const MtpRow row = rows[r];
+  if (!row.active) return;
+  const int i = threadIdx.x;
+  v[i] = qkv[(size_t)r * ldq + off_k + h * hd + i];
+  __syncthreads();
+  head_norm_rope(v, k_norm, eps, hd, rot, rope_cs + (size_t)row.pos * rot, &s_inv);
+  const size_t cb = (size_t)row.seq * cache_seq_stride + (size_t)row.pos * kvd;
+  const size_t sb = ((size_t)row.seq * cache_seq_stride + (size_t)row.pos * kvd) / 32;
+  kq[cb + h * hd + i] = warp_quant32(v[i], &ks[sb + (h * hd) / 32 + (i >> 5)]);
+  const float vv = qkv[(size_t)r * ldq + off_v + h * hd + i];
+  vq[cb + h * hd + i] = warp_quant32(vv, &vs[sb + (h * hd) / 32 + (i >> 5)]);
+}
+
+// Gated attention of one (row, head) over the row's MTP cache t <= pos:
+// q RMSNorm + RoPE, Q8 scores (32-element partial sums, sequential), the
+// reference softmax (sequential sum), weighted V sum (sequential over t),
+// times sigmoid(gate), then per-32 quantisation for o_proj.
+// src/forward_attn.c:17-41, 206-640, src/ops_norm.c:903-985.
+__global__ void mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
+                                const MtpRow* __restrict__ rows, const float* __restrict__ q_norm,
+                                float eps, int hd, int rot, int kvd, int kv_mul,
+                                const float* __restrict__ rope_cs, float scale,
+                                const int8_t* __restrict__ kq, const float* __restrict__ ks,
+                                const int8_t* __restrict__ vq, const float* __restrict__ vs,
+                                size_t cache_seq_stride, int8_t* aq, float* as) {
+  extern __shared__ float att[];
+  __shared__ float qh[64];
+  __shared__ float s_red[2];
+  const int h = blockIdx.x, r = blockIdx.y;
+  const MtpRow row = rows[r];
+  if (!row.active) return;
+  const int i = threadIdx.x;
+  const int kvh = h / kv_mul;
+  const int pos = row.pos;
+  if (i < hd) qh[i] = qkv[(size_t)r * ldq + (size_t)h * 2 * hd + i];
+  __syncthreads();
+  head_norm_rope(qh, q_norm, eps, hd, rot, rope_cs + (size_t)pos * rot, &s_red[0]);
+  const size_t cb = (size_t)row.seq * cache_seq_stride;
+  for (int t = i; t <= pos; t += blockDim.x) {
+    const int8_t* kt = kq + cb + (size_t)t * kvd + kvh * hd;
+    const float* kts = ks + (cb + (size_t)t * kvd + kvh * hd) / 32;
+    float sum = 0.0f;
+    for (int dd = 0; dd < hd; dd += 32) {
+      float acc = 0.0f;
+      for (int e = 0; e < 32; e++) acc = __fadd_rn(acc, __fmul_rn(qh[dd + e], (float)kt[dd + e]));
+      sum = __fadd_rn(sum, __fmul_rn(acc, kts[dd >> 5]));
+    }
+    att[t] = __fmul_rn(sum, scale);
+  }
+  __syncthreads();
+  uint32_t bk = 0;
+  for (int t = i; t <= pos; t += blockDim.x) { uint32_t k = fkey(att[t]); bk = k > bk ? k : bk; }
+  bk = warp_max_u32(bk);
+  __shared__ uint32_t wk[32];
+  if ((i & 31) == 0) wk[i >> 5] = bk;
+  __syncthreads();
+  if (i == 0) {
+    uint32_t m = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = wk[w] > m ? wk[w] : m;
+    const uint32_t u = (m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m;
+    s_red[1] = __uint_as_float(u);
+  }
+  __syncthreads();
+  const float mx = s_red[1];
+  for (int t = i; t <= pos; t += blockDim.x) att[t] = exp_body(__fsub_rn(att[t], mx));
+  __syncthreads();
+  if (i == 0) {
+    float sum = 0.0f;
+    for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, att[t]);
+    s_red[0] = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
+  }
+  __syncthreads();
+  const float inv = s_red[0];
+  for (int t = i; t <= pos; t += blockDim.x) att[t] = __fmul_rn(att[t], inv);
+  __syncthreads();
+  if (i < hd) {
+    float out = 0.0f;
+    for (int t = 0; t <= pos; t++) {
+      const size_t o = cb + (size_t)t * kvd + kvh * hd + i;
+      out = __fadd_rn(out, __fmul_rn(__fmul_rn(att[t], (float)vq[o]), vs[o / 32]));
+    }
+    out = __fmul_rn(out, sigmoid(qkv[(size_t)r * ldq + (size_t)h * 2 * hd + hd + i]));
+    aq[(size_t)r * qd + h * hd + i] = warp_quant32(out, &as[(size_t)r * (qd / 32) + (h * hd) / 32 + (i >> 5)]);
+  }
+}
+
+// ------------------------------------------------------- spec rounds
+
+struct SeqRound {          // per-sequence round bookkeeping on the device
+  int anchor, anchor_pos, mtp_pos, ssm_slot;
+  int k, n_accept, n_emit, done;
+  int draft[8], out[8];
+};
+
+// Greedy acceptance of one round (src/generate.c:232-243, 798-991): the
+// verify argmax of every row, accept the agreeing draft prefix, point
+// the state ring at the accepted slot, reseed the draft chain from the
+// verify hidden row n_accept, set up the catch-up rows and advance the
+// MTP position.
+__global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax, const int* __restrict__ vmax,
+                                          const float* __restrict__ vhid, int d, float* chain,
+                                          int depth, int seq_len, MtpRow* catch_rows, int* catch_tok,
+                                          int* catch_hidx) {
+  const int b = blockIdx.x;
+  if (b >= nseq) return;
+  SeqRound& s = sr[b];
+  const int k = s.k;
+  const int row0 = b * (kmax + 1);
+  __shared__ int n_acc_s;
+  if (threadIdx.x == 0) {
+    int n_accept = k;
+    for (int i = 0; i < k; i++) {
+      s.out[i] = vmax[row0 + i];
+      if (s.draft[i] != s.out[i]) { n_accept = i; break; }
+    }
+    if (n_accept == k) s.out[k] = vmax[row0 + k];
+    s.n_accept = n_accept;
+    s.n_emit = n_accept + 1;
+    s.ssm_slot = (s.ssm_slot + n_accept + 1) % depth;
+    for (int j = 0; j < kmax - 1; j++) {
+      MtpRow cr;
+      cr.seq = b;
+      cr.pos = s.mtp_pos + 1 + j;
+      cr.active = j < n_accept - 1 && cr.pos < seq_len;
+      catch_rows[b * (kmax - 1) + j] = cr;
+      catch_tok[b * (kmax - 1) + j] = s.out[j < 8 ? j : 0];
+      catch_hidx[b * (kmax - 1) + j] = row0 + j;
+    }
+    s.mtp_pos += n_accept;
+    s.anchor = s.out[n_accept];
+    s.anchor_pos = s.anchor_pos + 1 + n_accept;
+    n_acc_s = n_accept;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    chain[(size_t)b * d + i] = vhid[(size_t)(row0 + n_acc_s) * d + i];
+}
+
+}  // namespace lz98

@@ -1,0 +1,251 @@
+"""Python binding of the C ABI in include/lz98_gpu.h (liblz98gpu.so, built
+in-tree by build.py).  Mirrors the reference's entry points on the MTP
+speculative-decoding path: lz_open, lz_state_alloc, lz_forward*,
+lz_mtp_draft_step, lz_mtp_prefill, lz_spec_round, lz_spec_accept(_temp),
+plus the batched round.  There is no CPU fallback: loading fails loudly
+when the library is missing or no CUDA device is visible."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SO = os.path.join(HERE, "liblz98gpu.so")
+
+c_int, c_float, c_void_p, c_char_p = ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_char_p
+P = ctypes.POINTER
+
+_lib = None
+
+
+class LzError(RuntimeError):
+    pass
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(c_void_p)
+
+
+def lib():
+    """Load liblz98gpu.so and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(SO):
+        raise LzError(f"{SO} is missing: build it with llama98-zh_b200/build.py (nvcc, sm_100a)")
+    L = ctypes.CDLL(SO)
+    sig = {
+        "lz_open": (c_int, [P(c_void_p), c_char_p, c_char_p, c_int]),
+        "lz_free": (None, [c_void_p]),
+        "lz_model_info": (None, [c_void_p, c_void_p]),
+        "lz_model_weight_bytes": (ctypes.c_size_t, [c_void_p]),
+        "lz_state_alloc": (c_int, [P(c_void_p), c_void_p, c_int, c_int, c_char_p, c_int]),
+        "lz_state_alloc_batch": (c_int, [P(c_void_p), c_void_p, c_int, c_int, c_int, c_char_p, c_int]),
+        "lz_state_reset": (None, [c_void_p, c_void_p]),
+        "lz_state_free": (None, [c_void_p]),
+        "lz_state_get": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int)]),
+        "lz_state_set": (c_int, [c_void_p, c_int, c_int, c_int]),
+        "lz_state_get_chain": (c_int, [c_void_p, c_int, c_void_p]),
+        "lz_state_set_chain": (c_int, [c_void_p, c_int, c_void_p]),
+        "lz_forward": (P(c_float), [c_void_p, c_void_p, c_int, c_int]),
+        "lz_forward_capture": (P(c_float), [c_void_p, c_void_p, c_int, c_int]),
+        "lz_forward_batch_capture": (P(c_float), [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+        "lz_forward_verify": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
+        "lz_state_mtp_logits": (P(c_float), [c_void_p]),
+        "lz_state_mtp_verify_hidden": (P(c_float), [c_void_p]),
+        "lz_mtp_draft_step": (P(c_float), [c_void_p, c_void_p, c_int, c_int]),
+        "lz_mtp_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+        "lz_mtp_catchup": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+        "lz_spec_round": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p,
+                                  c_int, c_int, c_void_p, P(c_int), P(c_int), P(c_int), c_char_p, c_int]),
+        "lz_spec_round_temp": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p,
+                                       c_int, c_int, c_void_p, P(c_int), P(c_int), P(c_int), c_char_p, c_int]),
+        "lz_spec_accept": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+        "lz_spec_accept_temp": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float,
+                                        P(ctypes.c_uint64), P(c_int)]),
+        "lz_seq_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, P(c_int), c_char_p, c_int]),
+        "lz_spec_round_batch": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
+        "lz_set_graphs": (c_int, [c_void_p, c_int]),
+        "lz_generate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
+                                c_char_p, c_int]),
+        "lz_state_stream": (c_void_p, [c_void_p]),
+        "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+           "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
+           "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
+           "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
+           "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
+           "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
+           "lz_seq_prefill", "lz_spec_round_batch", "lz_set_graphs", "lz_generate", "lz_state_stream",
+           "lz_state_launches"]
+
+
+class Model:
+    def __init__(self, model_dir: str):
+        L = lib()
+        h = c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = L.lz_open(ctypes.byref(h), model_dir.encode(), err, 512)
+        if rc:
+            raise LzError(f"lz_open failed ({rc}): {err.value.decode()}")
+        self.h = h
+        info = np.zeros(16, np.int32)
+        L.lz_model_info(h, _ptr(info))
+        (self.vocab, self.hidden, self.n_layers, self.kda_heads, self.key_dim, self.latent,
+         self.n_experts, self.top_k, self.shared_w, self.head_dim, self.n_heads, self.n_kv_heads,
+         self.rotary_dim, self.seq_len_cfg, self.mtp_ffn, self.moe_ffn) = [int(x) for x in info]
+        self.weight_bytes = int(L.lz_model_weight_bytes(h))
+
+    def close(self):
+        if self.h:
+            lib().lz_free(self.h)
+            self.h = None
+
+
+class State:
+    def __init__(self, model: Model, seq_len: int, spec_k_max: int, n_seq: int = 1):
+        L = lib()
+        h = c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = L.lz_state_alloc_batch(ctypes.byref(h), model.h, n_seq, seq_len, spec_k_max, err, 512)
+        if rc:
+            raise LzError(f"lz_state_alloc failed ({rc}): {err.value.decode()}")
+        self.h, self.m, self.n_seq, self.k_max = h, model, n_seq, spec_k_max
+
+    def close(self):
+        if self.h:
+            lib().lz_state_free(self.h)
+            self.h = None
+
+    def reset(self):
+        lib().lz_state_reset(self.h, self.m.h)
+
+    def positions(self, seq=0):
+        a, b, c = c_int(), c_int(), c_int()
+        lib().lz_state_get(self.h, seq, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return a.value, b.value, c.value
+
+    def set_positions(self, seq=0, mtp_pos=-1, ssm_slot=-1):
+        lib().lz_state_set(self.h, seq, mtp_pos, ssm_slot)
+
+    def chain(self, seq=0):
+        c = np.zeros(self.m.hidden, np.float32)
+        lib().lz_state_get_chain(self.h, seq, _ptr(c))
+        return c
+
+    def set_chain(self, c, seq=0):
+        c = np.ascontiguousarray(c, np.float32)
+        lib().lz_state_set_chain(self.h, seq, _ptr(c))
+
+    def launches(self):
+        return int(lib().lz_state_launches(self.h))
+
+    def graphs(self, on: bool):
+        lib().lz_set_graphs(self.h, int(on))
+
+    # --- forwards of sequence 0
+    def forward(self, tok, pos, capture=False):
+        fn = lib().lz_forward_capture if capture else lib().lz_forward
+        p = fn(self.m.h, self.h, int(tok), int(pos))
+        if not p:
+            raise LzError("forward failed")
+        return np.ctypeslib.as_array(p, shape=(self.m.vocab,)).copy()
+
+    def batch_capture(self, tokens, pos0):
+        t = np.ascontiguousarray(tokens, np.int32)
+        hid = np.zeros((len(t), self.m.hidden), np.float32)
+        if not lib().lz_forward_batch_capture(self.m.h, self.h, _ptr(t), len(t), pos0, _ptr(hid)):
+            raise LzError("batch capture failed")
+        return hid
+
+    def verify(self, tokens, pos0):
+        t = np.ascontiguousarray(tokens, np.int32)
+        n = len(t)
+        if lib().lz_forward_verify(self.m.h, self.h, _ptr(t), n, pos0):
+            raise LzError("verify failed")
+        lg = np.ctypeslib.as_array(lib().lz_state_mtp_logits(self.h), shape=(n, self.m.vocab)).copy()
+        hid = np.ctypeslib.as_array(lib().lz_state_mtp_verify_hidden(self.h), shape=(n, self.m.hidden)).copy()
+        return hid, lg
+
+    def mtp_draft(self, tok, pos):
+        p = lib().lz_mtp_draft_step(self.m.h, self.h, int(tok), int(pos))
+        if not p:
+            raise LzError("draft step failed")
+        return np.ctypeslib.as_array(p, shape=(self.m.vocab,)).copy()
+
+    def mtp_prefill(self, hidden, nxt, pos0):
+        h = np.ascontiguousarray(hidden, np.float32)
+        t = np.ascontiguousarray(nxt, np.int32)
+        if lib().lz_mtp_prefill(self.m.h, self.h, _ptr(h), _ptr(t), len(t), pos0):
+            raise LzError("mtp prefill failed")
+
+    def spec_round(self, anchor, anchor_pos, k):
+        out = np.zeros(8, np.int32)
+        na, npos, ke = c_int(), c_int(), c_int()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_spec_round(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0, None, 0, 0, _ptr(out),
+                                 ctypes.byref(na), ctypes.byref(npos), ctypes.byref(ke), err, 256)
+        if rc < 0:
+            raise LzError(f"spec round failed ({rc}): {err.value.decode()}")
+        return out[:rc].copy(), na.value, npos.value, ke.value
+
+    # --- batched path
+    def seq_prefill(self, seq, prompt):
+        p = np.ascontiguousarray(prompt, np.int32)
+        a = c_int()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_seq_prefill(self.m.h, self.h, seq, _ptr(p), len(p), ctypes.byref(a), err, 256)
+        if rc:
+            raise LzError(f"prefill failed ({rc}): {err.value.decode()}")
+        return a.value
+
+    def round_batch(self, k, fetch=True):
+        err = ctypes.create_string_buffer(256)
+        toks = np.zeros((self.n_seq, k + 1), np.int32) if fetch else None
+        cnt = np.zeros(self.n_seq, np.int32) if fetch else None
+        rc = lib().lz_spec_round_batch(self.m.h, self.h, k, _ptr(toks), _ptr(cnt), err, 256)
+        if rc:
+            raise LzError(f"batched round failed ({rc}): {err.value.decode()}")
+        return toks, cnt
+
+    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(max_new + 16, np.int32)
+        rounds = np.zeros(2 * (max_new + 16), np.int32)
+        on, nr = c_int(), c_int()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_generate(self.m.h, self.h, _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
+                               _ptr(out), len(out), ctypes.byref(on), _ptr(rounds), len(rounds) // 2,
+                               ctypes.byref(nr), err, 256)
+        if rc:
+            raise LzError(f"generate failed ({rc}): {err.value.decode()}")
+        return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()
+
+
+def spec_accept(draft, targ, bonus):
+    d = np.ascontiguousarray(draft, np.int32)
+    t = np.ascontiguousarray(targ, np.int32)
+    out = np.zeros(len(d) + 1, np.int32)
+    n = lib().lz_spec_accept(_ptr(d), _ptr(t), len(d), int(bonus), _ptr(out))
+    return n, out[:n + 1].copy()
+
+
+def spec_accept_temp(p, q, x, u, rng):
+    p = np.ascontiguousarray(p, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    r = ctypes.c_uint64(rng)
+    acc = c_int()
+    tok = lib().lz_spec_accept_temp(_ptr(p), _ptr(q), int(x), len(p), float(u), ctypes.byref(r), ctypes.byref(acc))
+    return tok, acc.value, r.value

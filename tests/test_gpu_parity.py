@@ -1,0 +1,125 @@
+"""GPU parity of the CUDA path (through the C ABI) against the golden
+vectors of the reference engine and against the C restatement.  Integer
+and float work is bit-exact except the draft logits against the
+reference itself (RoPE table, relative tolerance 1e-5; the CUDA path and
+the oracle share the table and agree bit for bit)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracles import Oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def bits_equal(a, b):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.fixture(scope="module", params=["tiny", "mini"])
+def gcase(request):
+    from conftest import model_dir
+    import lz98
+    name = request.param
+    d = model_dir(name)
+    g = dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
+    m = lz98.Model(d)
+    yield name, d, g, m
+    m.close()
+
+
+def test_verify_forward_bit_exact(gcase):
+    import lz98
+    name, d, g, m = gcase
+    s = lz98.State(m, 512, 4)
+    p = g["prompt"]
+    h = s.batch_capture(p[:-1], 0)
+    assert bits_equal(h, g["prefill_hidden"])
+    hv, lv = s.verify(g["verify_tokens"], len(p) - 1)
+    assert bits_equal(hv, g["verify_hidden"])
+    assert bits_equal(lv, g["verify_logits"])
+    assert s.positions()[1] == int(g["ring_slot_after_verify"][0])
+    s.close()
+
+
+def test_capture_and_draft(gcase):
+    import lz98
+    name, d, g, m = gcase
+    s = lz98.State(m, 512, 4)
+    O = Oracle(d, 512, 4)
+    p = g["prompt"]
+    hb = s.batch_capture(p[:-1], 0)
+    s.mtp_prefill(hb, p[1:], 0)
+    lg = s.forward(p[-1], len(p) - 1, capture=True)
+    assert bits_equal(s.chain(), g["capture_chain"])
+    assert bits_equal(lg, g["capture_logits"])
+    hbo, _ = O.forward(p[:-1], 0, 0, want_logits=False)
+    O.mtp_prefill(hbo, p[1:], 0)
+    O.set_chain(g["capture_chain"])
+    for i, t in enumerate(g["draft_tokens"]):
+        lgd = s.mtp_draft(int(t), len(p) - 1 + i)
+        lgo = O.mtp_draft(int(t), len(p) - 1 + i)
+        assert bits_equal(lgd, lgo), f"draft step {i} differs from the oracle"
+        ref = g["draft_logits"][i]
+        assert np.abs(lgd - ref).max() / np.abs(ref).max() < 1e-5
+    assert bits_equal(s.chain(), O.chain())
+    s.close()
+    O.close()
+
+
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_greedy_generation_token_identical(gcase, k):
+    import lz98
+    name, d, g, m = gcase
+    s = lz98.State(m, 512, 4)
+    max_new = 40 if name == "tiny" else 48
+    toks, rounds = s.generate(g["prompt"], max_new, k)
+    tag = f"gen_t0_k{k}"
+    assert np.array_equal(toks, g[tag + "_tokens"])
+    assert np.array_equal(rounds, g[tag + "_rounds"])
+    s.close()
+
+
+def test_batched_rounds_match_per_sequence_oracle(gcase):
+    """Three sequences in one state, rounds on the device; every sequence's
+    emitted stream equals its own oracle generation."""
+    import lz98
+    name, d, g, m = gcase
+    k, B, n_rounds = 2, 3, 6
+    s = lz98.State(m, 256, 4, n_seq=B)
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, m.vocab, n).astype(np.int32) for n in (9, 17, 12)]
+    emitted = [[] for _ in range(B)]
+    for b in range(B):
+        emitted[b].append(s.seq_prefill(b, prompts[b]))
+    for _ in range(n_rounds):
+        toks, cnt = s.round_batch(k)
+        for b in range(B):
+            emitted[b].extend(toks[b, :cnt[b]].tolist())
+    O = Oracle(d, 256, 4)
+    for b in range(B):
+        n = len(emitted[b])
+        want, _ = O.generate(prompts[b], n + 8, k)
+        assert emitted[b] == want[:n].tolist(), f"sequence {b}"
+    O.close()
+    s.close()
+
+
+def test_graph_and_eager_rounds_agree(gcase):
+    import lz98
+    name, d, g, m = gcase
+    outs = []
+    for graphs in (True, False):
+        s = lz98.State(m, 256, 4, n_seq=2)
+        s.graphs(graphs)
+        for b in range(2):
+            s.seq_prefill(b, g["prompt"][: 10 + 5 * b])
+        res = [s.round_batch(3) for _ in range(4)]
+        outs.append([(t.tolist(), c.tolist()) for t, c in res])
+        s.close()
+    assert outs[0] == outs[1]

@@ -1,0 +1,199 @@
+"""CPU tests: the C restatement (oracle) against the golden vectors made by
+the reference engine, and op by op against the reference itself when its
+compiled library is present."""
+import os
+
+import numpy as np
+import pytest
+
+from oracles import Oracle, Reference, oracle_available, reference_available
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+pytestmark = pytest.mark.skipif(not oracle_available(), reason="oracle library not built")
+
+
+def bits_equal(a, b):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def load_golden(name):
+    return dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
+
+
+@pytest.fixture(scope="module", params=["tiny", "mini"])
+def case(request):
+    from conftest import model_dir
+    import lz98_synth
+    name = request.param
+    d = model_dir(name)
+    g = load_golden(name)
+    sha = lz98_synth.write_model(lz98_synth.CONFIGS[name], d)
+    assert bytes(g["sha256"]).hex() == sha, "model writer drifted from the golden vectors"
+    return name, d, g
+
+
+def test_oracle_forward_matches_golden(case):
+    name, d, g = case
+    O = Oracle(d, 512, 4)
+    p = g["prompt"]
+    h, _ = O.forward(p[:-1], 0, 0, want_logits=False)
+    assert bits_equal(h, g["prefill_hidden"])
+    hv, lv = O.forward(g["verify_tokens"], len(p) - 1, 1)
+    assert bits_equal(hv, g["verify_hidden"])
+    assert bits_equal(lv, g["verify_logits"])
+    assert O.positions()[1] == int(g["ring_slot_after_verify"][0])
+    O.close()
+
+
+def test_oracle_draft_matches_golden(case):
+    name, d, g = case
+    O = Oracle(d, 512, 4)
+    p = g["prompt"]
+    hb, _ = O.forward(p[:-1], 0, 0, want_logits=False)
+    O.mtp_prefill(hb, p[1:], 0)
+    hc, lc = O.forward(p[-1:], len(p) - 1, 0)
+    assert bits_equal(hc[0], g["capture_chain"])
+    assert bits_equal(lc[0], g["capture_logits"])
+    O.set_chain(hc[0])
+    for i, t in enumerate(g["draft_tokens"]):
+        lg = O.mtp_draft(int(t), len(p) - 1 + i)
+        ref = g["draft_logits"][i]
+        # the MTP RoPE table is the one documented difference (double-
+        # precision cos/sin/pow against the reference's all-float ports)
+        rel = np.abs(lg - ref).max() / np.abs(ref).max()
+        assert rel < 1e-5, rel
+        assert int(np.argmax(lg)) == int(np.argmax(ref))
+    O.close()
+
+
+@pytest.mark.parametrize("temp", [0.0, 0.8])
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_oracle_generation_matches_golden(case, temp, k):
+    name, d, g = case
+    O = Oracle(d, 512, 4)
+    tag = f"gen_t{int(temp * 10)}_k{k}"
+    toks, rounds = O.generate(g["prompt"], 40 if name == "tiny" else 48, k, temp=temp, seed=1234)
+    assert np.array_equal(toks, g[tag + "_tokens"])
+    assert np.array_equal(rounds, g[tag + "_rounds"])
+    O.close()
+
+
+# ------------------------------------------------- op level, against the reference
+
+needs_ref = pytest.mark.skipif(not reference_available(), reason="reference library not built here")
+
+
+@pytest.fixture(scope="module")
+def pair(tiny_dir):
+    O = Oracle(tiny_dir, 256, 4)
+    R = Reference(tiny_dir, 256, 4)
+    yield O, R
+    O.close()
+    R.close()
+
+
+@needs_ref
+@pytest.mark.parametrize("fn", ["exp", "rsqrt", "sigmoid"])
+def test_scalar_math_bit_exact(pair, fn):
+    O, R = pair
+    rng = np.random.default_rng(5)
+    xs = np.concatenate([rng.standard_normal(3000) * 30, rng.uniform(-90, 90, 2000),
+                         [0.0, -0.0, 88.0, 88.5, -87.3, -87.4, 1e-30, 1e30]]).astype(np.float32)
+    if fn == "rsqrt":
+        xs = np.abs(xs) + np.float32(1e-30)
+    fo, fr = getattr(O.L, "lzo_" + fn), getattr(R.L, "rd_" + fn)
+    bad = [float(x) for x in xs if np.float32(fo(float(x))).tobytes() != np.float32(fr(float(x))).tobytes()]
+    assert not bad, bad[:5]
+
+
+@needs_ref
+@pytest.mark.parametrize("gs_mode", ["32", "row"])
+@pytest.mark.parametrize("in_dim,out_dim,nt", [(64, 48, 1), (512, 33, 3), (1024, 40, 5), (2048, 16, 2)])
+def test_matmul_q8_bit_exact(pair, gs_mode, in_dim, out_dim, nt):
+    O, R = pair
+    import ctypes
+    rng = np.random.default_rng(in_dim + out_dim)
+    gs = 32 if gs_mode == "32" else in_dim
+    x = (rng.standard_normal((nt, in_dim)) * rng.uniform(0.01, 3)).astype(np.float32)
+    wq = rng.integers(-127, 128, (out_dim, in_dim)).astype(np.int8)
+    ws = (rng.random((out_dim, in_dim // gs)) * 0.01).astype(np.float32)
+    xq = np.zeros((nt, in_dim), np.int8)
+    xs = np.zeros((nt, in_dim // 32), np.float32)
+    xq2, xs2 = xq.copy(), xs.copy()
+    V = ctypes.c_void_p
+    for t in range(nt):
+        O.L.lzo_quantize_q8(V(x[t].ctypes.data), in_dim, 32, V(xq[t].ctypes.data), V(xs[t].ctypes.data))
+        R.L.rd_quantize_q8(V(x[t].ctypes.data), in_dim, 32, V(xq2[t].ctypes.data), V(xs2[t].ctypes.data))
+    assert np.array_equal(xq, xq2) and bits_equal(xs, xs2)
+    o1 = np.zeros((nt, out_dim), np.float32)
+    o2 = np.zeros((nt, out_dim), np.float32)
+    O.L.lzo_matmul_q8(V(o1.ctypes.data), V(xq.ctypes.data), V(xs.ctypes.data), V(wq.ctypes.data),
+                      V(ws.ctypes.data), gs, in_dim, out_dim, nt)
+    R.L.rd_matmul_q8(V(o2.ctypes.data), V(xq.ctypes.data), V(xs.ctypes.data), V(wq.ctypes.data),
+                     V(ws.ctypes.data), gs, in_dim, out_dim, nt)
+    assert bits_equal(o1, o2)
+
+
+@needs_ref
+def test_kda_recurrence_bit_exact(pair):
+    O, R = pair
+    import ctypes
+    V = ctypes.c_void_p
+    rng = np.random.default_rng(9)
+    kd = vd = 64
+    hi = rng.integers(-127, 128, (kd, vd)).astype(np.int8)
+    lo = rng.integers(-127, 128, (kd, vd)).astype(np.int8)
+    ss = (rng.random((kd, vd // 32)) * 0.01).astype(np.float32)
+    q = rng.standard_normal(kd).astype(np.float32); q /= np.linalg.norm(q)
+    k = rng.standard_normal(kd).astype(np.float32); k /= np.linalg.norm(k)
+    v = rng.standard_normal(vd).astype(np.float32)
+    g = rng.uniform(0.01, 1.0, kd).astype(np.float32)
+    outs = []
+    for L, fn in ((O.L, "lzo_recur_step"), (R.L, "rd_recur_step")):
+        out = np.zeros(vd, np.float32)
+        h2, l2, s2 = np.zeros_like(hi), np.zeros_like(lo), np.zeros_like(ss)
+        getattr(L, fn)(V(out.ctypes.data), V(hi.ctypes.data), V(h2.ctypes.data), V(lo.ctypes.data),
+                       V(l2.ctypes.data), V(ss.ctypes.data), V(s2.ctypes.data), V(q.ctypes.data),
+                       V(k.ctypes.data), V(v.ctypes.data), V(g.ctypes.data), ctypes.c_float(0.37), kd, vd)
+        outs.append((out, h2, l2, s2))
+    (o1, a1, b1, c1), (o2, a2, b2, c2) = outs
+    assert bits_equal(o1, o2) and np.array_equal(a1, a2) and np.array_equal(b1, b2) and bits_equal(c1, c2)
+
+
+@needs_ref
+@pytest.mark.parametrize("E,topk", [(8, 2), (64, 4), (128, 8)])
+def test_moe_route_matches(pair, E, topk):
+    O, R = pair
+    import ctypes
+    V = ctypes.c_void_p
+    rng = np.random.default_rng(E)
+    for trial in range(20):
+        lg = (rng.standard_normal(E) * 2).astype(np.float32)
+        if trial % 5 == 0:
+            lg[3] = lg[5]          # ties must keep the first index
+        bias = (rng.standard_normal(E) * 0.02).astype(np.float32)
+        res = []
+        for L, fn in ((O.L, "lzo_moe_route"), (R.L, "rd_moe_route")):
+            idx = np.zeros(topk, np.int32)
+            w = np.zeros(topk, np.float32)
+            getattr(L, fn)(V(lg.ctypes.data), V(bias.ctypes.data), E, topk, 1, 1, V(idx.ctypes.data), V(w.ctypes.data))
+            res.append((idx, w))
+        assert np.array_equal(res[0][0], res[1][0]) and bits_equal(res[0][1], res[1][1])
+
+
+@needs_ref
+def test_target_dist_matches(pair):
+    O, R = pair
+    import ctypes
+    V = ctypes.c_void_p
+    rng = np.random.default_rng(2)
+    for n in (100, 8192):
+        lg = (rng.standard_normal(n) * 1.5).astype(np.float32)
+        p1, p2 = np.zeros(n, np.float32), np.zeros(n, np.float32)
+        a, b = lg.copy(), lg.copy()
+        O.L.lzo_target_dist(ctypes.c_float(0.8), ctypes.c_float(0.95), V(a.ctypes.data), n, V(p1.ctypes.data))
+        R.L.rd_target_dist(ctypes.c_float(0.8), ctypes.c_float(0.95), V(b.ctypes.data), n, V(p2.ctypes.data))
+        assert bits_equal(p1, p2)
