@@ -142,6 +142,16 @@ int lz_generate(const LZModel *m, LZRunState *s, const int *prompt, int n_prompt
                 int *out_tok, int out_cap, int *out_n, int *rounds, int round_cap,
                 int *n_rounds, char *errbuf, int errlen);
 
+/* Running totals of sequence `seq` over its device rounds: rounds, emitted
+   tokens (n_accept + 1 per round), accepted drafts, drafted tokens. */
+int lz_state_counters(const LZRunState *s, int seq, int *rounds, int *emitted,
+                      int *accepted, int *drafted);
+/* Measurement hook: one eager greedy round of depth k with CUDA events
+   around every int8 GEMV launch.  Returns the summed GEMV device time, their
+   algorithmic bytes (weights, scales, activations, outputs), the GEMV count,
+   the round's device time and its kernel count. */
+int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
+                     int *n_gemv, double *round_ms, int *n_kernels);
 /* Stream the library launches on (cudaStream_t, NULL = a private stream). */
 void *lz_state_stream(LZRunState *s);
 /* Kernels this library launched since the state was created. */

@@ -206,7 +206,7 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
        !c.lat_norm && c.has_lb && c.sigm && c.renorm && c.kd == 64 && c.vd == 64 &&
        c.nk == c.nv && c.hd == 64 && c.conv_k == 4 && c.d % 32 == 0 && c.rank % 32 == 0 &&
        c.rank <= 256 && c.latent <= 1024 && c.latent % 32 == 0 && c.moe_ffn % 32 == 0 &&
-       c.shared_w % 32 == 0 && 2 * c.d <= 8192;
+       c.shared_w % 32 == 0 && 2 * c.d <= 4096 && c.moe_ffn <= 2048 && c.val_dim <= 4096;
   if (!ok) {
     set_err(errbuf, errlen, "unsupported KunMoe configuration (needs all-KDA layers, latent MoE with "
                             "sigmoid router, one MTP layer, head dims 64)");
@@ -346,7 +346,8 @@ struct LZRunState {
   float *x, *inproj, *conv_out, *gate, *moein, *h2, *shout, *hidden, *logits, *qkv, *mtpx, *hb;
   int8_t *xq, *oq, *latq, *hq, *yq, *shq, *aq;
   float *xs, *os, *lats, *hs, *ys, *shs, *as;
-  int *pair_e, *tok, *vmax, *catch_tok, *catch_hidx;
+  int *pair_e, *tok, *catch_tok, *catch_hidx;
+  unsigned long long* vmax;
   float* pair_w;
   KdaSeq* seqs;
   MtpRow *mrows, *crows;
@@ -357,6 +358,10 @@ struct LZRunState {
   std::vector<float> h_logits, h_hidden, h_draft;
   long long launches = 0;
   bool graphs = true;
+  // optional per-GEMV timing (lz_profile_round): event pairs and bytes
+  bool prof = false;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<double> prof_bytes;
   std::map<int, cudaGraphExec_t> graph;
   std::vector<void*> allocs;
 };
@@ -574,23 +579,43 @@ extern "C" int lz_set_graphs(LZRunState* s, int enable) {
 namespace {
 
 void gemv(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, float* y, int ldy,
-          int mode = 0, const float* z = nullptr, int ldz = 0) {
-  const int nsb = w.in / 32;
+          int mode = 0, const QW* w2 = nullptr, const int8_t* xq2 = nullptr, const float* xs2 = nullptr) {
+  GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode,
+             w2 ? w2->q : nullptr, w2 ? w2->s : nullptr, w2 ? w2->in : 0, w2 ? w2->gs : 32, xq2, xs2};
+  const int nsb = std::max(w.in, w2 ? w2->in : 0) / 32;
+  if (s->prof) {
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, s->st);
+    s->prof_ev.push_back(e0);
+    s->prof_ev.push_back(e1);
+    // algorithmic bytes: weights + weight scales + activations + outputs
+    auto bytes = [R](const QW& q) {
+      return (double)q.out * q.in + (double)q.out * (q.in / q.gs) * 4.0 + (double)R * q.in +
+             (double)R * (q.in / 32) * 4.0;
+    };
+    double b = bytes(w) + (w2 ? bytes(*w2) : 0.0) + (double)R * w.out * 4.0 * (mode ? 2.0 : 1.0);
+    s->prof_bytes.push_back(b);
+  }
   const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
-  if (nsb <= 32)
-    gemv_q8_kernel<1><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
-  else if (nsb <= 64)
-    gemv_q8_kernel<2><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
-  else if (nsb <= 128)
-    gemv_q8_kernel<4><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
-  else
-    gemv_q8_kernel<8><<<grid, blk, 0, s->st>>>(w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode, z, ldz);
+  if (nsb <= 32) gemv_q8_kernel<1><<<grid, blk, 0, s->st>>>(a);
+  else if (nsb <= 64) gemv_q8_kernel<2><<<grid, blk, 0, s->st>>>(a);
+  else gemv_q8_kernel<4><<<grid, blk, 0, s->st>>>(a);
   s->launches++;
+  if (s->prof) cudaEventRecord(s->prof_ev.back(), s->st);
 }
 
 void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
-                   int ldo, int8_t* xq, float* xs) {
-  rmsnorm_quant_kernel<<<R, 256, n * sizeof(float), s->st>>>(x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs);
+                   int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear = nullptr) {
+  rmsnorm_quant_kernel<<<R, 256, n * sizeof(float), s->st>>>(x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs,
+                                                             amax_clear);
+  s->launches++;
+}
+
+void argmax(LZRunState* s, const float* logits, int R, int p1_mode) {
+  const int V = s->m->c.vocab;
+  argmax_kernel<<<dim3((V + kArgmaxChunk - 1) / kArgmaxChunk, R), 256, 0, s->st>>>(logits, V, p1_mode, s->vmax);
   s->launches++;
 }
 
@@ -621,14 +646,13 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
     gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);
     rmsnorm_quant(s, s->x, d, L.post_ln, d, R, nullptr, 0, s->xq, s->xs);
     gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe);
-    moe_route_kernel<<<R, 32, 0, s->st>>>(s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
+    moe_route_kernel<<<R, 128, 0, s->st>>>(s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
                                           c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats);
     s->launches++;
     if (c.shared_w) {
       swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->moein, m->n_moe, m->off_shg, m->off_shu, c.shared_w,
                                                 s->shq, s->shs);
       s->launches++;
-      gemv(s, L.sh_down, s->shq, s->shs, R, s->shout, d);
     }
     moe_w13_kernel<<<dim3(c.moe_ffn / 32, R * c.topk), 256, 0, s->st>>>(
         L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
@@ -636,9 +660,10 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
         L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->hq, s->hs, s->h2);
     moe_combine_kernel<<<R, 256, 0, s->st>>>(s->h2, s->pair_w, s->pair_e, c.topk, c.latent, s->yq, s->ys);
     s->launches += 3;
-    gemv(s, L.up, s->yq, s->ys, R, s->x, d, c.shared_w ? 2 : 1, s->shout, d);
+    if (c.shared_w) gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1, &L.sh_down, s->shq, s->shs);
+    else gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1);
   }
-  rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs);
+  rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs, s->vmax);
   if (want_logits) gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
 }
 
@@ -675,7 +700,7 @@ void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const i
   swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->inproj, 2 * c.mtp_ffn, 0, c.mtp_ffn, c.mtp_ffn, s->shq, s->shs);
   s->launches++;
   gemv(s, M.down, s->shq, s->shs, R, s->mtpx, d, 1);
-  rmsnorm_quant(s, s->mtpx, d, M.norm, d, R, chain_out, d, s->xq, s->xs);
+  rmsnorm_quant(s, s->mtpx, d, M.norm, d, R, chain_out, d, s->xq, s->xs, s->vmax);
   gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
 }
 
@@ -695,10 +720,10 @@ __global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_
   rows[b] = MtpRow{b, pos, pos >= 0 && pos < seq_len};
 }
 
-__global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const int* amax) {
+__global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const unsigned long long* amax) {
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= nseq) return;
-  sr[b].draft[i] = amax[b];
+  sr[b].draft[i] = argmax_index(amax[b]);
   sr[b].k = k;
 }
 
@@ -724,17 +749,17 @@ void round_greedy(LZRunState* s, int k) {
   for (int i = 0; i < k; i++) {
     draft_setup_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, s->seq_len, s->tok, s->mrows);
     mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
-    argmax_kernel<<<B, 1024, 0, s->st>>>(s->logits, c.vocab, 1, s->vmax);
+    argmax(s, s->logits, B, 1);
     draft_store_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, k, s->vmax);
-    s->launches += 3;
+    s->launches += 2;
   }
   const int R = B * (k + 1);
   verify_setup_kernel<<<B, 32, 0, s->st>>>(s->sr, B, k, s->tok, s->seqs);
   body_forward(s, R, B, 1, true);
-  argmax_kernel<<<R, 1024, 0, s->st>>>(s->logits, c.vocab, 0, s->vmax);
+  argmax(s, s->logits, R, 0);
   spec_accept_greedy_kernel<<<B, 256, 0, s->st>>>(s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
                                                   s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
-  s->launches += 3;
+  s->launches += 2;
   if (k > 1)
     mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
 }
@@ -1032,10 +1057,10 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
   upload_seqs(s, {KdaSeq{0, 1, slot, seq}});
   body_forward(s, 1, 1, 0, true);
   cudaMemcpyAsync(s->chain + (size_t)seq * c.d, s->hidden, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
-  argmax_kernel<<<1, 1024, 0, s->st>>>(s->logits, c.vocab, 0, s->vmax);
-  s->launches++;
-  int anchor = 0;
-  cudaMemcpyAsync(&anchor, s->vmax, sizeof(int), cudaMemcpyDeviceToHost, s->st);
+  argmax(s, s->logits, 1, 0);
+  unsigned long long packed = 0;
+  cudaMemcpyAsync(&packed, s->vmax, sizeof(packed), cudaMemcpyDeviceToHost, s->st);
+  const int anchor = (int)(0xFFFFFFFFu - (uint32_t)packed);
   if (cudaStreamSynchronize(s->st) != cudaSuccess) {
     set_err(errbuf, errlen, "CUDA failure in prefill");
     return LZ98_ERR_CUDA;
@@ -1152,5 +1177,57 @@ extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, i
   }
   *out_n = n_out;
   *n_rounds = nr;
+  return 0;
+}
+
+extern "C" int lz_state_counters(const LZRunState* cs, int seq, int* rounds, int* emitted, int* accepted,
+                                 int* drafted) {
+  LZRunState* s = const_cast<LZRunState*>(cs);
+  if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  sr_down(s);
+  const SeqRound& r = s->h_sr[seq];
+  if (rounds) *rounds = r.rounds;
+  if (emitted) *emitted = r.emitted;
+  if (accepted) *accepted = r.accepted;
+  if (drafted) *drafted = r.drafted;
+  return 0;
+}
+
+// One eager greedy round of depth k with CUDA events around every int8
+// GEMV launch: total GEMV device time, their algorithmic bytes, the count,
+// the round's device time and its kernel count.
+extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* gemv_bytes, int* n_gemv,
+                                double* round_ms, int* n_kernels) {
+  if (!s || k < 1 || k > s->kmax) return LZ98_ERR_NULL_ARG;
+  cudaEvent_t r0, r1;
+  cudaEventCreate(&r0);
+  cudaEventCreate(&r1);
+  s->prof = true;
+  s->prof_ev.clear();
+  s->prof_bytes.clear();
+  const long long l0 = s->launches;
+  cudaEventRecord(r0, s->st);
+  round_greedy(s, k);
+  cudaEventRecord(r1, s->st);
+  s->prof = false;
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) return LZ98_ERR_CUDA;
+  double gt = 0.0, gb = 0.0;
+  for (size_t i = 0; i < s->prof_bytes.size(); i++) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, s->prof_ev[2 * i], s->prof_ev[2 * i + 1]);
+    gt += ms;
+    gb += s->prof_bytes[i];
+  }
+  for (auto e : s->prof_ev) cudaEventDestroy(e);
+  s->prof_ev.clear();
+  float rms = 0.0f;
+  cudaEventElapsedTime(&rms, r0, r1);
+  cudaEventDestroy(r0);
+  cudaEventDestroy(r1);
+  if (gemv_ms) *gemv_ms = gt;
+  if (gemv_bytes) *gemv_bytes = gb;
+  if (n_gemv) *n_gemv = (int)s->prof_bytes.size();
+  if (round_ms) *round_ms = rms;
+  if (n_kernels) *n_kernels = (int)(s->launches - l0);
   return 0;
 }

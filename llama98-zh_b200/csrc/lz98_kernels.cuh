@@ -11,7 +11,8 @@
 //
 // Every float reduction keeps the reference's order: where the reference
 // sums sequentially the kernel sums sequentially (one lane per chain, the
-// chains of different rows/columns in parallel); integer sums (int8 dot
+// chains of different rows/columns in parallel, operands staged in shared
+// memory so the chain runs at add latency); integer sums (int8 dot
 // products per 32-element sub-block) are order-free and run as __dp4a.
 #pragma once
 #include "lz98_dev.cuh"
@@ -20,7 +21,42 @@ namespace lz98 {
 
 constexpr int kGemvWarps = 4;
 constexpr int kGemvRB = 8;        // token rows per reduction pass
-constexpr int kNsbMax = 256;      // K <= 8192
+
+// ------------------------------------------------------- serial chains
+
+// Sequential sum of squares over a 16-byte aligned array, n % 4 == 0
+// (src/ops_norm.c:718): the adds stay in index order; the loads run ahead
+// in float4 groups.
+LZ_HD float seq_sumsq(const float* v, int n) {
+  float ss = 0.0f;
+  const float4* p = reinterpret_cast<const float4*>(v);
+#pragma unroll 8
+  for (int i = 0; i < n / 4; i++) {
+    const float4 q = p[i];
+    ss = __fadd_rn(ss, __fmul_rn(q.x, q.x));
+    ss = __fadd_rn(ss, __fmul_rn(q.y, q.y));
+    ss = __fadd_rn(ss, __fmul_rn(q.z, q.z));
+    ss = __fadd_rn(ss, __fmul_rn(q.w, q.w));
+  }
+  return ss;
+}
+
+// Sequential sum (index order) of a 16-byte aligned array, any n.
+LZ_HD float seq_sum(const float* v, int n) {
+  float s = 0.0f;
+  const float4* p = reinterpret_cast<const float4*>(v);
+  int i = 0;
+#pragma unroll 8
+  for (; i < n / 4; i++) {
+    const float4 q = p[i];
+    s = __fadd_rn(s, q.x);
+    s = __fadd_rn(s, q.y);
+    s = __fadd_rn(s, q.z);
+    s = __fadd_rn(s, q.w);
+  }
+  for (i *= 4; i < n; i++) s = __fadd_rn(s, v[i]);
+  return s;
+}
 
 // ------------------------------------------------------------------ GEMV
 
@@ -30,8 +66,10 @@ constexpr int kNsbMax = 256;      // K <= 8192
 //                   group) * ws[g], both sequential;
 //   rb == 1:        p[s] = acc[s]*(xs[s]*ws[s]); four interleaved
 //                   accumulators combined (a0+a2)+(a1+a3), tail into a0.
+// p is 16-byte aligned.
 LZ_HD float q8_reduce(const float* p, const float* wsr, int rb, int ng) {
   if (rb > 1) {
+    if (ng == 1) return __fadd_rn(0.0f, __fmul_rn(seq_sum(p, rb), wsr[0]));
     float sum = 0.0f;
     for (int g = 0; g < ng; g++) {
       float dot = 0.0f;
@@ -42,11 +80,14 @@ LZ_HD float q8_reduce(const float* p, const float* wsr, int rb, int ng) {
   }
   float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
   int g = 0;
+  const float4* p4 = reinterpret_cast<const float4*>(p);
+#pragma unroll 4
   for (; g + 3 < ng; g += 4) {
-    a0 = __fadd_rn(a0, p[g]);
-    a1 = __fadd_rn(a1, p[g + 1]);
-    a2 = __fadd_rn(a2, p[g + 2]);
-    a3 = __fadd_rn(a3, p[g + 3]);
+    const float4 q = p4[g >> 2];
+    a0 = __fadd_rn(a0, q.x);
+    a1 = __fadd_rn(a1, q.y);
+    a2 = __fadd_rn(a2, q.z);
+    a3 = __fadd_rn(a3, q.w);
   }
   for (; g < ng; g++) a0 = __fadd_rn(a0, p[g]);
   return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
@@ -61,57 +102,82 @@ LZ_HD int dot32(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
   return acc;
 }
 
-// Weight-streaming int8 GEMV/skinny GEMM: one warp per output row, each
-// lane owning 32-byte sub-blocks of that row (loaded once, reused for
-// every token row), per-sub-block int32 sums by __dp4a, then one lane per
-// token row runs the reference reduction.
-// mode 0: y = v;  mode 1: y = y + v;  mode 2: y = y + (v + z).
+struct GemvArgs {
+  const int8_t* W; const float* ws; int N, K, gs;
+  const int8_t* xq; const float* xs; int R;
+  float* y; int ldy; int mode;        // mode 0: y = v; mode 1: y = y + v
+  // optional second product over the same output rows, added before the
+  // store: v = v1 + v2 (up projection plus shared expert,
+  // src/forward_moe.c:434-545)
+  const int8_t* W2; const float* ws2; int K2, gs2;
+  const int8_t* xq2; const float* xs2;
+};
+
+// Products of one weight row with every token row for the sub-blocks this
+// lane owns; P[rr][s] receives the product fed to the reference reduction.
 template <int JM>
-__global__ void __launch_bounds__(kGemvWarps * 32)
-gemv_q8_kernel(const int8_t* __restrict__ W, const float* __restrict__ ws,
-               int N, int K, int gs,
-               const int8_t* __restrict__ xq, const float* __restrict__ xs, int R,
-               float* y, int ldy, int mode, const float* __restrict__ z, int ldz) {
-  __shared__ float P[kGemvWarps][kGemvRB][JM * 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * kGemvWarps + warp;
-  if (n >= N) return;
-  const int nsb = K >> 5, rb = gs >> 5, ng = K / gs;
-  const int8_t* wr = W + (size_t)n * K;
-  const float* wsr = ws + (size_t)n * ng;
+LZ_HD void gemv_products(const int8_t* __restrict__ wr, const float* __restrict__ wsr, int K, int rb,
+                         const int8_t* __restrict__ xq, const float* __restrict__ xs, int r0, int nr,
+                         float (*P)[JM * 32], int lane) {
+  const int nsb = K >> 5;
   int4 wa[JM], wb[JM];
+  float wsv[JM];
 #pragma unroll
   for (int j = 0; j < JM; j++) {
-    int s = lane + 32 * j;
+    const int s = lane + 32 * j;
     if (s < nsb) {
       wa[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
       wb[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+      wsv[j] = rb == 1 ? __ldg(wsr + s) : 0.0f;
     }
   }
-  for (int r0 = 0; r0 < R; r0 += kGemvRB) {
-    const int nr = min(kGemvRB, R - r0);
-    for (int rr = 0; rr < nr; rr++) {
+#pragma unroll
+  for (int rr = 0; rr < kGemvRB; rr++) {
+    if (rr < nr) {
       const int8_t* xr = xq + (size_t)(r0 + rr) * K;
       const float* xsr = xs + (size_t)(r0 + rr) * nsb;
 #pragma unroll
       for (int j = 0; j < JM; j++) {
-        int s = lane + 32 * j;
+        const int s = lane + 32 * j;
         if (s < nsb) {
-          int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
-          int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-          float a = (float)dot32(wa[j], wb[j], xa, xb);
-          P[warp][rr][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+          const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+          const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+          const float a = (float)dot32(wa[j], wb[j], xa, xb);
+          const float xsv = __ldg(xsr + s);
+          P[rr][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[j]));
         }
       }
     }
+  }
+}
+
+// Weight-streaming int8 GEMV/skinny GEMM: one warp per output row, each
+// lane owning 32-byte sub-blocks of the row (loaded once, reused for every
+// token row), per-sub-block int32 sums by __dp4a, then one lane per token
+// row runs the reference reduction.
+template <int JM>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_q8_kernel(const GemvArgs a) {
+  __shared__ __align__(16) float P[kGemvWarps][kGemvRB][JM * 32];
+  __shared__ __align__(16) float P2[kGemvWarps][kGemvRB][JM * 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kGemvWarps + warp;
+  if (n >= a.N) return;
+  const int rb = a.gs >> 5, ng = a.K / a.gs;
+  const int8_t* wr = a.W + (size_t)n * a.K;
+  const float* wsr = a.ws + (size_t)n * ng;
+  const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
+  const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
+  for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
+    const int nr = min(kGemvRB, a.R - r0);
+    gemv_products<JM>(wr, wsr, a.K, rb, a.xq, a.xs, r0, nr, P[warp], lane);
+    if (a.W2) gemv_products<JM>(a.W2 + (size_t)n * a.K2, wsr2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2[warp], lane);
+    float prev = 0.0f;
+    if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
     __syncwarp();
     if (lane < nr) {
       float v = q8_reduce(P[warp][lane], wsr, rb, ng);
-      const int r = r0 + lane;
-      float* yp = y + (size_t)r * ldy + n;
-      if (mode == 0) *yp = v;
-      else if (mode == 1) *yp = __fadd_rn(*yp, v);
-      else *yp = __fadd_rn(*yp, __fadd_rn(v, z[(size_t)r * ldz + n]));
+      if (a.W2) v = __fadd_rn(v, q8_reduce(P2[warp][lane], wsr2, rb2, ng2));
+      a.y[(size_t)(r0 + lane) * a.ldy + n] = a.mode == 1 ? __fadd_rn(prev, v) : v;
     }
     __syncwarp();
   }
@@ -119,32 +185,28 @@ gemv_q8_kernel(const int8_t* __restrict__ W, const float* __restrict__ ws,
 
 // --------------------------------------------------------- row kernels
 
-// Serial sum of squares by one thread (src/ops_norm.c:718).
-LZ_HD float seq_sumsq(const float* v, int n) {
-  float ss = 0.0f;
-  for (int i = 0; i < n; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-  return ss;
-}
-
 // rmsnorm (1+w) of one row, then per-32 quantisation of the result; the
-// float result is stored too when `out` is non-null.  One block per row.
-// src/ops_norm.c:690-747 and src/ops_quant.c:2152-2282.
+// float result is stored too when `out` is non-null; `amax_clear`, when
+// non-null, zeroes this row's arg-max slot for a following lm_head.
+// One block per row.  src/ops_norm.c:690-747, src/ops_quant.c:2152-2282.
 __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
                                      const float* __restrict__ w, int n, float eps,
-                                     float* out, int ldo, int8_t* xq, float* xs) {
-  extern __shared__ float sm[];
+                                     float* out, int ldo, int8_t* xq, float* xs,
+                                     unsigned long long* amax_clear) {
+  extern __shared__ __align__(16) float sm[];
   __shared__ float s_inv;
   const int r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
   for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = xr[i];
+  if (amax_clear && threadIdx.x == 0) amax_clear[r] = 0ull;
   __syncthreads();
   if (threadIdx.x == 0) s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, n), (float)n), eps));
   __syncthreads();
   const float inv = s_inv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int g = warp; g < n / 32; g += nw) {
-    int i = g * 32 + lane;
-    float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, w[i]));
+    const int i = g * 32 + lane;
+    const float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, w[i]));
     if (out) out[(size_t)r * ldo + i] = o;
     xq[(size_t)r * n + i] = warp_quant32(o, &xs[(size_t)r * (n / 32) + g]);
   }
@@ -167,48 +229,39 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ src, int lds, int 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const float* row = src + (size_t)r * lds;
   for (int g = warp; g < n / 32; g += nw) {
-    int i = g * 32 + lane;
-    float a = __fmul_rn(silu(row[g0 + i]), row[u0 + i]);
+    const int i = g * 32 + lane;
+    const float a = __fmul_rn(silu(row[g0 + i]), row[u0 + i]);
     xq[(size_t)r * n + i] = warp_quant32(a, &xs[(size_t)r * (n / 32) + g]);
   }
 }
 
-// ArgMax with the first index on ties.  p1_mode = 0 compares by the total
-// key of src/sampler.c:224-240; p1_mode = 1 by float `>` (lz_argmax_p1,
-// src/sampler.c:279-295), i.e. -0 and +0 compare equal.
-__global__ void argmax_kernel(const float* __restrict__ logits, int V, int p1_mode, int* out) {
-  const int r = blockIdx.x;
+// Arg-max of each row, first index on ties, into a packed 64-bit slot
+// (key << 32 | ~index) combined across blocks by atomicMax; the slot must
+// be zero beforehand.  p1_mode = 0 compares by the total key of
+// src/sampler.c:224-240; p1_mode = 1 by float `>` (lz_argmax_p1,
+// src/sampler.c:279-295), so -0 and +0 compare equal.
+constexpr int kArgmaxChunk = 4096;
+__global__ void argmax_kernel(const float* __restrict__ logits, int V, int p1_mode,
+                              unsigned long long* slot) {
+  const int r = blockIdx.y;
   const float* row = logits + (size_t)r * V;
-  uint32_t bk = 0;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float v = row[i];
+  const int i0 = blockIdx.x * kArgmaxChunk, i1 = min(V, i0 + kArgmaxChunk);
+  unsigned long long best = 0ull;
+#pragma unroll 4
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    float v = __ldg(row + i);
     if (p1_mode && v == 0.0f) v = 0.0f;
-    uint32_t k = fkey(v);
-    if (bi == 0x7fffffff || k > bk) { bk = k; bi = i; }
+    const unsigned long long key = ((unsigned long long)fkey(v) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+    best = key > best ? key : best;
   }
   for (int o = 16; o > 0; o >>= 1) {
-    uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
-    int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (k2 > bk || (k2 == bk && i2 < bi)) { bk = k2; bi = i2; }
+    const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    best = b2 > best ? b2 : best;
   }
-  __shared__ uint32_t sk[32];
-  __shared__ int si[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) { sk[warp] = bk; si[warp] = bi; }
-  __syncthreads();
-  if (warp == 0) {
-    int nw = blockDim.x >> 5;
-    bk = lane < nw ? sk[lane] : 0;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-    for (int o = 16; o > 0; o >>= 1) {
-      uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
-      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (k2 > bk || (k2 == bk && i2 < bi)) { bk = k2; bi = i2; }
-    }
-    if (lane == 0) out[r] = bi;
-  }
+  if ((threadIdx.x & 31) == 0) atomicMax(slot + r, best);
 }
+
+LZ_HD int argmax_index(unsigned long long packed) { return (int)(0xFFFFFFFFu - (uint32_t)packed); }
 
 // ---------------------------------------------------------------- KDA
 
@@ -218,7 +271,7 @@ struct KdaSeq {            // one sequence's rows inside a forward batch
 
 // f_b_proj of every token (quantised f_a latent, src/forward_kda.c:773-819)
 // then the per-channel decay gate gt = exp(lb * sigmoid(exp(A_log[h]) *
-// (pre + dt_bias))) (src/forward_kda.c:277-297, 847-851).
+// (pre + dt_bias))) (src/forward_kda.c:277-297, 847-851).  rank <= 256.
 __global__ void kda_fb_gate_kernel(const float* __restrict__ inproj, int ldi, int off_fa, int rank,
                                    const int8_t* __restrict__ fbq, const float* __restrict__ fbs, int fb_gs,
                                    const float* __restrict__ a_log, const float* __restrict__ dt_bias,
@@ -228,27 +281,35 @@ __global__ void kda_fb_gate_kernel(const float* __restrict__ inproj, int ldi, in
   const int r = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int g = warp; g < rank / 32; g += nw) {
-    float v = inproj[(size_t)r * ldi + off_fa + g * 32 + lane];
+    const float v = inproj[(size_t)r * ldi + off_fa + g * 32 + lane];
     lq[g * 32 + lane] = warp_quant32(v, &ls[g]);
   }
   __syncthreads();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= nvk) return;
   const int nsb = rank / 32, rb = fb_gs / 32, ng = rank / fb_gs;
-  float p[8];
+  __align__(16) float p[8];
   const int8_t* wr = fbq + (size_t)j * rank;
   const float* wsr = fbs + (size_t)j * ng;
-  for (int s = 0; s < nsb; s++) {
-    int4 wa = *reinterpret_cast<const int4*>(wr + s * 32);
-    int4 wb = *reinterpret_cast<const int4*>(wr + s * 32 + 16);
-    int4 xa = *reinterpret_cast<const int4*>(lq + s * 32);
-    int4 xb = *reinterpret_cast<const int4*>(lq + s * 32 + 16);
-    float a = (float)dot32(wa, wb, xa, xb);
-    p[s] = rb > 1 ? __fmul_rn(a, ls[s]) : __fmul_rn(a, __fmul_rn(ls[s], wsr[s]));
-  }
-  float pre = __fadd_rn(q8_reduce(p, wsr, rb, ng), dt_bias[j]);
-  float decay = exp_body(a_log[j / kd]);
-  float g = __fmul_rn(lb, sigmoid(__fmul_rn(decay, pre)));
+  int4 wa[8], wb[8];
+#pragma unroll
+  for (int s = 0; s < 8; s++)
+    if (s < nsb) {
+      wa[s] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+      wb[s] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+    }
+  const float dtb = __ldg(dt_bias + j), alg = __ldg(a_log + j / kd);
+#pragma unroll
+  for (int s = 0; s < 8; s++)
+    if (s < nsb) {
+      const int4 xa = *reinterpret_cast<const int4*>(lq + s * 32);
+      const int4 xb = *reinterpret_cast<const int4*>(lq + s * 32 + 16);
+      const float a = (float)dot32(wa[s], wb[s], xa, xb);
+      p[s] = rb > 1 ? __fmul_rn(a, ls[s]) : __fmul_rn(a, __fmul_rn(ls[s], wsr[s]));
+    }
+  const float pre = __fadd_rn(q8_reduce(p, wsr, rb, ng), dtb);
+  const float decay = exp_body(alg);
+  const float g = __fmul_rn(lb, sigmoid(__fmul_rn(decay, pre)));
   gate[(size_t)r * nvk + j] = exp_body(g);
 }
 
@@ -266,19 +327,19 @@ __global__ void kda_conv_kernel(const float* __restrict__ inproj, int ldi, int c
   float* st0 = conv_state + (size_t)sq.seq * seq_stride + (size_t)c * 3;
   const float* st = st0 + (size_t)sq.base_slot * slot_stride;
   float h0 = st[0], h1 = st[1], h2 = st[2];
-  const float w0 = cw[c * 4], w1 = cw[c * 4 + 1], w2 = cw[c * 4 + 2], w3 = cw[c * 4 + 3];
+  const float4 w = __ldg(reinterpret_cast<const float4*>(cw) + c);
   for (int t = 0; t < sq.nrows; t++) {
     const int r = sq.row0 + t;
     const float xv = inproj[(size_t)r * ldi + c];
     float sum = 0.0f;
-    sum = __fadd_rn(sum, __fmul_rn(w0, h0));
-    sum = __fadd_rn(sum, __fmul_rn(w1, h1));
-    sum = __fadd_rn(sum, __fmul_rn(w2, h2));
-    sum = __fadd_rn(sum, __fmul_rn(w3, xv));
+    sum = __fadd_rn(sum, __fmul_rn(w.x, h0));
+    sum = __fadd_rn(sum, __fmul_rn(w.y, h1));
+    sum = __fadd_rn(sum, __fmul_rn(w.z, h2));
+    sum = __fadd_rn(sum, __fmul_rn(w.w, xv));
     out[(size_t)r * ldo + c] = silu(sum);
     h0 = h1; h1 = h2; h2 = xv;
     if (adv) {
-      int so = (sq.base_slot + t + 1) % depth;
+      const int so = (sq.base_slot + t + 1) % depth;
       float* d = st0 + (size_t)so * slot_stride;
       d[0] = h0; d[1] = h1; d[2] = h2;
     }
@@ -297,7 +358,7 @@ __global__ void kda_conv_kernel(const float* __restrict__ inproj, int ldi, int c
 // output and its per-32 quantisation for o_proj.
 // src/forward_kda.c:856-936 and 1029-1040, src/ops_gdn.c:2488-2778,
 // src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
-constexpr int kRecurThreads = 512;
+constexpr int kRecurThreads = 1024;
 __global__ void __launch_bounds__(kRecurThreads)
 kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  const float* __restrict__ inproj, int ldi, int off_b, int off_g,
@@ -311,8 +372,10 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   constexpr int KD = 64, VD = 64;
   __shared__ __align__(16) int8_t hi[KD][VD];
   __shared__ __align__(16) int8_t lo[KD][VD];
-  __shared__ float sc[KD][2];
-  __shared__ float qn[KD], kn[KD], gv[KD], U[VD], OUT[VD], s_misc[4];
+  __shared__ __align__(16) float sc[KD][2];
+  __shared__ __align__(16) float qc[KD], kc[KD], vcs[VD], zs[VD];
+  __shared__ __align__(16) float qn[KD], kn[KD], gv[KD], U[VD], OUT[VD];
+  __shared__ float s_misc[4];
   const KdaSeq sq = seqs[blockIdx.y];
   const int h = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -320,20 +383,22 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   const size_t seq_off = (size_t)sq.seq * seq_stride_q;
   {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    const int4* sh = reinterpret_cast<const int4*>(st_hi + off);
-    const int4* sl = reinterpret_cast<const int4*>(st_lo + off);
-    for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
-      reinterpret_cast<int4*>(&hi[0][0])[i] = sh[i];
-      reinterpret_cast<int4*>(&lo[0][0])[i] = sl[i];
+    if (tid < KD * VD / 16) {
+      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
+      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
     }
-    const float* ss = st_sc + off / 32;
-    for (int i = tid; i < KD * 2; i += blockDim.x) (&sc[0][0])[i] = ss[i];
+    if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
   }
-  __syncthreads();
   for (int t = 0; t < sq.nrows; t++) {
     const int r = sq.row0 + t;
-    const float* qc = conv_out + (size_t)r * ldc + h * KD;
-    const float* kc = conv_out + (size_t)r * ldc + kdim + h * KD;
+    if (tid < 64) {
+      qc[tid] = conv_out[(size_t)r * ldc + h * KD + tid];
+      kc[tid] = conv_out[(size_t)r * ldc + kdim + h * KD + tid];
+      vcs[tid] = conv_out[(size_t)r * ldc + 2 * kdim + h * VD + tid];
+      zs[tid] = inproj[(size_t)r * ldi + off_g + h * VD + tid];
+      gv[tid] = gate[(size_t)r * nvk + h * KD + tid];
+    }
+    __syncthreads();
     if (tid == 0) s_misc[0] = rsqrt_body(__fadd_rn(seq_sumsq(qc, KD), kL2Eps));
     if (tid == 32) s_misc[1] = rsqrt_body(__fadd_rn(seq_sumsq(kc, KD), kL2Eps));
     if (tid == 64) s_misc[2] = sigmoid(inproj[(size_t)r * ldi + off_b + h]);
@@ -341,23 +406,23 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     if (tid < KD) {
       qn[tid] = __fmul_rn(__fmul_rn(qc[tid], s_misc[0]), ssm_scale);
       kn[tid] = __fmul_rn(kc[tid], s_misc[1]);
-      gv[tid] = gate[(size_t)r * nvk + h * KD + tid];
     }
     __syncthreads();
     if (tid < VD) {
       const int vv = tid, grp = vv >> 5;
       float u = 0.0f, w = 0.0f, kq = 0.0f;
+#pragma unroll 8
       for (int kk = 0; kk < KD; kk++) {
-        const float kcv = kn[kk], qcv = qn[kk];
-        const float kcw = __fmul_rn(kcv, gv[kk]), qcw = __fmul_rn(qcv, gv[kk]);
+        const float kcv = kn[kk], qcv = qn[kk], g = gv[kk];
+        const float kcw = __fmul_rn(kcv, g), qcw = __fmul_rn(qcv, g);
         kq = __fadd_rn(kq, __fmul_rn(kcv, qcv));
-        const float sck = __fmul_rn(sc[kk][grp], kcw), scq = __fmul_rn(sc[kk][grp], qcw);
+        const float s = sc[kk][grp];
+        const float sck = __fmul_rn(s, kcw), scq = __fmul_rn(s, qcw);
         const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
         u = __fadd_rn(u, __fmul_rn(e, sck));
         w = __fadd_rn(w, __fmul_rn(e, scq));
       }
-      const float vval = conv_out[(size_t)r * ldc + 2 * kdim + h * VD + vv];
-      u = __fmul_rn(__fsub_rn(vval, u), s_misc[2]);
+      u = __fmul_rn(__fsub_rn(vcs[vv], u), s_misc[2]);
       U[vv] = u;
       OUT[vv] = __fadd_rn(w, __fmul_rn(u, kq));
     }
@@ -384,21 +449,17 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     if (adv) {
       const int so = (sq.base_slot + t + 1) % depth;
       const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
-      int4* dh = reinterpret_cast<int4*>(st_hi + off);
-      int4* dl = reinterpret_cast<int4*>(st_lo + off);
-      for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
-        dh[i] = reinterpret_cast<const int4*>(&hi[0][0])[i];
-        dl[i] = reinterpret_cast<const int4*>(&lo[0][0])[i];
+      if (tid < KD * VD / 16) {
+        reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+        reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
       }
-      float* ds = st_sc + off / 32;
-      for (int i = tid; i < KD * 2; i += blockDim.x) ds[i] = (&sc[0][0])[i];
+      if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
     }
     // gated RMSNorm of the head output, then per-32 quantisation.
     if (tid == 0) s_misc[3] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT, VD), (float)VD), eps));
     __syncthreads();
     if (tid < VD) {
-      const float zg = inproj[(size_t)r * ldi + off_g + h * VD + tid];
-      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[tid], s_misc[3]), o_norm[tid]), silu(zg));
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[tid], s_misc[3]), o_norm[tid]), silu(zs[tid]));
       oq[(size_t)r * vdim + h * VD + tid] =
           warp_quant32(o, &os[(size_t)r * (vdim / 32) + (h * VD) / 32 + (tid >> 5)]);
     }
@@ -406,75 +467,73 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   }
   if (!adv) {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    int4* dh = reinterpret_cast<int4*>(st_hi + off);
-    int4* dl = reinterpret_cast<int4*>(st_lo + off);
-    for (int i = tid; i < KD * VD / 16; i += blockDim.x) {
-      dh[i] = reinterpret_cast<const int4*>(&hi[0][0])[i];
-      dl[i] = reinterpret_cast<const int4*>(&lo[0][0])[i];
+    if (tid < KD * VD / 16) {
+      reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+      reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
     }
-    float* ds = st_sc + off / 32;
-    for (int i = tid; i < KD * 2; i += blockDim.x) ds[i] = (&sc[0][0])[i];
+    if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
   }
 }
 
 // ---------------------------------------------------------------- MoE
 
-// Router of one token row per warp: sigmoid scores, key = score + bias,
-// top-k by key (first index on ties), weights = scores renormalised by
-// their sequential sum in selection order (src/ops_moe.c:12-163); then
-// the per-32 quantisation of the row's latent (src/forward_moe.c:150).
+// Router of one token row: sigmoid scores, key = score + bias, top-k by key
+// (first index on ties), weights = scores renormalised by their sequential
+// sum in selection order (src/ops_moe.c:12-163), by warp 0; then the per-32
+// quantisation of the row's latent (src/forward_moe.c:150) by all warps.
+// E <= 256.
 __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
                                  const float* __restrict__ bias, int E, int topk, int latent,
                                  int* pair_expert, float* pair_w, int8_t* latq, float* lats) {
-  const int r = blockIdx.x, lane = threadIdx.x;
-  float score[8], key[8];
-  const int nj = (E + 31) / 32;
-  for (int j = 0; j < nj; j++) {
-    int e = lane + 32 * j;
-    if (e < E) {
-      score[j] = sigmoid(moein[(size_t)r * ldm + off_router + e]);
-      key[j] = __fadd_rn(score[j], bias[e]);
-    } else {
-      score[j] = 0.0f;
-      key[j] = -1e30f;
-    }
-  }
-  float wsel[16];
-  int isel[16];
-  float wsum = 0.0f;
-  for (int t = 0; t < topk; t++) {
-    uint32_t bk = 0;
-    int bi = 0x7fffffff;
-    for (int j = 0; j < nj; j++) {
-      int e = lane + 32 * j;
-      if (e < E && key[j] > -1e30f) {
-        uint32_t k = fkey(key[j]);
-        if (bi == 0x7fffffff || k > bk) { bk = k; bi = e; }
+  const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    float score[8], key[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int e = lane + 32 * j;
+      if (e < E) {
+        score[j] = sigmoid(moein[(size_t)r * ldm + off_router + e]);
+        key[j] = __fadd_rn(score[j], bias[e]);
+      } else {
+        score[j] = 0.0f;
+        key[j] = -1e30f;
       }
     }
-    for (int o = 16; o > 0; o >>= 1) {
-      uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
-      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (i2 != 0x7fffffff && (bi == 0x7fffffff || k2 > bk || (k2 == bk && i2 < bi))) { bk = k2; bi = i2; }
-    }
-    float sw = 0.0f;
-    if (bi != 0x7fffffff && (bi & 31) == lane) {
-      sw = score[bi >> 5];
-      key[bi >> 5] = -1e30f;
-    }
-    sw = __shfl_sync(0xffffffffu, sw, bi == 0x7fffffff ? 0 : (bi & 31));
-    isel[t] = bi == 0x7fffffff ? -1 : bi;
-    wsel[t] = bi == 0x7fffffff ? 0.0f : sw;
-    wsum = __fadd_rn(wsum, wsel[t]);
-  }
-  if (lane == 0) {
+    float wsum = 0.0f;
     for (int t = 0; t < topk; t++) {
-      pair_expert[r * topk + t] = isel[t];
-      pair_w[r * topk + t] = (wsum > 0.0f && isel[t] >= 0) ? __fdiv_rn(wsel[t], wsum) : wsel[t];
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int e = lane + 32 * j;
+        if (e < E && key[j] > -1e30f) {
+          const unsigned long long kk = ((unsigned long long)fkey(key[j]) << 32) | (0xFFFFFFFFu - (uint32_t)e);
+          best = kk > best ? kk : best;
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+        best = b2 > best ? b2 : best;
+      }
+      const int bi = best ? argmax_index(best) : -1;
+      float sw = 0.0f;
+      if (bi >= 0 && (bi & 31) == lane) {
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j == (bi >> 5)) { sw = score[j]; key[j] = -1e30f; }
+      }
+      sw = __shfl_sync(0xffffffffu, sw, bi >= 0 ? (bi & 31) : 0);
+      wsum = __fadd_rn(wsum, bi >= 0 ? sw : 0.0f);
+      if (lane == 0) {
+        pair_expert[r * topk + t] = bi;
+        pair_w[r * topk + t] = bi >= 0 ? sw : 0.0f;
+      }
     }
+    __syncwarp();
+    if (lane < topk && wsum > 0.0f && pair_expert[r * topk + lane] >= 0)
+      pair_w[r * topk + lane] = __fdiv_rn(pair_w[r * topk + lane], wsum);
   }
-  for (int g = 0; g < latent / 32; g++) {
-    float v = moein[(size_t)r * ldm + off_lat + g * 32 + lane];
+  for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
+    const float v = moein[(size_t)r * ldm + off_lat + g * 32 + lane];
     latq[(size_t)r * latent + g * 32 + lane] = warp_quant32(v, &lats[(size_t)r * (latent / 32) + g]);
   }
 }
@@ -482,13 +541,13 @@ __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int o
 // One (token, expert) pair, 32 consecutive FFN outputs of w1 and of w3:
 // int8 GEMV over the pair's quantised latent, silu(w1.x)*(w3.x), and the
 // per-32 quantisation of that group (src/forward_moe.c:189-196).
-// w13 is the expert's [w1 rows; w3 rows] ([2*ffn][latent]).
+// w13 is the expert's [w1 rows; w3 rows] ([2*ffn][latent]), latent <= 1024.
 __global__ void __launch_bounds__(256)
 moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent, int gs,
                const int* __restrict__ pair_expert, int topk,
                const int8_t* __restrict__ latq, const float* __restrict__ lats,
                int8_t* hq, float* hs) {
-  __shared__ float P[8][32];
+  __shared__ __align__(16) float P[8][8][32];
   __shared__ float H[64];
   const int p = blockIdx.y, r = p / topk;
   const int e = pair_expert[p];
@@ -499,22 +558,37 @@ moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, 
   const float* xsr = lats + (size_t)r * nsb;
   const size_t wbase = (size_t)e * 2 * ffn * latent;
   const size_t sbase = (size_t)e * 2 * ffn * ng;
+  int4 xa = make_int4(0, 0, 0, 0), xb = xa;
+  float xsv = 0.0f;
+  if (lane < nsb) {
+    xa = __ldg(reinterpret_cast<const int4*>(xr + lane * 32));
+    xb = __ldg(reinterpret_cast<const int4*>(xr + lane * 32 + 16));
+    xsv = __ldg(xsr + lane);
+  }
+  int4 wa[8], wb[8];
+  float wsv[8];
+#pragma unroll
   for (int k = 0; k < 8; k++) {
-    const int lr = warp * 8 + k;                     // 0..63 within the block
+    const int lr = warp * 8 + k;
     const int orow = (lr < 32) ? blockIdx.x * 32 + lr : ffn + blockIdx.x * 32 + (lr - 32);
-    const int8_t* wr = w13q + wbase + (size_t)orow * latent;
-    const float* wsr = w13s + sbase + (size_t)orow * ng;
-    for (int s = lane; s < nsb; s += 32) {
-      int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-      int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
-      int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
-      int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-      float a = (float)dot32(wa, wb, xa, xb);
-      P[warp][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+    if (lane < nsb) {
+      const int8_t* wr = w13q + wbase + (size_t)orow * latent;
+      wa[k] = __ldg(reinterpret_cast<const int4*>(wr + lane * 32));
+      wb[k] = __ldg(reinterpret_cast<const int4*>(wr + lane * 32 + 16));
+      wsv[k] = rb == 1 ? __ldg(w13s + sbase + (size_t)orow * ng + lane) : 0.0f;
     }
-    __syncwarp();
-    if (lane == 0) H[lr] = q8_reduce(P[warp], wsr, rb, ng);
-    __syncwarp();
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k++)
+    if (lane < nsb) {
+      const float a = (float)dot32(wa[k], wb[k], xa, xb);
+      P[warp][k][lane] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[k]));
+    }
+  __syncwarp();
+  if (lane < 8) {
+    const int lr = warp * 8 + lane;
+    const int orow = (lr < 32) ? blockIdx.x * 32 + lr : ffn + blockIdx.x * 32 + (lr - 32);
+    H[lr] = q8_reduce(P[warp][lane], w13s + sbase + (size_t)orow * ng, rb, ng);
   }
   __syncthreads();
   if (warp == 0) {
@@ -524,12 +598,12 @@ moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, 
   }
 }
 
-// w2 (latent x ffn) of every pair, one warp per output row.
+// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048.
 __global__ void __launch_bounds__(256)
 moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int ffn, int latent, int gs,
               const int* __restrict__ pair_expert,
               const int8_t* __restrict__ hq, const float* __restrict__ hs, float* h2) {
-  __shared__ float P[8][kNsbMax];
+  __shared__ __align__(16) float P[8][64];
   const int p = blockIdx.y;
   const int e = pair_expert[p];
   if (e < 0) return;
@@ -541,13 +615,18 @@ moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int
   const float* wsr = w2s + ((size_t)e * latent + n) * ng;
   const int8_t* xr = hq + (size_t)p * ffn;
   const float* xsr = hs + (size_t)p * nsb;
-  for (int s = lane; s < nsb; s += 32) {
-    int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-    int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
-    int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
-    int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-    float a = (float)dot32(wa, wb, xa, xb);
-    P[warp][s] = rb > 1 ? __fmul_rn(a, xsr[s]) : __fmul_rn(a, __fmul_rn(xsr[s], wsr[s]));
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int s = lane + 32 * j;
+    if (s < nsb) {
+      const int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+      const int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+      const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+      const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+      const float a = (float)dot32(wa, wb, xa, xb);
+      const float xsv = __ldg(xsr + s);
+      P[warp][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, __ldg(wsr + s)));
+    }
   }
   __syncwarp();
   if (lane == 0) h2[(size_t)p * latent + n] = q8_reduce(P[warp], wsr, rb, ng);
@@ -581,7 +660,7 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
                                  const float* __restrict__ hid, const int* __restrict__ hid_idx,
                                  const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
                                  int8_t* xq, float* xs) {
-  extern __shared__ float sm[];           // [2][d]
+  extern __shared__ __align__(16) float sm[];           // [2][d]
   __shared__ float s_inv[2];
   const int r = blockIdx.x;
   const int hr = hid_idx ? hid_idx[r] : r;
@@ -606,7 +685,7 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
 }
 
 // Per-head RMSNorm (1+w) then RoPE of the first rot dims, in place on a
-// 64-wide shared vector; called by one warp pair (64 threads).
+// 64-wide shared vector; called by every thread of the block.
 LZ_HD void head_norm_rope(float* v, const float* w, float eps, int hd, int rot,
                           const float* cs_row, float* s_inv) {
   const int i = threadIdx.x;
@@ -638,13 +717,13 @@ struct MtpRow {            // one draft / prefill row of the MTP block
 
 // K/V side of the MTP attention for one (row, kv head): k RMSNorm, RoPE,
 // Q8 write of k and v into the row's sequence cache at `pos`
-// (src/forward_attn.c:909-965).
+// (src/forward_attn.c:909-965).  64 threads (hd = 64).
 __global__ void mtp_kv_write_kernel(const float* __restrict__ qkv, int ldq, int off_k, int off_v,
                                     const MtpRow* __restrict__ rows, const float* __restrict__ k_norm,
                                     float eps, int hd, int rot, int kvd, const float* __restrict__ rope_cs,
                                     int8_t* kq, float* ks, int8_t* vq, float* vs,
                                     size_t cache_seq_stride) {
-  __shared__ float v[64];
+  __shared__ __align__(16) float v[64];
   __shared__ float s_inv;
   const int h = blockIdx.x, r = blockIdx.y;
   const MtpRow row = rows[r];
@@ -654,27 +733,33 @@ __global__ void mtp_kv_write_kernel(const float* __restrict__ qkv, int ldq, int 
   __syncthreads();
   head_norm_rope(v, k_norm, eps, hd, rot, rope_cs + (size_t)row.pos * rot, &s_inv);
   const size_t cb = (size_t)row.seq * cache_seq_stride + (size_t)row.pos * kvd;
-  const size_t sb = ((size_t)row.seq * cache_seq_stride + (size_t)row.pos * kvd) / 32;
-  kq[cb + h * hd + i] = warp_quant32(v[i], &ks[sb + (h * hd) / 32 + (i >> 5)]);
+  kq[cb + h * hd + i] = warp_quant32(v[i], &ks[cb / 32 + (h * hd) / 32 + (i >> 5)]);
   const float vv = qkv[(size_t)r * ldq + off_v + h * hd + i];
-  vq[cb + h * hd + i] = warp_quant32(vv, &vs[sb + (h * hd) / 32 + (i >> 5)]);
+  vq[cb + h * hd + i] = warp_quant32(vv, &vs[cb / 32 + (h * hd) / 32 + (i >> 5)]);
 }
 
 // Gated attention of one (row, head) over the row's MTP cache t <= pos:
 // q RMSNorm + RoPE, Q8 scores (32-element partial sums, sequential), the
-// reference softmax (sequential sum), weighted V sum (sequential over t),
-// times sigmoid(gate), then per-32 quantisation for o_proj.
+// reference softmax (sequential sum), weighted V sum (sequential over t,
+// V staged through shared memory in chunks), times sigmoid(gate), then
+// per-32 quantisation for o_proj.  hd = 64.
 // src/forward_attn.c:17-41, 206-640, src/ops_norm.c:903-985.
-__global__ void mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
-                                const MtpRow* __restrict__ rows, const float* __restrict__ q_norm,
-                                float eps, int hd, int rot, int kvd, int kv_mul,
-                                const float* __restrict__ rope_cs, float scale,
-                                const int8_t* __restrict__ kq, const float* __restrict__ ks,
-                                const int8_t* __restrict__ vq, const float* __restrict__ vs,
-                                size_t cache_seq_stride, int8_t* aq, float* as) {
-  extern __shared__ float att[];
-  __shared__ float qh[64];
+constexpr int kAttnThreads = 128;
+constexpr int kAttnChunk = 256;
+__global__ void __launch_bounds__(kAttnThreads)
+mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
+                const MtpRow* __restrict__ rows, const float* __restrict__ q_norm,
+                float eps, int hd, int rot, int kvd, int kv_mul,
+                const float* __restrict__ rope_cs, float scale,
+                const int8_t* __restrict__ kq, const float* __restrict__ ks,
+                const int8_t* __restrict__ vq, const float* __restrict__ vs,
+                size_t cache_seq_stride, int8_t* aq, float* as) {
+  extern __shared__ __align__(16) float att[];
+  __shared__ __align__(16) float qh[64];
+  __shared__ __align__(16) int8_t vch[kAttnChunk][64];
+  __shared__ __align__(16) float vsc[kAttnChunk][2];
   __shared__ float s_red[2];
+  __shared__ uint32_t wk[kAttnThreads / 32];
   const int h = blockIdx.x, r = blockIdx.y;
   const MtpRow row = rows[r];
   if (!row.active) return;
@@ -685,27 +770,34 @@ __global__ void mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
   __syncthreads();
   head_norm_rope(qh, q_norm, eps, hd, rot, rope_cs + (size_t)pos * rot, &s_red[0]);
   const size_t cb = (size_t)row.seq * cache_seq_stride;
+  uint32_t bk = 0;
   for (int t = i; t <= pos; t += blockDim.x) {
     const int8_t* kt = kq + cb + (size_t)t * kvd + kvh * hd;
     const float* kts = ks + (cb + (size_t)t * kvd + kvh * hd) / 32;
+    int4 k4[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) k4[c] = __ldg(reinterpret_cast<const int4*>(kt) + c);
+    const float s0 = __ldg(kts), s1 = __ldg(kts + 1);
+    const int8_t* kb = reinterpret_cast<const int8_t*>(k4);
     float sum = 0.0f;
-    for (int dd = 0; dd < hd; dd += 32) {
+#pragma unroll
+    for (int dd = 0; dd < 64; dd += 32) {
       float acc = 0.0f;
-      for (int e = 0; e < 32; e++) acc = __fadd_rn(acc, __fmul_rn(qh[dd + e], (float)kt[dd + e]));
-      sum = __fadd_rn(sum, __fmul_rn(acc, kts[dd >> 5]));
+#pragma unroll
+      for (int e = 0; e < 32; e++) acc = __fadd_rn(acc, __fmul_rn(qh[dd + e], (float)kb[dd + e]));
+      sum = __fadd_rn(sum, __fmul_rn(acc, dd ? s1 : s0));
     }
-    att[t] = __fmul_rn(sum, scale);
+    const float a = __fmul_rn(sum, scale);
+    att[t] = a;
+    const uint32_t k = fkey(a);
+    bk = k > bk ? k : bk;
   }
-  __syncthreads();
-  uint32_t bk = 0;
-  for (int t = i; t <= pos; t += blockDim.x) { uint32_t k = fkey(att[t]); bk = k > bk ? k : bk; }
   bk = warp_max_u32(bk);
-  __shared__ uint32_t wk[32];
   if ((i & 31) == 0) wk[i >> 5] = bk;
   __syncthreads();
   if (i == 0) {
     uint32_t m = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = wk[w] > m ? wk[w] : m;
+    for (int w = 0; w < kAttnThreads / 32; w++) m = wk[w] > m ? wk[w] : m;
     const uint32_t u = (m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m;
     s_red[1] = __uint_as_float(u);
   }
@@ -714,20 +806,34 @@ __global__ void mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
   for (int t = i; t <= pos; t += blockDim.x) att[t] = exp_body(__fsub_rn(att[t], mx));
   __syncthreads();
   if (i == 0) {
-    float sum = 0.0f;
-    for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, att[t]);
+    const float sum = seq_sum(att, pos + 1);
     s_red[0] = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
   }
   __syncthreads();
   const float inv = s_red[0];
   for (int t = i; t <= pos; t += blockDim.x) att[t] = __fmul_rn(att[t], inv);
-  __syncthreads();
-  if (i < hd) {
-    float out = 0.0f;
-    for (int t = 0; t <= pos; t++) {
-      const size_t o = cb + (size_t)t * kvd + kvh * hd + i;
-      out = __fadd_rn(out, __fmul_rn(__fmul_rn(att[t], (float)vq[o]), vs[o / 32]));
+  float out = 0.0f;
+  for (int t0 = 0; t0 <= pos; t0 += kAttnChunk) {
+    const int nt = min(kAttnChunk, pos + 1 - t0);
+    __syncthreads();
+    for (int q = i; q < nt * 4; q += blockDim.x) {
+      const int tt = q >> 2, c = q & 3;
+      reinterpret_cast<int4*>(&vch[tt][0])[c] =
+          __ldg(reinterpret_cast<const int4*>(vq + cb + (size_t)(t0 + tt) * kvd + kvh * hd) + c);
     }
+    for (int q = i; q < nt * 2; q += blockDim.x) {
+      const int tt = q >> 1, c = q & 1;
+      vsc[tt][c] = __ldg(vs + (cb + (size_t)(t0 + tt) * kvd + kvh * hd) / 32 + c);
+    }
+    __syncthreads();
+    if (i < hd) {
+      const int g = i >> 5;
+#pragma unroll 8
+      for (int tt = 0; tt < nt; tt++)
+        out = __fadd_rn(out, __fmul_rn(__fmul_rn(att[t0 + tt], (float)vch[tt][i]), vsc[tt][g]));
+    }
+  }
+  if (i < hd) {
     out = __fmul_rn(out, sigmoid(qkv[(size_t)r * ldq + (size_t)h * 2 * hd + hd + i]));
     aq[(size_t)r * qd + h * hd + i] = warp_quant32(out, &as[(size_t)r * (qd / 32) + (h * hd) / 32 + (i >> 5)]);
   }
@@ -739,14 +845,16 @@ struct SeqRound {          // per-sequence round bookkeeping on the device
   int anchor, anchor_pos, mtp_pos, ssm_slot;
   int k, n_accept, n_emit, done;
   int draft[8], out[8];
+  int rounds, emitted, accepted, drafted;   // running totals
 };
 
 // Greedy acceptance of one round (src/generate.c:232-243, 798-991): the
-// verify argmax of every row, accept the agreeing draft prefix, point
+// verify arg-max of every row, accept the agreeing draft prefix, point
 // the state ring at the accepted slot, reseed the draft chain from the
 // verify hidden row n_accept, set up the catch-up rows and advance the
 // MTP position.
-__global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax, const int* __restrict__ vmax,
+__global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax,
+                                          const unsigned long long* __restrict__ vmax,
                                           const float* __restrict__ vhid, int d, float* chain,
                                           int depth, int seq_len, MtpRow* catch_rows, int* catch_tok,
                                           int* catch_hidx) {
@@ -759,12 +867,16 @@ __global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax, cons
   if (threadIdx.x == 0) {
     int n_accept = k;
     for (int i = 0; i < k; i++) {
-      s.out[i] = vmax[row0 + i];
+      s.out[i] = argmax_index(vmax[row0 + i]);
       if (s.draft[i] != s.out[i]) { n_accept = i; break; }
     }
-    if (n_accept == k) s.out[k] = vmax[row0 + k];
+    if (n_accept == k) s.out[k] = argmax_index(vmax[row0 + k]);
     s.n_accept = n_accept;
     s.n_emit = n_accept + 1;
+    s.rounds += 1;
+    s.emitted += n_accept + 1;
+    s.accepted += n_accept;
+    s.drafted += k;
     s.ssm_slot = (s.ssm_slot + n_accept + 1) % depth;
     for (int j = 0; j < kmax - 1; j++) {
       MtpRow cr;

@@ -71,6 +71,9 @@ def lib():
         "lz_generate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                 ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
                                 c_char_p, c_int]),
+        "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
+        "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
+                                     P(ctypes.c_double), P(c_int)]),
         "lz_state_stream": (c_void_p, [c_void_p]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
     }
@@ -89,7 +92,7 @@ EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_s
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
            "lz_seq_prefill", "lz_spec_round_batch", "lz_set_graphs", "lz_generate", "lz_state_stream",
-           "lz_state_launches"]
+           "lz_state_launches", "lz_state_counters", "lz_profile_round"]
 
 
 class Model:
@@ -148,6 +151,24 @@ class State:
     def set_chain(self, c, seq=0):
         c = np.ascontiguousarray(c, np.float32)
         lib().lz_state_set_chain(self.h, seq, _ptr(c))
+
+    def counters(self, seq=0):
+        v = [c_int() for _ in range(4)]
+        lib().lz_state_counters(self.h, seq, *[ctypes.byref(x) for x in v])
+        return tuple(x.value for x in v)
+
+    def profile_round(self, k):
+        gm, gb, rm = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        ng, nk = c_int(), c_int()
+        rc = lib().lz_profile_round(self.h, k, ctypes.byref(gm), ctypes.byref(gb), ctypes.byref(ng),
+                                    ctypes.byref(rm), ctypes.byref(nk))
+        if rc:
+            raise LzError(f"profile round failed ({rc})")
+        return {"gemv_ms": gm.value, "gemv_bytes": gb.value, "n_gemv": ng.value,
+                "round_ms": rm.value, "n_kernels": nk.value}
+
+    def stream(self):
+        return lib().lz_state_stream(self.h)
 
     def launches(self):
         return int(lib().lz_state_launches(self.h))

@@ -134,42 +134,6 @@ def quantize_q8_rows(w: np.ndarray, gs: int):
     return q.reshape(-1), scale
 
 
-class _Writer:
-    def __init__(self, f, cfg: KunMoeConfig):
-        self.f = f
-        self.cfg = cfg
-        self.idx = 0
-        self.digest = hashlib.sha256()
-
-    def _rng(self):
-        self.idx += 1
-        return np.random.default_rng([self.cfg.seed, self.idx])
-
-    def _put(self, b: bytes):
-        self.f.write(b)
-        self.digest.update(b)
-
-    def normal(self, shape, std=0.02, offset=0.0):
-        x = self._rng().standard_normal(int(np.prod(shape)), dtype=np.float32)
-        x = x * np.float32(std)
-        if offset:
-            x = x + np.float32(offset)
-        return _bf16_round(x)
-
-    def f32(self, arr: np.ndarray):
-        arr = np.ascontiguousarray(arr, dtype=np.float32).reshape(-1)
-        self._put(struct.pack("<BI", FMT_F32, arr.size))
-        self._put(arr.tobytes())
-
-    def q8(self, out_dim: int, in_dim: int):
-        gs = self.cfg.gs(in_dim)
-        w = self.normal((out_dim, in_dim))
-        q, s = quantize_q8_rows(w, gs)
-        self._put(struct.pack("<BII", FMT_Q8_0, q.size, gs))
-        self._put(q.tobytes())
-        self._put(s.astype("<f4").tobytes())
-
-
 def header_words(cfg: KunMoeConfig) -> bytes:
     c = cfg
     w = []
@@ -209,9 +173,91 @@ def header_words(cfg: KunMoeConfig) -> bytes:
     return b"L98Z" + struct.pack("<I", 5) + b"".join(w)
 
 
-def write_model(cfg: KunMoeConfig, out_dir: str) -> str:
-    """Write ``out_dir/model.bin`` (and a config.json describing it); returns
-    the sha256 of the tensor stream.  Idempotent: an existing file whose
+def tensor_specs(cfg: KunMoeConfig):
+    """Every tensor of the file in model_walk order: (kind, shape, std,
+    offset) with kind "q8" (shape = (out, in)) or "f32"."""
+    c = cfg
+    kdim = c.key_dim
+    q_dim = c.n_heads * c.head_dim
+    kv_dim = c.n_kv_heads * c.head_dim
+    specs = []
+    q8 = lambda o, i: specs.append(("q8", (o, i), 0.02, 0.0))
+    f32 = lambda shape, std=0.02, off=0.0: specs.append(("f32", shape, std, off))
+    q8(c.vocab, c.hidden)                          # embed_tokens (tied lm_head)
+    f32((c.hidden,))                               # final norm
+    for _ in range(c.n_layers):
+        f32((c.hidden,)); f32((c.hidden,))         # input / post_attention layernorm
+        q8(kdim, c.hidden); q8(kdim, c.hidden); q8(kdim, c.hidden)     # q, k, v proj
+        for _c in range(3):
+            f32((kdim, 1, c.conv_kernel), std=0.2) # q/k/v conv1d
+        f32((c.kda_heads,))                        # A_log
+        q8(c.gate_rank, c.hidden)                  # f_a_proj
+        q8(kdim, c.gate_rank)                      # f_b_proj
+        f32((kdim,))                               # dt_bias
+        q8(c.kda_heads, c.hidden)                  # b_proj
+        q8(kdim, c.hidden)                         # g_proj
+        f32((c.kda_head_dim,), off=1.0)            # o_norm (multiplies directly)
+        q8(c.hidden, kdim)                         # o_proj
+        q8(c.n_experts, c.hidden)                  # router
+        f32((c.n_experts,))                        # e_score_correction_bias
+        q8(c.latent, c.hidden)                     # routed_expert_down_proj
+        q8(c.hidden, c.latent)                     # routed_expert_up_proj
+        if c.shared_width:
+            q8(c.shared_width, c.hidden); q8(c.shared_width, c.hidden)   # shared gate / up
+            q8(c.hidden, c.shared_width)           # shared down
+        for _e in range(c.n_experts):
+            q8(c.moe_ffn, c.latent); q8(c.latent, c.moe_ffn); q8(c.moe_ffn, c.latent)  # w1, w2, w3
+    f32((c.hidden,)); f32((c.hidden,))             # MTP input / post_attention layernorm
+    q8(2 * q_dim, c.hidden)                        # q_proj (q | gate interleaved per head)
+    q8(kv_dim, c.hidden); q8(kv_dim, c.hidden)     # k_proj, v_proj
+    q8(c.hidden, q_dim)                            # o_proj
+    f32((c.head_dim,)); f32((c.head_dim,))         # q_norm, k_norm
+    q8(c.mtp_ffn, c.hidden); q8(c.mtp_ffn, c.hidden)   # mlp gate / up
+    q8(c.hidden, c.mtp_ffn)                        # mlp down
+    q8(c.hidden, 2 * c.hidden)                     # fc
+    f32((c.hidden,)); f32((c.hidden,)); f32((c.hidden,))   # norm, pre_fc_norm_hidden/embedding
+    out, off = [], len(header_words(cfg))
+    for kind, shape, std, o in specs:
+        n = int(np.prod(shape))
+        size = 5 + 4 * n if kind == "f32" else 9 + n + 4 * (n // cfg.gs(shape[1]))
+        out.append((kind, shape, std, o, off))
+        off += size
+    return out, off
+
+
+def _tensor_bytes(cfg: KunMoeConfig, idx: int, spec) -> bytes:
+    kind, shape, std, o, _ = spec
+    n = int(np.prod(shape))
+    rng = np.random.default_rng([cfg.seed, idx + 1])
+    x = rng.standard_normal(n, dtype=np.float32) * np.float32(std)
+    if o:
+        x = x + np.float32(o)
+    x = _bf16_round(x)
+    if kind == "f32":
+        return struct.pack("<BI", FMT_F32, n) + x.astype("<f4").tobytes()
+    gs = cfg.gs(shape[1])
+    q, s = quantize_q8_rows(x, gs)
+    return struct.pack("<BII", FMT_Q8_0, n, gs) + q.tobytes() + s.astype("<f4").tobytes()
+
+
+def _write_range(args):
+    cfg, path, lo, hi = args
+    specs, _ = tensor_specs(cfg)
+    fd = os.open(path, os.O_WRONLY)
+    try:
+        for i in range(lo, hi):
+            b = _tensor_bytes(cfg, i, specs[i])
+            os.pwrite(fd, b, specs[i][4])
+    finally:
+        os.close(fd)
+    return hi - lo
+
+
+def write_model(cfg: KunMoeConfig, out_dir: str, workers: int | None = None) -> str:
+    """Write ``out_dir/model.bin`` (and lz98_synth.json describing it);
+    returns the sha256 of the whole file.  Tensor i draws from
+    default_rng([seed, i + 1]), so the bytes do not depend on how many
+    worker processes share the work.  Idempotent: an existing file whose
     recorded config matches is kept."""
     os.makedirs(out_dir, exist_ok=True)
     meta_path = os.path.join(out_dir, "lz98_synth.json")
@@ -221,69 +267,37 @@ def write_model(cfg: KunMoeConfig, out_dir: str) -> str:
         try:
             with open(meta_path) as f:
                 have = json.load(f)
-            if have.get("config") == want:
+            if have.get("config") == want and os.path.getsize(bin_path) == have.get("bytes"):
                 return have["sha256"]
         except (OSError, ValueError, KeyError):
             pass
-    c = cfg
-    kdim = c.key_dim
-    q_dim = c.n_heads * c.head_dim
-    kv_dim = c.n_kv_heads * c.head_dim
+    specs, total = tensor_specs(cfg)
     tmp = bin_path + ".tmp"
     with open(tmp, "wb") as f:
         f.write(header_words(cfg))
-        w = _Writer(f, cfg)
-        w.q8(c.vocab, c.hidden)                       # embed_tokens (tied lm_head)
-        w.f32(w.normal((c.hidden,)))                  # final norm
-        for _ in range(c.n_layers):
-            w.f32(w.normal((c.hidden,)))              # input_layernorm
-            w.f32(w.normal((c.hidden,)))              # post_attention_layernorm
-            w.q8(kdim, c.hidden)                      # q_proj
-            w.q8(kdim, c.hidden)                      # k_proj
-            w.q8(kdim, c.hidden)                      # v_proj
-            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # q_conv1d
-            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # k_conv1d
-            w.f32(w.normal((kdim, 1, c.conv_kernel), std=0.2))   # v_conv1d
-            w.f32(w.normal((c.kda_heads,)))           # A_log
-            w.q8(c.gate_rank, c.hidden)               # f_a_proj
-            w.q8(kdim, c.gate_rank)                   # f_b_proj
-            w.f32(w.normal((kdim,)))                  # dt_bias
-            w.q8(c.kda_heads, c.hidden)               # b_proj
-            w.q8(kdim, c.hidden)                      # g_proj
-            w.f32(w.normal((c.kda_head_dim,), offset=1.0))   # o_norm (multiplies directly)
-            w.q8(c.hidden, kdim)                      # o_proj
-            w.q8(c.n_experts, c.hidden)               # router
-            w.f32(w.normal((c.n_experts,)))           # e_score_correction_bias
-            w.q8(c.latent, c.hidden)                  # routed_expert_down_proj
-            w.q8(c.hidden, c.latent)                  # routed_expert_up_proj
-            if c.shared_width:
-                w.q8(c.shared_width, c.hidden)        # shared gate
-                w.q8(c.shared_width, c.hidden)        # shared up
-                w.q8(c.hidden, c.shared_width)        # shared down
-            for _e in range(c.n_experts):
-                w.q8(c.moe_ffn, c.latent)             # w1
-                w.q8(c.latent, c.moe_ffn)             # w2
-                w.q8(c.moe_ffn, c.latent)             # w3
-        # MTP block: attention rows of LAYER_SPECS, dense FFN, then the head.
-        w.f32(w.normal((c.hidden,)))                  # input_layernorm
-        w.f32(w.normal((c.hidden,)))                  # post_attention_layernorm
-        w.q8(2 * q_dim, c.hidden)                     # q_proj (q | gate interleaved per head)
-        w.q8(kv_dim, c.hidden)                        # k_proj
-        w.q8(kv_dim, c.hidden)                        # v_proj
-        w.q8(c.hidden, q_dim)                         # o_proj
-        w.f32(w.normal((c.head_dim,)))                # q_norm
-        w.f32(w.normal((c.head_dim,)))                # k_norm
-        w.q8(c.mtp_ffn, c.hidden)                     # mlp.gate_proj
-        w.q8(c.mtp_ffn, c.hidden)                     # mlp.up_proj
-        w.q8(c.hidden, c.mtp_ffn)                     # mlp.down_proj
-        w.q8(c.hidden, 2 * c.hidden)                  # fc
-        w.f32(w.normal((c.hidden,)))                  # norm
-        w.f32(w.normal((c.hidden,)))                  # pre_fc_norm_hidden
-        w.f32(w.normal((c.hidden,)))                  # pre_fc_norm_embedding
-        sha = w.digest.hexdigest()
+        f.truncate(total)
+    if workers is None:
+        workers = min(32, os.cpu_count() or 1) if total > (64 << 20) else 1
+    import sys
+    main = sys.modules.get("__main__")
+    if workers > 1 and not os.path.isfile(getattr(main, "__file__", "") or ""):
+        workers = 1          # spawned workers re-import __main__ from its file
+    if workers <= 1:
+        _write_range((cfg, tmp, 0, len(specs)))
+    else:
+        import multiprocessing as mp
+        step = max(1, len(specs) // (workers * 4))
+        jobs = [(cfg, tmp, i, min(len(specs), i + step)) for i in range(0, len(specs), step)]
+        with mp.get_context("spawn").Pool(workers) as pool:
+            pool.map(_write_range, jobs)
+    h = hashlib.sha256()
+    with open(tmp, "rb") as f:
+        for blk in iter(lambda: f.read(1 << 24), b""):
+            h.update(blk)
+    sha = h.hexdigest()
     os.replace(tmp, bin_path)
     with open(meta_path, "w") as f:
-        json.dump({"config": want, "sha256": sha}, f, indent=1)
+        json.dump({"config": want, "sha256": sha, "bytes": total}, f, indent=1)
     return sha
 
 
