@@ -152,6 +152,22 @@ int lz_state_counters(const LZRunState *s, int seq, int *rounds, int *emitted,
    the round's device time and its kernel count. */
 int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
                      int *n_gemv, double *round_ms, int *n_kernels);
+/* Allocation-free logits (no counterpart in the reference): the tied
+   lm_head over n final-normed hidden rows (as lz_forward_verify captures
+   them), for callers that cannot allocate device memory themselves - a
+   process that must not call cudaMalloc, code running inside another
+   runtime's memory pool or budget.  hidden (n x hidden_size) and logits
+   (n x vocab) are device pointers the caller owns; stream is a
+   cudaStream_t (NULL = the legacy default stream).  The quantised rows go
+   to a static device array of at most 64 rows x 4096 columns (larger
+   requests return LZ98_ERR_SPEC_K_RANGE with a message); it is shared by
+   every call, so calls that overlap on the GPU race.  The first call on a
+   device resolves the array's device address (cudaGetSymbolAddress) and
+   should come before any stream capture.  Calls no cudaMalloc or
+   cudaFree. */
+int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logits,
+                      void *stream, char *errbuf, int errlen);
+
 /* Stream the library launches on (cudaStream_t, NULL = a private stream). */
 void *lz_state_stream(LZRunState *s);
 /* Kernels this library launched since the state was created. */

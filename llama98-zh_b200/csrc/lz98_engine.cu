@@ -26,6 +26,7 @@ void set_err(char* buf, int len, const char* fmt, const char* a = "") {
   if (buf && len > 0) snprintf(buf, (size_t)len, fmt, a);
 }
 
+
 #define CK(call)                                                              \
   do {                                                                        \
     cudaError_t e_ = (call);                                                  \
@@ -1229,5 +1230,90 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   if (n_gemv) *n_gemv = (int)s->prof_bytes.size();
   if (round_ms) *round_ms = rms;
   if (n_kernels) *n_kernels = (int)(s->launches - l0);
+  return 0;
+}
+
+// ============================================================ static scratch
+//
+// lz_lm_head_static: logits of final-normed hidden rows without any
+// allocation, for callers that cannot call cudaMalloc (a host process that
+// owns no CUDA allocator of its own, code running inside another runtime's
+// memory pool or under a capture-only budget).  The quantised activation
+// rows this path needs live in the file-scope arrays below, sized for at
+// most kStaticRows rows of at most kStaticDim columns; every GPU that loads
+// this library holds them (288 KiB) until the process exits.
+
+namespace {
+
+constexpr int kStaticRows = 64;
+constexpr int kStaticDim = 4096;
+
+static __device__ __align__(256) int8_t g_static_xq[kStaticRows * kStaticDim];
+static __device__ __align__(256) float g_static_xs[kStaticRows * kStaticDim / 32];
+
+constexpr int kMaxDevices = 64;
+int8_t* g_static_xq_addr[kMaxDevices];
+float* g_static_xs_addr[kMaxDevices];
+
+// Per-32 quantisation of n rows (src/ops_quant.c:2152-2282).
+__global__ void quant_rows_kernel(const float* __restrict__ x, int d, int8_t* xq, float* xs) {
+  const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = warp; g < d / 32; g += nw) {
+    const int i = g * 32 + lane;
+    xq[(size_t)r * d + i] = warp_quant32(x[(size_t)r * d + i], &xs[(size_t)r * (d / 32) + g]);
+  }
+}
+
+}  // namespace
+
+extern "C" int lz_lm_head_static(const LZModel* m, const float* hidden, int n, float* logits, void* stream,
+                                 char* errbuf, int errlen) {
+  if (!m || !hidden || !logits) {
+    set_err(errbuf, errlen, "lz_lm_head_static: null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const Cfg& c = m->c;
+  if (n < 1 || n > kStaticRows || c.d > kStaticDim) {
+    char msg[160];
+    snprintf(msg, sizeof msg, "lz_lm_head_static: %d rows of %d columns exceed the static scratch (%d x %d)",
+             n, c.d, kStaticRows, kStaticDim);
+    set_err(errbuf, errlen, "%s", msg);
+    return LZ98_ERR_SPEC_K_RANGE;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_err(errbuf, errlen, "lz_lm_head_static: no current CUDA device");
+    return LZ98_ERR_CUDA;
+  }
+  // One-time set-up per device, with that device current: the device
+  // addresses of the scratch arrays (their host-side names are not device
+  // addresses).  Done by the first call on the device.
+  if (!g_static_xq_addr[dev]) {
+    void* pq = nullptr;
+    void* ps = nullptr;
+    if (cudaGetSymbolAddress(&pq, g_static_xq) != cudaSuccess ||
+        cudaGetSymbolAddress(&ps, g_static_xs) != cudaSuccess || !pq || !ps) {
+      set_err(errbuf, errlen, "lz_lm_head_static: cudaGetSymbolAddress failed");
+      return LZ98_ERR_CUDA;
+    }
+    g_static_xs_addr[dev] = static_cast<float*>(ps);
+    g_static_xq_addr[dev] = static_cast<int8_t*>(pq);
+  }
+  int8_t* xq = g_static_xq_addr[dev];
+  float* xs = g_static_xs_addr[dev];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  quant_rows_kernel<<<n, 256, 0, st>>>(hidden, c.d, xq, xs);
+  const QW& w = m->embed;
+  GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, n, logits, c.vocab, 0, nullptr, nullptr, 0, 32, nullptr, nullptr};
+  const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
+  const int nsb = w.in / 32;
+  if (nsb <= 32) gemv_q8_kernel<1><<<grid, blk, 0, st>>>(a);
+  else if (nsb <= 64) gemv_q8_kernel<2><<<grid, blk, 0, st>>>(a);
+  else gemv_q8_kernel<4><<<grid, blk, 0, st>>>(a);
+  if (cudaGetLastError() != cudaSuccess) {
+    set_err(errbuf, errlen, "lz_lm_head_static: kernel launch failed");
+    return LZ98_ERR_CUDA;
+  }
   return 0;
 }

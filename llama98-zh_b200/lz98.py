@@ -74,6 +74,7 @@ def lib():
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
                                      P(ctypes.c_double), P(c_int)]),
+        "lz_lm_head_static": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_state_stream": (c_void_p, [c_void_p]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
     }
@@ -92,7 +93,7 @@ EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_s
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
            "lz_seq_prefill", "lz_spec_round_batch", "lz_set_graphs", "lz_generate", "lz_state_stream",
-           "lz_state_launches", "lz_state_counters", "lz_profile_round"]
+           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static"]
 
 
 class Model:
