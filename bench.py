@@ -147,6 +147,20 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def reduce_over_ranks(ms: float, emitted: float, e2e, world: int, device: str):
+    """Whole-job figures: the slowest rank's device time (MAX) and the
+    tokens of all ranks (SUM); every rank takes the same two collectives."""
+    if world <= 1:
+        return ms, emitted, e2e
+    import torch
+    import torch.distributed as dist
+    mx = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = torch.tensor([emitted, e2e or 0.0], dtype=torch.float64, device=device)
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), float(sm[0]), (float(sm[1]) if e2e is not None else None)
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -222,15 +236,7 @@ def run_ours(args):
         sr_bytes = 112
         h2d, d2h = sr_bytes, 2 * sr_bytes
         s1.close()
-    vals = torch.tensor([ms, float(emitted), e2e_val or 0.0], dtype=torch.float64, device="cuda")
-    if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx[0:1], op=dist.ReduceOp.MAX)
-        sm_ = vals.clone()
-        dist.all_reduce(sm_[1:3], op=dist.ReduceOp.SUM)
-        ms_max, emitted_all, e2e_all = float(mx[0]), float(sm_[1]), float(sm_[2])
-    else:
-        ms_max, emitted_all, e2e_all = ms, float(emitted), e2e_val
+    ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), e2e_val, world, "cuda")
     peak, peak_kind = measured_peak()
     gemv_gbs = prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9
     line = None

@@ -98,9 +98,12 @@ int    lz_mtp_catchup(const LZModel *m, LZRunState *s, const float *h_body_all,
                       const int *next_tokens, int n, int pos0);
 
 /* ---- rounds of sequence 0 (src/llama_zh.h:470-593,
-   src/generate.c:694-994 and 1234-1377).  p_min and n_min must be 0 and
-   samp must be NULL or carry identity penalties (the only settings the
-   benchmark workloads use). */
+   src/generate.c:694-994 and 1234-1377).  p_min and n_min must be 0, the
+   debug flags 0, and samp must be NULL or carry identity penalties (the
+   only settings the benchmark workloads use).  lz_spec_round is the greedy
+   round; lz_spec_round_temp the coupled temperature round (temperature
+   above the floor, top-p), which advances samp->rng_state as the
+   reference does. */
 int lz_spec_round(const LZModel *m, LZRunState *s, int anchor, int anchor_pos,
                   int k, float p_min, int n_min, const LZSampler *samp,
                   int debug_break_rollback, int debug_skip_catchup,
@@ -125,15 +128,27 @@ int lz_spec_accept_temp(const float *p, const float *q, int x, int vocab, float 
    prompt token.  Leaves the sequence ready for rounds; returns the anchor. */
 int lz_seq_prefill(const LZModel *m, LZRunState *s, int seq, const int *prompt,
                    int n_prompt, int *out_anchor, char *errbuf, int errlen);
-/* One greedy round of every sequence with draft depth k (device resident:
+/* Sampler of sequence `seq` (the LZSampler fields the path reads,
+   src/sampler.h:145-187): temperature (<= 1e-3 is greedy), top-p, and the
+   xorshift64* seed (0 is taken as 1, src/sampler.c:55-60).  Kept across
+   lz_state_reset, as the reference keeps its sampler apart from the run
+   state.  lz_seq_prefill picks the first anchor with it. */
+int lz_seq_set_sampler(LZRunState *s, int seq, float temperature, float topp, uint64_t seed);
+/* One round of every sequence with draft depth k (device resident:
    draft k steps, one (k+1)-row verify per sequence, acceptance, ring
-   rollback, chain reseed, catch-up).  out_tokens (n_seq x (k+1)) and
+   rollback, chain reseed, catch-up): greedy when every sequence's sampler
+   is at the temperature floor, temperature rounds when none is (mixed
+   batches are refused).  out_tokens (n_seq x (k+1)) and
    out_counts (n_seq) may be NULL, which skips the device-to-host copy. */
 int lz_spec_round_batch(const LZModel *m, LZRunState *s, int k,
                         int *out_tokens, int *out_counts, char *errbuf, int errlen);
 /* Capture the round of depth k into a CUDA graph (replayed by later
    lz_spec_round_batch calls of the same k); 0 disables graphs. */
 int lz_set_graphs(LZRunState *s, int enable);
+/* Launch every kernel with programmatic dependent launch (the default):
+   each kernel lets the next one start its prologue - weight prefetch -
+   while it finishes; 0 launches them plainly serialised. */
+int lz_set_pdl(LZRunState *s, int enable);
 /* Whole generation on token ids (the reference's lz_generate_call spec
    loop, src/generate.c:2781-3091, without EOS/stop strings): greedy when
    temp <= 1e-3, else the coupled temperature rounds with top-p `topp`. */
@@ -146,7 +161,7 @@ int lz_generate(const LZModel *m, LZRunState *s, const int *prompt, int n_prompt
    tokens (n_accept + 1 per round), accepted drafts, drafted tokens. */
 int lz_state_counters(const LZRunState *s, int seq, int *rounds, int *emitted,
                       int *accepted, int *drafted);
-/* Measurement hook: one eager greedy round of depth k with CUDA events
+/* Measurement hook: one eager round of depth k with CUDA events
    around every int8 GEMV launch.  Returns the summed GEMV device time, their
    algorithmic bytes (weights, scales, activations, outputs), the GEMV count,
    the round's device time and its kernel count. */

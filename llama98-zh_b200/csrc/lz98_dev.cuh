@@ -124,4 +124,11 @@ LZ_HD float random_f32(unsigned long long* st) {
   return __fdiv_rn((float)(r >> 8), 16777216.0f);
 }
 
+// Programmatic dependent launch (sm_90+): let the next kernel of the
+// stream start its independent prologue now, and wait here until every
+// prerequisite grid has completed and its writes are visible.  Both are
+// no-ops for a kernel launched without the programmatic attribute.
+LZ_HD void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+LZ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace lz98

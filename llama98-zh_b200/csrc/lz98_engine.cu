@@ -17,6 +17,7 @@
 
 #include "../../include/lz98_gpu.h"
 #include "lz98_kernels.cuh"
+#include "lz98_sample.cuh"
 
 using namespace lz98;
 
@@ -349,6 +350,15 @@ struct LZRunState {
   float *xs, *os, *lats, *hs, *ys, *shs, *as;
   int *pair_e, *tok, *catch_tok, *catch_hidx;
   unsigned long long* vmax;
+  int* row_counter;                  // last-block tails (reset by the last block)
+  // temperature rounds: draft distributions [B][kmax][V], target
+  // distributions [Rmax][V], sort scratch [Rmax][npow2], sampled token
+  float *qbuf = nullptr, *pbuf = nullptr, *sortbuf = nullptr;
+  int npow2 = 2;
+  int* tok_out = nullptr;
+  std::vector<char> seq_temp;        // per sequence: temperature mode
+  int n_sm = 148;
+  std::map<long, int> gemv_occ;      // resident GEMV blocks per SM by (JM, shared bytes)
   float* pair_w;
   KdaSeq* seqs;
   MtpRow *mrows, *crows;
@@ -359,6 +369,7 @@ struct LZRunState {
   std::vector<float> h_logits, h_hidden, h_draft;
   long long launches = 0;
   bool graphs = true;
+  bool pdl = true;                   // programmatic dependent launch
   // optional per-GEMV timing (lz_profile_round): event pairs and bytes
   bool prof = false;
   std::vector<cudaEvent_t> prof_ev;
@@ -368,6 +379,25 @@ struct LZRunState {
 };
 
 namespace {
+
+// Every kernel of the forward and the round is launched through here: with
+// programmatic stream serialisation when enabled, so the next kernel's
+// prologue (weight prefetch) overlaps this one's tail.
+template <typename... KArgs, typename... Args>
+void launch(LZRunState* s, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s->st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = s->pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  s->launches++;
+}
 
 template <typename T>
 bool dmalloc(LZRunState* s, T** p, size_t n) {
@@ -462,11 +492,43 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->pair_e, P) && dmalloc(s, &s->pair_w, P) && dmalloc(s, &s->tok, R) &&
             dmalloc(s, &s->vmax, R) && dmalloc(s, &s->catch_tok, R) && dmalloc(s, &s->catch_hidx, R) &&
             dmalloc(s, &s->seqs, R) && dmalloc(s, &s->mrows, R) && dmalloc(s, &s->crows, R) &&
-            dmalloc(s, &s->sr, B);
+            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4);
+  s->npow2 = 2;
+  while (s->npow2 < c.vocab) s->npow2 <<= 1;
+  ok = ok && dmalloc(s, &s->qbuf, B * s->kmax * (size_t)c.vocab) && dmalloc(s, &s->pbuf, R * (size_t)c.vocab) &&
+       dmalloc(s, &s->sortbuf, R * (size_t)s->npow2);
+  s->seq_temp.assign(B, 0);
   if (!ok) {
     set_err(errbuf, errlen, "device allocation failed");
     lz_state_free(s);
     return LZ98_ERR_ALLOC;
+  }
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&s->n_sm, cudaDevAttrMultiProcessorCount, dev);
+    // the GEMV input-norm prologue stages its rows in dynamic shared memory
+    const int gdyn = 160 * 1024;
+    if (cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
+        cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
+        cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
+        cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
+        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess) {
+      set_err(errbuf, errlen, "cannot raise the GEMV shared-memory limit");
+      lz_state_free(s);
+      return LZ98_ERR_CUDA;
+    }
+  }
+  {
+    // the attention kernel keeps one score per cached position in dynamic
+    // shared memory; lift the default 48 KiB cap when the cache is long
+    const int dyn = seq_len * (int)sizeof(float);
+    if (dyn > 24 * 1024 &&
+        cudaFuncSetAttribute(mtp_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) != cudaSuccess) {
+      set_err(errbuf, errlen, "sequence too long for the attention kernel's shared memory");
+      lz_state_free(s);
+      return LZ98_ERR_ALLOC;
+    }
   }
   std::vector<float> rope;
   build_rope(c, seq_len, rope);
@@ -516,7 +578,17 @@ static void clear_state(LZRunState* s) {
   cudaMemsetAsync(s->ks, 0, s->cache_seq * B / 32 * 4, s->st);
   cudaMemsetAsync(s->vs, 0, s->cache_seq * B / 32 * 4, s->st);
   cudaMemsetAsync(s->chain, 0, B * c.d * 4, s->st);
-  for (auto& r : s->h_sr) r = SeqRound{};
+  // the sampler (temperature, top-p, generator) is not part of the run
+  // state in the reference (LZSampler, src/sampler.h:145-187): kept
+  cudaMemcpyAsync(s->h_sr.data(), s->sr, B * sizeof(SeqRound), cudaMemcpyDeviceToHost, s->st);
+  cudaStreamSynchronize(s->st);
+  for (auto& r : s->h_sr) {
+    SeqRound z{};
+    z.rng = r.rng;
+    z.temp = r.temp;
+    z.topp = r.topp;
+    r = z;
+  }
   cudaMemcpyAsync(s->sr, s->h_sr.data(), B * sizeof(SeqRound), cudaMemcpyHostToDevice, s->st);
   cudaStreamSynchronize(s->st);
 }
@@ -575,14 +647,72 @@ extern "C" int lz_set_graphs(LZRunState* s, int enable) {
   return 0;
 }
 
+extern "C" int lz_set_pdl(LZRunState* s, int enable) {
+  if (!s) return LZ98_ERR_NULL_ARG;
+  if (s->pdl != (enable != 0)) {
+    for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
+    s->graph.clear();
+  }
+  s->pdl = enable != 0;
+  return 0;
+}
+
 // ================================================================== launches
 
 namespace {
 
-void gemv(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, float* y, int ldy,
-          int mode = 0, const QW* w2 = nullptr, const int8_t* xq2 = nullptr, const float* xs2 = nullptr) {
+// RMSNorm of a GEMV's input rows: the float rows (ld = the GEMV's K), the
+// norm weights, an optional float copy of the normalised rows and optional
+// arg-max slots to clear.
+struct InNorm {
+  const float* x;
+  const float* w;
+  float* out;
+  unsigned long long* amax;
+};
+
+constexpr int kPrologueRows = 8;    // above this the norm runs as its own grid
+constexpr int kGemvMaxBlocksPerSM = 16;
+
+void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
+                   int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear = nullptr);
+
+template <int JM, int WARPS>
+void gemv_launch(LZRunState* s, const GemvArgs& a, bool prologue) {
+  const size_t dyn = gemv_smem_bytes(JM, WARPS, a.W2 != nullptr, prologue, a.R, a.K);
+  const long key = (long)JM << 48 | (long)WARPS << 40 | (long)dyn;
+  auto it = s->gemv_occ.find(key);
+  int per_sm;
+  if (it == s->gemv_occ.end()) {
+    per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q8_kernel<JM, WARPS>, WARPS * 32, dyn);
+    per_sm = std::max(1, std::min(per_sm, kGemvMaxBlocksPerSM));
+    s->gemv_occ[key] = per_sm;
+  } else {
+    per_sm = it->second;
+  }
+  const int want = (a.N + WARPS - 1) / WARPS;
+  // a prologue is paid once per block: one block per SM
+  const int cap = s->n_sm * (prologue ? 1 : per_sm);
+  launch(s, gemv_q8_kernel<JM, WARPS>, dim3(std::min(want, cap)), dim3(WARPS * 32), dyn, a);
+}
+
+// y (R x N, ld ldy) = [y +] W x (+ W2 x2).  With `nin`, x is produced here
+// from the float rows nin->x by RMSNorm + quantisation: inside the GEMV
+// (every block, from shared memory) for R <= kPrologueRows, else by one
+// rmsnorm_quant grid into xq/xs first.
+void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, int ldy,
+          int mode = 0, const QW* w2 = nullptr, const int8_t* xq2 = nullptr, const float* xs2 = nullptr,
+          const InNorm* nin = nullptr) {
   GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode,
-             w2 ? w2->q : nullptr, w2 ? w2->s : nullptr, w2 ? w2->in : 0, w2 ? w2->gs : 32, xq2, xs2};
+             w2 ? w2->q : nullptr, w2 ? w2->s : nullptr, w2 ? w2->in : 0, w2 ? w2->gs : 32, xq2, xs2,
+             nullptr, nullptr, s->m->c.eps, nullptr, nullptr};
+  const bool prologue = nin && R <= kPrologueRows;
+  if (prologue) {
+    a.nx = nin->x; a.nw = nin->w; a.nout = nin->out; a.namax = nin->amax;
+  } else if (nin) {
+    rmsnorm_quant(s, nin->x, w.in, nin->w, w.in, R, nin->out, w.in, xq, xs, nin->amax);
+  }
   const int nsb = std::max(w.in, w2 ? w2->in : 0) / 32;
   if (s->prof) {
     cudaEvent_t e0, e1;
@@ -599,25 +729,26 @@ void gemv(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, 
     double b = bytes(w) + (w2 ? bytes(*w2) : 0.0) + (double)R * w.out * 4.0 * (mode ? 2.0 : 1.0);
     s->prof_bytes.push_back(b);
   }
-  const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
-  if (nsb <= 32) gemv_q8_kernel<1><<<grid, blk, 0, s->st>>>(a);
-  else if (nsb <= 64) gemv_q8_kernel<2><<<grid, blk, 0, s->st>>>(a);
-  else gemv_q8_kernel<4><<<grid, blk, 0, s->st>>>(a);
-  s->launches++;
+  if (prologue) {
+    if (nsb <= 32) gemv_launch<1, kGemvProWarps>(s, a, true);
+    else gemv_launch<2, kGemvProWarps>(s, a, true);
+  } else {
+    if (nsb <= 32) gemv_launch<1, kGemvWarps>(s, a, false);
+    else if (nsb <= 64) gemv_launch<2, kGemvWarps>(s, a, false);
+    else gemv_launch<4, kGemvWarps>(s, a, false);
+  }
   if (s->prof) cudaEventRecord(s->prof_ev.back(), s->st);
 }
 
 void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
-                   int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear = nullptr) {
-  rmsnorm_quant_kernel<<<R, 256, n * sizeof(float), s->st>>>(x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs,
-                                                             amax_clear);
-  s->launches++;
+                   int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear) {
+  launch(s, rmsnorm_quant_kernel, dim3(R), dim3(256), 2 * n * sizeof(float), x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs,
+                                                                 amax_clear);
 }
 
 void argmax(LZRunState* s, const float* logits, int R, int p1_mode) {
   const int V = s->m->c.vocab;
-  argmax_kernel<<<dim3((V + kArgmaxChunk - 1) / kArgmaxChunk, R), 256, 0, s->st>>>(logits, V, p1_mode, s->vmax);
-  s->launches++;
+  launch(s, argmax_kernel, dim3((V + kArgmaxChunk - 1) / kArgmaxChunk, R), dim3(256), 0, logits, V, p1_mode, s->vmax);
 }
 
 // Body forward of R rows (src/forward.c:1210-1617): embed, per layer
@@ -627,45 +758,41 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
   const LZModel* m = s->m;
   const Cfg& c = m->c;
   const int d = c.d, kdim = c.key_dim, vdim = c.val_dim, nvk = c.nv * c.kd;
-  embed_kernel<<<R, 256, 0, s->st>>>(m->embed.q, m->embed.s, m->embed.gs, d, s->tok, s->x);
-  s->launches++;
+  launch(s, embed_kernel, dim3(R), dim3(256), 0, m->embed.q, m->embed.s, m->embed.gs, d, s->tok, s->x);
   for (int l = 0; l < c.nl; l++) {
     const DLayer& L = m->L[l];
-    rmsnorm_quant(s, s->x, d, L.in_ln, d, R, nullptr, 0, s->xq, s->xs);
-    gemv(s, L.inproj, s->xq, s->xs, R, s->inproj, m->n_in);
-    kda_fb_gate_kernel<<<dim3((nvk + 255) / 256, R), 256, 0, s->st>>>(
-        s->inproj, m->n_in, m->off_fa, c.rank, L.fb.q, L.fb.s, L.fb.gs, L.a_log, L.dt_bias, c.lb, nvk,
-        c.kd, s->gate);
-    kda_conv_kernel<<<dim3((c.conv_dim + 127) / 128, nseq), 128, 0, s->st>>>(
-        s->inproj, m->n_in, c.conv_dim, L.conv_w, s->seqs, s->conv + (size_t)l * c.conv_dim * 3,
-        s->conv_seq, s->conv_slot, s->depth, adv, s->conv_out, c.conv_dim);
-    kda_recur_kernel<<<dim3(c.nv, nseq), kRecurThreads, 0, s->st>>>(
+    const InNorm in_ln{s->x, L.in_ln, nullptr, nullptr};
+    gemv(s, L.inproj, s->xq, s->xs, R, s->inproj, m->n_in, 0, nullptr, nullptr, nullptr, &in_ln);
+    KdaPreArgs pa{s->inproj, m->n_in, c.conv_dim, L.conv_w, s->seqs,
+                  s->conv + (size_t)l * c.conv_dim * 3, s->conv_seq, s->conv_slot, s->depth, adv, s->conv_out,
+                  m->off_fa, c.rank, L.fb.q, L.fb.s, L.fb.gs, L.a_log, L.dt_bias, c.lb, nvk, c.kd, s->gate,
+                  (c.conv_dim + 255) / 256, (nvk + 255) / 256, nseq};
+    launch(s, kda_pre_kernel, dim3(pa.nconv_x * nseq + pa.nfb_x * R), dim3(256), 0, pa);
+    launch(s, kda_recur_kernel, dim3(c.nv, nseq), dim3(kRecurThreads), 0, 
         s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
         s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
         s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
-    s->launches += 3;
     gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);
-    rmsnorm_quant(s, s->x, d, L.post_ln, d, R, nullptr, 0, s->xq, s->xs);
-    gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe);
-    moe_route_kernel<<<R, 128, 0, s->st>>>(s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
-                                          c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats);
-    s->launches++;
-    if (c.shared_w) {
-      swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->moein, m->n_moe, m->off_shg, m->off_shu, c.shared_w,
-                                                s->shq, s->shs);
-      s->launches++;
-    }
-    moe_w13_kernel<<<dim3(c.moe_ffn / 32, R * c.topk), 256, 0, s->st>>>(
+    const InNorm post{s->x, L.post_ln, nullptr, nullptr};
+    gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe, 0, nullptr, nullptr, nullptr, &post);
+    launch(s, moe_route_kernel, dim3(R), dim3(512), 0, s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
+                                           c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats,
+                                           m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
+    launch(s, moe_w13_kernel, dim3(c.moe_ffn / 32, R * c.topk), dim3(256), 0, 
         L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
-    moe_w2_kernel<<<dim3((c.latent + 7) / 8, R * c.topk), 256, 0, s->st>>>(
-        L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->hq, s->hs, s->h2);
-    moe_combine_kernel<<<R, 256, 0, s->st>>>(s->h2, s->pair_w, s->pair_e, c.topk, c.latent, s->yq, s->ys);
-    s->launches += 3;
+    launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, R * c.topk), dim3(256), 0, 
+        L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2,
+        s->row_counter, s->yq, s->ys);
     if (c.shared_w) gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1, &L.sh_down, s->shq, s->shs);
     else gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1);
   }
-  rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs, s->vmax);
-  if (want_logits) gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
+  // final norm: hidden capture, then the tied lm_head
+  if (want_logits) {
+    const InNorm fin{s->x, m->final_norm, s->hidden, s->vmax};
+    gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin);
+  } else {
+    rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs, s->vmax);
+  }
 }
 
 // MTP block over R rows (src/forward_mtp.c:32-144, 561-624): fc front,
@@ -678,34 +805,32 @@ void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const i
   const Cfg& c = m->c;
   const DMtp& M = m->mtp;
   const int d = c.d;
-  mtp_front_kernel<<<R, 256, 2 * d * sizeof(float), s->st>>>(m->embed.q, m->embed.s, m->embed.gs, d, tok,
+  launch(s, mtp_front_kernel, dim3(R), dim3(256), 2 * d * sizeof(float), m->embed.q, m->embed.s, m->embed.gs, d, tok,
                                                              hid, hid_idx, M.pre_e, M.pre_h, c.eps, s->xq,
                                                              s->xs);
-  s->launches++;
   gemv(s, M.fc, s->xq, s->xs, R, s->mtpx, d);
-  rmsnorm_quant(s, s->mtpx, d, M.in_ln, d, R, nullptr, 0, s->xq, s->xs);
-  gemv(s, M.qkv, s->xq, s->xs, R, s->qkv, m->n_qkv);
-  mtp_kv_write_kernel<<<dim3(c.nkv, R), 64, 0, s->st>>>(s->qkv, m->n_qkv, m->off_mk, m->off_mv, rows, M.k_norm,
+  const InNorm in_ln{s->mtpx, M.in_ln, nullptr, nullptr};
+  gemv(s, M.qkv, s->xq, s->xs, R, s->qkv, m->n_qkv, 0, nullptr, nullptr, nullptr, &in_ln);
+  launch(s, mtp_kv_write_kernel, dim3(c.nkv, R), dim3(64), 0, s->qkv, m->n_qkv, m->off_mk, m->off_mv, rows, M.k_norm,
                                                         c.eps, c.hd, c.rot, c.kv_dim, s->rope, s->kq, s->ks,
                                                         s->vq, s->vs, s->cache_seq);
-  s->launches++;
   if (!full) return;
   const size_t smem = (size_t)s->seq_len * sizeof(float);
-  mtp_attn_kernel<<<dim3(c.nh, R), 128, smem, s->st>>>(s->qkv, m->n_qkv, c.q_dim, rows, M.q_norm, c.eps, c.hd,
-                                                       c.rot, c.kv_dim, c.nh / c.nkv, s->rope, s->attn_scale,
-                                                       s->kq, s->ks, s->vq, s->vs, s->cache_seq, s->aq, s->as);
-  s->launches++;
+  launch(s, mtp_attn_kernel, dim3(c.nh, R), dim3(kAttnThreads), smem, 
+      s->qkv, m->n_qkv, c.q_dim, rows, M.q_norm, c.eps, c.hd, c.rot, c.kv_dim, c.nh / c.nkv, s->rope,
+      s->attn_scale, s->kq, s->ks, s->vq, s->vs, s->cache_seq, s->aq, s->as);
   gemv(s, M.o, s->aq, s->as, R, s->mtpx, d, 1);
-  rmsnorm_quant(s, s->mtpx, d, M.post_ln, d, R, nullptr, 0, s->xq, s->xs);
-  gemv(s, M.gu, s->xq, s->xs, R, s->inproj, 2 * c.mtp_ffn);
-  swiglu_quant_kernel<<<R, 256, 0, s->st>>>(s->inproj, 2 * c.mtp_ffn, 0, c.mtp_ffn, c.mtp_ffn, s->shq, s->shs);
-  s->launches++;
+  const InNorm post{s->mtpx, M.post_ln, nullptr, nullptr};
+  gemv(s, M.gu, s->xq, s->xs, R, s->inproj, 2 * c.mtp_ffn, 0, nullptr, nullptr, nullptr, &post);
+  launch(s, swiglu_quant_kernel, dim3(R), dim3(256), 0, s->inproj, 2 * c.mtp_ffn, 0, c.mtp_ffn, c.mtp_ffn, s->shq, s->shs);
   gemv(s, M.down, s->shq, s->shs, R, s->mtpx, d, 1);
-  rmsnorm_quant(s, s->mtpx, d, M.norm, d, R, chain_out, d, s->xq, s->xs, s->vmax);
-  gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab);
+  const InNorm fin{s->mtpx, M.norm, chain_out, s->vmax};
+  gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin);
 }
 
 __global__ void set_rows_kernel(MtpRow* rows, int n, int seq, int pos0, int seq_len) {
+  pdl_trigger();
+  pdl_wait();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) rows[i] = MtpRow{seq, pos0 + i, pos0 + i >= 0 && pos0 + i < seq_len};
 }
@@ -714,6 +839,8 @@ __global__ void set_rows_kernel(MtpRow* rows, int n, int seq, int pos0, int seq_
 // inactive (no cache write, no attention): the memory stays in bounds and
 // the host's budget check (max_pos) keeps such rounds from being asked for.
 __global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_len, int* tok, MtpRow* rows) {
+  pdl_trigger();
+  pdl_wait();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= nseq) return;
   tok[b] = i == 0 ? sr[b].anchor : sr[b].draft[i - 1];
@@ -722,6 +849,8 @@ __global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_
 }
 
 __global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const unsigned long long* amax) {
+  pdl_trigger();
+  pdl_wait();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= nseq) return;
   sr[b].draft[i] = argmax_index(amax[b]);
@@ -729,6 +858,8 @@ __global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const u
 }
 
 __global__ void verify_setup_kernel(const SeqRound* sr, int nseq, int k, int* tok, KdaSeq* seqs) {
+  pdl_trigger();
+  pdl_wait();
   int b = blockIdx.x;
   if (b >= nseq) return;
   if (threadIdx.x == 0) seqs[b] = KdaSeq{b * (k + 1), k + 1, sr[b].ssm_slot, b};
@@ -748,21 +879,68 @@ void round_greedy(LZRunState* s, int k) {
   const int B = s->B;
   const int tb = (B + 127) / 128;
   for (int i = 0; i < k; i++) {
-    draft_setup_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, s->seq_len, s->tok, s->mrows);
+    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
     mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
     argmax(s, s->logits, B, 1);
-    draft_store_kernel<<<tb, 128, 0, s->st>>>(s->sr, B, i, k, s->vmax);
-    s->launches += 2;
+    launch(s, draft_store_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, k, s->vmax);
   }
   const int R = B * (k + 1);
-  verify_setup_kernel<<<B, 32, 0, s->st>>>(s->sr, B, k, s->tok, s->seqs);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
   body_forward(s, R, B, 1, true);
   argmax(s, s->logits, R, 0);
-  spec_accept_greedy_kernel<<<B, 256, 0, s->st>>>(s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
+  launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
                                                   s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
-  s->launches += 2;
   if (k > 1)
     mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+}
+
+// One temperature round of every sequence (src/generate.c:1234-1377), all
+// on the device: k draft steps sampling q, the (k+1)-row verify, target
+// distributions, coupled acceptance, then the greedy round's ring,
+// chain and catch-up steps.
+void round_temp(LZRunState* s, int k) {
+  const LZModel* m = s->m;
+  const Cfg& c = m->c;
+  const int B = s->B, V = c.vocab;
+  const int tb = (B + 127) / 128;
+  for (int i = 0; i < k; i++) {
+    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
+    mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
+    launch(s, temp_draft_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, i, k, s->kmax,
+           s->qbuf);
+  }
+  const int R = B * (k + 1);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
+  body_forward(s, R, B, 1, true);
+  launch(s, temp_target_kernel, dim3(R), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, k, s->pbuf,
+         s->sortbuf, s->npow2);
+  launch(s, temp_accept_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->sr, k, s->kmax, s->pbuf, s->qbuf, V,
+         s->hidden, c.d, s->chain, s->depth, s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  if (k > 1)
+    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+}
+
+// 0: every sequence greedy, 1: every sequence in temperature mode, -1: mixed.
+int round_mode(const LZRunState* s) {
+  int t = 0;
+  for (char v : s->seq_temp) t += v != 0;
+  return t == 0 ? 0 : (t == (int)s->seq_temp.size() ? 1 : -1);
+}
+
+void round_any(LZRunState* s, int k) {
+  if (round_mode(s) == 1) round_temp(s, k);
+  else round_greedy(s, k);
+}
+
+// One token of sequence `seq` from logits row 0 by its sampler (arg-max at
+// the temperature floor), on the device; the sampler state advances there.
+int sample_row(LZRunState* s, int seq, int* tok) {
+  const Cfg& c = s->m->c;
+  launch(s, sample_row_kernel, dim3(1), dim3(kSampThreads), kSampSmem, s->logits, c.vocab, s->sr, seq, s->pbuf,
+         s->sortbuf, s->npow2, s->tok_out);
+  CK(cudaMemcpyAsync(tok, s->tok_out, sizeof(int), cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  return 0;
 }
 
 }  // namespace
@@ -844,8 +1022,7 @@ extern "C" float* lz_mtp_draft_step(const LZModel* m, LZRunState* s, int next_to
   const Cfg& c = m->c;
   if (next_token < 0 || next_token >= c.vocab || pos < 0 || pos >= s->seq_len) return nullptr;
   cudaMemcpyAsync(s->tok, &next_token, sizeof(int), cudaMemcpyHostToDevice, s->st);
-  set_rows_kernel<<<1, 32, 0, s->st>>>(s->mrows, 1, 0, pos, s->seq_len);
-  s->launches++;
+  launch(s, set_rows_kernel, dim3(1), dim3(32), 0, s->mrows, 1, 0, pos, s->seq_len);
   mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
   cudaMemcpyAsync(s->h_draft.data(), s->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
   if (cudaStreamSynchronize(s->st) != cudaSuccess) return nullptr;
@@ -863,8 +1040,7 @@ static int mtp_prefill_seq(LZRunState* s, int seq, const float* h_host, const fl
       cudaMemcpyAsync(s->hidden, h_host + (size_t)done * c.d, (size_t)R * c.d * 4, cudaMemcpyHostToDevice, s->st);
       hid = s->hidden;
     }
-    set_rows_kernel<<<(R + 127) / 128, 128, 0, s->st>>>(s->crows, R, seq, pos0 + done, s->seq_len);
-    s->launches++;
+    launch(s, set_rows_kernel, dim3((R + 127) / 128), dim3(128), 0, s->crows, R, seq, pos0 + done, s->seq_len);
     mtp_forward(s, R, s->catch_tok, hid, nullptr, s->crows, false, nullptr);
     done += R;
   }
@@ -952,23 +1128,38 @@ extern "C" int lz_spec_accept_temp(const float* p, const float* q, int x, int vo
 }
 
 static int run_round(LZRunState* s, int k) {
+  const int mode = round_mode(s);
+  if (mode < 0) return 1;
   if (s->graphs) {
-    auto it = s->graph.find(k);
+    const int key = k + 100 * mode;
+    auto it = s->graph.find(key);
     if (it == s->graph.end()) {
       cudaGraph_t g;
       CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
-      round_greedy(s, k);
+      round_any(s, k);
       CK(cudaStreamEndCapture(s->st, &g));
       cudaGraphExec_t ge;
       CK(cudaGraphInstantiate(&ge, g, 0));
       cudaGraphDestroy(g);
-      it = s->graph.emplace(k, ge).first;
+      it = s->graph.emplace(key, ge).first;
     }
     CK(cudaGraphLaunch(it->second, s->st));
   } else {
-    round_greedy(s, k);
+    round_any(s, k);
   }
   return 0;
+}
+
+extern "C" int lz_seq_set_sampler(LZRunState* s, int seq, float temperature, float topp, uint64_t seed) {
+  if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  sr_down(s);
+  SeqRound& r = s->h_sr[seq];
+  r.temp = temperature > 0.0f ? temperature : 0.0f;    // src/generate.c:2790
+  r.topp = topp;
+  r.rng = seed ? seed : 1ull;                         // src/sampler.c:55-60
+  s->seq_temp[seq] = r.temp > kTempFloor;
+  sr_up(s);
+  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
@@ -984,7 +1175,7 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
     return -LZ98_ERR_SPEC_K_RANGE;
   }
   if (p_min != 0.0f || n_min != 0 || debug_break_rollback || debug_skip_catchup ||
-      (samp && samp->temperature > 1e-3f) || s->B != 1) {
+      (samp && samp->temperature > kTempFloor) || s->B != 1) {
     set_err(errbuf, errlen, "unsupported round options on the device path");
     return -LZ98_ERR_FORWARD;
   }
@@ -993,6 +1184,8 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
   r.anchor = anchor;
   r.anchor_pos = anchor_pos;
   r.k = k;
+  r.temp = 0.0f;
+  s->seq_temp[0] = 0;
   sr_up(s);
   if (run_round(s, k)) {
     set_err(errbuf, errlen, "CUDA failure in the round");
@@ -1011,10 +1204,49 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
   return o.n_accept + 1;
 }
 
-extern "C" int lz_spec_round_temp(const LZModel*, LZRunState*, int, int, int, float, int, LZSampler*, int, int,
-                                  int*, int*, int*, int*, char* errbuf, int errlen) {
-  set_err(errbuf, errlen, "temperature rounds are not built yet on the device path");
-  return -LZ98_ERR_FORWARD;
+extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k,
+                                  float p_min, int n_min, LZSampler* samp, int debug_break_rollback,
+                                  int debug_skip_catchup, int* out, int* out_n_accept, int* out_new_pos,
+                                  int* out_k_eff, char* errbuf, int errlen) {
+  if (!m || !s || !samp || !out || !out_n_accept || !out_new_pos || !out_k_eff) {
+    set_err(errbuf, errlen, "null argument");
+    return -LZ98_ERR_NULL_ARG;
+  }
+  if (k < 1 || k > 6 || k > s->depth - 1) {
+    set_err(errbuf, errlen, "draft depth out of range");
+    return -LZ98_ERR_SPEC_K_RANGE;
+  }
+  if (p_min != 0.0f || n_min != 0 || debug_break_rollback || debug_skip_catchup || s->B != 1 ||
+      !(samp->temperature > kTempFloor)) {
+    set_err(errbuf, errlen, "unsupported round options on the device path");
+    return -LZ98_ERR_FORWARD;
+  }
+  sr_down(s);
+  SeqRound& r = s->h_sr[0];
+  r.anchor = anchor;
+  r.anchor_pos = anchor_pos;
+  r.k = k;
+  r.temp = samp->temperature;
+  r.topp = samp->topp;
+  r.rng = samp->rng_state;
+  s->seq_temp[0] = 1;
+  sr_up(s);
+  if (run_round(s, k)) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return -LZ98_ERR_CUDA;
+  }
+  sr_down(s);
+  if (cudaGetLastError() != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure in the round");
+    return -LZ98_ERR_CUDA;
+  }
+  const SeqRound& o = s->h_sr[0];
+  for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
+  samp->rng_state = o.rng;
+  *out_n_accept = o.n_accept;
+  *out_new_pos = anchor_pos + 1 + o.n_accept;
+  *out_k_eff = k;
+  return o.n_accept + 1;
 }
 
 extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const int* prompt, int n_prompt,
@@ -1058,14 +1290,12 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
   upload_seqs(s, {KdaSeq{0, 1, slot, seq}});
   body_forward(s, 1, 1, 0, true);
   cudaMemcpyAsync(s->chain + (size_t)seq * c.d, s->hidden, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
-  argmax(s, s->logits, 1, 0);
-  unsigned long long packed = 0;
-  cudaMemcpyAsync(&packed, s->vmax, sizeof(packed), cudaMemcpyDeviceToHost, s->st);
-  const int anchor = (int)(0xFFFFFFFFu - (uint32_t)packed);
-  if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+  int anchor = 0;
+  if (sample_row(s, seq, &anchor)) {
     set_err(errbuf, errlen, "CUDA failure in prefill");
     return LZ98_ERR_CUDA;
   }
+  sr_down(s);                        // the sampler state advanced on the device
   SeqRound& r = s->h_sr[seq];
   r.anchor = anchor;
   r.anchor_pos = n_prompt - 1;
@@ -1104,44 +1334,38 @@ extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* 
   return 0;
 }
 
-// The generation loop of src/generate.c:2781-3091 on token ids, greedy,
-// sequence 0.
+// The generation loop of src/generate.c:2781-3091 on token ids (sequence
+// 0): greedy at the temperature floor, else coupled temperature rounds with
+// top-p `topp` and the generator seeded by `seed`.  Every token is picked on
+// the device.
 extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
                            int spec_k, float temp, float topp, uint64_t seed, int* out_tok, int out_cap,
                            int* out_n, int* rounds, int round_cap, int* n_rounds, char* errbuf, int errlen) {
-  (void)topp; (void)seed;
   if (!m || !s || !prompt || n_prompt < 1 || !out_n || !n_rounds) return LZ98_ERR_NULL_ARG;
-  if (temp > 1e-3f) {
-    set_err(errbuf, errlen, "temperature generation is not built yet on the device path");
-    return LZ98_ERR_FORWARD;
+  if (n_prompt >= s->seq_len) {
+    set_err(errbuf, errlen, "prompt does not fit the state");
+    return LZ98_ERR_NULL_ARG;
   }
   const Cfg& c = m->c;
   clear_state(s);
+  LZSampler samp{temp > 0.0f ? temp : 0.0f, topp, seed ? seed : 1ull};
+  const bool use_temp = samp.temperature > kTempFloor;
+  if (int rc = lz_seq_set_sampler(s, 0, samp.temperature, topp, samp.rng_state)) return rc;
   int max_pos = n_prompt + max_new;
   if (max_pos > s->seq_len) max_pos = s->seq_len;
   if (max_pos < n_prompt + 1) max_pos = n_prompt + 1;
   int n_out = 0, nr = 0;
   auto emit = [&](int t) { if (n_out < out_cap) out_tok[n_out] = t; n_out++; };
   int pos = n_prompt - 1, token = prompt[n_prompt - 1];
-  bool have_seed = false;
+  // `pending` holds the anchor of a first round whose forward and sample
+  // already ran (lz_seq_prefill forwards the last prompt token and picks
+  // the anchor, as the first loop iteration of the reference does).
+  bool have_seed = false, pending = false;
   if (spec_k > 0) {
-    int anchor;
-    int rc = lz_seq_prefill(m, s, 0, prompt, n_prompt, &anchor, errbuf, errlen);
+    int rc = lz_seq_prefill(m, s, 0, prompt, n_prompt, &token, errbuf, errlen);
     if (rc) return rc;
-    // lz_seq_prefill already forwarded the last prompt token (the first
-    // round's capture) and picked the anchor.
-    int round_k = spec_k;
-    if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
-    if (round_k > 0) {
-      emit(anchor);
-      token = anchor;
-      pos = pos + 1;
-      have_seed = true;
-    } else {
-      token = anchor;
-      emit(anchor);
-      pos = pos + 1;
-    }
+    emit(token);
+    pending = true;
   } else if (n_prompt > 1) {
     std::vector<float> hb((size_t)(n_prompt - 1) * c.d);
     if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, 0, hb.data())) return LZ98_ERR_FORWARD;
@@ -1152,27 +1376,42 @@ extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, i
       round_k = spec_k;
       if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
     }
-    if (round_k > 0 && have_seed) {
+    if (pending && round_k <= 0) {
+      // the reference's plain step for this position already ran
+      pending = false;
+      pos++;
+      continue;
+    }
+    if (round_k > 0 && (have_seed || pending)) {
       int out[8], n_acc = 0, new_pos = 0, k_eff = 0;
-      int ne = lz_spec_round(m, s, token, pos - 1, round_k, 0.0f, 0, nullptr, 0, 0, out, &n_acc, &new_pos, &k_eff,
-                             errbuf, errlen);
+      const int anchor_pos = pending ? pos : pos - 1;
+      pending = false;
+      int ne;
+      if (use_temp) {
+        sr_down(s);
+        samp.rng_state = s->h_sr[0].rng;
+        ne = lz_spec_round_temp(m, s, token, anchor_pos, round_k, 0.0f, 0, &samp, 0, 0, out, &n_acc, &new_pos,
+                                &k_eff, errbuf, errlen);
+      } else {
+        ne = lz_spec_round(m, s, token, anchor_pos, round_k, 0.0f, 0, nullptr, 0, 0, out, &n_acc, &new_pos,
+                           &k_eff, errbuf, errlen);
+      }
       if (ne < 0) return -ne;
       if (rounds && nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_acc; }
       nr++;
+      have_seed = true;
       for (int ei = 0; ei <= n_acc; ei++) emit(out[ei]);
       pos = new_pos + 1;
       token = out[n_acc];
       continue;
     }
-    const float* lg = lz_forward(m, s, token, pos);
-    if (!lg) return LZ98_ERR_FORWARD;
-    int mi = 0;
-    uint32_t best = host_fkey(lg[0]);
-    for (int i = 1; i < c.vocab; i++) {
-      uint32_t kk = host_fkey(lg[i]);
-      if (kk > best) { best = kk; mi = i; }
-    }
-    token = mi;
+    // plain decode step: forward of one token, then one sampled token
+    sr_down(s);
+    const int slot = s->h_sr[0].ssm_slot;
+    CK(cudaMemcpyAsync(s->tok, &token, sizeof(int), cudaMemcpyHostToDevice, s->st));
+    upload_seqs(s, {KdaSeq{0, 1, slot, 0}});
+    body_forward(s, 1, 1, 0, true);
+    if (sample_row(s, 0, &token)) return LZ98_ERR_CUDA;
     emit(token);
     pos++;
   }
@@ -1194,7 +1433,7 @@ extern "C" int lz_state_counters(const LZRunState* cs, int seq, int* rounds, int
   return 0;
 }
 
-// One eager greedy round of depth k with CUDA events around every int8
+// One eager round of depth k with CUDA events around every int8
 // GEMV launch: total GEMV device time, their algorithmic bytes, the count,
 // the round's device time and its kernel count.
 extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* gemv_bytes, int* n_gemv,
@@ -1206,9 +1445,10 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   s->prof = true;
   s->prof_ev.clear();
   s->prof_bytes.clear();
+  if (round_mode(s) < 0) return LZ98_ERR_NULL_ARG;
   const long long l0 = s->launches;
   cudaEventRecord(r0, s->st);
-  round_greedy(s, k);
+  round_any(s, k);
   cudaEventRecord(r1, s->st);
   s->prof = false;
   if (cudaStreamSynchronize(s->st) != cudaSuccess) return LZ98_ERR_CUDA;
@@ -1257,6 +1497,8 @@ float* g_static_xs_addr[kMaxDevices];
 
 // Per-32 quantisation of n rows (src/ops_quant.c:2152-2282).
 __global__ void quant_rows_kernel(const float* __restrict__ x, int d, int8_t* xq, float* xs) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int g = warp; g < d / 32; g += nw) {
@@ -1308,9 +1550,9 @@ extern "C" int lz_lm_head_static(const LZModel* m, const float* hidden, int n, f
   GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, n, logits, c.vocab, 0, nullptr, nullptr, 0, 32, nullptr, nullptr};
   const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
   const int nsb = w.in / 32;
-  if (nsb <= 32) gemv_q8_kernel<1><<<grid, blk, 0, st>>>(a);
-  else if (nsb <= 64) gemv_q8_kernel<2><<<grid, blk, 0, st>>>(a);
-  else gemv_q8_kernel<4><<<grid, blk, 0, st>>>(a);
+  if (nsb <= 32) gemv_q8_kernel<1, kGemvWarps><<<grid, blk, gemv_smem_bytes(1, kGemvWarps, false, false, n, w.in), st>>>(a);
+  else if (nsb <= 64) gemv_q8_kernel<2, kGemvWarps><<<grid, blk, gemv_smem_bytes(2, kGemvWarps, false, false, n, w.in), st>>>(a);
+  else gemv_q8_kernel<4, kGemvWarps><<<grid, blk, gemv_smem_bytes(4, kGemvWarps, false, false, n, w.in), st>>>(a);
   if (cudaGetLastError() != cudaSuccess) {
     set_err(errbuf, errlen, "lz_lm_head_static: kernel launch failed");
     return LZ98_ERR_CUDA;

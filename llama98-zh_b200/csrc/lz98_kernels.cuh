@@ -20,6 +20,7 @@
 namespace lz98 {
 
 constexpr int kGemvWarps = 4;
+constexpr int kGemvProWarps = 16;   // warps of a GEMV block that runs the input-norm prologue
 constexpr int kGemvRB = 8;        // token rows per reduction pass
 
 // ------------------------------------------------------- serial chains
@@ -104,33 +105,73 @@ LZ_HD int dot32(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
 
 struct GemvArgs {
   const int8_t* W; const float* ws; int N, K, gs;
-  const int8_t* xq; const float* xs; int R;
+  const int8_t* xq; const float* xs; int R;      // quantised input rows
   float* y; int ldy; int mode;        // mode 0: y = v; mode 1: y = y + v
   // optional second product over the same output rows, added before the
   // store: v = v1 + v2 (up projection plus shared expert,
   // src/forward_moe.c:434-545)
   const int8_t* W2; const float* ws2; int K2, gs2;
   const int8_t* xq2; const float* xs2;
+  // optional input-norm prologue (R <= kGemvRB): every block normalises the
+  // R float rows of nx (length K) with RMSNorm (1+nw) and quantises them
+  // per 32 into shared memory; block 0 also stores the normalised rows to
+  // nout and clears the arg-max slots namax.
+  const float* nx; const float* nw; float eps; float* nout; unsigned long long* namax;
 };
 
-// Products of one weight row with every token row for the sub-blocks this
-// lane owns; P[rr][s] receives the product fed to the reference reduction.
+// Four 32-element groups at once (one element of each per lane): the
+// reference quantiser (src/ops_quant.c:2152-2282) with the four max
+// reductions interleaved.
+LZ_HD void warp_quant32_x4(const float* v, int8_t* q, float* sg) {
+  uint32_t m[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) m[k] = abs_bits(v[k]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t w = __shfl_xor_sync(0xffffffffu, m[k], o);
+      m[k] = m[k] > w ? m[k] : w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    float inv;
+    q8_scale_from_amax(m[k], &sg[k], &inv);
+    q[k] = (int8_t)q8_clamp(q8_round(__fmul_rn(v[k], inv)));
+  }
+}
+
+// One weight row held in registers: the lane's 32-byte sub-blocks and,
+// for gs = 32, their scales.
 template <int JM>
-LZ_HD void gemv_products(const int8_t* __restrict__ wr, const float* __restrict__ wsr, int K, int rb,
-                         const int8_t* __restrict__ xq, const float* __restrict__ xs, int r0, int nr,
-                         float (*P)[JM * 32], int lane) {
+struct WRow {
+  int4 a[JM], b[JM];
+  float s[JM];
+};
+
+template <int JM>
+LZ_HD void load_wrow(WRow<JM>& w, const int8_t* __restrict__ wr, const float* __restrict__ wsr, int K, int rb,
+                     int lane) {
   const int nsb = K >> 5;
-  int4 wa[JM], wb[JM];
-  float wsv[JM];
 #pragma unroll
   for (int j = 0; j < JM; j++) {
     const int s = lane + 32 * j;
     if (s < nsb) {
-      wa[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-      wb[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
-      wsv[j] = rb == 1 ? __ldg(wsr + s) : 0.0f;
+      w.a[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+      w.b[j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+      w.s[j] = rb == 1 ? __ldg(wsr + s) : 0.0f;
     }
   }
+}
+
+// Products of one weight row with every token row for the sub-blocks this
+// lane owns; P[rr][s] receives the product fed to the reference reduction.
+// The quantised rows are read from shared memory (SH) or global memory.
+template <int JM, bool SH>
+LZ_HD void gemv_products(const WRow<JM>& w, int K, int rb, const int8_t* xq, const float* xs, int r0, int nr,
+                         float (*P)[JM * 32], int lane) {
+  const int nsb = K >> 5;
 #pragma unroll
   for (int rr = 0; rr < kGemvRB; rr++) {
     if (rr < nr) {
@@ -140,47 +181,157 @@ LZ_HD void gemv_products(const int8_t* __restrict__ wr, const float* __restrict_
       for (int j = 0; j < JM; j++) {
         const int s = lane + 32 * j;
         if (s < nsb) {
-          const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
-          const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-          const float a = (float)dot32(wa[j], wb[j], xa, xb);
-          const float xsv = __ldg(xsr + s);
-          P[rr][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[j]));
+          int4 xa, xb;
+          float xsv;
+          if (SH) {
+            xa = *reinterpret_cast<const int4*>(xr + s * 32);
+            xb = *reinterpret_cast<const int4*>(xr + s * 32 + 16);
+            xsv = xsr[s];
+          } else {
+            xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+            xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+            xsv = __ldg(xsr + s);
+          }
+          const float a = (float)dot32(w.a[j], w.b[j], xa, xb);
+          P[rr][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, w.s[j]));
         }
       }
     }
   }
 }
 
-// Weight-streaming int8 GEMV/skinny GEMM: one warp per output row, each
-// lane owning 32-byte sub-blocks of the row (loaded once, reused for every
-// token row), per-sub-block int32 sums by __dp4a, then one lane per token
-// row runs the reference reduction.
-template <int JM>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_q8_kernel(const GemvArgs a) {
-  __shared__ __align__(16) float P[kGemvWarps][kGemvRB][JM * 32];
-  __shared__ __align__(16) float P2[kGemvWarps][kGemvRB][JM * 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * kGemvWarps + warp;
-  if (n >= a.N) return;
+// Bytes of dynamic shared memory of one GEMV block: per-warp product
+// buffers (two with a second weight) and, with the input-norm prologue,
+// the rows, norm weights, quantised rows, scales and inverse norms.
+inline size_t gemv_smem_bytes(int JM, int warps, bool w2, bool prologue, int R, int K) {
+  size_t b = (size_t)(w2 ? 2 : 1) * warps * kGemvRB * JM * 32 * 4;
+  if (prologue) b += (size_t)R * K * 4 + (size_t)K * 4 + (size_t)R * K + (size_t)R * (K / 32) * 4 + 64;
+  return b;
+}
+
+template <int JM, int WARPS, bool SH>
+LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM>& wn1, WRow<JM>& wn2,
+                     float (*P)[JM * 32], float (*P2)[JM * 32], int n, int lane) {
   const int rb = a.gs >> 5, ng = a.K / a.gs;
-  const int8_t* wr = a.W + (size_t)n * a.K;
-  const float* wsr = a.ws + (size_t)n * ng;
   const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
-  const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
-  for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
-    const int nr = min(kGemvRB, a.R - r0);
-    gemv_products<JM>(wr, wsr, a.K, rb, a.xq, a.xs, r0, nr, P[warp], lane);
-    if (a.W2) gemv_products<JM>(a.W2 + (size_t)n * a.K2, wsr2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2[warp], lane);
-    float prev = 0.0f;
-    if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
-    __syncwarp();
-    if (lane < nr) {
-      float v = q8_reduce(P[warp][lane], wsr, rb, ng);
-      if (a.W2) v = __fadd_rn(v, q8_reduce(P2[warp][lane], wsr2, rb2, ng2));
-      a.y[(size_t)(r0 + lane) * a.ldy + n] = a.mode == 1 ? __fadd_rn(prev, v) : v;
+  const int nstep = gridDim.x * WARPS;
+  for (; n < a.N; n += nstep) {
+    const WRow<JM> w1 = wn1, w2 = wn2;
+    if (n + nstep < a.N) {                 // the next row's weights stay in flight
+      load_wrow<JM>(wn1, a.W + (size_t)(n + nstep) * a.K, a.ws + (size_t)(n + nstep) * ng, a.K, rb, lane);
+      if (a.W2) load_wrow<JM>(wn2, a.W2 + (size_t)(n + nstep) * a.K2, a.ws2 + (size_t)(n + nstep) * ng2, a.K2, rb2, lane);
     }
-    __syncwarp();
+    const float* wsr = a.ws + (size_t)n * ng;
+    const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
+    for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
+      const int nr = min(kGemvRB, a.R - r0);
+      gemv_products<JM, SH>(w1, a.K, rb, xq, xs, r0, nr, P, lane);
+      if (a.W2) gemv_products<JM, false>(w2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2, lane);
+      float prev = 0.0f;
+      if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
+      __syncwarp();
+      if (lane < nr) {
+        float v = q8_reduce(P[lane], wsr, rb, ng);
+        if (a.W2) v = __fadd_rn(v, q8_reduce(P2[lane], wsr2, rb2, ng2));
+        a.y[(size_t)(r0 + lane) * a.ldy + n] = a.mode == 1 ? __fadd_rn(prev, v) : v;
+      }
+      __syncwarp();
+    }
   }
+}
+
+// Weight-streaming int8 GEMV/skinny GEMM, persistent over output rows: one
+// warp per output row at a time, each lane owning 32-byte sub-blocks of
+// the row (the first row loaded before the wait on the producing kernel,
+// each next row while the current one computes), per-sub-block int32 sums
+// by __dp4a, then one lane per token row runs the reference reduction.
+// With an input-norm prologue the grid is one WARPS-warp block per SM so
+// the prologue is paid once per SM.
+template <int JM, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
+  // dynamic shared memory: per-warp products P (and P2 with a second
+  // weight), then the prologue's rows (gemv_smem_bytes)
+  extern __shared__ __align__(16) float gsm[];
+  typedef float PBuf[kGemvRB][JM * 32];
+  PBuf* P = reinterpret_cast<PBuf*>(gsm);
+  PBuf* P2 = a.W2 ? P + WARPS : P;
+  float* pro = reinterpret_cast<float*>(a.W2 ? P2 + WARPS : P + WARPS);
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * WARPS + warp;
+  const int rb = a.gs >> 5, ng = a.K / a.gs;
+  const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
+  WRow<JM> w1, w2;
+  if (n0 < a.N) {
+    load_wrow<JM>(w1, a.W + (size_t)n0 * a.K, a.ws + (size_t)n0 * ng, a.K, rb, lane);
+    if (a.W2) load_wrow<JM>(w2, a.W2 + (size_t)n0 * a.K2, a.ws2 + (size_t)n0 * ng2, a.K2, rb2, lane);
+  }
+  pdl_wait();
+  if (!a.nx) {
+    gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P[warp], P2[warp], n0, lane);
+    return;
+  }
+  // input-norm prologue: rows -> shared (every load issued before the
+  // first store), one sequential sum of squares per row, then the (1+w)
+  // scaling and per-32 quantisation (src/ops_norm.c:690-747,
+  // src/ops_quant.c:2152-2282)
+  const int K = a.K, R = a.R, gpr = K / 32;
+  float* fx = pro;                                   // [R][K]
+  float* fw = fx + (size_t)R * K;                    // [K]
+  int8_t* sxq = reinterpret_cast<int8_t*>(fw + K);   // [R][K]
+  float* sxs = reinterpret_cast<float*>(sxq + (size_t)R * K);   // [R][K/32]
+  float* sinv = sxs + (size_t)R * gpr;               // [R]
+  {
+    constexpr int U = 8;
+    const int nv = (R * K + K) / 4, step = WARPS * 32;
+    for (int i0 = threadIdx.x; i0 < nv; i0 += U * step) {
+      float4 t[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * step;
+        if (i < nv)
+          t[u] = i * 4 < R * K ? __ldcg(reinterpret_cast<const float4*>(a.nx) + i)
+                               : __ldg(reinterpret_cast<const float4*>(a.nw) + (i - R * K / 4));
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * step;
+        if (i < nv) reinterpret_cast<float4*>(fx)[i] = t[u];
+      }
+    }
+  }
+  if (a.namax && blockIdx.x == 0 && threadIdx.x < R) a.namax[threadIdx.x] = 0ull;
+  __syncthreads();
+  {
+    const int r = warp + WARPS * lane;
+    if (r < R) sinv[r] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(fx + (size_t)r * K, K), (float)K), a.eps));
+  }
+  __syncthreads();
+  const bool store = a.nout && blockIdx.x == 0;
+  for (int g0 = warp * 4; g0 < R * gpr; g0 += WARPS * 4) {
+    float v[4];
+    int8_t q[4];
+    float sg[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int g = min(g0 + k, R * gpr - 1);
+      const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
+      v[k] = __fmul_rn(__fmul_rn(fx[(size_t)r * K + i], sinv[r]), __fadd_rn(1.0f, fw[i]));
+    }
+    warp_quant32_x4(v, q, sg);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int g = g0 + k;
+      if (g < R * gpr) {
+        const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
+        sxq[(size_t)r * K + i] = q[k];
+        if (lane == 0) sxs[g] = sg[k];
+        if (store) a.nout[(size_t)r * K + i] = v[k];
+      }
+    }
+  }
+  __syncthreads();
+  gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P[warp], P2[warp], n0, lane);
 }
 
 // --------------------------------------------------------- row kernels
@@ -193,11 +344,16 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
                                      const float* __restrict__ w, int n, float eps,
                                      float* out, int ldo, int8_t* xq, float* xs,
                                      unsigned long long* amax_clear) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   __shared__ float s_inv;
   const int r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = xr[i];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    sm[i] = xr[i];
+    sm[n + i] = w[i];
+  }
   if (amax_clear && threadIdx.x == 0) amax_clear[r] = 0ull;
   __syncthreads();
   if (threadIdx.x == 0) s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, n), (float)n), eps));
@@ -206,7 +362,7 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int g = warp; g < n / 32; g += nw) {
     const int i = g * 32 + lane;
-    const float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, w[i]));
+    const float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, sm[n + i]));
     if (out) out[(size_t)r * ldo + i] = o;
     xq[(size_t)r * n + i] = warp_quant32(o, &xs[(size_t)r * (n / 32) + g]);
   }
@@ -215,6 +371,8 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
 // Embedding rows: x[i] = q[i] * scale[group]  (src/ops_epi.c:1276-1280).
 __global__ void embed_kernel(const int8_t* __restrict__ eq, const float* __restrict__ es,
                              int gs, int d, const int* __restrict__ tok, float* x) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const size_t base = (size_t)tok[r] * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x)
@@ -225,6 +383,8 @@ __global__ void embed_kernel(const int8_t* __restrict__ eq, const float* __restr
 // followed by lz_quantize_q8).  gate at column g0, up at column u0.
 __global__ void swiglu_quant_kernel(const float* __restrict__ src, int lds, int g0, int u0,
                                     int n, int8_t* xq, float* xs) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const float* row = src + (size_t)r * lds;
@@ -243,6 +403,8 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ src, int lds, int 
 constexpr int kArgmaxChunk = 4096;
 __global__ void argmax_kernel(const float* __restrict__ logits, int V, int p1_mode,
                               unsigned long long* slot) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.y;
   const float* row = logits + (size_t)r * V;
   const int i0 = blockIdx.x * kArgmaxChunk, i1 = min(V, i0 + kArgmaxChunk);
@@ -269,96 +431,100 @@ struct KdaSeq {            // one sequence's rows inside a forward batch
   int row0, nrows, base_slot, seq;
 };
 
-// f_b_proj of every token (quantised f_a latent, src/forward_kda.c:773-819)
-// then the per-channel decay gate gt = exp(lb * sigmoid(exp(A_log[h]) *
-// (pre + dt_bias))) (src/forward_kda.c:277-297, 847-851).  rank <= 256.
-__global__ void kda_fb_gate_kernel(const float* __restrict__ inproj, int ldi, int off_fa, int rank,
-                                   const int8_t* __restrict__ fbq, const float* __restrict__ fbs, int fb_gs,
-                                   const float* __restrict__ a_log, const float* __restrict__ dt_bias,
-                                   float lb, int nvk, int kd, float* gate) {
+// Both pre-recurrence steps in one grid: blocks [0, nconv) run the conv1d
+// of (sequence, 256-channel slice) and the rest the f_b_proj/decay gate of
+// (token row, 256-output slice).  Same arithmetic as the two kernels above.
+struct KdaPreArgs {
+  const float* inproj; int ldi; int conv_dim; const float* cw; const KdaSeq* seqs;
+  float* conv_state; size_t seq_stride, slot_stride; int depth, adv; float* conv_out;
+  int off_fa, rank; const int8_t* fbq; const float* fbs; int fb_gs; const float* a_log;
+  const float* dt_bias; float lb; int nvk, kd; float* gate; int nconv_x, nfb_x, nseq;
+};
+
+__global__ void __launch_bounds__(256) kda_pre_kernel(const KdaPreArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) int8_t lq[256];
   __shared__ float ls[8];
-  const int r = blockIdx.y;
+  const int nconv = a.nconv_x * a.nseq;
+  if ((int)blockIdx.x < nconv) {
+    const KdaSeq sq = a.seqs[blockIdx.x / a.nconv_x];
+    const int c = (blockIdx.x % a.nconv_x) * 256 + threadIdx.x;
+    if (c >= a.conv_dim) return;
+    float* st0 = a.conv_state + (size_t)sq.seq * a.seq_stride + (size_t)c * 3;
+    const float* st = st0 + (size_t)sq.base_slot * a.slot_stride;
+    float h0 = st[0], h1 = st[1], h2 = st[2];
+    const float4 w = __ldg(reinterpret_cast<const float4*>(a.cw) + c);
+    for (int t = 0; t < sq.nrows; t++) {
+      const int r = sq.row0 + t;
+      const float xv = a.inproj[(size_t)r * a.ldi + c];
+      float sum = 0.0f;
+      sum = __fadd_rn(sum, __fmul_rn(w.x, h0));
+      sum = __fadd_rn(sum, __fmul_rn(w.y, h1));
+      sum = __fadd_rn(sum, __fmul_rn(w.z, h2));
+      sum = __fadd_rn(sum, __fmul_rn(w.w, xv));
+      a.conv_out[(size_t)r * a.conv_dim + c] = silu(sum);
+      h0 = h1; h1 = h2; h2 = xv;
+      if (a.adv) {
+        float* d = st0 + (size_t)((sq.base_slot + t + 1) % a.depth) * a.slot_stride;
+        d[0] = h0; d[1] = h1; d[2] = h2;
+      }
+    }
+    if (!a.adv) {
+      float* d = st0 + (size_t)sq.base_slot * a.slot_stride;
+      d[0] = h0; d[1] = h1; d[2] = h2;
+    }
+    return;
+  }
+  const int b2 = blockIdx.x - nconv;
+  const int r = b2 / a.nfb_x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int g = warp; g < rank / 32; g += nw) {
-    const float v = inproj[(size_t)r * ldi + off_fa + g * 32 + lane];
+  for (int g = warp; g < a.rank / 32; g += nw) {
+    const float v = a.inproj[(size_t)r * a.ldi + a.off_fa + g * 32 + lane];
     lq[g * 32 + lane] = warp_quant32(v, &ls[g]);
   }
   __syncthreads();
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= nvk) return;
-  const int nsb = rank / 32, rb = fb_gs / 32, ng = rank / fb_gs;
+  const int j = (b2 % a.nfb_x) * 256 + threadIdx.x;
+  if (j >= a.nvk) return;
+  const int nsb = a.rank / 32, rb = a.fb_gs / 32, ng = a.rank / a.fb_gs;
   __align__(16) float p[8];
-  const int8_t* wr = fbq + (size_t)j * rank;
-  const float* wsr = fbs + (size_t)j * ng;
+  const int8_t* wr = a.fbq + (size_t)j * a.rank;
+  const float* wsr = a.fbs + (size_t)j * ng;
   int4 wa[8], wb[8];
 #pragma unroll
-  for (int s = 0; s < 8; s++)
-    if (s < nsb) {
-      wa[s] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-      wb[s] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+  for (int q = 0; q < 8; q++)
+    if (q < nsb) {
+      wa[q] = __ldg(reinterpret_cast<const int4*>(wr + q * 32));
+      wb[q] = __ldg(reinterpret_cast<const int4*>(wr + q * 32 + 16));
     }
-  const float dtb = __ldg(dt_bias + j), alg = __ldg(a_log + j / kd);
+  const float dtb = __ldg(a.dt_bias + j), alg = __ldg(a.a_log + j / a.kd);
 #pragma unroll
-  for (int s = 0; s < 8; s++)
-    if (s < nsb) {
-      const int4 xa = *reinterpret_cast<const int4*>(lq + s * 32);
-      const int4 xb = *reinterpret_cast<const int4*>(lq + s * 32 + 16);
-      const float a = (float)dot32(wa[s], wb[s], xa, xb);
-      p[s] = rb > 1 ? __fmul_rn(a, ls[s]) : __fmul_rn(a, __fmul_rn(ls[s], wsr[s]));
+  for (int q = 0; q < 8; q++)
+    if (q < nsb) {
+      const int4 xa = *reinterpret_cast<const int4*>(lq + q * 32);
+      const int4 xb = *reinterpret_cast<const int4*>(lq + q * 32 + 16);
+      const float av = (float)dot32(wa[q], wb[q], xa, xb);
+      p[q] = rb > 1 ? __fmul_rn(av, ls[q]) : __fmul_rn(av, __fmul_rn(ls[q], wsr[q]));
     }
   const float pre = __fadd_rn(q8_reduce(p, wsr, rb, ng), dtb);
   const float decay = exp_body(alg);
-  const float g = __fmul_rn(lb, sigmoid(__fmul_rn(decay, pre)));
-  gate[(size_t)r * nvk + j] = exp_body(g);
+  const float g = __fmul_rn(a.lb, sigmoid(__fmul_rn(decay, pre)));
+  a.gate[(size_t)r * a.nvk + j] = exp_body(g);
 }
 
-// Depthwise causal conv1d (kernel 4) + SiLU over q, k and v channels,
-// token-serial per sequence through the state ring (src/ops_conv1d.c:26-53,
-// src/forward_kda.c:680-749).  adv = 1: token t reads slot base+t and
-// writes slot base+t+1; adv = 0: one slot, updated in place.
-__global__ void kda_conv_kernel(const float* __restrict__ inproj, int ldi, int conv_dim,
-                                const float* __restrict__ cw, const KdaSeq* __restrict__ seqs,
-                                float* conv_state, size_t seq_stride, size_t slot_stride,
-                                int depth, int adv, float* out, int ldo) {
-  const KdaSeq sq = seqs[blockIdx.y];
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= conv_dim) return;
-  float* st0 = conv_state + (size_t)sq.seq * seq_stride + (size_t)c * 3;
-  const float* st = st0 + (size_t)sq.base_slot * slot_stride;
-  float h0 = st[0], h1 = st[1], h2 = st[2];
-  const float4 w = __ldg(reinterpret_cast<const float4*>(cw) + c);
-  for (int t = 0; t < sq.nrows; t++) {
-    const int r = sq.row0 + t;
-    const float xv = inproj[(size_t)r * ldi + c];
-    float sum = 0.0f;
-    sum = __fadd_rn(sum, __fmul_rn(w.x, h0));
-    sum = __fadd_rn(sum, __fmul_rn(w.y, h1));
-    sum = __fadd_rn(sum, __fmul_rn(w.z, h2));
-    sum = __fadd_rn(sum, __fmul_rn(w.w, xv));
-    out[(size_t)r * ldo + c] = silu(sum);
-    h0 = h1; h1 = h2; h2 = xv;
-    if (adv) {
-      const int so = (sq.base_slot + t + 1) % depth;
-      float* d = st0 + (size_t)so * slot_stride;
-      d[0] = h0; d[1] = h1; d[2] = h2;
-    }
-  }
-  if (!adv) {
-    float* d = st0 + (size_t)sq.base_slot * slot_stride;
-    d[0] = h0; d[1] = h1; d[2] = h2;
-  }
-}
-
-// The KDA recurrence of one (sequence, head), token-serial, with the 64x64
-// two-plane int8 state resident in shared memory: l2norm(q)*kd^-1/2,
-// l2norm(k), beta = sigmoid(b), pass 1 (u = S^T(g.k), w = S^T(g.q),
-// kq = k.q, all sequential over the 64 state rows), pass 2 (each state row
-// g*S + k*u requantised in two planes), then the gated RMSNorm of the head
-// output and its per-32 quantisation for o_proj.
-// src/forward_kda.c:856-936 and 1029-1040, src/ops_gdn.c:2488-2778,
-// src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
+// The KDA recurrence of one (sequence, head) with the 64x64 two-plane int8
+// state resident in shared memory.  Everything that does not read the
+// state runs for a batch of up to kRecurTB tokens at once: l2norm(q) *
+// kd^-1/2, l2norm(k), beta = sigmoid(b); then per token, serially, pass 1
+// (u = S^T(g.k), w = S^T(g.q), kq = k.q, each a sequential sum over the 64
+// state rows, products formed by all warps first), the head output
+// w + u*kq with u = (v - u)*beta, and pass 2 (each state row g*S + k*u
+// requantised in two planes, one warp per 32-wide group); finally the
+// gated RMSNorm and per-32 quantisation of every token's output in
+// parallel.  src/forward_kda.c:856-936 and 1029-1040,
+// src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
 constexpr int kRecurThreads = 1024;
+constexpr int kRecurTB = 4;
 __global__ void __launch_bounds__(kRecurThreads)
 kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  const float* __restrict__ inproj, int ldi, int off_b, int off_g,
@@ -369,16 +535,19 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  int depth, int adv, float ssm_scale,
                  const float* __restrict__ o_norm, float eps, int vdim,
                  int8_t* oq, float* os) {
-  constexpr int KD = 64, VD = 64;
+  pdl_trigger();
+  pdl_wait();
+  constexpr int KD = 64, VD = 64, TB = kRecurTB;
   __shared__ __align__(16) int8_t hi[KD][VD];
   __shared__ __align__(16) int8_t lo[KD][VD];
   __shared__ __align__(16) float sc[KD][2];
-  __shared__ __align__(16) float qc[KD], kc[KD], vcs[VD], zs[VD];
-  __shared__ __align__(16) float qn[KD], kn[KD], gv[KD], U[VD], OUT[VD];
-  __shared__ float s_misc[4];
+  __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], vcs[TB][VD], zs[TB][VD], OUT[TB][VD];
+  __shared__ __align__(16) float PU[KD][VD], PW[KD][VD];   // pass-1 products
+  __shared__ __align__(16) float U[VD];
+  __shared__ float inv_q[TB], inv_k[TB], beta[TB], kqv[TB], inv_o[TB];
   const KdaSeq sq = seqs[blockIdx.y];
   const int h = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
   const size_t head_off = (size_t)layer_off_q + (size_t)h * KD * VD;
   const size_t seq_off = (size_t)sq.seq * seq_stride_q;
   {
@@ -389,79 +558,103 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     }
     if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
   }
-  for (int t = 0; t < sq.nrows; t++) {
-    const int r = sq.row0 + t;
-    if (tid < 64) {
-      qc[tid] = conv_out[(size_t)r * ldc + h * KD + tid];
-      kc[tid] = conv_out[(size_t)r * ldc + kdim + h * KD + tid];
-      vcs[tid] = conv_out[(size_t)r * ldc + 2 * kdim + h * VD + tid];
-      zs[tid] = inproj[(size_t)r * ldi + off_g + h * VD + tid];
-      gv[tid] = gate[(size_t)r * nvk + h * KD + tid];
+  for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
+    const int nt = min(TB, sq.nrows - t0);
+    // stage the batch (raw q, k in qn/kn until normalised)
+    for (int q = tid; q < nt * 64; q += blockDim.x) {
+      const int t = q >> 6, i = q & 63;
+      const size_t r = (size_t)(sq.row0 + t0 + t);
+      qn[t][i] = conv_out[r * ldc + h * KD + i];
+      kn[t][i] = conv_out[r * ldc + kdim + h * KD + i];
+      vcs[t][i] = conv_out[r * ldc + 2 * kdim + h * VD + i];
+      zs[t][i] = inproj[r * ldi + off_g + h * VD + i];
+      gv[t][i] = gate[r * nvk + h * KD + i];
     }
     __syncthreads();
-    if (tid == 0) s_misc[0] = rsqrt_body(__fadd_rn(seq_sumsq(qc, KD), kL2Eps));
-    if (tid == 32) s_misc[1] = rsqrt_body(__fadd_rn(seq_sumsq(kc, KD), kL2Eps));
-    if (tid == 64) s_misc[2] = sigmoid(inproj[(size_t)r * ldi + off_b + h]);
-    __syncthreads();
-    if (tid < KD) {
-      qn[tid] = __fmul_rn(__fmul_rn(qc[tid], s_misc[0]), ssm_scale);
-      kn[tid] = __fmul_rn(kc[tid], s_misc[1]);
+    if (lane == 0 && warp < 3 * nt) {          // independent chains on separate warps
+      const int t = warp % nt, which = warp / nt;
+      if (which == 0) inv_q[t] = rsqrt_body(__fadd_rn(seq_sumsq(qn[t], KD), kL2Eps));
+      else if (which == 1) inv_k[t] = rsqrt_body(__fadd_rn(seq_sumsq(kn[t], KD), kL2Eps));
+      else beta[t] = sigmoid(inproj[(size_t)(sq.row0 + t0 + t) * ldi + off_b + h]);
     }
     __syncthreads();
-    if (tid < VD) {
-      const int vv = tid, grp = vv >> 5;
-      float u = 0.0f, w = 0.0f, kq = 0.0f;
-#pragma unroll 8
-      for (int kk = 0; kk < KD; kk++) {
-        const float kcv = kn[kk], qcv = qn[kk], g = gv[kk];
-        const float kcw = __fmul_rn(kcv, g), qcw = __fmul_rn(qcv, g);
-        kq = __fadd_rn(kq, __fmul_rn(kcv, qcv));
-        const float s = sc[kk][grp];
-        const float sck = __fmul_rn(s, kcw), scq = __fmul_rn(s, qcw);
+    for (int q = tid; q < nt * 64; q += blockDim.x) {
+      const int t = q >> 6, i = q & 63;
+      qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), ssm_scale);
+      kn[t][i] = __fmul_rn(kn[t][i], inv_k[t]);
+    }
+    __syncthreads();
+    for (int t = 0; t < nt; t++) {
+      // pass 1 products: all warps, one (kk, vv) element each
+      for (int q = tid; q < KD * VD; q += blockDim.x) {
+        const int kk = q >> 6, vv = q & 63;
+        const float g = gv[t][kk], s = sc[kk][vv >> 5];
+        const float sck = __fmul_rn(s, __fmul_rn(kn[t][kk], g));
+        const float scq = __fmul_rn(s, __fmul_rn(qn[t][kk], g));
         const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-        u = __fadd_rn(u, __fmul_rn(e, sck));
-        w = __fadd_rn(w, __fmul_rn(e, scq));
+        PU[kk][vv] = __fmul_rn(e, sck);
+        PW[kk][vv] = __fmul_rn(e, scq);
       }
-      u = __fmul_rn(__fsub_rn(vcs[vv], u), s_misc[2]);
-      U[vv] = u;
-      OUT[vv] = __fadd_rn(w, __fmul_rn(u, kq));
-    }
-    __syncthreads();
-    for (int unit = warp; unit < KD * 2; unit += blockDim.x >> 5) {
-      const int kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-      const float scg = __fmul_rn(sc[kk][grp], gv[kk]);
-      const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-      const float buf = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[kk], U[vv]));
-      const uint32_t am = warp_max_u32(abs_bits(buf));
-      float sg, inv;
-      q8_scale_from_amax(am, &sg, &inv);
-      const float f = __fmul_rn(buf, inv);
-      int hq = q8_clamp(q8_round(f));
-      float res = __fsub_rn(f, (float)hq);
-      if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
-      else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
-      __syncwarp();
-      hi[kk][vv] = (int8_t)hq;
-      lo[kk][vv] = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
-      if (lane == 0) sc[kk][grp] = sg;
-    }
-    __syncthreads();
-    if (adv) {
-      const int so = (sq.base_slot + t + 1) % depth;
-      const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
-      if (tid < KD * VD / 16) {
-        reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-        reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+      if (tid == 128) {                       // kq = k.q, sequential over kk
+        float kq = 0.0f;
+        for (int kk = 0; kk < KD; kk++) kq = __fadd_rn(kq, __fmul_rn(kn[t][kk], qn[t][kk]));
+        kqv[t] = kq;
       }
-      if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+      __syncthreads();
+      if (tid < 2 * VD) {                     // the sequential sums over kk
+        const int vv = tid & 63;
+        const float(*PP)[VD] = tid < VD ? PU : PW;
+        float acc = 0.0f;
+#pragma unroll 16
+        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, PP[kk][vv]);
+        if (tid < VD) PU[0][vv] = acc; else PW[0][vv] = acc;
+      }
+      __syncthreads();
+      if (tid < VD) {
+        const float u = __fmul_rn(__fsub_rn(vcs[t][tid], PU[0][tid]), beta[t]);
+        U[tid] = u;
+        OUT[t][tid] = __fadd_rn(PW[0][tid], __fmul_rn(u, kqv[t]));
+      }
+      __syncthreads();
+      // pass 2: one warp per (state row, 32-wide group)
+      for (int unit = warp; unit < KD * 2; unit += nwarp) {
+        const int kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
+        const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);
+        const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+        const float buf = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[t][kk], U[vv]));
+        const uint32_t am = warp_max_u32(abs_bits(buf));
+        float sg, iv;
+        q8_scale_from_amax(am, &sg, &iv);
+        const float f = __fmul_rn(buf, iv);
+        int hq = q8_clamp(q8_round(f));
+        float res = __fsub_rn(f, (float)hq);
+        if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
+        else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
+        __syncwarp();
+        hi[kk][vv] = (int8_t)hq;
+        lo[kk][vv] = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
+        if (lane == 0) sc[kk][grp] = sg;
+      }
+      __syncthreads();
+      if (adv) {
+        const int so = (sq.base_slot + t0 + t + 1) % depth;
+        const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
+        if (tid < KD * VD / 16) {
+          reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+          reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+        }
+        if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+      }
     }
-    // gated RMSNorm of the head output, then per-32 quantisation.
-    if (tid == 0) s_misc[3] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT, VD), (float)VD), eps));
+    // gated RMSNorm of every token's head output, then per-32 quantisation
+    if (lane == 0 && warp < nt)
+      inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), eps));
     __syncthreads();
-    if (tid < VD) {
-      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[tid], s_misc[3]), o_norm[tid]), silu(zs[tid]));
-      oq[(size_t)r * vdim + h * VD + tid] =
-          warp_quant32(o, &os[(size_t)r * (vdim / 32) + (h * VD) / 32 + (tid >> 5)]);
+    for (int q = tid; q < nt * 64; q += blockDim.x) {
+      const int t = q >> 6, i = q & 63;
+      const size_t r = (size_t)(sq.row0 + t0 + t);
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), o_norm[i]), silu(zs[t][i]));
+      oq[r * vdim + h * VD + i] = warp_quant32(o, &os[r * (vdim / 32) + (h * VD) / 32 + (i >> 5)]);
     }
     __syncthreads();
   }
@@ -484,7 +677,10 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
 // E <= 256.
 __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
                                  const float* __restrict__ bias, int E, int topk, int latent,
-                                 int* pair_expert, float* pair_w, int8_t* latq, float* lats) {
+                                 int* pair_expert, float* pair_w, int8_t* latq, float* lats,
+                                 int off_shg, int off_shu, int sw, int8_t* shq, float* shs) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) {
     float score[8], key[8];
@@ -532,9 +728,18 @@ __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int o
     if (lane < topk && wsum > 0.0f && pair_expert[r * topk + lane] >= 0)
       pair_w[r * topk + lane] = __fdiv_rn(pair_w[r * topk + lane], wsum);
   }
-  for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
-    const float v = moein[(size_t)r * ldm + off_lat + g * 32 + lane];
-    latq[(size_t)r * latent + g * 32 + lane] = warp_quant32(v, &lats[(size_t)r * (latent / 32) + g]);
+  // the routed latent, then (when present) the shared expert's
+  // silu(gate)*up (src/forward_moe.c:484-536), both quantised per 32
+  const int ng_l = latent / 32, ng_s = sw / 32;
+  for (int g = warp; g < ng_l + ng_s; g += blockDim.x >> 5) {
+    if (g < ng_l) {
+      const float v = moein[(size_t)r * ldm + off_lat + g * 32 + lane];
+      latq[(size_t)r * latent + g * 32 + lane] = warp_quant32(v, &lats[(size_t)r * ng_l + g]);
+    } else {
+      const int gg = g - ng_l, i = gg * 32 + lane;
+      const float gv = moein[(size_t)r * ldm + off_shg + i], uv = moein[(size_t)r * ldm + off_shu + i];
+      shq[(size_t)r * sw + i] = warp_quant32(__fmul_rn(silu(gv), uv), &shs[(size_t)r * ng_s + gg]);
+    }
   }
 }
 
@@ -547,6 +752,8 @@ moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, 
                const int* __restrict__ pair_expert, int topk,
                const int8_t* __restrict__ latq, const float* __restrict__ lats,
                int8_t* hq, float* hs) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) float P[8][8][32];
   __shared__ float H[64];
   const int p = blockIdx.y, r = p / topk;
@@ -598,57 +805,64 @@ moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, 
   }
 }
 
-// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048.
+// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
+// the last block to finish among a token row's pairs then forms
+// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
+// the last block to finish among a token row's pairs then forms
+// lat_y = sum over the row's selected experts, in selection order, of
+// w * h2 (src/forward_moe.c:198-199) and quantises it per 32.
 __global__ void __launch_bounds__(256)
 moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int ffn, int latent, int gs,
-              const int* __restrict__ pair_expert,
-              const int8_t* __restrict__ hq, const float* __restrict__ hs, float* h2) {
+              const int* __restrict__ pair_expert, const float* __restrict__ pair_w, int topk,
+              const int8_t* __restrict__ hq, const float* __restrict__ hs, float* h2,
+              int* row_counter, int8_t* yq, float* ys) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) float P[8][64];
-  const int p = blockIdx.y;
+  __shared__ int s_last;
+  const int p = blockIdx.y, r = p / topk;
   const int e = pair_expert[p];
-  if (e < 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * 8 + warp;
-  if (n >= latent) return;
-  const int nsb = ffn / 32, rb = gs / 32, ng = ffn / gs;
-  const int8_t* wr = w2q + ((size_t)e * latent + n) * ffn;
-  const float* wsr = w2s + ((size_t)e * latent + n) * ng;
-  const int8_t* xr = hq + (size_t)p * ffn;
-  const float* xsr = hs + (size_t)p * nsb;
+  if (e >= 0 && n < latent) {
+    const int nsb = ffn / 32, rb = gs / 32, ng = ffn / gs;
+    const int8_t* wr = w2q + ((size_t)e * latent + n) * ffn;
+    const float* wsr = w2s + ((size_t)e * latent + n) * ng;
+    const int8_t* xr = hq + (size_t)p * ffn;
+    const float* xsr = hs + (size_t)p * nsb;
 #pragma unroll
-  for (int j = 0; j < 2; j++) {
-    const int s = lane + 32 * j;
-    if (s < nsb) {
-      const int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-      const int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
-      const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
-      const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-      const float a = (float)dot32(wa, wb, xa, xb);
-      const float xsv = __ldg(xsr + s);
-      P[warp][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, __ldg(wsr + s)));
+    for (int j = 0; j < 2; j++) {
+      const int s = lane + 32 * j;
+      if (s < nsb) {
+        const int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+        const int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+        const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
+        const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
+        const float a = (float)dot32(wa, wb, xa, xb);
+        const float xsv = __ldg(xsr + s);
+        P[warp][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, __ldg(wsr + s)));
+      }
     }
+    __syncwarp();
+    if (lane == 0) h2[(size_t)p * latent + n] = q8_reduce(P[warp], wsr, rb, ng);
   }
-  __syncwarp();
-  if (lane == 0) h2[(size_t)p * latent + n] = q8_reduce(P[warp], wsr, rb, ng);
-}
-
-// lat_y = sum over the row's selected experts, in selection order, of
-// w * h2 (src/forward_moe.c:198-199), then its per-32 quantisation.
-__global__ void moe_combine_kernel(const float* __restrict__ h2, const float* __restrict__ pair_w,
-                                   const int* __restrict__ pair_expert, int topk, int latent,
-                                   int8_t* yq, float* ys) {
-  const int r = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int g = warp; g < latent / 32; g += nw) {
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(row_counter + r, 1) == topk * (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
     const int i = g * 32 + lane;
     float acc = 0.0f;
     for (int t = 0; t < topk; t++) {
-      const int p = r * topk + t;
-      if (pair_expert[p] < 0) continue;
-      acc = __fadd_rn(acc, __fmul_rn(pair_w[p], h2[(size_t)p * latent + i]));
+      const int pp = r * topk + t;
+      if (pair_expert[pp] < 0) continue;
+      acc = __fadd_rn(acc, __fmul_rn(pair_w[pp], __ldcg(h2 + (size_t)pp * latent + i)));
     }
     yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
   }
+  if (threadIdx.x == 0) row_counter[r] = 0;
 }
 
 // ---------------------------------------------------------------- MTP
@@ -660,6 +874,8 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
                                  const float* __restrict__ hid, const int* __restrict__ hid_idx,
                                  const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
                                  int8_t* xq, float* xs) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float sm[];           // [2][d]
   __shared__ float s_inv[2];
   const int r = blockIdx.x;
@@ -723,6 +939,8 @@ __global__ void mtp_kv_write_kernel(const float* __restrict__ qkv, int ldq, int 
                                     float eps, int hd, int rot, int kvd, const float* __restrict__ rope_cs,
                                     int8_t* kq, float* ks, int8_t* vq, float* vs,
                                     size_t cache_seq_stride) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) float v[64];
   __shared__ float s_inv;
   const int h = blockIdx.x, r = blockIdx.y;
@@ -754,6 +972,8 @@ mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
                 const int8_t* __restrict__ kq, const float* __restrict__ ks,
                 const int8_t* __restrict__ vq, const float* __restrict__ vs,
                 size_t cache_seq_stride, int8_t* aq, float* as) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float att[];
   __shared__ __align__(16) float qh[64];
   __shared__ __align__(16) int8_t vch[kAttnChunk][64];
@@ -842,11 +1062,41 @@ mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
 // ------------------------------------------------------- spec rounds
 
 struct SeqRound {          // per-sequence round bookkeeping on the device
+  unsigned long long rng;   // sampler xorshift64* state (src/sampler.c:185-203)
+  float temp, topp;         // sampler temperature and top-p
   int anchor, anchor_pos, mtp_pos, ssm_slot;
   int k, n_accept, n_emit, done;
   int draft[8], out[8];
   int rounds, emitted, accepted, drafted;   // running totals
 };
+
+// After the acceptance of a round (src/generate.c:798-991, 1234-1377):
+// counters, the state ring pointed at the accepted slot
+// ((base + n_accept + 1) % depth, src/forward_ckpt.c), the catch-up rows
+// (MTP cache rows of accepted drafts 1..n_accept-1), the MTP position and
+// the next anchor.
+LZ_HD void round_bookkeeping(SeqRound& s, int b, int n_accept, int k, int kmax, int row0, int depth, int seq_len,
+                             MtpRow* catch_rows, int* catch_tok, int* catch_hidx) {
+  s.n_accept = n_accept;
+  s.n_emit = n_accept + 1;
+  s.rounds += 1;
+  s.emitted += n_accept + 1;
+  s.accepted += n_accept;
+  s.drafted += k;
+  s.ssm_slot = (s.ssm_slot + n_accept + 1) % depth;
+  for (int j = 0; j < kmax - 1; j++) {
+    MtpRow cr;
+    cr.seq = b;
+    cr.pos = s.mtp_pos + 1 + j;
+    cr.active = j < n_accept - 1 && cr.pos < seq_len;
+    catch_rows[b * (kmax - 1) + j] = cr;
+    catch_tok[b * (kmax - 1) + j] = s.out[j < 8 ? j : 0];
+    catch_hidx[b * (kmax - 1) + j] = row0 + j;
+  }
+  s.mtp_pos += n_accept;
+  s.anchor = s.out[n_accept];
+  s.anchor_pos = s.anchor_pos + 1 + n_accept;
+}
 
 // Greedy acceptance of one round (src/generate.c:232-243, 798-991): the
 // verify arg-max of every row, accept the agreeing draft prefix, point
@@ -858,6 +1108,8 @@ __global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax,
                                           const float* __restrict__ vhid, int d, float* chain,
                                           int depth, int seq_len, MtpRow* catch_rows, int* catch_tok,
                                           int* catch_hidx) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   if (b >= nseq) return;
   SeqRound& s = sr[b];
@@ -871,25 +1123,7 @@ __global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax,
       if (s.draft[i] != s.out[i]) { n_accept = i; break; }
     }
     if (n_accept == k) s.out[k] = argmax_index(vmax[row0 + k]);
-    s.n_accept = n_accept;
-    s.n_emit = n_accept + 1;
-    s.rounds += 1;
-    s.emitted += n_accept + 1;
-    s.accepted += n_accept;
-    s.drafted += k;
-    s.ssm_slot = (s.ssm_slot + n_accept + 1) % depth;
-    for (int j = 0; j < kmax - 1; j++) {
-      MtpRow cr;
-      cr.seq = b;
-      cr.pos = s.mtp_pos + 1 + j;
-      cr.active = j < n_accept - 1 && cr.pos < seq_len;
-      catch_rows[b * (kmax - 1) + j] = cr;
-      catch_tok[b * (kmax - 1) + j] = s.out[j < 8 ? j : 0];
-      catch_hidx[b * (kmax - 1) + j] = row0 + j;
-    }
-    s.mtp_pos += n_accept;
-    s.anchor = s.out[n_accept];
-    s.anchor_pos = s.anchor_pos + 1 + n_accept;
+    round_bookkeeping(s, b, n_accept, k, kmax, row0, depth, seq_len, catch_rows, catch_tok, catch_hidx);
     n_acc_s = n_accept;
   }
   __syncthreads();

@@ -66,8 +66,10 @@ def lib():
         "lz_spec_accept_temp": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float,
                                         P(ctypes.c_uint64), P(c_int)]),
         "lz_seq_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, P(c_int), c_char_p, c_int]),
+        "lz_seq_set_sampler": (c_int, [c_void_p, c_int, c_float, c_float, ctypes.c_uint64]),
         "lz_spec_round_batch": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_set_graphs": (c_int, [c_void_p, c_int]),
+        "lz_set_pdl": (c_int, [c_void_p, c_int]),
         "lz_generate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                 ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
                                 c_char_p, c_int]),
@@ -92,8 +94,12 @@ EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_s
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
-           "lz_seq_prefill", "lz_spec_round_batch", "lz_set_graphs", "lz_generate", "lz_state_stream",
+           "lz_seq_prefill", "lz_seq_set_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
            "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static"]
+
+
+class LZSampler(ctypes.Structure):
+    _fields_ = [("temperature", c_float), ("topp", c_float), ("rng_state", ctypes.c_uint64)]
 
 
 class Model:
@@ -177,6 +183,9 @@ class State:
     def graphs(self, on: bool):
         lib().lz_set_graphs(self.h, int(on))
 
+    def pdl(self, on: bool):
+        lib().lz_set_pdl(self.h, int(on))
+
     # --- forwards of sequence 0
     def forward(self, tok, pos, capture=False):
         fn = lib().lz_forward_capture if capture else lib().lz_forward
@@ -223,7 +232,25 @@ class State:
             raise LzError(f"spec round failed ({rc}): {err.value.decode()}")
         return out[:rc].copy(), na.value, npos.value, ke.value
 
+    def spec_round_temp(self, anchor, anchor_pos, k, temp, topp, rng):
+        """One coupled temperature round of sequence 0; returns the tokens,
+        n_accept, the new position, k_eff and the advanced generator."""
+        out = np.zeros(8, np.int32)
+        na, npos, ke = c_int(), c_int(), c_int()
+        err = ctypes.create_string_buffer(256)
+        samp = LZSampler(float(temp), float(topp), int(rng))
+        rc = lib().lz_spec_round_temp(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0, ctypes.byref(samp), 0, 0,
+                                      _ptr(out), ctypes.byref(na), ctypes.byref(npos), ctypes.byref(ke), err, 256)
+        if rc < 0:
+            raise LzError(f"temperature round failed ({rc}): {err.value.decode()}")
+        return out[:rc].copy(), na.value, npos.value, ke.value, samp.rng_state
+
     # --- batched path
+    def set_sampler(self, seq, temp, topp, seed):
+        rc = lib().lz_seq_set_sampler(self.h, seq, float(temp), float(topp), int(seed))
+        if rc:
+            raise LzError(f"set sampler failed ({rc})")
+
     def seq_prefill(self, seq, prompt):
         p = np.ascontiguousarray(prompt, np.int32)
         a = c_int()

@@ -111,15 +111,90 @@ def test_batched_rounds_match_per_sequence_oracle(gcase):
 
 
 def test_graph_and_eager_rounds_agree(gcase):
+    """Graph replay with programmatic dependent launch against plain
+    eager launches: identical tokens."""
     import lz98
     name, d, g, m = gcase
     outs = []
     for graphs in (True, False):
         s = lz98.State(m, 256, 4, n_seq=2)
         s.graphs(graphs)
+        s.pdl(graphs)
         for b in range(2):
             s.seq_prefill(b, g["prompt"][: 10 + 5 * b])
         res = [s.round_batch(3) for _ in range(4)]
         outs.append([(t.tolist(), c.tolist()) for t, c in res])
         s.close()
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_temperature_generation_token_identical(gcase, k):
+    """Coupled temperature rounds (temp 0.8, top-p 0.95, seed 1234): the
+    device draft sampling, target distributions, acceptance and residual
+    resampling reproduce the reference's token stream and round record."""
+    import lz98
+    name, d, g, m = gcase
+    s = lz98.State(m, 512, 4)
+    max_new = 40 if name == "tiny" else 48
+    toks, rounds = s.generate(g["prompt"], max_new, k, temp=0.8, topp=0.95, seed=1234)
+    tag = f"gen_t8_k{k}"
+    assert np.array_equal(toks, g[tag + "_tokens"])
+    assert np.array_equal(rounds, g[tag + "_rounds"])
+    s.close()
+
+
+def test_batched_temperature_rounds_match_per_sequence_oracle(gcase):
+    """Three sequences with their own generators in one state: the batched
+    device temperature rounds emit each sequence's oracle stream."""
+    import lz98
+    name, d, g, m = gcase
+    k, B, n_rounds = 3, 3, 5
+    s = lz98.State(m, 256, 4, n_seq=B)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, m.vocab, n).astype(np.int32) for n in (11, 7, 15)]
+    seeds = [1000 + b for b in range(B)]
+    emitted = [[] for _ in range(B)]
+    for b in range(B):
+        s.set_sampler(b, 0.8, 0.95, seeds[b])
+        emitted[b].append(s.seq_prefill(b, prompts[b]))
+    for _ in range(n_rounds):
+        toks, cnt = s.round_batch(k)
+        for b in range(B):
+            emitted[b].extend(toks[b, :cnt[b]].tolist())
+    O = Oracle(d, 256, 4)
+    for b in range(B):
+        n = len(emitted[b])
+        want, _ = O.generate(prompts[b], n + 8, k, temp=0.8, topp=0.95, seed=seeds[b])
+        assert emitted[b] == want[:n].tolist(), f"sequence {b}"
+    O.close()
+    s.close()
+
+
+def test_temperature_round_abi_advances_generator(gcase):
+    """lz_spec_round_temp through the reference-shaped entry point: the
+    generator state it returns continues the oracle's stream."""
+    import lz98
+    name, d, g, m = gcase
+    p = g["prompt"]
+    max_new = 40 if name == "tiny" else 48
+    O = Oracle(d, 512, 4)
+    want, want_rounds = O.generate(p, max_new, 2, temp=0.8, topp=0.95, seed=77)
+    O.close()
+    s = lz98.State(m, 512, 4)
+    toks, rounds = s.generate(p, max_new, 2, temp=0.8, topp=0.95, seed=77)
+    assert np.array_equal(toks, want) and np.array_equal(rounds, want_rounds)
+    s.close()
+
+
+def test_mixed_batch_is_refused(gcase):
+    import lz98
+    name, d, g, m = gcase
+    s = lz98.State(m, 128, 2, n_seq=2)
+    s.set_sampler(0, 0.8, 0.95, 3)
+    s.set_sampler(1, 0.0, 0.95, 3)
+    for b in range(2):
+        s.seq_prefill(b, g["prompt"][:8])
+    with pytest.raises(lz98.LzError):
+        s.round_batch(2)
+    s.close()
