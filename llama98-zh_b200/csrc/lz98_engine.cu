@@ -356,6 +356,10 @@ struct LZRunState {
   float *qbuf = nullptr, *pbuf = nullptr, *sortbuf = nullptr;
   int npow2 = 2;
   int* tok_out = nullptr;
+  // grouped experts: pair indices by expert, tiles, tile count
+  int* glist = nullptr;
+  MoeTile* gtiles = nullptr;
+  int* gntiles = nullptr;
   std::vector<char> seq_temp;        // per sequence: temperature mode
   int n_sm = 148;
   std::map<long, int> gemv_occ;      // resident GEMV blocks per SM by (JM, shared bytes)
@@ -495,6 +499,8 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4);
   s->npow2 = 2;
   while (s->npow2 < c.vocab) s->npow2 <<= 1;
+  ok = ok && dmalloc(s, &s->glist, P) && dmalloc(s, &s->gtiles, P / 16 + std::min((size_t)c.ne, P) + 1) &&
+       dmalloc(s, &s->gntiles, 1);
   ok = ok && dmalloc(s, &s->qbuf, B * s->kmax * (size_t)c.vocab) && dmalloc(s, &s->pbuf, R * (size_t)c.vocab) &&
        dmalloc(s, &s->sortbuf, R * (size_t)s->npow2);
   s->seq_temp.assign(B, 0);
@@ -513,7 +519,12 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
         cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
         cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
         cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess) {
+        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_q8_mma_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(1)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_q8_mma_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(2)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_q8_mma_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(1)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_q8_mma_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(2)) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_q8_mma_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(4)) != cudaSuccess) {
       set_err(errbuf, errlen, "cannot raise the GEMV shared-memory limit");
       lz_state_free(s);
       return LZ98_ERR_CUDA;
@@ -729,7 +740,13 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
     double b = bytes(w) + (w2 ? bytes(*w2) : 0.0) + (double)R * w.out * 4.0 * (mode ? 2.0 : 1.0);
     s->prof_bytes.push_back(b);
   }
-  if (prologue) {
+  const bool rb1 = w.gs == 32;
+  if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
+    // tensor-core warp tiles: 16 token rows x 16 outputs per warp
+    const dim3 grid((w.out + 63) / 64, (R + 15) / 16);
+    if (rb1) launch(s, gemm_q8_warp_kernel<2, true>, grid, dim3(128), 0, a);
+    else launch(s, gemm_q8_warp_kernel<2, false>, grid, dim3(128), 0, a);
+  } else if (prologue) {
     if (nsb <= 32) gemv_launch<1, kGemvProWarps>(s, a, true);
     else gemv_launch<2, kGemvProWarps>(s, a, true);
   } else {
@@ -778,11 +795,34 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
     launch(s, moe_route_kernel, dim3(R), dim3(512), 0, s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
                                            c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats,
                                            m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
-    launch(s, moe_w13_kernel, dim3(c.moe_ffn / 32, R * c.topk), dim3(256), 0, 
-        L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
-    launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, R * c.topk), dim3(256), 0, 
-        L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2,
-        s->row_counter, s->yq, s->ys);
+    const int P = R * c.topk;
+    if (R > kPrologueRows && P <= 2048) {
+      // grouped experts: pairs bucketed by expert into 16-row tiles
+      const int tmax = P / 16 + std::min(c.ne, P) + 1;
+      launch(s, moe_group_kernel, dim3(1), dim3(1024), 0, s->pair_e, P, c.ne, s->glist, s->gtiles, s->gntiles);
+      if (L.w13_gs == 32)
+        launch(s, moe_w13_group_kernel<true>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
+               c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
+               s->hs);
+      else
+        launch(s, moe_w13_group_kernel<false>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
+               c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
+               s->hs);
+      if (L.w2_gs == 32)
+        launch(s, moe_w2_group_kernel<true>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, L.w2q, L.w2s,
+               c.moe_ffn, c.latent, L.w2_gs, s->glist, s->gtiles, s->gntiles, s->hq, s->hs, s->h2);
+      else
+        launch(s, moe_w2_group_kernel<false>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, L.w2q, L.w2s,
+               c.moe_ffn, c.latent, L.w2_gs, s->glist, s->gtiles, s->gntiles, s->hq, s->hs, s->h2);
+      launch(s, moe_combine_kernel, dim3(R), dim3(256), 0, s->pair_e, s->pair_w, c.topk, s->h2, c.latent, s->yq,
+             s->ys);
+    } else {
+      launch(s, moe_w13_kernel, dim3(c.moe_ffn / 32, R * c.topk), dim3(256), 0, 
+          L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
+      launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, R * c.topk), dim3(256), 0, 
+          L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2,
+          s->row_counter, s->yq, s->ys);
+    }
     if (c.shared_w) gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1, &L.sh_down, s->shq, s->shs);
     else gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1);
   }

@@ -334,6 +334,384 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P[warp], P2[warp], n0, lane);
 }
 
+// ------------------------------------------------- tensor-core skinny GEMM
+//
+// For R > 8 token rows the weight-streaming GEMV re-reads every activation
+// row per output row.  This kernel tiles BM tokens x 64 outputs per block and
+// computes every 32-element sub-block dot product with one int8 tensor-core
+// MMA (mma.sync m16n8k32, s8 x s8 -> s32, accumulator input zero): the exact
+// int32 the reference accumulates per 32 (src/ops_matmul.c:336-647).  The
+// reference's float epilogue (src/ops_epi.c:983-1023) then runs per
+// (token, output) in K order in registers, so the kernel is bound by that
+// float work, not by the MMA.  Operands stream through a 3-stage cp.async
+// pipeline in XOR-swizzled shared memory read by ldmatrix.
+
+constexpr int kMmaBN = 64;          // outputs per block (4 warps x 16)
+constexpr int kMmaKc = 128;         // bytes of K per stage (4 sub-blocks)
+constexpr int kMmaStages = 3;
+
+LZ_HD void cp_async16(void* sdst, const void* gsrc, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(sdst);
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gsrc), "r"(sz) : "memory");
+}
+LZ_HD void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+LZ_HD void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+LZ_HD void ldsm_x4(unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3, const void* p) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+
+LZ_HD void mma_s8(int* d, const unsigned* a, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// int32 -> float, exact for |v| < 2^22 (a 32-element int8 dot product is at
+// most 32 * 127 * 127): the 1.5 * 2^23 magic add.
+LZ_HD float i2f_small(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }
+
+// byte offset of 16-byte chunk c of row r in a swizzled 128-byte-row tile
+LZ_HD int swz(int r, int c) { return r * kMmaKc + ((c ^ (r & 7)) << 4); }
+
+// Per-element reduction state of one output element; the order of every
+// float operation is the reference's (see q8_reduce).
+// RB1 (gs = 32): the four interleaved accumulators; otherwise a[0] is the
+// running group dot and a[1] the sum over groups.
+template <bool RB1>
+struct RedState {
+  float a[RB1 ? 4 : 2];
+};
+
+template <int MT, bool RB1>
+struct MmaTile {
+  RedState<RB1> st[MT][2][4];    // [m tile][n tile][fragment element]
+};
+
+template <int MT, bool RB1>
+LZ_HD void mma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
+                    const int8_t* __restrict__ xq, const float* __restrict__ xs, int R, int n0, int r0,
+                    char* smem, MmaTile<MT, RB1>& T) {
+  constexpr int BM = MT * 16;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gid = lane >> 2, tq = lane & 3;
+  const int rb = gs >> 5, ng = K / gs, nsb = K >> 5;
+  // stage layout: A [BM][128] | B [64][128] | xs [BM][4] | wsg [64][4]
+  const int a_bytes = BM * kMmaKc, b_bytes = kMmaBN * kMmaKc;
+  const int st_bytes = a_bytes + b_bytes + BM * 16 + kMmaBN * 16;
+  const int nst = (K + kMmaKc - 1) / kMmaKc;
+  auto load_stage = [&](int st, int buf) {
+    char* base = smem + buf * st_bytes;
+    const int k0 = st * kMmaKc;
+    const int kb = min(kMmaKc, K - k0);           // bytes valid in this stage (multiple of 32)
+    for (int c = tid; c < BM * 8; c += 128) {
+      const int r = c >> 3, ch = c & 7;
+      const bool ok = r0 + r < R && ch * 16 < kb;
+      cp_async16(base + swz(r, ch), ok ? xq + (size_t)(r0 + r) * K + k0 + ch * 16 : xq, ok);
+    }
+    for (int c = tid; c < kMmaBN * 8; c += 128) {
+      const int r = c >> 3, ch = c & 7;
+      const bool ok = n0 + r < N && ch * 16 < kb;
+      cp_async16(base + a_bytes + swz(r, ch), ok ? W + (size_t)(n0 + r) * K + k0 + ch * 16 : W, ok);
+    }
+    // 4 consecutive sub-block scales per token (and per output for gs = 32):
+    // one 16-byte copy when the row of scales is 16-byte aligned and holds
+    // all four, plain loads otherwise (never both on one slot)
+    float* sxs = reinterpret_cast<float*>(base + a_bytes + b_bytes);
+    const int s0 = k0 >> 5;
+    for (int c = tid; c < BM; c += 128) {
+      const bool ok = r0 + c < R;
+      if (ok && (nsb & 3) == 0 && s0 + 4 <= nsb) {
+        cp_async16(sxs + c * 4, xs + (size_t)(r0 + c) * nsb + s0, true);
+      } else {
+        for (int j = 0; j < 4; j++)
+          sxs[c * 4 + j] = ok && s0 + j < nsb ? xs[(size_t)(r0 + c) * nsb + s0 + j] : 0.0f;
+      }
+    }
+    if (RB1) {
+      float* sws = sxs + BM * 4;
+      for (int c = tid; c < kMmaBN; c += 128) {
+        const bool ok = n0 + c < N;
+        if (ok && (ng & 3) == 0 && s0 + 4 <= ng) {
+          cp_async16(sws + c * 4, ws + (size_t)(n0 + c) * ng + s0, true);
+        } else {
+          for (int j = 0; j < 4; j++)
+            sws[c * 4 + j] = ok && s0 + j < ng ? ws[(size_t)(n0 + c) * ng + s0 + j] : 0.0f;
+        }
+      }
+    }
+  };
+#pragma unroll
+  for (int m = 0; m < MT; m++)
+#pragma unroll
+    for (int t = 0; t < 2; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int j = 0; j < (RB1 ? 4 : 2); j++) T.st[m][t][e].a[j] = 0.0f;
+  for (int st = 0; st < kMmaStages - 1; st++) {
+    if (st < nst) load_stage(st, st);
+    cp_async_commit();
+  }
+  // this warp's outputs: n0 + warp*16 + t*8 + tq*2 + (e&1)
+  float wsr[2][2];
+#pragma unroll
+  for (int t = 0; t < 2; t++)
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int o = n0 + warp * 16 + t * 8 + tq * 2 + j;
+      wsr[t][j] = 0.0f;
+      if (!RB1 && ng == 1 && o < N) wsr[t][j] = __ldg(ws + o);
+    }
+  for (int st = 0; st < nst; st++) {
+    cp_async_wait<kMmaStages - 2>();
+    __syncthreads();
+    {
+      const int nx = st + kMmaStages - 1;
+      if (nx < nst) load_stage(nx, nx % kMmaStages);
+      cp_async_commit();
+    }
+    const char* base = smem + (st % kMmaStages) * st_bytes;
+    const float* sxs = reinterpret_cast<const float*>(base + a_bytes + b_bytes);
+    const float* sws = sxs + BM * 4;
+    const int kb = min(kMmaKc, K - st * kMmaKc);
+    for (int g = 0; g < kb / 32; g++) {
+      const int s = st * 4 + g;                  // global sub-block index
+      unsigned bf[4];
+      {
+        // two n8 tiles x two 16-byte halves of the sub-block
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = warp * 16 + (mi >> 1) * 8 + rr, ch = 2 * g + (mi & 1);
+        ldsm_x4(bf[0], bf[1], bf[2], bf[3], base + a_bytes + swz(row, ch));
+      }
+#pragma unroll
+      for (int m = 0; m < MT; m++) {
+        unsigned af[4];
+        {
+          const int mi = lane >> 3, rr = lane & 7;
+          const int row = m * 16 + (mi & 1) * 8 + rr, ch = 2 * g + (mi >> 1);
+          ldsm_x4(af[0], af[1], af[2], af[3], base + swz(row, ch));
+        }
+        const float x0 = sxs[(m * 16 + gid) * 4 + g], x1 = sxs[(m * 16 + gid + 8) * 4 + g];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+          int d[4];
+          mma_s8(d, af, bf[2 * t], bf[2 * t + 1]);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float xsv = e < 2 ? x0 : x1;
+            const float a = i2f_small(d[e]);
+            RedState<RB1>& R_ = T.st[m][t][e];
+            if (!RB1) {
+              R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+              if ((s + 1) % rb == 0) {
+                const int o = n0 + warp * 16 + t * 8 + tq * 2 + (e & 1);
+                const float wg = ng == 1 ? wsr[t][e & 1] : (o < N ? __ldg(ws + (size_t)o * ng + s / rb) : 0.0f);
+                R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg));
+                R_.a[0] = 0.0f;
+              }
+            } else {
+              const float p = __fmul_rn(a, __fmul_rn(xsv, sws[(warp * 16 + t * 8 + tq * 2 + (e & 1)) * 4 + g]));
+              const int slot = s < (nsb & ~3) ? (s & 3) : 0;
+#pragma unroll
+              for (int j = 0; j < (RB1 ? 4 : 2); j++)
+                if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
+            }
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+}
+
+LZ_HD float mma_result(const RedState<false>& r) { return r.a[1]; }
+LZ_HD float mma_result(const RedState<true>& r) {
+  return __fadd_rn(__fadd_rn(r.a[0], r.a[2]), __fadd_rn(r.a[1], r.a[3]));
+}
+
+// y (R x N, ld ldy) = [y +] W x (+ W2 x2), R > 8 rows.  Grid
+// (ceil(N / 64), ceil(R / (16 MT))), 128 threads.
+// Both weights of a dual call must share the group-size class (gs = 32 or
+// gs > 32); the launcher checks.
+template <int MT, bool RB1>
+__global__ void __launch_bounds__(128) gemm_q8_mma_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) char msm[];
+  pdl_trigger();
+  pdl_wait();
+  const int n0 = blockIdx.x * kMmaBN, r0 = blockIdx.y * MT * 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  MmaTile<MT, RB1> T;
+  mma_pass<MT, RB1>(a.W, a.ws, a.N, a.K, a.gs, a.xq, a.xs, a.R, n0, r0, msm, T);
+  float v[MT][2][4];
+#pragma unroll
+  for (int m = 0; m < MT; m++)
+#pragma unroll
+    for (int t = 0; t < 2; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) v[m][t][e] = mma_result(T.st[m][t][e]);
+  if (a.W2) {
+    mma_pass<MT, RB1>(a.W2, a.ws2, a.N, a.K2, a.gs2, a.xq2, a.xs2, a.R, n0, r0, msm, T);
+#pragma unroll
+    for (int m = 0; m < MT; m++)
+#pragma unroll
+      for (int t = 0; t < 2; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[m][t][e] = __fadd_rn(v[m][t][e], mma_result(T.st[m][t][e]));
+  }
+#pragma unroll
+  for (int m = 0; m < MT; m++)
+#pragma unroll
+    for (int t = 0; t < 2; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int r = r0 + m * 16 + gid + (e >= 2 ? 8 : 0);
+        const int o = n0 + warp * 16 + t * 8 + tq * 2 + (e & 1);
+        if (r < a.R && o < a.N) {
+          float* yp = a.y + (size_t)r * a.ldy + o;
+          *yp = a.mode == 1 ? __fadd_rn(*yp, v[m][t][e]) : v[m][t][e];
+        }
+      }
+}
+
+inline size_t gemm_mma_smem(int MT) {
+  const int BM = MT * 16;
+  return (size_t)kMmaStages * (BM * kMmaKc + kMmaBN * kMmaKc + BM * 16 + kMmaBN * 16);
+}
+
+// ------------------------------------------- warp-tile tensor-core skinny GEMM
+//
+// One warp per 16 token rows x 8*NT outputs; no shared memory.  Each lane
+// loads its MMA fragments straight from global memory: for sub-block s,
+// lane (g, q) takes 8 contiguous bytes at s*32 + 8q of token rows g and
+// g+8 (A) and of weight row g of each n tile (B), used as the fragment
+// elements k = 4q..4q+3 and 16+4q..16+4q+3.  A and B share that byte
+// permutation inside the sub-block, so each MMA (accumulator input zero)
+// still yields the exact int32 sum over the 32 bytes.  With K never split
+// across warps, each output's float reduction runs in K order in the
+// lane that holds it.
+// A rows ra (fragment rows g) and rc (rows g+8) of xq; n tile t covers
+// weight rows nb[t] .. nb[t]+7 (clamped to N-1).
+template <int NT, bool RB1>
+LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
+                     const int8_t* __restrict__ xq, const float* __restrict__ xs, int ra, int rc,
+                     const int (&nb)[NT], RedState<RB1> (&st)[NT][4]) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int rb = gs >> 5, ng = K / gs, nsb = K >> 5;
+  const int8_t* pa = xq + (size_t)ra * K + tq * 8;
+  const int8_t* pc = xq + (size_t)rc * K + tq * 8;
+  const float* xa = xs + (size_t)ra * nsb;
+  const float* xc = xs + (size_t)rc * nsb;
+  const int8_t* pb[NT];
+  int oc[NT][2];
+#pragma unroll
+  for (int t = 0; t < NT; t++) {
+    pb[t] = W + (size_t)min(nb[t] + gid, N - 1) * K + tq * 8;
+    oc[t][0] = min(nb[t] + tq * 2, N - 1);
+    oc[t][1] = min(nb[t] + tq * 2 + 1, N - 1);
+  }
+  float wrow[NT][2];
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int j = 0; j < 2; j++) wrow[t][j] = (!RB1 && ng == 1) ? __ldg(ws + oc[t][j]) : 0.0f;
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+#pragma unroll
+      for (int j = 0; j < (RB1 ? 4 : 2); j++) st[t][e].a[j] = 0.0f;
+#pragma unroll 2
+  for (int s = 0; s < nsb; s++) {
+    const int2 A0 = __ldg(reinterpret_cast<const int2*>(pa + s * 32));
+    const int2 A1 = __ldg(reinterpret_cast<const int2*>(pc + s * 32));
+    const unsigned af[4] = {(unsigned)A0.x, (unsigned)A1.x, (unsigned)A0.y, (unsigned)A1.y};
+    const float x0 = __ldg(xa + s), x1 = __ldg(xc + s);
+    const bool gend = !RB1 && (s + 1) % rb == 0;
+    const int slot = s < (nsb & ~3) ? (s & 3) : 0;
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      const int2 B = __ldg(reinterpret_cast<const int2*>(pb[t] + s * 32));
+      int d[4];
+      mma_s8(d, af, (unsigned)B.x, (unsigned)B.y);
+      float wg[2] = {wrow[t][0], wrow[t][1]};
+      if (RB1) {
+        wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s);
+        wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s);
+      } else if (gend && ng > 1) {
+        wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s / rb);
+        wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s / rb);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float a = i2f_small(d[e]);
+        const float xsv = e < 2 ? x0 : x1;
+        RedState<RB1>& R_ = st[t][e];
+        if (!RB1) {
+          R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+          if (gend) {
+            R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[e & 1]));
+            R_.a[0] = 0.0f;
+          }
+        } else {
+          const float p = __fmul_rn(a, __fmul_rn(xsv, wg[e & 1]));
+#pragma unroll
+          for (int j = 0; j < (RB1 ? 4 : 2); j++)
+            if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
+        }
+      }
+    }
+  }
+}
+
+// y (R x N, ld ldy) = [y +] W x (+ W2 x2) for R > 8 rows.  Block = 4 warps
+// along N; grid (ceil(N / (32 NT)), ceil(R / 16)).  Both weights of a dual
+// call share the group-size class (the launcher checks).
+template <int NT, bool RB1>
+__global__ void __launch_bounds__(128) gemm_q8_warp_kernel(const GemvArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int n0 = (blockIdx.x * 4 + warp) * 8 * NT, r0 = blockIdx.y * 16;
+  if (n0 >= a.N) return;
+  RedState<RB1> st[NT][4];
+  int nb[NT];
+#pragma unroll
+  for (int t = 0; t < NT; t++) nb[t] = n0 + t * 8;
+  const int ra = min(r0 + gid, a.R - 1), rc = min(r0 + gid + 8, a.R - 1);
+  wmma_pass<NT, RB1>(a.W, a.ws, a.N, a.K, a.gs, a.xq, a.xs, ra, rc, nb, st);
+  float v[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[t][e] = mma_result(st[t][e]);
+  if (a.W2) {
+    wmma_pass<NT, RB1>(a.W2, a.ws2, a.N, a.K2, a.gs2, a.xq2, a.xs2, ra, rc, nb, st);
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) v[t][e] = __fadd_rn(v[t][e], mma_result(st[t][e]));
+  }
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int r = r0 + gid + (e >= 2 ? 8 : 0);
+      const int o = n0 + t * 8 + tq * 2 + (e & 1);
+      if (r < a.R && o < a.N) {
+        float* yp = a.y + (size_t)r * a.ldy + o;
+        *yp = a.mode == 1 ? __fadd_rn(*yp, v[t][e]) : v[t][e];
+      }
+    }
+}
+
 // --------------------------------------------------------- row kernels
 
 // rmsnorm (1+w) of one row, then per-32 quantisation of the result; the
@@ -863,6 +1241,160 @@ moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int
     yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
   }
   if (threadIdx.x == 0) row_counter[r] = 0;
+}
+
+// ------------------------------------------------ grouped experts (R > 8)
+//
+// With many token rows the (token, expert) pairs are bucketed by expert
+// into tiles of at most 16 pair rows; each tile runs the warp-tile
+// tensor-core GEMM over its expert's weights, so every expert's weights
+// are streamed once per 16 rows instead of once per pair.  The arithmetic
+// per pair is that of moe_w13_kernel / moe_w2_kernel.
+
+struct MoeTile {
+  int e, start, count;
+};
+
+// Buckets the P pairs by expert: list holds pair indices grouped by
+// expert, tiles the (expert, start, count) of every 16-row tile, *ntiles
+// their number.  One block; E <= 256.
+__global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ pair_expert, int P, int E,
+                                                         int* list, MoeTile* tiles, int* ntiles) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int cnt[256], off[256];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  int slot[2] = {-1, -1}, ex[2] = {-1, -1};
+  for (int k = 0; k < 2; k++) {
+    const int p = threadIdx.x + k * blockDim.x;
+    if (p < P) {
+      ex[k] = pair_expert[p];
+      if (ex[k] >= 0) slot[k] = atomicAdd(&cnt[ex[k]], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0, nt = 0;
+    for (int e = 0; e < E; e++) {
+      off[e] = o;
+      for (int i = 0; i < cnt[e]; i += 16) tiles[nt++] = MoeTile{e, o + i, min(16, cnt[e] - i)};
+      o += cnt[e];
+    }
+    *ntiles = nt;
+  }
+  __syncthreads();
+  for (int k = 0; k < 2; k++)
+    if (slot[k] >= 0) list[off[ex[k]] + slot[k]] = threadIdx.x + k * blockDim.x;
+}
+
+// w1/w3 of one tile: each warp 32 FFN outputs (4 n tiles of w1 rows, 4 of
+// w3 rows) for the tile's pair rows, then silu(w1.x) * (w3.x) quantised per
+// 32 into hq / hs of each pair.  Grid (ffn / 128, max tiles), 128 threads.
+template <bool RB1>
+__global__ void __launch_bounds__(128)
+moe_w13_group_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent,
+                     int gs, const int* __restrict__ list, const MoeTile* __restrict__ tiles,
+                     const int* __restrict__ ntiles, int topk, const int8_t* __restrict__ latq,
+                     const float* __restrict__ lats, int8_t* hq, float* hs) {
+  pdl_trigger();
+  pdl_wait();
+  if ((int)blockIdx.y >= *ntiles) return;
+  const MoeTile T = tiles[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int j0 = (blockIdx.x * 4 + warp) * 32;
+  if (j0 >= ffn) return;
+  const int ng = latent / gs;
+  const int pa = list[T.start + min(gid, T.count - 1)], pc = list[T.start + min(gid + 8, T.count - 1)];
+  int nb[8];
+#pragma unroll
+  for (int t = 0; t < 8; t++) nb[t] = t < 4 ? j0 + 8 * t : ffn + j0 + 8 * (t - 4);
+  RedState<RB1> st[8][4];
+  wmma_pass<8, RB1>(w13q + (size_t)T.e * 2 * ffn * latent, w13s + (size_t)T.e * 2 * ffn * ng, 2 * ffn, latent, gs,
+                    latq, lats, pa / topk, pc / topk, nb, st);
+  // rows g (e < 2) and g+8 (e >= 2): 8 values each per lane, 32 per row
+  // across the 4 lanes of the row
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+    float h[8];
+    uint32_t am = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        const int e = half * 2 + c;
+        h[t * 2 + c] = __fmul_rn(silu(mma_result(st[t][e])), mma_result(st[t + 4][e]));
+        const uint32_t b = abs_bits(h[t * 2 + c]);
+        am = am > b ? am : b;
+      }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      const uint32_t w = __shfl_xor_sync(0xffffffffu, am, o);
+      am = am > w ? am : w;
+    }
+    float sg, inv;
+    q8_scale_from_amax(am, &sg, &inv);
+    const int row = gid + half * 8;
+    if (row < T.count) {
+      const int p = half ? pc : pa;
+#pragma unroll
+      for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+          hq[(size_t)p * ffn + j0 + t * 8 + tq * 2 + c] = (int8_t)q8_clamp(q8_round(__fmul_rn(h[t * 2 + c], inv)));
+      if (tq == 0) hs[(size_t)p * (ffn / 32) + j0 / 32] = sg;
+    }
+  }
+}
+
+// w2 of one tile: each warp 16 latent outputs of the tile's pair rows into
+// h2 (pair x latent).  Grid (latent / 64, max tiles), 128 threads.
+template <bool RB1>
+__global__ void __launch_bounds__(128)
+moe_w2_group_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int ffn, int latent, int gs,
+                    const int* __restrict__ list, const MoeTile* __restrict__ tiles,
+                    const int* __restrict__ ntiles, const int8_t* __restrict__ hq, const float* __restrict__ hs,
+                    float* h2) {
+  pdl_trigger();
+  pdl_wait();
+  if ((int)blockIdx.y >= *ntiles) return;
+  const MoeTile T = tiles[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int n0 = (blockIdx.x * 4 + warp) * 16;
+  if (n0 >= latent) return;
+  const int ng = ffn / gs;
+  const int pa = list[T.start + min(gid, T.count - 1)], pc = list[T.start + min(gid + 8, T.count - 1)];
+  int nb[2] = {n0, n0 + 8};
+  RedState<RB1> st[2][4];
+  wmma_pass<2, RB1>(w2q + (size_t)T.e * latent * ffn, w2s + (size_t)T.e * latent * ng, latent, ffn, gs, hq, hs, pa,
+                    pc, nb, st);
+#pragma unroll
+  for (int t = 0; t < 2; t++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int row = gid + (e >= 2 ? 8 : 0);
+      const int o = n0 + t * 8 + tq * 2 + (e & 1);
+      if (row < T.count && o < latent) h2[(size_t)(e >= 2 ? pc : pa) * latent + o] = mma_result(st[t][e]);
+    }
+}
+
+// lat_y of one token row = sum over its selected experts, in selection
+// order, of w * h2 (src/forward_moe.c:198-199), quantised per 32.
+__global__ void moe_combine_kernel(const int* __restrict__ pair_expert, const float* __restrict__ pair_w, int topk,
+                                   const float* __restrict__ h2, int latent, int8_t* yq, float* ys) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
+    const int i = g * 32 + lane;
+    float acc = 0.0f;
+    for (int t = 0; t < topk; t++) {
+      const int pp = r * topk + t;
+      if (pair_expert[pp] < 0) continue;
+      acc = __fadd_rn(acc, __fmul_rn(pair_w[pp], h2[(size_t)pp * latent + i]));
+    }
+    yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
+  }
 }
 
 // ---------------------------------------------------------------- MTP
