@@ -183,6 +183,16 @@ int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
 int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logits,
                       void *stream, char *errbuf, int errlen);
 
+/* Test hook (no counterpart in the reference): the device primitive that
+   computes the sampler's sequential float sums (softmax normaliser,
+   cumulative distributions, top-p mass), run on n host values in one
+   block.  mode 0: the sequential sum; 1: the first index whose cumulative
+   is > target; 2: the first index whose cumulative is >= target.
+   *out_value = the sum, or the cumulative at the hit (the total if none);
+   *out_hit = the index or -1. */
+int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *out_value,
+                     int *out_hit);
+
 /* Stream the library launches on (cudaStream_t, NULL = a private stream). */
 void *lz_state_stream(LZRunState *s);
 /* Kernels this library launched since the state was created. */

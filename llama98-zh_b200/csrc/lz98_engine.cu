@@ -519,12 +519,7 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
         cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
         cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
         cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_q8_mma_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(1)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_q8_mma_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(2)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_q8_mma_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(1)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_q8_mma_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(2)) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_q8_mma_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_mma_smem(4)) != cudaSuccess) {
+        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess) {
       set_err(errbuf, errlen, "cannot raise the GEMV shared-memory limit");
       lz_state_free(s);
       return LZ98_ERR_CUDA;
@@ -1597,5 +1592,31 @@ extern "C" int lz_lm_head_static(const LZModel* m, const float* hidden, int n, f
     set_err(errbuf, errlen, "lz_lm_head_static: kernel launch failed");
     return LZ98_ERR_CUDA;
   }
+  return 0;
+}
+
+// ================================================================ test hooks
+
+extern "C" int lz_debug_seq_sum(const float* vals, int n, int mode, float target, float* out_value, int* out_hit) {
+  if (!vals || n < 0 || mode < 0 || mode > 2 || !out_value || !out_hit) return LZ98_ERR_NULL_ARG;
+  float* dv = nullptr;
+  float* dout = nullptr;
+  if (cudaMalloc(&dv, (size_t)std::max(n, 1) * 4) != cudaSuccess) return LZ98_ERR_ALLOC;
+  if (cudaMalloc(&dout, 8) != cudaSuccess) {
+    cudaFree(dv);
+    return LZ98_ERR_ALLOC;
+  }
+  int rc = 0;
+  float h[2] = {0.0f, 0.0f};
+  if (cudaMemcpy(dv, vals, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  if (!rc) {
+    chain_probe_kernel<<<1, kSampThreads, kSampSmem>>>(dv, n, mode, target, dout);
+    if (cudaMemcpy(h, dout, 8, cudaMemcpyDeviceToHost) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  }
+  cudaFree(dv);
+  cudaFree(dout);
+  if (rc) return rc;
+  *out_value = h[0];
+  memcpy(out_hit, &h[1], 4);
   return 0;
 }

@@ -334,36 +334,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P[warp], P2[warp], n0, lane);
 }
 
-// ------------------------------------------------- tensor-core skinny GEMM
-//
-// For R > 8 token rows the weight-streaming GEMV re-reads every activation
-// row per output row.  This kernel tiles BM tokens x 64 outputs per block and
-// computes every 32-element sub-block dot product with one int8 tensor-core
-// MMA (mma.sync m16n8k32, s8 x s8 -> s32, accumulator input zero): the exact
-// int32 the reference accumulates per 32 (src/ops_matmul.c:336-647).  The
-// reference's float epilogue (src/ops_epi.c:983-1023) then runs per
-// (token, output) in K order in registers, so the kernel is bound by that
-// float work, not by the MMA.  Operands stream through a 3-stage cp.async
-// pipeline in XOR-swizzled shared memory read by ldmatrix.
-
-constexpr int kMmaBN = 64;          // outputs per block (4 warps x 16)
-constexpr int kMmaKc = 128;         // bytes of K per stage (4 sub-blocks)
-constexpr int kMmaStages = 3;
-
-LZ_HD void cp_async16(void* sdst, const void* gsrc, bool valid) {
-  const unsigned sa = (unsigned)__cvta_generic_to_shared(sdst);
-  const int sz = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gsrc), "r"(sz) : "memory");
-}
-LZ_HD void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-LZ_HD void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-LZ_HD void ldsm_x4(unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3, const void* p) {
-  const unsigned a = (unsigned)__cvta_generic_to_shared(p);
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
-}
+// ------------------------------------------------------ tensor-core helpers
 
 LZ_HD void mma_s8(int* d, const unsigned* a, unsigned b0, unsigned b1) {
   asm volatile(
@@ -377,217 +348,29 @@ LZ_HD void mma_s8(int* d, const unsigned* a, unsigned b0, unsigned b1) {
 // most 32 * 127 * 127): the 1.5 * 2^23 magic add.
 LZ_HD float i2f_small(int v) { return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f); }
 
-// byte offset of 16-byte chunk c of row r in a swizzled 128-byte-row tile
-LZ_HD int swz(int r, int c) { return r * kMmaKc + ((c ^ (r & 7)) << 4); }
-
-// Per-element reduction state of one output element; the order of every
-// float operation is the reference's (see q8_reduce).
-// RB1 (gs = 32): the four interleaved accumulators; otherwise a[0] is the
-// running group dot and a[1] the sum over groups.
+// Per-element reduction state of one output element, the order of every
+// float operation the reference's (q8_reduce): RB1 (gs = 32) keeps the four
+// interleaved accumulators; otherwise a[0] is the running group dot and
+// a[1] the sum over groups.
 template <bool RB1>
 struct RedState {
   float a[RB1 ? 4 : 2];
 };
-
-template <int MT, bool RB1>
-struct MmaTile {
-  RedState<RB1> st[MT][2][4];    // [m tile][n tile][fragment element]
-};
-
-template <int MT, bool RB1>
-LZ_HD void mma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
-                    const int8_t* __restrict__ xq, const float* __restrict__ xs, int R, int n0, int r0,
-                    char* smem, MmaTile<MT, RB1>& T) {
-  constexpr int BM = MT * 16;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gid = lane >> 2, tq = lane & 3;
-  const int rb = gs >> 5, ng = K / gs, nsb = K >> 5;
-  // stage layout: A [BM][128] | B [64][128] | xs [BM][4] | wsg [64][4]
-  const int a_bytes = BM * kMmaKc, b_bytes = kMmaBN * kMmaKc;
-  const int st_bytes = a_bytes + b_bytes + BM * 16 + kMmaBN * 16;
-  const int nst = (K + kMmaKc - 1) / kMmaKc;
-  auto load_stage = [&](int st, int buf) {
-    char* base = smem + buf * st_bytes;
-    const int k0 = st * kMmaKc;
-    const int kb = min(kMmaKc, K - k0);           // bytes valid in this stage (multiple of 32)
-    for (int c = tid; c < BM * 8; c += 128) {
-      const int r = c >> 3, ch = c & 7;
-      const bool ok = r0 + r < R && ch * 16 < kb;
-      cp_async16(base + swz(r, ch), ok ? xq + (size_t)(r0 + r) * K + k0 + ch * 16 : xq, ok);
-    }
-    for (int c = tid; c < kMmaBN * 8; c += 128) {
-      const int r = c >> 3, ch = c & 7;
-      const bool ok = n0 + r < N && ch * 16 < kb;
-      cp_async16(base + a_bytes + swz(r, ch), ok ? W + (size_t)(n0 + r) * K + k0 + ch * 16 : W, ok);
-    }
-    // 4 consecutive sub-block scales per token (and per output for gs = 32):
-    // one 16-byte copy when the row of scales is 16-byte aligned and holds
-    // all four, plain loads otherwise (never both on one slot)
-    float* sxs = reinterpret_cast<float*>(base + a_bytes + b_bytes);
-    const int s0 = k0 >> 5;
-    for (int c = tid; c < BM; c += 128) {
-      const bool ok = r0 + c < R;
-      if (ok && (nsb & 3) == 0 && s0 + 4 <= nsb) {
-        cp_async16(sxs + c * 4, xs + (size_t)(r0 + c) * nsb + s0, true);
-      } else {
-        for (int j = 0; j < 4; j++)
-          sxs[c * 4 + j] = ok && s0 + j < nsb ? xs[(size_t)(r0 + c) * nsb + s0 + j] : 0.0f;
-      }
-    }
-    if (RB1) {
-      float* sws = sxs + BM * 4;
-      for (int c = tid; c < kMmaBN; c += 128) {
-        const bool ok = n0 + c < N;
-        if (ok && (ng & 3) == 0 && s0 + 4 <= ng) {
-          cp_async16(sws + c * 4, ws + (size_t)(n0 + c) * ng + s0, true);
-        } else {
-          for (int j = 0; j < 4; j++)
-            sws[c * 4 + j] = ok && s0 + j < ng ? ws[(size_t)(n0 + c) * ng + s0 + j] : 0.0f;
-        }
-      }
-    }
-  };
-#pragma unroll
-  for (int m = 0; m < MT; m++)
-#pragma unroll
-    for (int t = 0; t < 2; t++)
-#pragma unroll
-      for (int e = 0; e < 4; e++)
-#pragma unroll
-        for (int j = 0; j < (RB1 ? 4 : 2); j++) T.st[m][t][e].a[j] = 0.0f;
-  for (int st = 0; st < kMmaStages - 1; st++) {
-    if (st < nst) load_stage(st, st);
-    cp_async_commit();
-  }
-  // this warp's outputs: n0 + warp*16 + t*8 + tq*2 + (e&1)
-  float wsr[2][2];
-#pragma unroll
-  for (int t = 0; t < 2; t++)
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-      const int o = n0 + warp * 16 + t * 8 + tq * 2 + j;
-      wsr[t][j] = 0.0f;
-      if (!RB1 && ng == 1 && o < N) wsr[t][j] = __ldg(ws + o);
-    }
-  for (int st = 0; st < nst; st++) {
-    cp_async_wait<kMmaStages - 2>();
-    __syncthreads();
-    {
-      const int nx = st + kMmaStages - 1;
-      if (nx < nst) load_stage(nx, nx % kMmaStages);
-      cp_async_commit();
-    }
-    const char* base = smem + (st % kMmaStages) * st_bytes;
-    const float* sxs = reinterpret_cast<const float*>(base + a_bytes + b_bytes);
-    const float* sws = sxs + BM * 4;
-    const int kb = min(kMmaKc, K - st * kMmaKc);
-    for (int g = 0; g < kb / 32; g++) {
-      const int s = st * 4 + g;                  // global sub-block index
-      unsigned bf[4];
-      {
-        // two n8 tiles x two 16-byte halves of the sub-block
-        const int mi = lane >> 3, rr = lane & 7;
-        const int row = warp * 16 + (mi >> 1) * 8 + rr, ch = 2 * g + (mi & 1);
-        ldsm_x4(bf[0], bf[1], bf[2], bf[3], base + a_bytes + swz(row, ch));
-      }
-#pragma unroll
-      for (int m = 0; m < MT; m++) {
-        unsigned af[4];
-        {
-          const int mi = lane >> 3, rr = lane & 7;
-          const int row = m * 16 + (mi & 1) * 8 + rr, ch = 2 * g + (mi >> 1);
-          ldsm_x4(af[0], af[1], af[2], af[3], base + swz(row, ch));
-        }
-        const float x0 = sxs[(m * 16 + gid) * 4 + g], x1 = sxs[(m * 16 + gid + 8) * 4 + g];
-#pragma unroll
-        for (int t = 0; t < 2; t++) {
-          int d[4];
-          mma_s8(d, af, bf[2 * t], bf[2 * t + 1]);
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float xsv = e < 2 ? x0 : x1;
-            const float a = i2f_small(d[e]);
-            RedState<RB1>& R_ = T.st[m][t][e];
-            if (!RB1) {
-              R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
-              if ((s + 1) % rb == 0) {
-                const int o = n0 + warp * 16 + t * 8 + tq * 2 + (e & 1);
-                const float wg = ng == 1 ? wsr[t][e & 1] : (o < N ? __ldg(ws + (size_t)o * ng + s / rb) : 0.0f);
-                R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg));
-                R_.a[0] = 0.0f;
-              }
-            } else {
-              const float p = __fmul_rn(a, __fmul_rn(xsv, sws[(warp * 16 + t * 8 + tq * 2 + (e & 1)) * 4 + g]));
-              const int slot = s < (nsb & ~3) ? (s & 3) : 0;
-#pragma unroll
-              for (int j = 0; j < (RB1 ? 4 : 2); j++)
-                if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
-            }
-          }
-        }
-      }
-    }
-  }
-  cp_async_wait<0>();
-  __syncthreads();
-}
 
 LZ_HD float mma_result(const RedState<false>& r) { return r.a[1]; }
 LZ_HD float mma_result(const RedState<true>& r) {
   return __fadd_rn(__fadd_rn(r.a[0], r.a[2]), __fadd_rn(r.a[1], r.a[3]));
 }
 
-// y (R x N, ld ldy) = [y +] W x (+ W2 x2), R > 8 rows.  Grid
-// (ceil(N / 64), ceil(R / (16 MT))), 128 threads.
-// Both weights of a dual call must share the group-size class (gs = 32 or
-// gs > 32); the launcher checks.
-template <int MT, bool RB1>
-__global__ void __launch_bounds__(128) gemm_q8_mma_kernel(const GemvArgs a) {
-  extern __shared__ __align__(128) char msm[];
-  pdl_trigger();
-  pdl_wait();
-  const int n0 = blockIdx.x * kMmaBN, r0 = blockIdx.y * MT * 16;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
-  MmaTile<MT, RB1> T;
-  mma_pass<MT, RB1>(a.W, a.ws, a.N, a.K, a.gs, a.xq, a.xs, a.R, n0, r0, msm, T);
-  float v[MT][2][4];
-#pragma unroll
-  for (int m = 0; m < MT; m++)
-#pragma unroll
-    for (int t = 0; t < 2; t++)
-#pragma unroll
-      for (int e = 0; e < 4; e++) v[m][t][e] = mma_result(T.st[m][t][e]);
-  if (a.W2) {
-    mma_pass<MT, RB1>(a.W2, a.ws2, a.N, a.K2, a.gs2, a.xq2, a.xs2, a.R, n0, r0, msm, T);
-#pragma unroll
-    for (int m = 0; m < MT; m++)
-#pragma unroll
-      for (int t = 0; t < 2; t++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) v[m][t][e] = __fadd_rn(v[m][t][e], mma_result(T.st[m][t][e]));
-  }
-#pragma unroll
-  for (int m = 0; m < MT; m++)
-#pragma unroll
-    for (int t = 0; t < 2; t++)
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int r = r0 + m * 16 + gid + (e >= 2 ? 8 : 0);
-        const int o = n0 + warp * 16 + t * 8 + tq * 2 + (e & 1);
-        if (r < a.R && o < a.N) {
-          float* yp = a.y + (size_t)r * a.ldy + o;
-          *yp = a.mode == 1 ? __fadd_rn(*yp, v[m][t][e]) : v[m][t][e];
-        }
-      }
-}
-
-inline size_t gemm_mma_smem(int MT) {
-  const int BM = MT * 16;
-  return (size_t)kMmaStages * (BM * kMmaKc + kMmaBN * kMmaKc + BM * 16 + kMmaBN * 16);
-}
-
 // ------------------------------------------- warp-tile tensor-core skinny GEMM
 //
+// For R > 8 token rows the weight-streaming GEMV would re-read every
+// activation row per output row.  Here each 32-element sub-block dot
+// product is one int8 tensor-core MMA (mma.sync m16n8k32, s8 x s8 -> s32,
+// accumulator input zero): the exact int32 the reference accumulates per 32
+// (src/ops_matmul.c:336-647); the reference's float epilogue
+// (src/ops_epi.c:983-1023) then runs per (token, output) in K order in
+// registers, so the kernel is bound by that float work, not by the MMA.
 // One warp per 16 token rows x 8*NT outputs; no shared memory.  Each lane
 // loads its MMA fragments straight from global memory: for sub-block s,
 // lane (g, q) takes 8 contiguous bytes at s*32 + 8q of token rows g and

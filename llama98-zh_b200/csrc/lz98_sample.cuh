@@ -6,12 +6,9 @@
 // sequential index-order sums and cumulative sums (src/ops_norm.c:903-985,
 // src/sampler.c:526-745, src/generate.c:264-349).
 //
-// The sequential sums are the critical path.  They run on one thread of a
-// 1024-thread block while the other 31 warps compute the next values into
-// shared memory, and the thread writes the running sum back in place so the
-// block can find the first position whose cumulative passes a threshold in
-// parallel (a cumulative sum of non-negative values is non-decreasing, so
-// "threshold reached" is monotone along the array).
+// The sequential sums are the critical path.  block_chain computes them
+// exactly but in parallel (binade segments with integer ulp prefix sums),
+// see its comment.
 #pragma once
 #include <climits>
 #include "lz98_kernels.cuh"
@@ -20,14 +17,13 @@ namespace lz98 {
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampWarps = kSampThreads / 32;
-constexpr int kChainStage = 2048;      // values per staged chunk
 constexpr int kSortChunk = 8192;       // bitonic stages below this run in shared memory
 constexpr float kTempFloor = 1e-3f;    // LZ_TEMP_FLOOR, src/sampler.h:130
 
 // Dynamic shared memory of every sampling kernel (the chain's three stage
 // buffers and the sort chunk share it).
 constexpr size_t kSampSmem = (size_t)kSortChunk * sizeof(float);
-static_assert(3 * kChainStage <= kSortChunk, "stage buffers must fit the sort chunk");
+static_assert(1024 <= kSortChunk, "the chain's head must fit the stage");
 
 struct SampShared {
   float red_f[kSampWarps];
@@ -91,67 +87,221 @@ LZ_HD int block_max_i(int v, SampShared& sh) {
 
 enum ChainMode { kChainSum = 0, kChainFindLt = 1, kChainFindGe = 2 };
 
-// Sequential float sum acc = ((0 + v(0)) + v(1)) + ... over j < n (values
-// must be >= 0 for the find modes).  kChainSum returns the total.  The find
-// modes stop at the first j whose cumulative c satisfies target < c
-// (kChainFindLt) or c >= target (kChainFindGe): *hit = j and the return
-// value is c; with no such j, *hit = -1 and the total is returned.
-// Called by every thread of the block; `stage` holds 3 * kChainStage floats.
+// ---------------------------------------------------------------------------
+// Exact sequential float sums, computed in parallel.
+//
+// acc_j = fl(acc_{j-1} + v_j) (round to nearest even, v_j >= 0 finite).
+// While the running sum s stays in one binade its grid is u = ulp(s), and
+// fl(s + v) = s + u * rne(v / u): the rounding of each addend does not
+// depend on s, except at an exact tie (v / u ending in .5, where the even
+// rule looks at s).  So inside a segment the running sum is s/u plus an
+// integer prefix sum of per-addend ulp counts.  A segment ends at the first
+// addend that ties or whose rounded prefix reaches the next binade (2^24
+// ulps); that addend is added with a real fadd and a new segment starts
+// from the exact result.  Every cumulative equals the sequential one bit
+// for bit (zeros keep s at 0; the first non-zero addend after them is
+// taken exactly).
+//
+// Values are decomposed as v = M * 2^(E - 150) with E = max(biased
+// exponent, 1), which covers subnormals with the same formulas.
+
+LZ_HD void fdecomp(float x, int& E, uint32_t& M) {
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t e = b >> 23;
+  M = (b & 0x7FFFFFu) | (e ? 0x800000u : 0u);
+  E = e ? (int)e : 1;
+}
+
+// s = m * 2^(E - 150) for m < 2^24 (m < 2^23 only when E == 1)
+LZ_HD float frecon(int E, unsigned long long m) {
+  return m >= 0x800000ull ? __uint_as_float(((uint32_t)E << 23) | ((uint32_t)m & 0x7FFFFFu))
+                          : __uint_as_float((uint32_t)m);
+}
+
+// ulps of v = Mj * 2^(Ej - 150) on the grid of exponent Es, rounded to
+// nearest; tie flags an exact half.
+LZ_HD unsigned long long fulps(int Ej, uint32_t Mj, int Es, bool& tie) {
+  tie = false;
+  if (Mj == 0u) return 0ull;
+  const int sh = Ej - Es;
+  if (sh >= 0) return sh >= 7 ? (1ull << 30) : (unsigned long long)(Mj << sh);
+  const int r = -sh;
+  if (r >= 25) return 0ull;
+  const uint32_t q = Mj >> r, rem = Mj & ((1u << r) - 1u), half = 1u << (r - 1);
+  tie = rem == half;
+  return q + (rem > half ? 1u : 0u);
+}
+
+template <int MODE>
+LZ_HD bool chain_cond(float c, float target) {
+  return MODE == kChainFindLt ? (target < c) : (MODE == kChainFindGe ? (c >= target) : false);
+}
+
+constexpr int kChainHead = 1024;      // leading values summed serially
+constexpr int kChainPer = 8;          // values per thread per window
+constexpr int kChainWin = kChainPer * kSampThreads;
+
+struct ChainShared {
+  unsigned long long wt[kSampWarps];  // warp totals, then exclusive offsets
+  int wstop[kSampWarps], wfind[kSampWarps];
+  int S, F;
+  float sum;
+  int hit;
+};
+
+LZ_HD unsigned long long warp_incl_scan_u64(unsigned long long v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long w = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += w;
+  }
+  return v;
+}
+
+// Block-wide minima of two ints (warp 0 finishes; two barriers).
+LZ_HD void block_min2(int a, int b, ChainShared& cs, int& A, int& B) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = __reduce_min_sync(0xffffffffu, a);
+  b = __reduce_min_sync(0xffffffffu, b);
+  if (lane == 0) { cs.wstop[warp] = a; cs.wfind[warp] = b; }
+  __syncthreads();
+  if (warp == 0) {
+    const int x = __reduce_min_sync(0xffffffffu, cs.wstop[lane]);
+    const int y = __reduce_min_sync(0xffffffffu, cs.wfind[lane]);
+    if (lane == 0) { cs.S = x; cs.F = y; }
+  }
+  __syncthreads();
+  A = cs.S;
+  B = cs.F;
+}
+
+// Sum (kChainSum) or first cumulative meeting the target (find modes) of
+// v(0..n-1) in sequential float order.  The find modes stop at the first j
+// whose cumulative c satisfies target < c (kChainFindLt) or c >= target
+// (kChainFindGe): *hit = j and c is returned; with no such j, *hit = -1 and
+// the total is returned.  Every thread of the block calls it; `stage` holds
+// kChainHead floats.
 template <int MODE, class F>
 __device__ float block_chain(F val, int n, float target, float* stage, SampShared& sh, int* hit) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int nch = (n + kChainStage - 1) / kChainStage;
-  for (int t = tid; t < min(kChainStage, n); t += kSampThreads) stage[t] = val(t);
-  if (tid == 0) { sh.hit = -1; sh.acc = 0.0f; }
+  __shared__ ChainShared cs;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // serial head: crossings are dense while the sum is small
+  const int nh = min(n, kChainHead);
+  for (int t = tid; t < nh; t += kSampThreads) stage[t] = val(t);
   __syncthreads();
-  float acc = 0.0f;
-  int found = -1;
-  for (int c = 0; c <= nch && found < 0; c++) {
-    if (tid == 0 && c < nch) {
-      float* b = stage + (c % 3) * kChainStage;
-      const int len = min(kChainStage, n - c * kChainStage);
-      int t = 0;
-      for (; t + 4 <= len; t += 4) {
-        float4 v4 = *reinterpret_cast<float4*>(b + t);
-        v4.x = acc = __fadd_rn(acc, v4.x);
-        v4.y = acc = __fadd_rn(acc, v4.y);
-        v4.z = acc = __fadd_rn(acc, v4.z);
-        v4.w = acc = __fadd_rn(acc, v4.w);
-        if (MODE != kChainSum) *reinterpret_cast<float4*>(b + t) = v4;
-      }
-      for (; t < len; t++) {
-        acc = __fadd_rn(acc, b[t]);
-        if (MODE != kChainSum) b[t] = acc;
-      }
-    } else if (warp > 0) {
-      // the previous chunk's cumulatives: first position meeting the target
-      if (MODE != kChainSum && c >= 1) {
-        const float* b = stage + ((c - 1) % 3) * kChainStage;
-        const int base = (c - 1) * kChainStage, len = min(kChainStage, n - base);
-        for (int t = tid - 32; t < len; t += kSampThreads - 32) {
-          const float cu = b[t];
-          const bool ok = MODE == kChainFindLt ? (target < cu) : (cu >= target);
-          const bool prev = t > 0 && (MODE == kChainFindLt ? (target < b[t - 1]) : (b[t - 1] >= target));
-          if (ok && !prev) { sh.hit = base + t; sh.acc = cu; }
-        }
-      }
-      if (c + 1 < nch) {
-        float* b = stage + ((c + 1) % 3) * kChainStage;
-        const int base = (c + 1) * kChainStage, len = min(kChainStage, n - base);
-        for (int t = tid - 32; t < len; t += kSampThreads - 32) b[t] = val(base + t);
-      }
+  if (tid == 0) {
+    float acc = 0.0f;
+    int h = -1;
+    for (int t = 0; t < nh; t++) {
+      acc = __fadd_rn(acc, stage[t]);
+      if (MODE != kChainSum && chain_cond<MODE>(acc, target)) { h = t; break; }
     }
-    __syncthreads();
-    found = sh.hit;
+    cs.sum = acc;
+    cs.hit = h;
   }
-  if (found < 0) {
-    if (tid == 0) sh.acc = acc;
-    __syncthreads();
-  }
-  const float r = sh.acc;
-  if (hit) *hit = found;
   __syncthreads();
-  return r;
+  float s = cs.sum;
+  int found = cs.hit;
+  for (int w0 = nh; w0 < n && found < 0; w0 += kChainWin) {
+    const int j0 = w0 + tid * kChainPer;
+    const int wend = min(n, w0 + kChainWin);
+    float v[kChainPer];
+    int ve[kChainPer];
+    uint32_t vm[kChainPer];
+#pragma unroll
+    for (int k = 0; k < kChainPer; k++) {
+      v[k] = j0 + k < wend ? val(j0 + k) : 0.0f;
+      fdecomp(v[k], ve[k], vm[k]);
+    }
+    int cur = w0;                      // first index of the open segment
+    while (cur < wend && found < 0) {
+      if (s == 0.0f) {
+        // the sum stays 0 up to the first non-zero value, taken exactly
+        if (MODE != kChainSum && chain_cond<MODE>(0.0f, target)) { found = cur; break; }
+        int fz = INT_MAX;
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++)
+          if (j0 + k >= cur && j0 + k < wend && v[k] > 0.0f) fz = min(fz, j0 + k);
+        int z, unused;
+        block_min2(fz, INT_MAX, cs, z, unused);
+        if (z == INT_MAX) { cur = wend; break; }
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++)
+          if (j0 + k == z) cs.sum = v[k];
+        __syncthreads();
+        s = cs.sum;
+        __syncthreads();
+        if (MODE != kChainSum && chain_cond<MODE>(s, target)) { found = z; break; }
+        cur = z + 1;
+        continue;
+      }
+      int Es;
+      uint32_t Ms;
+      fdecomp(s, Es, Ms);
+      unsigned long long pre[kChainPer], nu[kChainPer];
+      bool tie[kChainPer];
+      unsigned long long run = 0ull;
+#pragma unroll
+      for (int k = 0; k < kChainPer; k++) {
+        const bool live = j0 + k >= cur && j0 + k < wend;
+        nu[k] = live ? fulps(ve[k], vm[k], Es, tie[k]) : 0ull;
+        tie[k] = live && tie[k];
+        run += nu[k];
+        pre[k] = run;
+      }
+      // block exclusive scan of the thread totals (warp 0 scans the warps)
+      const unsigned long long incl = warp_incl_scan_u64(run);
+      if (lane == 31) cs.wt[warp] = incl;
+      __syncthreads();
+      if (warp == 0) {
+        const unsigned long long t = cs.wt[lane];
+        cs.wt[lane] = warp_incl_scan_u64(t) - t;
+      }
+      __syncthreads();
+      const unsigned long long off = Ms + cs.wt[warp] + incl - run;
+      // first stop and first hit of this segment
+      int st = INT_MAX, fd = INT_MAX;
+#pragma unroll
+      for (int k = 0; k < kChainPer; k++) {
+        const int j = j0 + k;
+        if (j < cur || j >= wend || st != INT_MAX) continue;
+        const unsigned long long m = off + pre[k];
+        if (tie[k] || m >= 0x1000000ull) st = j;
+        else if (MODE != kChainSum && fd == INT_MAX && chain_cond<MODE>(frecon(Es, m), target)) fd = j;
+      }
+      int S, Fd;
+      block_min2(st, fd, cs, S, Fd);
+      int next;
+      if (Fd < S) {
+        // a cumulative inside the segment meets the target
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++)
+          if (j0 + k == Fd) cs.sum = frecon(Es, off + pre[k]);
+        found = Fd;
+        next = wend;
+      } else if (S == INT_MAX) {
+        // no stop: the segment runs to the window's end
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++)
+          if (j0 + k == wend - 1) cs.sum = frecon(Es, off + pre[k]);
+        next = wend;
+      } else {
+        // the stopping addend, by a real add from the exact cumulative before it
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++)
+          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, off + pre[k] - nu[k]), v[k]);
+        next = S + 1;
+      }
+      __syncthreads();
+      s = cs.sum;
+      __syncthreads();
+      if (found < 0 && S != INT_MAX && Fd >= S && MODE != kChainSum && chain_cond<MODE>(s, target)) found = S;
+      cur = next;
+    }
+  }
+  if (hit) *hit = found;
+  return s;
 }
 
 // Numerically the reference softmax of logits * inv_t (src/ops_norm.c:903-985
@@ -528,6 +678,25 @@ __global__ void __launch_bounds__(kSampThreads) sample_row_kernel(const float* _
   SeqRound& s = sr[seq];
   const int tok = block_sample_ex(logits, V, s.temp, s.topp, &s.rng, p, sorted, npow2, stage, sh);
   if (threadIdx.x == 0) *out = tok;
+}
+
+// Test hook: block_chain over n values in global memory (mode 0 sum, 1 first
+// cumulative > target, 2 first cumulative >= target); out[0] = result,
+// out[1] = hit index as float bits.
+__global__ void __launch_bounds__(kSampThreads) chain_probe_kernel(const float* __restrict__ v, int n, int mode,
+                                                                   float target, float* out) {
+  extern __shared__ __align__(16) float stage[];
+  __shared__ SampShared sh;
+  auto f = [&](int j) { return v[j]; };
+  int hit = -1;
+  float r;
+  if (mode == 0) r = block_chain<kChainSum>(f, n, target, stage, sh, &hit);
+  else if (mode == 1) r = block_chain<kChainFindLt>(f, n, target, stage, sh, &hit);
+  else r = block_chain<kChainFindGe>(f, n, target, stage, sh, &hit);
+  if (threadIdx.x == 0) {
+    out[0] = r;
+    out[1] = __int_as_float(hit);
+  }
 }
 
 }  // namespace lz98

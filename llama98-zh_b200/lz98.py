@@ -78,6 +78,7 @@ def lib():
                                      P(ctypes.c_double), P(c_int)]),
         "lz_lm_head_static": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_state_stream": (c_void_p, [c_void_p]),
+        "lz_debug_seq_sum": (c_int, [c_void_p, c_int, c_int, c_float, P(c_float), P(c_int)]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
     }
     for name, (res, args) in sig.items():
@@ -95,7 +96,7 @@ EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_s
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
            "lz_seq_prefill", "lz_seq_set_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
-           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static"]
+           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static", "lz_debug_seq_sum"]
 
 
 class LZSampler(ctypes.Structure):
@@ -281,6 +282,16 @@ class State:
         if rc:
             raise LzError(f"generate failed ({rc}): {err.value.decode()}")
         return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()
+
+
+def debug_seq_sum(vals, mode=0, target=0.0):
+    """The device's sequential-sum primitive on host values: (value, hit)."""
+    v = np.ascontiguousarray(vals, np.float32)
+    out, hit = c_float(), c_int()
+    rc = lib().lz_debug_seq_sum(_ptr(v), len(v), int(mode), float(target), ctypes.byref(out), ctypes.byref(hit))
+    if rc:
+        raise LzError(f"debug_seq_sum failed ({rc})")
+    return out.value, hit.value
 
 
 def spec_accept(draft, targ, bonus):

@@ -1,0 +1,58 @@
+"""The device primitive behind every sequential float sum of the sampler
+(softmax normaliser, cumulative distributions, top-p mass): it runs the
+sum in parallel by binade segments and must equal the sequential
+float32 cumulatives bit for bit, including exact ties, zeros, subnormals
+and large jumps, and find the same first index against a threshold."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _seq(v):
+    out = np.empty(len(v), np.float32)
+    s = np.float32(0)
+    for j, x in enumerate(v):
+        s = np.float32(s + x)
+        out[j] = s
+    return out
+
+
+def families(rng):
+    for n in (1, 7, 1000, 1024, 1025, 5000, 8193, 9217, 20000, 64000, 70001):
+        yield f"uniform{n}", rng.random(n).astype(np.float32)
+    n = 64000
+    yield "softmax-like", np.exp(rng.normal(0, 1, n) - 4).astype(np.float32)
+    yield "probabilities", (rng.random(n) / (n / 2)).astype(np.float32)
+    yield "few-bit ties", (rng.integers(0, 16, n) * 2.0 ** rng.integers(-30, 3, n)).astype(np.float32)
+    sub = (rng.integers(0, 1 << 20, n) * 2.0 ** -149).astype(np.float32)
+    sub[rng.random(n) < 0.3] = 0
+    yield "subnormal+zeros", sub
+    z = rng.random(n).astype(np.float32)
+    z[rng.random(n) < 0.5] = 0
+    z[rng.random(n) < 0.01] = 1e6
+    yield "zeros+jumps", z
+    lead = np.zeros(n, np.float32)
+    lead[3000:] = rng.random(n - 3000)
+    yield "leading zeros", lead
+    yield "all zeros", np.zeros(5000, np.float32)
+    yield "sorted desc", np.sort(rng.random(n).astype(np.float32) / 1000)[::-1].copy()
+
+
+def test_sum_and_find_bit_exact():
+    import lz98
+    rng = np.random.default_rng(3)
+    for name, v in families(rng):
+        c = _seq(v)
+        tot, hit = lz98.debug_seq_sum(v, 0)
+        assert np.float32(tot).view(np.uint32) == c[-1].view(np.uint32), name
+        assert hit == -1
+        for frac in (0.0, 0.3, 0.999, 1.5):
+            target = np.float32(c[-1] * frac)
+            for mode, cond in ((1, target < c), (2, c >= target)):
+                idx = np.nonzero(cond)[0]
+                val, hit = lz98.debug_seq_sum(v, mode, float(target))
+                want = int(idx[0]) if len(idx) else -1
+                assert hit == want, (name, frac, mode, hit, want)
+                want_val = c[want] if want >= 0 else c[-1]
+                assert np.float32(val).view(np.uint32) == want_val.view(np.uint32), (name, frac, mode)
