@@ -23,8 +23,11 @@ LZ_HD float rsqrt_body(float x) {
   return y;
 }
 
-// 2^(i/32), the reference's own table (src/ops_quant.c:244-253).
-__constant__ float kExpTab32[32] = {
+// 2^(i/32), the reference's own table (src/ops_quant.c:244-253).  Kept in
+// global memory and read through the read-only cache: the 32 entries share
+// one 128-byte line, so a warp's divergent lookups are one access (constant
+// memory would serialise them).
+__device__ const float kExpTab32[32] = {
     1.000000000f, 1.021897149f, 1.044273782f, 1.067140401f,
     1.090507733f, 1.114386743f, 1.138788635f, 1.163724859f,
     1.189207115f, 1.215247360f, 1.241857812f, 1.269050957f,
@@ -50,7 +53,7 @@ LZ_HD float exp_body(float x) {
   float w = __fadd_rn(1.0f, __fmul_rn(r, 0.03125f));
   float p2n = __int_as_float((n + 127) << 23);
   float c = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(0.242844437f, w), 0.207425515f), w), 0.549730133f);
-  return __fmul_rn(p2n, __fmul_rn(kExpTab32[idx], c));
+  return __fmul_rn(p2n, __fmul_rn(__ldg(kExpTab32 + idx), c));
 }
 
 // src/ops_quant.c:1836-1842 (float arm).

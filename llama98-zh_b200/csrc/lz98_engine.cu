@@ -502,7 +502,7 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
   ok = ok && dmalloc(s, &s->glist, P) && dmalloc(s, &s->gtiles, P / 16 + std::min((size_t)c.ne, P) + 1) &&
        dmalloc(s, &s->gntiles, 1);
   ok = ok && dmalloc(s, &s->qbuf, B * s->kmax * (size_t)c.vocab) && dmalloc(s, &s->pbuf, R * (size_t)c.vocab) &&
-       dmalloc(s, &s->sortbuf, R * (size_t)s->npow2);
+       dmalloc(s, &s->sortbuf, R * 2 * (size_t)s->npow2);
   s->seq_temp.assign(B, 0);
   if (!ok) {
     set_err(errbuf, errlen, "device allocation failed");
@@ -737,10 +737,17 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
   }
   const bool rb1 = w.gs == 32;
   if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
-    // tensor-core warp tiles: 16 token rows x 16 outputs per warp
-    const dim3 grid((w.out + 63) / 64, (R + 15) / 16);
-    if (rb1) launch(s, gemm_q8_warp_kernel<2, true>, grid, dim3(128), 0, a);
-    else launch(s, gemm_q8_warp_kernel<2, false>, grid, dim3(128), 0, a);
+    // tensor-core warp tiles: 16 token rows x 8 NT outputs per warp (NT = 1
+    // for narrow outputs, so enough warps are resident to hide latency)
+    const int NT = w.out <= 2048 ? 1 : 2;
+    const dim3 grid((w.out + 32 * NT - 1) / (32 * NT), (R + 15) / 16);
+    if (NT == 1) {
+      if (rb1) launch(s, gemm_q8_warp_kernel<1, true>, grid, dim3(128), 0, a);
+      else launch(s, gemm_q8_warp_kernel<1, false>, grid, dim3(128), 0, a);
+    } else {
+      if (rb1) launch(s, gemm_q8_warp_kernel<2, true>, grid, dim3(128), 0, a);
+      else launch(s, gemm_q8_warp_kernel<2, false>, grid, dim3(128), 0, a);
+    }
   } else if (prologue) {
     if (nsb <= 32) gemv_launch<1, kGemvProWarps>(s, a, true);
     else gemv_launch<2, kGemvProWarps>(s, a, true);

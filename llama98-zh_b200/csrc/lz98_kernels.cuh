@@ -411,46 +411,73 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
     for (int e = 0; e < 4; e++)
 #pragma unroll
       for (int j = 0; j < (RB1 ? 4 : 2); j++) st[t][e].a[j] = 0.0f;
-#pragma unroll 2
-  for (int s = 0; s < nsb; s++) {
-    const int2 A0 = __ldg(reinterpret_cast<const int2*>(pa + s * 32));
-    const int2 A1 = __ldg(reinterpret_cast<const int2*>(pc + s * 32));
-    const unsigned af[4] = {(unsigned)A0.x, (unsigned)A1.x, (unsigned)A0.y, (unsigned)A1.y};
-    const float x0 = __ldg(xa + s), x1 = __ldg(xc + s);
-    const bool gend = !RB1 && (s + 1) % rb == 0;
-    const int slot = s < (nsb & ~3) ? (s & 3) : 0;
+  // fragments of U sub-blocks are loaded while the previous U compute
+  constexpr int U = NT >= 8 ? 1 : 4;
+  struct Frag {
+    int2 A0, A1, B[NT];
+    float x0, x1;
+  };
+  Frag cur[U], nxt[U];
+  auto load = [&](Frag (&f)[U], int sb) {
 #pragma unroll
-    for (int t = 0; t < NT; t++) {
-      const int2 B = __ldg(reinterpret_cast<const int2*>(pb[t] + s * 32));
-      int d[4];
-      mma_s8(d, af, (unsigned)B.x, (unsigned)B.y);
-      float wg[2] = {wrow[t][0], wrow[t][1]};
-      if (RB1) {
-        wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s);
-        wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s);
-      } else if (gend && ng > 1) {
-        wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s / rb);
-        wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s / rb);
+    for (int u = 0; u < U; u++) {
+      const int s = sb + u;
+      if (s < nsb) {
+        f[u].A0 = __ldg(reinterpret_cast<const int2*>(pa + s * 32));
+        f[u].A1 = __ldg(reinterpret_cast<const int2*>(pc + s * 32));
+#pragma unroll
+        for (int t = 0; t < NT; t++) f[u].B[t] = __ldg(reinterpret_cast<const int2*>(pb[t] + s * 32));
+        f[u].x0 = __ldg(xa + s);
+        f[u].x1 = __ldg(xc + s);
       }
+    }
+  };
+  load(cur, 0);
+  for (int sb = 0; sb < nsb; sb += U) {
+    if (sb + U < nsb) load(nxt, sb + U);
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float a = i2f_small(d[e]);
-        const float xsv = e < 2 ? x0 : x1;
-        RedState<RB1>& R_ = st[t][e];
-        if (!RB1) {
-          R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
-          if (gend) {
-            R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[e & 1]));
-            R_.a[0] = 0.0f;
+    for (int u = 0; u < U; u++) {
+      const int s = sb + u;
+      if (s >= nsb) break;
+      const unsigned af[4] = {(unsigned)cur[u].A0.x, (unsigned)cur[u].A1.x, (unsigned)cur[u].A0.y,
+                              (unsigned)cur[u].A1.y};
+      const float x0 = cur[u].x0, x1 = cur[u].x1;
+      const bool gend = !RB1 && (s + 1) % rb == 0;
+      const int slot = s < (nsb & ~3) ? (s & 3) : 0;
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+        int d[4];
+        mma_s8(d, af, (unsigned)cur[u].B[t].x, (unsigned)cur[u].B[t].y);
+        float wg[2] = {wrow[t][0], wrow[t][1]};
+        if (RB1) {
+          wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s);
+          wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s);
+        } else if (gend && ng > 1) {
+          wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s / rb);
+          wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s / rb);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float a = i2f_small(d[e]);
+          const float xsv = e < 2 ? x0 : x1;
+          RedState<RB1>& R_ = st[t][e];
+          if (!RB1) {
+            R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+            if (gend) {
+              R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[e & 1]));
+              R_.a[0] = 0.0f;
+            }
+          } else {
+            const float p = __fmul_rn(a, __fmul_rn(xsv, wg[e & 1]));
+#pragma unroll
+            for (int j = 0; j < (RB1 ? 4 : 2); j++)
+              if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
           }
-        } else {
-          const float p = __fmul_rn(a, __fmul_rn(xsv, wg[e & 1]));
-#pragma unroll
-          for (int j = 0; j < (RB1 ? 4 : 2); j++)
-            if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
         }
       }
     }
+#pragma unroll
+    for (int u = 0; u < U; u++) cur[u] = nxt[u];
   }
 }
 

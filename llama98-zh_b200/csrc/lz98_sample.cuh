@@ -17,7 +17,7 @@ namespace lz98 {
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampWarps = kSampThreads / 32;
-constexpr int kSortChunk = 8192;       // bitonic stages below this run in shared memory
+constexpr int kSortChunk = 8192;       // floats of dynamic shared memory (radix histograms)
 constexpr float kTempFloor = 1e-3f;    // LZ_TEMP_FLOOR, src/sampler.h:130
 
 // Dynamic shared memory of every sampling kernel (the chain's three stage
@@ -118,18 +118,44 @@ LZ_HD float frecon(int E, unsigned long long m) {
                           : __uint_as_float((uint32_t)m);
 }
 
+// Prefix sums of ulp counts saturate at 2^25: everything at or above 2^24
+// ends the segment anyway, and saturating addition of non-negative
+// numbers is associative, so the scans stay exact where they are used.
+constexpr uint32_t kUlpSat = 1u << 25;
+LZ_HD uint32_t sadd(uint32_t a, uint32_t b) { return min(a + b, kUlpSat); }
+
 // ulps of v = Mj * 2^(Ej - 150) on the grid of exponent Es, rounded to
-// nearest; tie flags an exact half.
-LZ_HD unsigned long long fulps(int Ej, uint32_t Mj, int Es, bool& tie) {
+// nearest (saturated); tie flags an exact half.
+LZ_HD uint32_t fulps(int Ej, uint32_t Mj, int Es, bool& tie) {
   tie = false;
-  if (Mj == 0u) return 0ull;
+  if (Mj == 0u) return 0u;
   const int sh = Ej - Es;
-  if (sh >= 0) return sh >= 7 ? (1ull << 30) : (unsigned long long)(Mj << sh);
+  if (sh >= 0) return sh >= 2 ? kUlpSat : min(Mj << sh, kUlpSat);
   const int r = -sh;
-  if (r >= 25) return 0ull;
+  if (r >= 25) return 0u;
   const uint32_t q = Mj >> r, rem = Mj & ((1u << r) - 1u), half = 1u << (r - 1);
   tie = rem == half;
   return q + (rem > half ? 1u : 0u);
+}
+
+// The find condition on the grid of exponent Es: a cumulative m * u meets
+// the target iff m > floor(target / u) (kChainFindLt) or m >= ceil(target /
+// u) (kChainFindGe); returns that integer bound (target >= 0 here; a
+// negative target is met by every cumulative).
+template <int MODE>
+LZ_HD int chain_bound(float target, int Es) {
+  if (!(target >= 0.0f)) return MODE == kChainFindLt ? -1 : 0;
+  int Et;
+  uint32_t Mt;
+  fdecomp(target, Et, Mt);
+  const int sh = Et - Es;
+  uint32_t fl, rem = 0;
+  if (Mt == 0u) fl = 0u;
+  else if (sh >= 0) fl = sh >= 2 ? kUlpSat : min(Mt << sh, kUlpSat);
+  else if (-sh >= 25) { fl = 0u; rem = 1u; }
+  else { fl = Mt >> -sh; rem = Mt & ((1u << -sh) - 1u); }
+  if (MODE == kChainFindLt) return (int)fl;
+  return (int)min(fl + (rem ? 1u : 0u), kUlpSat);
 }
 
 template <int MODE>
@@ -142,19 +168,19 @@ constexpr int kChainPer = 8;          // values per thread per window
 constexpr int kChainWin = kChainPer * kSampThreads;
 
 struct ChainShared {
-  unsigned long long wt[kSampWarps];  // warp totals, then exclusive offsets
+  uint32_t wt[kSampWarps];            // warp totals, then exclusive offsets
   int wstop[kSampWarps], wfind[kSampWarps];
   int S, F;
   float sum;
   int hit;
 };
 
-LZ_HD unsigned long long warp_incl_scan_u64(unsigned long long v) {
+LZ_HD uint32_t warp_incl_scan_sat(uint32_t v) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long w = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += w;
+    const uint32_t w = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v = sadd(v, w);
   }
   return v;
 }
@@ -239,37 +265,46 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
       int Es;
       uint32_t Ms;
       fdecomp(s, Es, Ms);
-      unsigned long long pre[kChainPer], nu[kChainPer];
-      bool tie[kChainPer];
-      unsigned long long run = 0ull;
+      uint32_t pre[kChainPer], nu[kChainPer];
+      uint32_t tiemask = 0u, livemask = 0u;
+      uint32_t run = 0u;
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
         const bool live = j0 + k >= cur && j0 + k < wend;
-        nu[k] = live ? fulps(ve[k], vm[k], Es, tie[k]) : 0ull;
-        tie[k] = live && tie[k];
-        run += nu[k];
+        bool t;
+        nu[k] = live ? fulps(ve[k], vm[k], Es, t) : 0u;
+        tiemask |= (live && t) ? 1u << k : 0u;
+        livemask |= live ? 1u << k : 0u;
+        run = sadd(run, nu[k]);
         pre[k] = run;
       }
       // block exclusive scan of the thread totals (warp 0 scans the warps)
-      const unsigned long long incl = warp_incl_scan_u64(run);
+      const uint32_t incl = warp_incl_scan_sat(run);
       if (lane == 31) cs.wt[warp] = incl;
       __syncthreads();
       if (warp == 0) {
-        const unsigned long long t = cs.wt[lane];
-        cs.wt[lane] = warp_incl_scan_u64(t) - t;
+        const uint32_t t = cs.wt[lane];
+        const uint32_t x = warp_incl_scan_sat(t);
+        // exclusive value: the inclusive scan of the warps before
+        const uint32_t ex = __shfl_up_sync(0xffffffffu, x, 1);
+        cs.wt[lane] = lane ? ex : 0u;
       }
       __syncthreads();
-      const unsigned long long off = Ms + cs.wt[warp] + incl - run;
-      // first stop and first hit of this segment
-      int st = INT_MAX, fd = INT_MAX;
+      // inclusive scan of the warp before this thread (saturated)
+      const uint32_t before = __shfl_up_sync(0xffffffffu, incl, 1);
+      const uint32_t off = sadd(sadd(Ms, cs.wt[warp]), lane ? before : 0u);
+      const int bound = MODE == kChainSum ? 0 : chain_bound<MODE>(target, Es);
+      uint32_t stopmask = tiemask, hitmask = 0u;
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
-        const int j = j0 + k;
-        if (j < cur || j >= wend || st != INT_MAX) continue;
-        const unsigned long long m = off + pre[k];
-        if (tie[k] || m >= 0x1000000ull) st = j;
-        else if (MODE != kChainSum && fd == INT_MAX && chain_cond<MODE>(frecon(Es, m), target)) fd = j;
+        const uint32_t m = sadd(off, pre[k]);
+        stopmask |= ((livemask >> k) & 1u) && m >= 0x1000000u ? 1u << k : 0u;
+        if (MODE == kChainFindLt) hitmask |= ((livemask >> k) & 1u) && (int)m > bound ? 1u << k : 0u;
+        if (MODE == kChainFindGe) hitmask |= ((livemask >> k) & 1u) && (int)m >= bound ? 1u << k : 0u;
       }
+      const int st = stopmask ? j0 + __ffs(stopmask) - 1 : INT_MAX;
+      int fd = hitmask ? j0 + __ffs(hitmask) - 1 : INT_MAX;
+      if (fd >= st) fd = INT_MAX;
       int S, Fd;
       block_min2(st, fd, cs, S, Fd);
       int next;
@@ -277,26 +312,26 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
         // a cumulative inside the segment meets the target
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == Fd) cs.sum = frecon(Es, off + pre[k]);
+          if (j0 + k == Fd) cs.sum = frecon(Es, sadd(off, pre[k]));
         found = Fd;
         next = wend;
       } else if (S == INT_MAX) {
         // no stop: the segment runs to the window's end
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == wend - 1) cs.sum = frecon(Es, off + pre[k]);
+          if (j0 + k == wend - 1) cs.sum = frecon(Es, sadd(off, pre[k]));
         next = wend;
       } else {
         // the stopping addend, by a real add from the exact cumulative before it
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, off + pre[k] - nu[k]), v[k]);
+          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, sadd(off, k ? pre[k - 1] : 0u)), v[k]);
         next = S + 1;
       }
       __syncthreads();
       s = cs.sum;
       __syncthreads();
-      if (found < 0 && S != INT_MAX && Fd >= S && MODE != kChainSum && chain_cond<MODE>(s, target)) found = S;
+      if (found < 0 && S != INT_MAX && MODE != kChainSum && chain_cond<MODE>(s, target)) found = S;
       cur = next;
     }
   }
@@ -350,53 +385,103 @@ __device__ int block_argmax(const float* v, int n, SampShared& sh) {
   return r;
 }
 
-// Descending bitonic sort of a[0..N), N a power of two >= 2, by one block:
-// stages whose partner distance is below the chunk run in shared memory.
-__device__ void block_sort_desc(float* a, int N, float* sh) {
-  const int S = min(N, kSortChunk);
-  auto cx = [](float* v, int i, int l, bool desc) {
-    const float x = v[i], y = v[l];
-    if (desc ? (x < y) : (x > y)) { v[i] = y; v[l] = x; }
-  };
-  // phase 1: sort every chunk (direction alternating with the chunk's place
-  // in the global network)
-  for (int c0 = 0; c0 < N; c0 += S) {
-    for (int t = threadIdx.x; t < S; t += kSampThreads) sh[t] = a[c0 + t];
-    __syncthreads();
-    for (int k = 2; k <= S; k <<= 1)
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int t = threadIdx.x; t < S / 2; t += kSampThreads) {
-          const int i = (t / j) * 2 * j + (t % j);
-          cx(sh, i, i + j, ((c0 + i) & k) == 0);
-        }
-        __syncthreads();
-      }
-    for (int t = threadIdx.x; t < S; t += kSampThreads) a[c0 + t] = sh[t];
-    __syncthreads();
+// Descending sort of n non-negative floats by one block: a stable LSD radix
+// sort on the complemented bit patterns (4 passes of 8 bits; for floats
+// >= 0 the bit pattern orders like the value).  a holds the keys ~bits(v)
+// on entry (0xFFFFFFFF for entries that must sort last) and the sorted
+// values on exit; tmp is n words of scratch; hist is 32 x 256 words of
+// shared memory.  Each warp owns a contiguous chunk and walks it in order,
+// ranking equal digits within the warp by ballots, so every pass is stable.
+// Lanes of the warp holding the same 8-bit digit (among lanes with ok set):
+// the intersection over the digit's bits of the ballot of that bit or of
+// its complement.
+LZ_HD unsigned digit_peers(uint32_t d, bool ok) {
+  unsigned m = __ballot_sync(0xffffffffu, ok);
+#pragma unroll
+  for (int b = 0; b < 8; b++) {
+    const unsigned v = __ballot_sync(0xffffffffu, (d >> b) & 1u);
+    m &= ((d >> b) & 1u) ? v : ~v;
   }
-  // merges across chunks
-  for (int k = 2 * S; k <= N; k <<= 1) {
-    for (int j = k >> 1; j >= S; j >>= 1) {
-      for (int t = threadIdx.x; t < N / 2; t += kSampThreads) {
-        const int i = (t / j) * 2 * j + (t % j);
-        cx(a, i, i + j, (i & k) == 0);
+  return m;
+}
+
+__device__ void block_radix_sort_desc(uint32_t* a, uint32_t* tmp, int n, uint32_t* hist) {
+  constexpr int U = 16;                // keys per lane loaded ahead of the in-order walk
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = ((n + kSampWarps - 1) / kSampWarps + 32 * U - 1) / (32 * U) * (32 * U);
+  const int c0 = min(n, warp * chunk), c1 = min(n, c0 + chunk);
+  const unsigned lt = (1u << lane) - 1u;
+  uint32_t* src = a;
+  uint32_t* dst = tmp;
+  for (int pass = 0; pass < 4; pass++) {
+    const int shift = pass * 8;
+    for (int i = tid; i < kSampWarps * 256; i += kSampThreads) hist[i] = 0u;
+    __syncthreads();
+    uint32_t* h = hist + warp * 256;
+    for (int i0 = c0; i0 < c1; i0 += 32 * U) {
+      uint32_t kk[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * 32 + lane;
+        kk[u] = i < c1 ? __ldcg(src + i) : 0u;
       }
-      __syncthreads();
-    }
-    for (int c0 = 0; c0 < N; c0 += S) {
-      for (int t = threadIdx.x; t < S; t += kSampThreads) sh[t] = a[c0 + t];
-      __syncthreads();
-      for (int j = S >> 1; j > 0; j >>= 1) {
-        for (int t = threadIdx.x; t < S / 2; t += kSampThreads) {
-          const int i = (t / j) * 2 * j + (t % j);
-          cx(sh, i, i + j, ((c0 + i) & k) == 0);
-        }
-        __syncthreads();
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const bool ok = i0 + u * 32 + lane < c1;
+        const uint32_t d = (kk[u] >> shift) & 255u;
+        const unsigned peers = digit_peers(d, ok);
+        if (ok && (peers & lt) == 0u) h[d] += __popc(peers);
+        __syncwarp();
       }
-      for (int t = threadIdx.x; t < S; t += kSampThreads) a[c0 + t] = sh[t];
-      __syncthreads();
     }
+    __syncthreads();
+    // exclusive offsets per (warp, digit): digit bases in digit order, then
+    // the warps in chunk order
+    if (tid < 256) {
+      uint32_t t = 0;
+      for (int w = 0; w < kSampWarps; w++) t += hist[w * 256 + tid];
+      uint32_t x = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      __shared__ uint32_t wsum[8];
+      if (lane == 31) wsum[warp] = x;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      uint32_t base = x - t;
+      for (int w = 0; w < warp; w++) base += wsum[w];
+      for (int w = 0; w < kSampWarps; w++) {
+        const uint32_t c = hist[w * 256 + tid];
+        hist[w * 256 + tid] = base;
+        base += c;
+      }
+    }
+    __syncthreads();
+    for (int i0 = c0; i0 < c1; i0 += 32 * U) {
+      uint32_t kk[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * 32 + lane;
+        kk[u] = i < c1 ? __ldcg(src + i) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const bool ok = i0 + u * 32 + lane < c1;
+        const uint32_t d = (kk[u] >> shift) & 255u;
+        const unsigned peers = digit_peers(d, ok);
+        if (ok) dst[h[d] + __popc(peers & lt)] = pass == 3 ? ~kk[u] : kk[u];
+        __syncwarp();
+        if (ok && (peers & lt) == 0u) h[d] += __popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    uint32_t* t2 = src;
+    src = dst;
+    dst = t2;
   }
+  // four passes: the result is back in a (as value bits)
 }
 
 // The r-th (0-based) index j in ascending order with p[j] == v, by tiles of
@@ -439,15 +524,16 @@ struct Nucleus {
 };
 
 // p holds the softmax probabilities (length n); sorted is scratch of
-// npow2 floats; returns the nucleus.
+// 2 * npow2 floats (sorted candidates first); returns the nucleus.
 __device__ Nucleus block_nucleus(const float* p, int n, float topp, float* sorted, int npow2, float* stage,
                                  SampShared& sh) {
   const float cut = n > 1 ? __fdiv_rn(__fsub_rn(1.0f, topp), (float)(n - 1)) : 0.0f;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sorted);
   int cnt = 0;
-  for (int j = threadIdx.x; j < npow2; j += kSampThreads) {
-    const float v = j < n ? p[j] : -1.0f;
-    const bool c = j < n && v >= cut;
-    sorted[j] = c ? v : -1.0f;
+  for (int j = threadIdx.x; j < n; j += kSampThreads) {
+    const float v = p[j];
+    const bool c = v >= cut;
+    keys[j] = c ? ~__float_as_uint(v) : 0xFFFFFFFFu;
     cnt += c;
   }
   Nucleus nu;
@@ -455,7 +541,7 @@ __device__ Nucleus block_nucleus(const float* p, int n, float topp, float* sorte
   nu.last = -1;
   nu.mass = 0.0f;
   if (nu.n0 <= 0) return nu;
-  block_sort_desc(sorted, npow2, stage);
+  block_radix_sort_desc(keys, keys + npow2, n, reinterpret_cast<uint32_t*>(stage));
   int hit;
   auto sv = [&](int j) { return sorted[j]; };
   const float limit = __fmul_rn(topp, 1.0f);
@@ -474,7 +560,7 @@ __device__ int block_first_pos(const float* sorted, int pos, SampShared& sh) {
 }
 
 // lz_target_dist (src/sampler.c:682-714): p row in place; sorted is
-// npow2 floats of scratch.
+// 2 * npow2 floats of scratch.
 __device__ void block_target_dist(const float* lg, int n, float temp, float topp, float* p, float* sorted,
                                   int npow2, float* stage, SampShared& sh) {
   const float inv_t = __fdiv_rn(1.0f, temp);
@@ -519,7 +605,7 @@ __device__ void block_target_dist(const float* lg, int n, float temp, float topp
 
 // sample_ex with identity penalties (src/sampler.c:794-901): the coin is
 // drawn first; top-p sample from the sorted nucleus.  p and sorted are
-// scratch rows (n and npow2 floats).  Thread 0 owns *rng.
+// scratch rows (n and 2 * npow2 floats).  Thread 0 owns *rng.
 __device__ int block_sample_ex(const float* lg, int n, float temp, float topp, unsigned long long* rng, float* p,
                                float* sorted, int npow2, float* stage, SampShared& sh) {
   if (!(temp > kTempFloor)) return block_argmax(lg, n, sh);
@@ -584,7 +670,7 @@ __global__ void __launch_bounds__(kSampThreads) temp_target_kernel(const float* 
   __shared__ SampShared sh;
   const int row = blockIdx.x, b = row / (k + 1);
   block_target_dist(logits + (size_t)row * V, V, sr[b].temp, sr[b].topp, pbuf + (size_t)row * V,
-                    sortbuf + (size_t)row * npow2, npow2, stage, sh);
+                    sortbuf + (size_t)row * 2 * npow2, npow2, stage, sh);
 }
 
 // Coupled acceptance of a temperature round (src/generate.c:1300-1377 with
