@@ -15,6 +15,10 @@ emitted tokens (n_accept + 1 per round per sequence) of all ranks over
 the slowest rank's time.  The round's weight stream (about 0.95 GB) is far
 larger than L2, so no explicit flush is used.
 
+The same line carries "batch32": BASELINE configs[2] (32 sequences per GPU,
+Zipf prompts of 256-1024 tokens, temperature 0.8, top-p 0.95, k = 3),
+measured the same way after the headline workload (--no-b32 skips it).
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 --impl reference runs the reference engine itself (oracle/_ref, compiled
@@ -161,6 +165,82 @@ def reduce_over_ranks(ms: float, emitted: float, e2e, world: int, device: str):
     return float(mx[0]), float(sm[0]), (float(sm[1]) if e2e is not None else None)
 
 
+B32 = 32          # configs[2]: sequences per GPU
+K32 = 3
+NEW32 = 512
+
+
+def run_batch32(m, args, rank: int, world: int):
+    """BASELINE configs[2] on this rank: 32 independent sequences, prompts of
+    256-1024 Zipf(1.1) token ids, temperature 0.8, top-p 0.95, per-sequence
+    seeds, draft depth 3.  Device-timed rounds (CUDA graph replay), then an
+    end-to-end pass through lz_spec_round_batch that reads every round's
+    tokens back to the host.  Every rank takes the same collectives."""
+    import torch
+    import torch.distributed as dist
+    import lz98
+    import lz98_synth
+    cfg = lz98_synth.CONFIGS[MODEL]
+    prompts = lz98_synth.workload_prompts(cfg, B32, 256, 1024, 1.1, seed=rank)
+    e2e_steps = 8
+    steps = max(1, min(args.steps, NEW32 // (K32 + 1) - args.warmup - e2e_steps - 2))
+    seq_len = 1024 + (K32 + 1) * (args.warmup + steps + e2e_steps + 2) + 64
+    s = lz98.State(m, seq_len, K32, n_seq=B32)
+    t0 = time.time()
+    for b, p in enumerate(prompts):
+        s.set_sampler(b, 0.8, 0.95, 1000 + rank * B32 + b)
+        s.seq_prefill(b, p)
+    prefill_s = time.time() - t0
+    print(f"[bench] b32_prefill_launches={s.launches()}", file=sys.stderr, flush=True)
+    stream = torch.cuda.ExternalStream(s.stream())
+    for _ in range(args.warmup):
+        s.round_batch(K32, fetch=False)
+    torch.cuda.synchronize()
+    c0 = [s.counters(b) for b in range(B32)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        s.round_batch(K32, fetch=False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    c1 = [s.counters(b) for b in range(B32)]
+    emitted = sum(c1[b][1] - c0[b][1] for b in range(B32))
+    accepted = sum(c1[b][2] - c0[b][2] for b in range(B32))
+    drafted = sum(c1[b][3] - c0[b][3] for b in range(B32))
+    rounds = sum(c1[b][0] - c0[b][0] for b in range(B32))
+    # end to end: the public batched round with the tokens read back
+    torch.cuda.synchronize()
+    t_e = time.perf_counter()
+    n_e = 0
+    for _ in range(e2e_steps):
+        toks, cnt = s.round_batch(K32, fetch=True)
+        n_e += int(cnt.sum())
+    dt_e = time.perf_counter() - t_e
+    prof = s.profile_round(K32)
+    s.close()
+    ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), n_e / dt_e, world, "cuda")
+    return {
+        "workload": "configs[2]: ~0.5B KunMoe, 32 sequences per GPU, prompts 256-1024 Zipf(1.1), "
+                    "temperature 0.8, top-p 0.95, k=3",
+        "value": emitted_all / (ms_max * 1e-3), "unit": UNIT, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / steps, "global_batch": B32 * world, "scaling": "weak",
+        "mean_accept_len": (accepted + rounds) / max(1, rounds), "alpha": accepted / max(1, drafted),
+        "prefill_s": prefill_s,
+        "e2e": {"value": e2e_all, "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": B32 * (K32 + 1) * 4 + B32 * 4,
+                "api": "lz_spec_round_batch (round state device-resident, tokens and counts read back)"},
+        "gemm_ms_per_round": prof["gemv_ms"], "round_ms_eager": prof["round_ms"],
+        "gemm_algorithmic_gbs": prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9,
+        "gpu_launches": prof["n_kernels"] * steps,
+    }
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -180,6 +260,15 @@ def run_ours(args):
         dist.barrier()
         d = model_dir()
     m = lz98.Model(d)
+    if args.b32_only:
+        b32 = run_batch32(m, args, rank, world)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "n_gpus": world, "batch32": b32}), flush=True)
+        m.close()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return b32
     seq_len = PROMPT + (k + 1) * (args.warmup + args.steps + 2) + 64
     s = lz98.State(m, seq_len, k, n_seq=n_seq)
     t0 = time.time()
@@ -237,6 +326,7 @@ def run_ours(args):
         h2d, d2h = sr_bytes, 2 * sr_bytes
         s1.close()
     ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), e2e_val, world, "cuda")
+    b32 = None if args.no_b32 else run_batch32(m, args, rank, world)
     peak, peak_kind = measured_peak()
     gemv_gbs = prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9
     line = None
@@ -268,6 +358,7 @@ def run_ours(args):
                     "api": "lz_spec_round (host anchor in, host tokens out)"} if e2e_val else None,
             "gpu_launches": prof["n_kernels"] * args.steps,
             "clocks": clk,
+            "batch32": b32,
         }
         print(json.dumps(line), flush=True)
     s.close()
@@ -343,6 +434,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the C-ABI end-to-end pass")
+    ap.add_argument("--no-b32", action="store_true", help="skip the batch-32 temperature workload")
+    ap.add_argument("--b32-only", action="store_true", help="run only the batch-32 workload (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
