@@ -165,6 +165,7 @@ def reduce_over_ranks(ms: float, emitted: float, e2e, world: int, device: str):
     return float(mx[0]), float(sm[0]), (float(sm[1]) if e2e is not None else None)
 
 
+GEMV_TRAFFIC_RATIO = 1.045   # ncu dram bytes / algorithmic bytes of the int8 GEMV
 B32 = 32          # configs[2]: sequences per GPU
 K32 = 3
 NEW32 = 512
@@ -350,7 +351,12 @@ def run_ours(args):
             "hbm_gbs_round": rb / (per_round_ms * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "gemv_q8_kernel (int8 weight streaming, all GEMVs of one round)",
                          "achieved": gemv_gbs, "peak": peak, "unit": "GB/s", "frac": gemv_gbs / peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind,
+                         # DRAM bytes of the round's GEMV launches: the algorithmic
+                         # bytes times the mean DRAM/algorithmic ratio of an ncu
+                         # capture (profiles/gemv_b1_dram_traffic.md)
+                         "traffic": prof["gemv_bytes"] * GEMV_TRAFFIC_RATIO,
+                         "traffic_unit": "bytes per round (all GEMV launches)",
                          "gemv_share_of_round": prof["gemv_ms"] / max(1e-9, prof["round_ms"]),
                          "round_algorithmic_bytes": rb},
             "cpu_baseline": cpu,
