@@ -704,15 +704,30 @@ __global__ void __launch_bounds__(256) kda_pre_kernel(const KdaPreArgs a) {
 // state resident in shared memory.  Everything that does not read the
 // state runs for a batch of up to kRecurTB tokens at once: l2norm(q) *
 // kd^-1/2, l2norm(k), beta = sigmoid(b); then per token, serially, pass 1
-// (u = S^T(g.k), w = S^T(g.q), kq = k.q, each a sequential sum over the 64
-// state rows, products formed by all warps first), the head output
-// w + u*kq with u = (v - u)*beta, and pass 2 (each state row g*S + k*u
-// requantised in two planes, one warp per 32-wide group); finally the
-// gated RMSNorm and per-32 quantisation of every token's output in
-// parallel.  src/forward_kda.c:856-936 and 1029-1040,
-// src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
-constexpr int kRecurThreads = 1024;
+// (u = S^T(g.k) and w = S^T(g.q), each a sequential sum over the 64 state
+// rows, one thread per output column forming its products in order; kq =
+// k.q on another thread), the head output w + u*kq with u = (v - u)*beta,
+// and pass 2 (each state row g*S + k*u requantised in two planes, four
+// 32-wide groups per warp at a time); finally the gated RMSNorm and per-32
+// quantisation of every token's output.  src/forward_kda.c:856-936 and
+// 1029-1040, src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340,
+// src/ops_norm.c:749-842.
+constexpr int kRecurThreads = 256;
 constexpr int kRecurTB = 4;
+
+// One two-plane requantisation of a 32-wide state group held one element
+// per lane (src/ops_gdn.c:1191-1340): hi = q8 of buf, residual rounded
+// half up into hi when possible, lo = rne(residual * 256).
+LZ_HD void requant_2p(float buf, float sg, float iv, int8_t& h8, int8_t& l8) {
+  const float f = __fmul_rn(buf, iv);
+  int hq = q8_clamp(q8_round(f));
+  float res = __fsub_rn(f, (float)hq);
+  if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
+  else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
+  h8 = (int8_t)hq;
+  l8 = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
+}
+
 __global__ void __launch_bounds__(kRecurThreads)
 kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  const float* __restrict__ inproj, int ldi, int off_b, int off_g,
@@ -725,31 +740,28 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  int8_t* oq, float* os) {
   pdl_trigger();
   pdl_wait();
-  constexpr int KD = 64, VD = 64, TB = kRecurTB;
+  constexpr int KD = 64, VD = 64, TB = kRecurTB, NW = kRecurThreads / 32;
   __shared__ __align__(16) int8_t hi[KD][VD];
   __shared__ __align__(16) int8_t lo[KD][VD];
   __shared__ __align__(16) float sc[KD][2];
   __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], vcs[TB][VD], zs[TB][VD], OUT[TB][VD];
-  __shared__ __align__(16) float PU[KD][VD], PW[KD][VD];   // pass-1 products
   __shared__ __align__(16) float U[VD];
   __shared__ float inv_q[TB], inv_k[TB], beta[TB], kqv[TB], inv_o[TB];
   const KdaSeq sq = seqs[blockIdx.y];
   const int h = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t head_off = (size_t)layer_off_q + (size_t)h * KD * VD;
   const size_t seq_off = (size_t)sq.seq * seq_stride_q;
   {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
-      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
-    }
+    reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
+    reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
     if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
   }
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
     // stage the batch (raw q, k in qn/kn until normalised)
-    for (int q = tid; q < nt * 64; q += blockDim.x) {
+    for (int q = tid; q < nt * 64; q += kRecurThreads) {
       const int t = q >> 6, i = q & 63;
       const size_t r = (size_t)(sq.row0 + t0 + t);
       qn[t][i] = conv_out[r * ldc + h * KD + i];
@@ -759,78 +771,88 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
       gv[t][i] = gate[r * nvk + h * KD + i];
     }
     __syncthreads();
-    if (lane == 0 && warp < 3 * nt) {          // independent chains on separate warps
-      const int t = warp % nt, which = warp / nt;
-      if (which == 0) inv_q[t] = rsqrt_body(__fadd_rn(seq_sumsq(qn[t], KD), kL2Eps));
-      else if (which == 1) inv_k[t] = rsqrt_body(__fadd_rn(seq_sumsq(kn[t], KD), kL2Eps));
-      else beta[t] = sigmoid(inproj[(size_t)(sq.row0 + t0 + t) * ldi + off_b + h]);
+    {                                          // 3 nt independent chains, two per warp
+      const int c = warp * 2 + (lane >> 4);
+      if ((lane & 15) == 0 && c < 3 * nt) {
+        const int t = c % nt, which = c / nt;
+        if (which == 0) inv_q[t] = rsqrt_body(__fadd_rn(seq_sumsq(qn[t], KD), kL2Eps));
+        else if (which == 1) inv_k[t] = rsqrt_body(__fadd_rn(seq_sumsq(kn[t], KD), kL2Eps));
+        else beta[t] = sigmoid(inproj[(size_t)(sq.row0 + t0 + t) * ldi + off_b + h]);
+      }
     }
+    static_assert(2 * (kRecurThreads / 32) >= 3 * kRecurTB, "chains per batch exceed the warps");
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += blockDim.x) {
+    for (int q = tid; q < nt * 64; q += kRecurThreads) {
       const int t = q >> 6, i = q & 63;
       qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), ssm_scale);
       kn[t][i] = __fmul_rn(kn[t][i], inv_k[t]);
     }
     __syncthreads();
     for (int t = 0; t < nt; t++) {
-      // pass 1 products: all warps, one (kk, vv) element each
-      for (int q = tid; q < KD * VD; q += blockDim.x) {
-        const int kk = q >> 6, vv = q & 63;
-        const float g = gv[t][kk], s = sc[kk][vv >> 5];
-        const float sck = __fmul_rn(s, __fmul_rn(kn[t][kk], g));
-        const float scq = __fmul_rn(s, __fmul_rn(qn[t][kk], g));
-        const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-        PU[kk][vv] = __fmul_rn(e, sck);
-        PW[kk][vv] = __fmul_rn(e, scq);
-      }
-      if (tid == 128) {                       // kq = k.q, sequential over kk
+      // pass 1: thread vv (< 64) sums u, thread 64 + vv sums w, each over
+      // the 64 state rows in order; thread 128 forms kq
+      if (tid < 2 * VD) {
+        const int vv = tid & 63;
+        const float* qk = tid < VD ? kn[t] : qn[t];
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int kk = 0; kk < KD; kk++) {
+          const float scx = __fmul_rn(sc[kk][vv >> 5], __fmul_rn(qk[kk], gv[t][kk]));
+          const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+          acc = __fadd_rn(acc, __fmul_rn(e, scx));
+        }
+        if (tid < VD) U[vv] = acc; else OUT[t][vv] = acc;
+      } else if (tid == 2 * VD) {
         float kq = 0.0f;
         for (int kk = 0; kk < KD; kk++) kq = __fadd_rn(kq, __fmul_rn(kn[t][kk], qn[t][kk]));
         kqv[t] = kq;
       }
       __syncthreads();
-      if (tid < 2 * VD) {                     // the sequential sums over kk
-        const int vv = tid & 63;
-        const float(*PP)[VD] = tid < VD ? PU : PW;
-        float acc = 0.0f;
-#pragma unroll 16
-        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, PP[kk][vv]);
-        if (tid < VD) PU[0][vv] = acc; else PW[0][vv] = acc;
-      }
-      __syncthreads();
       if (tid < VD) {
-        const float u = __fmul_rn(__fsub_rn(vcs[t][tid], PU[0][tid]), beta[t]);
+        const float u = __fmul_rn(__fsub_rn(vcs[t][tid], U[tid]), beta[t]);
         U[tid] = u;
-        OUT[t][tid] = __fadd_rn(PW[0][tid], __fmul_rn(u, kqv[t]));
+        OUT[t][tid] = __fadd_rn(OUT[t][tid], __fmul_rn(u, kqv[t]));
       }
       __syncthreads();
-      // pass 2: one warp per (state row, 32-wide group)
-      for (int unit = warp; unit < KD * 2; unit += nwarp) {
-        const int kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-        const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);
-        const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-        const float buf = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[t][kk], U[vv]));
-        const uint32_t am = warp_max_u32(abs_bits(buf));
-        float sg, iv;
-        q8_scale_from_amax(am, &sg, &iv);
-        const float f = __fmul_rn(buf, iv);
-        int hq = q8_clamp(q8_round(f));
-        float res = __fsub_rn(f, (float)hq);
-        if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
-        else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
+      // pass 2: the 128 (state row, 32-wide group) units, four per warp at
+      // a time with their max reductions interleaved
+      for (int u0 = warp * 4; u0 < KD * 2; u0 += NW * 4) {
+        float buf[4];
+        uint32_t am[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
+          const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);
+          const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+          buf[c] = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[t][kk], U[vv]));
+          am[c] = abs_bits(buf[c]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            const uint32_t w = __shfl_xor_sync(0xffffffffu, am[c], o);
+            am[c] = am[c] > w ? am[c] : w;
+          }
         __syncwarp();
-        hi[kk][vv] = (int8_t)hq;
-        lo[kk][vv] = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
-        if (lane == 0) sc[kk][grp] = sg;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
+          float sg, iv;
+          q8_scale_from_amax(am[c], &sg, &iv);
+          int8_t h8, l8;
+          requant_2p(buf[c], sg, iv, h8, l8);
+          hi[kk][vv] = h8;
+          lo[kk][vv] = l8;
+          if (lane == 0) sc[kk][grp] = sg;
+        }
       }
       __syncthreads();
       if (adv) {
         const int so = (sq.base_slot + t0 + t + 1) % depth;
         const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
-        if (tid < KD * VD / 16) {
-          reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-          reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
-        }
+        reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+        reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
         if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
       }
     }
@@ -838,7 +860,7 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     if (lane == 0 && warp < nt)
       inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), eps));
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += blockDim.x) {
+    for (int q = tid; q < nt * 64; q += kRecurThreads) {
       const int t = q >> 6, i = q & 63;
       const size_t r = (size_t)(sq.row0 + t0 + t);
       const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), o_norm[i]), silu(zs[t][i]));
@@ -848,10 +870,8 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   }
   if (!adv) {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-      reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
-    }
+    reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+    reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
     if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
   }
 }
