@@ -515,11 +515,12 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
     cudaDeviceGetAttribute(&s->n_sm, cudaDevAttrMultiProcessorCount, dev);
     // the GEMV input-norm prologue stages its rows in dynamic shared memory
     const int gdyn = 160 * 1024;
-    if (cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvProWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<1, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<2, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess ||
-        cudaFuncSetAttribute(gemv_q8_kernel<4, kGemvWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) != cudaSuccess) {
+    auto attr = [gdyn](auto kern) {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) == cudaSuccess;
+    };
+    if (!attr(gemv_q8_kernel<1, kGemvProWarps, 1, true, false>) || !attr(gemv_q8_kernel<1, kGemvProWarps, 4, true, false>) ||
+        !attr(gemv_q8_kernel<1, kGemvProWarps, 8, true, false>) || !attr(gemv_q8_kernel<2, kGemvProWarps, 1, true, false>) ||
+        !attr(gemv_q8_kernel<2, kGemvProWarps, 4, true, false>) || !attr(gemv_q8_kernel<2, kGemvProWarps, 8, true, false>)) {
       set_err(errbuf, errlen, "cannot raise the GEMV shared-memory limit");
       lz_state_free(s);
       return LZ98_ERR_CUDA;
@@ -683,15 +684,17 @@ constexpr int kGemvMaxBlocksPerSM = 16;
 void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
                    int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear = nullptr);
 
-template <int JM, int WARPS>
-void gemv_launch(LZRunState* s, const GemvArgs& a, bool prologue) {
-  const size_t dyn = gemv_smem_bytes(JM, WARPS, a.W2 != nullptr, prologue, a.R, a.K);
-  const long key = (long)JM << 48 | (long)WARPS << 40 | (long)dyn;
+template <int JM, int WARPS, int RB, bool PRO, bool SINGLE>
+void gemv_launch(LZRunState* s, const GemvArgs& a) {
+  const size_t dyn = gemv_smem_bytes(JM, WARPS, RB, SINGLE, PRO, a.R, a.K);
+  const long key = (long)JM << 56 | (long)WARPS << 48 | (long)RB << 44 | (long)PRO << 43 | (long)SINGLE << 42 |
+                   (long)dyn;
   auto it = s->gemv_occ.find(key);
   int per_sm;
   if (it == s->gemv_occ.end()) {
     per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q8_kernel<JM, WARPS>, WARPS * 32, dyn);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q8_kernel<JM, WARPS, RB, PRO, SINGLE>, WARPS * 32,
+                                                  dyn);
     per_sm = std::max(1, std::min(per_sm, kGemvMaxBlocksPerSM));
     s->gemv_occ[key] = per_sm;
   } else {
@@ -699,8 +702,15 @@ void gemv_launch(LZRunState* s, const GemvArgs& a, bool prologue) {
   }
   const int want = (a.N + WARPS - 1) / WARPS;
   // a prologue is paid once per block: one block per SM
-  const int cap = s->n_sm * (prologue ? 1 : per_sm);
-  launch(s, gemv_q8_kernel<JM, WARPS>, dim3(std::min(want, cap)), dim3(WARPS * 32), dyn, a);
+  const int cap = s->n_sm * (PRO ? 1 : per_sm);
+  launch(s, gemv_q8_kernel<JM, WARPS, RB, PRO, SINGLE>, dim3(std::min(want, cap)), dim3(WARPS * 32), dyn, a);
+}
+
+template <int JM, int WARPS, bool PRO>
+void gemv_launch_rb(LZRunState* s, const GemvArgs& a) {
+  if (a.R <= 1) gemv_launch<JM, WARPS, 1, PRO, false>(s, a);
+  else if (a.R <= 4) gemv_launch<JM, WARPS, 4, PRO, false>(s, a);
+  else gemv_launch<JM, WARPS, 8, PRO, false>(s, a);
 }
 
 // y (R x N, ld ldy) = [y +] W x (+ W2 x2).  With `nin`, x is produced here
@@ -749,12 +759,16 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
       else launch(s, gemm_q8_warp_kernel<2, false>, grid, dim3(128), 0, a);
     }
   } else if (prologue) {
-    if (nsb <= 32) gemv_launch<1, kGemvProWarps>(s, a, true);
-    else gemv_launch<2, kGemvProWarps>(s, a, true);
+    if (nsb <= 32) gemv_launch_rb<1, kGemvProWarps, true>(s, a);
+    else gemv_launch_rb<2, kGemvProWarps, true>(s, a);
+  } else if (w2 || R > kGemvRB) {
+    if (nsb <= 32) gemv_launch<1, kGemvWarps, kGemvRB, false, true>(s, a);
+    else if (nsb <= 64) gemv_launch<2, kGemvWarps, kGemvRB, false, true>(s, a);
+    else gemv_launch<4, kGemvWarps, kGemvRB, false, true>(s, a);
   } else {
-    if (nsb <= 32) gemv_launch<1, kGemvWarps>(s, a, false);
-    else if (nsb <= 64) gemv_launch<2, kGemvWarps>(s, a, false);
-    else gemv_launch<4, kGemvWarps>(s, a, false);
+    if (nsb <= 32) gemv_launch_rb<1, kGemvWarps, false>(s, a);
+    else if (nsb <= 64) gemv_launch_rb<2, kGemvWarps, false>(s, a);
+    else gemv_launch_rb<4, kGemvWarps, false>(s, a);
   }
   if (s->prof) cudaEventRecord(s->prof_ev.back(), s->st);
 }
@@ -1592,9 +1606,15 @@ extern "C" int lz_lm_head_static(const LZModel* m, const float* hidden, int n, f
   GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, n, logits, c.vocab, 0, nullptr, nullptr, 0, 32, nullptr, nullptr};
   const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
   const int nsb = w.in / 32;
-  if (nsb <= 32) gemv_q8_kernel<1, kGemvWarps><<<grid, blk, gemv_smem_bytes(1, kGemvWarps, false, false, n, w.in), st>>>(a);
-  else if (nsb <= 64) gemv_q8_kernel<2, kGemvWarps><<<grid, blk, gemv_smem_bytes(2, kGemvWarps, false, false, n, w.in), st>>>(a);
-  else gemv_q8_kernel<4, kGemvWarps><<<grid, blk, gemv_smem_bytes(4, kGemvWarps, false, false, n, w.in), st>>>(a);
+  if (nsb <= 32)
+    gemv_q8_kernel<1, kGemvWarps, kGemvRB, false, true>
+        <<<grid, blk, gemv_smem_bytes(1, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
+  else if (nsb <= 64)
+    gemv_q8_kernel<2, kGemvWarps, kGemvRB, false, true>
+        <<<grid, blk, gemv_smem_bytes(2, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
+  else
+    gemv_q8_kernel<4, kGemvWarps, kGemvRB, false, true>
+        <<<grid, blk, gemv_smem_bytes(4, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
   if (cudaGetLastError() != cudaSuccess) {
     set_err(errbuf, errlen, "lz_lm_head_static: kernel launch failed");
     return LZ98_ERR_CUDA;

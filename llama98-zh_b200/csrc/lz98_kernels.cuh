@@ -168,12 +168,12 @@ LZ_HD void load_wrow(WRow<JM>& w, const int8_t* __restrict__ wr, const float* __
 // Products of one weight row with every token row for the sub-blocks this
 // lane owns; P[rr][s] receives the product fed to the reference reduction.
 // The quantised rows are read from shared memory (SH) or global memory.
-template <int JM, bool SH>
+template <int JM, bool SH, int RB>
 LZ_HD void gemv_products(const WRow<JM>& w, int K, int rb, const int8_t* xq, const float* xs, int r0, int nr,
                          float (*P)[JM * 32], int lane) {
   const int nsb = K >> 5;
 #pragma unroll
-  for (int rr = 0; rr < kGemvRB; rr++) {
+  for (int rr = 0; rr < RB; rr++) {
     if (rr < nr) {
       const int8_t* xr = xq + (size_t)(r0 + rr) * K;
       const float* xsr = xs + (size_t)(r0 + rr) * nsb;
@@ -200,15 +200,22 @@ LZ_HD void gemv_products(const WRow<JM>& w, int K, int rb, const int8_t* xq, con
   }
 }
 
+// Weight rows a warp takes per step on the multi-row path.
+template <int JM>
+__host__ __device__ constexpr int gemv_nr() { return 4 / JM; }
+
 // Bytes of dynamic shared memory of one GEMV block: per-warp product
-// buffers (two with a second weight) and, with the input-norm prologue,
-// the rows, norm weights, quantised rows, scales and inverse norms.
-inline size_t gemv_smem_bytes(int JM, int warps, bool w2, bool prologue, int R, int K) {
-  size_t b = (size_t)(w2 ? 2 : 1) * warps * kGemvRB * JM * 32 * 4;
+// buffers (multi-row path: RB x NR rows; single-row path: 8 rows for each
+// of the two weights) and, with the input-norm prologue, the rows, norm
+// weights, quantised rows, scales and inverse norms.
+inline size_t gemv_smem_bytes(int JM, int warps, int RB, bool single, bool prologue, int R, int K) {
+  size_t b = single ? (size_t)warps * 2 * kGemvRB * JM * 32 * 4 : (size_t)warps * RB * (4 / JM) * JM * 32 * 4;
   if (prologue) b += (size_t)R * K * 4 + (size_t)K * 4 + (size_t)R * K + (size_t)R * (K / 32) * 4 + 64;
   return b;
 }
 
+// One output row per step, any number of token rows (8 at a time) and an
+// optional second weight over the same outputs.
 template <int JM, int WARPS, bool SH>
 LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM>& wn1, WRow<JM>& wn2,
                      float (*P)[JM * 32], float (*P2)[JM * 32], int n, int lane) {
@@ -225,8 +232,8 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
     const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
     for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
       const int nr = min(kGemvRB, a.R - r0);
-      gemv_products<JM, SH>(w1, a.K, rb, xq, xs, r0, nr, P, lane);
-      if (a.W2) gemv_products<JM, false>(w2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2, lane);
+      gemv_products<JM, SH, kGemvRB>(w1, a.K, rb, xq, xs, r0, nr, P, lane);
+      if (a.W2) gemv_products<JM, false, kGemvRB>(w2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2, lane);
       float prev = 0.0f;
       if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
       __syncwarp();
@@ -240,41 +247,90 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
   }
 }
 
-// Weight-streaming int8 GEMV/skinny GEMM, persistent over output rows: one
-// warp per output row at a time, each lane owning 32-byte sub-blocks of
-// the row (the first row loaded before the wait on the producing kernel,
-// each next row while the current one computes), per-sub-block int32 sums
-// by __dp4a, then one lane per token row runs the reference reduction.
-// With an input-norm prologue the grid is one WARPS-warp block per SM so
-// the prologue is paid once per SM.
-template <int JM, int WARPS>
+// Rows of one warp taken NR at a time (weights of the next NR rows in
+// flight while these compute): the products of all NR rows x R token rows
+// (R <= RB <= 8), then their NR * R reductions on as many lanes at once.
+template <int JM, int WARPS, bool SH, int RB>
+LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM> (&wc)[gemv_nr<JM>()],
+                           float (*P)[JM * 32], int n0, int lane) {
+  constexpr int NR = gemv_nr<JM>();
+  const int rb = a.gs >> 5, ng = a.K / a.gs, R = a.R;
+  const int nstep = gridDim.x * WARPS;
+  WRow<JM> wn[NR];
+  for (int base = n0; base < a.N; base += NR * nstep) {
+    const int nb = base + NR * nstep;
+#pragma unroll
+    for (int i = 0; i < NR; i++) {
+      const int r = nb + i * nstep;
+      if (r < a.N) load_wrow<JM>(wn[i], a.W + (size_t)r * a.K, a.ws + (size_t)r * ng, a.K, rb, lane);
+    }
+#pragma unroll
+    for (int i = 0; i < NR; i++)
+      if (base + i * nstep < a.N) gemv_products<JM, SH, RB>(wc[i], a.K, rb, xq, xs, 0, R, P + i * R, lane);
+    __syncwarp();
+    if (lane < NR * R) {
+      const int i = lane / R, rr = lane - i * R, r = base + i * nstep;
+      if (r < a.N) {
+        float* yp = a.y + (size_t)rr * a.ldy + r;
+        const float prev = a.mode == 1 ? *yp : 0.0f;
+        const float v = q8_reduce(P[lane], a.ws + (size_t)r * ng, rb, ng);
+        *yp = a.mode == 1 ? __fadd_rn(prev, v) : v;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < NR; i++) wc[i] = wn[i];
+  }
+}
+
+// Weight-streaming int8 GEMV/skinny GEMM, persistent over output rows: each
+// lane owns 32-byte sub-blocks of a weight row (the first rows loaded
+// before the wait on the producing kernel, the next while the current
+// compute), per-sub-block int32 sums by __dp4a, then the reference
+// reduction per (output, token row) on separate lanes.  Compile-time
+// variants keep each launched kernel small: RB bounds the token rows of
+// the multi-row path (R <= RB); PRO adds the input-norm prologue (one
+// WARPS-warp block per SM, so the prologue is paid once per SM); SINGLE is
+// the one-row-per-step path for a second weight or more than 8 token rows.
+template <int JM, int WARPS, int RB, bool PRO, bool SINGLE>
 __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
-  // dynamic shared memory: per-warp products P (and P2 with a second
-  // weight), then the prologue's rows (gemv_smem_bytes)
+  constexpr int NR = gemv_nr<JM>();
   extern __shared__ __align__(16) float gsm[];
-  typedef float PBuf[kGemvRB][JM * 32];
-  PBuf* P = reinterpret_cast<PBuf*>(gsm);
-  PBuf* P2 = a.W2 ? P + WARPS : P;
-  float* pro = reinterpret_cast<float*>(a.W2 ? P2 + WARPS : P + WARPS);
+  typedef float PRow[JM * 32];
+  PRow* P = reinterpret_cast<PRow*>(gsm) + (size_t)(threadIdx.x >> 5) * (SINGLE ? 2 * kGemvRB : RB * NR);
+  PRow* P2 = P + kGemvRB;
+  float* pro = gsm + (size_t)WARPS * (SINGLE ? 2 * kGemvRB : RB * NR) * JM * 32;
   pdl_trigger();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * WARPS + warp;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * WARPS + (threadIdx.x >> 5);
   const int rb = a.gs >> 5, ng = a.K / a.gs;
-  const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
+  const int nstep = gridDim.x * WARPS;
   WRow<JM> w1, w2;
-  if (n0 < a.N) {
-    load_wrow<JM>(w1, a.W + (size_t)n0 * a.K, a.ws + (size_t)n0 * ng, a.K, rb, lane);
-    if (a.W2) load_wrow<JM>(w2, a.W2 + (size_t)n0 * a.K2, a.ws2 + (size_t)n0 * ng2, a.K2, rb2, lane);
+  WRow<JM> wc[NR];
+  if (SINGLE) {
+    const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
+    if (n0 < a.N) {
+      load_wrow<JM>(w1, a.W + (size_t)n0 * a.K, a.ws + (size_t)n0 * ng, a.K, rb, lane);
+      if (a.W2) load_wrow<JM>(w2, a.W2 + (size_t)n0 * a.K2, a.ws2 + (size_t)n0 * ng2, a.K2, rb2, lane);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NR; i++) {
+      const int r = n0 + i * nstep;
+      if (r < a.N) load_wrow<JM>(wc[i], a.W + (size_t)r * a.K, a.ws + (size_t)r * ng, a.K, rb, lane);
+    }
   }
   pdl_wait();
-  if (!a.nx) {
-    gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P[warp], P2[warp], n0, lane);
+  if (!PRO) {
+    if (SINGLE) gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P, P2, n0, lane);
+    else gemv_rows_multi<JM, WARPS, false, RB>(a, a.xq, a.xs, wc, P, n0, lane);
     return;
   }
   // input-norm prologue: rows -> shared (every load issued before the
   // first store), one sequential sum of squares per row, then the (1+w)
   // scaling and per-32 quantisation (src/ops_norm.c:690-747,
   // src/ops_quant.c:2152-2282)
+  const int warp = threadIdx.x >> 5;
   const int K = a.K, R = a.R, gpr = K / 32;
   float* fx = pro;                                   // [R][K]
   float* fw = fx + (size_t)R * K;                    // [K]
@@ -331,7 +387,8 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
     }
   }
   __syncthreads();
-  gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P[warp], P2[warp], n0, lane);
+  if (SINGLE) gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P, P2, n0, lane);
+  else gemv_rows_multi<JM, WARPS, true, RB>(a, sxq, sxs, wc, P, n0, lane);
 }
 
 // ------------------------------------------------------ tensor-core helpers
