@@ -253,7 +253,8 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     n_seq = args.seqs
     k = SPEC_K
     d = model_dir() if rank == 0 or world == 1 else None
