@@ -747,17 +747,19 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
   }
   const bool rb1 = w.gs == 32;
   if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
-    // tensor-core warp tiles: 16 token rows x 8 NT outputs per warp (NT = 1
-    // for narrow outputs, so enough warps are resident to hide latency)
-    const int NT = w.out <= 2048 ? 1 : 2;
-    const dim3 grid((w.out + 32 * NT - 1) / (32 * NT), (R + 15) / 16);
-    if (NT == 1) {
-      if (rb1) launch(s, gemm_q8_warp_kernel<1, true>, grid, dim3(128), 0, a);
-      else launch(s, gemm_q8_warp_kernel<1, false>, grid, dim3(128), 0, a);
-    } else {
-      if (rb1) launch(s, gemm_q8_warp_kernel<2, true>, grid, dim3(128), 0, a);
-      else launch(s, gemm_q8_warp_kernel<2, false>, grid, dim3(128), 0, a);
-    }
+    // tensor-core warp tiles of 16 MT token rows x 8 NT outputs (measured
+    // best: 32 x 16 for wide outputs, 32 x 8 for narrow ones, 16-row tiles
+    // when R <= 16)
+    const int MT = R > 16 ? 2 : 1, NT = w.out >= 2048 ? 2 : 1;
+    const dim3 grid((w.out + 32 * NT - 1) / (32 * NT), (R + 16 * MT - 1) / (16 * MT));
+#define LZ_GEMM(mt, nt)                                                                   \
+  if (rb1) launch(s, gemm_q8_warp_kernel<mt, nt, true>, grid, dim3(128), 0, a);           \
+  else launch(s, gemm_q8_warp_kernel<mt, nt, false>, grid, dim3(128), 0, a);
+    if (MT == 1 && NT == 1) { LZ_GEMM(1, 1) }
+    else if (MT == 1) { LZ_GEMM(1, 2) }
+    else if (NT == 1) { LZ_GEMM(2, 1) }
+    else { LZ_GEMM(2, 2) }
+#undef LZ_GEMM
   } else if (prologue) {
     if (nsb <= 32) gemv_launch_rb<1, kGemvProWarps, true>(s, a);
     else gemv_launch_rb<2, kGemvProWarps, true>(s, a);

@@ -437,18 +437,25 @@ LZ_HD float mma_result(const RedState<true>& r) {
 // still yields the exact int32 sum over the 32 bytes.  With K never split
 // across warps, each output's float reduction runs in K order in the
 // lane that holds it.
-// A rows ra (fragment rows g) and rc (rows g+8) of xq; n tile t covers
-// weight rows nb[t] .. nb[t]+7 (clamped to N-1).
-template <int NT, bool RB1>
-LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
-                     const int8_t* __restrict__ xq, const float* __restrict__ xs, int ra, int rc,
-                     const int (&nb)[NT], RedState<RB1> (&st)[NT][4]) {
+// MT m tiles (A rows ra[i] for fragment rows g, rc[i] for rows g+8) by NT
+// n tiles (weight rows nb[t] .. nb[t]+7, clamped to N-1).
+template <int MT, int NT, bool RB1, int UF = 0>
+LZ_HD void wmma_pass_mt(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
+                        const int8_t* __restrict__ xq, const float* __restrict__ xs, const int (&ra)[MT],
+                        const int (&rc)[MT], const int (&nb)[NT], RedState<RB1> (&st)[MT][NT][4]) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
   const int rb = gs >> 5, ng = K / gs, nsb = K >> 5;
-  const int8_t* pa = xq + (size_t)ra * K + tq * 8;
-  const int8_t* pc = xq + (size_t)rc * K + tq * 8;
-  const float* xa = xs + (size_t)ra * nsb;
-  const float* xc = xs + (size_t)rc * nsb;
+  const int8_t* pa[MT];
+  const int8_t* pc[MT];
+  const float* xa[MT];
+  const float* xc[MT];
+#pragma unroll
+  for (int i = 0; i < MT; i++) {
+    pa[i] = xq + (size_t)ra[i] * K + tq * 8;
+    pc[i] = xq + (size_t)rc[i] * K + tq * 8;
+    xa[i] = xs + (size_t)ra[i] * nsb;
+    xc[i] = xs + (size_t)rc[i] * nsb;
+  }
   const int8_t* pb[NT];
   int oc[NT][2];
 #pragma unroll
@@ -463,16 +470,18 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
 #pragma unroll
     for (int j = 0; j < 2; j++) wrow[t][j] = (!RB1 && ng == 1) ? __ldg(ws + oc[t][j]) : 0.0f;
 #pragma unroll
-  for (int t = 0; t < NT; t++)
+  for (int i = 0; i < MT; i++)
 #pragma unroll
-    for (int e = 0; e < 4; e++)
+    for (int t = 0; t < NT; t++)
 #pragma unroll
-      for (int j = 0; j < (RB1 ? 4 : 2); j++) st[t][e].a[j] = 0.0f;
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int j = 0; j < (RB1 ? 4 : 2); j++) st[i][t][e].a[j] = 0.0f;
   // fragments of U sub-blocks are loaded while the previous U compute
-  constexpr int U = NT >= 8 ? 1 : 4;
+  constexpr int U = UF ? UF : (MT * 2 + NT >= 8 ? 1 : (MT * 2 + NT >= 5 ? 2 : 4));
   struct Frag {
-    int2 A0, A1, B[NT];
-    float x0, x1;
+    int2 A0[MT], A1[MT], B[NT];
+    float x0[MT], x1[MT];
   };
   Frag cur[U], nxt[U];
   auto load = [&](Frag (&f)[U], int sb) {
@@ -480,12 +489,15 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
     for (int u = 0; u < U; u++) {
       const int s = sb + u;
       if (s < nsb) {
-        f[u].A0 = __ldg(reinterpret_cast<const int2*>(pa + s * 32));
-        f[u].A1 = __ldg(reinterpret_cast<const int2*>(pc + s * 32));
+#pragma unroll
+        for (int i = 0; i < MT; i++) {
+          f[u].A0[i] = __ldg(reinterpret_cast<const int2*>(pa[i] + s * 32));
+          f[u].A1[i] = __ldg(reinterpret_cast<const int2*>(pc[i] + s * 32));
+          f[u].x0[i] = __ldg(xa[i] + s);
+          f[u].x1[i] = __ldg(xc[i] + s);
+        }
 #pragma unroll
         for (int t = 0; t < NT; t++) f[u].B[t] = __ldg(reinterpret_cast<const int2*>(pb[t] + s * 32));
-        f[u].x0 = __ldg(xa + s);
-        f[u].x1 = __ldg(xc + s);
       }
     }
   };
@@ -496,15 +508,10 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
     for (int u = 0; u < U; u++) {
       const int s = sb + u;
       if (s >= nsb) break;
-      const unsigned af[4] = {(unsigned)cur[u].A0.x, (unsigned)cur[u].A1.x, (unsigned)cur[u].A0.y,
-                              (unsigned)cur[u].A1.y};
-      const float x0 = cur[u].x0, x1 = cur[u].x1;
       const bool gend = !RB1 && (s + 1) % rb == 0;
       const int slot = s < (nsb & ~3) ? (s & 3) : 0;
 #pragma unroll
       for (int t = 0; t < NT; t++) {
-        int d[4];
-        mma_s8(d, af, (unsigned)cur[u].B[t].x, (unsigned)cur[u].B[t].y);
         float wg[2] = {wrow[t][0], wrow[t][1]};
         if (RB1) {
           wg[0] = __ldg(ws + (size_t)oc[t][0] * ng + s);
@@ -514,21 +521,28 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
           wg[1] = __ldg(ws + (size_t)oc[t][1] * ng + s / rb);
         }
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float a = i2f_small(d[e]);
-          const float xsv = e < 2 ? x0 : x1;
-          RedState<RB1>& R_ = st[t][e];
-          if (!RB1) {
-            R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
-            if (gend) {
-              R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[e & 1]));
-              R_.a[0] = 0.0f;
-            }
-          } else {
-            const float p = __fmul_rn(a, __fmul_rn(xsv, wg[e & 1]));
+        for (int i = 0; i < MT; i++) {
+          const unsigned af[4] = {(unsigned)cur[u].A0[i].x, (unsigned)cur[u].A1[i].x, (unsigned)cur[u].A0[i].y,
+                                  (unsigned)cur[u].A1[i].y};
+          int d[4];
+          mma_s8(d, af, (unsigned)cur[u].B[t].x, (unsigned)cur[u].B[t].y);
 #pragma unroll
-            for (int j = 0; j < (RB1 ? 4 : 2); j++)
-              if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
+          for (int e = 0; e < 4; e++) {
+            const float a = i2f_small(d[e]);
+            const float xsv = e < 2 ? cur[u].x0[i] : cur[u].x1[i];
+            RedState<RB1>& R_ = st[i][t][e];
+            if (!RB1) {
+              R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+              if (gend) {
+                R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[e & 1]));
+                R_.a[0] = 0.0f;
+              }
+            } else {
+              const float p = __fmul_rn(a, __fmul_rn(xsv, wg[e & 1]));
+#pragma unroll
+              for (int j = 0; j < (RB1 ? 4 : 2); j++)
+                if (j == slot) R_.a[j] = __fadd_rn(R_.a[j], p);
+            }
           }
         }
       }
@@ -538,45 +552,66 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
   }
 }
 
-// y (R x N, ld ldy) = [y +] W x (+ W2 x2) for R > 8 rows.  Block = 4 warps
-// along N; grid (ceil(N / (32 NT)), ceil(R / 16)).  Both weights of a dual
-// call share the group-size class (the launcher checks).
+// One m tile (the grouped expert kernels).
 template <int NT, bool RB1>
+LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws, int N, int K, int gs,
+                     const int8_t* __restrict__ xq, const float* __restrict__ xs, int ra, int rc,
+                     const int (&nb)[NT], RedState<RB1> (&st)[NT][4]) {
+  const int rav[1] = {ra}, rcv[1] = {rc};
+  wmma_pass_mt<1, NT, RB1>(W, ws, N, K, gs, xq, xs, rav, rcv, nb,
+                           *reinterpret_cast<RedState<RB1>(*)[1][NT][4]>(&st));
+}
+
+// y (R x N, ld ldy) = [y +] W x (+ W2 x2) for R > 8 rows.  Warp tile 16 MT
+// token rows x 8 NT outputs; block = 4 warps along N; grid
+// (ceil(N / (32 NT)), ceil(R / (16 MT))).  Both weights of a dual call share
+// the group-size class (the launcher checks).
+template <int MT, int NT, bool RB1, int UF = 0>
 __global__ void __launch_bounds__(128) gemm_q8_warp_kernel(const GemvArgs a) {
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
-  const int n0 = (blockIdx.x * 4 + warp) * 8 * NT, r0 = blockIdx.y * 16;
+  const int n0 = (blockIdx.x * 4 + warp) * 8 * NT, r0 = blockIdx.y * 16 * MT;
   if (n0 >= a.N) return;
-  RedState<RB1> st[NT][4];
-  int nb[NT];
+  RedState<RB1> st[MT][NT][4];
+  int nb[NT], ra[MT], rc[MT];
 #pragma unroll
   for (int t = 0; t < NT; t++) nb[t] = n0 + t * 8;
-  const int ra = min(r0 + gid, a.R - 1), rc = min(r0 + gid + 8, a.R - 1);
-  wmma_pass<NT, RB1>(a.W, a.ws, a.N, a.K, a.gs, a.xq, a.xs, ra, rc, nb, st);
-  float v[NT][4];
 #pragma unroll
-  for (int t = 0; t < NT; t++)
+  for (int i = 0; i < MT; i++) {
+    ra[i] = min(r0 + i * 16 + gid, a.R - 1);
+    rc[i] = min(r0 + i * 16 + gid + 8, a.R - 1);
+  }
+  wmma_pass_mt<MT, NT, RB1, UF>(a.W, a.ws, a.N, a.K, a.gs, a.xq, a.xs, ra, rc, nb, st);
+  float v[MT][NT][4];
 #pragma unroll
-    for (int e = 0; e < 4; e++) v[t][e] = mma_result(st[t][e]);
-  if (a.W2) {
-    wmma_pass<NT, RB1>(a.W2, a.ws2, a.N, a.K2, a.gs2, a.xq2, a.xs2, ra, rc, nb, st);
+  for (int i = 0; i < MT; i++)
 #pragma unroll
     for (int t = 0; t < NT; t++)
 #pragma unroll
-      for (int e = 0; e < 4; e++) v[t][e] = __fadd_rn(v[t][e], mma_result(st[t][e]));
+      for (int e = 0; e < 4; e++) v[i][t][e] = mma_result(st[i][t][e]);
+  if (a.W2) {
+    wmma_pass_mt<MT, NT, RB1, UF>(a.W2, a.ws2, a.N, a.K2, a.gs2, a.xq2, a.xs2, ra, rc, nb, st);
+#pragma unroll
+    for (int i = 0; i < MT; i++)
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[i][t][e] = __fadd_rn(v[i][t][e], mma_result(st[i][t][e]));
   }
 #pragma unroll
-  for (int t = 0; t < NT; t++)
+  for (int i = 0; i < MT; i++)
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int r = r0 + gid + (e >= 2 ? 8 : 0);
-      const int o = n0 + t * 8 + tq * 2 + (e & 1);
-      if (r < a.R && o < a.N) {
-        float* yp = a.y + (size_t)r * a.ldy + o;
-        *yp = a.mode == 1 ? __fadd_rn(*yp, v[t][e]) : v[t][e];
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int r = r0 + i * 16 + gid + (e >= 2 ? 8 : 0);
+        const int o = n0 + t * 8 + tq * 2 + (e & 1);
+        if (r < a.R && o < a.N) {
+          float* yp = a.y + (size_t)r * a.ldy + o;
+          *yp = a.mode == 1 ? __fadd_rn(*yp, v[i][t][e]) : v[i][t][e];
+        }
       }
-    }
 }
 
 // --------------------------------------------------------- row kernels
