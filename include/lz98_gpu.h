@@ -36,16 +36,20 @@ typedef struct {
     uint64_t rng_state;
 } LZSampler;
 
-/* LZErr codes used on this path (values of the reference's err.h). */
+/* LZErr codes used on this path, with the values of the reference's
+   err.h (src/err.h:19-...), plus two of this library's own above 1000. */
 enum {
     LZ98_ERR_OK = 0,
-    LZ98_ERR_NULL_ARG = 1,
-    LZ98_ERR_FORWARD = 2,
-    LZ98_ERR_SPEC_NO_HEAD = 3,
-    LZ98_ERR_SPEC_K_RANGE = 4,
-    LZ98_ERR_CUDA = 5,
-    LZ98_ERR_ALLOC = 6,
-    LZ98_ERR_MODEL = 7
+    LZ98_ERR_NULL_ARG = 6,
+    LZ98_ERR_ALLOC = 7,          /* LZ_ERR_STATE_ALLOC */
+    LZ98_ERR_FORWARD = 20,
+    LZ98_ERR_CKPT_EMPTY = 21,
+    LZ98_ERR_CKPT_STALE = 22,
+    LZ98_ERR_CKPT_SHAPE = 23,
+    LZ98_ERR_SPEC_NO_HEAD = 24,
+    LZ98_ERR_SPEC_K_RANGE = 25,
+    LZ98_ERR_CUDA = 1000,        /* a CUDA call failed */
+    LZ98_ERR_MODEL = 1001        /* model.bin not loadable by this library */
 };
 
 /* ---- model: replaces lz_open + lz_read_weights + lz_free
@@ -192,6 +196,29 @@ int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logit
    *out_hit = the index or -1. */
 int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *out_value,
                      int *out_hit);
+
+/* ---- recurrent-state checkpoints: replace lz_ckpt_alloc / lz_ckpt_free /
+   lz_ckpt_save / lz_ckpt_restore (src/forward.h:1847-1862,
+   src/forward_ckpt.c:75-342).  The checkpoint lives in device memory; it
+   holds the KDA state planes and scales and the conv history of the
+   state's current ring slot (the KV cache is not copied, as in the
+   reference), the saved position and the state's epoch.  Restore writes
+   ring slot 0 and points the ring there; it refuses an empty checkpoint
+   (LZ98_ERR_CKPT_EMPTY), a state reset or reallocated since the save
+   (LZ98_ERR_CKPT_STALE) and a shape mismatch (LZ98_ERR_CKPT_SHAPE).  The
+   reference signatures act on sequence 0; the _seq forms on any sequence
+   of a batched state. */
+typedef struct LZStateCkpt LZStateCkpt;
+int  lz_ckpt_alloc(LZStateCkpt **out, const LZModel *m, char *errbuf, int errlen);
+void lz_ckpt_free(LZStateCkpt *ck);
+int  lz_ckpt_save(LZStateCkpt *ck, const LZRunState *s, const LZModel *m, int pos,
+                  char *errbuf, int errlen);
+int  lz_ckpt_restore(const LZStateCkpt *ck, LZRunState *s, const LZModel *m, int *out_pos,
+                     char *errbuf, int errlen);
+int  lz_ckpt_save_seq(LZStateCkpt *ck, const LZRunState *s, int seq, int pos, char *errbuf,
+                      int errlen);
+int  lz_ckpt_restore_seq(const LZStateCkpt *ck, LZRunState *s, int seq, int *out_pos,
+                         char *errbuf, int errlen);
 
 /* Stream the library launches on (cudaStream_t, NULL = a private stream). */
 void *lz_state_stream(LZRunState *s);

@@ -380,6 +380,9 @@ struct LZRunState {
   std::vector<double> prof_bytes;
   std::map<int, cudaGraphExec_t> graph;
   std::vector<void*> allocs;
+  // 1 at allocation, +1 per reset (src/forward_state.c:1412,
+  // src/forward.c:782); a checkpoint records it and restore refuses a change
+  unsigned epoch = 1;
 };
 
 namespace {
@@ -601,7 +604,9 @@ static void clear_state(LZRunState* s) {
 }
 
 extern "C" void lz_state_reset(LZRunState* s, const LZModel*) {
-  if (s) clear_state(s);
+  if (!s) return;
+  clear_state(s);
+  s->epoch++;
 }
 
 static void sr_down(LZRunState* s) {
@@ -1405,7 +1410,7 @@ extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, i
     return LZ98_ERR_NULL_ARG;
   }
   const Cfg& c = m->c;
-  clear_state(s);
+  lz_state_reset(s, m);                     // src/generate.c:2813
   LZSampler samp{temp > 0.0f ? temp : 0.0f, topp, seed ? seed : 1ull};
   const bool use_temp = samp.temperature > kTempFloor;
   if (int rc = lz_seq_set_sampler(s, 0, samp.temperature, topp, samp.rng_state)) return rc;
@@ -1648,4 +1653,127 @@ extern "C" int lz_debug_seq_sum(const float* vals, int n, int mode, float target
   *out_value = h[0];
   memcpy(out_hit, &h[1], 4);
   return 0;
+}
+
+// =============================================================== checkpoints
+
+struct LZStateCkpt {
+  const LZModel* m = nullptr;
+  int8_t *hi = nullptr, *lo = nullptr;
+  float *sc = nullptr, *conv = nullptr;
+  size_t n_q = 0, n_conv = 0;          // element counts of one ring slot
+  int pos = -1;                        // -1: never saved into
+  unsigned epoch = 0;
+};
+
+extern "C" int lz_ckpt_alloc(LZStateCkpt** out, const LZModel* m, char* errbuf, int errlen) {
+  if (!out || !m) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const Cfg& c = m->c;
+  LZStateCkpt* ck = new LZStateCkpt();
+  ck->m = m;
+  ck->n_q = (size_t)c.nl * c.nv * c.kd * c.vd;
+  ck->n_conv = (size_t)c.nl * c.conv_dim * 3;
+  if (cudaMalloc(&ck->hi, ck->n_q) != cudaSuccess || cudaMalloc(&ck->lo, ck->n_q) != cudaSuccess ||
+      cudaMalloc(&ck->sc, ck->n_q / 32 * 4) != cudaSuccess || cudaMalloc(&ck->conv, ck->n_conv * 4) != cudaSuccess) {
+    lz_ckpt_free(ck);
+    set_err(errbuf, errlen, "device allocation failed");
+    return LZ98_ERR_ALLOC;
+  }
+  *out = ck;
+  return 0;
+}
+
+extern "C" void lz_ckpt_free(LZStateCkpt* ck) {
+  if (!ck) return;
+  cudaFree(ck->hi);
+  cudaFree(ck->lo);
+  cudaFree(ck->sc);
+  cudaFree(ck->conv);
+  delete ck;
+}
+
+extern "C" int lz_ckpt_save_seq(LZStateCkpt* ck, const LZRunState* cs, int seq, int pos, char* errbuf,
+                                int errlen) {
+  LZRunState* s = const_cast<LZRunState*>(cs);
+  if (!ck || !s || seq < 0 || seq >= s->B || pos < 0) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  if (ck->m != s->m || ck->n_q != s->q_slot || ck->n_conv != s->conv_slot) {
+    set_err(errbuf, errlen, "checkpoint does not match this model's shapes");
+    return LZ98_ERR_CKPT_SHAPE;
+  }
+  sr_down(s);
+  const int slot = s->h_sr[seq].ssm_slot;   // the live slot of the ring
+  const size_t oq = (size_t)seq * s->q_seq + (size_t)slot * s->q_slot;
+  const size_t oc = (size_t)seq * s->conv_seq + (size_t)slot * s->conv_slot;
+  if (cudaMemcpyAsync(ck->hi, s->hi + oq, ck->n_q, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(ck->lo, s->lo + oq, ck->n_q, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(ck->sc, s->sc + oq / 32, ck->n_q / 32 * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(ck->conv, s->conv + oc, ck->n_conv * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaStreamSynchronize(s->st) != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure while saving");
+    return LZ98_ERR_CUDA;
+  }
+  ck->pos = pos;
+  ck->epoch = s->epoch;
+  return 0;
+}
+
+extern "C" int lz_ckpt_restore_seq(const LZStateCkpt* ck, LZRunState* s, int seq, int* out_pos, char* errbuf,
+                                   int errlen) {
+  if (!ck || !s || seq < 0 || seq >= s->B) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  if (ck->pos < 0) {
+    set_err(errbuf, errlen, "checkpoint has never been saved into");
+    return LZ98_ERR_CKPT_EMPTY;
+  }
+  if (ck->epoch != s->epoch) {
+    set_err(errbuf, errlen, "run state was reset or reallocated since the save");
+    return LZ98_ERR_CKPT_STALE;
+  }
+  if (ck->m != s->m || ck->n_q != s->q_slot || ck->n_conv != s->conv_slot || ck->pos >= s->seq_len) {
+    set_err(errbuf, errlen, "checkpoint does not match this model's shapes");
+    return LZ98_ERR_CKPT_SHAPE;
+  }
+  const size_t oq = (size_t)seq * s->q_seq, oc = (size_t)seq * s->conv_seq;   // ring slot 0
+  if (cudaMemcpyAsync(s->hi + oq, ck->hi, ck->n_q, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(s->lo + oq, ck->lo, ck->n_q, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(s->sc + oq / 32, ck->sc, ck->n_q / 32 * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
+      cudaMemcpyAsync(s->conv + oc, ck->conv, ck->n_conv * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure while restoring");
+    return LZ98_ERR_CUDA;
+  }
+  sr_down(s);
+  s->h_sr[seq].ssm_slot = 0;
+  sr_up(s);
+  if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+    set_err(errbuf, errlen, "CUDA failure while restoring");
+    return LZ98_ERR_CUDA;
+  }
+  if (out_pos) *out_pos = ck->pos;
+  return 0;
+}
+
+extern "C" int lz_ckpt_save(LZStateCkpt* ck, const LZRunState* s, const LZModel* m, int pos, char* errbuf,
+                            int errlen) {
+  if (ck && s && m && m != s->m) {
+    set_err(errbuf, errlen, "checkpoint does not match this model's shapes");
+    return LZ98_ERR_CKPT_SHAPE;
+  }
+  return lz_ckpt_save_seq(ck, s, 0, pos, errbuf, errlen);
+}
+
+extern "C" int lz_ckpt_restore(const LZStateCkpt* ck, LZRunState* s, const LZModel* m, int* out_pos, char* errbuf,
+                               int errlen) {
+  if (ck && s && m && m != s->m) {
+    set_err(errbuf, errlen, "checkpoint does not match this model's shapes");
+    return LZ98_ERR_CKPT_SHAPE;
+  }
+  return lz_ckpt_restore_seq(ck, s, 0, out_pos, errbuf, errlen);
 }

@@ -78,6 +78,12 @@ def lib():
                                      P(ctypes.c_double), P(c_int)]),
         "lz_lm_head_static": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_state_stream": (c_void_p, [c_void_p]),
+        "lz_ckpt_alloc": (c_int, [P(c_void_p), c_void_p, c_char_p, c_int]),
+        "lz_ckpt_free": (None, [c_void_p]),
+        "lz_ckpt_save": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_char_p, c_int]),
+        "lz_ckpt_restore": (c_int, [c_void_p, c_void_p, c_void_p, P(c_int), c_char_p, c_int]),
+        "lz_ckpt_save_seq": (c_int, [c_void_p, c_void_p, c_int, c_int, c_char_p, c_int]),
+        "lz_ckpt_restore_seq": (c_int, [c_void_p, c_void_p, c_int, P(c_int), c_char_p, c_int]),
         "lz_debug_seq_sum": (c_int, [c_void_p, c_int, c_int, c_float, P(c_float), P(c_int)]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
     }
@@ -96,7 +102,9 @@ EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_s
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
            "lz_seq_prefill", "lz_seq_set_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
-           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static", "lz_debug_seq_sum"]
+           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static", "lz_debug_seq_sum",
+           "lz_ckpt_alloc", "lz_ckpt_free", "lz_ckpt_save", "lz_ckpt_restore", "lz_ckpt_save_seq",
+           "lz_ckpt_restore_seq"]
 
 
 class LZSampler(ctypes.Structure):
@@ -282,6 +290,34 @@ class State:
         if rc:
             raise LzError(f"generate failed ({rc}): {err.value.decode()}")
         return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()
+
+
+class Checkpoint:
+    """Device snapshot of one sequence's recurrent state (lz_ckpt_*)."""
+
+    def __init__(self, model: "Model"):
+        h = c_void_p()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_ckpt_alloc(ctypes.byref(h), model.h, err, 256)
+        if rc:
+            raise LzError(f"lz_ckpt_alloc failed ({rc}): {err.value.decode()}")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().lz_ckpt_free(self.h)
+            self.h = None
+
+    def save(self, state: "State", pos: int, seq: int = 0) -> int:
+        err = ctypes.create_string_buffer(256)
+        return lib().lz_ckpt_save_seq(self.h, state.h, seq, pos, err, 256)
+
+    def restore(self, state: "State", seq: int = 0):
+        """(rc, position)."""
+        err = ctypes.create_string_buffer(256)
+        pos = c_int(-1)
+        rc = lib().lz_ckpt_restore_seq(self.h, state.h, seq, ctypes.byref(pos), err, 256)
+        return rc, pos.value
 
 
 def debug_seq_sum(vals, mode=0, target=0.0):
