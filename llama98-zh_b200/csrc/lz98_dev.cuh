@@ -134,4 +134,77 @@ LZ_HD float random_f32(unsigned long long* st) {
 LZ_HD void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 LZ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ------------------------------------------------ TMA, mbarriers, ldmatrix
+
+LZ_HD uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+LZ_HD void mbar_init(uint32_t bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// make barrier initialisation visible to the async (TMA) proxy
+LZ_HD void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+LZ_HD void mbar_expect_tx(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+LZ_HD void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+LZ_HD bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+LZ_HD unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait until the phase of parity `parity` of the barrier has completed,
+// giving up after about a second (returns false): no wait in this library
+// can spin for ever.
+LZ_HD bool mbar_wait(uint32_t bar, uint32_t parity) {
+#pragma unroll 1
+  for (int i = 0; i < 256; i++)
+    if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+#pragma unroll 1
+  while (!mbar_try(bar, parity))
+    if (global_ns() - t0 > 1000000000ull) return false;
+  return true;
+}
+// 2-D tiled TMA load of the box at (x, y) (x in elements of the innermost
+// dimension) into shared memory, completing on the barrier.
+LZ_HD void tma_load_2d(uint32_t dst, const void* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+LZ_HD void ldsm_x4(uint32_t addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+LZ_HD void ldsm_x2(uint32_t addr, unsigned& r0, unsigned& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// Ask L2 to fetch [p, p + bytes) from HBM without waiting (bulk prefetch,
+// sm_90+).  p must be 16-byte aligned; the range is cut down to whole
+// 16-byte units so that it never reaches past the caller's buffer.
+LZ_HD void prefetch_l2(const void* p, size_t bytes) {
+  const char* c = static_cast<const char*>(p);
+  bytes &= ~(size_t)15;
+  while (bytes) {
+    const unsigned n = bytes > 65536 ? 65536u : (unsigned)bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+    c += n;
+    bytes -= n;
+  }
+}
+
 }  // namespace lz98

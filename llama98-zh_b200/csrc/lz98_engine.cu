@@ -4,6 +4,7 @@
 // (body verify forward, MTP draft step, MTP prefill/catch-up) and the C ABI
 // declared in include/lz98_gpu.h.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cmath>
 #include <cstdio>
@@ -13,6 +14,7 @@
 #include <initializer_list>
 #include <map>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/lz98_gpu.h"
@@ -383,7 +385,21 @@ struct LZRunState {
   // 1 at allocation, +1 per reset (src/forward_state.c:1412,
   // src/forward.c:782); a checkpoint records it and restore refuses a change
   unsigned epoch = 1;
+  // TMA descriptors of the staged GEMM by (base, inner extent, rows, box
+  // inner, box rows); built on first use, baked into captured graphs
+  std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> tmaps;
+  // device-side error word in mapped pinned memory: set by a kernel whose
+  // bounded wait gave up; read after every synchronisation
+  int* h_err = nullptr;
+  int* d_err = nullptr;
 };
+
+// Wait for the state's stream; false on a CUDA error or when a kernel
+// reported a wait that gave up (the error word stays set until the state
+// is freed: the run state is then not trustworthy).
+static bool sync_ok(const LZRunState* s) {
+  return cudaStreamSynchronize(s->st) == cudaSuccess && !(s->h_err && *(volatile int*)s->h_err);
+}
 
 namespace {
 
@@ -404,6 +420,21 @@ void launch(LZRunState* s, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t
   cfg.numAttrs = s->pdl ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   s->launches++;
+}
+
+// Every TMA GEMM variant the launcher uses, with its dynamic shared memory
+// (the limit is raised for each at state allocation).
+template <typename F>
+void tma_variants(F f) {
+  f(gemm_q8_tma_kernel<1, 1, true, 0>, TmaTile<1, 1, true>::smem());
+  f(gemm_q8_tma_kernel<1, 2, true, 0>, TmaTile<1, 2, true>::smem());
+  f(gemm_q8_tma_kernel<2, 1, true, 0>, TmaTile<2, 1, true>::smem());
+  f(gemm_q8_tma_kernel<1, 1, false, 1>, TmaTile<1, 1, false>::smem());
+  f(gemm_q8_tma_kernel<1, 2, false, 1>, TmaTile<1, 2, false>::smem());
+  f(gemm_q8_tma_kernel<2, 1, false, 1>, TmaTile<2, 1, false>::smem());
+  f(gemm_q8_tma_kernel<1, 1, false, 2>, TmaTile<1, 1, false>::smem());
+  f(gemm_q8_tma_kernel<1, 2, false, 2>, TmaTile<1, 2, false>::smem());
+  f(gemm_q8_tma_kernel<2, 1, false, 2>, TmaTile<2, 1, false>::smem());
 }
 
 template <typename T>
@@ -468,6 +499,13 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
     set_err(errbuf, errlen, "cudaStreamCreate failed");
     return LZ98_ERR_CUDA;
   }
+  if (cudaHostAlloc((void**)&s->h_err, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer((void**)&s->d_err, s->h_err, 0) != cudaSuccess) {
+    set_err(errbuf, errlen, "cannot map the device error word");
+    lz_state_free(s);
+    return LZ98_ERR_ALLOC;
+  }
+  *s->h_err = 0;
   s->q_slot = (size_t)c.nl * c.nv * c.kd * c.vd;
   s->q_seq = s->q_slot * s->depth;
   s->conv_slot = (size_t)c.nl * c.conv_dim * 3;
@@ -521,6 +559,15 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
     auto attr = [gdyn](auto kern) {
       return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gdyn) == cudaSuccess;
     };
+    bool tma_ok = true;
+    tma_variants([&](auto kern, size_t bytes) {
+      tma_ok = tma_ok && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess;
+    });
+    if (!tma_ok) {
+      set_err(errbuf, errlen, "cannot raise the TMA GEMM shared-memory limit");
+      lz_state_free(s);
+      return LZ98_ERR_CUDA;
+    }
     if (!attr(gemv_q8_kernel<1, kGemvProWarps, 1, true, false>) || !attr(gemv_q8_kernel<1, kGemvProWarps, 4, true, false>) ||
         !attr(gemv_q8_kernel<1, kGemvProWarps, 8, true, false>) || !attr(gemv_q8_kernel<2, kGemvProWarps, 1, true, false>) ||
         !attr(gemv_q8_kernel<2, kGemvProWarps, 4, true, false>) || !attr(gemv_q8_kernel<2, kGemvProWarps, 8, true, false>)) {
@@ -572,6 +619,7 @@ extern "C" void lz_state_free(LZRunState* s) {
   if (!s) return;
   for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
   for (void* p : s->allocs) cudaFree(p);
+  if (s->h_err) cudaFreeHost(s->h_err);
   if (s->st) cudaStreamDestroy(s->st);
   delete s;
 }
@@ -641,14 +689,14 @@ extern "C" int lz_state_get_chain(const LZRunState* s, int seq, float* chain) {
   if (!s || !chain || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
   const int d = s->m->c.d;
   cudaMemcpyAsync(chain, s->chain + (size_t)seq * d, d * 4, cudaMemcpyDeviceToHost, s->st);
-  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+  return sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" int lz_state_set_chain(LZRunState* s, int seq, const float* chain) {
   if (!s || !chain || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
   const int d = s->m->c.d;
   cudaMemcpyAsync(s->chain + (size_t)seq * d, chain, d * 4, cudaMemcpyHostToDevice, s->st);
-  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+  return sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" void* lz_state_stream(LZRunState* s) { return s ? (void*)s->st : nullptr; }
@@ -718,6 +766,105 @@ void gemv_launch_rb(LZRunState* s, const GemvArgs& a) {
   else gemv_launch<JM, WARPS, 8, PRO, false>(s, a);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+PFN_cuTensorMapEncodeTiled_v12000 tma_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// The 2-D TMA map of a row-major operand, cached per state: int8 rows of
+// `inner` bytes in 128-byte boxes with the 128-byte swizzle (box_inner
+// 128), or f32 rows of `inner` floats in 16-byte boxes (box_inner 4).
+// Rows past `rows` read as zeros.
+const CUtensorMap* tmap(LZRunState* s, const void* base, int inner, int rows, int box_inner, int box_rows) {
+  const auto key = std::make_tuple(base, inner, rows, box_inner, box_rows);
+  auto it = s->tmaps.find(key);
+  if (it != s->tmaps.end()) return &it->second;
+  auto enc = tma_encoder();
+  if (!enc) return nullptr;
+  const bool f32 = box_inner == 4;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t stride[1] = {(cuuint64_t)inner * (f32 ? 4 : 1)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows}, es[2] = {1, 1};
+  if (enc(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+          stride, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return nullptr;
+  return &(s->tmaps[key] = m);
+}
+
+template <int MT, int NT, bool RB1, int GM>
+void tma_launch(LZRunState* s, const GemmTmaArgs& a) {
+  using T = TmaTile<MT, NT, RB1>;
+  launch(s, gemm_q8_tma_kernel<MT, NT, RB1, GM>, dim3((a.N + T::BN - 1) / T::BN, (a.R + T::BM - 1) / T::BM), dim3(288),
+         T::smem(), a);
+}
+
+// R > 8 token rows with K (and K2) % 128 == 0: the TMA-staged tensor-core
+// GEMM.  Tiles: 32-row token tiles while the grid stays within ~4 blocks
+// per SM, 64-row ones above; 64-output tiles for the wide lm_head at
+// R <= 32.  False when the shape does not fit (the caller then launches
+// the warp-tile kernel).
+bool gemm_tma(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, float* y, int ldy, int mode,
+              const QW* w2, const int8_t* xq2, const float* xs2) {
+  if (w.in % 128 || (w2 && w2->in % 128)) return false;
+  const bool rb1 = w.gs == 32;
+  const int GM = rb1 ? 0 : (w.gs == w.in && (!w2 || w2->gs == w2->in)) ? 1 : 2;
+  int MT = 1, NT = 1;
+  if (R <= 32) NT = w.out >= 8192 ? 2 : 1;
+  else MT = (long)((w.out + 31) / 32) * ((R + 31) / 32) <= 4L * s->n_sm ? 1 : 2;
+  const int BM = 32 * MT, BN = 32 * NT;
+  GemmTmaArgs a;
+  memset(&a, 0, sizeof(a));
+  const CUtensorMap* m[8] = {tmap(s, xq, w.in, R, 128, BM), tmap(s, xs, w.in / 32, R, 4, BM),
+                             tmap(s, w.q, w.in, w.out, 128, BN), rb1 ? tmap(s, w.s, w.in / 32, w.out, 4, BN) : nullptr,
+                             nullptr, nullptr, nullptr, nullptr};
+  if (w2) {
+    m[4] = tmap(s, xq2, w2->in, R, 128, BM);
+    m[5] = tmap(s, xs2, w2->in / 32, R, 4, BM);
+    m[6] = tmap(s, w2->q, w2->in, w.out, 128, BN);
+    m[7] = rb1 ? tmap(s, w2->s, w2->in / 32, w.out, 4, BN) : nullptr;
+  }
+  for (int i = 0; i < (w2 ? 8 : 4); i++)
+    if (!m[i] && (rb1 || (i & 3) != 3)) return false;
+  a.a = *m[0]; a.x = *m[1]; a.b = *m[2];
+  if (rb1) a.w = *m[3];
+  if (w2) {
+    a.a2 = *m[4]; a.x2 = *m[5]; a.b2 = *m[6];
+    if (rb1) a.w2 = *m[7];
+  }
+  a.ws = w.s; a.ws2 = w2 ? w2->s : nullptr; a.W = w.q; a.W2 = w2 ? w2->q : nullptr;
+  a.y = y; a.err = s->d_err;
+  a.N = w.out; a.K = w.in; a.gs = w.gs; a.K2 = w2 ? w2->in : 0; a.gs2 = w2 ? w2->gs : 32;
+  a.R = R; a.ldy = ldy; a.mode = mode; a.dual = w2 ? 1 : 0;
+  const int v = MT * 10 + NT;
+  if (GM == 0) {
+    if (v == 11) tma_launch<1, 1, true, 0>(s, a);
+    else if (v == 12) tma_launch<1, 2, true, 0>(s, a);
+    else tma_launch<2, 1, true, 0>(s, a);
+  } else if (GM == 1) {
+    if (v == 11) tma_launch<1, 1, false, 1>(s, a);
+    else if (v == 12) tma_launch<1, 2, false, 1>(s, a);
+    else tma_launch<2, 1, false, 1>(s, a);
+  } else {
+    if (v == 11) tma_launch<1, 1, false, 2>(s, a);
+    else if (v == 12) tma_launch<1, 2, false, 2>(s, a);
+    else tma_launch<2, 1, false, 2>(s, a);
+  }
+  return true;
+}
+
 // y (R x N, ld ldy) = [y +] W x (+ W2 x2).  With `nin`, x is produced here
 // from the float rows nin->x by RMSNorm + quantisation: inside the GEMV
 // (every block, from shared memory) for R <= kPrologueRows, else by one
@@ -751,7 +898,9 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
     s->prof_bytes.push_back(b);
   }
   const bool rb1 = w.gs == 32;
-  if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
+  if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1) && gemm_tma(s, w, xq, xs, R, y, ldy, mode, w2, xq2, xs2)) {
+    // launched
+  } else if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
     // tensor-core warp tiles of 16 MT token rows x 8 NT outputs (measured
     // best: 32 x 16 for wide outputs, 32 x 8 for narrow ones, 16-row tiles
     // when R <= 16)
@@ -1002,8 +1151,7 @@ int sample_row(LZRunState* s, int seq, int* tok) {
   launch(s, sample_row_kernel, dim3(1), dim3(kSampThreads), kSampSmem, s->logits, c.vocab, s->sr, seq, s->pbuf,
          s->sortbuf, s->npow2, s->tok_out);
   CK(cudaMemcpyAsync(tok, s->tok_out, sizeof(int), cudaMemcpyDeviceToHost, s->st));
-  CK(cudaStreamSynchronize(s->st));
-  return 0;
+  return sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
 }  // namespace
@@ -1040,7 +1188,7 @@ static float* forward_one(const LZModel* m, LZRunState* s, const int* tokens, in
       cudaMemcpyAsync(s->chain, s->hidden + (size_t)(R - 1) * c.d, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
     done += R;
   }
-  if (cudaStreamSynchronize(s->st) != cudaSuccess) return nullptr;
+  if (!sync_ok(s)) return nullptr;
   return last;
 }
 
@@ -1072,7 +1220,7 @@ extern "C" int lz_forward_verify(const LZModel* m, LZRunState* s, const int* tok
   cudaMemcpyAsync(s->h_hidden.data(), s->hidden, (size_t)n * c.d * 4, cudaMemcpyDeviceToHost, s->st);
   s->h_sr[0].ssm_slot = (slot + n) % s->depth;
   sr_up(s);
-  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : 1;
+  return sync_ok(s) ? 0 : 1;
 }
 
 extern "C" const float* lz_state_mtp_logits(const LZRunState* s) { return s ? s->h_logits.data() : nullptr; }
@@ -1088,7 +1236,7 @@ extern "C" float* lz_mtp_draft_step(const LZModel* m, LZRunState* s, int next_to
   launch(s, set_rows_kernel, dim3(1), dim3(32), 0, s->mrows, 1, 0, pos, s->seq_len);
   mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
   cudaMemcpyAsync(s->h_draft.data(), s->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
-  if (cudaStreamSynchronize(s->st) != cudaSuccess) return nullptr;
+  if (!sync_ok(s)) return nullptr;
   return s->h_draft.data();
 }
 
@@ -1107,7 +1255,7 @@ static int mtp_prefill_seq(LZRunState* s, int seq, const float* h_host, const fl
     mtp_forward(s, R, s->catch_tok, hid, nullptr, s->crows, false, nullptr);
     done += R;
   }
-  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : 1;
+  return sync_ok(s) ? 0 : 1;
 }
 
 extern "C" int lz_mtp_prefill(const LZModel* m, LZRunState* s, const float* h_body_all, const int* next_tokens,
@@ -1222,7 +1370,7 @@ extern "C" int lz_seq_set_sampler(LZRunState* s, int seq, float temperature, flo
   r.rng = seed ? seed : 1ull;                         // src/sampler.c:55-60
   s->seq_temp[seq] = r.temp > kTempFloor;
   sr_up(s);
-  return cudaStreamSynchronize(s->st) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+  return sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
@@ -1514,7 +1662,7 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   round_any(s, k);
   cudaEventRecord(r1, s->st);
   s->prof = false;
-  if (cudaStreamSynchronize(s->st) != cudaSuccess) return LZ98_ERR_CUDA;
+  if (!sync_ok(s)) return LZ98_ERR_CUDA;
   double gt = 0.0, gb = 0.0;
   for (size_t i = 0; i < s->prof_bytes.size(); i++) {
     float ms = 0.0f;
@@ -1714,7 +1862,7 @@ extern "C" int lz_ckpt_save_seq(LZStateCkpt* ck, const LZRunState* cs, int seq, 
       cudaMemcpyAsync(ck->lo, s->lo + oq, ck->n_q, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
       cudaMemcpyAsync(ck->sc, s->sc + oq / 32, ck->n_q / 32 * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
       cudaMemcpyAsync(ck->conv, s->conv + oc, ck->n_conv * 4, cudaMemcpyDeviceToDevice, s->st) != cudaSuccess ||
-      cudaStreamSynchronize(s->st) != cudaSuccess) {
+      !sync_ok(s)) {
     set_err(errbuf, errlen, "CUDA failure while saving");
     return LZ98_ERR_CUDA;
   }
@@ -1752,7 +1900,7 @@ extern "C" int lz_ckpt_restore_seq(const LZStateCkpt* ck, LZRunState* s, int seq
   sr_down(s);
   s->h_sr[seq].ssm_slot = 0;
   sr_up(s);
-  if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+  if (!sync_ok(s)) {
     set_err(errbuf, errlen, "CUDA failure while restoring");
     return LZ98_ERR_CUDA;
   }

@@ -15,6 +15,7 @@
 // memory so the chain runs at add latency); integer sums (int8 dot
 // products per 32-element sub-block) are order-free and run as __dp4a.
 #pragma once
+#include <cuda.h>   // CUtensorMap (the type only; maps are encoded through the runtime's driver entry point)
 #include "lz98_dev.cuh"
 
 namespace lz98 {
@@ -569,9 +570,21 @@ LZ_HD void wmma_pass(const int8_t* __restrict__ W, const float* __restrict__ ws,
 template <int MT, int NT, bool RB1, int UF = 0>
 __global__ void __launch_bounds__(128) gemm_q8_warp_kernel(const GemvArgs a) {
   pdl_trigger();
-  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
   const int n0 = (blockIdx.x * 4 + warp) * 8 * NT, r0 = blockIdx.y * 16 * MT;
+  // the weights do not depend on the producing kernel: the warp's rows of
+  // both weights start streaming into L2 before the wait (once per n
+  // range, by the first token tile's warps)
+  if (n0 < a.N && blockIdx.y == 0 && lane == 0) {
+    const int rows = min(8 * NT, a.N - n0);
+    prefetch_l2(a.W + (size_t)n0 * a.K, (size_t)rows * a.K);
+    prefetch_l2(a.ws + (size_t)n0 * (a.K / a.gs), (size_t)rows * (a.K / a.gs) * 4);
+    if (a.W2) {
+      prefetch_l2(a.W2 + (size_t)n0 * a.K2, (size_t)rows * a.K2);
+      prefetch_l2(a.ws2 + (size_t)n0 * (a.K2 / a.gs2), (size_t)rows * (a.K2 / a.gs2) * 4);
+    }
+  }
+  pdl_wait();
   if (n0 >= a.N) return;
   RedState<RB1> st[MT][NT][4];
   int nb[NT], ra[MT], rc[MT];
@@ -610,6 +623,269 @@ __global__ void __launch_bounds__(128) gemm_q8_warp_kernel(const GemvArgs a) {
         if (r < a.R && o < a.N) {
           float* yp = a.y + (size_t)r * a.ldy + o;
           *yp = a.mode == 1 ? __fadd_rn(*yp, v[i][t][e]) : v[i][t][e];
+        }
+      }
+}
+
+// ------------------------------------------- TMA-staged tensor-core GEMM
+//
+// The same products and epilogue as gemm_q8_warp_kernel, with the operands
+// staged in shared memory instead of loaded fragment by fragment from
+// global memory (whose 8-row scattered loads kept the L1 pipe busy and the
+// warps waiting).  A block of 8 consumer warps (2 along tokens x 4 along
+// outputs, warp tile 16 MT x 8 NT) shares one token tile of 32 MT rows and
+// one output tile of 32 NT rows; a producer warp streams 128-byte K slices
+// of both (4 sub-blocks) with 2-D TMA loads into a ring of kTmaStages
+// stages (128-byte swizzle, so the ldmatrix fragment reads are free of bank
+// conflicts), with the per-32 activation scales (and, for gs = 32, the
+// weight scales) as 16-byte boxes beside them.  Full / empty mbarriers pace
+// the ring; every wait is bounded and a timeout sets *err and skips the
+// stores.  Requires K (and K2) % 128 == 0.
+#ifndef LZ_TMA_STAGES
+#define LZ_TMA_STAGES 4
+#endif
+constexpr int kTmaStages = LZ_TMA_STAGES;
+constexpr int kTmaSub = 4;   // 32-byte sub-blocks per stage
+
+struct alignas(64) GemmTmaArgs {
+  CUtensorMap a, x, b, w;      // xq [rows][K] u8, xs [rows][K/32] f32, W [N][K] u8, ws [N][K/32] f32 (gs = 32)
+  CUtensorMap a2, x2, b2, w2;  // second product over the same outputs
+  const float* ws;             // weight scales, read directly when gs > 32
+  const float* ws2;
+  const int8_t* W;             // weight rows, for the L2 prefetch
+  const int8_t* W2;
+  float* y;
+  int* err;
+  int N, K, gs, K2, gs2, R, ldy, mode, dual;
+};
+
+LZ_HD float f4_at(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+template <int MT, int NT, bool RB1>
+struct TmaTile {
+  static constexpr int BM = 32 * MT, BN = 32 * NT;
+  static constexpr int A = BM * 128, B = BN * 128, X = BM * 16, W = RB1 ? BN * 16 : 0;
+  static constexpr int TILES = A + B;  // swizzled tiles of one stage (multiple of 1024 bytes)
+  static constexpr int SMALL = X + W;  // scale boxes of one stage
+  static constexpr size_t smem() { return 1024 + (size_t)kTmaStages * (TILES + SMALL) + 2 * kTmaStages * 8; }
+};
+
+// Consumer side of one product: pipeline iterations [itb, ite) (K slices
+// c = it - itb) accumulated into st.  GM is the weight-scale class: 0 for
+// gs = 32 (RB1), 1 for one group per row (gs = K), 2 for anything between.
+// False on a barrier timeout.
+template <int MT, int NT, bool RB1, int GM>
+LZ_HD bool tma_pass(uint32_t base, const uint8_t* gsmall, uint32_t bars, int itb, int ite, int gs, int K,
+                    const float* __restrict__ ws, int N, int n0, RedState<RB1> (&st)[MT][NT][4]) {
+  using T = TmaTile<MT, NT, RB1>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int wm = warp >> 2, wn = warp & 3;
+  const int rb = gs >> 5, ng = K / gs;
+  int oc[NT][2];
+  float wrow[NT][2];
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      oc[t][j] = min(n0 + wn * 8 * NT + t * 8 + tq * 2 + j, N - 1);
+      wrow[t][j] = GM == 1 ? __ldg(ws + oc[t][j]) : 0.0f;
+    }
+#pragma unroll
+  for (int i = 0; i < MT; i++)
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+#pragma unroll
+        for (int j = 0; j < (RB1 ? 4 : 2); j++) st[i][t][e].a[j] = 0.0f;
+  int gcnt = 0, gidx = 0;
+  // lane addresses inside a stage (row & 7 == lane & 7 for every fragment row)
+  const int sw = lane & 7;
+  uint32_t aoff[MT];
+#pragma unroll
+  for (int i = 0; i < MT; i++) aoff[i] = (uint32_t)(wm * 16 * MT + i * 16 + sw + (((lane >> 3) & 1) << 3)) * 128u;
+  const int ach = lane >> 4;
+  const uint32_t boff = (uint32_t)T::A + (uint32_t)(wn * 8 * NT + (NT == 2 ? ((lane >> 4) << 3) : 0) + sw) * 128u;
+  const int bch = (lane >> 3) & 1;
+#pragma unroll 1
+  for (int it = itb; it < ite; it++) {
+    const int stg = it % kTmaStages;
+    if (!mbar_wait(bars + 8 * stg, (it / kTmaStages) & 1)) return false;
+    const uint32_t tile = base + stg * T::TILES;
+    const float* xsm = reinterpret_cast<const float*>(gsmall + stg * T::SMALL);
+    const float* wsm = xsm + T::BM * 4;
+    // the stage's 4 sub-blocks: fragments and scales first, then the math
+    unsigned bf[kTmaSub][NT][2], af[kTmaSub][MT][4];
+    float4 xv[MT][2];
+#pragma unroll
+    for (int sl = 0; sl < kTmaSub; sl++) {
+      if (NT == 2)
+        ldsm_x4(tile + boff + ((uint32_t)((2 * sl + bch) ^ sw) << 4), bf[sl][0][0], bf[sl][0][1], bf[sl][NT - 1][0],
+                bf[sl][NT - 1][1]);
+      else
+        ldsm_x2(tile + boff + ((uint32_t)((2 * sl + bch) ^ sw) << 4), bf[sl][0][0], bf[sl][0][1]);
+#pragma unroll
+      for (int i = 0; i < MT; i++)
+        ldsm_x4(tile + aoff[i] + ((uint32_t)((2 * sl + ach) ^ sw) << 4), af[sl][i][0], af[sl][i][1], af[sl][i][2],
+                af[sl][i][3]);
+    }
+#pragma unroll
+    for (int i = 0; i < MT; i++) {
+      const int rr = wm * 16 * MT + i * 16 + gid;
+      xv[i][0] = *reinterpret_cast<const float4*>(xsm + rr * 4);
+      xv[i][1] = *reinterpret_cast<const float4*>(xsm + (rr + 8) * 4);
+    }
+    float4 wv[NT][2];
+    if (RB1) {
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) wv[t][j] = *reinterpret_cast<const float4*>(wsm + (wn * 8 * NT + t * 8 + tq * 2 + j) * 4);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + 8 * (kTmaStages + stg));   // the stage is in registers: release it
+#pragma unroll
+    for (int sl = 0; sl < kTmaSub; sl++) {
+      bool gend = false;
+      float wg[NT][2];
+      if (GM == 1) {
+        gend = (it - itb) * kTmaSub + sl == (K >> 5) - 1;
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+          for (int j = 0; j < 2; j++) wg[t][j] = wrow[t][j];
+      } else if (GM == 2) {
+        gend = ++gcnt == rb;
+        if (gend) {
+          gcnt = 0;
+#pragma unroll
+          for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) wg[t][j] = __ldg(ws + (size_t)oc[t][j] * ng + gidx);
+          gidx++;
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+          for (int j = 0; j < 2; j++) wg[t][j] = f4_at(wv[t][j], sl);
+      }
+#pragma unroll
+      for (int i = 0; i < MT; i++) {
+        const float x0 = f4_at(xv[i][0], sl), x1 = f4_at(xv[i][1], sl);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+          int d[4];
+          mma_s8(d, af[sl][i], bf[sl][t][0], bf[sl][t][1]);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float a = i2f_small(d[e]);
+            const float xsv = e < 2 ? x0 : x1;
+            RedState<RB1>& R_ = st[i][t][e];
+            if (!RB1) {
+              R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+              if (gend) {
+                R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[t][e & 1]));
+                R_.a[0] = 0.0f;
+              }
+            } else {
+              // K % 128 == 0: the interleaved accumulator of sub-block s is s & 3 == sl
+              R_.a[sl] = __fadd_rn(R_.a[sl], __fmul_rn(a, __fmul_rn(xsv, wg[t][e & 1])));
+            }
+          }
+        }
+      }
+    }
+  }
+  return true;
+}
+
+template <int MT, int NT, bool RB1, int GM>
+__global__ void __launch_bounds__(288) gemm_q8_tma_kernel(const __grid_constant__ GemmTmaArgs p) {
+  using T = TmaTile<MT, NT, RB1>;
+  extern __shared__ uint8_t tma_smem[];
+  const uint32_t raw = smem_u32(tma_smem);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t small = base + kTmaStages * T::TILES;
+  const uint32_t bars = small + kTmaStages * T::SMALL;  // full[s] at +8s, empty[s] at +8(kTmaStages + s)
+  const uint8_t* gsmall = tma_smem + (small - raw);
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * T::BN, r0 = blockIdx.y * T::BM;
+  const int nsb = p.K >> 5, nsb2 = p.dual ? p.K2 >> 5 : 0;
+  const int it1 = (nsb + kTmaSub - 1) / kTmaSub, nit = it1 + (nsb2 + kTmaSub - 1) / kTmaSub;
+  if (warp == 8 && lane == 0 && blockIdx.y == 0) {  // weights stream into L2 before the wait
+    const int rows = min(T::BN, p.N - n0);
+    prefetch_l2(p.W + (size_t)n0 * p.K, (size_t)rows * p.K);
+    if (p.dual) prefetch_l2(p.W2 + (size_t)n0 * p.K2, (size_t)rows * p.K2);
+  }
+  pdl_wait();
+  if (threadIdx.x == 256) {
+    for (int s = 0; s < kTmaStages; s++) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (kTmaStages + s), 8);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 8) {
+    if (lane != 0) return;
+    bool ok = true;
+    int it = 0;
+    for (; it < nit; it++) {
+      const int stg = it % kTmaStages;
+      if (it >= kTmaStages && !mbar_wait(bars + 8 * (kTmaStages + stg), (it / kTmaStages - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const bool two = it >= it1;
+      const int c = two ? it - it1 : it;
+      const uint32_t full = bars + 8 * stg, tile = base + stg * T::TILES, sm = small + stg * T::SMALL;
+      mbar_expect_tx(full, T::A + T::B + T::X + T::W);
+      tma_load_2d(tile, two ? &p.a2 : &p.a, c * 128, r0, full);
+      tma_load_2d(tile + T::A, two ? &p.b2 : &p.b, c * 128, n0, full);
+      tma_load_2d(sm, two ? &p.x2 : &p.x, c * kTmaSub, r0, full);
+      if (RB1) tma_load_2d(sm + T::X, two ? &p.w2 : &p.w, c * kTmaSub, n0, full);
+    }
+    if (!ok) atomicExch(p.err, 1);
+    // every copy issued lands before the block exits
+    for (int j = max(0, it - kTmaStages); j < it; j++) mbar_wait(bars + 8 * (j % kTmaStages), (j / kTmaStages) & 1);
+    return;
+  }
+  RedState<RB1> st[MT][NT][4];
+  float v[MT][NT][4];
+  bool ok = tma_pass<MT, NT, RB1, GM>(base, gsmall, bars, 0, it1, p.gs, p.K, p.ws, p.N, n0, st);
+#pragma unroll
+  for (int i = 0; i < MT; i++)
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) v[i][t][e] = mma_result(st[i][t][e]);
+  if (ok && p.dual) {
+    ok = tma_pass<MT, NT, RB1, GM>(base, gsmall, bars, it1, nit, p.gs2, p.K2, p.ws2, p.N, n0, st);
+#pragma unroll
+    for (int i = 0; i < MT; i++)
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[i][t][e] = __fadd_rn(v[i][t][e], mma_result(st[i][t][e]));
+  }
+  if (!ok) {
+    atomicExch(p.err, 1);
+    return;
+  }
+  const int wm = warp >> 2, wn = warp & 3, gid = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int i = 0; i < MT; i++)
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int r = r0 + wm * 16 * MT + i * 16 + gid + (e >= 2 ? 8 : 0);
+        const int o = n0 + wn * 8 * NT + t * 8 + tq * 2 + (e & 1);
+        if (r < p.R && o < p.N) {
+          float* yp = p.y + (size_t)r * p.ldy + o;
+          *yp = p.mode == 1 ? __fadd_rn(*yp, v[i][t][e]) : v[i][t][e];
         }
       }
 }
@@ -1227,6 +1503,14 @@ moe_w13_group_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ 
   const int j0 = (blockIdx.x * 4 + warp) * 32;
   if (j0 >= ffn) return;
   const int ng = latent / gs;
+  if (lane == 0) {   // the rest of the warp's w1 and w3 rows stream into L2 meanwhile
+    const size_t eo = (size_t)T.e * 2 * ffn;
+    const int rows = min(32, ffn - j0);
+    prefetch_l2(w13q + (eo + j0) * latent, (size_t)rows * latent);
+    prefetch_l2(w13q + (eo + ffn + j0) * latent, (size_t)rows * latent);
+    prefetch_l2(w13s + (eo + j0) * ng, (size_t)rows * ng * 4);
+    prefetch_l2(w13s + (eo + ffn + j0) * ng, (size_t)rows * ng * 4);
+  }
   const int pa = list[T.start + min(gid, T.count - 1)], pc = list[T.start + min(gid + 8, T.count - 1)];
   int nb[8];
 #pragma unroll
@@ -1285,6 +1569,11 @@ moe_w2_group_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2
   const int n0 = (blockIdx.x * 4 + warp) * 16;
   if (n0 >= latent) return;
   const int ng = ffn / gs;
+  if (lane == 0) {
+    const int rows = min(16, latent - n0);
+    prefetch_l2(w2q + ((size_t)T.e * latent + n0) * ffn, (size_t)rows * ffn);
+    prefetch_l2(w2s + ((size_t)T.e * latent + n0) * ng, (size_t)rows * ng * 4);
+  }
   const int pa = list[T.start + min(gid, T.count - 1)], pc = list[T.start + min(gid + 8, T.count - 1)];
   int nb[2] = {n0, n0 + 8};
   RedState<RB1> st[2][4];
