@@ -435,6 +435,12 @@ void tma_variants(F f) {
   f(gemm_q8_tma_kernel<1, 1, false, 2>, TmaTile<1, 1, false>::smem());
   f(gemm_q8_tma_kernel<1, 2, false, 2>, TmaTile<1, 2, false>::smem());
   f(gemm_q8_tma_kernel<2, 1, false, 2>, TmaTile<2, 1, false>::smem());
+  f(moe_tma_kernel<true, true, 0>, MoeTma<true, true>::smem(MoeTma<true, true>::KMAX));
+  f(moe_tma_kernel<true, false, 1>, MoeTma<true, false>::smem(MoeTma<true, false>::KMAX));
+  f(moe_tma_kernel<true, false, 2>, MoeTma<true, false>::smem(MoeTma<true, false>::KMAX));
+  f(moe_tma_kernel<false, true, 0>, MoeTma<false, true>::smem(MoeTma<false, true>::KMAX));
+  f(moe_tma_kernel<false, false, 1>, MoeTma<false, false>::smem(MoeTma<false, false>::KMAX));
+  f(moe_tma_kernel<false, false, 2>, MoeTma<false, false>::smem(MoeTma<false, false>::KMAX));
 }
 
 template <typename T>
@@ -540,7 +546,7 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4);
   s->npow2 = 2;
   while (s->npow2 < c.vocab) s->npow2 <<= 1;
-  ok = ok && dmalloc(s, &s->glist, P) && dmalloc(s, &s->gtiles, P / 16 + std::min((size_t)c.ne, P) + 1) &&
+  ok = ok && dmalloc(s, &s->glist, P) && dmalloc(s, &s->gtiles, P / kMoeTileRows + std::min((size_t)c.ne, P) + 1) &&
        dmalloc(s, &s->gntiles, 1);
   ok = ok && dmalloc(s, &s->qbuf, B * s->kmax * (size_t)c.vocab) && dmalloc(s, &s->pbuf, R * (size_t)c.vocab) &&
        dmalloc(s, &s->sortbuf, R * 2 * (size_t)s->npow2);
@@ -811,6 +817,49 @@ void tma_launch(LZRunState* s, const GemmTmaArgs& a) {
          T::smem(), a);
 }
 
+// Grouped w1/w3 (w13) or w2 of one layer on the TMA-staged expert kernel;
+// false when the shapes do not fit it (K % 128, K > 1024, output chunks).
+// The expert shapes the TMA-staged kernels take (K % 128, K <= 1024,
+// output chunks of 128 for both products).
+bool moe_tma_fits(const Cfg& c) {
+  return c.latent % 128 == 0 && c.moe_ffn % 128 == 0 && c.latent <= MoeTma<true, true>::KMAX &&
+         c.moe_ffn <= MoeTma<true, true>::KMAX;
+}
+
+bool moe_tma(LZRunState* s, bool w13, const int8_t* wq, const float* wsc, int gs, int tmax) {
+  const Cfg& c = s->m->c;
+  const int K = w13 ? c.latent : c.moe_ffn, rows_e = w13 ? 2 * c.moe_ffn : c.latent;
+  const int chunk = 128;   // j values (w13) or latent outputs (w2) per block
+  if (!moe_tma_fits(c)) return false;
+  const bool rb1 = gs == 32;
+  const int GM = rb1 ? 0 : gs == K ? 1 : 2;
+  MoeTmaArgs a;
+  memset(&a, 0, sizeof(a));
+  const CUtensorMap* mq = tmap(s, wq, K, c.ne * rows_e, 128, 128);
+  const CUtensorMap* ms = rb1 ? tmap(s, wsc, K / 32, c.ne * rows_e, 4, 128) : nullptr;
+  if (!mq || (rb1 && !ms)) return false;
+  a.wq = *mq;
+  if (rb1) a.wsc = *ms;
+  a.ws = wsc; a.list = s->glist; a.tiles = s->gtiles; a.ntiles = s->gntiles;
+  a.xq = w13 ? s->latq : s->hq; a.xs = w13 ? s->lats : s->hs;
+  a.hq = s->hq; a.hs = s->hs; a.h2 = s->h2; a.err = s->d_err;
+  a.K = K; a.gs = gs; a.rows_e = rows_e; a.ffn = c.moe_ffn; a.latent = c.latent; a.topk = c.topk;
+  const dim3 grid((w13 ? c.moe_ffn : c.latent) / chunk, tmax);
+#define LZ_MOE(W, RB, G) \
+  launch(s, moe_tma_kernel<W, RB, G>, grid, dim3((MoeTma<W, RB>::CW + 1) * 32), MoeTma<W, RB>::smem(K), a)
+  if (w13) {
+    if (GM == 0) LZ_MOE(true, true, 0);
+    else if (GM == 1) LZ_MOE(true, false, 1);
+    else LZ_MOE(true, false, 2);
+  } else {
+    if (GM == 0) LZ_MOE(false, true, 0);
+    else if (GM == 1) LZ_MOE(false, false, 1);
+    else LZ_MOE(false, false, 2);
+  }
+#undef LZ_MOE
+  return true;
+}
+
 // R > 8 token rows with K (and K2) % 128 == 0: the TMA-staged tensor-core
 // GEMM.  Tiles: 32-row token tiles while the grid stays within ~4 blocks
 // per SM, 64-row ones above; 64-output tiles for the wide lm_head at
@@ -969,10 +1018,14 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
                                            m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
     const int P = R * c.topk;
     if (R > kPrologueRows && P <= 2048) {
-      // grouped experts: pairs bucketed by expert into 16-row tiles
-      const int tmax = P / 16 + std::min(c.ne, P) + 1;
-      launch(s, moe_group_kernel, dim3(1), dim3(1024), 0, s->pair_e, P, c.ne, s->glist, s->gtiles, s->gntiles);
-      if (L.w13_gs == 32)
+      // grouped experts: pairs bucketed by expert into tiles of 8 pairs
+      // (TMA-staged kernels) or 16 (warp-tile kernels)
+      const int trows = moe_tma_fits(c) ? kMoeTileRows : 16;
+      const int tmax = P / trows + std::min(c.ne, P) + 1;
+      launch(s, moe_group_kernel, dim3(1), dim3(1024), 0, s->pair_e, P, c.ne, s->glist, s->gtiles, s->gntiles, trows);
+      if (moe_tma(s, true, L.w13q, L.w13s, L.w13_gs, tmax)) {
+        // launched
+      } else if (L.w13_gs == 32)
         launch(s, moe_w13_group_kernel<true>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
                c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
                s->hs);
@@ -980,7 +1033,9 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
         launch(s, moe_w13_group_kernel<false>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
                c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
                s->hs);
-      if (L.w2_gs == 32)
+      if (moe_tma(s, false, L.w2q, L.w2s, L.w2_gs, tmax)) {
+        // launched
+      } else if (L.w2_gs == 32)
         launch(s, moe_w2_group_kernel<true>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, L.w2q, L.w2s,
                c.moe_ffn, c.latent, L.w2_gs, s->glist, s->gtiles, s->gntiles, s->hq, s->hs, s->h2);
       else

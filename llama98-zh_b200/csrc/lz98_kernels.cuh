@@ -1457,7 +1457,7 @@ struct MoeTile {
 // expert, tiles the (expert, start, count) of every 16-row tile, *ntiles
 // their number.  One block; E <= 256.
 __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ pair_expert, int P, int E,
-                                                         int* list, MoeTile* tiles, int* ntiles) {
+                                                         int* list, MoeTile* tiles, int* ntiles, int trows) {
   pdl_trigger();
   pdl_wait();
   __shared__ int cnt[256], off[256];
@@ -1476,7 +1476,7 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
     int o = 0, nt = 0;
     for (int e = 0; e < E; e++) {
       off[e] = o;
-      for (int i = 0; i < cnt[e]; i += 16) tiles[nt++] = MoeTile{e, o + i, min(16, cnt[e] - i)};
+      for (int i = 0; i < cnt[e]; i += trows) tiles[nt++] = MoeTile{e, o + i, min(trows, cnt[e] - i)};
       o += cnt[e];
     }
     *ntiles = nt;
@@ -1587,6 +1587,285 @@ moe_w2_group_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2
       const int o = n0 + t * 8 + tq * 2 + (e & 1);
       if (row < T.count && o < latent) h2[(size_t)(e >= 2 ? pc : pa) * latent + o] = mma_result(st[t][e]);
     }
+}
+
+// ------------------------------------- TMA-staged grouped expert kernels
+//
+// The grouped w1/w3 and w2 products with the roles of the MMA operands
+// swapped: the expert's weight rows are the 16-row A operand, streamed by
+// 2-D TMA loads (128-byte K slices, 128-byte swizzle) through an mbarrier
+// ring, and the tile's <= 8 gathered activation rows (token rows of latq
+// for w1/w3, pair rows of hq for w2) are the 8-column B operand, copied
+// once into a resident swizzled buffer.  With about 8 pairs per expert this
+// wastes no MMA rows on padding.  Each (output, pair) keeps the reference
+// float epilogue in K order.  Block = CW consumer warps of MW 16-row weight
+// tiles each + one producer warp; grid (output chunks of 128, tiles).
+constexpr int kMoeTileRows = 8;   // pairs per tile on this path
+
+struct alignas(64) MoeTmaArgs {
+  CUtensorMap wq;            // stacked expert weights [E * rows_e][K] u8
+  CUtensorMap wsc;           // their scales [E * rows_e][K/32] f32 (gs = 32 only)
+  const float* ws;           // scales read directly (gs > 32)
+  const int* list;
+  const MoeTile* tiles;
+  const int* ntiles;
+  const int8_t* xq;          // activation rows: latq (w1/w3) or hq (w2)
+  const float* xs;
+  int8_t* hq;                // w1/w3 outputs: silu(w1 x) * (w3 x) quantised per 32
+  float* hs;
+  float* h2;                 // w2 outputs [pair][latent]
+  int* err;
+  int K, gs, rows_e, ffn, latent, topk;
+};
+
+template <bool W13, bool RB1>
+struct MoeTma {
+  static constexpr int CW = 4;                      // consumer warps
+  static constexpr int MW = W13 ? 4 : 2;            // 16-row weight tiles per warp (w13: 2 of w1 + 2 of w3)
+  static constexpr int BOX = 128;                   // weight rows per box (w13: a w1 box and a w3 box)
+  static constexpr int NBOX = W13 ? 2 : 1;
+  static constexpr int NST = 3;
+  static constexpr int B = NBOX * BOX * 128;        // swizzled weight tile per stage
+  static constexpr int WS = RB1 ? NBOX * BOX * 16 : 0;
+  static constexpr int KMAX = 1024;
+  // bytes of dynamic shared memory for inner dimension K
+  static size_t smem(int K) { return 1024 + (size_t)NST * (B + WS) + 8 * (size_t)K + 8 * (K / 32) * 4 + 2 * NST * 8; }
+};
+
+template <bool W13, bool RB1, int GM>
+__global__ void __launch_bounds__((MoeTma<W13, RB1>::CW + 1) * 32) moe_tma_kernel(const __grid_constant__ MoeTmaArgs p) {
+  using C = MoeTma<W13, RB1>;
+  constexpr int CW = C::CW, MW = C::MW, NST = C::NST;
+  extern __shared__ uint8_t moe_smem[];
+  const int K = p.K, nsb = K >> 5, nit = K >> 7;
+  const uint32_t raw = smem_u32(moe_smem);
+  const uint32_t base = (raw + 1023u) & ~1023u;       // NST weight tiles
+  const uint32_t wsb = base + NST * C::B;             // weight-scale boxes (gs = 32)
+  const uint32_t bbase = wsb + NST * C::WS;           // resident B: K/128 slices of 8 rows x 128 B
+  const uint32_t xsb = bbase + 8 * K;                 // activation scales [8][K/32]
+  const uint32_t bars = xsb + 8 * nsb * 4;
+  uint8_t* gen = moe_smem + (base - raw);
+  pdl_trigger();
+  pdl_wait();
+  if ((int)blockIdx.y >= *p.ntiles) return;
+  const MoeTile T = p.tiles[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o0 = blockIdx.x * 128;      // first j (w1/w3) or latent output (w2) of the block
+  const int erow = T.e * p.rows_e;
+  if (threadIdx.x == CW * 32) {
+    for (int s = 0; s < NST; s++) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 8 * (NST + s), CW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  auto issue = [&](int it) {
+    const int stg = it % NST;
+    const uint32_t full = bars + 8 * stg, tile = base + stg * C::B;
+    mbar_expect_tx(full, C::B + C::WS);
+#pragma unroll
+    for (int b = 0; b < C::NBOX; b++) {
+      const int row = erow + o0 + b * p.ffn;
+      tma_load_2d(tile + b * C::BOX * 128, &p.wq, it * 128, row, full);
+      if (RB1) tma_load_2d(wsb + stg * C::WS + b * C::BOX * 16, &p.wsc, it * 4, row, full);
+    }
+  };
+  if (threadIdx.x == CW * 32)
+    for (int it = 0; it < min(nit, NST); it++) issue(it);
+  // resident activation rows of the tile (rows past the count repeat the last)
+  {
+    const int cpr = K >> 4;   // 16-byte chunks per row
+    for (int idx = threadIdx.x; idx < 8 * cpr; idx += blockDim.x) {
+      const int r = idx / cpr, j = idx - r * cpr;
+      const int pr = p.list[T.start + min(r, T.count - 1)];
+      const int src = W13 ? pr / p.topk : pr;
+      const uint4 v = *reinterpret_cast<const uint4*>(p.xq + (size_t)src * K + j * 16);
+      *reinterpret_cast<uint4*>(gen + (bbase - base) + (j >> 3) * 1024 + r * 128 + (((j & 7) ^ r) << 4)) = v;
+    }
+    float* xsm = reinterpret_cast<float*>(gen + (xsb - base));
+    for (int idx = threadIdx.x; idx < 8 * nsb; idx += blockDim.x) {
+      const int r = idx / nsb, c = idx - r * nsb;
+      const int pr = p.list[T.start + min(r, T.count - 1)];
+      const int src = W13 ? pr / p.topk : pr;
+      xsm[idx] = p.xs[(size_t)src * nsb + c];
+    }
+  }
+  __syncthreads();
+  if (warp == CW) {
+    if (lane != 0) return;
+    bool ok = true;
+    int it = min(nit, NST);
+    for (; it < nit; it++) {
+      if (!mbar_wait(bars + 8 * (NST + it % NST), (it / NST - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      issue(it);
+    }
+    if (!ok) atomicExch(p.err, 1);
+    for (int j = max(0, it - NST); j < it; j++) mbar_wait(bars + 8 * (j % NST), (j / NST) & 1);
+    return;
+  }
+  const int gid = lane >> 2, tq = lane & 3, sw = lane & 7;
+  // stage row of weight tile i of this warp: w13 tiles 0, 1 in the w1 box,
+  // 2, 3 the same j in the w3 box; w2 tiles i
+  auto trow = [&](int i) { return W13 ? (i >> 1) * C::BOX + warp * 32 + (i & 1) * 16 : warp * 32 + i * 16; };
+  const int rb = p.gs >> 5, ng = K / p.gs;
+  int grow[MW][2];   // stacked-tensor weight rows of fragment rows gid, gid + 8
+  float wrow[MW][2];
+#pragma unroll
+  for (int i = 0; i < MW; i++)
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int r = trow(i) + gid + 8 * h;
+      const int b = W13 ? r / C::BOX : 0;
+      grow[i][h] = erow + o0 + b * p.ffn + (r - b * C::BOX);
+      wrow[i][h] = GM == 1 ? __ldg(p.ws + grow[i][h]) : 0.0f;
+    }
+  RedState<RB1> st[MW][4];
+#pragma unroll
+  for (int i = 0; i < MW; i++)
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+#pragma unroll
+      for (int j = 0; j < (RB1 ? 4 : 2); j++) st[i][e].a[j] = 0.0f;
+  uint32_t aoff[MW];
+#pragma unroll
+  for (int i = 0; i < MW; i++) aoff[i] = (uint32_t)(trow(i) + sw + (((lane >> 3) & 1) << 3)) * 128u;
+  const int ach = lane >> 4, bch = (lane >> 3) & 1;
+  const uint32_t boff = (uint32_t)sw * 128u;
+  const float* xsm = reinterpret_cast<const float*>(gen + (xsb - base));
+  int gcnt = 0, gidx = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int it = 0; it < nit; it++) {
+    const int stg = it % NST;
+    if (!mbar_wait(bars + 8 * stg, (it / NST) & 1)) {
+      ok = false;
+      break;
+    }
+    const uint32_t tile = base + stg * C::B, bslice = bbase + it * 1024;
+    const float* wsm = reinterpret_cast<const float*>(gen + (wsb - base) + stg * C::WS);
+    unsigned af[4][MW][4], bf[4][2];
+#pragma unroll
+    for (int sl = 0; sl < 4; sl++) {
+      ldsm_x2(bslice + boff + ((uint32_t)((2 * sl + bch) ^ sw) << 4), bf[sl][0], bf[sl][1]);
+#pragma unroll
+      for (int i = 0; i < MW; i++)
+        ldsm_x4(tile + aoff[i] + ((uint32_t)((2 * sl + ach) ^ sw) << 4), af[sl][i][0], af[sl][i][1], af[sl][i][2],
+                af[sl][i][3]);
+    }
+    float4 wv[MW][2];
+    if (RB1) {
+#pragma unroll
+      for (int i = 0; i < MW; i++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) wv[i][h] = *reinterpret_cast<const float4*>(wsm + (trow(i) + gid + 8 * h) * 4);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + 8 * (NST + stg));   // the stage is in registers
+#pragma unroll
+    for (int sl = 0; sl < 4; sl++) {
+      const int s = it * 4 + sl;
+      const float x0 = xsm[(2 * tq) * nsb + s], x1 = xsm[(2 * tq + 1) * nsb + s];
+      bool gend = false;
+      float wg[MW][2];
+      if (GM == 1) {
+        gend = s == nsb - 1;
+#pragma unroll
+        for (int i = 0; i < MW; i++) wg[i][0] = wrow[i][0], wg[i][1] = wrow[i][1];
+      } else if (GM == 2) {
+        gend = ++gcnt == rb;
+        if (gend) {
+          gcnt = 0;
+#pragma unroll
+          for (int i = 0; i < MW; i++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) wg[i][h] = __ldg(p.ws + (size_t)grow[i][h] * ng + gidx);
+          gidx++;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < MW; i++)
+#pragma unroll
+          for (int h = 0; h < 2; h++) wg[i][h] = f4_at(wv[i][h], sl);
+      }
+#pragma unroll
+      for (int i = 0; i < MW; i++) {
+        int d[4];
+        mma_s8(d, af[sl][i], bf[sl][0], bf[sl][1]);
+        // d[e]: weight row gid + 8 (e >> 1), pair column 2 tq + (e & 1)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float a = i2f_small(d[e]);
+          const float xsv = (e & 1) ? x1 : x0;
+          RedState<RB1>& R_ = st[i][e];
+          if (!RB1) {
+            R_.a[0] = __fadd_rn(R_.a[0], __fmul_rn(a, xsv));
+            if (gend) {
+              R_.a[1] = __fadd_rn(R_.a[1], __fmul_rn(R_.a[0], wg[i][e >> 1]));
+              R_.a[0] = 0.0f;
+            }
+          } else {
+            R_.a[sl] = __fadd_rn(R_.a[sl], __fmul_rn(a, __fmul_rn(xsv, wg[i][e >> 1])));
+          }
+        }
+      }
+    }
+  }
+  if (!ok) {
+    atomicExch(p.err, 1);
+    return;
+  }
+  int pr[2];
+#pragma unroll
+  for (int c = 0; c < 2; c++) pr[c] = p.list[T.start + min(2 * tq + c, T.count - 1)];
+  if (W13) {
+    // per pair column c: the warp's 32 j values sit in the 8 lanes of equal
+    // tq (tiles i = 0, 1; rows gid and gid + 8): silu(w1) * w3, amax over
+    // those lanes, per-32 quantisation (src/forward_moe.c:434-545)
+    const int j0 = o0 + warp * 32;
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      float h[4];
+      uint32_t am = 0;
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+          const int e = hh * 2 + c;
+          h[i * 2 + hh] = __fmul_rn(silu(mma_result(st[i][e])), mma_result(st[i + 2][e]));
+          const uint32_t b = abs_bits(h[i * 2 + hh]);
+          am = am > b ? am : b;
+        }
+#pragma unroll
+      for (int o = 4; o <= 16; o <<= 1) {
+        const uint32_t w = __shfl_xor_sync(0xffffffffu, am, o);
+        am = am > w ? am : w;
+      }
+      float sg, inv;
+      q8_scale_from_amax(am, &sg, &inv);
+      if (2 * tq + c < T.count) {
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++)
+            p.hq[(size_t)pr[c] * p.ffn + j0 + i * 16 + hh * 8 + gid] =
+                (int8_t)q8_clamp(q8_round(__fmul_rn(h[i * 2 + hh], inv)));
+        if (gid == 0) p.hs[(size_t)pr[c] * (p.ffn / 32) + j0 / 32] = sg;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < MW; i++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int c = e & 1;
+        const int o = o0 + warp * 32 + i * 16 + gid + 8 * (e >> 1);
+        if (2 * tq + c < T.count && o < p.latent) p.h2[(size_t)pr[c] * p.latent + o] = mma_result(st[i][e]);
+      }
+  }
 }
 
 // lat_y of one token row = sum over its selected experts, in selection

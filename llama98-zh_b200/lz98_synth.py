@@ -110,6 +110,12 @@ CONFIGS = {
                          vocab=1024, n_experts=8, top_k=4, latent=64,
                          moe_ffn=128, shared_width=128, seq_len=256,
                          gs_mode="row", seed=7),
+    # Per-row scales with every matmul width a multiple of 128: the shapes
+    # that reach the TMA-staged dense and grouped-expert kernels.
+    "midi": KunMoeConfig(name="midi", hidden=256, n_layers=2, kda_heads=4,
+                         vocab=2048, n_experts=16, top_k=4, latent=128,
+                         moe_ffn=256, shared_width=256, seq_len=256,
+                         gs_mode="row", seed=11),
 }
 
 

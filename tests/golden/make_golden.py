@@ -24,6 +24,7 @@ CASES = {
     # name: (prompt length, verify tokens, draft tokens, max_new)
     "tiny": (24, 4, 3, 40),
     "mini": (40, 4, 3, 48),
+    "midi": (40, 4, 3, 48),
 }
 
 

@@ -21,7 +21,7 @@ def bits_equal(a, b):
     return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-@pytest.fixture(scope="module", params=["tiny", "mini"])
+@pytest.fixture(scope="module", params=["tiny", "mini", "midi"])
 def gcase(request):
     from conftest import model_dir
     import lz98

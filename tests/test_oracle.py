@@ -23,7 +23,7 @@ def load_golden(name):
     return dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
 
 
-@pytest.fixture(scope="module", params=["tiny", "mini"])
+@pytest.fixture(scope="module", params=["tiny", "mini", "midi"])
 def case(request):
     from conftest import model_dir
     import lz98_synth
