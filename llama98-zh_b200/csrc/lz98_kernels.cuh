@@ -1086,17 +1086,22 @@ constexpr int kRecurTB = 4;
 // One two-plane requantisation of a 32-wide state group held one element
 // per lane (src/ops_gdn.c:1191-1340): hi = q8 of buf, residual rounded
 // half up into hi when possible, lo = rne(residual * 256).
-LZ_HD void requant_2p(float buf, float sg, float iv, int8_t& h8, int8_t& l8) {
+// Also returns e = hi + lo / 256, the element as the next token dequantises
+// it (hi as a float is exact, so it is adjusted with hq).
+LZ_HD void requant_2p(float buf, float iv, int8_t& h8, int8_t& l8, float& e) {
   const float f = __fmul_rn(buf, iv);
   int hq = q8_clamp(q8_round(f));
-  float res = __fsub_rn(f, (float)hq);
-  if (res >= 0.5f) { if (hq < 127) { hq += 1; res = __fsub_rn(res, 1.0f); } }
-  else if (res < -0.5f) { if (hq > -127) { hq -= 1; res = __fadd_rn(res, 1.0f); } }
+  float hf = (float)hq;
+  float res = __fsub_rn(f, hf);
+  if (res >= 0.5f) { if (hq < 127) { hq += 1; hf = __fadd_rn(hf, 1.0f); res = __fsub_rn(res, 1.0f); } }
+  else if (res < -0.5f) { if (hq > -127) { hq -= 1; hf = __fsub_rn(hf, 1.0f); res = __fadd_rn(res, 1.0f); } }
   h8 = (int8_t)hq;
-  l8 = (int8_t)q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
+  const int lq = q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
+  l8 = (int8_t)lq;
+  e = __fadd_rn(hf, __fmul_rn((float)lq, 1.0f / kLoScale));
 }
 
-__global__ void __launch_bounds__(kRecurThreads)
+__global__ void __launch_bounds__(kRecurThreads, 4)
 kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  const float* __restrict__ inproj, int ldi, int off_b, int off_g,
                  const float* __restrict__ gate, int nvk,
@@ -1115,6 +1120,10 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], vcs[TB][VD], zs[TB][VD], OUT[TB][VD];
   __shared__ __align__(16) float U[VD];
   __shared__ float inv_q[TB], inv_k[TB], beta[TB], kqv[TB], inv_o[TB];
+  // the state dequantised (hi + lo / 256, unscaled), refreshed right after
+  // each requantisation; per-token scale products of the two passes
+  __shared__ __align__(16) float E[KD][VD];
+  __shared__ float SCX[2][KD][2], SCG[KD][2];
   const KdaSeq sq = seqs[blockIdx.y];
   const int h = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1125,6 +1134,11 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
     reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
     if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
+  }
+  __syncthreads();
+  for (int q = tid; q < KD * VD; q += kRecurThreads) {
+    const int kk = q >> 6, vv = q & 63;
+    E[kk][vv] = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
   }
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
@@ -1157,18 +1171,26 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     }
     __syncthreads();
     for (int t = 0; t < nt; t++) {
+      // scale products of this token: SCX[k|q][row][group] = sc * (k|q * g)
+      // (pass 1), SCG[row][group] = sc * g (pass 2)
+      {
+        const int kk = tid & 63, grp = (tid >> 6) & 1;
+        if (tid < 2 * VD) {
+          const float g = gv[t][kk];
+          SCX[0][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(kn[t][kk], g));
+          SCX[1][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(qn[t][kk], g));
+        } else {
+          SCG[kk][grp] = __fmul_rn(sc[kk][grp], gv[t][kk]);
+        }
+      }
+      __syncthreads();
       // pass 1: thread vv (< 64) sums u, thread 64 + vv sums w, each over
       // the 64 state rows in order; thread 128 forms kq
       if (tid < 2 * VD) {
-        const int vv = tid & 63;
-        const float* qk = tid < VD ? kn[t] : qn[t];
+        const int vv = tid & 63, which = tid >> 6, grp = vv >> 5;
         float acc = 0.0f;
 #pragma unroll 8
-        for (int kk = 0; kk < KD; kk++) {
-          const float scx = __fmul_rn(sc[kk][vv >> 5], __fmul_rn(qk[kk], gv[t][kk]));
-          const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-          acc = __fadd_rn(acc, __fmul_rn(e, scx));
-        }
+        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, __fmul_rn(E[kk][vv], SCX[which][kk][grp]));
         if (tid < VD) U[vv] = acc; else OUT[t][vv] = acc;
       } else if (tid == 2 * VD) {
         float kq = 0.0f;
@@ -1190,28 +1212,24 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-          const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);
-          const float e = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
-          buf[c] = __fadd_rn(__fmul_rn(e, scg), __fmul_rn(kn[t][kk], U[vv]));
+          buf[c] = __fadd_rn(__fmul_rn(E[kk][vv], SCG[kk][grp]), __fmul_rn(kn[t][kk], U[vv]));
           am[c] = abs_bits(buf[c]);
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int c = 0; c < 4; c++) {
-            const uint32_t w = __shfl_xor_sync(0xffffffffu, am[c], o);
-            am[c] = am[c] > w ? am[c] : w;
-          }
-        __syncwarp();
+        for (int c = 0; c < 4; c++) am[c] = __reduce_max_sync(0xffffffffu, am[c]);
+        // the four groups' scales on lanes 0-3 at once, then broadcast
+        float sg4, iv4;
+        q8_scale_from_amax(lane == 1 ? am[1] : lane == 2 ? am[2] : lane == 3 ? am[3] : am[0], &sg4, &iv4);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-          float sg, iv;
-          q8_scale_from_amax(am[c], &sg, &iv);
+          const float sg = __shfl_sync(0xffffffffu, sg4, c), iv = __shfl_sync(0xffffffffu, iv4, c);
           int8_t h8, l8;
-          requant_2p(buf[c], sg, iv, h8, l8);
+          float e;
+          requant_2p(buf[c], iv, h8, l8, e);
           hi[kk][vv] = h8;
           lo[kk][vv] = l8;
+          E[kk][vv] = e;
           if (lane == 0) sc[kk][grp] = sg;
         }
       }

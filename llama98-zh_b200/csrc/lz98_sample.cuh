@@ -93,14 +93,16 @@ enum ChainMode { kChainSum = 0, kChainFindLt = 1, kChainFindGe = 2 };
 // acc_j = fl(acc_{j-1} + v_j) (round to nearest even, v_j >= 0 finite).
 // While the running sum s stays in one binade its grid is u = ulp(s), and
 // fl(s + v) = s + u * rne(v / u): the rounding of each addend does not
-// depend on s, except at an exact tie (v / u ending in .5, where the even
-// rule looks at s).  So inside a segment the running sum is s/u plus an
-// integer prefix sum of per-addend ulp counts.  A segment ends at the first
-// addend that ties or whose rounded prefix reaches the next binade (2^24
-// ulps); that addend is added with a real fadd and a new segment starts
-// from the exact result.  Every cumulative equals the sequential one bit
-// for bit (zeros keep s at 0; the first non-zero addend after them is
-// taken exactly).
+// depend on s, except at an exact tie (v / u ending in .5), where the even
+// rule adds floor(v / u) or one more by the parity of the running count.
+// So inside a segment the running sum is s/u plus an integer prefix of
+// per-addend counts, each a function of that parity (a pair: count when
+// even, count when odd); pairs compose associatively, so the prefix is a
+// parallel scan.  A segment ends at the first addend whose rounded prefix
+// reaches the next binade (2^24 ulps); that addend is added with a real
+// fadd and a new segment starts from the exact result.  Every cumulative
+// equals the sequential one bit for bit (zeros keep s at 0; the first
+// non-zero addend after them is taken exactly).
 //
 // Values are decomposed as v = M * 2^(E - 150) with E = max(biased
 // exponent, 1), which covers subnormals with the same formulas.
@@ -167,7 +169,28 @@ constexpr int kChainHead = 1024;      // leading values summed serially
 constexpr int kChainPer = 8;          // values per thread per window
 constexpr int kChainWin = kChainPer * kSampThreads;
 
+// Composition of per-addend ulp counts that depend on the parity of the
+// running count (a: count even before, b: odd): `x then y`.  Saturating,
+// hence associative where it is used (below 2^24 ulps).
+struct U2 {
+  uint32_t a, b;
+};
+LZ_HD U2 u2_then(U2 x, U2 y) {
+  return U2{sadd(x.a, (x.a & 1u) ? y.b : y.a), sadd(x.b, ((x.b + 1u) & 1u) ? y.b : y.a)};
+}
+
+LZ_HD U2 warp_incl_scan_u2(U2 v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const U2 w = {__shfl_up_sync(0xffffffffu, v.a, o), __shfl_up_sync(0xffffffffu, v.b, o)};
+    if (lane >= o) v = u2_then(w, v);
+  }
+  return v;
+}
+
 struct ChainShared {
+  U2 wt2[kSampWarps];                 // warp compositions, then exclusive prefixes
   uint32_t wt[kSampWarps];            // warp totals, then exclusive offsets
   int wstop[kSampWarps], wfind[kSampWarps];
   int S, F;
@@ -265,39 +288,44 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
       int Es;
       uint32_t Ms;
       fdecomp(s, Es, Ms);
-      uint32_t pre[kChainPer], nu[kChainPer];
-      uint32_t tiemask = 0u, livemask = 0u;
-      uint32_t run = 0u;
+      // per addend a parity function (ulps if the running count is even,
+      // ulps if odd): equal halves except at an exact tie
+      U2 pre[kChainPer];
+      uint32_t livemask = 0u;
+      U2 run = {0u, 0u};
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
         const bool live = j0 + k >= cur && j0 + k < wend;
         bool t;
-        nu[k] = live ? fulps(ve[k], vm[k], Es, t) : 0u;
-        tiemask |= (live && t) ? 1u << k : 0u;
+        const uint32_t q = live ? fulps(ve[k], vm[k], Es, t) : 0u;
         livemask |= live ? 1u << k : 0u;
-        run = sadd(run, nu[k]);
+        const U2 d = (live && t) ? U2{q + (q & 1u), q + ((q + 1u) & 1u)} : U2{q, q};
+        run = u2_then(run, d);
         pre[k] = run;
       }
-      // block exclusive scan of the thread totals (warp 0 scans the warps)
-      const uint32_t incl = warp_incl_scan_sat(run);
-      if (lane == 31) cs.wt[warp] = incl;
+      // block exclusive scan of the thread compositions (warp 0 scans the warps)
+      const U2 incl = warp_incl_scan_u2(run);
+      if (lane == 31) cs.wt2[warp] = incl;
       __syncthreads();
       if (warp == 0) {
-        const uint32_t t = cs.wt[lane];
-        const uint32_t x = warp_incl_scan_sat(t);
-        // exclusive value: the inclusive scan of the warps before
-        const uint32_t ex = __shfl_up_sync(0xffffffffu, x, 1);
-        cs.wt[lane] = lane ? ex : 0u;
+        const U2 x = warp_incl_scan_u2(cs.wt2[lane]);
+        const U2 ex = {__shfl_up_sync(0xffffffffu, x.a, 1), __shfl_up_sync(0xffffffffu, x.b, 1)};
+        cs.wt2[lane] = lane ? ex : U2{0u, 0u};
       }
       __syncthreads();
-      // inclusive scan of the warp before this thread (saturated)
-      const uint32_t before = __shfl_up_sync(0xffffffffu, incl, 1);
-      const uint32_t off = sadd(sadd(Ms, cs.wt[warp]), lane ? before : 0u);
+      // composition of everything before this thread, applied to Ms
+      const U2 lb = {__shfl_up_sync(0xffffffffu, incl.a, 1), __shfl_up_sync(0xffffffffu, incl.b, 1)};
+      const U2 before = u2_then(cs.wt2[warp], lane ? lb : U2{0u, 0u});
+      const uint32_t p0 = Ms & 1u;
+      const uint32_t off = sadd(Ms, p0 ? before.b : before.a);
+      const uint32_t p1 = off & 1u;          // parity entering this thread's addends
       const int bound = MODE == kChainSum ? 0 : chain_bound<MODE>(target, Es);
-      uint32_t stopmask = tiemask, hitmask = 0u;
+      uint32_t stopmask = 0u, hitmask = 0u;
+      uint32_t mk[kChainPer];
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
-        const uint32_t m = sadd(off, pre[k]);
+        mk[k] = sadd(off, p1 ? pre[k].b : pre[k].a);
+        const uint32_t m = mk[k];
         stopmask |= ((livemask >> k) & 1u) && m >= 0x1000000u ? 1u << k : 0u;
         if (MODE == kChainFindLt) hitmask |= ((livemask >> k) & 1u) && (int)m > bound ? 1u << k : 0u;
         if (MODE == kChainFindGe) hitmask |= ((livemask >> k) & 1u) && (int)m >= bound ? 1u << k : 0u;
@@ -312,20 +340,21 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
         // a cumulative inside the segment meets the target
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == Fd) cs.sum = frecon(Es, sadd(off, pre[k]));
+          if (j0 + k == Fd) cs.sum = frecon(Es, mk[k]);
         found = Fd;
         next = wend;
       } else if (S == INT_MAX) {
         // no stop: the segment runs to the window's end
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == wend - 1) cs.sum = frecon(Es, sadd(off, pre[k]));
+          if (j0 + k == wend - 1) cs.sum = frecon(Es, mk[k]);
         next = wend;
       } else {
-        // the stopping addend, by a real add from the exact cumulative before it
+        // the addend that leaves the binade, by a real add from the exact
+        // cumulative before it
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, sadd(off, k ? pre[k - 1] : 0u)), v[k]);
+          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, k ? mk[k - 1] : off), v[k]);
         next = S + 1;
       }
       __syncthreads();
