@@ -102,12 +102,18 @@ int    lz_mtp_catchup(const LZModel *m, LZRunState *s, const float *h_body_all,
                       const int *next_tokens, int n, int pos0);
 
 /* ---- rounds of sequence 0 (src/llama_zh.h:470-593,
-   src/generate.c:694-994 and 1234-1377).  p_min and n_min must be 0, the
-   debug flags 0, and samp must be NULL or carry identity penalties (the
-   only settings the benchmark workloads use).  lz_spec_round is the greedy
+   src/generate.c:694-994 and 1234-1377).  The debug flags must be 0 and
+   samp NULL or carrying identity penalties.  lz_spec_round is the greedy
    round; lz_spec_round_temp the coupled temperature round (temperature
    above the floor, top-p), which advances samp->rng_state as the
-   reference does. */
+   reference does.  p_min > 0 stops drafting at the first step whose
+   confidence - lz_argmax_p1's probability of the greedy draft, q(x) of a
+   sampled one - is below it (that token is not drafted); n_min > 0
+   discards a draft of fewer than n_min tokens: the call returns 0 with
+   out[0] = anchor, *out_n_accept = 0, *out_new_pos = anchor_pos and
+   nothing verified (src/generate.c:421-440, 741-791).  With either set the
+   round runs its draft steps one at a time (a host read of each step's
+   confidence) instead of as one captured graph. */
 int lz_spec_round(const LZModel *m, LZRunState *s, int anchor, int anchor_pos,
                   int k, float p_min, int n_min, const LZSampler *samp,
                   int debug_break_rollback, int debug_skip_catchup,
@@ -160,6 +166,13 @@ int lz_generate(const LZModel *m, LZRunState *s, const int *prompt, int n_prompt
                 int max_new, int spec_k, float temp, float topp, uint64_t seed,
                 int *out_tok, int out_cap, int *out_n, int *rounds, int round_cap,
                 int *n_rounds, char *errbuf, int errlen);
+/* lz_generate with the rounds' p_min / n_min (a discarded draft emits
+   nothing and the next round starts from a fresh capture forward,
+   src/generate.c:1972-2080). */
+int lz_generate_ex(const LZModel *m, LZRunState *s, const int *prompt, int n_prompt,
+                   int max_new, int spec_k, float temp, float topp, uint64_t seed,
+                   float p_min, int n_min, int *out_tok, int out_cap, int *out_n,
+                   int *rounds, int round_cap, int *n_rounds, char *errbuf, int errlen);
 
 /* Running totals of sequence `seq` over its device rounds: rounds, emitted
    tokens (n_accept + 1 per round), accepted drafts, drafted tokens. */
@@ -196,6 +209,10 @@ int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logit
    *out_hit = the index or -1. */
 int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *out_value,
                      int *out_hit);
+/* Test hook: lz_argmax_p1 (src/sampler.c:279-295) of n host values on the
+   device - the arg-max and the online-softmax probability the greedy
+   p_min compares. */
+int lz_debug_argmax_p1(const float *vals, int n, int *out_idx, float *out_p1);
 
 /* ---- recurrent-state checkpoints: replace lz_ckpt_alloc / lz_ckpt_free /
    lz_ckpt_save / lz_ckpt_restore (src/forward.h:1847-1862,

@@ -392,6 +392,7 @@ struct LZRunState {
   // bounded wait gave up; read after every synchronisation
   int* h_err = nullptr;
   int* d_err = nullptr;
+  float* pconf = nullptr;            // confidence of a p_min draft step
 };
 
 // Wait for the state's stream; false on a CUDA error or when a kernel
@@ -543,7 +544,8 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->pair_e, P) && dmalloc(s, &s->pair_w, P) && dmalloc(s, &s->tok, R) &&
             dmalloc(s, &s->vmax, R) && dmalloc(s, &s->catch_tok, R) && dmalloc(s, &s->catch_hidx, R) &&
             dmalloc(s, &s->seqs, R) && dmalloc(s, &s->mrows, R) && dmalloc(s, &s->crows, R) &&
-            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4);
+            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4) &&
+            dmalloc(s, &s->pconf, 4);
   s->npow2 = 2;
   while (s->npow2 < c.vocab) s->npow2 <<= 1;
   ok = ok && dmalloc(s, &s->glist, P) && dmalloc(s, &s->gtiles, P / kMoeTileRows + std::min((size_t)c.ne, P) + 1) &&
@@ -1139,10 +1141,37 @@ int upload_seqs(LZRunState* s, const std::vector<KdaSeq>& v) {
   return 0;
 }
 
+// The verify half of a greedy round with drafts sr[b].draft[0..k) and
+// sr[b].k == k: the (k+1)-row verify, acceptance, ring, chain reseed and
+// catch-up.
+void verify_greedy(LZRunState* s, int k) {
+  const Cfg& c = s->m->c;
+  const int B = s->B, R = B * (k + 1);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
+  body_forward(s, R, B, 1, true);
+  argmax(s, s->logits, R, 0);
+  launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
+                                                  s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  if (k > 1)
+    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+}
+
+// The verify half of a temperature round (drafts and their q rows in place).
+void verify_temp(LZRunState* s, int k) {
+  const Cfg& c = s->m->c;
+  const int B = s->B, V = c.vocab, R = B * (k + 1);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
+  body_forward(s, R, B, 1, true);
+  launch(s, temp_target_kernel, dim3(R), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, k, s->pbuf,
+         s->sortbuf, s->npow2);
+  launch(s, temp_accept_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->sr, k, s->kmax, s->pbuf, s->qbuf, V,
+         s->hidden, c.d, s->chain, s->depth, s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  if (k > 1)
+    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+}
+
 // One greedy round of every sequence, all on the device.
 void round_greedy(LZRunState* s, int k) {
-  const LZModel* m = s->m;
-  const Cfg& c = m->c;
   const int B = s->B;
   const int tb = (B + 127) / 128;
   for (int i = 0; i < k; i++) {
@@ -1151,14 +1180,7 @@ void round_greedy(LZRunState* s, int k) {
     argmax(s, s->logits, B, 1);
     launch(s, draft_store_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, k, s->vmax);
   }
-  const int R = B * (k + 1);
-  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
-  body_forward(s, R, B, 1, true);
-  argmax(s, s->logits, R, 0);
-  launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
-                                                  s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
-  if (k > 1)
-    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+  verify_greedy(s, k);
 }
 
 // One temperature round of every sequence (src/generate.c:1234-1377), all
@@ -1176,15 +1198,7 @@ void round_temp(LZRunState* s, int k) {
     launch(s, temp_draft_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, i, k, s->kmax,
            s->qbuf);
   }
-  const int R = B * (k + 1);
-  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
-  body_forward(s, R, B, 1, true);
-  launch(s, temp_target_kernel, dim3(R), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, k, s->pbuf,
-         s->sortbuf, s->npow2);
-  launch(s, temp_accept_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->sr, k, s->kmax, s->pbuf, s->qbuf, V,
-         s->hidden, c.d, s->chain, s->depth, s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
-  if (k > 1)
-    mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+  verify_temp(s, k);
 }
 
 // 0: every sequence greedy, 1: every sequence in temperature mode, -1: mixed.
@@ -1197,6 +1211,53 @@ int round_mode(const LZRunState* s) {
 void round_any(LZRunState* s, int k) {
   if (round_mode(s) == 1) round_temp(s, k);
   else round_greedy(s, k);
+}
+
+// Drafting of sequence 0 with the early stop of p_min (src/generate.c:
+// 741-762 greedy, 1258-1280 temperature): step by step, each step's
+// confidence read back - lz_argmax_p1's probability of the greedy draft,
+// q(x) of the sampled one - and the first step below p_min not recorded.
+// Returns k_eff, or -1 on a CUDA failure.
+int draft_pmin(LZRunState* s, int k, bool temp, float p_min) {
+  const Cfg& c = s->m->c;
+  int k_eff = 0;
+  for (int i = 0; i < k; i++) {
+    launch(s, draft_setup_kernel, dim3(1), dim3(128), 0, s->sr, 1, i, s->seq_len, s->tok, s->mrows);
+    mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
+    float conf = 0.0f;
+    if (temp) {
+      launch(s, temp_draft_kernel, dim3(1), dim3(kSampThreads), kSampSmem, s->logits, c.vocab, s->sr, i, k, s->kmax,
+             s->qbuf);
+      sr_down(s);
+      const int x = s->h_sr[0].draft[i];
+      if (cudaMemcpyAsync(&conf, s->qbuf + (size_t)i * c.vocab + x, 4, cudaMemcpyDeviceToHost, s->st) != cudaSuccess)
+        return -1;
+    } else {
+      launch(s, argmax_p1_kernel, dim3(1), dim3(kSampThreads), kSampSmem, s->logits, c.vocab, s->sr, i, k,
+             reinterpret_cast<int*>(s->sortbuf), s->pconf);
+      if (cudaMemcpyAsync(&conf, s->pconf, 4, cudaMemcpyDeviceToHost, s->st) != cudaSuccess) return -1;
+    }
+    if (!sync_ok(s)) return -1;
+    if (conf < p_min) break;
+    k_eff = i + 1;
+  }
+  return k_eff;
+}
+
+// A round of sequence 0 with p_min / n_min (eager): drafting as above; a
+// draft shorter than n_min is discarded (returns 0: no verify, positions
+// unchanged, src/generate.c:765-791), else the verify half runs at k_eff.
+// Returns -1 on a CUDA failure, else 0 (discarded) or 1.
+int round_pmin(LZRunState* s, int k, bool temp, float p_min, int n_min, int* k_eff) {
+  *k_eff = draft_pmin(s, k, temp, p_min);
+  if (*k_eff < 0) return -1;
+  if (*k_eff < n_min) return 0;   // k_eff == 0 with n_min == 0 still verifies the anchor row
+  sr_down(s);
+  s->h_sr[0].k = *k_eff;
+  sr_up(s);
+  if (temp) verify_temp(s, *k_eff);
+  else verify_greedy(s, *k_eff);
+  return sync_ok(s) ? 1 : -1;
 }
 
 // One token of sequence `seq` from logits row 0 by its sampler (arg-max at
@@ -1440,8 +1501,7 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
     set_err(errbuf, errlen, "draft depth out of range");
     return -LZ98_ERR_SPEC_K_RANGE;
   }
-  if (p_min != 0.0f || n_min != 0 || debug_break_rollback || debug_skip_catchup ||
-      (samp && samp->temperature > kTempFloor) || s->B != 1) {
+  if (debug_break_rollback || debug_skip_catchup || (samp && samp->temperature > kTempFloor) || s->B != 1) {
     set_err(errbuf, errlen, "unsupported round options on the device path");
     return -LZ98_ERR_FORWARD;
   }
@@ -1453,6 +1513,27 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
   r.temp = 0.0f;
   s->seq_temp[0] = 0;
   sr_up(s);
+  if (p_min > 0.0f || n_min > 0) {
+    int k_eff = 0;
+    const int rc = round_pmin(s, k, false, p_min, n_min, &k_eff);
+    if (rc < 0) {
+      set_err(errbuf, errlen, "CUDA failure in the round");
+      return -LZ98_ERR_CUDA;
+    }
+    *out_k_eff = k_eff;
+    if (rc == 0) {   // draft discarded (src/generate.c:765-791)
+      out[0] = anchor;
+      *out_n_accept = 0;
+      *out_new_pos = anchor_pos;
+      return 0;
+    }
+    sr_down(s);
+    const SeqRound& o = s->h_sr[0];
+    for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
+    *out_n_accept = o.n_accept;
+    *out_new_pos = anchor_pos + 1 + o.n_accept;
+    return o.n_accept + 1;
+  }
   if (run_round(s, k)) {
     set_err(errbuf, errlen, "CUDA failure in the round");
     return -LZ98_ERR_CUDA;
@@ -1482,8 +1563,7 @@ extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, i
     set_err(errbuf, errlen, "draft depth out of range");
     return -LZ98_ERR_SPEC_K_RANGE;
   }
-  if (p_min != 0.0f || n_min != 0 || debug_break_rollback || debug_skip_catchup || s->B != 1 ||
-      !(samp->temperature > kTempFloor)) {
+  if (debug_break_rollback || debug_skip_catchup || s->B != 1 || !(samp->temperature > kTempFloor)) {
     set_err(errbuf, errlen, "unsupported round options on the device path");
     return -LZ98_ERR_FORWARD;
   }
@@ -1497,6 +1577,28 @@ extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, i
   r.rng = samp->rng_state;
   s->seq_temp[0] = 1;
   sr_up(s);
+  if (p_min > 0.0f || n_min > 0) {
+    int k_eff = 0;
+    const int rc = round_pmin(s, k, true, p_min, n_min, &k_eff);
+    if (rc < 0) {
+      set_err(errbuf, errlen, "CUDA failure in the round");
+      return -LZ98_ERR_CUDA;
+    }
+    *out_k_eff = k_eff;
+    sr_down(s);
+    const SeqRound& o = s->h_sr[0];
+    samp->rng_state = o.rng;   // the draft samples advanced the generator either way
+    if (rc == 0) {
+      out[0] = anchor;
+      *out_n_accept = 0;
+      *out_new_pos = anchor_pos;
+      return 0;
+    }
+    for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
+    *out_n_accept = o.n_accept;
+    *out_new_pos = anchor_pos + 1 + o.n_accept;
+    return o.n_accept + 1;
+  }
   if (run_round(s, k)) {
     set_err(errbuf, errlen, "CUDA failure in the round");
     return -LZ98_ERR_CUDA;
@@ -1604,9 +1706,10 @@ extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* 
 // 0): greedy at the temperature floor, else coupled temperature rounds with
 // top-p `topp` and the generator seeded by `seed`.  Every token is picked on
 // the device.
-extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
-                           int spec_k, float temp, float topp, uint64_t seed, int* out_tok, int out_cap,
-                           int* out_n, int* rounds, int round_cap, int* n_rounds, char* errbuf, int errlen) {
+extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
+                              int spec_k, float temp, float topp, uint64_t seed, float p_min, int n_min,
+                              int* out_tok, int out_cap, int* out_n, int* rounds, int round_cap, int* n_rounds,
+                              char* errbuf, int errlen) {
   if (!m || !s || !prompt || n_prompt < 1 || !out_n || !n_rounds) return LZ98_ERR_NULL_ARG;
   if (n_prompt >= s->seq_len) {
     set_err(errbuf, errlen, "prompt does not fit the state");
@@ -1623,6 +1726,17 @@ extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, i
   int n_out = 0, nr = 0;
   auto emit = [&](int t) { if (n_out < out_cap) out_tok[n_out] = t; n_out++; };
   int pos = n_prompt - 1, token = prompt[n_prompt - 1];
+  // one forward of `token` at `pos` in place (optionally captured into the
+  // draft chain), then one token sampled by the sequence's sampler
+  auto step = [&](bool capture, int* next) {
+    sr_down(s);
+    const int slot = s->h_sr[0].ssm_slot;
+    if (cudaMemcpyAsync(s->tok, &token, sizeof(int), cudaMemcpyHostToDevice, s->st) != cudaSuccess) return 1;
+    upload_seqs(s, {KdaSeq{0, 1, slot, 0}});
+    body_forward(s, 1, 1, 0, true);
+    if (capture) cudaMemcpyAsync(s->chain, s->hidden, c.d * 4, cudaMemcpyDeviceToDevice, s->st);
+    return sample_row(s, 0, next);
+  };
   // `pending` holds the anchor of a first round whose forward and sample
   // already ran (lz_seq_prefill forwards the last prompt token and picks
   // the anchor, as the first loop iteration of the reference does).
@@ -1636,54 +1750,68 @@ extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, i
     std::vector<float> hb((size_t)(n_prompt - 1) * c.d);
     if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, 0, hb.data())) return LZ98_ERR_FORWARD;
   }
+  // the spec loop of lz_generate_call (src/generate.c:2841-3035, rounds by
+  // src/generate.c:1900-2100)
   while (pos < max_pos - 1) {
     int round_k = 0;
     if (spec_k > 0) {
       round_k = spec_k;
       if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
     }
-    if (pending && round_k <= 0) {
-      // the reference's plain step for this position already ran
+    if (round_k > 0) {
+      int anchor, anchor_pos;
+      if (have_seed || pending) {
+        anchor = token;
+        anchor_pos = pending ? pos : pos - 1;
+      } else {
+        // no seed (after a discarded draft): capture forward, fresh anchor
+        if (step(true, &anchor)) return LZ98_ERR_CUDA;
+        anchor_pos = pos;
+        emit(anchor);
+      }
       pending = false;
-      pos++;
-      continue;
-    }
-    if (round_k > 0 && (have_seed || pending)) {
       int out[8], n_acc = 0, new_pos = 0, k_eff = 0;
-      const int anchor_pos = pending ? pos : pos - 1;
-      pending = false;
       int ne;
       if (use_temp) {
         sr_down(s);
         samp.rng_state = s->h_sr[0].rng;
-        ne = lz_spec_round_temp(m, s, token, anchor_pos, round_k, 0.0f, 0, &samp, 0, 0, out, &n_acc, &new_pos,
-                                &k_eff, errbuf, errlen);
+        ne = lz_spec_round_temp(m, s, anchor, anchor_pos, round_k, p_min, n_min, &samp, 0, 0, out, &n_acc,
+                                &new_pos, &k_eff, errbuf, errlen);
       } else {
-        ne = lz_spec_round(m, s, token, anchor_pos, round_k, 0.0f, 0, nullptr, 0, 0, out, &n_acc, &new_pos,
+        ne = lz_spec_round(m, s, anchor, anchor_pos, round_k, p_min, n_min, nullptr, 0, 0, out, &n_acc, &new_pos,
                            &k_eff, errbuf, errlen);
       }
       if (ne < 0) return -ne;
       if (rounds && nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_acc; }
       nr++;
-      have_seed = true;
-      for (int ei = 0; ei <= n_acc; ei++) emit(out[ei]);
+      have_seed = ne > 0;
+      if (ne > 0)
+        for (int ei = 0; ei <= n_acc; ei++) emit(out[ei]);
       pos = new_pos + 1;
       token = out[n_acc];
       continue;
     }
+    if (pending) {
+      // the reference's plain step for this position already ran
+      pending = false;
+      pos++;
+      continue;
+    }
     // plain decode step: forward of one token, then one sampled token
-    sr_down(s);
-    const int slot = s->h_sr[0].ssm_slot;
-    CK(cudaMemcpyAsync(s->tok, &token, sizeof(int), cudaMemcpyHostToDevice, s->st));
-    upload_seqs(s, {KdaSeq{0, 1, slot, 0}});
-    body_forward(s, 1, 1, 0, true);
-    if (sample_row(s, 0, &token)) return LZ98_ERR_CUDA;
+    if (step(false, &token)) return LZ98_ERR_CUDA;
     emit(token);
     pos++;
   }
   *out_n = n_out;
   *n_rounds = nr;
   return 0;
+}
+
+extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
+                           int spec_k, float temp, float topp, uint64_t seed, int* out_tok, int out_cap,
+                           int* out_n, int* rounds, int round_cap, int* n_rounds, char* errbuf, int errlen) {
+  return lz_generate_ex(m, s, prompt, n_prompt, max_new, spec_k, temp, topp, seed, 0.0f, 0, out_tok, out_cap, out_n,
+                        rounds, round_cap, n_rounds, errbuf, errlen);
 }
 
 extern "C" int lz_state_counters(const LZRunState* cs, int seq, int* rounds, int* emitted, int* accepted,
@@ -1855,6 +1983,32 @@ extern "C" int lz_debug_seq_sum(const float* vals, int n, int mode, float target
   if (rc) return rc;
   *out_value = h[0];
   memcpy(out_hit, &h[1], 4);
+  return 0;
+}
+
+extern "C" int lz_debug_argmax_p1(const float* vals, int n, int* out_idx, float* out_p1) {
+  if (!vals || n < 1 || !out_idx || !out_p1) return LZ98_ERR_NULL_ARG;
+  float *dv = nullptr, *dout = nullptr;
+  int* drec = nullptr;
+  if (cudaMalloc(&dv, (size_t)n * 4) != cudaSuccess) return LZ98_ERR_ALLOC;
+  if (cudaMalloc(&drec, (size_t)n * 4) != cudaSuccess || cudaMalloc(&dout, 8) != cudaSuccess) {
+    cudaFree(dv);
+    cudaFree(drec);
+    return LZ98_ERR_ALLOC;
+  }
+  int rc = 0;
+  float h[2] = {0.0f, 0.0f};
+  if (cudaMemcpy(dv, vals, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  if (!rc) {
+    argmax_p1_probe_kernel<<<1, kSampThreads, kSampSmem>>>(dv, n, drec, dout);
+    if (cudaMemcpy(h, dout, 8, cudaMemcpyDeviceToHost) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  }
+  cudaFree(dv);
+  cudaFree(drec);
+  cudaFree(dout);
+  if (rc) return rc;
+  *out_p1 = h[0];
+  memcpy(out_idx, &h[1], 4);
   return 0;
 }
 

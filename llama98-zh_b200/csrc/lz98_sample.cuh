@@ -229,10 +229,10 @@ LZ_HD void block_min2(int a, int b, ChainShared& cs, int& A, int& B) {
 // v(0..n-1) in sequential float order.  The find modes stop at the first j
 // whose cumulative c satisfies target < c (kChainFindLt) or c >= target
 // (kChainFindGe): *hit = j and c is returned; with no such j, *hit = -1 and
-// the total is returned.  Every thread of the block calls it; `stage` holds
+// the total is returned.  The running sum starts at `init` (0 by default).  Every thread of the block calls it; `stage` holds
 // kChainHead floats.
 template <int MODE, class F>
-__device__ float block_chain(F val, int n, float target, float* stage, SampShared& sh, int* hit) {
+__device__ float block_chain(F val, int n, float target, float* stage, SampShared& sh, int* hit, float init = 0.0f) {
   __shared__ ChainShared cs;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // serial head: crossings are dense while the sum is small
@@ -240,7 +240,7 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
   for (int t = tid; t < nh; t += kSampThreads) stage[t] = val(t);
   __syncthreads();
   if (tid == 0) {
-    float acc = 0.0f;
+    float acc = init;
     int h = -1;
     for (int t = 0; t < nh; t++) {
       acc = __fadd_rn(acc, stage[t]);
@@ -385,6 +385,109 @@ __device__ void block_softmax(const float* __restrict__ lg, int n, float inv_t, 
   const float invs = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
   for (int j = threadIdx.x; j < n; j += kSampThreads) out[j] = __fmul_rn(ev(j), invs);
   __syncthreads();
+}
+
+// Exclusive scan over the block's threads in index order (every thread
+// calls; `id` is the value before thread 0), with the block total.
+template <class Op>
+__device__ uint32_t block_excl_scan_u32(uint32_t v, uint32_t id, Op op, uint32_t* total) {
+  __shared__ uint32_t wsh[kSampWarps];
+  static_assert(kSampWarps == 32, "one warp scans the warp totals");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t w = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x = op(w, x);
+  }
+  __syncthreads();
+  if (lane == 31) wsh[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t t = wsh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t w = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t = op(w, t);
+    }
+    wsh[lane] = t;
+  }
+  __syncthreads();
+  const uint32_t wex = warp ? op(id, wsh[warp - 1]) : id;
+  const uint32_t lex = __shfl_up_sync(0xffffffffu, x, 1);
+  if (total) *total = op(id, wsh[kSampWarps - 1]);
+  __syncthreads();
+  return lane ? op(wex, lex) : wex;
+}
+
+// lz_argmax_p1 (src/sampler.c:279-295): the first index of the maximum (by
+// `>`) and 1 / l, l the online softmax normaliser: l starts at 1 for
+// element 0; a new running maximum v rescales it, l = l * exp(best - v) + 1;
+// every other element adds exp(v - best) in index order.  The positions of
+// the running maxima (records) are found by a block scan and written to
+// recs (n ints); the sums between records run as exact sequential chains
+// from the current l.  Every thread calls; all get the result.
+__device__ int block_argmax_p1(const float* __restrict__ lg, int n, float* p1, int* recs, float* stage, SampShared& sh) {
+  __shared__ int nrec_s;
+  const int tid = threadIdx.x;
+  const int per = (n + kSampThreads - 1) / kSampThreads;
+  const int a = min(n, tid * per), b = min(n, a + per);
+  uint32_t mk = 0u;
+  for (int i = a; i < b; i++) {
+    const uint32_t k = fkey(lg[i]);
+    mk = k > mk ? k : mk;
+  }
+  auto umax = [](uint32_t x, uint32_t y) { return x > y ? x : y; };
+  const uint32_t before = block_excl_scan_u32(mk, 0u, umax, nullptr);
+  // records of this thread's range, counted then written in order
+  auto walk = [&](int* out) {
+    int c = 0;
+    float run;
+    int i0 = a;
+    if (a == 0) {
+      run = lg[0];
+      i0 = 1;
+    } else {
+      run = key_float(before);
+    }
+    for (int i = i0; i < b; i++) {
+      const float v = lg[i];
+      if (v > run) {
+        if (out) out[c] = i;
+        c++;
+        run = v;
+      }
+    }
+    return c;
+  };
+  const int cnt = a < b ? walk(nullptr) : 0;
+  uint32_t tot;
+  const uint32_t off = block_excl_scan_u32((uint32_t)cnt, 0u, [](uint32_t x, uint32_t y) { return x + y; }, &tot);
+  if (a < b) walk(recs + off);
+  if (tid == 0) nrec_s = (int)tot;
+  __syncthreads();
+  const int nrec = nrec_s;
+  float l = 1.0f, best = lg[0];
+  int prev = 0;
+  for (int j = 0; j <= nrec; j++) {
+    const int r = j < nrec ? recs[j] : n;
+    const int len = r - prev - 1;
+    if (len > 0) {
+      const float bb = best;
+      const int p0 = prev + 1;
+      auto ev = [&](int t) { return exp_body(__fsub_rn(__ldcg(lg + p0 + t), bb)); };
+      l = block_chain<kChainSum>(ev, len, 0.0f, stage, sh, nullptr, l);
+    }
+    if (j < nrec) {
+      const float v = lg[r];
+      l = __fadd_rn(__fmul_rn(l, exp_body(__fsub_rn(best, v))), 1.0f);
+      best = v;
+      prev = r;
+    }
+  }
+  *p1 = l > 0.0f ? __fdiv_rn(1.0f, l) : 1.0f;
+  __syncthreads();
+  return prev;
 }
 
 // First index of the maximum by order key (src/sampler.c:224-240).
@@ -688,6 +791,25 @@ __global__ void __launch_bounds__(kSampThreads) temp_draft_kernel(const float* _
   }
 }
 
+// One greedy draft step's arg-max with its lz_argmax_p1 probability (the
+// confidence p_min is compared with, src/generate.c:756-762): sequence 0's
+// logits row; the token goes to sr[0].draft[i], the probability to conf[0].
+__global__ void __launch_bounds__(kSampThreads) argmax_p1_kernel(const float* __restrict__ logits, int V,
+                                                                SeqRound* sr, int i, int k, int* recs,
+                                                                float* conf) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) float stage[];
+  __shared__ SampShared sh;
+  float p1;
+  const int idx = block_argmax_p1(logits, V, &p1, recs, stage, sh);
+  if (threadIdx.x == 0) {
+    sr[0].draft[i] = idx;
+    sr[0].k = k;
+    conf[0] = p1;
+  }
+}
+
 // Target distributions of every verify row (lz_target_dist with the
 // sequence's temperature and top-p), one block per row b * (k + 1) + j.
 __global__ void __launch_bounds__(kSampThreads) temp_target_kernel(const float* __restrict__ logits, int V,
@@ -811,6 +933,19 @@ __global__ void __launch_bounds__(kSampThreads) chain_probe_kernel(const float* 
   if (threadIdx.x == 0) {
     out[0] = r;
     out[1] = __int_as_float(hit);
+  }
+}
+
+// Test hook: lz_argmax_p1 of one row (out[0] = probability, out[1] = index bits).
+__global__ void __launch_bounds__(kSampThreads) argmax_p1_probe_kernel(const float* __restrict__ v, int n, int* recs,
+                                                                      float* out) {
+  extern __shared__ __align__(16) float stage[];
+  __shared__ SampShared sh;
+  float p1;
+  const int idx = block_argmax_p1(v, n, &p1, recs, stage, sh);
+  if (threadIdx.x == 0) {
+    out[0] = p1;
+    out[1] = __int_as_float(idx);
   }
 }
 

@@ -73,6 +73,10 @@ def lib():
         "lz_generate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                 ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
                                 c_char_p, c_int]),
+        "lz_generate_ex": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                   ctypes.c_uint64, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p, c_int,
+                                   P(c_int), c_char_p, c_int]),
+        "lz_debug_argmax_p1": (c_int, [c_void_p, c_int, P(c_int), P(c_float)]),
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
                                      P(ctypes.c_double), P(c_int)]),
@@ -95,7 +99,7 @@ def lib():
     return L
 
 
-EXPORTS = ["lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+EXPORTS = ["lz_generate_ex", "lz_debug_argmax_p1", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
            "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
            "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
@@ -278,15 +282,20 @@ class State:
             raise LzError(f"batched round failed ({rc}): {err.value.decode()}")
         return toks, cnt
 
-    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1):
+    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max_new + 16, np.int32)
         rounds = np.zeros(2 * (max_new + 16), np.int32)
         on, nr = c_int(), c_int()
         err = ctypes.create_string_buffer(256)
-        rc = lib().lz_generate(self.m.h, self.h, _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
-                               _ptr(out), len(out), ctypes.byref(on), _ptr(rounds), len(rounds) // 2,
-                               ctypes.byref(nr), err, 256)
+        if p_min == 0.0 and n_min == 0:
+            rc = lib().lz_generate(self.m.h, self.h, _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
+                                   _ptr(out), len(out), ctypes.byref(on), _ptr(rounds), len(rounds) // 2,
+                                   ctypes.byref(nr), err, 256)
+        else:
+            rc = lib().lz_generate_ex(self.m.h, self.h, _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
+                                      float(p_min), int(n_min), _ptr(out), len(out), ctypes.byref(on),
+                                      _ptr(rounds), len(rounds) // 2, ctypes.byref(nr), err, 256)
         if rc:
             raise LzError(f"generate failed ({rc}): {err.value.decode()}")
         return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()
@@ -318,6 +327,16 @@ class Checkpoint:
         pos = c_int(-1)
         rc = lib().lz_ckpt_restore_seq(self.h, state.h, seq, ctypes.byref(pos), err, 256)
         return rc, pos.value
+
+
+def debug_argmax_p1(vals):
+    """The device lz_argmax_p1 of host values: (index, probability)."""
+    v = np.ascontiguousarray(vals, np.float32)
+    idx, p1 = c_int(), c_float()
+    rc = lib().lz_debug_argmax_p1(_ptr(v), len(v), ctypes.byref(idx), ctypes.byref(p1))
+    if rc:
+        raise LzError(f"lz_debug_argmax_p1 failed ({rc})")
+    return idx.value, p1.value
 
 
 def debug_seq_sum(vals, mode=0, target=0.0):

@@ -150,11 +150,32 @@ void rd_set_chain(void *vh, const float *chain) {
    out_tok receives every emitted token in order (cap out_cap);
    rounds receives (k_eff, n_accept) per speculative round (cap round_cap).
    Returns 0 on success, else a positive LZErr code. */
+int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
+                   int spec_k, float temp, float topp, unsigned long long seed,
+                   float p_min, int n_min,
+                   int *out_tok, int out_cap, int *out_n,
+                   int *rounds, int round_cap, int *n_rounds,
+                   double *elapsed_ms, double *prefill_ms);
+
 int rd_generate(void *vh, const int *prompt, int n_prompt, int max_new,
                 int spec_k, float temp, float topp, unsigned long long seed,
                 int *out_tok, int out_cap, int *out_n,
                 int *rounds, int round_cap, int *n_rounds,
                 double *elapsed_ms, double *prefill_ms) {
+    return rd_generate_pm(vh, prompt, n_prompt, max_new, spec_k, temp, topp, seed, 0.0f, 0,
+                          out_tok, out_cap, out_n, rounds, round_cap, n_rounds,
+                          elapsed_ms, prefill_ms);
+}
+
+/* The same loop with the rounds' p_min / n_min: a discarded draft
+   (n_emit == 0) emits nothing and forces a fresh capture next round
+   (src/generate.c:1972-2080). */
+int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
+                   int spec_k, float temp, float topp, unsigned long long seed,
+                   float p_min, int n_min,
+                   int *out_tok, int out_cap, int *out_n,
+                   int *rounds, int round_cap, int *n_rounds,
+                   double *elapsed_ms, double *prefill_ms) {
     RdHandle *h = (RdHandle *)vh;
     const LZModel *m = &h->m;
     LZRunState *s = &h->s;
@@ -228,20 +249,22 @@ int rd_generate(void *vh, const int *prompt, int n_prompt, int max_new,
             }
             if (temp > 0.0f)
                 n_emit = lz_spec_round_temp(m, s, anchor, anchor_pos, round_k,
-                                            0.0f, 0, &samp, 0, 0, out, &n_accept,
+                                            p_min, n_min, &samp, 0, 0, out, &n_accept,
                                             &new_pos, &k_eff, err, (int)sizeof err);
             else
                 n_emit = lz_spec_round(m, s, anchor, anchor_pos, round_k,
-                                       0.0f, 0, &samp, 0, 0, out, &n_accept,
+                                       p_min, n_min, &samp, 0, 0, out, &n_accept,
                                        &new_pos, &k_eff, err, (int)sizeof err);
             if (n_emit < 0) { rc = -n_emit; goto out; }
             if (nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_accept; }
             nr++;
             have_seed = (n_emit > 0);
-            for (ei = 0; ei <= n_accept; ei++) {
-                lz_sampler_observe(&samp, out[ei]);
-                if (n_out < out_cap) out_tok[n_out] = out[ei];
-                n_out++;
+            if (n_emit > 0) {
+                for (ei = 0; ei <= n_accept; ei++) {
+                    lz_sampler_observe(&samp, out[ei]);
+                    if (n_out < out_cap) out_tok[n_out] = out[ei];
+                    n_out++;
+                }
             }
             pos = new_pos + 1;
             token = out[n_accept];

@@ -28,6 +28,12 @@ CASES = {
 }
 
 
+PM_CASES = {
+    "tiny": [(3.5e-4, 0, 0.0), (3.5e-4, 2, 0.0), (2e-4, 0, 0.8), (1e-4, 2, 0.8)],
+    "midi": [(1.2e-3, 0, 0.0), (1.2e-3, 2, 0.0), (2e-4, 0, 0.8), (6e-4, 2, 0.8)],
+}
+
+
 def make(name):
     d = model_dir(name)
     cfg = lz98_synth.CONFIGS[name]
@@ -62,6 +68,14 @@ def make(name):
             toks, rounds = R.generate(prompt, max_new, k, temp=temp, seed=1234)
             tag = f"gen_t{int(temp * 10)}_k{k}"
             out[tag + "_tokens"], out[tag + "_rounds"] = toks, rounds
+    # rounds with p_min / n_min: (p_min, n_min, temperature), thresholds
+    # where the drafts' confidences straddle them on this model
+    cases = PM_CASES.get(name, [])
+    if cases:
+        out["pm_cases"] = np.array(cases, np.float64)
+        for j, (pm, nm, temp) in enumerate(cases):
+            toks, rounds = R.generate(prompt, max_new, 3, temp=temp, seed=1234, p_min=pm, n_min=int(nm))
+            out[f"pm{j}_tokens"], out[f"pm{j}_rounds"] = toks, rounds
     R.close()
     path = os.path.join(HERE, f"{name}.npz")
     np.savez_compressed(path, **out)

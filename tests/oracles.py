@@ -161,6 +161,9 @@ class Reference:
         L.rd_generate.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                   ctypes.c_ulonglong, c_void_p, c_int, P(c_int), c_void_p, c_int,
                                   P(c_int), P(ctypes.c_double), P(ctypes.c_double)]
+        L.rd_generate_pm.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                     ctypes.c_ulonglong, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p,
+                                     c_int, P(c_int), P(ctypes.c_double), P(ctypes.c_double)]
         L.rd_forward_verify.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
         L.rd_batch_capture.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
         L.rd_forward_capture.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p]
@@ -231,15 +234,16 @@ class Reference:
         t = np.ascontiguousarray(nxt, np.int32)
         return self.L.rd_mtp_prefill(c_void_p(self.h), _ptr(h), _ptr(t), len(t), pos0)
 
-    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1):
+    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max_new + 16, np.int32)
         rounds = np.zeros(2 * (max_new + 16), np.int32)
         on, nr = c_int(), c_int()
         el, pf = ctypes.c_double(), ctypes.c_double()
-        rc = self.L.rd_generate(c_void_p(self.h), _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
-                                _ptr(out), len(out), ctypes.byref(on), _ptr(rounds), len(rounds) // 2,
-                                ctypes.byref(nr), ctypes.byref(el), ctypes.byref(pf))
+        rc = self.L.rd_generate_pm(c_void_p(self.h), _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
+                                   c_float(p_min), int(n_min), _ptr(out), len(out), ctypes.byref(on),
+                                   _ptr(rounds), len(rounds) // 2, ctypes.byref(nr), ctypes.byref(el),
+                                   ctypes.byref(pf))
         if rc:
             raise RuntimeError(f"reference generate failed rc={rc}")
         self.last_elapsed_ms, self.last_prefill_ms = el.value, pf.value

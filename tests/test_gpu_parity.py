@@ -144,6 +144,25 @@ def test_temperature_generation_token_identical(gcase, k):
     s.close()
 
 
+def test_pmin_nmin_generation_matches_reference(gcase):
+    """Rounds with p_min (draft stops at the first step whose confidence -
+    lz_argmax_p1 greedy, q(x) sampled - is below it) and n_min (short drafts
+    discarded, then a fresh capture): the token stream and the (k_eff,
+    n_accept) record of each round equal the reference engine's."""
+    import lz98
+    name, d, g, m = gcase
+    if "pm_cases" not in g:
+        pytest.skip("no p_min vectors for this model")
+    max_new = 40 if name == "tiny" else 48
+    s = lz98.State(m, 512, 4)
+    for j, (pm, nm, temp) in enumerate(g["pm_cases"]):
+        toks, rounds = s.generate(g["prompt"], max_new, 3, temp=float(temp), topp=0.95, seed=1234,
+                                  p_min=float(pm), n_min=int(nm))
+        assert np.array_equal(rounds, g[f"pm{j}_rounds"]), (j, rounds[:, 0], g[f"pm{j}_rounds"][:, 0])
+        assert np.array_equal(toks, g[f"pm{j}_tokens"]), j
+    s.close()
+
+
 def test_batched_temperature_rounds_match_per_sequence_oracle(gcase):
     """Three sequences with their own generators in one state: the batched
     device temperature rounds emit each sequence's oracle stream."""

@@ -56,3 +56,21 @@ def test_sum_and_find_bit_exact():
                 assert hit == want, (name, frac, mode, hit, want)
                 want_val = c[want] if want >= 0 else c[-1]
                 assert np.float32(val).view(np.uint32) == want_val.view(np.uint32), (name, frac, mode)
+
+
+def test_argmax_p1_bit_exact():
+    """The device lz_argmax_p1 (records by a block scan, exact sequential
+    sums between them) against the oracle's sequential loop."""
+    import ctypes
+    import lz98
+    from argmax_rows import argmax_rows
+    from oracles import _Lib, ORACLE_SO
+    L = _Lib.load(ORACLE_SO)
+    L.lzo_argmax_p1.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+    for row in argmax_rows():
+        ref = ctypes.c_float()
+        ri = L.lzo_argmax_p1(ctypes.c_void_p(row.ctypes.data), len(row), ctypes.byref(ref))
+        gi, gp = lz98.debug_argmax_p1(row)
+        assert gi == ri
+        assert np.float32(gp).view(np.uint32) == np.float32(ref.value).view(np.uint32), (len(row), gp, ref.value)
+

@@ -197,3 +197,22 @@ def test_target_dist_matches(pair):
         O.L.lzo_target_dist(ctypes.c_float(0.8), ctypes.c_float(0.95), V(a.ctypes.data), n, V(p1.ctypes.data))
         R.L.rd_target_dist(ctypes.c_float(0.8), ctypes.c_float(0.95), V(b.ctypes.data), n, V(p2.ctypes.data))
         assert bits_equal(p1, p2)
+
+
+@needs_ref
+def test_argmax_p1_matches(pair):
+    """lz_argmax_p1 (src/sampler.c:279-295): the oracle's index and
+    online-softmax probability equal the reference's bit for bit."""
+    import ctypes
+    from argmax_rows import argmax_rows
+    O, R = pair
+    V, P = ctypes.c_void_p, ctypes.POINTER
+    O.L.lzo_argmax_p1.argtypes = [V, ctypes.c_int, P(ctypes.c_float)]
+    R.L.rd_argmax_p1.argtypes = [V, ctypes.c_int, P(ctypes.c_float)]
+    for row in argmax_rows():
+        a, b = ctypes.c_float(), ctypes.c_float()
+        i1 = O.L.lzo_argmax_p1(V(row.ctypes.data), len(row), ctypes.byref(a))
+        i2 = R.L.rd_argmax_p1(V(row.ctypes.data), len(row), ctypes.byref(b))
+        assert i1 == i2
+        assert np.float32(a.value).view(np.uint32) == np.float32(b.value).view(np.uint32)
+
