@@ -56,6 +56,9 @@ enum {
    (src/model.h:1333-1339).  Reads DIR/model.bin ("L98Z" v5) and uploads
    every tensor to device memory of the current CUDA device. */
 int  lz_open(LZModel **out, const char *dir, char *errbuf, int errlen);
+/* The tensors are already resident after lz_open: returns 0 for a valid
+   handle (kept so that the reference's open-then-read call order works). */
+int  lz_read_weights(LZModel *m, char *errbuf, int errlen);
 void lz_free(LZModel *m);
 /* vocab, hidden, n_layers, kda_heads, key_dim, latent, n_experts, top_k,
    shared_width, head_dim, n_heads, n_kv_heads, rotary_dim, seq_len,
@@ -213,6 +216,18 @@ int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *ou
    device - the arg-max and the online-softmax probability the greedy
    p_min compares. */
 int lz_debug_argmax_p1(const float *vals, int n, int *out_idx, float *out_p1);
+
+/* ---- debug data (src/forward.c:86-124, src/generate.c:226): host
+   microseconds spent in capture forwards, verify forwards, draft steps and
+   catch-ups, the capture and catch-up call counts, and the rounds that
+   rolled the state ring back (n_accept < k_eff, counted by lz_spec_round /
+   lz_spec_round_temp).  The direct entry points time themselves; the
+   parts of a device round are timed by CUDA events only while
+   lz_set_debug_timing(s, 1) is on (the events cut the programmatic-launch
+   overlap at their boundaries, so it is off by default). */
+extern long long lz_debug_us_verify, lz_debug_us_draft, lz_debug_us_capture, lz_debug_us_catchup;
+extern long long lz_debug_n_capture, lz_debug_n_catchup, lz_debug_n_ring_rollback;
+int lz_set_debug_timing(LZRunState *s, int enable);
 
 /* ---- recurrent-state checkpoints: replace lz_ckpt_alloc / lz_ckpt_free /
    lz_ckpt_save / lz_ckpt_restore (src/forward.h:1847-1862,

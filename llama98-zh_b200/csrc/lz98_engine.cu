@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <chrono>
 #include <initializer_list>
 #include <map>
 #include <string>
@@ -318,6 +319,17 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
   return 0;
 }
 
+// The reference reads the tensors in a second call after lz_open
+// (src/model.h:1333-1339); here lz_open already uploaded them to HBM, so
+// this only checks the handle.
+extern "C" int lz_read_weights(LZModel* m, char* errbuf, int errlen) {
+  if (!m) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  return 0;
+}
+
 extern "C" void lz_free(LZModel* m) {
   if (!m) return;
   for (void* p : m->allocs) cudaFree(p);
@@ -393,6 +405,8 @@ struct LZRunState {
   int* h_err = nullptr;
   int* d_err = nullptr;
   float* pconf = nullptr;            // confidence of a p_min draft step
+  bool dbg_timing = false;           // events around the parts of a round
+  cudaEvent_t dbg_ev[4] = {nullptr, nullptr, nullptr, nullptr};
 };
 
 // Wait for the state's stream; false on a CUDA error or when a kernel
@@ -418,7 +432,8 @@ void launch(LZRunState* s, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = s->pdl ? 1 : 0;
+  // debug timing puts event records between kernels: plain launches then
+  cfg.numAttrs = s->pdl && !s->dbg_timing ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   s->launches++;
 }
@@ -628,6 +643,8 @@ extern "C" void lz_state_free(LZRunState* s) {
   for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_err) cudaFreeHost(s->h_err);
+  for (auto e : s->dbg_ev)
+    if (e) cudaEventDestroy(e);
   if (s->st) cudaStreamDestroy(s->st);
   delete s;
 }
@@ -1141,6 +1158,13 @@ int upload_seqs(LZRunState* s, const std::vector<KdaSeq>& v) {
   return 0;
 }
 
+// Debug timing marks of a round: 0 before drafting, 1 before the verify, 2
+// after the acceptance, 3 after the catch-up.
+void dbg_mark(LZRunState* s, int i) {
+  // external records become event nodes of a captured round graph
+  if (s->dbg_timing) cudaEventRecordWithFlags(s->dbg_ev[i], s->st, cudaEventRecordExternal);
+}
+
 // The verify half of a greedy round with drafts sr[b].draft[0..k) and
 // sr[b].k == k: the (k+1)-row verify, acceptance, ring, chain reseed and
 // catch-up.
@@ -1152,8 +1176,10 @@ void verify_greedy(LZRunState* s, int k) {
   argmax(s, s->logits, R, 0);
   launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
                                                   s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  dbg_mark(s, 2);
   if (k > 1)
     mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+  dbg_mark(s, 3);
 }
 
 // The verify half of a temperature round (drafts and their q rows in place).
@@ -1166,20 +1192,24 @@ void verify_temp(LZRunState* s, int k) {
          s->sortbuf, s->npow2);
   launch(s, temp_accept_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->sr, k, s->kmax, s->pbuf, s->qbuf, V,
          s->hidden, c.d, s->chain, s->depth, s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  dbg_mark(s, 2);
   if (k > 1)
     mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
+  dbg_mark(s, 3);
 }
 
 // One greedy round of every sequence, all on the device.
 void round_greedy(LZRunState* s, int k) {
   const int B = s->B;
   const int tb = (B + 127) / 128;
+  dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
     launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
     mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
     argmax(s, s->logits, B, 1);
     launch(s, draft_store_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, k, s->vmax);
   }
+  dbg_mark(s, 1);
   verify_greedy(s, k);
 }
 
@@ -1192,12 +1222,14 @@ void round_temp(LZRunState* s, int k) {
   const Cfg& c = m->c;
   const int B = s->B, V = c.vocab;
   const int tb = (B + 127) / 128;
+  dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
     launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
     mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
     launch(s, temp_draft_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, i, k, s->kmax,
            s->qbuf);
   }
+  dbg_mark(s, 1);
   verify_temp(s, k);
 }
 
@@ -1221,6 +1253,7 @@ void round_any(LZRunState* s, int k) {
 int draft_pmin(LZRunState* s, int k, bool temp, float p_min) {
   const Cfg& c = s->m->c;
   int k_eff = 0;
+  dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
     launch(s, draft_setup_kernel, dim3(1), dim3(128), 0, s->sr, 1, i, s->seq_len, s->tok, s->mrows);
     mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
@@ -1255,6 +1288,7 @@ int round_pmin(LZRunState* s, int k, bool temp, float p_min, int n_min, int* k_e
   sr_down(s);
   s->h_sr[0].k = *k_eff;
   sr_up(s);
+  dbg_mark(s, 1);
   if (temp) verify_temp(s, *k_eff);
   else verify_greedy(s, *k_eff);
   return sync_ok(s) ? 1 : -1;
@@ -1271,6 +1305,68 @@ int sample_row(LZRunState* s, int seq, int* tok) {
 }
 
 }  // namespace
+
+// ============================================================ debug counters
+//
+// The reference's exported debug data (src/forward.c:86-124,
+// src/generate.c:226): microseconds of host time in capture forwards,
+// verify forwards, draft steps and catch-ups, their call counts, and the
+// number of rounds that rolled the state ring back (n_accept < k_eff).
+// The direct entry points time themselves; a device round is split into
+// its draft / verify / catch-up parts by CUDA events when
+// lz_set_debug_timing is on (off by default: the events cut the
+// programmatic-launch overlap at their boundaries).
+extern "C" {
+long long lz_debug_us_verify = 0;
+long long lz_debug_us_draft = 0;
+long long lz_debug_us_capture = 0;
+long long lz_debug_n_capture = 0;
+long long lz_debug_us_catchup = 0;
+long long lz_debug_n_catchup = 0;
+long long lz_debug_n_ring_rollback = 0;
+}
+
+namespace {
+struct UsTimer {
+  long long* acc;
+  std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+  explicit UsTimer(long long* a) : acc(a) {}
+  ~UsTimer() {
+    *acc += std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+  }
+};
+
+// Adds the event-timed parts of the last device round of sequence 0 (when
+// debug timing recorded them) and counts a rollback.
+void round_debug(LZRunState* s, int n_accept, int k_eff) {
+  if (n_accept < k_eff) lz_debug_n_ring_rollback++;
+  if (!s->dbg_timing) return;
+  float a = 0.0f, b = 0.0f, c = 0.0f;
+  if (cudaEventElapsedTime(&a, s->dbg_ev[0], s->dbg_ev[1]) == cudaSuccess &&
+      cudaEventElapsedTime(&b, s->dbg_ev[1], s->dbg_ev[2]) == cudaSuccess &&
+      cudaEventElapsedTime(&c, s->dbg_ev[2], s->dbg_ev[3]) == cudaSuccess) {
+    lz_debug_us_draft += (long long)(a * 1000.0f);
+    lz_debug_us_verify += (long long)(b * 1000.0f);
+    lz_debug_us_catchup += (long long)(c * 1000.0f);
+  } else {
+    cudaGetLastError();   // a failed timing query is not a failure of the round
+  }
+}
+}  // namespace
+
+extern "C" int lz_set_debug_timing(LZRunState* s, int enable) {
+  if (!s) return LZ98_ERR_NULL_ARG;
+  const bool on = enable != 0;
+  if (on && !s->dbg_ev[0])
+    for (auto& e : s->dbg_ev)
+      if (cudaEventCreate(&e) != cudaSuccess) return LZ98_ERR_CUDA;
+  if (on != s->dbg_timing) {
+    for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
+    s->graph.clear();
+  }
+  s->dbg_timing = on;
+  return 0;
+}
 
 // ================================================================== forwards
 
@@ -1313,6 +1409,8 @@ extern "C" float* lz_forward(const LZModel* m, LZRunState* s, int token, int pos
 }
 
 extern "C" float* lz_forward_capture(const LZModel* m, LZRunState* s, int token, int pos) {
+  UsTimer t(&lz_debug_us_capture);
+  lz_debug_n_capture++;
   return forward_one(m, s, &token, 1, pos, true, nullptr, false);
 }
 
@@ -1323,6 +1421,7 @@ extern "C" float* lz_forward_batch_capture(const LZModel* m, LZRunState* s, cons
 }
 
 extern "C" int lz_forward_verify(const LZModel* m, LZRunState* s, const int* tokens, int n, int pos0) {
+  UsTimer t(&lz_debug_us_verify);
   if (!m || !s || !tokens || n < 1 || n > s->kmax + 1) return 1;
   const Cfg& c = m->c;
   for (int i = 0; i < n; i++)
@@ -1345,6 +1444,7 @@ extern "C" const float* lz_state_mtp_verify_hidden(const LZRunState* s) {
 }
 
 extern "C" float* lz_mtp_draft_step(const LZModel* m, LZRunState* s, int next_token, int pos) {
+  UsTimer t(&lz_debug_us_draft);
   if (!m || !s) return nullptr;
   const Cfg& c = m->c;
   if (next_token < 0 || next_token >= c.vocab || pos < 0 || pos >= s->seq_len) return nullptr;
@@ -1382,6 +1482,8 @@ extern "C" int lz_mtp_prefill(const LZModel* m, LZRunState* s, const float* h_bo
 
 extern "C" int lz_mtp_catchup(const LZModel* m, LZRunState* s, const float* h_body_all, const int* next_tokens,
                               int n, int pos0) {
+  UsTimer t(&lz_debug_us_catchup);
+  lz_debug_n_catchup++;
   return lz_mtp_prefill(m, s, h_body_all, next_tokens, n, pos0);
 }
 
@@ -1532,10 +1634,11 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
     for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
     *out_n_accept = o.n_accept;
     *out_new_pos = anchor_pos + 1 + o.n_accept;
+    round_debug(s, o.n_accept, k_eff);
     return o.n_accept + 1;
   }
   if (run_round(s, k)) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
+    set_err(errbuf, errlen, "CUDA failure in the round: %s", cudaGetErrorString(cudaGetLastError()));
     return -LZ98_ERR_CUDA;
   }
   sr_down(s);
@@ -1548,6 +1651,7 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
   *out_n_accept = o.n_accept;
   *out_new_pos = anchor_pos + 1 + o.n_accept;
   *out_k_eff = k;
+  round_debug(s, o.n_accept, k);
   return o.n_accept + 1;
 }
 
@@ -1597,10 +1701,11 @@ extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, i
     for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
     *out_n_accept = o.n_accept;
     *out_new_pos = anchor_pos + 1 + o.n_accept;
+    round_debug(s, o.n_accept, k_eff);
     return o.n_accept + 1;
   }
   if (run_round(s, k)) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
+    set_err(errbuf, errlen, "CUDA failure in the round: %s", cudaGetErrorString(cudaGetLastError()));
     return -LZ98_ERR_CUDA;
   }
   sr_down(s);
@@ -1614,6 +1719,7 @@ extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, i
   *out_n_accept = o.n_accept;
   *out_new_pos = anchor_pos + 1 + o.n_accept;
   *out_k_eff = k;
+  round_debug(s, o.n_accept, k);
   return o.n_accept + 1;
 }
 

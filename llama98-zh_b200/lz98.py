@@ -77,6 +77,8 @@ def lib():
                                    ctypes.c_uint64, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p, c_int,
                                    P(c_int), c_char_p, c_int]),
         "lz_debug_argmax_p1": (c_int, [c_void_p, c_int, P(c_int), P(c_float)]),
+        "lz_read_weights": (c_int, [c_void_p, c_char_p, c_int]),
+        "lz_set_debug_timing": (c_int, [c_void_p, c_int]),
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
                                      P(ctypes.c_double), P(c_int)]),
@@ -99,7 +101,7 @@ def lib():
     return L
 
 
-EXPORTS = ["lz_generate_ex", "lz_debug_argmax_p1", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+EXPORTS = ["lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
            "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
            "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
@@ -327,6 +329,15 @@ class Checkpoint:
         pos = c_int(-1)
         rc = lib().lz_ckpt_restore_seq(self.h, state.h, seq, ctypes.byref(pos), err, 256)
         return rc, pos.value
+
+
+DEBUG_COUNTERS = ("lz_debug_us_verify", "lz_debug_us_draft", "lz_debug_us_capture", "lz_debug_us_catchup",
+                  "lz_debug_n_capture", "lz_debug_n_catchup", "lz_debug_n_ring_rollback")
+
+
+def debug_counters():
+    """The exported debug data symbols, by name."""
+    return {n: ctypes.c_longlong.in_dll(lib(), n).value for n in DEBUG_COUNTERS}
 
 
 def debug_argmax_p1(vals):

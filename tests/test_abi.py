@@ -34,6 +34,26 @@ def test_every_declared_symbol_is_exported(so):
     assert not missing, missing
 
 
+def declared_data():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    out = []
+    for decl in re.findall(r"extern\s+long\s+long\s+([^;]+);", txt):
+        out += [n.strip() for n in decl.split(",")]
+    return sorted(out)
+
+
+def test_debug_data_symbols_exported(so):
+    """The reference's debug data (src/forward.c:86-124, src/generate.c:226)
+    are exported as 64-bit integers that start at 0."""
+    import lz98
+    names = declared_data()
+    assert "lz_debug_n_ring_rollback" in names and "lz_debug_us_verify" in names
+    assert sorted(lz98.DEBUG_COUNTERS) == names
+    for n in names:
+        assert ctypes.c_longlong.in_dll(so, n).value >= 0
+
+
 def test_binding_covers_header():
     import lz98
     assert sorted(lz98.EXPORTS) == declared()

@@ -163,6 +163,26 @@ def test_pmin_nmin_generation_matches_reference(gcase):
     s.close()
 
 
+def test_debug_counters(gcase):
+    """With debug timing on, a generation still reproduces the reference's
+    stream; lz_debug_n_ring_rollback grows by the rounds with n_accept <
+    k_eff, and the event-timed draft and verify microseconds grow."""
+    import lz98
+    name, d, g, m = gcase
+    max_new = 40 if name == "tiny" else 48
+    s = lz98.State(m, 512, 4)
+    assert lz98.lib().lz_set_debug_timing(s.h, 1) == 0
+    c0 = lz98.debug_counters()
+    toks, rounds = s.generate(g["prompt"], max_new, 2)
+    c1 = lz98.debug_counters()
+    assert np.array_equal(toks, g["gen_t0_k2_tokens"])
+    assert c1["lz_debug_n_ring_rollback"] - c0["lz_debug_n_ring_rollback"] == int((rounds[:, 1] < rounds[:, 0]).sum())
+    assert c1["lz_debug_us_draft"] > c0["lz_debug_us_draft"]
+    assert c1["lz_debug_us_verify"] > c0["lz_debug_us_verify"]
+    assert lz98.lib().lz_set_debug_timing(s.h, 0) == 0
+    s.close()
+
+
 def test_batched_temperature_rounds_match_per_sequence_oracle(gcase):
     """Three sequences with their own generators in one state: the batched
     device temperature rounds emit each sequence's oracle stream."""
