@@ -708,6 +708,17 @@ __device__ void block_target_dist(const float* lg, int n, float temp, float topp
   // kept: every p > v_last, and the first `need` (by index) of p == v_last
   const float vl = sorted[nu.last];
   const int need = nu.last + 1 - block_first_pos(sorted, nu.last, sh);
+  // every element equal to v_last kept (the usual case): no ordered count
+  int eq_all = 0;
+  for (int j = threadIdx.x; j < n; j += kSampThreads) eq_all += p[j] == vl;
+  if (block_sum_i(eq_all, sh) <= need) {
+    for (int j = threadIdx.x; j < n; j += kSampThreads) {
+      const float v = p[j];
+      p[j] = v >= vl ? __fdiv_rn(v, nu.mass) : 0.0f;
+    }
+    __syncthreads();
+    return;
+  }
   if (threadIdx.x == 0) sh.carry = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
