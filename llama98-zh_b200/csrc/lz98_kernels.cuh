@@ -1642,7 +1642,7 @@ struct MoeTma {
   static constexpr int MW = W13 ? 4 : 2;            // 16-row weight tiles per warp (w13: 2 of w1 + 2 of w3)
   static constexpr int BOX = 128;                   // weight rows per box (w13: a w1 box and a w3 box)
   static constexpr int NBOX = W13 ? 2 : 1;
-  static constexpr int NST = 3;
+  static constexpr int NST = W13 ? 2 : 3;          // w13: two stages let 3 blocks fit per SM (measured faster)
   static constexpr int B = NBOX * BOX * 128;        // swizzled weight tile per stage
   static constexpr int WS = RB1 ? NBOX * BOX * 16 : 0;
   static constexpr int KMAX = 1024;
