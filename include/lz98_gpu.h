@@ -216,6 +216,11 @@ int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *ou
    device - the arg-max and the online-softmax probability the greedy
    p_min compares. */
 int lz_debug_argmax_p1(const float *vals, int n, int *out_idx, float *out_p1);
+/* Test hook: a kernel waits on an mbarrier that nothing arrives on; its
+   bounded wait (about a second, the limit every wait of this library has)
+   gives up and reports 2 in *out_err without a fault.  *out_ms: the call's
+   duration. */
+int lz_debug_wait_timeout(int *out_err, double *out_ms);
 
 /* ---- debug data (src/forward.c:86-124, src/generate.c:226): host
    microseconds spent in capture forwards, verify forwards, draft steps and

@@ -2092,6 +2092,25 @@ extern "C" int lz_debug_seq_sum(const float* vals, int n, int mode, float target
   return 0;
 }
 
+extern "C" int lz_debug_wait_timeout(int* out_err, double* out_ms) {
+  if (!out_err) return LZ98_ERR_NULL_ARG;
+  int* h = nullptr;
+  int* d = nullptr;
+  if (cudaHostAlloc((void**)&h, sizeof(int), cudaHostAllocMapped) != cudaSuccess) return LZ98_ERR_ALLOC;
+  *h = 0;
+  int rc = cudaHostGetDevicePointer((void**)&d, h, 0) == cudaSuccess ? 0 : LZ98_ERR_CUDA;
+  const auto t0 = std::chrono::steady_clock::now();
+  if (!rc) {
+    wait_timeout_probe_kernel<<<1, 32>>>(d);
+    if (cudaDeviceSynchronize() != cudaSuccess) rc = LZ98_ERR_CUDA;
+  }
+  if (out_ms)
+    *out_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  *out_err = *(volatile int*)h;
+  cudaFreeHost(h);
+  return rc;
+}
+
 extern "C" int lz_debug_argmax_p1(const float* vals, int n, int* out_idx, float* out_p1) {
   if (!vals || n < 1 || !out_idx || !out_p1) return LZ98_ERR_NULL_ARG;
   float *dv = nullptr, *dout = nullptr;

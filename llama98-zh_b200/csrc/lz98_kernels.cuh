@@ -890,6 +890,19 @@ __global__ void __launch_bounds__(288) gemm_q8_tma_kernel(const __grid_constant_
       }
 }
 
+// Test hook: one thread waits on an mbarrier that nothing ever arrives on.
+// The bounded wait gives up after about a second and the kernel reports
+// through *err, with no fault and the context still usable.
+__global__ void wait_timeout_probe_kernel(int* err) {
+  __shared__ __align__(8) unsigned long long bar;
+  if (threadIdx.x == 0) {
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    mbar_fence_init();
+    if (!mbar_wait(b, 0)) atomicExch(err, 2);
+  }
+}
+
 // --------------------------------------------------------- row kernels
 
 // rmsnorm (1+w) of one row, then per-32 quantisation of the result; the

@@ -74,3 +74,17 @@ def test_argmax_p1_bit_exact():
         assert gi == ri
         assert np.float32(gp).view(np.uint32) == np.float32(ref.value).view(np.uint32), (len(row), gp, ref.value)
 
+
+def test_bounded_wait_reports_and_context_survives():
+    """A wait that never completes (an mbarrier nothing arrives on) gives up
+    after about a second and reports through the error word; the context
+    stays usable (the next device call works)."""
+    import ctypes
+    import lz98
+    err, ms = ctypes.c_int(-1), ctypes.c_double()
+    assert lz98.lib().lz_debug_wait_timeout(ctypes.byref(err), ctypes.byref(ms)) == 0
+    assert err.value == 2
+    assert 500.0 < ms.value < 20000.0
+    v, hit = lz98.debug_seq_sum(np.ones(100, np.float32))
+    assert v == 100.0
+
