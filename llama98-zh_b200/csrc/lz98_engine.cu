@@ -1025,10 +1025,18 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
                   m->off_fa, c.rank, L.fb.q, L.fb.s, L.fb.gs, L.a_log, L.dt_bias, c.lb, nvk, c.kd, s->gate,
                   (c.conv_dim + 255) / 256, (nvk + 255) / 256, nseq};
     launch(s, kda_pre_kernel, dim3(pa.nconv_x * nseq + pa.nfb_x * R), dim3(256), 0, pa);
-    launch(s, kda_recur_kernel, dim3(c.nv, nseq), dim3(kRecurThreads), 0, 
-        s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
-        s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
-        s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
+    // few (head, sequence) blocks (batch 1): 16 warps per block halve the
+    // per-token requantisation pass; otherwise 8 warps, 4 blocks per SM
+    if (c.nv * nseq <= s->n_sm / 2)
+      launch(s, kda_recur_kernel<2 * kRecurThreads>, dim3(c.nv, nseq), dim3(2 * kRecurThreads), 0,
+             s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
+             s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
+             s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
+    else
+      launch(s, kda_recur_kernel<kRecurThreads>, dim3(c.nv, nseq), dim3(kRecurThreads), 0,
+             s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
+             s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
+             s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
     gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);
     const InNorm post{s->x, L.post_ln, nullptr, nullptr};
     gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe, 0, nullptr, nullptr, nullptr, &post);

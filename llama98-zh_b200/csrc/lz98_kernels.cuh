@@ -1114,7 +1114,8 @@ LZ_HD void requant_2p(float buf, float iv, int8_t& h8, int8_t& l8, float& e) {
   e = __fadd_rn(hf, __fmul_rn((float)lq, 1.0f / kLoScale));
 }
 
-__global__ void __launch_bounds__(kRecurThreads, 4)
+template <int NTH>
+__global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2)
 kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  const float* __restrict__ inproj, int ldi, int off_b, int off_g,
                  const float* __restrict__ gate, int nvk,
@@ -1126,7 +1127,7 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
                  int8_t* oq, float* os) {
   pdl_trigger();
   pdl_wait();
-  constexpr int KD = 64, VD = 64, TB = kRecurTB, NW = kRecurThreads / 32;
+  constexpr int KD = 64, VD = 64, TB = kRecurTB, NW = NTH / 32;
   __shared__ __align__(16) int8_t hi[KD][VD];
   __shared__ __align__(16) int8_t lo[KD][VD];
   __shared__ __align__(16) float sc[KD][2];
@@ -1144,19 +1145,21 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   const size_t seq_off = (size_t)sq.seq * seq_stride_q;
   {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
-    reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
+    if (tid < KD * VD / 16) {
+      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
+      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
+    }
     if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
   }
   __syncthreads();
-  for (int q = tid; q < KD * VD; q += kRecurThreads) {
+  for (int q = tid; q < KD * VD; q += NTH) {
     const int kk = q >> 6, vv = q & 63;
     E[kk][vv] = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
   }
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
     // stage the batch (raw q, k in qn/kn until normalised)
-    for (int q = tid; q < nt * 64; q += kRecurThreads) {
+    for (int q = tid; q < nt * 64; q += NTH) {
       const int t = q >> 6, i = q & 63;
       const size_t r = (size_t)(sq.row0 + t0 + t);
       qn[t][i] = conv_out[r * ldc + h * KD + i];
@@ -1175,9 +1178,9 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
         else beta[t] = sigmoid(inproj[(size_t)(sq.row0 + t0 + t) * ldi + off_b + h]);
       }
     }
-    static_assert(2 * (kRecurThreads / 32) >= 3 * kRecurTB, "chains per batch exceed the warps");
+    static_assert(2 * (NTH / 32) >= 3 * kRecurTB, "chains per batch exceed the warps");
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += kRecurThreads) {
+    for (int q = tid; q < nt * 64; q += NTH) {
       const int t = q >> 6, i = q & 63;
       qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), ssm_scale);
       kn[t][i] = __fmul_rn(kn[t][i], inv_k[t]);
@@ -1192,7 +1195,7 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
           const float g = gv[t][kk];
           SCX[0][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(kn[t][kk], g));
           SCX[1][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(qn[t][kk], g));
-        } else {
+        } else if (tid < 4 * VD) {
           SCG[kk][grp] = __fmul_rn(sc[kk][grp], gv[t][kk]);
         }
       }
@@ -1250,8 +1253,10 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
       if (adv) {
         const int so = (sq.base_slot + t0 + t + 1) % depth;
         const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
-        reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-        reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+        if (tid < KD * VD / 16) {
+          reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+          reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+        }
         if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
       }
     }
@@ -1259,7 +1264,7 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
     if (lane == 0 && warp < nt)
       inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), eps));
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += kRecurThreads) {
+    for (int q = tid; q < nt * 64; q += NTH) {
       const int t = q >> 6, i = q & 63;
       const size_t r = (size_t)(sq.row0 + t0 + t);
       const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), o_norm[i]), silu(zs[t][i]));
@@ -1269,8 +1274,10 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   }
   if (!adv) {
     const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
-    reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-    reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+    if (tid < KD * VD / 16) {
+      reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+      reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+    }
     if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
   }
 }

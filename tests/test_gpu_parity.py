@@ -110,6 +110,35 @@ def test_batched_rounds_match_per_sequence_oracle(gcase):
     s.close()
 
 
+def test_recurrence_block_shapes_agree(gcase):
+    """The recurrence runs 16 warps per block when few (head, sequence)
+    blocks exist and 8 otherwise: 40 sequences (8-warp blocks) reproduce,
+    for the first three, the streams of a 3-sequence state (16-warp blocks,
+    checked against the oracle above), greedy and at temperature 0.8."""
+    import lz98
+    name, d, g, m = gcase
+    k, n_rounds = 2, 4
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, m.vocab, 9 + (b * 7) % 13).astype(np.int32) for b in range(40)]
+    for temp in (0.0, 0.8):
+        streams = []
+        for B in (3, 40):
+            s = lz98.State(m, 256, 4, n_seq=B)
+            out = [[] for _ in range(3)]
+            for b in range(B):
+                s.set_sampler(b, temp, 0.95, 1000 + b)
+                t = s.seq_prefill(b, prompts[b])
+                if b < 3:
+                    out[b].append(t)
+            for _ in range(n_rounds):
+                toks, cnt = s.round_batch(k)
+                for b in range(3):
+                    out[b].extend(toks[b, :cnt[b]].tolist())
+            streams.append(out)
+            s.close()
+        assert streams[0] == streams[1], temp
+
+
 def test_graph_and_eager_rounds_agree(gcase):
     """Graph replay with programmatic dependent launch against plain
     eager launches: identical tokens."""
