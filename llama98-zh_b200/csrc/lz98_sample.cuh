@@ -140,6 +140,21 @@ LZ_HD uint32_t fulps(int Ej, uint32_t Mj, int Es, bool& tie) {
   return q + (rem > half ? 1u : 0u);
 }
 
+// fulps without branches (the rounding of every addend of a window runs in
+// one pass): shifts right by r = Es - Ej (clamped to 31, zero when the
+// addend's exponent is at or above the grid's), round half up, flag exact
+// halves; addends one binade above the grid double, two or more saturate.
+LZ_HD uint32_t fulps_bf(int Ej, uint32_t Mj, int Es, bool& tie) {
+  const int sh = Ej - Es;
+  const uint32_t r = (uint32_t)min(max(-sh, 0), 31);
+  const uint32_t rem = Mj & ((1u << r) - 1u);
+  const uint32_t half = r ? 1u << (r - 1u) : 0u;
+  tie = r != 0u && rem == half;
+  const uint32_t down = (Mj >> r) + (rem > half ? 1u : 0u);
+  const uint32_t up = sh >= 2 ? kUlpSat : min(Mj << 1, kUlpSat);
+  return sh >= 1 ? up : down;
+}
+
 // The find condition on the grid of exponent Es: a cumulative m * u meets
 // the target iff m > floor(target / u) (kChainFindLt) or m >= ceil(target /
 // u) (kChainFindGe); returns that integer bound (target >= 0 here; a
@@ -191,10 +206,12 @@ LZ_HD U2 warp_incl_scan_u2(U2 v) {
 
 struct ChainShared {
   U2 wt2[kSampWarps];                 // warp compositions, then exclusive prefixes
-  uint32_t wt[kSampWarps];            // warp totals, then exclusive offsets
+  uint32_t wt[kSampWarps];            // warp totals
+  int wtie[kSampWarps];               // warp has a tie
   int wstop[kSampWarps], wfind[kSampWarps];
   int S, F;
   float sum;
+  float sum2[2];                      // running sum after a round, by round parity
   int hit;
 };
 
@@ -252,6 +269,7 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
   __syncthreads();
   float s = cs.sum;
   int found = cs.hit;
+  int par = 0;   // slot of cs.sum2 the next round writes
   for (int w0 = nh; w0 < n && found < 0; w0 += kChainWin) {
     const int j0 = w0 + tid * kChainPer;
     const int wend = min(n, w0 + kChainWin);
@@ -288,43 +306,79 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
       int Es;
       uint32_t Ms;
       fdecomp(s, Es, Ms);
-      // per addend a parity function (ulps if the running count is even,
-      // ulps if odd): equal halves except at an exact tie
-      U2 pre[kChainPer];
-      uint32_t livemask = 0u;
-      U2 run = {0u, 0u};
+      // per addend its ulp count and whether it ties; a tie adds floor or
+      // one more by the parity of the running count
+      uint32_t qv[kChainPer];
+      uint32_t livemask = 0u, tiemask = 0u;
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
         const bool live = j0 + k >= cur && j0 + k < wend;
         bool t;
-        const uint32_t q = live ? fulps(ve[k], vm[k], Es, t) : 0u;
+        const uint32_t q = fulps_bf(ve[k], vm[k], Es, t);
+        qv[k] = live ? q : 0u;
         livemask |= live ? 1u << k : 0u;
-        const U2 d = (live && t) ? U2{q + (q & 1u), q + ((q + 1u) & 1u)} : U2{q, q};
-        run = u2_then(run, d);
-        pre[k] = run;
+        tiemask |= (live && t) ? 1u << k : 0u;
       }
-      // block exclusive scan of the thread compositions (warp 0 scans the warps)
-      const U2 incl = warp_incl_scan_u2(run);
-      if (lane == 31) cs.wt2[warp] = incl;
-      __syncthreads();
-      if (warp == 0) {
-        const U2 x = warp_incl_scan_u2(cs.wt2[lane]);
-        const U2 ex = {__shfl_up_sync(0xffffffffu, x.a, 1), __shfl_up_sync(0xffffffffu, x.b, 1)};
-        cs.wt2[lane] = lane ? ex : U2{0u, 0u};
-      }
-      __syncthreads();
-      // composition of everything before this thread, applied to Ms
-      const U2 lb = {__shfl_up_sync(0xffffffffu, incl.a, 1), __shfl_up_sync(0xffffffffu, incl.b, 1)};
-      const U2 before = u2_then(cs.wt2[warp], lane ? lb : U2{0u, 0u});
-      const uint32_t p0 = Ms & 1u;
-      const uint32_t off = sadd(Ms, p0 ? before.b : before.a);
-      const uint32_t p1 = off & 1u;          // parity entering this thread's addends
-      const int bound = MODE == kChainSum ? 0 : chain_bound<MODE>(target, Es);
-      uint32_t stopmask = 0u, hitmask = 0u;
+      // plain saturating prefix sums first; the block learns at the same
+      // barrier whether any addend of the window ties
+      // (a thread's counts are each <= 2^25: eight of them stay below 2^28
+      // without saturating; the warp and block sums saturate)
       uint32_t mk[kChainPer];
+      uint32_t off;
+      uint32_t run = 0u;
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
-        mk[k] = sadd(off, p1 ? pre[k].b : pre[k].a);
+        run += qv[k];
+        mk[k] = run;
+      }
+      const uint32_t incl = warp_incl_scan_sat(run);
+      const bool wtie = __any_sync(0xffffffffu, tiemask != 0u);
+      if (lane == 31) {
+        cs.wt[warp] = incl;
+        cs.wtie[warp] = wtie;
+      }
+      __syncthreads();
+      if (!__any_sync(0xffffffffu, cs.wtie[lane] != 0)) {
+        // every warp scans the 32 warp totals itself
+        const uint32_t xw = warp_incl_scan_sat(cs.wt[lane]);
+        const uint32_t wex = warp ? __shfl_sync(0xffffffffu, xw, warp - 1) : 0u;
+        const uint32_t lb = __shfl_up_sync(0xffffffffu, incl, 1);
+        off = sadd(sadd(Ms, wex), lane ? lb : 0u);
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++) mk[k] += off;   // < 2^25 + 2^28: no wrap
+      } else {
+        // a parity function per addend (count if the running count is
+        // even, count if odd), composed associatively
+        U2 pre[kChainPer];
+        U2 r2 = {0u, 0u};
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++) {
+          const uint32_t q = qv[k];
+          const U2 d = ((tiemask >> k) & 1u) ? U2{q + (q & 1u), q + ((q + 1u) & 1u)} : U2{q, q};
+          r2 = u2_then(r2, d);
+          pre[k] = r2;
+        }
+        const U2 in2 = warp_incl_scan_u2(r2);
+        if (lane == 31) cs.wt2[warp] = in2;
+        __syncthreads();
+        if (warp == 0) {
+          const U2 x = warp_incl_scan_u2(cs.wt2[lane]);
+          const U2 ex = {__shfl_up_sync(0xffffffffu, x.a, 1), __shfl_up_sync(0xffffffffu, x.b, 1)};
+          cs.wt2[lane] = lane ? ex : U2{0u, 0u};
+        }
+        __syncthreads();
+        // composition of everything before this thread, applied to Ms
+        const U2 lb = {__shfl_up_sync(0xffffffffu, in2.a, 1), __shfl_up_sync(0xffffffffu, in2.b, 1)};
+        const U2 before = u2_then(cs.wt2[warp], lane ? lb : U2{0u, 0u});
+        off = sadd(Ms, (Ms & 1u) ? before.b : before.a);
+        const uint32_t p1 = off & 1u;        // parity entering this thread's addends
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++) mk[k] = sadd(off, p1 ? pre[k].b : pre[k].a);
+      }
+      const int bound = MODE == kChainSum ? 0 : chain_bound<MODE>(target, Es);
+      uint32_t stopmask = 0u, hitmask = 0u;
+#pragma unroll
+      for (int k = 0; k < kChainPer; k++) {
         const uint32_t m = mk[k];
         stopmask |= ((livemask >> k) & 1u) && m >= 0x1000000u ? 1u << k : 0u;
         if (MODE == kChainFindLt) hitmask |= ((livemask >> k) & 1u) && (int)m > bound ? 1u << k : 0u;
@@ -333,33 +387,43 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
       const int st = stopmask ? j0 + __ffs(stopmask) - 1 : INT_MAX;
       int fd = hitmask ? j0 + __ffs(hitmask) - 1 : INT_MAX;
       if (fd >= st) fd = INT_MAX;
-      int S, Fd;
-      block_min2(st, fd, cs, S, Fd);
+      // block minima: every warp reduces the 32 warp minima itself
+      {
+        const int ws = __reduce_min_sync(0xffffffffu, st), wf = __reduce_min_sync(0xffffffffu, fd);
+        if (lane == 0) {
+          cs.wstop[warp] = ws;
+          cs.wfind[warp] = wf;
+        }
+      }
+      __syncthreads();
+      const int S = __reduce_min_sync(0xffffffffu, cs.wstop[lane]);
+      const int Fd = __reduce_min_sync(0xffffffffu, cs.wfind[lane]);
       int next;
+      float* nsum = &cs.sum2[par];
       if (Fd < S) {
         // a cumulative inside the segment meets the target
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == Fd) cs.sum = frecon(Es, mk[k]);
+          if (j0 + k == Fd) *nsum = frecon(Es, mk[k]);
         found = Fd;
         next = wend;
       } else if (S == INT_MAX) {
         // no stop: the segment runs to the window's end
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == wend - 1) cs.sum = frecon(Es, mk[k]);
+          if (j0 + k == wend - 1) *nsum = frecon(Es, mk[k]);
         next = wend;
       } else {
         // the addend that leaves the binade, by a real add from the exact
         // cumulative before it
 #pragma unroll
         for (int k = 0; k < kChainPer; k++)
-          if (j0 + k == S) cs.sum = __fadd_rn(frecon(Es, k ? mk[k - 1] : off), v[k]);
+          if (j0 + k == S) *nsum = __fadd_rn(frecon(Es, k ? mk[k - 1] : off), v[k]);
         next = S + 1;
       }
       __syncthreads();
-      s = cs.sum;
-      __syncthreads();
+      s = *nsum;
+      par ^= 1;   // the other slot next round: no barrier needed after the read
       if (found < 0 && S != INT_MAX && MODE != kChainSum && chain_cond<MODE>(s, target)) found = S;
       cur = next;
     }
