@@ -182,7 +182,8 @@ def run_batch32(m, args, rank: int, world: int):
     import lz98
     import lz98_synth
     cfg = lz98_synth.CONFIGS[MODEL]
-    prompts = lz98_synth.workload_prompts(cfg, B32, 256, 1024, 1.1, seed=rank)
+    lo, hi = args.b32_prompts                 # 256-1024 for the workload; shorter only to profile
+    prompts = lz98_synth.workload_prompts(cfg, B32, lo, hi, 1.1, seed=rank)
     e2e_steps = 8
     steps = max(1, min(args.steps, NEW32 // (K32 + 1) - args.warmup - e2e_steps - 2))
     seq_len = 1024 + (K32 + 1) * (args.warmup + steps + e2e_steps + 2) + 64
@@ -227,7 +228,7 @@ def run_batch32(m, args, rank: int, world: int):
     s.close()
     ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), n_e / dt_e, world, "cuda")
     return {
-        "workload": "configs[2]: ~0.5B KunMoe, 32 sequences per GPU, prompts 256-1024 Zipf(1.1), "
+        "workload": f"configs[2]: ~0.5B KunMoe, 32 sequences per GPU, prompts {lo}-{hi} Zipf(1.1), "
                     "temperature 0.8, top-p 0.95, k=3",
         "value": emitted_all / (ms_max * 1e-3), "unit": UNIT, "steps": steps, "warmup": args.warmup,
         "ms_per_step": ms_max / steps, "global_batch": B32 * world, "scaling": "weak",
@@ -443,6 +444,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the C-ABI end-to-end pass")
     ap.add_argument("--no-b32", action="store_true", help="skip the batch-32 temperature workload")
     ap.add_argument("--b32-only", action="store_true", help="run only the batch-32 workload (profiling)")
+    ap.add_argument("--b32-prompts", type=int, nargs=2, default=[256, 1024], metavar=("LO", "HI"),
+                    help="prompt length range of the batch-32 workload (default 256 1024, BASELINE configs[2]; "
+                         "shorter ranges only shorten the prefill for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
