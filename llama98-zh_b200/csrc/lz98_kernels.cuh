@@ -641,10 +641,7 @@ __global__ void __launch_bounds__(128) gemm_q8_warp_kernel(const GemvArgs a) {
 // weight scales) as 16-byte boxes beside them.  Full / empty mbarriers pace
 // the ring; every wait is bounded and a timeout sets *err and skips the
 // stores.  Requires K (and K2) % 128 == 0.
-#ifndef LZ_TMA_STAGES
-#define LZ_TMA_STAGES 4
-#endif
-constexpr int kTmaStages = LZ_TMA_STAGES;
+constexpr int kTmaStages = 4;
 constexpr int kTmaSub = 4;   // 32-byte sub-blocks per stage
 
 struct alignas(64) GemmTmaArgs {
