@@ -93,9 +93,60 @@ struct LZModel {
 
 namespace {
 
+// IEEE binary16 to binary32, exact (every half is a float): sign, then
+// zero / subnormal (normalised into a float exponent) / normal / inf-NaN.
+float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  uint32_t m = h & 0x3FFu, u;
+  if (e == 0) {
+    if (m == 0) {
+      u = sign;
+    } else {
+      int sh = 0;
+      while (!(m & 0x400u)) { m <<= 1; sh++; }
+      u = sign | ((uint32_t)(127 - 14 - sh) << 23) | ((m & 0x3FFu) << 13);
+    }
+  } else if (e == 0x1Fu) {
+    u = sign | 0x7F800000u | (m << 13);
+  } else {
+    u = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
 struct Reader {
   FILE* f = nullptr;
   bool bad = false;
+  int layout = 0;   // Q8_0 scale planes (src/model.c:3510-3556): 0 f32, 1 binary16, 2 binary16 row base + u8
+  // one scale plane of ng groups over `rows` rows, decoded to f32
+  void scales(float* dst, uint32_t ng, int rows) {
+    if (layout == 0) {
+      bytes(dst, (size_t)ng * 4);
+      return;
+    }
+    if (layout == 1) {
+      std::vector<uint16_t> h(ng);
+      bytes(h.data(), (size_t)ng * 2);
+      for (uint32_t i = 0; i < ng && !bad; i++) dst[i] = half_to_float(h[i]);
+      return;
+    }
+    if (rows <= 0 || ng % (uint32_t)rows) { bad = true; return; }
+    std::vector<uint16_t> hb(rows);
+    std::vector<uint8_t> code(ng);
+    bytes(hb.data(), (size_t)rows * 2);
+    bytes(code.data(), ng);
+    const uint32_t gpr = ng / (uint32_t)rows;
+    for (uint32_t i = 0; i < ng && !bad; i++) {
+      // base * (code / 255), the quotient and the product each rounded to
+      // float (the reference's lz_scale_u8_decode)
+      volatile float q = (float)code[i] / 255.0f;
+      volatile float p = half_to_float(hb[i / gpr]) * q;
+      dst[i] = p;
+    }
+  }
   void bytes(void* p, size_t n) {
     if (!bad && fread(p, 1, n, f) != n) bad = true;
   }
@@ -123,7 +174,7 @@ struct Reader {
     t.q.resize(cnt);
     t.s.resize(cnt / gs);
     bytes(t.q.data(), cnt);
-    bytes(t.s.data(), (cnt / gs) * 4);
+    scales(t.s.data(), cnt / gs, out);
     return t;
   }
 };
@@ -182,8 +233,8 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
   char magic[4];
   r.bytes(magic, 4);
   int ver = r.i32();
-  if (memcmp(magic, "L98Z", 4) != 0 || ver != 5) {
-    set_err(errbuf, errlen, "not an L98Z v5 model.bin");
+  if (memcmp(magic, "L98Z", 4) != 0 || ver < 5 || ver > 9) {
+    set_err(errbuf, errlen, "not an L98Z v5-v9 model.bin");
     fclose(r.f); delete m; return LZ98_ERR_MODEL;
   }
   // Header words in the order of src/model.c:3993-4301.
@@ -205,7 +256,26 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
   for (int i = 0; i < 3 * 128; i++) r.i32();
   for (int i = 0; i < 6; i++) r.i32();
   for (int i = 0; i < 128; i++) r.i32();
-  bool ok = !r.bad;
+  // v6-v9 words (src/model.c:4352-4440): this path takes the identity
+  // layer schedule, one MTP draft, no embedding rotation and no input
+  // mixing or local attention window; any scale layout
+  bool sched_ok = true;
+  if (ver >= 6) {
+    const int exec_len = r.i32();
+    int app_layer[128], app_loop[128];
+    for (int i = 0; i < 128; i++) app_layer[i] = r.i32();
+    for (int i = 0; i < 128; i++) app_loop[i] = r.i32();
+    const int n_draft = r.i32(), hadamard = r.i32();
+    r.i32();   // embed_signs_seed
+    r.layout = r.i32();
+    sched_ok = exec_len == c.nl && n_draft <= 1 && hadamard == 0 && r.layout >= 0 && r.layout <= 2;
+    for (int i = 0; i < 128 && sched_ok; i++)
+      sched_ok = app_layer[i] == (i < c.nl ? i : 0) && app_loop[i] == 0;
+  }
+  if (ver >= 7 && r.i32() != 0) sched_ok = false;   // loop_input_mix
+  if (ver >= 8 && r.i32() != 0) sched_ok = false;   // ced_local
+  if (ver >= 9) r.i32();                            // loop_input_mix_from (unused without mixing)
+  bool ok = !r.bad && sched_ok;
   for (int l = 0; l < c.nl && ok; l++) ok = lt[l] == 2;
   ok = ok && c.fkdr == 0 && c.ne > 0 && c.ne <= 256 && c.topk <= 16 && c.mtp_layers == 1 &&
        !c.lat_norm && c.has_lb && c.sigm && c.renorm && c.kd == 64 && c.vd == 64 &&

@@ -13,7 +13,8 @@ so this module writes the file from the loader's side of the contract:
   then the MTP block (attention rows of LAYER_SPECS, its dense FFN, then
   fc/norm/pre_fc_norm_hidden/pre_fc_norm_embedding);
 * each tensor as ``{dtype u8, n u32, [gs u32], data, [f32 scales]}``
-  (src/model.c:3567-3804, scale_layout 0).
+  (src/model.c:3567-3804); scale layouts 1 and 2 with a v6 header
+  (src/model.c:3510-3556, 4352-4410).
 
 Weights are N(0, 0.02), rounded to bf16, then quantised to Q8_0 with the
 activation quantiser's rule (scale = amax * (1/127), q = rne(x * 127/amax)
@@ -61,6 +62,7 @@ class KunMoeConfig:
     rope_theta: float = 10000000.0
     partial_rotary: float = 0.25
     seed: int = 0
+    scale_layout: int = 0         # Q8_0 scale planes: 0 f32, 1 binary16, 2 binary16 row base + u8 (v6 header)
 
     @property
     def n_heads(self) -> int:
@@ -116,6 +118,16 @@ CONFIGS = {
                          vocab=2048, n_experts=16, top_k=4, latent=128,
                          moe_ffn=256, shared_width=256, seq_len=256,
                          gs_mode="row", seed=11),
+    # The v6 scale layouts: binary16 scales (per row) and binary16 row base
+    # + u8 codes (per 32).
+    "midi_f16": KunMoeConfig(name="midi_f16", hidden=256, n_layers=2, kda_heads=4,
+                             vocab=2048, n_experts=16, top_k=4, latent=128,
+                             moe_ffn=256, shared_width=256, seq_len=256,
+                             gs_mode="row", seed=13, scale_layout=1),
+    "tiny_u8": KunMoeConfig(name="tiny_u8", hidden=256, n_layers=2, kda_heads=4,
+                            vocab=4096, n_experts=8, top_k=2, latent=128,
+                            moe_ffn=512, shared_width=0, seq_len=512,
+                            gs_mode="32", seed=17, scale_layout=2),
 }
 
 
@@ -176,7 +188,42 @@ def header_words(cfg: KunMoeConfig) -> bytes:
     w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([-1] * LZ_MAX_LAYERS)))     # csa2_source
     i32(0); i32(4); i32(64); i32(1); i32(64); i32(64)  # replay_w, compress_m, topk, idx heads/dim/rank
     w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([0] * LZ_MAX_LAYERS)))      # csa2_compress_m_layer
-    return b"L98Z" + struct.pack("<I", 5) + b"".join(w)
+    if not c.scale_layout:
+        return b"L98Z" + struct.pack("<I", 5) + b"".join(w)
+    # v6 words (src/model.c:4352-4410): the identity layer schedule, one
+    # MTP draft, no embedding rotation, then the scale layout
+    i32(c.n_layers)
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *(list(range(c.n_layers)) + [0] * (LZ_MAX_LAYERS - c.n_layers))))
+    w.append(struct.pack("<%di" % LZ_MAX_LAYERS, *([0] * LZ_MAX_LAYERS)))
+    i32(1); i32(0); i32(0); i32(c.scale_layout)
+    return b"L98Z" + struct.pack("<I", 6) + b"".join(w)
+
+
+def scale_plane_bytes(cfg: KunMoeConfig, ng: int, rows: int) -> int:
+    """Bytes of one Q8_0 tensor's scale plane under the config's layout
+    (src/model.c:3510-3556)."""
+    return {0: 4 * ng, 1: 2 * ng, 2: 2 * rows + ng}[cfg.scale_layout]
+
+
+def encode_scales(cfg: KunMoeConfig, scale: np.ndarray, rows: int):
+    """The stored scale plane and the f32 scales the engines decode from it:
+    layout 1 binary16 (round to nearest even); layout 2 a binary16 base per
+    row (the row's largest scale) and a u8 code per group, decoded as
+    base * (code / 255) with each step rounded to f32."""
+    if cfg.scale_layout == 0:
+        return scale.astype("<f4").tobytes(), scale
+    if cfg.scale_layout == 1:
+        h = scale.astype(np.float16)
+        return h.astype("<f2").tobytes(), h.astype(np.float32)
+    gpr = scale.size // rows
+    s2 = scale.reshape(rows, gpr)
+    base = s2.max(axis=1).astype(np.float16)
+    b32 = base.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        code = np.where(b32[:, None] > 0, np.rint(s2 / b32[:, None] * np.float32(255.0)), 0.0)
+    code = code.clip(0, 255).astype(np.uint8)
+    dec = (b32[:, None] * (code.astype(np.float32) / np.float32(255.0)).astype(np.float32)).astype(np.float32)
+    return base.astype("<f2").tobytes() + code.tobytes(), dec.reshape(-1)
 
 
 def tensor_specs(cfg: KunMoeConfig):
@@ -225,7 +272,7 @@ def tensor_specs(cfg: KunMoeConfig):
     out, off = [], len(header_words(cfg))
     for kind, shape, std, o in specs:
         n = int(np.prod(shape))
-        size = 5 + 4 * n if kind == "f32" else 9 + n + 4 * (n // cfg.gs(shape[1]))
+        size = 5 + 4 * n if kind == "f32" else 9 + n + scale_plane_bytes(cfg, n // cfg.gs(shape[1]), shape[0])
         out.append((kind, shape, std, o, off))
         off += size
     return out, off
@@ -243,6 +290,14 @@ def _tensor_bytes(cfg: KunMoeConfig, idx: int, spec) -> bytes:
         return struct.pack("<BI", FMT_F32, n) + x.astype("<f4").tobytes()
     gs = cfg.gs(shape[1])
     q, s = quantize_q8_rows(x, gs)
+    if cfg.scale_layout:
+        # quantise against the scales the engines will decode
+        plane, dec = encode_scales(cfg, s, shape[0])
+        flat = x.astype(np.float32).reshape(-1, gs)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            qq = np.where(dec[:, None] > 0, np.rint(flat / dec[:, None]), 0.0)
+        q = qq.clip(-127, 127).astype(np.int8).reshape(-1)
+        return struct.pack("<BII", FMT_Q8_0, n, gs) + q.tobytes() + plane
     return struct.pack("<BII", FMT_Q8_0, n, gs) + q.tobytes() + s.astype("<f4").tobytes()
 
 

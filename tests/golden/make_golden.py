@@ -25,6 +25,8 @@ CASES = {
     "tiny": (24, 4, 3, 40),
     "mini": (40, 4, 3, 48),
     "midi": (40, 4, 3, 48),
+    "midi_f16": (40, 4, 3, 48),
+    "tiny_u8": (24, 4, 3, 40),
 }
 
 

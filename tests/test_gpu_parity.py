@@ -21,7 +21,7 @@ def bits_equal(a, b):
     return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-@pytest.fixture(scope="module", params=["tiny", "mini", "midi"])
+@pytest.fixture(scope="module", params=["tiny", "mini", "midi", "midi_f16", "tiny_u8"])
 def gcase(request):
     from conftest import model_dir
     import lz98
@@ -77,7 +77,7 @@ def test_greedy_generation_token_identical(gcase, k):
     import lz98
     name, d, g, m = gcase
     s = lz98.State(m, 512, 4)
-    max_new = 40 if name == "tiny" else 48
+    max_new = 40 if name.startswith("tiny") else 48
     toks, rounds = s.generate(g["prompt"], max_new, k)
     tag = f"gen_t0_k{k}"
     assert np.array_equal(toks, g[tag + "_tokens"])
@@ -165,7 +165,7 @@ def test_temperature_generation_token_identical(gcase, k):
     import lz98
     name, d, g, m = gcase
     s = lz98.State(m, 512, 4)
-    max_new = 40 if name == "tiny" else 48
+    max_new = 40 if name.startswith("tiny") else 48
     toks, rounds = s.generate(g["prompt"], max_new, k, temp=0.8, topp=0.95, seed=1234)
     tag = f"gen_t8_k{k}"
     assert np.array_equal(toks, g[tag + "_tokens"])
@@ -182,7 +182,7 @@ def test_pmin_nmin_generation_matches_reference(gcase):
     name, d, g, m = gcase
     if "pm_cases" not in g:
         pytest.skip("no p_min vectors for this model")
-    max_new = 40 if name == "tiny" else 48
+    max_new = 40 if name.startswith("tiny") else 48
     s = lz98.State(m, 512, 4)
     for j, (pm, nm, temp) in enumerate(g["pm_cases"]):
         toks, rounds = s.generate(g["prompt"], max_new, 3, temp=float(temp), topp=0.95, seed=1234,
@@ -198,7 +198,7 @@ def test_debug_counters(gcase):
     k_eff, and the event-timed draft and verify microseconds grow."""
     import lz98
     name, d, g, m = gcase
-    max_new = 40 if name == "tiny" else 48
+    max_new = 40 if name.startswith("tiny") else 48
     s = lz98.State(m, 512, 4)
     assert lz98.lib().lz_set_debug_timing(s.h, 1) == 0
     c0 = lz98.debug_counters()
@@ -245,7 +245,7 @@ def test_temperature_round_abi_advances_generator(gcase):
     import lz98
     name, d, g, m = gcase
     p = g["prompt"]
-    max_new = 40 if name == "tiny" else 48
+    max_new = 40 if name.startswith("tiny") else 48
     O = Oracle(d, 512, 4)
     want, want_rounds = O.generate(p, max_new, 2, temp=0.8, topp=0.95, seed=77)
     O.close()

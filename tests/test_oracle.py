@@ -23,7 +23,7 @@ def load_golden(name):
     return dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
 
 
-@pytest.fixture(scope="module", params=["tiny", "mini", "midi"])
+@pytest.fixture(scope="module", params=["tiny", "mini", "midi", "midi_f16", "tiny_u8"])
 def case(request):
     from conftest import model_dir
     import lz98_synth
@@ -75,7 +75,7 @@ def test_oracle_generation_matches_golden(case, temp, k):
     name, d, g = case
     O = Oracle(d, 512, 4)
     tag = f"gen_t{int(temp * 10)}_k{k}"
-    toks, rounds = O.generate(g["prompt"], 40 if name == "tiny" else 48, k, temp=temp, seed=1234)
+    toks, rounds = O.generate(g["prompt"], 40 if name.startswith("tiny") else 48, k, temp=temp, seed=1234)
     assert np.array_equal(toks, g[tag + "_tokens"])
     assert np.array_equal(rounds, g[tag + "_rounds"])
     O.close()
