@@ -166,9 +166,24 @@ def reduce_over_ranks(ms: float, emitted: float, e2e, world: int, device: str):
 
 
 GEMV_TRAFFIC_RATIO = 1.045   # ncu dram bytes / algorithmic bytes of the int8 GEMV
+# ncu DRAM bytes / algorithmic bytes of the grouped-expert kernels at batch
+# 32 (w1/w3: 68.65 MB for 67.6 MB, w2: 34.30 MB for 33.7 MB per launch)
+EXPERT_TRAFFIC_RATIO = 1.016
 B32 = 32          # configs[2]: sequences per GPU
 K32 = 3
 NEW32 = 512
+
+
+def _expert_roofline(prof):
+    peak, peak_kind = measured_peak()
+    if not prof.get("n_expert"):
+        return None
+    achieved = prof["expert_bytes"] / (prof["expert_ms"] * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": "moe_tma_kernel (grouped experts w1/w3 and w2, all launches of one round)",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+            "traffic": prof["expert_bytes"] * EXPERT_TRAFFIC_RATIO,
+            "traffic_unit": "bytes per round (all grouped-expert launches)",
+            "launches": prof["n_expert"], "ms_per_round": prof["expert_ms"]}
 
 
 def run_batch32(m, args, rank: int, world: int):
@@ -239,6 +254,9 @@ def run_batch32(m, args, rank: int, world: int):
                 "api": "lz_spec_round_batch (round state device-resident, tokens and counts read back)"},
         "gemm_ms_per_round": prof["gemv_ms"], "round_ms_eager": prof["round_ms"],
         "gemm_algorithmic_gbs": prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9,
+        # the workload's HBM-bound kernels: every grouped-expert launch of
+        # one eager round, event-timed one by one on the state's stream
+        "roofline": _expert_roofline(prof),
         "gpu_launches": prof["n_kernels"] * steps,
     }
 

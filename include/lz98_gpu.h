@@ -187,6 +187,10 @@ int lz_state_counters(const LZRunState *s, int seq, int *rounds, int *emitted,
    the round's device time and its kernel count. */
 int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
                      int *n_gemv, double *round_ms, int *n_kernels);
+/* After lz_profile_round: the TMA-staged grouped-expert launches of that
+   round (event-timed one by one): summed device time, algorithmic bytes
+   (every expert's int8 weights and scales) and launch count. */
+int lz_profile_experts(const LZRunState *s, double *ms, double *bytes, int *n);
 /* Allocation-free logits (no counterpart in the reference): the tied
    lm_head over n final-normed hidden rows (as lz_forward_verify captures
    them), for callers that cannot allocate device memory themselves - a

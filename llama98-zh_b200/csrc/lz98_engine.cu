@@ -462,6 +462,11 @@ struct LZRunState {
   bool prof = false;
   std::vector<cudaEvent_t> prof_ev;
   std::vector<double> prof_bytes;
+  // and per grouped-expert launch (lz_profile_experts): event pairs, bytes
+  std::vector<cudaEvent_t> prof_moe_ev;
+  std::vector<double> prof_moe_bytes;
+  double prof_moe_ms = 0.0, prof_moe_b = 0.0;
+  int prof_moe_n = 0;
   std::map<int, cudaGraphExec_t> graph;
   std::vector<void*> allocs;
   // 1 at allocation, +1 per reset (src/forward_state.c:1412,
@@ -934,6 +939,18 @@ bool moe_tma(LZRunState* s, bool w13, const int8_t* wq, const float* wsc, int gs
   a.hq = s->hq; a.hs = s->hs; a.h2 = s->h2; a.err = s->d_err;
   a.K = K; a.gs = gs; a.rows_e = rows_e; a.ffn = c.moe_ffn; a.latent = c.latent; a.topk = c.topk;
   const dim3 grid((w13 ? c.moe_ffn : c.latent) / chunk, tmax);
+  if (s->prof) {
+    // algorithmic bytes with every expert touched (R >= 4 E / top_k makes
+    // an untouched expert unlikely): int8 weights + their scales
+    const double rows = (double)c.ne * rows_e;
+    s->prof_moe_bytes.push_back(rows * K + rows * (K / gs) * 4.0);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, s->st);
+    s->prof_moe_ev.push_back(e0);
+    s->prof_moe_ev.push_back(e1);
+  }
 #define LZ_MOE(W, RB, G) \
   launch(s, moe_tma_kernel<W, RB, G>, grid, dim3((MoeTma<W, RB>::CW + 1) * 32), MoeTma<W, RB>::smem(K), a)
   if (w13) {
@@ -946,6 +963,7 @@ bool moe_tma(LZRunState* s, bool w13, const int8_t* wq, const float* wsc, int gs
     else LZ_MOE(false, false, 2);
   }
 #undef LZ_MOE
+  if (s->prof) cudaEventRecord(s->prof_moe_ev.back(), s->st);
   return true;
 }
 
@@ -2023,6 +2041,8 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   s->prof = true;
   s->prof_ev.clear();
   s->prof_bytes.clear();
+  s->prof_moe_ev.clear();
+  s->prof_moe_bytes.clear();
   if (round_mode(s) < 0) return LZ98_ERR_NULL_ARG;
   const long long l0 = s->launches;
   cudaEventRecord(r0, s->st);
@@ -2039,6 +2059,16 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   }
   for (auto e : s->prof_ev) cudaEventDestroy(e);
   s->prof_ev.clear();
+  s->prof_moe_ms = s->prof_moe_b = 0.0;
+  for (size_t i = 0; i < s->prof_moe_bytes.size(); i++) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, s->prof_moe_ev[2 * i], s->prof_moe_ev[2 * i + 1]);
+    s->prof_moe_ms += ms;
+    s->prof_moe_b += s->prof_moe_bytes[i];
+  }
+  s->prof_moe_n = (int)s->prof_moe_bytes.size();
+  for (auto e : s->prof_moe_ev) cudaEventDestroy(e);
+  s->prof_moe_ev.clear();
   float rms = 0.0f;
   cudaEventElapsedTime(&rms, r0, r1);
   cudaEventDestroy(r0);
@@ -2048,6 +2078,16 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   if (n_gemv) *n_gemv = (int)s->prof_bytes.size();
   if (round_ms) *round_ms = rms;
   if (n_kernels) *n_kernels = (int)(s->launches - l0);
+  return 0;
+}
+
+// The grouped-expert launches of the last lz_profile_round: summed device
+// time, algorithmic bytes and launch count.
+extern "C" int lz_profile_experts(const LZRunState* s, double* ms, double* bytes, int* n) {
+  if (!s) return LZ98_ERR_NULL_ARG;
+  if (ms) *ms = s->prof_moe_ms;
+  if (bytes) *bytes = s->prof_moe_b;
+  if (n) *n = s->prof_moe_n;
   return 0;
 }
 

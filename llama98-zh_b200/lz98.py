@@ -78,6 +78,7 @@ def lib():
                                    P(c_int), c_char_p, c_int]),
         "lz_debug_argmax_p1": (c_int, [c_void_p, c_int, P(c_int), P(c_float)]),
         "lz_read_weights": (c_int, [c_void_p, c_char_p, c_int]),
+        "lz_profile_experts": (c_int, [c_void_p, P(ctypes.c_double), P(ctypes.c_double), P(c_int)]),
         "lz_debug_wait_timeout": (c_int, [P(c_int), P(ctypes.c_double)]),
         "lz_set_debug_timing": (c_int, [c_void_p, c_int]),
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
@@ -102,7 +103,7 @@ def lib():
     return L
 
 
-EXPORTS = ["lz_debug_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
            "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
            "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
@@ -187,8 +188,11 @@ class State:
                                     ctypes.byref(rm), ctypes.byref(nk))
         if rc:
             raise LzError(f"profile round failed ({rc})")
+        em, eb, en = ctypes.c_double(), ctypes.c_double(), c_int()
+        lib().lz_profile_experts(self.h, ctypes.byref(em), ctypes.byref(eb), ctypes.byref(en))
         return {"gemv_ms": gm.value, "gemv_bytes": gb.value, "n_gemv": ng.value,
-                "round_ms": rm.value, "n_kernels": nk.value}
+                "round_ms": rm.value, "n_kernels": nk.value,
+                "expert_ms": em.value, "expert_bytes": eb.value, "n_expert": en.value}
 
     def stream(self):
         return lib().lz_state_stream(self.h)
