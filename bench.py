@@ -374,7 +374,7 @@ def run_ours(args):
                          "peak_kind": peak_kind,
                          # DRAM bytes of the round's GEMV launches: the algorithmic
                          # bytes times the mean DRAM/algorithmic ratio of an ncu
-                         # capture (profiles/gemv_b1_dram_traffic.md)
+                         # capture of three GEMV launches (1.03-1.06)
                          "traffic": prof["gemv_bytes"] * GEMV_TRAFFIC_RATIO,
                          "traffic_unit": "bytes per round (all GEMV launches)",
                          "gemv_share_of_round": prof["gemv_ms"] / max(1e-9, prof["round_ms"]),
