@@ -66,7 +66,7 @@ def make(name):
     out["draft_logits"] = np.stack(dl)
     # whole generations
     for temp in (0.0, 0.8):
-        for k in (1, 2, 3):
+        for k in (0, 1, 2, 3):
             toks, rounds = R.generate(prompt, max_new, k, temp=temp, seed=1234)
             tag = f"gen_t{int(temp * 10)}_k{k}"
             out[tag + "_tokens"], out[tag + "_rounds"] = toks, rounds

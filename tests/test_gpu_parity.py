@@ -72,7 +72,7 @@ def test_capture_and_draft(gcase):
     O.close()
 
 
-@pytest.mark.parametrize("k", [1, 2, 3])
+@pytest.mark.parametrize("k", [0, 1, 2, 3])
 def test_greedy_generation_token_identical(gcase, k):
     import lz98
     name, d, g, m = gcase
@@ -157,7 +157,7 @@ def test_graph_and_eager_rounds_agree(gcase):
     assert outs[0] == outs[1]
 
 
-@pytest.mark.parametrize("k", [1, 2, 3])
+@pytest.mark.parametrize("k", [0, 1, 2, 3])
 def test_temperature_generation_token_identical(gcase, k):
     """Coupled temperature rounds (temp 0.8, top-p 0.95, seed 1234): the
     device draft sampling, target distributions, acceptance and residual

@@ -70,7 +70,7 @@ def test_oracle_draft_matches_golden(case):
 
 
 @pytest.mark.parametrize("temp", [0.0, 0.8])
-@pytest.mark.parametrize("k", [1, 2, 3])
+@pytest.mark.parametrize("k", [0, 1, 2, 3])
 def test_oracle_generation_matches_golden(case, temp, k):
     name, d, g = case
     O = Oracle(d, 512, 4)
