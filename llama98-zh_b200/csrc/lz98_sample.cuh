@@ -183,6 +183,7 @@ LZ_HD bool chain_cond(float c, float target) {
 constexpr int kChainHead = 1024;      // leading values summed serially
 constexpr int kChainPer = 8;          // values per thread per window
 constexpr int kChainWin = kChainPer * kSampThreads;
+constexpr uint32_t kChainAll = (1u << kChainPer) - 1u;   // all of a thread's addends
 
 // Composition of per-addend ulp counts that depend on the parity of the
 // running count (a: count even before, b: odd): `x then y`.  Saturating,
@@ -276,10 +277,14 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
     float v[kChainPer];
     int ve[kChainPer];
     uint32_t vm[kChainPer];
+    uint32_t inwin = 0u;               // this thread's addends inside the window
+    int emax = 1;                      // their largest exponent
 #pragma unroll
     for (int k = 0; k < kChainPer; k++) {
       v[k] = j0 + k < wend ? val(j0 + k) : 0.0f;
       fdecomp(v[k], ve[k], vm[k]);
+      inwin |= j0 + k < wend ? 1u << k : 0u;
+      emax = max(emax, ve[k]);
     }
     int cur = w0;                      // first index of the open segment
     while (cur < wend && found < 0) {
@@ -308,17 +313,33 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
       fdecomp(s, Es, Ms);
       // per addend its ulp count and whether it ties; a tie adds floor or
       // one more by the parity of the running count
+      const int dc = cur - j0;         // this thread's addends before cur are closed
+      const uint32_t livemask = dc <= 0 ? inwin : (dc >= kChainPer ? 0u : inwin & (kChainAll << dc));
       uint32_t qv[kChainPer];
-      uint32_t livemask = 0u, tiemask = 0u;
+      uint32_t tiemask = 0u;
+      if (emax <= Es) {
+        // every addend at or below the running sum's binade (the usual
+        // case): round half up by the added half, less one at an exact
+        // half, whose floor count the parity rule then settles
 #pragma unroll
-      for (int k = 0; k < kChainPer; k++) {
-        const bool live = j0 + k >= cur && j0 + k < wend;
-        bool t;
-        const uint32_t q = fulps_bf(ve[k], vm[k], Es, t);
-        qv[k] = live ? q : 0u;
-        livemask |= live ? 1u << k : 0u;
-        tiemask |= (live && t) ? 1u << k : 0u;
+        for (int k = 0; k < kChainPer; k++) {
+          const uint32_t r = (uint32_t)min(Es - ve[k], 31);
+          const uint32_t p2 = 1u << r, half = p2 >> 1;
+          const bool t = half != 0u && (vm[k] & (p2 - 1u)) == half;
+          qv[k] = ((vm[k] + half) >> r) - (t ? 1u : 0u);
+          tiemask |= t ? 1u << k : 0u;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kChainPer; k++) {
+          bool t;
+          qv[k] = fulps_bf(ve[k], vm[k], Es, t);
+          tiemask |= t ? 1u << k : 0u;
+        }
       }
+      tiemask &= livemask;
+#pragma unroll
+      for (int k = 0; k < kChainPer; k++) qv[k] = (livemask >> k) & 1u ? qv[k] : 0u;
       // plain saturating prefix sums first; the block learns at the same
       // barrier whether any addend of the window ties
       // (a thread's counts are each <= 2^25: eight of them stay below 2^28
@@ -380,10 +401,12 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
 #pragma unroll
       for (int k = 0; k < kChainPer; k++) {
         const uint32_t m = mk[k];
-        stopmask |= ((livemask >> k) & 1u) && m >= 0x1000000u ? 1u << k : 0u;
-        if (MODE == kChainFindLt) hitmask |= ((livemask >> k) & 1u) && (int)m > bound ? 1u << k : 0u;
-        if (MODE == kChainFindGe) hitmask |= ((livemask >> k) & 1u) && (int)m >= bound ? 1u << k : 0u;
+        stopmask |= m >= 0x1000000u ? 1u << k : 0u;
+        if (MODE == kChainFindLt) hitmask |= (int)m > bound ? 1u << k : 0u;
+        if (MODE == kChainFindGe) hitmask |= (int)m >= bound ? 1u << k : 0u;
       }
+      stopmask &= livemask;
+      hitmask &= livemask;
       const int st = stopmask ? j0 + __ffs(stopmask) - 1 : INT_MAX;
       int fd = hitmask ? j0 + __ffs(hitmask) - 1 : INT_MAX;
       if (fd >= st) fd = INT_MAX;
@@ -444,10 +467,16 @@ __device__ void block_softmax(const float* __restrict__ lg, int n, float inv_t, 
     best = k > best ? k : best;
   }
   const float mx = key_float(block_max_u32(best, sh));
-  auto ev = [&](int j) { return exp_body(__fsub_rn(__fmul_rn(__ldcg(lg + j), inv_t), mx)); };
+  // the sum chain evaluates every exp exactly once; each is kept in out
+  // and scaled there once the sum is known
+  auto ev = [&](int j) {
+    const float e = exp_body(__fsub_rn(__fmul_rn(__ldcg(lg + j), inv_t), mx));
+    out[j] = e;
+    return e;
+  };
   const float sum = block_chain<kChainSum>(ev, n, 0.0f, stage, sh, nullptr);
   const float invs = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
-  for (int j = threadIdx.x; j < n; j += kSampThreads) out[j] = __fmul_rn(ev(j), invs);
+  for (int j = threadIdx.x; j < n; j += kSampThreads) out[j] = __fmul_rn(out[j], invs);
   __syncthreads();
 }
 
