@@ -260,10 +260,35 @@ __device__ float block_chain(F val, int n, float target, float* stage, SampShare
   if (tid == 0) {
     float acc = init;
     int h = -1;
-    for (int t = 0; t < nh; t++) {
-      acc = __fadd_rn(acc, stage[t]);
-      if (MODE != kChainSum && chain_cond<MODE>(acc, target)) { h = t; break; }
+    int t = 0;
+    // four addends per 16-byte load, the loads ahead of the adds; the find
+    // modes test each cumulative in index order
+#pragma unroll 4
+    for (; t + 4 <= nh; t += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(stage + t);
+      const float a0 = __fadd_rn(acc, q.x);
+      const float a1 = __fadd_rn(a0, q.y);
+      const float a2 = __fadd_rn(a1, q.z);
+      const float a3 = __fadd_rn(a2, q.w);
+      if (MODE != kChainSum) {
+        const int c = chain_cond<MODE>(a0, target)   ? 0
+                      : chain_cond<MODE>(a1, target) ? 1
+                      : chain_cond<MODE>(a2, target) ? 2
+                      : chain_cond<MODE>(a3, target) ? 3
+                                                     : -1;
+        if (c >= 0) {
+          h = t + c;
+          acc = c == 0 ? a0 : (c == 1 ? a1 : (c == 2 ? a2 : a3));
+          break;
+        }
+      }
+      acc = a3;
     }
+    if (h < 0)
+      for (; t < nh; t++) {
+        acc = __fadd_rn(acc, stage[t]);
+        if (MODE != kChainSum && chain_cond<MODE>(acc, target)) { h = t; break; }
+      }
     cs.sum = acc;
     cs.hit = h;
   }
