@@ -13,8 +13,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SO = os.path.join(HERE, "liblz98gpu.so")
 SRCS = [os.path.join(HERE, "csrc", "lz98_engine.cu")]
-DEPS = SRCS + [os.path.join(HERE, "csrc", f) for f in ("lz98_kernels.cuh", "lz98_dev.cuh")] + \
-    [os.path.join(ROOT, "include", "lz98_gpu.h")]
+# every source and header of csrc/ (the engine includes them all) and the C ABI header
+DEPS = SRCS + sorted(os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))
+                     if f.endswith((".cu", ".cuh", ".h"))) + [os.path.join(ROOT, "include", "lz98_gpu.h")]
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
