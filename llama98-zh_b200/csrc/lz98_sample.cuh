@@ -668,6 +668,8 @@ __device__ void block_radix_sort_desc(uint32_t* a, uint32_t* tmp, int n, uint32_
     for (int i = tid; i < kSampWarps * 256; i += kSampThreads) hist[i] = 0u;
     __syncthreads();
     uint32_t* h = hist + warp * 256;
+    // the warp's digit counts (its own histogram: the order of the adds
+    // does not matter)
     for (int i0 = c0; i0 < c1; i0 += 32 * U) {
       uint32_t kk[U];
 #pragma unroll
@@ -676,13 +678,8 @@ __device__ void block_radix_sort_desc(uint32_t* a, uint32_t* tmp, int n, uint32_
         kk[u] = i < c1 ? __ldcg(src + i) : 0u;
       }
 #pragma unroll
-      for (int u = 0; u < U; u++) {
-        const bool ok = i0 + u * 32 + lane < c1;
-        const uint32_t d = (kk[u] >> shift) & 255u;
-        const unsigned peers = digit_peers(d, ok);
-        if (ok && (peers & lt) == 0u) h[d] += __popc(peers);
-        __syncwarp();
-      }
+      for (int u = 0; u < U; u++)
+        if (i0 + u * 32 + lane < c1) atomicAdd(&h[(kk[u] >> shift) & 255u], 1u);
     }
     __syncthreads();
     // exclusive offsets per (warp, digit): digit bases in digit order, then
