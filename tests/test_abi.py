@@ -105,3 +105,22 @@ def test_writer_header_layout():
     # magic + version + 28 words + 128 layer types + 13 + 17 + 3*128 + 6 + 128
     assert len(h) == 4 + 4 + 4 * (28 + 128 + 13 + 17 + 3 * 128 + 6 + 128)
     assert h[:4] == b"L98Z"
+
+
+def test_build_tracks_every_source():
+    """The in-tree build rebuilds the library when any source or header of
+    csrc/ (or the C-ABI header) is newer than it, and compiles the one
+    translation unit that includes them all."""
+    import build
+    csrc = os.path.join(ROOT, "llama98-zh_b200", "csrc")
+    files = {os.path.join(csrc, f) for f in os.listdir(csrc) if f.endswith((".cu", ".cuh", ".h"))}
+    assert files <= set(build.DEPS)
+    assert HEADER in build.DEPS
+    engine = open(os.path.join(csrc, "lz98_engine.cu")).read()
+    included = set(re.findall(r'#include "([^"]+)"', engine))
+    for f in files:
+        name = os.path.basename(f)
+        if name.endswith(".cuh"):
+            reach = name in included or any(
+                name in open(os.path.join(csrc, g)).read() for g in included if os.path.exists(os.path.join(csrc, g)))
+            assert reach, f"{name} is not included by the engine"
