@@ -395,10 +395,12 @@ def run_ours(args):
     return line
 
 
-def ref_sample(seconds_target: float = 20.0):
+def ref_sample(seconds_target: float = 20.0, stock: bool = False):
     """The reference engine on a bounded sample of the workload: a 16-token
-    prompt then greedy k=2 rounds until about `seconds_target` of decode.
-    Returns (tokens/s, detail)."""
+    prompt then greedy k=2 rounds until about `seconds_target` of decode,
+    in the parity float tier (the faster of the two on x86) or, with
+    `stock`, in the reference's default fixed-point tier.  Returns
+    (tokens/s, detail)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from oracles import Reference, reference_available
     import numpy as np
@@ -406,6 +408,8 @@ def ref_sample(seconds_target: float = 20.0):
         return None, "oracle/_ref/liblz98ref.so not built"
     d = model_dir()
     R = Reference(d, 2048, SPEC_K)
+    if stock:
+        R.stock_tier()
     rng = np.random.default_rng([0, 1000])
     prompt = rng.integers(0, R.vocab, 16).astype(np.int32)
     toks, rounds = R.generate(prompt, 8, SPEC_K)
@@ -414,14 +418,19 @@ def ref_sample(seconds_target: float = 20.0):
     toks, rounds = R.generate(prompt, n_new, SPEC_K)
     dec_ms = R.last_elapsed_ms - R.last_prefill_ms
     R.close()
-    return len(toks) / (dec_ms * 1e-3), f"reference C99 engine, 16-token prompt + {len(toks)} greedy k=2 tokens ({len(rounds)} rounds), decode only"
+    tier = "stock tier (--fixed all, --fastfp on)" if stock else "float tier (--fixed off, --fastfp off)"
+    return len(toks) / (dec_ms * 1e-3), f"reference C99 engine, {tier}, 16-token prompt + {len(toks)} greedy k=2 tokens ({len(rounds)} rounds), decode only"
 
 
 def cpu_baseline(args):
     v, sample = ref_sample(args.cpu_seconds)
     if v is None:
         return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample}
-    return {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample}
+    # the reference's default arithmetic too, on a shorter sample: the
+    # baseline above is the faster of the two
+    vs, sample_s = ref_sample(max(2.0, args.cpu_seconds / 3), stock=True)
+    return {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample,
+            "stock_tier": {"value": vs, "sample": sample_s}}
 
 
 def run_reference(args):

@@ -44,6 +44,19 @@ void rd_set_tier(int kernel) {
     lz_kernel_select(kernel);
 }
 
+/* The reference's stock arithmetic, its CLI defaults (cli_main.c:483,
+   cli_main.c:531): --fixed all (the shipping fixed-point tier) and --fastfp
+   on (round toward zero, flush to zero inside the engine's float regions,
+   which restore the caller's MXCSR on exit, ops_quant.c:2015-2050), with
+   the given kernel tier.  Used only to time the reference as shipped; its
+   tokens differ from the parity tier's by design.  Process-global like
+   rd_set_tier: it holds for every handle until the next call of either. */
+void rd_set_stock_tier(int kernel) {
+    lz_float_ref_select("all");
+    lz_fastfp_select("on");
+    lz_kernel_select(kernel);
+}
+
 void *rd_open(const char *dir, int seq_len, int spec_k_max, int nt_cap,
               int kernel, char *err, int errlen) {
     RdHandle *h = (RdHandle *)calloc(1, sizeof(RdHandle));

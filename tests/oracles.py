@@ -173,6 +173,8 @@ class Reference:
         L.rd_set_chain.argtypes = [c_void_p, c_void_p]
         L.rd_info.argtypes = [c_void_p, c_void_p]
         L.rd_reset.argtypes = [c_void_p]
+        L.rd_set_stock_tier.argtypes = [c_int]
+        L.rd_set_tier.argtypes = [c_int]
         L.rd_close.argtypes = [c_void_p]
         err = ctypes.create_string_buffer(512)
         self.h = L.rd_open(model_dir.encode(), seq_len, spec_k_max, nt_cap, kernel, err, 512)
@@ -186,6 +188,12 @@ class Reference:
         info = np.zeros(16, np.int32)
         self.L.rd_info(c_void_p(self.h), _ptr(info))
         return info
+
+    def stock_tier(self, kernel: int = 7):
+        """Switch the (process-global) reference arithmetic to its CLI
+        defaults, --fixed all and --fastfp on, for timing the reference as
+        shipped; its tokens then differ from the parity tier's."""
+        self.L.rd_set_stock_tier(kernel)
 
     def close(self):
         if self.h:

@@ -216,3 +216,24 @@ def test_argmax_p1_matches(pair):
         assert i1 == i2
         assert np.float32(a.value).view(np.uint32) == np.float32(b.value).view(np.uint32)
 
+
+
+@needs_ref
+def test_reference_stock_tier_and_back(tiny_dir):
+    """The reference's default arithmetic (--fixed all, --fastfp on), which
+    the bench times beside the parity tier, runs on the same model; the
+    tier is process-global, and selecting the parity tier again brings back
+    the golden greedy stream exactly."""
+    g = load_golden("tiny")
+    R = Reference(tiny_dir, 512, 4)
+    try:
+        R.stock_tier()
+        toks, _ = R.generate(g["prompt"], 40, 1)
+        assert len(toks) == 40 and int(toks.min()) >= 0 and int(toks.max()) < R.vocab
+        R.L.rd_set_tier(7)
+        toks, rounds = R.generate(g["prompt"], 40, 1)
+        assert np.array_equal(toks, g["gen_t0_k1_tokens"])
+        assert np.array_equal(rounds, g["gen_t0_k1_rounds"])
+    finally:
+        R.L.rd_set_tier(7)
+        R.close()
