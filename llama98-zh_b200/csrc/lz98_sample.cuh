@@ -126,24 +126,11 @@ LZ_HD float frecon(int E, unsigned long long m) {
 constexpr uint32_t kUlpSat = 1u << 25;
 LZ_HD uint32_t sadd(uint32_t a, uint32_t b) { return min(a + b, kUlpSat); }
 
-// ulps of v = Mj * 2^(Ej - 150) on the grid of exponent Es, rounded to
-// nearest (saturated); tie flags an exact half.
-LZ_HD uint32_t fulps(int Ej, uint32_t Mj, int Es, bool& tie) {
-  tie = false;
-  if (Mj == 0u) return 0u;
-  const int sh = Ej - Es;
-  if (sh >= 0) return sh >= 2 ? kUlpSat : min(Mj << sh, kUlpSat);
-  const int r = -sh;
-  if (r >= 25) return 0u;
-  const uint32_t q = Mj >> r, rem = Mj & ((1u << r) - 1u), half = 1u << (r - 1);
-  tie = rem == half;
-  return q + (rem > half ? 1u : 0u);
-}
-
-// fulps without branches (the rounding of every addend of a window runs in
-// one pass): shifts right by r = Es - Ej (clamped to 31, zero when the
-// addend's exponent is at or above the grid's), round half up, flag exact
-// halves; addends one binade above the grid double, two or more saturate.
+// ulps of v = Mj * 2^(Ej - 150) on the grid of exponent Es, without
+// branches (the rounding of every addend of a window runs in one pass):
+// shift right by r = Es - Ej (clamped to 31, zero when the addend's
+// exponent is at or above the grid's), round half up, flag exact halves
+// (tie); addends one binade above the grid double, two or more saturate.
 LZ_HD uint32_t fulps_bf(int Ej, uint32_t Mj, int Es, bool& tie) {
   const int sh = Ej - Es;
   const uint32_t r = (uint32_t)min(max(-sh, 0), 31);
