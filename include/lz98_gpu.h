@@ -53,18 +53,20 @@ enum {
 };
 
 /* ---- model: replaces lz_open + lz_read_weights + lz_free
-   (src/model.h:1333-1339).  Reads DIR/model.bin ("L98Z" v5) and uploads
+   (src/model.h:1333-1339).  Reads DIR/model.bin ("L98Z" v5-v9 headers,
+   scale layouts 0/1/2) and uploads
    every tensor to device memory of the current CUDA device. */
 int  lz_open(LZModel **out, const char *dir, char *errbuf, int errlen);
 /* The tensors are already resident after lz_open: returns 0 for a valid
    handle (kept so that the reference's open-then-read call order works). */
 int  lz_read_weights(LZModel *m, char *errbuf, int errlen);
 void lz_free(LZModel *m);
-/* vocab, hidden, n_layers, kda_heads, key_dim, latent, n_experts, top_k,
-   shared_width, head_dim, n_heads, n_kv_heads, rotary_dim, seq_len,
-   mtp_ffn, moe_ffn */
+/* (no counterpart in the reference, whose LZModel is a by-value struct the
+   caller reads) vocab, hidden, n_layers, kda_heads, key_dim, latent,
+   n_experts, top_k, shared_width, head_dim, n_heads, n_kv_heads,
+   rotary_dim, seq_len, mtp_ffn, moe_ffn */
 void lz_model_info(const LZModel *m, int *out16);
-/* Bytes of weights resident in HBM. */
+/* Bytes of weights resident in HBM (no counterpart in the reference). */
 size_t lz_model_weight_bytes(const LZModel *m);
 
 /* ---- run state: replaces lz_state_alloc / lz_state_reset /
@@ -76,7 +78,9 @@ int  lz_state_alloc_batch(LZRunState **out, const LZModel *m, int n_seq,
                           int seq_len, int spec_k_max, char *errbuf, int errlen);
 void lz_state_reset(LZRunState *s, const LZModel *m);
 void lz_state_free(LZRunState *s);
-/* Host mirrors of LZRunState fields for sequence `seq`. */
+/* Host mirrors of the LZRunState fields the reference's round loop reads
+   and writes directly (mtp_pos, ssm_slot, ssm_ring_depth, mtp_chain;
+   src/forward.h:824-1164), for sequence `seq`. */
 int  lz_state_get(const LZRunState *s, int seq, int *mtp_pos, int *ssm_slot,
                   int *ring_depth);
 int  lz_state_set(LZRunState *s, int seq, int mtp_pos, int ssm_slot);
@@ -89,8 +93,10 @@ float *lz_forward_capture(const LZModel *m, LZRunState *s, int token, int pos);
 float *lz_forward_batch_capture(const LZModel *m, LZRunState *s,
                                 const int *tokens, int n, int pos0,
                                 float *hidden_out);
-/* Verify forward: logits of every row into the state's mtp_logits mirror,
-   captured hidden rows into mtp_verify_hidden. */
+/* Verify forward (src/forward.c:1774-1837): logits of every row into the
+   state's mtp_logits mirror, captured hidden rows into mtp_verify_hidden
+   (the reference's s->mtp_logits and s->mtp_verify_hidden,
+   src/forward.h:824-1164, read through the two accessors below). */
 int    lz_forward_verify(const LZModel *m, LZRunState *s, const int *tokens,
                          int n, int pos0);
 const float *lz_state_mtp_logits(const LZRunState *s);
@@ -155,10 +161,12 @@ int lz_seq_set_sampler(LZRunState *s, int seq, float temperature, float topp, ui
    out_counts (n_seq) may be NULL, which skips the device-to-host copy. */
 int lz_spec_round_batch(const LZModel *m, LZRunState *s, int k,
                         int *out_tokens, int *out_counts, char *errbuf, int errlen);
-/* Capture the round of depth k into a CUDA graph (replayed by later
-   lz_spec_round_batch calls of the same k); 0 disables graphs. */
+/* (no counterpart in the reference) Capture the round of depth k into a
+   CUDA graph (replayed by later lz_spec_round_batch calls of the same k);
+   0 disables graphs. */
 int lz_set_graphs(LZRunState *s, int enable);
-/* Launch every kernel with programmatic dependent launch (the default):
+/* (no counterpart in the reference) Launch every kernel with
+   programmatic dependent launch (the default):
    each kernel lets the next one start its prologue - weight prefetch -
    while it finishes; 0 launches them plainly serialised. */
 int lz_set_pdl(LZRunState *s, int enable);
@@ -177,17 +185,20 @@ int lz_generate_ex(const LZModel *m, LZRunState *s, const int *prompt, int n_pro
                    float p_min, int n_min, int *out_tok, int out_cap, int *out_n,
                    int *rounds, int round_cap, int *n_rounds, char *errbuf, int errlen);
 
-/* Running totals of sequence `seq` over its device rounds: rounds, emitted
+/* (no counterpart in the reference) Running totals of sequence `seq` over
+   its device rounds: rounds, emitted
    tokens (n_accept + 1 per round), accepted drafts, drafted tokens. */
 int lz_state_counters(const LZRunState *s, int seq, int *rounds, int *emitted,
                       int *accepted, int *drafted);
-/* Measurement hook: one eager round of depth k with CUDA events
+/* Measurement hook (no counterpart in the reference): one eager round of
+   depth k with CUDA events
    around every int8 GEMV launch.  Returns the summed GEMV device time, their
    algorithmic bytes (weights, scales, activations, outputs), the GEMV count,
    the round's device time and its kernel count. */
 int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
                      int *n_gemv, double *round_ms, int *n_kernels);
-/* After lz_profile_round: the TMA-staged grouped-expert launches of that
+/* Measurement hook (no counterpart in the reference), after
+   lz_profile_round: the TMA-staged grouped-expert launches of that
    round (event-timed one by one): summed device time, algorithmic bytes
    (every expert's int8 weights and scales) and launch count. */
 int lz_profile_experts(const LZRunState *s, double *ms, double *bytes, int *n);
@@ -220,7 +231,8 @@ int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *ou
    device - the arg-max and the online-softmax probability the greedy
    p_min compares. */
 int lz_debug_argmax_p1(const float *vals, int n, int *out_idx, float *out_p1);
-/* Test hook: a kernel waits on an mbarrier that nothing arrives on; its
+/* Test hook (no counterpart in the reference): a kernel waits on an
+   mbarrier that nothing arrives on; its
    bounded wait (about a second, the limit every wait of this library has)
    gives up and reports 2 in *out_err without a fault.  *out_ms: the call's
    duration. */
@@ -261,9 +273,11 @@ int  lz_ckpt_save_seq(LZStateCkpt *ck, const LZRunState *s, int seq, int pos, ch
 int  lz_ckpt_restore_seq(const LZStateCkpt *ck, LZRunState *s, int seq, int *out_pos,
                          char *errbuf, int errlen);
 
-/* Stream the library launches on (cudaStream_t, NULL = a private stream). */
+/* (no counterpart in the reference) Stream the library launches on
+   (cudaStream_t, NULL = a private stream). */
 void *lz_state_stream(LZRunState *s);
-/* Kernels this library launched since the state was created. */
+/* (no counterpart in the reference) Kernels this library launched since
+   the state was created. */
 long long lz_state_launches(const LZRunState *s);
 
 #ifdef __cplusplus
