@@ -23,6 +23,7 @@ namespace lz98 {
 constexpr int kGemvWarps = 4;
 constexpr int kGemvProWarps = 16;   // warps of a GEMV block that runs the input-norm prologue
 constexpr int kGemvRB = 8;        // token rows per reduction pass
+constexpr int kRowLoadU = 4;      // loads a thread of a row kernel issues before its stores
 
 // ------------------------------------------------------- serial chains
 
@@ -916,9 +917,23 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
   __shared__ float s_inv;
   const int r = blockIdx.x;
   const float* xr = x + (size_t)r * ldx;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    sm[i] = xr[i];
-    sm[n + i] = w[i];
+  // each thread's loads issued together, then its stores
+  for (int i0 = threadIdx.x; i0 < n; i0 += kRowLoadU * blockDim.x) {
+    float a[kRowLoadU], b[kRowLoadU];
+#pragma unroll
+    for (int u = 0; u < kRowLoadU; u++) {
+      const int i = i0 + u * blockDim.x;
+      a[u] = i < n ? xr[i] : 0.0f;
+      b[u] = i < n ? __ldg(w + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowLoadU; u++) {
+      const int i = i0 + u * blockDim.x;
+      if (i < n) {
+        sm[i] = a[u];
+        sm[n + i] = b[u];
+      }
+    }
   }
   if (amax_clear && threadIdx.x == 0) amax_clear[r] = 0ull;
   __syncthreads();
@@ -1938,9 +1953,25 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
   const int r = blockIdx.x;
   const int hr = hid_idx ? hid_idx[r] : r;
   const size_t base = (size_t)tok[r] * d;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    sm[i] = __fmul_rn((float)eq[base + i], es[(base + i) / egs]);
-    sm[d + i] = hid[(size_t)hr * d + i];
+  // each thread's loads issued together, then its stores
+  for (int i0 = threadIdx.x; i0 < d; i0 += kRowLoadU * blockDim.x) {
+    int8_t qv[kRowLoadU];
+    float sv[kRowLoadU], hv[kRowLoadU];
+#pragma unroll
+    for (int u = 0; u < kRowLoadU; u++) {
+      const int i = i0 + u * blockDim.x;
+      qv[u] = i < d ? eq[base + i] : (int8_t)0;
+      sv[u] = i < d ? es[(base + i) / egs] : 0.0f;
+      hv[u] = i < d ? hid[(size_t)hr * d + i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowLoadU; u++) {
+      const int i = i0 + u * blockDim.x;
+      if (i < d) {
+        sm[i] = __fmul_rn((float)qv[u], sv[u]);
+        sm[d + i] = hv[u];
+      }
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) s_inv[0] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, d), (float)d), eps));
