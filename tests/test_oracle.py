@@ -237,3 +237,28 @@ def test_reference_stock_tier_and_back(tiny_dir):
     finally:
         R.L.rd_set_tier(7)
         R.close()
+
+
+@needs_ref
+@pytest.mark.parametrize("plen", [1, 2, 3, 5])
+def test_oracle_generation_edge_cases_match_reference(tiny_dir, plen):
+    """Short prompts (down to one token, where the capture prefill is empty)
+    and short generations (max_new below k + 1, so the last round is cut)
+    for every draft depth 0..3, greedy and temperature: the restatement and
+    the live reference emit the same tokens and the same round records."""
+    O = Oracle(tiny_dir, 512, 4)
+    R = Reference(tiny_dir, 512, 4)
+    try:
+        rng = np.random.default_rng([7, plen])
+        prompt = rng.integers(0, O.vocab, plen).astype(np.int32)
+        for max_new in (1, 2, 3, 7):
+            for k in (0, 1, 2, 3):
+                for temp in (0.0, 0.8):
+                    to, ro = O.generate(prompt, max_new, k, temp=temp, seed=99)
+                    tr, rr = R.generate(prompt, max_new, k, temp=temp, seed=99)
+                    ctx = (plen, max_new, k, temp)
+                    assert np.array_equal(to, tr), ctx
+                    assert np.array_equal(ro, rr), ctx
+    finally:
+        O.close()
+        R.close()
