@@ -240,14 +240,20 @@ def test_reference_stock_tier_and_back(tiny_dir):
 
 
 @needs_ref
-@pytest.mark.parametrize("plen", [1, 2, 3, 5])
-def test_oracle_generation_edge_cases_match_reference(tiny_dir, plen):
+@pytest.mark.parametrize("name,plen", [("tiny", 1), ("tiny", 2), ("tiny", 3), ("tiny", 5),
+                                       ("mini", 1), ("mini", 5), ("midi", 1), ("midi", 5),
+                                       ("midi_f16", 1), ("midi_f16", 5), ("tiny_u8", 1), ("tiny_u8", 5)])
+def test_oracle_generation_edge_cases_match_reference(name, plen):
     """Short prompts (down to one token, where the capture prefill is empty)
     and short generations (max_new below k + 1, so the last round is cut)
-    for every draft depth 0..3, greedy and temperature: the restatement and
-    the live reference emit the same tokens and the same round records."""
-    O = Oracle(tiny_dir, 512, 4)
-    R = Reference(tiny_dir, 512, 4)
+    for every draft depth 0..3, greedy and temperature, on every parity
+    config (per-32 and per-row scales, binary16 and u8-code scale planes):
+    the restatement and the live reference emit the same tokens and the
+    same round records."""
+    from conftest import model_dir
+    d = model_dir(name)
+    O = Oracle(d, 512, 4)
+    R = Reference(d, 512, 4)
     try:
         rng = np.random.default_rng([7, plen])
         prompt = rng.integers(0, O.vocab, plen).astype(np.int32)
