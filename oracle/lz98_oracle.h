@@ -38,6 +38,11 @@ int lzo_generate(const LzoModel *m, LzoState *s, const int *prompt, int n_prompt
                  int max_new, int spec_k, float temp, float topp,
                  unsigned long long seed, int *out_tok, int out_cap, int *out_n,
                  int *rounds, int round_cap, int *n_rounds);
+int lzo_generate_pm(const LzoModel *m, LzoState *s, const int *prompt, int n_prompt,
+                    int max_new, int spec_k, float temp, float topp,
+                    unsigned long long seed, float p_min, int n_min,
+                    int *out_tok, int out_cap, int *out_n,
+                    int *rounds, int round_cap, int *n_rounds);
 
 /* Op-level restatements. */
 float lzo_exp(float x);

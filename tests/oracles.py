@@ -65,6 +65,9 @@ class Oracle:
         L.lzo_mtp_prefill.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]
         L.lzo_generate.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                    ctypes.c_ulonglong, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int)]
+        L.lzo_generate_pm.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                      ctypes.c_ulonglong, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p,
+                                      c_int, P(c_int)]
         L.lzo_set_positions.argtypes = [c_void_p, c_int, c_int]
         L.lzo_get_positions.argtypes = [c_void_p, P(c_int), P(c_int), P(c_int)]
         L.lzo_set_chain.argtypes = [c_void_p, c_void_p]
@@ -134,14 +137,14 @@ class Oracle:
         t = np.ascontiguousarray(nxt, np.int32)
         return self.L.lzo_mtp_prefill(c_void_p(self.m), c_void_p(self.s), _ptr(h), _ptr(t), len(t), pos0)
 
-    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1):
+    def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max_new + 16, np.int32)
         rounds = np.zeros(2 * (max_new + 16), np.int32)
         on, nr = c_int(), c_int()
-        rc = self.L.lzo_generate(c_void_p(self.m), c_void_p(self.s), _ptr(p), len(p), max_new, spec_k,
-                                 temp, topp, seed, _ptr(out), len(out), ctypes.byref(on),
-                                 _ptr(rounds), len(rounds) // 2, ctypes.byref(nr))
+        rc = self.L.lzo_generate_pm(c_void_p(self.m), c_void_p(self.s), _ptr(p), len(p), max_new, spec_k,
+                                    temp, topp, seed, c_float(p_min), int(n_min), _ptr(out), len(out),
+                                    ctypes.byref(on), _ptr(rounds), len(rounds) // 2, ctypes.byref(nr))
         if rc:
             raise RuntimeError(f"oracle generate failed rc={rc}")
         return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()

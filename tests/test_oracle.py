@@ -268,3 +268,47 @@ def test_oracle_generation_edge_cases_match_reference(name, plen):
     finally:
         O.close()
         R.close()
+
+
+def test_oracle_pmin_nmin_matches_golden():
+    """Rounds with p_min / n_min (drafting stopped at a low-confidence
+    step, short drafts discarded before the verify) reproduce the
+    reference's golden generations, greedy and temperature."""
+    from conftest import model_dir
+    for name in ("tiny", "midi"):
+        g = load_golden(name)
+        O = Oracle(model_dir(name), 512, 4)
+        try:
+            max_new = 40 if name.startswith("tiny") else 48
+            for j, (pm, nm, temp) in enumerate(g["pm_cases"]):
+                toks, rounds = O.generate(g["prompt"], max_new, 3, temp=float(temp), seed=1234,
+                                          p_min=float(pm), n_min=int(nm))
+                assert np.array_equal(toks, g[f"pm{j}_tokens"]), (name, j)
+                assert np.array_equal(rounds, g[f"pm{j}_rounds"]), (name, j)
+        finally:
+            O.close()
+
+
+@needs_ref
+@pytest.mark.parametrize("name", ["tiny", "mini", "midi", "midi_f16", "tiny_u8"])
+def test_oracle_pmin_nmin_matches_reference(name):
+    """A sweep of p_min thresholds (from never stopping to stopping at the
+    first step) and n_min 0..3, greedy and temperature, against the live
+    reference: same tokens and the same (k_eff, n_accept) round records,
+    discarded rounds included."""
+    from conftest import model_dir
+    d = model_dir(name)
+    g = load_golden(name)
+    O = Oracle(d, 512, 4)
+    R = Reference(d, 512, 4)
+    try:
+        for pm in (0.0, 1e-4, 3.5e-4, 1.2e-3, 0.5):
+            for nm in (0, 2, 3):
+                for temp in (0.0, 0.8):
+                    to, ro = O.generate(g["prompt"], 24, 3, temp=temp, seed=1234, p_min=pm, n_min=nm)
+                    tr, rr = R.generate(g["prompt"], 24, 3, temp=temp, seed=1234, p_min=pm, n_min=nm)
+                    assert np.array_equal(to, tr), (pm, nm, temp)
+                    assert np.array_equal(ro, rr), (pm, nm, temp)
+    finally:
+        O.close()
+        R.close()
