@@ -30,6 +30,13 @@ CASES = {
 }
 
 
+# token-stream-only fixtures of larger configs: name: (prompt length,
+# max_new, [(k, temperature), ...])
+TOKEN_CASES = {
+    "0p5b": (12, 12, [(0, 0.0), (2, 0.0), (2, 0.8), (3, 0.8)]),
+}
+
+
 PM_CASES = {
     "tiny": [(3.5e-4, 0, 0.0), (3.5e-4, 2, 0.0), (2e-4, 0, 0.8), (1e-4, 2, 0.8)],
     "midi": [(1.2e-3, 0, 0.0), (1.2e-3, 2, 0.0), (2e-4, 0, 0.8), (6e-4, 2, 0.8)],
@@ -84,6 +91,27 @@ def make(name):
     print(path, os.path.getsize(path))
 
 
+def make_tokens(name):
+    """Prompt and whole generations only (no logits), for configs whose
+    logits rows would make the fixture large."""
+    d = model_dir(name)
+    cfg = lz98_synth.CONFIGS[name]
+    sha = lz98_synth.write_model(cfg, d)
+    n_prompt, max_new, runs = TOKEN_CASES[name]
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, cfg.vocab, n_prompt).astype(np.int32)
+    R = Reference(d, 512, 4)
+    out = {"sha256": np.frombuffer(bytes.fromhex(sha), np.uint8), "prompt": prompt,
+           "runs": np.array(runs, np.float64), "max_new": np.array([max_new], np.int32)}
+    for j, (k, temp) in enumerate(runs):
+        toks, rounds = R.generate(prompt, max_new, k, temp=temp, seed=1234)
+        out[f"run{j}_tokens"], out[f"run{j}_rounds"] = toks, rounds
+    R.close()
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, **out)
+    print(path, os.path.getsize(path))
+
+
 if __name__ == "__main__":
-    for n in (sys.argv[1:] or CASES):
-        make(n)
+    for n in (sys.argv[1:] or list(CASES) + list(TOKEN_CASES)):
+        make_tokens(n) if n in TOKEN_CASES else make(n)

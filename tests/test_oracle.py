@@ -312,3 +312,24 @@ def test_oracle_pmin_nmin_matches_reference(name):
     finally:
         O.close()
         R.close()
+
+
+def test_oracle_headline_config_matches_golden():
+    """The ~0.5B bench config itself (d 1024, 24 layers, 64 experts top-4,
+    vocabulary 64000, MTP depth 2): the restatement reproduces the
+    reference's token streams and round records, greedy and temperature,
+    plain decode and k = 2, 3."""
+    from conftest import model_dir
+    import lz98_synth
+    d = model_dir("0p5b")
+    g = load_golden("0p5b")
+    sha = lz98_synth.write_model(lz98_synth.CONFIGS["0p5b"], d)
+    assert bytes(g["sha256"]).hex() == sha, "model writer drifted from the golden vectors"
+    O = Oracle(d, 512, 4)
+    try:
+        for j, (k, temp) in enumerate(g["runs"]):
+            toks, rounds = O.generate(g["prompt"], int(g["max_new"][0]), int(k), temp=float(temp), seed=1234)
+            assert np.array_equal(toks, g[f"run{j}_tokens"]), (j, k, temp)
+            assert np.array_equal(rounds, g[f"run{j}_rounds"]), (j, k, temp)
+    finally:
+        O.close()
