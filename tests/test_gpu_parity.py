@@ -266,3 +266,27 @@ def test_mixed_batch_is_refused(gcase):
     with pytest.raises(lz98.LzError):
         s.round_batch(2)
     s.close()
+
+
+def test_headline_config_token_identical():
+    """The ~0.5B bench config itself (d 1024, 24 layers, 64 experts top-4,
+    vocabulary 64000, MTP depth 2): the device generations reproduce the
+    reference's token streams and round records, greedy and temperature,
+    plain decode and k = 2, 3."""
+    import lz98
+    import lz98_synth
+    from conftest import model_dir
+    d = model_dir("0p5b")
+    g = dict(np.load(os.path.join(GOLDEN, "0p5b.npz")))
+    assert bytes(g["sha256"]).hex() == lz98_synth.write_model(lz98_synth.CONFIGS["0p5b"], d)
+    m = lz98.Model(d)
+    s = lz98.State(m, 512, 4)
+    try:
+        for j, (k, temp) in enumerate(g["runs"]):
+            toks, rounds = s.generate(g["prompt"], int(g["max_new"][0]), int(k), temp=float(temp), topp=0.95,
+                                      seed=1234)
+            assert np.array_equal(toks, g[f"run{j}_tokens"]), (j, k, temp)
+            assert np.array_equal(rounds, g[f"run{j}_rounds"]), (j, k, temp)
+    finally:
+        s.close()
+        m.close()
