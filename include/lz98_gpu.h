@@ -28,16 +28,52 @@ extern "C" {
 typedef struct LZModel LZModel;
 typedef struct LZRunState LZRunState;
 
-/* Sampler state of the temperature round: the subset of LZSampler
-   (src/sampler.h:145-187) that the acceptance path reads. */
+/* The reference's sampler, field for field (src/sampler.h:140-186), so a
+   caller's own LZSampler passes through lz_spec_round / lz_spec_round_temp
+   unchanged.  When the reference's sampler.h has been included first
+   (its guard LZ_SAMPLER_H), its definitions are used instead.  The rounds
+   read p.temperature, p.topp and rng_state (advanced by the temperature
+   round), and refuse what the device path does not carry: penalties that
+   act (repeat_last_n != 0 with a repetition penalty != 1 or a presence or
+   frequency penalty != 0; the reference's assumed-window penalties,
+   src/generate.c:517-529), and top-k in (0, vocab) and min-p > 0
+   (temperature rounds only; the greedy round reads penalties only, as the
+   reference's does).  The think temperature is not read by the rounds. */
+#ifndef LZ_SAMPLER_H
+typedef struct {
+    float prob;
+    int   index;
+} LZProbIndex;
+
 typedef struct {
     float temperature;
+    float temp_think;
+    int   think_temp_enabled;
     float topp;
-    uint64_t rng_state;
+    float minp;
+    int   topk;
+    float presence_penalty;
+    float frequency_penalty;
+    float repetition_penalty;
+    int   repeat_last_n;
+    int   minp_llamacpp;
+} LZSampleParams;
+
+typedef struct {
+    int            vocab_size;
+    LZSampleParams p;
+    uint64_t       rng_state;
+    LZProbIndex   *probindex;
+    unsigned short *counts;
+    int           *ring;
+    int            cap;
+    int            head;
+    int            n_win;
 } LZSampler;
+#endif
 
 /* LZErr codes used on this path, with the values of the reference's
-   err.h (src/err.h:19-...), plus two of this library's own above 1000. */
+   err.h (src/err.h:19-...), plus four of this library's own from 1000. */
 enum {
     LZ98_ERR_OK = 0,
     LZ98_ERR_NULL_ARG = 6,
@@ -48,8 +84,10 @@ enum {
     LZ98_ERR_CKPT_SHAPE = 23,
     LZ98_ERR_SPEC_NO_HEAD = 24,
     LZ98_ERR_SPEC_K_RANGE = 25,
-    LZ98_ERR_CUDA = 1000,        /* a CUDA call failed */
-    LZ98_ERR_MODEL = 1001        /* model.bin not loadable by this library */
+    LZ98_ERR_CUDA = 1000,        /* a CUDA call failed, or a device wait gave up */
+    LZ98_ERR_MODEL = 1001,       /* model.bin not loadable by this library */
+    LZ98_ERR_SIZE = 1002,        /* a request exceeds a fixed limit of this library */
+    LZ98_ERR_DEVICE = 1003       /* the current CUDA device is not the model's */
 };
 
 /* ---- model: replaces lz_open + lz_read_weights + lz_free
@@ -111,11 +149,18 @@ int    lz_mtp_catchup(const LZModel *m, LZRunState *s, const float *h_body_all,
                       const int *next_tokens, int n, int pos0);
 
 /* ---- rounds of sequence 0 (src/llama_zh.h:470-593,
-   src/generate.c:694-994 and 1234-1377).  The debug flags must be 0 and
-   samp NULL or carrying identity penalties.  lz_spec_round is the greedy
-   round; lz_spec_round_temp the coupled temperature round (temperature
-   above the floor, top-p), which advances samp->rng_state as the
-   reference does.  p_min > 0 stops drafting at the first step whose
+   src/generate.c:694-994 and 1234-1377).  lz_spec_round is the greedy
+   round (samp may be NULL; a non-NULL samp with acting penalties is
+   refused with -LZ98_ERR_FORWARD, its temperature is not read);
+   lz_spec_round_temp the coupled temperature round (temperature above the
+   floor, top-p; the refusals listed at LZSampler), which advances
+   samp->rng_state as the reference does.  debug_break_rollback is the
+   reference's known-bad control (src/generate.c:827-844): a round that
+   rejects a draft leaves the state ring where the full verify left it
+   instead of rolling it back; debug_skip_catchup skips the MTP catch-up
+   (src/generate.c:976-982).  A device wait that gave up during the round
+   returns -LZ98_ERR_CUDA; the state is then not usable (free it).
+   p_min > 0 stops drafting at the first step whose
    confidence - lz_argmax_p1's probability of the greedy draft, q(x) of a
    sampled one - is below it (that token is not drafted); n_min > 0
    discards a draft of fewer than n_min tokens: the call returns 0 with
@@ -153,6 +198,11 @@ int lz_seq_prefill(const LZModel *m, LZRunState *s, int seq, const int *prompt,
    lz_state_reset, as the reference keeps its sampler apart from the run
    state.  lz_seq_prefill picks the first anchor with it. */
 int lz_seq_set_sampler(LZRunState *s, int seq, float temperature, float topp, uint64_t seed);
+/* (no counterpart in the reference, whose caller owns its LZSampler) The
+   sampler of sequence `seq` as the device holds it: temperature, top-p and
+   the generator state, which lz_seq_prefill's anchor sample and the
+   temperature rounds advance.  Any output pointer may be NULL. */
+int lz_seq_get_sampler(const LZRunState *s, int seq, float *temperature, float *topp, uint64_t *rng);
 /* One round of every sequence with draft depth k (device resident:
    draft k steps, one (k+1)-row verify per sequence, acceptance, ring
    rollback, chain reseed, catch-up): greedy when every sequence's sampler
@@ -210,11 +260,13 @@ int lz_profile_experts(const LZRunState *s, double *ms, double *bytes, int *n);
    (n x vocab) are device pointers the caller owns; stream is a
    cudaStream_t (NULL = the legacy default stream).  The quantised rows go
    to a static device array of at most 64 rows x 4096 columns (larger
-   requests return LZ98_ERR_SPEC_K_RANGE with a message); it is shared by
-   every call, so calls that overlap on the GPU race.  The first call on a
-   device resolves the array's device address (cudaGetSymbolAddress) and
-   should come before any stream capture.  Calls no cudaMalloc or
-   cudaFree. */
+   requests return LZ98_ERR_SIZE with a message); it is shared by
+   every call, so calls that overlap on the GPU race.  The current device
+   must be the one lz_open uploaded the model to (else LZ98_ERR_DEVICE).
+   The first call on a device resolves the array's device address
+   (cudaGetSymbolAddress, once per device even with several calling
+   threads) and should come before any stream capture.  Calls no
+   cudaMalloc or cudaFree. */
 int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logits,
                       void *stream, char *errbuf, int errlen);
 
@@ -237,6 +289,17 @@ int lz_debug_argmax_p1(const float *vals, int n, int *out_idx, float *out_p1);
    gives up and reports 2 in *out_err without a fault.  *out_ms: the call's
    duration. */
 int lz_debug_wait_timeout(int *out_err, double *out_ms);
+
+/* Test hook (no counterpart in the reference): with `on` nonzero, the
+   producer of every TMA-staged launch (the GEMMs and grouped experts of
+   rounds with more than 8 token rows) issues nothing for its first
+   pipeline stage, and every bounded device wait gives up after limit_ms
+   instead of about a second.  The consumers' waits on that stage run out,
+   the launch sets the state's error word (no copy is in flight: the
+   skipped stage was never issued, every issued one is waited for) and the
+   round returns LZ98_ERR_CUDA.  on = 0 restores both.  Acts on the
+   current device. */
+int lz_debug_inject_wait_timeout(int on, double limit_ms);
 
 /* ---- debug data (src/forward.c:86-124, src/generate.c:226): host
    microseconds spent in capture forwards, verify forwards, draft steps and

@@ -163,17 +163,23 @@ LZ_HD unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+// Limit of every bounded device wait (about a second), and a test switch
+// that makes the producer of every TMA-staged launch issue nothing for its
+// first pipeline stage; both set only by lz_debug_inject_wait_timeout.
+__device__ unsigned long long g_wait_limit_ns = 1000000000ull;
+__device__ int g_dbg_skip_stage = 0;
+
 // Wait until the phase of parity `parity` of the barrier has completed,
-// giving up after about a second (returns false): no wait in this library
+// giving up after g_wait_limit_ns (returns false): no wait in this library
 // can spin for ever.
 LZ_HD bool mbar_wait(uint32_t bar, uint32_t parity) {
 #pragma unroll 1
   for (int i = 0; i < 256; i++)
     if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
+  const unsigned long long t0 = global_ns(), lim = g_wait_limit_ns;
 #pragma unroll 1
   while (!mbar_try(bar, parity))
-    if (global_ns() - t0 > 1000000000ull) return false;
+    if (global_ns() - t0 > lim) return false;
   return true;
 }
 // 2-D tiled TMA load of the box at (x, y) (x in elements of the innermost

@@ -14,6 +14,7 @@
 #include <chrono>
 #include <initializer_list>
 #include <map>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -83,6 +84,7 @@ struct LZModel {
   float* final_norm = nullptr;
   std::vector<DLayer> L;
   DMtp mtp;
+  int dev = 0;                    // the CUDA device the tensors live on
   size_t wbytes = 0;
   std::vector<void*> allocs;
   // column offsets inside the fused projection groups
@@ -230,6 +232,7 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
   if (!r.f) { set_err(errbuf, errlen, "cannot open %s", path.c_str()); return LZ98_ERR_MODEL; }
   LZModel* m = new LZModel();
   Cfg& c = m->c;
+  cudaGetDevice(&m->dev);
   char magic[4];
   r.bytes(magic, 4);
   int ver = r.i32();
@@ -757,18 +760,35 @@ extern "C" void lz_state_reset(LZRunState* s, const LZModel*) {
   s->epoch++;
 }
 
-static void sr_down(LZRunState* s) {
-  cudaMemcpyAsync(s->h_sr.data(), s->sr, s->B * sizeof(SeqRound), cudaMemcpyDeviceToHost, s->st);
-  cudaStreamSynchronize(s->st);
+// Round records device -> host (waits for the stream) and host -> device
+// (queued); false on a CUDA failure or, for sr_down, a device wait that
+// gave up (sync_ok).
+static bool sr_down(LZRunState* s) {
+  return cudaMemcpyAsync(s->h_sr.data(), s->sr, s->B * sizeof(SeqRound), cudaMemcpyDeviceToHost, s->st) ==
+             cudaSuccess &&
+         sync_ok(s);
 }
-static void sr_up(LZRunState* s) {
-  cudaMemcpyAsync(s->sr, s->h_sr.data(), s->B * sizeof(SeqRound), cudaMemcpyHostToDevice, s->st);
+static bool sr_up(LZRunState* s) {
+  return cudaMemcpyAsync(s->sr, s->h_sr.data(), s->B * sizeof(SeqRound), cudaMemcpyHostToDevice, s->st) ==
+         cudaSuccess;
+}
+
+// errbuf text of a failed device round: a bounded device wait that gave up
+// (the state's error word) or the CUDA error.
+static void round_fail(const LZRunState* s, char* errbuf, int errlen, const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  char msg[200];
+  if (s->h_err && *(volatile int*)s->h_err)
+    snprintf(msg, sizeof msg, "%s: a device wait gave up (the state is not usable)", what);
+  else
+    snprintf(msg, sizeof msg, "%s: %s", what, cudaGetErrorString(e));
+  set_err(errbuf, errlen, "%s", msg);
 }
 
 extern "C" int lz_state_get(const LZRunState* cs, int seq, int* mtp_pos, int* ssm_slot, int* depth) {
   LZRunState* s = const_cast<LZRunState*>(cs);
   if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
-  sr_down(s);
+  if (!sr_down(s)) return LZ98_ERR_CUDA;
   if (mtp_pos) *mtp_pos = s->h_sr[seq].mtp_pos;
   if (ssm_slot) *ssm_slot = s->h_sr[seq].ssm_slot;
   if (depth) *depth = s->depth;
@@ -777,12 +797,10 @@ extern "C" int lz_state_get(const LZRunState* cs, int seq, int* mtp_pos, int* ss
 
 extern "C" int lz_state_set(LZRunState* s, int seq, int mtp_pos, int ssm_slot) {
   if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
-  sr_down(s);
+  if (!sr_down(s)) return LZ98_ERR_CUDA;
   if (mtp_pos >= 0) s->h_sr[seq].mtp_pos = mtp_pos;
   if (ssm_slot >= 0) s->h_sr[seq].ssm_slot = ssm_slot % s->depth;
-  sr_up(s);
-  cudaStreamSynchronize(s->st);
-  return 0;
+  return sr_up(s) && sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" int lz_state_get_chain(const LZRunState* s, int seq, float* chain) {
@@ -1357,7 +1375,7 @@ int draft_pmin(LZRunState* s, int k, bool temp, float p_min) {
     if (temp) {
       launch(s, temp_draft_kernel, dim3(1), dim3(kSampThreads), kSampSmem, s->logits, c.vocab, s->sr, i, k, s->kmax,
              s->qbuf);
-      sr_down(s);
+      if (!sr_down(s)) return -1;
       const int x = s->h_sr[0].draft[i];
       if (cudaMemcpyAsync(&conf, s->qbuf + (size_t)i * c.vocab + x, 4, cudaMemcpyDeviceToHost, s->st) != cudaSuccess)
         return -1;
@@ -1381,9 +1399,9 @@ int round_pmin(LZRunState* s, int k, bool temp, float p_min, int n_min, int* k_e
   *k_eff = draft_pmin(s, k, temp, p_min);
   if (*k_eff < 0) return -1;
   if (*k_eff < n_min) return 0;   // k_eff == 0 with n_min == 0 still verifies the anchor row
-  sr_down(s);
+  if (!sr_down(s)) return -1;
   s->h_sr[0].k = *k_eff;
-  sr_up(s);
+  if (!sr_up(s)) return -1;
   dbg_mark(s, 1);
   if (temp) verify_temp(s, *k_eff);
   else verify_greedy(s, *k_eff);
@@ -1472,7 +1490,7 @@ static float* forward_one(const LZModel* m, LZRunState* s, const int* tokens, in
   if (!m || !s || !tokens || n < 1) return nullptr;
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= c.vocab || pos0 + i < 0 || pos0 + i >= s->seq_len) return nullptr;
-  sr_down(s);
+  if (!sr_down(s)) return nullptr;
   const int slot = s->h_sr[0].ssm_slot;
   float* last = nullptr;
   for (int done = 0; done < n;) {
@@ -1522,7 +1540,7 @@ extern "C" int lz_forward_verify(const LZModel* m, LZRunState* s, const int* tok
   const Cfg& c = m->c;
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= c.vocab || pos0 + i < 0 || pos0 + i >= s->seq_len) return 1;
-  sr_down(s);
+  if (!sr_down(s)) return 1;
   const int slot = s->h_sr[0].ssm_slot;
   cudaMemcpyAsync(s->tok, tokens, n * sizeof(int), cudaMemcpyHostToDevice, s->st);
   upload_seqs(s, {KdaSeq{0, n, slot, 0}});
@@ -1530,8 +1548,7 @@ extern "C" int lz_forward_verify(const LZModel* m, LZRunState* s, const int* tok
   cudaMemcpyAsync(s->h_logits.data(), s->logits, (size_t)n * c.vocab * 4, cudaMemcpyDeviceToHost, s->st);
   cudaMemcpyAsync(s->h_hidden.data(), s->hidden, (size_t)n * c.d * 4, cudaMemcpyDeviceToHost, s->st);
   s->h_sr[0].ssm_slot = (slot + n) % s->depth;
-  sr_up(s);
-  return sync_ok(s) ? 0 : 1;
+  return sr_up(s) && sync_ok(s) ? 0 : 1;
 }
 
 extern "C" const float* lz_state_mtp_logits(const LZRunState* s) { return s ? s->h_logits.data() : nullptr; }
@@ -1677,21 +1694,52 @@ static int run_round(LZRunState* s, int k) {
 
 extern "C" int lz_seq_set_sampler(LZRunState* s, int seq, float temperature, float topp, uint64_t seed) {
   if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
-  sr_down(s);
+  if (!sr_down(s)) return LZ98_ERR_CUDA;
   SeqRound& r = s->h_sr[seq];
   r.temp = temperature > 0.0f ? temperature : 0.0f;    // src/generate.c:2790
   r.topp = topp;
   r.rng = seed ? seed : 1ull;                         // src/sampler.c:55-60
   s->seq_temp[seq] = r.temp > kTempFloor;
-  sr_up(s);
-  return sync_ok(s) ? 0 : LZ98_ERR_CUDA;
+  return sr_up(s) && sync_ok(s) ? 0 : LZ98_ERR_CUDA;
 }
 
-extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
-                             int n_min, const LZSampler* samp, int debug_break_rollback, int debug_skip_catchup,
-                             int* out, int* out_n_accept, int* out_new_pos, int* out_k_eff, char* errbuf,
-                             int errlen) {
-  if (!m || !s || !out || !out_n_accept || !out_new_pos || !out_k_eff) {
+extern "C" int lz_seq_get_sampler(const LZRunState* cs, int seq, float* temperature, float* topp, uint64_t* rng) {
+  LZRunState* s = const_cast<LZRunState*>(cs);
+  if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
+  if (!sr_down(s)) return LZ98_ERR_CUDA;
+  const SeqRound& r = s->h_sr[seq];
+  if (temperature) *temperature = r.temp;
+  if (topp) *topp = r.topp;
+  if (rng) *rng = r.rng;
+  return 0;
+}
+
+// Sampler options the device rounds do not carry, refused rather than
+// ignored: penalties that act (the reference applies them to every verify
+// row through an assumed window, src/generate.c:517-529, 639-690) and, for
+// the temperature round, top-k and min-p (src/sampler.c:682-714).  The
+// think temperature is not read by the rounds.
+static const char* sampler_refusal(const LZSampler* sp, int vocab, bool temp) {
+  const LZSampleParams& p = sp->p;
+  const bool has_rep = p.repetition_penalty != 1.0f;
+  const bool has_add = p.presence_penalty != 0.0f || p.frequency_penalty != 0.0f;
+  if (p.repeat_last_n != 0 && (has_rep || has_add)) return "sampler penalties are not supported on the device path";
+  if (!temp) return nullptr;
+  if (p.topk > 0 && p.topk < vocab) return "top-k is not supported on the device path";
+  if (p.minp > 0.0f) return "min-p is not supported on the device path";
+  if (!(p.temperature > kTempFloor)) return "temperature round with a temperature at the greedy floor";
+  return nullptr;
+}
+
+// One round of sequence 0 behind lz_spec_round (temp false) and
+// lz_spec_round_temp (temp true): argument checks and refusals in the
+// reference's order, the device round (captured graph) or the p_min /
+// n_min round, then the reference's outputs.
+static int spec_round_seq0(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
+                           int n_min, const LZSampler* samp, bool temp, int dbg_break, int dbg_skip, int* out,
+                           int* out_n_accept, int* out_new_pos, int* out_k_eff, uint64_t* rng_out, char* errbuf,
+                           int errlen) {
+  if (!m || !s || (temp && !samp) || !out || !out_n_accept || !out_new_pos || !out_k_eff) {
     set_err(errbuf, errlen, "null argument");
     return -LZ98_ERR_NULL_ARG;
   }
@@ -1699,124 +1747,85 @@ extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int an
     set_err(errbuf, errlen, "draft depth out of range");
     return -LZ98_ERR_SPEC_K_RANGE;
   }
-  if (debug_break_rollback || debug_skip_catchup || (samp && samp->temperature > kTempFloor) || s->B != 1) {
-    set_err(errbuf, errlen, "unsupported round options on the device path");
+  if (s->B != 1) {
+    set_err(errbuf, errlen, "a batched state runs its rounds through lz_spec_round_batch");
     return -LZ98_ERR_FORWARD;
   }
-  sr_down(s);
+  if (samp)
+    if (const char* why = sampler_refusal(samp, m->c.vocab, temp)) {
+      set_err(errbuf, errlen, "%s", why);
+      return -LZ98_ERR_FORWARD;
+    }
+  if (!sr_down(s)) {
+    round_fail(s, errbuf, errlen, "CUDA failure before the round");
+    return -LZ98_ERR_CUDA;
+  }
   SeqRound& r = s->h_sr[0];
   r.anchor = anchor;
   r.anchor_pos = anchor_pos;
   r.k = k;
-  r.temp = 0.0f;
-  s->seq_temp[0] = 0;
-  sr_up(s);
+  r.dbg = (dbg_break ? kDbgBreakRollback : 0) | (dbg_skip ? kDbgSkipCatchup : 0);
+  if (temp) {
+    r.temp = samp->p.temperature;
+    r.topp = samp->p.topp;
+    r.rng = samp->rng_state;
+  } else {
+    r.temp = 0.0f;
+  }
+  s->seq_temp[0] = temp ? 1 : 0;
+  if (!sr_up(s)) {
+    round_fail(s, errbuf, errlen, "CUDA failure before the round");
+    return -LZ98_ERR_CUDA;
+  }
+  int k_eff = k;
   if (p_min > 0.0f || n_min > 0) {
-    int k_eff = 0;
-    const int rc = round_pmin(s, k, false, p_min, n_min, &k_eff);
-    if (rc < 0) {
-      set_err(errbuf, errlen, "CUDA failure in the round");
+    const int rc = round_pmin(s, k, temp, p_min, n_min, &k_eff);
+    if (rc < 0 || !sr_down(s)) {
+      round_fail(s, errbuf, errlen, "CUDA failure in the round");
       return -LZ98_ERR_CUDA;
     }
     *out_k_eff = k_eff;
+    if (temp) *rng_out = s->h_sr[0].rng;   // the draft samples advanced the generator either way
     if (rc == 0) {   // draft discarded (src/generate.c:765-791)
       out[0] = anchor;
       *out_n_accept = 0;
       *out_new_pos = anchor_pos;
       return 0;
     }
-    sr_down(s);
-    const SeqRound& o = s->h_sr[0];
-    for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
-    *out_n_accept = o.n_accept;
-    *out_new_pos = anchor_pos + 1 + o.n_accept;
-    round_debug(s, o.n_accept, k_eff);
-    return o.n_accept + 1;
-  }
-  if (run_round(s, k)) {
-    set_err(errbuf, errlen, "CUDA failure in the round: %s", cudaGetErrorString(cudaGetLastError()));
-    return -LZ98_ERR_CUDA;
-  }
-  sr_down(s);
-  if (cudaGetLastError() != cudaSuccess) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
-    return -LZ98_ERR_CUDA;
+  } else {
+    if (run_round(s, k) || !sr_down(s)) {
+      round_fail(s, errbuf, errlen, "CUDA failure in the round");
+      return -LZ98_ERR_CUDA;
+    }
+    *out_k_eff = k;
+    if (temp) *rng_out = s->h_sr[0].rng;
   }
   const SeqRound& o = s->h_sr[0];
   for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
   *out_n_accept = o.n_accept;
   *out_new_pos = anchor_pos + 1 + o.n_accept;
-  *out_k_eff = k;
-  round_debug(s, o.n_accept, k);
+  round_debug(s, o.n_accept, k_eff);
   return o.n_accept + 1;
+}
+
+extern "C" int lz_spec_round(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k, float p_min,
+                             int n_min, const LZSampler* samp, int debug_break_rollback, int debug_skip_catchup,
+                             int* out, int* out_n_accept, int* out_new_pos, int* out_k_eff, char* errbuf,
+                             int errlen) {
+  return spec_round_seq0(m, s, anchor, anchor_pos, k, p_min, n_min, samp, false, debug_break_rollback,
+                         debug_skip_catchup, out, out_n_accept, out_new_pos, out_k_eff, nullptr, errbuf, errlen);
 }
 
 extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, int anchor_pos, int k,
                                   float p_min, int n_min, LZSampler* samp, int debug_break_rollback,
                                   int debug_skip_catchup, int* out, int* out_n_accept, int* out_new_pos,
                                   int* out_k_eff, char* errbuf, int errlen) {
-  if (!m || !s || !samp || !out || !out_n_accept || !out_new_pos || !out_k_eff) {
-    set_err(errbuf, errlen, "null argument");
-    return -LZ98_ERR_NULL_ARG;
-  }
-  if (k < 1 || k > 6 || k > s->depth - 1) {
-    set_err(errbuf, errlen, "draft depth out of range");
-    return -LZ98_ERR_SPEC_K_RANGE;
-  }
-  if (debug_break_rollback || debug_skip_catchup || s->B != 1 || !(samp->temperature > kTempFloor)) {
-    set_err(errbuf, errlen, "unsupported round options on the device path");
-    return -LZ98_ERR_FORWARD;
-  }
-  sr_down(s);
-  SeqRound& r = s->h_sr[0];
-  r.anchor = anchor;
-  r.anchor_pos = anchor_pos;
-  r.k = k;
-  r.temp = samp->temperature;
-  r.topp = samp->topp;
-  r.rng = samp->rng_state;
-  s->seq_temp[0] = 1;
-  sr_up(s);
-  if (p_min > 0.0f || n_min > 0) {
-    int k_eff = 0;
-    const int rc = round_pmin(s, k, true, p_min, n_min, &k_eff);
-    if (rc < 0) {
-      set_err(errbuf, errlen, "CUDA failure in the round");
-      return -LZ98_ERR_CUDA;
-    }
-    *out_k_eff = k_eff;
-    sr_down(s);
-    const SeqRound& o = s->h_sr[0];
-    samp->rng_state = o.rng;   // the draft samples advanced the generator either way
-    if (rc == 0) {
-      out[0] = anchor;
-      *out_n_accept = 0;
-      *out_new_pos = anchor_pos;
-      return 0;
-    }
-    for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
-    *out_n_accept = o.n_accept;
-    *out_new_pos = anchor_pos + 1 + o.n_accept;
-    round_debug(s, o.n_accept, k_eff);
-    return o.n_accept + 1;
-  }
-  if (run_round(s, k)) {
-    set_err(errbuf, errlen, "CUDA failure in the round: %s", cudaGetErrorString(cudaGetLastError()));
-    return -LZ98_ERR_CUDA;
-  }
-  sr_down(s);
-  if (cudaGetLastError() != cudaSuccess) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
-    return -LZ98_ERR_CUDA;
-  }
-  const SeqRound& o = s->h_sr[0];
-  for (int i = 0; i <= o.n_accept; i++) out[i] = o.out[i];
-  samp->rng_state = o.rng;
-  *out_n_accept = o.n_accept;
-  *out_new_pos = anchor_pos + 1 + o.n_accept;
-  *out_k_eff = k;
-  round_debug(s, o.n_accept, k);
-  return o.n_accept + 1;
+  uint64_t rng = samp ? samp->rng_state : 0;
+  const int rc = spec_round_seq0(m, s, anchor, anchor_pos, k, p_min, n_min, samp, true, debug_break_rollback,
+                                 debug_skip_catchup, out, out_n_accept, out_new_pos, out_k_eff, &rng, errbuf,
+                                 errlen);
+  if (rc >= 0) samp->rng_state = rng;
+  return rc;
 }
 
 extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const int* prompt, int n_prompt,
@@ -1826,7 +1835,10 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
     return LZ98_ERR_NULL_ARG;
   }
   const Cfg& c = m->c;
-  sr_down(s);
+  if (!sr_down(s)) {
+    round_fail(s, errbuf, errlen, "CUDA failure before prefill");
+    return LZ98_ERR_CUDA;
+  }
   const int slot = s->h_sr[seq].ssm_slot;
   int mtp_pos = s->h_sr[seq].mtp_pos;
   const int n = n_prompt - 1;
@@ -1865,14 +1877,20 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
     set_err(errbuf, errlen, "CUDA failure in prefill");
     return LZ98_ERR_CUDA;
   }
-  sr_down(s);                        // the sampler state advanced on the device
+  if (!sr_down(s)) {                 // the sampler state advanced on the device
+    round_fail(s, errbuf, errlen, "CUDA failure in prefill");
+    return LZ98_ERR_CUDA;
+  }
   SeqRound& r = s->h_sr[seq];
   r.anchor = anchor;
   r.anchor_pos = n_prompt - 1;
   r.mtp_pos = mtp_pos;
   r.ssm_slot = slot;
-  sr_up(s);
-  cudaStreamSynchronize(s->st);
+  r.dbg = 0;
+  if (!sr_up(s) || !sync_ok(s)) {
+    round_fail(s, errbuf, errlen, "CUDA failure in prefill");
+    return LZ98_ERR_CUDA;
+  }
   if (out_anchor) *out_anchor = anchor;
   return 0;
 }
@@ -1885,20 +1903,24 @@ extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* 
     return LZ98_ERR_SPEC_K_RANGE;
   }
   if (run_round(s, k)) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
+    round_fail(s, errbuf, errlen, "CUDA failure in the round");
     return LZ98_ERR_CUDA;
   }
   if (out_tokens || out_counts) {
-    sr_down(s);
+    if (!sr_down(s)) {
+      round_fail(s, errbuf, errlen, "CUDA failure in the round");
+      return LZ98_ERR_CUDA;
+    }
     for (int b = 0; b < s->B; b++) {
       const SeqRound& o = s->h_sr[b];
       if (out_counts) out_counts[b] = o.n_emit;
       if (out_tokens)
         for (int i = 0; i <= k; i++) out_tokens[b * (k + 1) + i] = i <= o.n_accept ? o.out[i] : -1;
     }
-  }
-  if (cudaGetLastError() != cudaSuccess) {
-    set_err(errbuf, errlen, "CUDA failure in the round");
+  } else if (cudaPeekAtLastError() != cudaSuccess || (s->h_err && *(volatile int*)s->h_err)) {
+    // without a read-back the round is not waited for: launch errors and
+    // a wait that gave up in an earlier round are reported here
+    round_fail(s, errbuf, errlen, "CUDA failure in the round");
     return LZ98_ERR_CUDA;
   }
   return 0;
@@ -1919,9 +1941,18 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
   }
   const Cfg& c = m->c;
   lz_state_reset(s, m);                     // src/generate.c:2813
-  LZSampler samp{temp > 0.0f ? temp : 0.0f, topp, seed ? seed : 1ull};
-  const bool use_temp = samp.temperature > kTempFloor;
-  if (int rc = lz_seq_set_sampler(s, 0, samp.temperature, topp, samp.rng_state)) return rc;
+  // the reference loop's sampler (oracle-free restatement of its settings,
+  // src/generate.c:2790): temperature, top-p, identity penalties, no top-k
+  // or min-p, the generator seeded with `seed` (0 taken as 1)
+  LZSampler samp;
+  memset(&samp, 0, sizeof samp);
+  samp.vocab_size = c.vocab;
+  samp.p.temperature = temp > 0.0f ? temp : 0.0f;
+  samp.p.topp = topp;
+  samp.p.repetition_penalty = 1.0f;
+  samp.rng_state = seed ? seed : 1ull;
+  const bool use_temp = samp.p.temperature > kTempFloor;
+  if (int rc = lz_seq_set_sampler(s, 0, samp.p.temperature, topp, samp.rng_state)) return rc;
   int max_pos = n_prompt + max_new;
   if (max_pos > s->seq_len) max_pos = s->seq_len;
   if (max_pos < n_prompt + 1) max_pos = n_prompt + 1;
@@ -1931,7 +1962,7 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
   // one forward of `token` at `pos` in place (optionally captured into the
   // draft chain), then one token sampled by the sequence's sampler
   auto step = [&](bool capture, int* next) {
-    sr_down(s);
+    if (!sr_down(s)) return 1;
     const int slot = s->h_sr[0].ssm_slot;
     if (cudaMemcpyAsync(s->tok, &token, sizeof(int), cudaMemcpyHostToDevice, s->st) != cudaSuccess) return 1;
     upload_seqs(s, {KdaSeq{0, 1, slot, 0}});
@@ -1975,7 +2006,7 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
       int out[8], n_acc = 0, new_pos = 0, k_eff = 0;
       int ne;
       if (use_temp) {
-        sr_down(s);
+        if (!sr_down(s)) return LZ98_ERR_CUDA;
         samp.rng_state = s->h_sr[0].rng;
         ne = lz_spec_round_temp(m, s, anchor, anchor_pos, round_k, p_min, n_min, &samp, 0, 0, out, &n_acc,
                                 &new_pos, &k_eff, errbuf, errlen);
@@ -2020,7 +2051,7 @@ extern "C" int lz_state_counters(const LZRunState* cs, int seq, int* rounds, int
                                  int* drafted) {
   LZRunState* s = const_cast<LZRunState*>(cs);
   if (!s || seq < 0 || seq >= s->B) return LZ98_ERR_NULL_ARG;
-  sr_down(s);
+  if (!sr_down(s)) return LZ98_ERR_CUDA;
   const SeqRound& r = s->h_sr[seq];
   if (rounds) *rounds = r.rounds;
   if (emitted) *emitted = r.emitted;
@@ -2110,8 +2141,16 @@ static __device__ __align__(256) int8_t g_static_xq[kStaticRows * kStaticDim];
 static __device__ __align__(256) float g_static_xs[kStaticRows * kStaticDim / 32];
 
 constexpr int kMaxDevices = 64;
-int8_t* g_static_xq_addr[kMaxDevices];
-float* g_static_xs_addr[kMaxDevices];
+
+// Device addresses of the two arrays, resolved once per device (the
+// arrays' host-side names are not device addresses).
+struct StaticScratch {
+  std::once_flag once;
+  cudaError_t rc = cudaSuccess;
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+};
+StaticScratch g_static[kMaxDevices];
 
 // Per-32 quantisation of n rows (src/ops_quant.c:2152-2282).
 __global__ void quant_rows_kernel(const float* __restrict__ x, int d, int8_t* xq, float* xs) {
@@ -2139,46 +2178,62 @@ extern "C" int lz_lm_head_static(const LZModel* m, const float* hidden, int n, f
     snprintf(msg, sizeof msg, "lz_lm_head_static: %d rows of %d columns exceed the static scratch (%d x %d)",
              n, c.d, kStaticRows, kStaticDim);
     set_err(errbuf, errlen, "%s", msg);
-    return LZ98_ERR_SPEC_K_RANGE;
+    return LZ98_ERR_SIZE;
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     set_err(errbuf, errlen, "lz_lm_head_static: no current CUDA device");
     return LZ98_ERR_CUDA;
   }
-  // One-time set-up per device, with that device current: the device
-  // addresses of the scratch arrays (their host-side names are not device
-  // addresses).  Done by the first call on the device.
-  if (!g_static_xq_addr[dev]) {
+  if (dev != m->dev) {
+    set_err(errbuf, errlen, "lz_lm_head_static: the current CUDA device is not the model's");
+    return LZ98_ERR_DEVICE;
+  }
+  // One-time set-up per device, with that device current (the first call
+  // on the device does it; std::call_once makes concurrent first calls
+  // from several host threads wait for one resolution).
+  StaticScratch& g = g_static[dev];
+  std::call_once(g.once, [&g] {
     void* pq = nullptr;
     void* ps = nullptr;
-    if (cudaGetSymbolAddress(&pq, g_static_xq) != cudaSuccess ||
-        cudaGetSymbolAddress(&ps, g_static_xs) != cudaSuccess || !pq || !ps) {
-      set_err(errbuf, errlen, "lz_lm_head_static: cudaGetSymbolAddress failed");
+    g.rc = cudaGetSymbolAddress(&pq, g_static_xq);
+    if (g.rc == cudaSuccess) g.rc = cudaGetSymbolAddress(&ps, g_static_xs);
+    if (g.rc == cudaSuccess && (!pq || !ps)) g.rc = cudaErrorInvalidSymbol;
+    g.xq = static_cast<int8_t*>(pq);
+    g.xs = static_cast<float*>(ps);
+  });
+  if (g.rc != cudaSuccess) {
+    set_err(errbuf, errlen, "lz_lm_head_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(g.rc));
+    return LZ98_ERR_CUDA;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // each launch's own status (cudaLaunchKernel), not a sticky earlier error
+  const int8_t* xq = g.xq;
+  const float* xs = g.xs;
+  {
+    int8_t* q = g.xq;
+    float* sc = g.xs;
+    int d = c.d;
+    void* args[] = {(void*)&hidden, &d, &q, &sc};
+    const cudaError_t e = cudaLaunchKernel((const void*)quant_rows_kernel, dim3(n), dim3(256), args, 0, st);
+    if (e != cudaSuccess) {
+      set_err(errbuf, errlen, "lz_lm_head_static: quantisation launch failed: %s", cudaGetErrorString(e));
       return LZ98_ERR_CUDA;
     }
-    g_static_xs_addr[dev] = static_cast<float*>(ps);
-    g_static_xq_addr[dev] = static_cast<int8_t*>(pq);
   }
-  int8_t* xq = g_static_xq_addr[dev];
-  float* xs = g_static_xs_addr[dev];
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  quant_rows_kernel<<<n, 256, 0, st>>>(hidden, c.d, xq, xs);
   const QW& w = m->embed;
   GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, n, logits, c.vocab, 0, nullptr, nullptr, 0, 32, nullptr, nullptr};
   const dim3 grid((w.out + kGemvWarps - 1) / kGemvWarps), blk(kGemvWarps * 32);
   const int nsb = w.in / 32;
-  if (nsb <= 32)
-    gemv_q8_kernel<1, kGemvWarps, kGemvRB, false, true>
-        <<<grid, blk, gemv_smem_bytes(1, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
-  else if (nsb <= 64)
-    gemv_q8_kernel<2, kGemvWarps, kGemvRB, false, true>
-        <<<grid, blk, gemv_smem_bytes(2, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
-  else
-    gemv_q8_kernel<4, kGemvWarps, kGemvRB, false, true>
-        <<<grid, blk, gemv_smem_bytes(4, kGemvWarps, kGemvRB, true, false, n, w.in), st>>>(a);
-  if (cudaGetLastError() != cudaSuccess) {
-    set_err(errbuf, errlen, "lz_lm_head_static: kernel launch failed");
+  const int jm = nsb <= 32 ? 1 : nsb <= 64 ? 2 : 4;
+  const void* kern = jm == 1 ? (const void*)gemv_q8_kernel<1, kGemvWarps, kGemvRB, false, true>
+                     : jm == 2 ? (const void*)gemv_q8_kernel<2, kGemvWarps, kGemvRB, false, true>
+                               : (const void*)gemv_q8_kernel<4, kGemvWarps, kGemvRB, false, true>;
+  void* gargs[] = {&a};
+  const cudaError_t e =
+      cudaLaunchKernel(kern, grid, blk, gargs, gemv_smem_bytes(jm, kGemvWarps, kGemvRB, true, false, n, w.in), st);
+  if (e != cudaSuccess) {
+    set_err(errbuf, errlen, "lz_lm_head_static: lm_head launch failed: %s", cudaGetErrorString(e));
     return LZ98_ERR_CUDA;
   }
   return 0;
@@ -2227,6 +2282,16 @@ extern "C" int lz_debug_wait_timeout(int* out_err, double* out_ms) {
   *out_err = *(volatile int*)h;
   cudaFreeHost(h);
   return rc;
+}
+
+extern "C" int lz_debug_inject_wait_timeout(int on, double limit_ms) {
+  const int skip = on ? 1 : 0;
+  const unsigned long long lim =
+      on ? (unsigned long long)(std::max(limit_ms, 0.001) * 1e6) : 1000000000ull;   // default: about a second
+  if (cudaMemcpyToSymbol(g_dbg_skip_stage, &skip, sizeof skip) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof lim) != cudaSuccess)
+    return LZ98_ERR_CUDA;
+  return cudaDeviceSynchronize() == cudaSuccess ? 0 : LZ98_ERR_CUDA;
 }
 
 extern "C" int lz_debug_argmax_p1(const float* vals, int n, int* out_idx, float* out_p1) {
@@ -2306,7 +2371,10 @@ extern "C" int lz_ckpt_save_seq(LZStateCkpt* ck, const LZRunState* cs, int seq, 
     set_err(errbuf, errlen, "checkpoint does not match this model's shapes");
     return LZ98_ERR_CKPT_SHAPE;
   }
-  sr_down(s);
+  if (!sr_down(s)) {
+    set_err(errbuf, errlen, "CUDA failure while saving");
+    return LZ98_ERR_CUDA;
+  }
   const int slot = s->h_sr[seq].ssm_slot;   // the live slot of the ring
   const size_t oq = (size_t)seq * s->q_seq + (size_t)slot * s->q_slot;
   const size_t oc = (size_t)seq * s->conv_seq + (size_t)slot * s->conv_slot;
@@ -2349,10 +2417,9 @@ extern "C" int lz_ckpt_restore_seq(const LZStateCkpt* ck, LZRunState* s, int seq
     set_err(errbuf, errlen, "CUDA failure while restoring");
     return LZ98_ERR_CUDA;
   }
-  sr_down(s);
+  const bool ok = sr_down(s);
   s->h_sr[seq].ssm_slot = 0;
-  sr_up(s);
-  if (!sync_ok(s)) {
+  if (!ok || !sr_up(s) || !sync_ok(s)) {
     set_err(errbuf, errlen, "CUDA failure while restoring");
     return LZ98_ERR_CUDA;
   }

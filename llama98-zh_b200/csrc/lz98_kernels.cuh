@@ -830,12 +830,14 @@ __global__ void __launch_bounds__(288) gemm_q8_tma_kernel(const __grid_constant_
     if (lane != 0) return;
     bool ok = true;
     int it = 0;
+    const bool skip0 = g_dbg_skip_stage != 0;   // test hook: stage 0 is never filled
     for (; it < nit; it++) {
       const int stg = it % kTmaStages;
       if (it >= kTmaStages && !mbar_wait(bars + 8 * (kTmaStages + stg), (it / kTmaStages - 1) & 1)) {
         ok = false;
         break;
       }
+      if (skip0 && it == 0) continue;
       const bool two = it >= it1;
       const int c = two ? it - it1 : it;
       const uint32_t full = bars + 8 * stg, tile = base + stg * T::TILES, sm = small + stg * T::SMALL;
@@ -1722,7 +1724,7 @@ __global__ void __launch_bounds__((MoeTma<W13, RB1>::CW + 1) * 32) moe_tma_kerne
     }
   };
   if (threadIdx.x == CW * 32)
-    for (int it = 0; it < min(nit, NST); it++) issue(it);
+    for (int it = g_dbg_skip_stage ? 1 : 0; it < min(nit, NST); it++) issue(it);   // the hook skips stage 0
   // resident activation rows of the tile (rows past the count repeat the last)
   {
     const int cpr = K >> 4;   // 16-byte chunks per row
@@ -2149,11 +2151,16 @@ mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
 
 // ------------------------------------------------------- spec rounds
 
+// SeqRound.dbg: the rounds' test-only switches of lz_spec_round
+// (src/generate.c:827-844, 976-982).
+constexpr int kDbgBreakRollback = 1;   // a rejecting round leaves the ring where the verify left it
+constexpr int kDbgSkipCatchup = 2;     // no MTP catch-up rows
+
 struct SeqRound {          // per-sequence round bookkeeping on the device
   unsigned long long rng;   // sampler xorshift64* state (src/sampler.c:185-203)
   float temp, topp;         // sampler temperature and top-p
   int anchor, anchor_pos, mtp_pos, ssm_slot;
-  int k, n_accept, n_emit, done;
+  int k, n_accept, n_emit, dbg;
   int draft[8], out[8];
   int rounds, emitted, accepted, drafted;   // running totals
 };
@@ -2171,12 +2178,16 @@ LZ_HD void round_bookkeeping(SeqRound& s, int b, int n_accept, int k, int kmax, 
   s.emitted += n_accept + 1;
   s.accepted += n_accept;
   s.drafted += k;
-  s.ssm_slot = (s.ssm_slot + n_accept + 1) % depth;
+  // the ring rollback: the verify advanced the ring by k + 1 slots; a
+  // round that rejected a draft points it at slot base + n_accept + 1
+  // instead (the known-bad control leaves it at base + k + 1)
+  const bool broken = (s.dbg & kDbgBreakRollback) && n_accept < k;
+  s.ssm_slot = (s.ssm_slot + (broken ? k : n_accept) + 1) % depth;
   for (int j = 0; j < kmax - 1; j++) {
     MtpRow cr;
     cr.seq = b;
     cr.pos = s.mtp_pos + 1 + j;
-    cr.active = j < n_accept - 1 && cr.pos < seq_len;
+    cr.active = j < n_accept - 1 && cr.pos < seq_len && !(s.dbg & kDbgSkipCatchup);
     catch_rows[b * (kmax - 1) + j] = cr;
     catch_tok[b * (kmax - 1) + j] = s.out[j < 8 ? j : 0];
     catch_hidx[b * (kmax - 1) + j] = row0 + j;

@@ -21,7 +21,11 @@ _lib = None
 
 
 class LzError(RuntimeError):
-    pass
+    """A failed call; .code is the library's return code when known."""
+
+    def __init__(self, msg, code=None):
+        super().__init__(msg)
+        self.code = code
 
 
 def _ptr(a):
@@ -67,6 +71,7 @@ def lib():
                                         P(ctypes.c_uint64), P(c_int)]),
         "lz_seq_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, P(c_int), c_char_p, c_int]),
         "lz_seq_set_sampler": (c_int, [c_void_p, c_int, c_float, c_float, ctypes.c_uint64]),
+        "lz_seq_get_sampler": (c_int, [c_void_p, c_int, P(c_float), P(c_float), P(ctypes.c_uint64)]),
         "lz_spec_round_batch": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_set_graphs": (c_int, [c_void_p, c_int]),
         "lz_set_pdl": (c_int, [c_void_p, c_int]),
@@ -80,6 +85,7 @@ def lib():
         "lz_read_weights": (c_int, [c_void_p, c_char_p, c_int]),
         "lz_profile_experts": (c_int, [c_void_p, P(ctypes.c_double), P(ctypes.c_double), P(c_int)]),
         "lz_debug_wait_timeout": (c_int, [P(c_int), P(ctypes.c_double)]),
+        "lz_debug_inject_wait_timeout": (c_int, [c_int, ctypes.c_double]),
         "lz_set_debug_timing": (c_int, [c_void_p, c_int]),
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
@@ -103,20 +109,45 @@ def lib():
     return L
 
 
-EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_debug_inject_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
            "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
            "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
-           "lz_seq_prefill", "lz_seq_set_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
+           "lz_seq_prefill", "lz_seq_set_sampler", "lz_seq_get_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
            "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static", "lz_debug_seq_sum",
            "lz_ckpt_alloc", "lz_ckpt_free", "lz_ckpt_save", "lz_ckpt_restore", "lz_ckpt_save_seq",
            "lz_ckpt_restore_seq"]
 
 
+class LZSampleParams(ctypes.Structure):
+    """The reference's LZSampleParams (src/sampler.h:144-173), field for field."""
+    _fields_ = [("temperature", c_float), ("temp_think", c_float), ("think_temp_enabled", c_int),
+                ("topp", c_float), ("minp", c_float), ("topk", c_int), ("presence_penalty", c_float),
+                ("frequency_penalty", c_float), ("repetition_penalty", c_float), ("repeat_last_n", c_int),
+                ("minp_llamacpp", c_int)]
+
+
 class LZSampler(ctypes.Structure):
-    _fields_ = [("temperature", c_float), ("topp", c_float), ("rng_state", ctypes.c_uint64)]
+    """The reference's LZSampler (src/sampler.h:176-186), field for field."""
+    _fields_ = [("vocab_size", c_int), ("p", LZSampleParams), ("rng_state", ctypes.c_uint64),
+                ("probindex", c_void_p), ("counts", c_void_p), ("ring", c_void_p), ("cap", c_int),
+                ("head", c_int), ("n_win", c_int)]
+
+
+def make_sampler(vocab, temp, topp, rng, **params):
+    """An LZSampler with the reference loop's settings (identity penalties,
+    no top-k or min-p) and any field of LZSampleParams overridden."""
+    smp = LZSampler()
+    smp.vocab_size = int(vocab)
+    smp.p.temperature = float(temp)
+    smp.p.topp = float(topp)
+    smp.p.repetition_penalty = 1.0
+    for k, v in params.items():
+        setattr(smp.p, k, v)
+    smp.rng_state = int(rng)
+    return smp
 
 
 class Model:
@@ -242,27 +273,32 @@ class State:
         if lib().lz_mtp_prefill(self.m.h, self.h, _ptr(h), _ptr(t), len(t), pos0):
             raise LzError("mtp prefill failed")
 
-    def spec_round(self, anchor, anchor_pos, k):
+    def spec_round(self, anchor, anchor_pos, k, samp=None, break_rollback=0, skip_catchup=0):
         out = np.zeros(8, np.int32)
         na, npos, ke = c_int(), c_int(), c_int()
         err = ctypes.create_string_buffer(256)
-        rc = lib().lz_spec_round(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0, None, 0, 0, _ptr(out),
-                                 ctypes.byref(na), ctypes.byref(npos), ctypes.byref(ke), err, 256)
+        rc = lib().lz_spec_round(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0,
+                                 ctypes.byref(samp) if samp is not None else None, int(break_rollback),
+                                 int(skip_catchup), _ptr(out), ctypes.byref(na), ctypes.byref(npos),
+                                 ctypes.byref(ke), err, 256)
         if rc < 0:
-            raise LzError(f"spec round failed ({rc}): {err.value.decode()}")
+            raise LzError(f"spec round failed ({rc}): {err.value.decode()}", rc)
         return out[:rc].copy(), na.value, npos.value, ke.value
 
-    def spec_round_temp(self, anchor, anchor_pos, k, temp, topp, rng):
+    def spec_round_temp(self, anchor, anchor_pos, k, temp, topp, rng, break_rollback=0, skip_catchup=0,
+                        samp=None):
         """One coupled temperature round of sequence 0; returns the tokens,
         n_accept, the new position, k_eff and the advanced generator."""
         out = np.zeros(8, np.int32)
         na, npos, ke = c_int(), c_int(), c_int()
         err = ctypes.create_string_buffer(256)
-        samp = LZSampler(float(temp), float(topp), int(rng))
-        rc = lib().lz_spec_round_temp(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0, ctypes.byref(samp), 0, 0,
-                                      _ptr(out), ctypes.byref(na), ctypes.byref(npos), ctypes.byref(ke), err, 256)
+        if samp is None:
+            samp = make_sampler(self.m.vocab, temp, topp, rng)
+        rc = lib().lz_spec_round_temp(self.m.h, self.h, anchor, anchor_pos, k, 0.0, 0, ctypes.byref(samp),
+                                      int(break_rollback), int(skip_catchup), _ptr(out), ctypes.byref(na),
+                                      ctypes.byref(npos), ctypes.byref(ke), err, 256)
         if rc < 0:
-            raise LzError(f"temperature round failed ({rc}): {err.value.decode()}")
+            raise LzError(f"temperature round failed ({rc}): {err.value.decode()}", rc)
         return out[:rc].copy(), na.value, npos.value, ke.value, samp.rng_state
 
     # --- batched path
@@ -270,6 +306,14 @@ class State:
         rc = lib().lz_seq_set_sampler(self.h, seq, float(temp), float(topp), int(seed))
         if rc:
             raise LzError(f"set sampler failed ({rc})")
+
+    def get_sampler(self, seq=0):
+        """(temperature, top-p, generator state) of sequence `seq` on the device."""
+        t, p, r = c_float(), c_float(), ctypes.c_uint64()
+        rc = lib().lz_seq_get_sampler(self.h, seq, ctypes.byref(t), ctypes.byref(p), ctypes.byref(r))
+        if rc:
+            raise LzError(f"get sampler failed ({rc})", rc)
+        return t.value, p.value, r.value
 
     def seq_prefill(self, seq, prompt):
         p = np.ascontiguousarray(prompt, np.int32)
@@ -286,7 +330,7 @@ class State:
         cnt = np.zeros(self.n_seq, np.int32) if fetch else None
         rc = lib().lz_spec_round_batch(self.m.h, self.h, k, _ptr(toks), _ptr(cnt), err, 256)
         if rc:
-            raise LzError(f"batched round failed ({rc}): {err.value.decode()}")
+            raise LzError(f"batched round failed ({rc}): {err.value.decode()}", rc)
         return toks, cnt
 
     def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):

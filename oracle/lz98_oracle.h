@@ -71,4 +71,8 @@ float lzo_random_f32(unsigned long long *state);
 #ifdef __cplusplus
 }
 #endif
+/* Logits of n final-normed hidden rows over vocabulary rows
+   [v0, v0 + nv) of the tied lm_head. */
+int lzo_lm_head_cols(const LzoModel *m, const float *hidden, int n, int v0, int nv, float *out);
+
 #endif

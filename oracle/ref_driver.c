@@ -32,6 +32,19 @@ typedef struct {
     int have_m, have_s;
 } RdHandle;
 
+/* The rounds' two test-only switches, passed unchanged to lz_spec_round /
+   lz_spec_round_temp by the generation loop below: debug_break_rollback
+   (the reference's known-bad control, src/generate.c:827-844: a rejected
+   round leaves the state ring where the full verify left it) and
+   debug_skip_catchup (src/generate.c:976-982).  Process-global; 0 by
+   default. */
+static int rd_dbg_break_rollback = 0, rd_dbg_skip_catchup = 0;
+
+void rd_set_round_debug(int break_rollback, int skip_catchup) {
+    rd_dbg_break_rollback = break_rollback;
+    rd_dbg_skip_catchup = skip_catchup;
+}
+
 static double rd_now_ms(void) {
     struct timespec ts;
     clock_gettime(CLOCK_MONOTONIC, &ts);
@@ -262,11 +275,13 @@ int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
             }
             if (temp > 0.0f)
                 n_emit = lz_spec_round_temp(m, s, anchor, anchor_pos, round_k,
-                                            p_min, n_min, &samp, 0, 0, out, &n_accept,
+                                            p_min, n_min, &samp, rd_dbg_break_rollback,
+                                            rd_dbg_skip_catchup, out, &n_accept,
                                             &new_pos, &k_eff, err, (int)sizeof err);
             else
                 n_emit = lz_spec_round(m, s, anchor, anchor_pos, round_k,
-                                       p_min, n_min, &samp, 0, 0, out, &n_accept,
+                                       p_min, n_min, &samp, rd_dbg_break_rollback,
+                                       rd_dbg_skip_catchup, out, &n_accept,
                                        &new_pos, &k_eff, err, (int)sizeof err);
             if (n_emit < 0) { rc = -n_emit; goto out; }
             if (nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_accept; }

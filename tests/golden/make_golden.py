@@ -37,6 +37,29 @@ TOKEN_CASES = {
 }
 
 
+# The benchmarked workloads themselves (bench.py), on the ~0.5B config:
+#  - b1: the headline, bench.prompts(1, 0)[0] (512 uniform ids), greedy,
+#    k = 2, BENCH_B1_NEW new tokens;
+#  - b32: four sequences of the batch-32 workload
+#    (lz98_synth.workload_prompts(cfg, 32, 256, 1024, 1.1, seed=0): the
+#    shortest, the longest and two more), each with its own sampler
+#    (temperature 0.8, top-p 0.95, seed 1000 + b), k = 3, BENCH_B32_NEW
+#    new tokens.
+BENCH_B1_NEW = 48
+BENCH_B32_NEW = 32
+BENCH_B32_SEQS = 32
+
+
+# The rounds' test-only switches on the reference itself: (model, k,
+# temperature, debug_break_rollback, debug_skip_catchup).  The temperature
+# rounds both reject and accept runs of drafts, so both switches change the
+# stream (it leaves the normal generation within the first 10 tokens on
+# every case below); the greedy streams of these random-weight models repeat
+# one token, so the greedy case only pins the switch's bookkeeping.
+DEBUG_CASES = [("tiny", 3, 0.8, 1, 0), ("tiny", 3, 0.8, 0, 1), ("midi", 3, 0.8, 1, 0),
+               ("midi_f16", 3, 0.8, 0, 1), ("tiny", 2, 0.0, 1, 0)]
+
+
 PM_CASES = {
     "tiny": [(3.5e-4, 0, 0.0), (3.5e-4, 2, 0.0), (2e-4, 0, 0.8), (1e-4, 2, 0.8)],
     "midi": [(1.2e-3, 0, 0.0), (1.2e-3, 2, 0.0), (2e-4, 0, 0.8), (6e-4, 2, 0.8)],
@@ -112,6 +135,86 @@ def make_tokens(name):
     print(path, os.path.getsize(path))
 
 
+def b32_pick(prompts):
+    """The four pinned batch-32 sequences: shortest, longest, then the
+    first two others."""
+    lens = [len(p) for p in prompts]
+    pick = [int(np.argmin(lens)), int(np.argmax(lens))]
+    for b in range(len(prompts)):
+        if len(pick) == 4:
+            break
+        if b not in pick:
+            pick.append(b)
+    return pick
+
+
+def _bench_job(job):
+    kind, idx = job
+    d = model_dir("0p5b")
+    if kind == "b1":
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        import bench
+        prompt = bench.prompts(1, 0)[0]
+        R = Reference(d, len(prompt) + BENCH_B1_NEW + 64, 4)
+        toks, rounds = R.generate(prompt, BENCH_B1_NEW, 2)
+    else:
+        cfg = lz98_synth.CONFIGS["0p5b"]
+        prompt = np.array(lz98_synth.workload_prompts(cfg, BENCH_B32_SEQS, 256, 1024, 1.1, seed=0)[idx], np.int32)
+        R = Reference(d, len(prompt) + BENCH_B32_NEW + 64, 4)
+        toks, rounds = R.generate(prompt, BENCH_B32_NEW, 3, temp=0.8, topp=0.95, seed=1000 + idx)
+    R.close()
+    return kind, idx, np.asarray(prompt, np.int32), toks, rounds
+
+
+def make_bench():
+    """tests/golden/0p5b_bench.npz: the reference's token streams and round
+    records on the benchmarked workloads (one reference process per
+    sequence)."""
+    import multiprocessing as mp
+    d = model_dir("0p5b")
+    sha = lz98_synth.write_model(lz98_synth.CONFIGS["0p5b"], d)
+    cfg = lz98_synth.CONFIGS["0p5b"]
+    pick = b32_pick(lz98_synth.workload_prompts(cfg, BENCH_B32_SEQS, 256, 1024, 1.1, seed=0))
+    jobs = [("b1", 0)] + [("b32", b) for b in pick]
+    with mp.get_context("spawn").Pool(len(jobs)) as pool:
+        res = pool.map(_bench_job, jobs)
+    out = {"sha256": np.frombuffer(bytes.fromhex(sha), np.uint8), "b32_pick": np.array(pick, np.int32),
+           "b1_max_new": np.array([BENCH_B1_NEW], np.int32), "b32_max_new": np.array([BENCH_B32_NEW], np.int32)}
+    for kind, idx, prompt, toks, rounds in res:
+        tag = "b1" if kind == "b1" else f"b32_{idx}"
+        out[tag + "_prompt"], out[tag + "_tokens"], out[tag + "_rounds"] = prompt, toks, rounds
+    path = os.path.join(HERE, "0p5b_bench.npz")
+    np.savez_compressed(path, **out)
+    print(path, os.path.getsize(path))
+
+
+def make_debug():
+    """tests/golden/round_debug.npz: generations of the reference with its
+    rounds' debug_break_rollback / debug_skip_catchup switches on (the
+    prompt of each model's own fixture, seed 1234, top-p 0.95)."""
+    out = {"cases": np.array([(k, t, br, sc) for _, k, t, br, sc in DEBUG_CASES], np.float64),
+           "models": np.array([m for m, *_ in DEBUG_CASES])}
+    for j, (name, k, temp, br, sc) in enumerate(DEBUG_CASES):
+        d = model_dir(name)
+        g = np.load(os.path.join(HERE, f"{name}.npz"))
+        R = Reference(d, 512, 4)
+        R.round_debug(br, sc)
+        toks, rounds = R.generate(g["prompt"], CASES[name][3], k, temp=temp, seed=1234)
+        R.round_debug(0, 0)
+        R.close()
+        out[f"c{j}_prompt"], out[f"c{j}_tokens"], out[f"c{j}_rounds"] = g["prompt"], toks, rounds
+    path = os.path.join(HERE, "round_debug.npz")
+    np.savez_compressed(path, **out)
+    print(path, os.path.getsize(path))
+
+
 if __name__ == "__main__":
-    for n in (sys.argv[1:] or list(CASES) + list(TOKEN_CASES)):
-        make_tokens(n) if n in TOKEN_CASES else make(n)
+    for n in (sys.argv[1:] or list(CASES) + list(TOKEN_CASES) + ["bench", "debug"]):
+        if n == "bench":
+            make_bench()
+        elif n == "debug":
+            make_debug()
+        elif n in TOKEN_CASES:
+            make_tokens(n)
+        else:
+            make(n)

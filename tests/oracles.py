@@ -73,6 +73,7 @@ class Oracle:
         L.lzo_set_chain.argtypes = [c_void_p, c_void_p]
         L.lzo_get_chain.argtypes = [c_void_p, c_void_p]
         L.lzo_state_reset.argtypes = [c_void_p]
+        L.lzo_lm_head_cols.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]
         L.lzo_info.argtypes = [c_void_p, c_void_p]
         L.lzo_free.argtypes = [c_void_p]
         L.lzo_state_free.argtypes = [c_void_p]
@@ -126,6 +127,14 @@ class Oracle:
             raise RuntimeError("oracle forward failed")
         return hid.reshape(n, -1), (lg.reshape(n, -1) if lg is not None else None)
 
+    def lm_head_cols(self, hidden, v0, nv):
+        """Logits of the hidden rows over vocabulary rows [v0, v0 + nv)."""
+        h = np.ascontiguousarray(hidden, np.float32)
+        out = _f32(len(h) * nv)
+        if self.L.lzo_lm_head_cols(c_void_p(self.m), _ptr(h), len(h), v0, nv, _ptr(out)):
+            raise RuntimeError("oracle lm_head failed")
+        return out.reshape(len(h), nv)
+
     def mtp_draft(self, tok, pos):
         lg = _f32(self.vocab)
         if self.L.lzo_mtp_draft(c_void_p(self.m), c_void_p(self.s), tok, pos, _ptr(lg)):
@@ -178,6 +187,7 @@ class Reference:
         L.rd_reset.argtypes = [c_void_p]
         L.rd_set_stock_tier.argtypes = [c_int]
         L.rd_set_tier.argtypes = [c_int]
+        L.rd_set_round_debug.argtypes = [c_int, c_int]
         L.rd_close.argtypes = [c_void_p]
         err = ctypes.create_string_buffer(512)
         self.h = L.rd_open(model_dir.encode(), seq_len, spec_k_max, nt_cap, kernel, err, 512)
@@ -197,6 +207,11 @@ class Reference:
         defaults, --fixed all and --fastfp on, for timing the reference as
         shipped; its tokens then differ from the parity tier's."""
         self.L.rd_set_stock_tier(kernel)
+
+    def round_debug(self, break_rollback: int = 0, skip_catchup: int = 0):
+        """The rounds' test-only switches (process-global in the driver):
+        debug_break_rollback and debug_skip_catchup of lz_spec_round."""
+        self.L.rd_set_round_debug(int(break_rollback), int(skip_catchup))
 
     def close(self):
         if self.h:

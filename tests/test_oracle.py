@@ -333,3 +333,22 @@ def test_oracle_headline_config_matches_golden():
             assert np.array_equal(rounds, g[f"run{j}_rounds"]), (j, k, temp)
     finally:
         O.close()
+
+
+def test_bench_golden_inputs_regenerate():
+    """The pinned bench workloads (tests/golden/0p5b_bench.npz) are the ones
+    bench.py runs: the batch-1 prompt is bench.prompts(1, 0)[0], the batch-32
+    prompts are workload_prompts(cfg, 32, 256, 1024, 1.1, seed=0) with the
+    shortest and the longest among the pinned four."""
+    import bench
+    import lz98_synth
+    from golden.make_golden import b32_pick
+    g = np.load(os.path.join(GOLDEN, "0p5b_bench.npz"))
+    assert np.array_equal(bench.prompts(1, 0)[0], g["b1_prompt"])
+    prompts = lz98_synth.workload_prompts(lz98_synth.CONFIGS["0p5b"], 32, 256, 1024, 1.1, seed=0)
+    assert b32_pick(prompts) == g["b32_pick"].tolist()
+    lens = [len(p) for p in prompts]
+    assert min(lens) in [len(g[f"b32_{b}_prompt"]) for b in g["b32_pick"]]
+    assert max(lens) in [len(g[f"b32_{b}_prompt"]) for b in g["b32_pick"]]
+    for b in g["b32_pick"]:
+        assert np.array_equal(np.array(prompts[b], np.int32), g[f"b32_{b}_prompt"])
