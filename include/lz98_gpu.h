@@ -252,6 +252,11 @@ int lz_profile_round(LZRunState *s, int k, double *gemv_ms, double *gemv_bytes,
    round (event-timed one by one): summed device time, algorithmic bytes
    (every expert's int8 weights and scales) and launch count. */
 int lz_profile_experts(const LZRunState *s, double *ms, double *bytes, int *n);
+/* Measurement hook (no counterpart in the reference): one eager round of
+   depth k with CUDA events around every kernel launch (launched plainly,
+   without programmatic overlap): "kernel<TAB>microseconds" lines into buf
+   in launch order.  Returns the launch count, or a negative code. */
+int lz_profile_launches(LZRunState *s, int k, char *buf, int buflen);
 /* Allocation-free logits (no counterpart in the reference): the tied
    lm_head over n final-normed hidden rows (as lz_forward_verify captures
    them), for callers that cannot allocate device memory themselves - a

@@ -470,6 +470,9 @@ struct LZRunState {
   std::vector<double> prof_moe_bytes;
   double prof_moe_ms = 0.0, prof_moe_b = 0.0;
   int prof_moe_n = 0;
+  // optional per-launch timing (lz_profile_launches): kernel and event pair
+  bool prof_all = false;
+  std::vector<std::tuple<const void*, cudaEvent_t, cudaEvent_t>> prof_launch;
   std::map<int, cudaGraphExec_t> graph;
   std::vector<void*> allocs;
   // 1 at allocation, +1 per reset (src/forward_state.c:1412,
@@ -511,8 +514,15 @@ void launch(LZRunState* s, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   // debug timing puts event records between kernels: plain launches then
-  cfg.numAttrs = s->pdl && !s->dbg_timing ? 1 : 0;
+  cfg.numAttrs = s->pdl && !s->dbg_timing && !s->prof_all ? 1 : 0;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (s->prof_all && cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess)
+    cudaEventRecord(e0, s->st);
   cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e1) {
+    cudaEventRecord(e1, s->st);
+    s->prof_launch.emplace_back((const void*)kern, e0, e1);
+  }
   s->launches++;
 }
 
@@ -2110,6 +2120,34 @@ extern "C" int lz_profile_round(LZRunState* s, int k, double* gemv_ms, double* g
   if (round_ms) *round_ms = rms;
   if (n_kernels) *n_kernels = (int)(s->launches - l0);
   return 0;
+}
+
+// One eager round of depth k with events around every launch: "kernel<TAB>
+// microseconds" lines into buf, in launch order.  Returns the launch count.
+extern "C" int lz_profile_launches(LZRunState* s, int k, char* buf, int buflen) {
+  if (!s || !buf || buflen < 1 || k < 1 || k > s->kmax || round_mode(s) < 0) return -LZ98_ERR_NULL_ARG;
+  s->prof_launch.clear();
+  s->prof_all = true;
+  round_any(s, k);
+  s->prof_all = false;
+  if (!sync_ok(s)) return -LZ98_ERR_CUDA;
+  int used = 0;
+  buf[0] = 0;
+  for (auto& t : s->prof_launch) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, std::get<1>(t), std::get<2>(t));
+    const char* name = "?";
+    if (cudaFuncGetName(&name, std::get<0>(t)) != cudaSuccess) name = "?";
+    if (used < buflen - 1) {
+      const int w = snprintf(buf + used, (size_t)(buflen - used), "%s\t%.3f\n", name, ms * 1000.0f);
+      used += w < 0 ? 0 : std::min(w, buflen - 1 - used);   // a cut line stays cut
+    }
+    cudaEventDestroy(std::get<1>(t));
+    cudaEventDestroy(std::get<2>(t));
+  }
+  const int n = (int)s->prof_launch.size();
+  s->prof_launch.clear();
+  return n;
 }
 
 // The grouped-expert launches of the last lz_profile_round: summed device

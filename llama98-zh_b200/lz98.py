@@ -90,6 +90,7 @@ def lib():
         "lz_state_counters": (c_int, [c_void_p, c_int, P(c_int), P(c_int), P(c_int), P(c_int)]),
         "lz_profile_round": (c_int, [c_void_p, c_int, P(ctypes.c_double), P(ctypes.c_double), P(c_int),
                                      P(ctypes.c_double), P(c_int)]),
+        "lz_profile_launches": (c_int, [c_void_p, c_int, c_char_p, c_int]),
         "lz_lm_head_static": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_state_stream": (c_void_p, [c_void_p]),
         "lz_ckpt_alloc": (c_int, [P(c_void_p), c_void_p, c_char_p, c_int]),
@@ -116,7 +117,7 @@ EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_debug_inject_wait_
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
            "lz_seq_prefill", "lz_seq_set_sampler", "lz_seq_get_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
-           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_lm_head_static", "lz_debug_seq_sum",
+           "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_profile_launches", "lz_lm_head_static", "lz_debug_seq_sum",
            "lz_ckpt_alloc", "lz_ckpt_free", "lz_ckpt_save", "lz_ckpt_restore", "lz_ckpt_save_seq",
            "lz_ckpt_restore_seq"]
 
@@ -224,6 +225,18 @@ class State:
         return {"gemv_ms": gm.value, "gemv_bytes": gb.value, "n_gemv": ng.value,
                 "round_ms": rm.value, "n_kernels": nk.value,
                 "expert_ms": em.value, "expert_bytes": eb.value, "n_expert": en.value}
+
+    def profile_launches(self, k):
+        """One eager round with every launch event-timed: [(kernel, us), ...]."""
+        buf = ctypes.create_string_buffer(1 << 20)
+        n = lib().lz_profile_launches(self.h, k, buf, len(buf))
+        if n < 0:
+            raise LzError(f"profile failed ({n})", n)
+        out = []
+        for line in buf.value.decode().splitlines():
+            name, us = line.rsplit("\t", 1)
+            out.append((name, float(us)))
+        return out
 
     def stream(self):
         return lib().lz_state_stream(self.h)
