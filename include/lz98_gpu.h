@@ -220,6 +220,11 @@ int lz_set_graphs(LZRunState *s, int enable);
    each kernel lets the next one start its prologue - weight prefetch -
    while it finishes; 0 launches them plainly serialised. */
 int lz_set_pdl(LZRunState *s, int enable);
+/* (no counterpart in the reference) Dense int8 GEMMs of more than 8 token
+   rows on the 5th-generation tensor cores (tcgen05.mma kind::i8 into tensor
+   memory, the default); 0 selects the warp-level mma.sync kernel.  Both
+   give the same bits. */
+int lz_set_umma(LZRunState *s, int enable);
 /* Whole generation on token ids (the reference's lz_generate_call spec
    loop, src/generate.c:2781-3091, without EOS/stop strings): greedy when
    temp <= 1e-3, else the coupled temperature rounds with top-p `topp`. */
@@ -234,6 +239,40 @@ int lz_generate_ex(const LZModel *m, LZRunState *s, const int *prompt, int n_pro
                    int max_new, int spec_k, float temp, float topp, uint64_t seed,
                    float p_min, int n_min, int *out_tok, int out_cap, int *out_n,
                    int *rounds, int round_cap, int *n_rounds, char *errbuf, int errlen);
+
+/* The generation loop of sequence 0 continued from body position
+   start_pos with the suffix tokens as its prompt, the state NOT reset (the
+   reference's lz_generate_resume, src/generate.c:2781-2840, on token ids):
+   after lz_prefix_prepare_tokens, start_pos is its *out_start_pos. */
+int lz_generate_resume(const LZModel *m, LZRunState *s, int start_pos, const int *suffix, int n_suffix,
+                       int max_new, int spec_k, float temp, float topp, uint64_t seed, int *out_tok,
+                       int out_cap, int *out_n, int *rounds, int round_cap, int *n_rounds, char *errbuf,
+                       int errlen);
+
+/* ---- prefix reuse: replaces LZPrefixCache, lz_prefix_init / _free /
+   _reset / _match / _prepare / _stats (src/llama_zh.h:781-888,
+   src/generate.c:3209-3390) on token ids.  The cache holds a device
+   checkpoint of sequence 0's recurrent state and the token prefix it
+   covers.  lz_prefix_prepare_tokens is lz_prefix_prepare with the render
+   already encoded by the caller: cur = encode(render), pre =
+   encode(render[:split]), tail = encode(render[split:]).  It checks that
+   the split is token-exact (else the full path: *out_start_pos = 0), that
+   the cached prefix is a prefix of cur and that the state was not reset
+   since the save (the checkpoint's epoch), restores on a hit, forwards the
+   rest of pre, saves the new prefix and returns 0 with *out_start_pos =
+   n_pre and *out_reused = the tokens not re-forwarded; generate from there
+   with lz_generate_resume(m, s, *out_start_pos, tail, n_tail, ...).  A
+   failed forward resets the state and the cache (LZ98_ERR_FORWARD). */
+typedef struct LZPrefixCache LZPrefixCache;
+int  lz_prefix_init(LZPrefixCache **out, const LZModel *m, char *errbuf, int errlen);
+void lz_prefix_free(LZPrefixCache *pc);
+void lz_prefix_reset(LZPrefixCache *pc);
+int  lz_prefix_match(const LZPrefixCache *pc, const int *pre, int n_pre);
+int  lz_prefix_prepare_tokens(LZPrefixCache *pc, const LZModel *m, LZRunState *s, const int *cur, int n_cur,
+                              const int *pre, int n_pre, const int *tail, int n_tail, int *out_start_pos,
+                              int *out_reused, char *errbuf, int errlen);
+void lz_prefix_stats(const LZPrefixCache *pc, long *calls, long *hits, long *tokens_saved, long *mismatch,
+                     long *unsplittable);
 
 /* (no counterpart in the reference) Running totals of sequence `seq` over
    its device rounds: rounds, emitted

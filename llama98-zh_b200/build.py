@@ -1,7 +1,8 @@
 """Build of the CUDA library liblz98gpu.so for sm_100a (in-tree, next to
 this file).  -fmad=false keeps every float multiply and add separately
 rounded, as the reference float tier is (its gcc build uses
--ffp-contract=off); division and square root stay IEEE-rounded and
+-ffp-contract=off; the host side, which builds the RoPE table, is compiled
+with it too); division and square root stay IEEE-rounded and
 denormals are kept (no --use_fast_math, no -ftz)."""
 from __future__ import annotations
 
@@ -20,7 +21,7 @@ DEPS = SRCS + sorted(os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.j
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
     "-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false",
-    "-Xcompiler", "-fPIC", "-shared", "-Xlinker", "-Bsymbolic",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "-shared", "-Xlinker", "-Bsymbolic",
 ]
 
 

@@ -22,6 +22,8 @@
 #include "../../include/lz98_gpu.h"
 #include "lz98_kernels.cuh"
 #include "lz98_sample.cuh"
+#include "lz98_umma.cuh"
+#include "lz98_rope_table.h"
 
 using namespace lz98;
 
@@ -461,6 +463,7 @@ struct LZRunState {
   long long launches = 0;
   bool graphs = true;
   bool pdl = true;                   // programmatic dependent launch
+  bool umma = true;                  // R > 8 dense GEMMs on tcgen05 (else the mma.sync TMA kernel)
   // optional per-GEMV timing (lz_profile_round): event pairs and bytes
   bool prof = false;
   std::vector<cudaEvent_t> prof_ev;
@@ -539,6 +542,9 @@ void tma_variants(F f) {
   f(gemm_q8_tma_kernel<1, 1, false, 2>, TmaTile<1, 1, false>::smem());
   f(gemm_q8_tma_kernel<1, 2, false, 2>, TmaTile<1, 2, false>::smem());
   f(gemm_q8_tma_kernel<2, 1, false, 2>, TmaTile<2, 1, false>::smem());
+  f(gemm_q8_umma_kernel<16, 0>, UmmaTile<16, true>::smem());
+  f(gemm_q8_umma_kernel<16, 1>, UmmaTile<16, false>::smem());
+  f(gemm_q8_umma_kernel<16, 2>, UmmaTile<16, false>::smem());
   f(moe_tma_kernel<true, true, 0>, MoeTma<true, true>::smem(MoeTma<true, true>::KMAX));
   f(moe_tma_kernel<true, false, 1>, MoeTma<true, false>::smem(MoeTma<true, false>::KMAX));
   f(moe_tma_kernel<true, false, 2>, MoeTma<true, false>::smem(MoeTma<true, false>::KMAX));
@@ -555,21 +561,11 @@ bool dmalloc(LZRunState* s, T** p, size_t n) {
   return true;
 }
 
-// RoPE table (src/forward_rope.c:178-187, no scaling): freq_i =
-// theta^(-2i/rot), angle = l * freq_i; cos/sin/pow evaluated in double
-// and rounded once.
+// RoPE table (src/forward_rope.c:178-187, no scaling), with the
+// reference's own float pow / cos / sin restated in lz98_rope_table.h.
 void build_rope(const Cfg& c, int seq_len, std::vector<float>& t) {
-  int half = c.rot / 2;
   t.assign((size_t)seq_len * c.rot, 0.0f);
-  for (int i = 0; i < half; i++) {
-    float ex = -2.0f * (float)i / (float)c.rot;
-    float freq = (float)pow((double)c.theta, (double)ex);
-    for (int l = 0; l < seq_len; l++) {
-      float ang = (float)l * freq;
-      t[((size_t)l * half + i) * 2] = (float)cos((double)ang);
-      t[((size_t)l * half + i) * 2 + 1] = (float)sin((double)ang);
-    }
-  }
+  lz98_rope_table(c.theta, c.rot, seq_len, t.data());
 }
 
 float host_rsqrt_body(float x) {         // src/ops_quant.c:126-135
@@ -835,6 +831,16 @@ extern "C" int lz_set_graphs(LZRunState* s, int enable) {
   return 0;
 }
 
+extern "C" int lz_set_umma(LZRunState* s, int enable) {
+  if (!s) return LZ98_ERR_NULL_ARG;
+  if (s->umma != (enable != 0)) {
+    for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
+    s->graph.clear();
+  }
+  s->umma = enable != 0;
+  return 0;
+}
+
 extern "C" int lz_set_pdl(LZRunState* s, int enable) {
   if (!s) return LZ98_ERR_NULL_ARG;
   if (s->pdl != (enable != 0)) {
@@ -1049,6 +1055,45 @@ bool gemm_tma(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int
   return true;
 }
 
+// R > 8 token rows with K (and K2) % 128 == 0 on the tcgen05 kernel: 128
+// weight rows x 16 token rows per CTA.  False when a map cannot be built.
+bool gemm_umma(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, int R, float* y, int ldy, int mode,
+               const QW* w2, const int8_t* xq2, const float* xs2) {
+  if (w.in % 128 || (w2 && w2->in % 128)) return false;
+  const bool rb1 = w.gs == 32;
+  const int GM = rb1 ? 0 : (w.gs == w.in && (!w2 || w2->gs == w2->in)) ? 1 : 2;
+  constexpr int NT = 16;
+  GemmTmaArgs a;
+  memset(&a, 0, sizeof(a));
+  const CUtensorMap* m[8] = {tmap(s, xq, w.in, R, 128, NT), tmap(s, xs, w.in / 32, R, 4, NT),
+                             tmap(s, w.q, w.in, w.out, 128, kUmmaM),
+                             rb1 ? tmap(s, w.s, w.in / 32, w.out, 4, kUmmaM) : nullptr,
+                             nullptr, nullptr, nullptr, nullptr};
+  if (w2) {
+    m[4] = tmap(s, xq2, w2->in, R, 128, NT);
+    m[5] = tmap(s, xs2, w2->in / 32, R, 4, NT);
+    m[6] = tmap(s, w2->q, w2->in, w.out, 128, kUmmaM);
+    m[7] = rb1 ? tmap(s, w2->s, w2->in / 32, w.out, 4, kUmmaM) : nullptr;
+  }
+  for (int i = 0; i < (w2 ? 8 : 4); i++)
+    if (!m[i] && (rb1 || (i & 3) != 3)) return false;
+  a.a = *m[0]; a.x = *m[1]; a.b = *m[2];
+  if (rb1) a.w = *m[3];
+  if (w2) {
+    a.a2 = *m[4]; a.x2 = *m[5]; a.b2 = *m[6];
+    if (rb1) a.w2 = *m[7];
+  }
+  a.ws = w.s; a.ws2 = w2 ? w2->s : nullptr; a.W = w.q; a.W2 = w2 ? w2->q : nullptr;
+  a.y = y; a.err = s->d_err;
+  a.N = w.out; a.K = w.in; a.gs = w.gs; a.K2 = w2 ? w2->in : 0; a.gs2 = w2 ? w2->gs : 32;
+  a.R = R; a.ldy = ldy; a.mode = mode; a.dual = w2 ? 1 : 0;
+  const dim3 grid((w.out + kUmmaM - 1) / kUmmaM, (R + NT - 1) / NT);
+  if (GM == 0) launch(s, gemm_q8_umma_kernel<NT, 0>, grid, dim3(kUmmaThreads), UmmaTile<NT, true>::smem(), a);
+  else if (GM == 1) launch(s, gemm_q8_umma_kernel<NT, 1>, grid, dim3(kUmmaThreads), UmmaTile<NT, false>::smem(), a);
+  else launch(s, gemm_q8_umma_kernel<NT, 2>, grid, dim3(kUmmaThreads), UmmaTile<NT, false>::smem(), a);
+  return true;
+}
+
 // y (R x N, ld ldy) = [y +] W x (+ W2 x2).  With `nin`, x is produced here
 // from the float rows nin->x by RMSNorm + quantisation: inside the GEMV
 // (every block, from shared memory) for R <= kPrologueRows, else by one
@@ -1082,7 +1127,11 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
     s->prof_bytes.push_back(b);
   }
   const bool rb1 = w.gs == 32;
-  if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1) && gemm_tma(s, w, xq, xs, R, y, ldy, mode, w2, xq2, xs2)) {
+  if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1) && s->umma &&
+      gemm_umma(s, w, xq, xs, R, y, ldy, mode, w2, xq2, xs2)) {
+    // launched
+  } else if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1) &&
+             gemm_tma(s, w, xq, xs, R, y, ldy, mode, w2, xq2, xs2)) {
     // launched
   } else if (R > kPrologueRows && (!w2 || (w2->gs == 32) == rb1)) {
     // tensor-core warp tiles of 16 MT token rows x 8 NT outputs (measured
@@ -1838,9 +1887,15 @@ extern "C" int lz_spec_round_temp(const LZModel* m, LZRunState* s, int anchor, i
   return rc;
 }
 
-extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const int* prompt, int n_prompt,
-                              int* out_anchor, char* errbuf, int errlen) {
-  if (!m || !s || !prompt || n_prompt < 1 || seq < 0 || seq >= s->B || n_prompt >= s->seq_len) {
+// Prefill of sequence `seq` with the prompt tokens at body positions
+// start_pos.. (0 for a fresh sequence, the end of a restored prefix for a
+// resumed one, src/generate.c:2841-2900): capture prefill, MTP prefill from
+// the sequence's MTP position, capture forward of the last token and the
+// first anchor.
+static int seq_prefill_impl(const LZModel* m, LZRunState* s, int seq, int start_pos, const int* prompt,
+                            int n_prompt, int* out_anchor, char* errbuf, int errlen) {
+  if (!m || !s || !prompt || n_prompt < 1 || seq < 0 || seq >= s->B || start_pos < 0 ||
+      start_pos + n_prompt >= s->seq_len) {
     set_err(errbuf, errlen, "bad prefill arguments");
     return LZ98_ERR_NULL_ARG;
   }
@@ -1893,7 +1948,7 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
   }
   SeqRound& r = s->h_sr[seq];
   r.anchor = anchor;
-  r.anchor_pos = n_prompt - 1;
+  r.anchor_pos = start_pos + n_prompt - 1;
   r.mtp_pos = mtp_pos;
   r.ssm_slot = slot;
   r.dbg = 0;
@@ -1903,6 +1958,11 @@ extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const in
   }
   if (out_anchor) *out_anchor = anchor;
   return 0;
+}
+
+extern "C" int lz_seq_prefill(const LZModel* m, LZRunState* s, int seq, const int* prompt, int n_prompt,
+                              int* out_anchor, char* errbuf, int errlen) {
+  return seq_prefill_impl(m, s, seq, 0, prompt, n_prompt, out_anchor, errbuf, errlen);
 }
 
 extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* out_tokens, int* out_counts,
@@ -1940,17 +2000,20 @@ extern "C" int lz_spec_round_batch(const LZModel* m, LZRunState* s, int k, int* 
 // 0): greedy at the temperature floor, else coupled temperature rounds with
 // top-p `topp` and the generator seeded by `seed`.  Every token is picked on
 // the device.
-extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
-                              int spec_k, float temp, float topp, uint64_t seed, float p_min, int n_min,
-                              int* out_tok, int out_cap, int* out_n, int* rounds, int round_cap, int* n_rounds,
-                              char* errbuf, int errlen) {
-  if (!m || !s || !prompt || n_prompt < 1 || !out_n || !n_rounds) return LZ98_ERR_NULL_ARG;
-  if (n_prompt >= s->seq_len) {
+// The generation loop of sequence 0 from body position start_pos (0 with
+// a reset state: lz_generate; the end of a restored prefix: the resume
+// path, src/generate.c:2781-2840).
+static int generate_impl(const LZModel* m, LZRunState* s, int start_pos, bool reset, const int* prompt,
+                         int n_prompt, int max_new, int spec_k, float temp, float topp, uint64_t seed, float p_min,
+                         int n_min, int* out_tok, int out_cap, int* out_n, int* rounds, int round_cap,
+                         int* n_rounds, char* errbuf, int errlen) {
+  if (!m || !s || !prompt || n_prompt < 1 || !out_n || !n_rounds || start_pos < 0) return LZ98_ERR_NULL_ARG;
+  if (start_pos + n_prompt >= s->seq_len) {
     set_err(errbuf, errlen, "prompt does not fit the state");
     return LZ98_ERR_NULL_ARG;
   }
   const Cfg& c = m->c;
-  lz_state_reset(s, m);                     // src/generate.c:2813
+  if (reset) lz_state_reset(s, m);          // src/generate.c:2813
   // the reference loop's sampler (oracle-free restatement of its settings,
   // src/generate.c:2790): temperature, top-p, identity penalties, no top-k
   // or min-p, the generator seeded with `seed` (0 taken as 1)
@@ -1963,12 +2026,12 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
   samp.rng_state = seed ? seed : 1ull;
   const bool use_temp = samp.p.temperature > kTempFloor;
   if (int rc = lz_seq_set_sampler(s, 0, samp.p.temperature, topp, samp.rng_state)) return rc;
-  int max_pos = n_prompt + max_new;
+  int max_pos = start_pos + n_prompt + max_new;
   if (max_pos > s->seq_len) max_pos = s->seq_len;
-  if (max_pos < n_prompt + 1) max_pos = n_prompt + 1;
+  if (max_pos < start_pos + n_prompt + 1) max_pos = start_pos + n_prompt + 1;
   int n_out = 0, nr = 0;
   auto emit = [&](int t) { if (n_out < out_cap) out_tok[n_out] = t; n_out++; };
-  int pos = n_prompt - 1, token = prompt[n_prompt - 1];
+  int pos = start_pos + n_prompt - 1, token = prompt[n_prompt - 1];
   // one forward of `token` at `pos` in place (optionally captured into the
   // draft chain), then one token sampled by the sequence's sampler
   auto step = [&](bool capture, int* next) {
@@ -1985,13 +2048,13 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
   // the anchor, as the first loop iteration of the reference does).
   bool have_seed = false, pending = false;
   if (spec_k > 0) {
-    int rc = lz_seq_prefill(m, s, 0, prompt, n_prompt, &token, errbuf, errlen);
+    int rc = seq_prefill_impl(m, s, 0, start_pos, prompt, n_prompt, &token, errbuf, errlen);
     if (rc) return rc;
     emit(token);
     pending = true;
   } else if (n_prompt > 1) {
     std::vector<float> hb((size_t)(n_prompt - 1) * c.d);
-    if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, 0, hb.data())) return LZ98_ERR_FORWARD;
+    if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, start_pos, hb.data())) return LZ98_ERR_FORWARD;
   }
   // the spec loop of lz_generate_call (src/generate.c:2841-3035, rounds by
   // src/generate.c:1900-2100)
@@ -2048,6 +2111,22 @@ extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt
   *out_n = n_out;
   *n_rounds = nr;
   return 0;
+}
+
+extern "C" int lz_generate_ex(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
+                              int spec_k, float temp, float topp, uint64_t seed, float p_min, int n_min,
+                              int* out_tok, int out_cap, int* out_n, int* rounds, int round_cap, int* n_rounds,
+                              char* errbuf, int errlen) {
+  return generate_impl(m, s, 0, true, prompt, n_prompt, max_new, spec_k, temp, topp, seed, p_min, n_min, out_tok,
+                       out_cap, out_n, rounds, round_cap, n_rounds, errbuf, errlen);
+}
+
+extern "C" int lz_generate_resume(const LZModel* m, LZRunState* s, int start_pos, const int* suffix, int n_suffix,
+                                  int max_new, int spec_k, float temp, float topp, uint64_t seed, int* out_tok,
+                                  int out_cap, int* out_n, int* rounds, int round_cap, int* n_rounds, char* errbuf,
+                                  int errlen) {
+  return generate_impl(m, s, start_pos, false, suffix, n_suffix, max_new, spec_k, temp, topp, seed, 0.0f, 0,
+                       out_tok, out_cap, out_n, rounds, round_cap, n_rounds, errbuf, errlen);
 }
 
 extern "C" int lz_generate(const LZModel* m, LZRunState* s, const int* prompt, int n_prompt, int max_new,
@@ -2481,4 +2560,128 @@ extern "C" int lz_ckpt_restore(const LZStateCkpt* ck, LZRunState* s, const LZMod
     return LZ98_ERR_CKPT_SHAPE;
   }
   return lz_ckpt_restore_seq(ck, s, 0, out_pos, errbuf, errlen);
+}
+
+// ============================================================== prefix cache
+//
+// The reference's LZPrefixCache (src/llama_zh.h:781-888,
+// src/generate.c:3209-3390) on token ids: one conversation's reusable
+// prefix as a device checkpoint of the recurrent state plus the token
+// sequence it covers.  The render/tokenizer half of lz_prefix_prepare stays
+// with the caller, who passes the three encodings (whole render, the part
+// before the split, the part after it); the checks and the state work are
+// the reference's, in its order.
+
+struct LZPrefixCache {
+  const LZModel* m = nullptr;
+  LZStateCkpt* ck = nullptr;
+  std::vector<int> tok;   // the covered token prefix
+  int n = 0;              // tokens covered; 0 = nothing cached
+  int have = 0;           // a checkpoint has been saved
+  long n_calls = 0, n_hits = 0, n_tokens_saved = 0, n_mismatch = 0, n_unsplittable = 0;
+};
+
+extern "C" int lz_prefix_init(LZPrefixCache** out, const LZModel* m, char* errbuf, int errlen) {
+  if (!out || !m) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  *out = nullptr;
+  LZPrefixCache* pc = new LZPrefixCache();
+  pc->m = m;
+  if (int rc = lz_ckpt_alloc(&pc->ck, m, errbuf, errlen)) {
+    delete pc;
+    return rc;
+  }
+  *out = pc;
+  return 0;
+}
+
+extern "C" void lz_prefix_free(LZPrefixCache* pc) {
+  if (!pc) return;
+  lz_ckpt_free(pc->ck);
+  delete pc;
+}
+
+extern "C" void lz_prefix_reset(LZPrefixCache* pc) {
+  if (!pc) return;
+  pc->n = 0;
+  pc->have = 0;
+}
+
+extern "C" int lz_prefix_match(const LZPrefixCache* pc, const int* pre, int n_pre) {
+  if (!pc || !pre || n_pre <= 0) return 0;
+  if (!pc->have || pc->n <= 0 || pc->n > n_pre) return 0;
+  if (memcmp(pre, pc->tok.data(), (size_t)pc->n * sizeof(int)) != 0) return 0;
+  return pc->n;
+}
+
+extern "C" int lz_prefix_prepare_tokens(LZPrefixCache* pc, const LZModel* m, LZRunState* s, const int* cur,
+                                        int n_cur, const int* pre, int n_pre, const int* tail, int n_tail,
+                                        int* out_start_pos, int* out_reused, char* errbuf, int errlen) {
+  if (out_start_pos) *out_start_pos = 0;
+  if (out_reused) *out_reused = 0;
+  if (!pc || !m || !s || !cur || n_cur < 0 || (n_pre > 0 && !pre) || (n_tail > 0 && !tail)) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  pc->n_calls++;
+  // nothing to reuse: the full path (not an error)
+  if (n_pre <= 0 || n_tail <= 0) return 0;
+  // check 1: the split is token-exact
+  if (n_cur <= 0 || n_pre + n_tail != n_cur || memcmp(cur, pre, (size_t)n_pre * sizeof(int)) != 0 ||
+      memcmp(cur + n_pre, tail, (size_t)n_tail * sizeof(int)) != 0) {
+    pc->n_unsplittable++;
+    lz_prefix_reset(pc);
+    return 0;
+  }
+  if (n_pre >= s->seq_len) {
+    set_err(errbuf, errlen, "prefix does not fit the state");
+    return LZ98_ERR_NULL_ARG;
+  }
+  // check 2: the cached prefix is a prefix of this render (check 3, the
+  // state not reset since the save, is the checkpoint's epoch test)
+  int base = 0;
+  if (lz_prefix_match(pc, cur, n_pre) > 0) {
+    int p = 0;
+    if (lz_ckpt_restore(pc->ck, s, m, &p, nullptr, 0) == 0 && p == pc->n) {
+      base = pc->n;
+      pc->n_hits++;
+      pc->n_tokens_saved += base;
+    } else {
+      pc->have = 0;   // stale: rebuild from scratch
+    }
+  } else if (pc->have) {
+    pc->n_mismatch++;
+  }
+  if (base == 0) lz_state_reset(s, m);
+  if (n_pre > base && !forward_one(m, s, cur + base, n_pre - base, base, false, nullptr, false)) {
+    // the state is half-forwarded and the cache would describe a prefix
+    // that is not there: both are torn down
+    lz_state_reset(s, m);
+    lz_prefix_reset(pc);
+    set_err(errbuf, errlen, "forward of the prefix failed");
+    return LZ98_ERR_FORWARD;
+  }
+  // cache this render's prefix for the next turn (a failed save only loses
+  // the reuse next time)
+  if (lz_ckpt_save(pc->ck, s, m, n_pre, nullptr, 0) == 0) {
+    pc->tok.assign(cur, cur + n_pre);
+    pc->n = n_pre;
+    pc->have = 1;
+  } else {
+    pc->have = 0;
+  }
+  if (out_start_pos) *out_start_pos = n_pre;
+  if (out_reused) *out_reused = base;
+  return 0;
+}
+
+extern "C" void lz_prefix_stats(const LZPrefixCache* pc, long* calls, long* hits, long* tokens_saved, long* mismatch,
+                                long* unsplittable) {
+  if (calls) *calls = pc ? pc->n_calls : 0;
+  if (hits) *hits = pc ? pc->n_hits : 0;
+  if (tokens_saved) *tokens_saved = pc ? pc->n_tokens_saved : 0;
+  if (mismatch) *mismatch = pc ? pc->n_mismatch : 0;
+  if (unsplittable) *unsplittable = pc ? pc->n_unsplittable : 0;
 }

@@ -75,6 +75,7 @@ def lib():
         "lz_spec_round_batch": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_char_p, c_int]),
         "lz_set_graphs": (c_int, [c_void_p, c_int]),
         "lz_set_pdl": (c_int, [c_void_p, c_int]),
+        "lz_set_umma": (c_int, [c_void_p, c_int]),
         "lz_generate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                 ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
                                 c_char_p, c_int]),
@@ -101,6 +102,17 @@ def lib():
         "lz_ckpt_restore_seq": (c_int, [c_void_p, c_void_p, c_int, P(c_int), c_char_p, c_int]),
         "lz_debug_seq_sum": (c_int, [c_void_p, c_int, c_int, c_float, P(c_float), P(c_int)]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
+        "lz_generate_resume": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                       ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
+                                       c_char_p, c_int]),
+        "lz_prefix_init": (c_int, [P(c_void_p), c_void_p, c_char_p, c_int]),
+        "lz_prefix_free": (None, [c_void_p]),
+        "lz_prefix_reset": (None, [c_void_p]),
+        "lz_prefix_match": (c_int, [c_void_p, c_void_p, c_int]),
+        "lz_prefix_prepare_tokens": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int,
+                                             c_void_p, c_int, P(c_int), P(c_int), c_char_p, c_int]),
+        "lz_prefix_stats": (None, [c_void_p, P(ctypes.c_long), P(ctypes.c_long), P(ctypes.c_long),
+                                   P(ctypes.c_long), P(ctypes.c_long)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -116,10 +128,11 @@ EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_debug_inject_wait_
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
            "lz_state_mtp_verify_hidden", "lz_mtp_draft_step", "lz_mtp_prefill", "lz_mtp_catchup",
            "lz_spec_round", "lz_spec_round_temp", "lz_spec_accept", "lz_spec_accept_temp",
-           "lz_seq_prefill", "lz_seq_set_sampler", "lz_seq_get_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_generate", "lz_state_stream",
+           "lz_seq_prefill", "lz_seq_set_sampler", "lz_seq_get_sampler", "lz_spec_round_batch", "lz_set_graphs", "lz_set_pdl", "lz_set_umma", "lz_generate", "lz_state_stream",
            "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_profile_launches", "lz_lm_head_static", "lz_debug_seq_sum",
            "lz_ckpt_alloc", "lz_ckpt_free", "lz_ckpt_save", "lz_ckpt_restore", "lz_ckpt_save_seq",
-           "lz_ckpt_restore_seq"]
+           "lz_ckpt_restore_seq", "lz_generate_resume", "lz_prefix_init", "lz_prefix_free", "lz_prefix_reset",
+           "lz_prefix_match", "lz_prefix_prepare_tokens", "lz_prefix_stats"]
 
 
 class LZSampleParams(ctypes.Structure):
@@ -247,6 +260,10 @@ class State:
     def graphs(self, on: bool):
         lib().lz_set_graphs(self.h, int(on))
 
+    def umma(self, on: bool):
+        """tcgen05 dense GEMMs for more than 8 token rows (default on)."""
+        lib().lz_set_umma(self.h, 1 if on else 0)
+
     def pdl(self, on: bool):
         lib().lz_set_pdl(self.h, int(on))
 
@@ -346,6 +363,19 @@ class State:
             raise LzError(f"batched round failed ({rc}): {err.value.decode()}", rc)
         return toks, cnt
 
+    def generate_resume(self, start_pos, suffix, max_new, spec_k, temp=0.0, topp=0.95, seed=1):
+        p = np.ascontiguousarray(suffix, np.int32)
+        out = np.zeros(max_new + 16, np.int32)
+        rounds = np.zeros(2 * (max_new + 16), np.int32)
+        on, nr = c_int(), c_int()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_generate_resume(self.m.h, self.h, start_pos, _ptr(p), len(p), max_new, spec_k, temp, topp,
+                                      seed, _ptr(out), len(out), ctypes.byref(on), _ptr(rounds), len(rounds) // 2,
+                                      ctypes.byref(nr), err, 256)
+        if rc:
+            raise LzError(f"generate resume failed ({rc}): {err.value.decode()}", rc)
+        return out[:on.value].copy(), rounds[:2 * nr.value].reshape(-1, 2).copy()
+
     def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
         p = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max_new + 16, np.int32)
@@ -395,6 +425,43 @@ class Checkpoint:
 
 DEBUG_COUNTERS = ("lz_debug_us_verify", "lz_debug_us_draft", "lz_debug_us_capture", "lz_debug_us_catchup",
                   "lz_debug_n_capture", "lz_debug_n_catchup", "lz_debug_n_ring_rollback")
+
+
+class PrefixCache:
+    """LZPrefixCache on token ids (one conversation's reusable prefix)."""
+
+    def __init__(self, model: "Model"):
+        self.m = model
+        self.h = c_void_p()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_prefix_init(ctypes.byref(self.h), model.h, err, 256)
+        if rc:
+            raise LzError(f"prefix init failed ({rc}): {err.value.decode()}", rc)
+
+    def close(self):
+        if self.h:
+            lib().lz_prefix_free(self.h)
+            self.h = None
+
+    def match(self, pre):
+        p = np.ascontiguousarray(pre, np.int32)
+        return lib().lz_prefix_match(self.h, _ptr(p), len(p))
+
+    def prepare(self, state: "State", cur, pre, tail):
+        """Returns (start_pos, reused)."""
+        c, p, t = (np.ascontiguousarray(a, np.int32) for a in (cur, pre, tail))
+        sp, ru = c_int(), c_int()
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_prefix_prepare_tokens(self.h, self.m.h, state.h, _ptr(c), len(c), _ptr(p), len(p), _ptr(t),
+                                            len(t), ctypes.byref(sp), ctypes.byref(ru), err, 256)
+        if rc:
+            raise LzError(f"prefix prepare failed ({rc}): {err.value.decode()}", rc)
+        return sp.value, ru.value
+
+    def stats(self):
+        v = [ctypes.c_long() for _ in range(5)]
+        lib().lz_prefix_stats(self.h, *[ctypes.byref(x) for x in v])
+        return dict(zip(("calls", "hits", "tokens_saved", "mismatch", "unsplittable"), (x.value for x in v)))
 
 
 def debug_counters():

@@ -75,4 +75,7 @@ float lzo_random_f32(unsigned long long *state);
    [v0, v0 + nv) of the tied lm_head. */
 int lzo_lm_head_cols(const LzoModel *m, const float *hidden, int n, int v0, int nv, float *out);
 
+/* The RoPE table [seq_len][rot/2][cos, sin] of the MTP attention. */
+void lzo_rope_table(float theta, int rot, int seq_len, float *out);
+
 #endif

@@ -40,6 +40,16 @@ typedef struct {
    default. */
 static int rd_dbg_break_rollback = 0, rd_dbg_skip_catchup = 0;
 
+/* The state's RoPE table (s->rope_cs, [seq_len][rot/2][cos, sin], built by
+   lz_rope_build_table, src/forward_rope.c:178-187) into out. */
+int rd_rope_table(void *vh, float *out, int n) {
+    RdHandle *h = (RdHandle *)vh;
+    int need = h->s.seq_len * h->m.config.rotary_dim;
+    if (!h->s.rope_cs || n < need) return -1;
+    memcpy(out, h->s.rope_cs, sizeof(float) * (size_t)need);
+    return need;
+}
+
 void rd_set_round_debug(int break_rollback, int skip_catchup) {
     rd_dbg_break_rollback = break_rollback;
     rd_dbg_skip_catchup = skip_catchup;

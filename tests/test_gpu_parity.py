@@ -1,8 +1,7 @@
 """GPU parity of the CUDA path (through the C ABI) against the golden
-vectors of the reference engine and against the C restatement.  Integer
-and float work is bit-exact except the draft logits against the
-reference itself (RoPE table, relative tolerance 1e-5; the CUDA path and
-the oracle share the table and agree bit for bit)."""
+vectors of the reference engine and against the C restatement: integer
+and float work bit-exact, draft logits included (the MTP RoPE table is
+built with the reference's own float pow / cos / sin)."""
 import os
 
 import numpy as np
@@ -65,8 +64,7 @@ def test_capture_and_draft(gcase):
         lgd = s.mtp_draft(int(t), len(p) - 1 + i)
         lgo = O.mtp_draft(int(t), len(p) - 1 + i)
         assert bits_equal(lgd, lgo), f"draft step {i} differs from the oracle"
-        ref = g["draft_logits"][i]
-        assert np.abs(lgd - ref).max() / np.abs(ref).max() < 1e-5
+        assert bits_equal(lgd, g["draft_logits"][i]), f"draft step {i} differs from the reference"
     assert bits_equal(s.chain(), O.chain())
     s.close()
     O.close()
@@ -290,3 +288,37 @@ def test_headline_config_token_identical():
     finally:
         s.close()
         m.close()
+
+
+def test_umma_and_mma_sync_gemms_agree(gcase):
+    """The dense GEMMs of more than 8 token rows run on tcgen05 (default) or
+    on the warp-level mma.sync kernel: the prompt capture (up to 39 rows)
+    and 40-sequence rounds (120 verify rows, 40 draft rows, 80 catch-up
+    rows) give the same bits either way, greedy and at temperature 0.8."""
+    import lz98
+    name, d, g, m = gcase
+    p = g["prompt"]
+    hs = []
+    for on in (True, False):
+        s = lz98.State(m, 512, 4)
+        s.umma(on)
+        hs.append(s.batch_capture(p[:-1], 0))
+        s.close()
+    assert bits_equal(hs[0], hs[1]) and bits_equal(hs[0], g["prefill_hidden"])
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, m.vocab, 9 + (b * 5) % 11).astype(np.int32) for b in range(40)]
+    for temp in (0.0, 0.8):
+        streams = []
+        for on in (True, False):
+            s = lz98.State(m, 256, 4, n_seq=40)
+            s.umma(on)
+            out = []
+            for b in range(40):
+                s.set_sampler(b, temp, 0.95, 500 + b)
+                out.append(s.seq_prefill(b, prompts[b]))
+            for _ in range(4):
+                toks, cnt = s.round_batch(2)
+                out.append((toks.tolist(), cnt.tolist()))
+            streams.append(out)
+            s.close()
+        assert streams[0] == streams[1], temp

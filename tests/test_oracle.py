@@ -60,12 +60,36 @@ def test_oracle_draft_matches_golden(case):
     O.set_chain(hc[0])
     for i, t in enumerate(g["draft_tokens"]):
         lg = O.mtp_draft(int(t), len(p) - 1 + i)
-        ref = g["draft_logits"][i]
-        # the MTP RoPE table is the one documented difference (double-
-        # precision cos/sin/pow against the reference's all-float ports)
-        rel = np.abs(lg - ref).max() / np.abs(ref).max()
-        assert rel < 1e-5, rel
-        assert int(np.argmax(lg)) == int(np.argmax(ref))
+        # bit-exact: the MTP RoPE table is built with the reference's own
+        # all-float pow / cos / sin (lz98_rope_table.h)
+        assert bits_equal(lg, g["draft_logits"][i]), f"draft step {i}"
+    O.close()
+
+
+@pytest.mark.skipif(not reference_available(), reason="oracle/_ref not built")
+def test_rope_table_matches_reference():
+    """The restated RoPE table (llama98-zh_b200/csrc/lz98_rope_table.h, used
+    by the library and the oracle) equals the reference's own rope_cs bit for
+    bit over 4096 positions, including the angles above 120 radians that take
+    the 192-bit reduction."""
+    import ctypes
+    from conftest import model_dir
+    d = model_dir("midi")
+    R = Reference(d, 4096, 4)
+    R.L.rd_rope_table.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    O = Oracle(d, 16, 4)
+    O.L.lzo_rope_table.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    n = 4096 * 64
+    ref = np.zeros(n, np.float32)
+    got = R.L.rd_rope_table(ctypes.c_void_p(R.h), ref.ctypes.data_as(ctypes.c_void_p), n)
+    assert got > 0
+    rot = got // 4096
+    import lz98_synth
+    theta = lz98_synth.CONFIGS["midi"].rope_theta
+    ours = np.zeros(got, np.float32)
+    O.L.lzo_rope_table(theta, rot, 4096, ours.ctypes.data_as(ctypes.c_void_p))
+    assert bits_equal(ours, ref[:got])
+    R.close()
     O.close()
 
 
