@@ -220,9 +220,9 @@ int lz_set_graphs(LZRunState *s, int enable);
    each kernel lets the next one start its prologue - weight prefetch -
    while it finishes; 0 launches them plainly serialised. */
 int lz_set_pdl(LZRunState *s, int enable);
-/* (no counterpart in the reference) Dense int8 GEMMs of more than 8 token
-   rows on the 5th-generation tensor cores (tcgen05.mma kind::i8 into tensor
-   memory, the default); 0 selects the warp-level mma.sync kernel.  Both
+/* (no counterpart in the reference) 1: dense int8 GEMMs of more than 8
+   token rows on the 5th-generation tensor cores (tcgen05.mma kind::i8 into
+   tensor memory); 0 (the default): the warp-level mma.sync kernel.  Both
    give the same bits. */
 int lz_set_umma(LZRunState *s, int enable);
 /* Whole generation on token ids (the reference's lz_generate_call spec

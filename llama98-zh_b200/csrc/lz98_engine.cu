@@ -463,7 +463,7 @@ struct LZRunState {
   long long launches = 0;
   bool graphs = true;
   bool pdl = true;                   // programmatic dependent launch
-  bool umma = true;                  // R > 8 dense GEMMs on tcgen05 (else the mma.sync TMA kernel)
+  bool umma = false;                 // R > 8 dense GEMMs on tcgen05 (else the mma.sync TMA kernel)
   // optional per-GEMV timing (lz_profile_round): event pairs and bytes
   bool prof = false;
   std::vector<cudaEvent_t> prof_ev;

@@ -99,11 +99,32 @@ LZ_HD void tmem_ld_4x8(uint32_t taddr, uint32_t step, int (&v)[4][8]) {
       : "memory");
 }
 
+// Two-lane float arithmetic of the epilogue: with LZ98_PACKED_F32X2 = 1
+// the packed f32x2 operations, else the scalar __fadd_rn / __fmul_rn lane
+// by lane (the default).
+#ifndef LZ98_PACKED_F32X2
+#define LZ98_PACKED_F32X2 0
+#endif
+LZ_HD float2 add2(float2 a, float2 b) {
+#if LZ98_PACKED_F32X2
+  return __fadd2_rn(a, b);
+#else
+  return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+#endif
+}
+LZ_HD float2 mul2(float2 a, float2 b) {
+#if LZ98_PACKED_F32X2
+  return __fmul2_rn(a, b);
+#else
+  return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+#endif
+}
+
 // Exact int32 -> float of two sub-block sums (|v| < 2^22: the 1.5 2^23
 // magic add, then the magic subtracted; x - c and x + (-c) round alike).
 LZ_HD float2 i2f_small2(int v0, int v1) {
-  return __fadd2_rn(make_float2(__int_as_float(0x4B400000 + v0), __int_as_float(0x4B400000 + v1)),
-                    make_float2(-12582912.0f, -12582912.0f));
+  return add2(make_float2(__int_as_float(0x4B400000 + v0), __int_as_float(0x4B400000 + v1)),
+              make_float2(-12582912.0f, -12582912.0f));
 }
 
 // Stage layout of the UMMA GEMM with NT token rows per CTA.
@@ -290,14 +311,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 2) gemm_q8_umma_kernel(const __g
           const float2 xs2 = (j & 1) ? make_float2(xv[2 * cp].y, xv[2 * cp + 1].y)
                                      : make_float2(xv[2 * cp].x, xv[2 * cp + 1].x);
           if (!RB1) {
-            st.a[0][cp] = __fadd2_rn(st.a[0][cp], __fmul2_rn(a, xs2));
+            st.a[0][cp] = add2(st.a[0][cp], mul2(a, xs2));
             if (gend) {
-              st.a[1][cp] = __fadd2_rn(st.a[1][cp], __fmul2_rn(st.a[0][cp], wg2));
+              st.a[1][cp] = add2(st.a[1][cp], mul2(st.a[0][cp], wg2));
               st.a[0][cp] = zero2;
             }
           } else {
             // K % 128 == 0: the interleaved accumulator of sub-block s is s & 3 == j
-            st.a[j][cp] = __fadd2_rn(st.a[j][cp], __fmul2_rn(a, __fmul2_rn(xs2, wg2)));
+            st.a[j][cp] = add2(st.a[j][cp], mul2(a, mul2(xs2, wg2)));
           }
         }
       }
@@ -305,9 +326,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 2) gemm_q8_umma_kernel(const __g
         // a product ends: its value per token (the second is added to the first)
 #pragma unroll
         for (int cp = 0; cp < 4; cp++) {
-          const float2 r = RB1 ? __fadd2_rn(__fadd2_rn(st.a[0][cp], st.a[2][cp]), __fadd2_rn(st.a[1][cp], st.a[3][cp]))
+          const float2 r = RB1 ? add2(add2(st.a[0][cp], st.a[2][cp]), add2(st.a[1][cp], st.a[3][cp]))
                                : st.a[1][cp];
-          v[cp] = it == it1 - 1 ? r : __fadd2_rn(v[cp], r);
+          v[cp] = it == it1 - 1 ? r : add2(v[cp], r);
         }
       }
     }

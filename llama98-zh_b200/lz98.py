@@ -261,7 +261,7 @@ class State:
         lib().lz_set_graphs(self.h, int(on))
 
     def umma(self, on: bool):
-        """tcgen05 dense GEMMs for more than 8 token rows (default on)."""
+        """tcgen05 dense GEMMs for more than 8 token rows (default off: the mma.sync kernel)."""
         lib().lz_set_umma(self.h, 1 if on else 0)
 
     def pdl(self, on: bool):
