@@ -249,6 +249,24 @@ int lz_generate_resume(const LZModel *m, LZRunState *s, int start_pos, const int
                        int out_cap, int *out_n, int *rounds, int round_cap, int *n_rounds, char *errbuf,
                        int errlen);
 
+/* ---- expert parallelism (no counterpart in the reference, which runs one
+   process on one CPU).  The routed experts of every MoE layer are split
+   over `world` ranks, one process per GPU: rank r computes experts
+   [r E/world, (r+1) E/world) for the pairs of every rank, each rank keeps
+   its own sequences.  Per layer the (token, expert) pairs go to their
+   expert's owner and the expert outputs come back (NCCL send/recv over
+   NVLink, the library bound at run time); the combine keeps the
+   reference's selection order, so results are those of one GPU bit for
+   bit.  Rank 0 makes the id with lz_ep_unique_id and the caller hands it
+   to every rank; every rank then calls lz_ep_init together (collective).
+   Every rank must then run the same sequence of forwards (the same
+   rounds, prefills of the same lengths): each layer exchanges with every
+   peer.  Expert-parallel rounds run eagerly, without graph capture.  A
+   stream that does not drain within 60 s aborts the communicator and the
+   call returns LZ98_ERR_CUDA.  world <= 8, E divisible by world. */
+int lz_ep_unique_id(uint8_t *out128, char *errbuf, int errlen);
+int lz_ep_init(LZRunState *s, const uint8_t *id128, int rank, int world, char *errbuf, int errlen);
+
 /* ---- prefix reuse: replaces LZPrefixCache, lz_prefix_init / _free /
    _reset / _match / _prepare / _stats (src/llama_zh.h:781-888,
    src/generate.c:3209-3390) on token ids.  The cache holds a device

@@ -35,7 +35,7 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if force or needs_build():
         nvcc = os.environ.get("NVCC", "nvcc")
-        cmd = [nvcc, *NVCC_FLAGS, "-o", SO + ".tmp", *SRCS, "-lcudart"]
+        cmd = [nvcc, *NVCC_FLAGS, "-o", SO + ".tmp", *SRCS, "-lcudart", "-ldl"]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)

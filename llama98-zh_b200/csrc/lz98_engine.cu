@@ -5,6 +5,9 @@
 // declared in include/lz98_gpu.h.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>   // types only: the functions are bound at run time (nccl_api)
+#include <unistd.h>
 
 #include <cmath>
 #include <cstdio>
@@ -24,6 +27,7 @@
 #include "lz98_sample.cuh"
 #include "lz98_umma.cuh"
 #include "lz98_rope_table.h"
+#include "lz98_ep.cuh"
 
 using namespace lz98;
 
@@ -285,7 +289,7 @@ extern "C" int lz_open(LZModel** out, const char* dir, char* errbuf, int errlen)
   ok = ok && c.fkdr == 0 && c.ne > 0 && c.ne <= 256 && c.topk <= 16 && c.mtp_layers == 1 &&
        !c.lat_norm && c.has_lb && c.sigm && c.renorm && c.kd == 64 && c.vd == 64 &&
        c.nk == c.nv && c.hd == 64 && c.conv_k == 4 && c.d % 32 == 0 && c.rank % 32 == 0 &&
-       c.rank <= 256 && c.latent <= 1024 && c.latent % 32 == 0 && c.moe_ffn % 32 == 0 &&
+       c.rank <= 128 && c.latent <= 1024 && c.latent % 32 == 0 && c.moe_ffn % 32 == 0 &&
        c.shared_w % 32 == 0 && 2 * c.d <= 4096 && c.moe_ffn <= 2048 && c.val_dim <= 4096;
   if (!ok) {
     set_err(errbuf, errlen, "unsupported KunMoe configuration (needs all-KDA layers, latent MoE with "
@@ -420,6 +424,63 @@ extern "C" void lz_model_info(const LZModel* m, int* o) {
 
 extern "C" size_t lz_model_weight_bytes(const LZModel* m) { return m ? m->wbytes : 0; }
 
+// ======================================================================= NCCL
+//
+// Expert parallelism exchanges pairs with NCCL send/recv.  The library is
+// bound at run time: the NCCL a host process already loaded (a PyTorch
+// process has one) is reused, else libnccl.so.2 is opened; nothing links
+// against it, so one-GPU use needs no NCCL at all.
+namespace {
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*);
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+  ncclResult_t (*comm_abort)(ncclComm_t);
+  ncclResult_t (*group_start)();
+  ncclResult_t (*group_end)();
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+  const char* (*error_string)(ncclResult_t);
+};
+
+const NcclApi* nccl_api() {
+  static std::once_flag once;
+  static NcclApi api;
+  static bool ok = false;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return;
+    auto take = [h](auto& fn, const char* name) {
+      void* p = dlsym(h, name);
+      memcpy(&fn, &p, sizeof p);
+      return p != nullptr;
+    };
+    ok = take(api.get_unique_id, "ncclGetUniqueId") && take(api.comm_init_rank, "ncclCommInitRank") &&
+         take(api.comm_destroy, "ncclCommDestroy") && take(api.comm_abort, "ncclCommAbort") &&
+         take(api.group_start, "ncclGroupStart") && take(api.group_end, "ncclGroupEnd") &&
+         take(api.send, "ncclSend") && take(api.recv, "ncclRecv") && take(api.error_string, "ncclGetErrorString");
+  });
+  return ok ? &api : nullptr;
+}
+
+// Expert-parallel context of a run state (lz_ep_init): communicator, the
+// owned expert range, the slot buffers and the per-layer scratch.
+struct EpCtx {
+  int world = 1, rank = 0, epr = 0, e0 = 0;
+  ncclComm_t comm = nullptr;
+  EpBuf buf{};
+  int *pair_dest = nullptr, *pair_slot = nullptr;       // per local pair: owner, slot
+  int *expert = nullptr, *src = nullptr, *slot = nullptr, *total = nullptr;   // per received pair
+  int *list = nullptr, *ntiles = nullptr;
+  MoeTile* tiles = nullptr;
+  int8_t *latq = nullptr, *hq = nullptr;
+  float *lats = nullptr, *hs = nullptr, *h2 = nullptr, *sendback = nullptr, *recvback = nullptr;
+  bool failed = false;                                   // an exchange failed or timed out
+};
+constexpr double kEpTimeoutS = 60.0;   // a stream of an expert-parallel state that has not drained by then is aborted
+}  // namespace
+
 // ====================================================================== state
 
 struct LZRunState {
@@ -434,7 +495,7 @@ struct LZRunState {
   size_t q_slot = 0, q_seq = 0, conv_slot = 0, conv_seq = 0, cache_seq = 0;
   float attn_scale = 0, ssm_scale = 0;
   // scratch
-  float *x, *inproj, *conv_out, *gate, *moein, *h2, *shout, *hidden, *logits, *qkv, *mtpx, *hb;
+  float *x, *inproj, *moein, *h2, *shout, *hidden, *logits, *qkv, *mtpx, *hb;
   int8_t *xq, *oq, *latq, *hq, *yq, *shq, *aq;
   float *xs, *os, *lats, *hs, *ys, *shs, *as;
   int *pair_e, *tok, *catch_tok, *catch_hidx;
@@ -489,6 +550,7 @@ struct LZRunState {
   int* h_err = nullptr;
   int* d_err = nullptr;
   float* pconf = nullptr;            // confidence of a p_min draft step
+  EpCtx ep;                          // expert parallelism (lz_ep_init)
   bool dbg_timing = false;           // events around the parts of a round
   cudaEvent_t dbg_ev[4] = {nullptr, nullptr, nullptr, nullptr};
 };
@@ -496,8 +558,29 @@ struct LZRunState {
 // Wait for the state's stream; false on a CUDA error or when a kernel
 // reported a wait that gave up (the error word stays set until the state
 // is freed: the run state is then not trustworthy).
-static bool sync_ok(const LZRunState* s) {
-  return cudaStreamSynchronize(s->st) == cudaSuccess && !(s->h_err && *(volatile int*)s->h_err);
+static bool sync_ok(const LZRunState* cs) {
+  LZRunState* s = const_cast<LZRunState*>(cs);
+  if (s->ep.comm) {
+    // an expert-parallel stream waits on its peers: poll it with a deadline
+    // and abort the communicator (its kernels then return) if it passes
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      const cudaError_t q = cudaStreamQuery(s->st);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) return false;
+      if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kEpTimeoutS) {
+        if (const NcclApi* n = nccl_api()) n->comm_abort(s->ep.comm);
+        s->ep.comm = nullptr;
+        s->ep.failed = true;
+        return false;
+      }
+      usleep(20);
+    }
+    if (s->ep.failed) return false;
+  } else if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+    return false;
+  }
+  return !(s->h_err && *(volatile int*)s->h_err);
 }
 
 namespace {
@@ -600,6 +683,11 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
   s->depth = spec_k_max + 1;              // src/forward_state.c:738-744
   s->kmax = spec_k_max;
   s->Rmax = std::max(64, n_seq * (spec_k_max + 1));
+  if ((long)s->Rmax * m->c.topk > 1024L * kMoeGroupPer) {
+    set_err(errbuf, errlen, "too many sequences for one forward (rows x top-k above the expert grouping's limit)");
+    delete s;
+    return LZ98_ERR_SIZE;
+  }
   if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
     delete s;
     set_err(errbuf, errlen, "cudaStreamCreate failed");
@@ -627,7 +715,6 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->ks, s->cache_seq * B / 32) && dmalloc(s, &s->vs, s->cache_seq * B / 32) &&
             dmalloc(s, &s->chain, B * c.d) && dmalloc(s, &s->rope, (size_t)seq_len * c.rot) &&
             dmalloc(s, &s->x, R * c.d) && dmalloc(s, &s->inproj, R * nwide) &&
-            dmalloc(s, &s->conv_out, R * c.conv_dim) && dmalloc(s, &s->gate, R * c.nv * c.kd) &&
             dmalloc(s, &s->moein, R * m->n_moe) && dmalloc(s, &s->h2, P * c.latent) &&
             dmalloc(s, &s->shout, R * c.d) && dmalloc(s, &s->hidden, R * c.d) &&
             dmalloc(s, &s->logits, R * (size_t)c.vocab) && dmalloc(s, &s->qkv, R * m->n_qkv) &&
@@ -724,6 +811,14 @@ extern "C" int lz_state_alloc_batch(LZRunState** out, const LZModel* m, int n_se
 
 extern "C" void lz_state_free(LZRunState* s) {
   if (!s) return;
+  if (s->ep.comm) {
+    const bool drained = sync_ok(s);    // aborts the communicator itself when the stream does not drain
+    if (const NcclApi* n = nccl_api()) {
+      if (drained && s->ep.comm) n->comm_destroy(s->ep.comm);
+      else if (s->ep.comm) n->comm_abort(s->ep.comm);
+    }
+    s->ep.comm = nullptr;
+  }
   for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_err) cudaFreeHost(s->h_err);
@@ -827,7 +922,7 @@ extern "C" void* lz_state_stream(LZRunState* s) { return s ? (void*)s->st : null
 extern "C" long long lz_state_launches(const LZRunState* s) { return s ? s->launches : 0; }
 extern "C" int lz_set_graphs(LZRunState* s, int enable) {
   if (!s) return LZ98_ERR_NULL_ARG;
-  s->graphs = enable != 0;
+  s->graphs = enable != 0 && !s->ep.comm;   // expert-parallel rounds run eagerly
   return 0;
 }
 
@@ -954,29 +1049,41 @@ bool moe_tma_fits(const Cfg& c) {
          c.moe_ffn <= MoeTma<true, true>::KMAX;
 }
 
-bool moe_tma(LZRunState* s, bool w13, const int8_t* wq, const float* wsc, int gs, int tmax) {
+// Operands of the grouped expert kernels: the pairs (expert per pair,
+// relative to the first expert e0 of ne), the grouping scratch, the
+// activation rows (pair p reads latent row p / topk) and the outputs.
+struct MoeIO {
+  const int* pair_e; int P, topk, ne, e0;
+  int* list; MoeTile* tiles; int* ntiles;
+  const int8_t* latq; const float* lats;
+  int8_t* hq; float* hs; float* h2;
+};
+
+bool moe_tma(LZRunState* s, bool w13, const int8_t* wq0, const float* wsc0, int gs, int tmax, const MoeIO& io) {
   const Cfg& c = s->m->c;
   const int K = w13 ? c.latent : c.moe_ffn, rows_e = w13 ? 2 * c.moe_ffn : c.latent;
   const int chunk = 128;   // j values (w13) or latent outputs (w2) per block
   if (!moe_tma_fits(c)) return false;
   const bool rb1 = gs == 32;
   const int GM = rb1 ? 0 : gs == K ? 1 : 2;
+  const int8_t* wq = wq0 + (size_t)io.e0 * rows_e * K;
+  const float* wsc = wsc0 + (size_t)io.e0 * rows_e * (K / gs);
   MoeTmaArgs a;
   memset(&a, 0, sizeof(a));
-  const CUtensorMap* mq = tmap(s, wq, K, c.ne * rows_e, 128, 128);
-  const CUtensorMap* ms = rb1 ? tmap(s, wsc, K / 32, c.ne * rows_e, 4, 128) : nullptr;
+  const CUtensorMap* mq = tmap(s, wq, K, io.ne * rows_e, 128, 128);
+  const CUtensorMap* ms = rb1 ? tmap(s, wsc, K / 32, io.ne * rows_e, 4, 128) : nullptr;
   if (!mq || (rb1 && !ms)) return false;
   a.wq = *mq;
   if (rb1) a.wsc = *ms;
-  a.ws = wsc; a.list = s->glist; a.tiles = s->gtiles; a.ntiles = s->gntiles;
-  a.xq = w13 ? s->latq : s->hq; a.xs = w13 ? s->lats : s->hs;
-  a.hq = s->hq; a.hs = s->hs; a.h2 = s->h2; a.err = s->d_err;
-  a.K = K; a.gs = gs; a.rows_e = rows_e; a.ffn = c.moe_ffn; a.latent = c.latent; a.topk = c.topk;
+  a.ws = wsc; a.list = io.list; a.tiles = io.tiles; a.ntiles = io.ntiles;
+  a.xq = w13 ? io.latq : io.hq; a.xs = w13 ? io.lats : io.hs;
+  a.hq = io.hq; a.hs = io.hs; a.h2 = io.h2; a.err = s->d_err;
+  a.K = K; a.gs = gs; a.rows_e = rows_e; a.ffn = c.moe_ffn; a.latent = c.latent; a.topk = io.topk;
   const dim3 grid((w13 ? c.moe_ffn : c.latent) / chunk, tmax);
   if (s->prof) {
     // algorithmic bytes with every expert touched (R >= 4 E / top_k makes
     // an untouched expert unlikely): int8 weights + their scales
-    const double rows = (double)c.ne * rows_e;
+    const double rows = (double)io.ne * rows_e;
     s->prof_moe_bytes.push_back(rows * K + rows * (K / gs) * 4.0);
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
@@ -1173,74 +1280,126 @@ void argmax(LZRunState* s, const float* logits, int R, int p1_mode) {
   launch(s, argmax_kernel, dim3((V + kArgmaxChunk - 1) / kArgmaxChunk, R), dim3(256), 0, logits, V, p1_mode, s->vmax);
 }
 
+// The routed experts of io's pairs (src/forward_moe.c:55-206): pairs
+// bucketed by expert into tiles of 8 pairs (TMA-staged kernels) or 16
+// (warp-tile kernels), w1/w3 with SiLU x up and the per-32 quantisation,
+// then w2 into io.h2 (one latent row per pair).
+void grouped_experts(LZRunState* s, const DLayer& L, const MoeIO& io) {
+  const Cfg& c = s->m->c;
+  const int trows = moe_tma_fits(c) ? kMoeTileRows : 16;
+  const int tmax = io.P / trows + std::min(io.ne, io.P) + 1;
+  launch(s, moe_group_kernel, dim3(1), dim3(1024), 0, io.pair_e, io.P, io.ne, io.list, io.tiles, io.ntiles, trows);
+  const int8_t* w13q = L.w13q + (size_t)io.e0 * 2 * c.moe_ffn * c.latent;
+  const float* w13s = L.w13s + (size_t)io.e0 * 2 * c.moe_ffn * (c.latent / L.w13_gs);
+  const int8_t* w2q = L.w2q + (size_t)io.e0 * c.latent * c.moe_ffn;
+  const float* w2s = L.w2s + (size_t)io.e0 * c.latent * (c.moe_ffn / L.w2_gs);
+  if (moe_tma(s, true, L.w13q, L.w13s, L.w13_gs, tmax, io)) {
+    // launched
+  } else if (L.w13_gs == 32)
+    launch(s, moe_w13_group_kernel<true>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, w13q, w13s, c.moe_ffn,
+           c.latent, L.w13_gs, io.list, io.tiles, io.ntiles, io.topk, io.latq, io.lats, io.hq, io.hs);
+  else
+    launch(s, moe_w13_group_kernel<false>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, w13q, w13s, c.moe_ffn,
+           c.latent, L.w13_gs, io.list, io.tiles, io.ntiles, io.topk, io.latq, io.lats, io.hq, io.hs);
+  if (moe_tma(s, false, L.w2q, L.w2s, L.w2_gs, tmax, io)) {
+    // launched
+  } else if (L.w2_gs == 32)
+    launch(s, moe_w2_group_kernel<true>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, w2q, w2s, c.moe_ffn,
+           c.latent, L.w2_gs, io.list, io.tiles, io.ntiles, io.hq, io.hs, io.h2);
+  else
+    launch(s, moe_w2_group_kernel<false>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, w2q, w2s, c.moe_ffn,
+           c.latent, L.w2_gs, io.list, io.tiles, io.ntiles, io.hq, io.hs, io.h2);
+}
+
+// One exchange of equal-size per-peer blocks with every other rank (NCCL
+// send/recv in one group, on the state's stream).
+void ep_exchange(LZRunState* s, const void* send, void* recv, size_t bytes) {
+  const NcclApi* n = nccl_api();
+  EpCtx& E = s->ep;
+  if (!n || !E.comm) {
+    E.failed = true;
+    return;
+  }
+  bool ok = n->group_start() == ncclSuccess;
+  for (int p = 0; p < E.world && ok; p++) {
+    if (p == E.rank) continue;
+    ok = n->send(static_cast<const uint8_t*>(send) + (size_t)p * bytes, bytes, ncclUint8, p, E.comm, s->st) ==
+             ncclSuccess &&
+         n->recv(static_cast<uint8_t*>(recv) + (size_t)p * bytes, bytes, ncclUint8, p, E.comm, s->st) == ncclSuccess;
+  }
+  if (n->group_end() != ncclSuccess || !ok) E.failed = true;
+}
+
+// Expert-parallel MoE of one layer (lz98_ep.cuh): pack the pairs by owner,
+// exchange, the owned experts over every rank's pairs, return the rows,
+// combine in selection order.
+void moe_ep(LZRunState* s, const DLayer& L, int R) {
+  const Cfg& c = s->m->c;
+  EpCtx& E = s->ep;
+  const int P = R * c.topk;
+  const EpBuf b = E.buf;
+  launch(s, ep_pack_kernel, dim3(1), dim3(1024), 0, s->pair_e, P, c.topk, E.epr, s->latq, s->lats, b, E.pair_dest,
+         E.pair_slot);
+  ep_exchange(s, b.send, b.recv, b.buf_bytes);
+  launch(s, ep_unpack_kernel, dim3(1), dim3(1024), 0, b, E.latq, E.lats, E.expert, E.src, E.slot, E.total);
+  const MoeIO io{E.expert, b.world * b.cap, 1, E.epr, E.e0, E.list, E.tiles, E.ntiles, E.latq, E.lats, E.hq, E.hs,
+                 E.h2};
+  grouped_experts(s, L, io);
+  launch(s, ep_reply_kernel, dim3(b.world * b.cap), dim3(128), 0, E.h2, E.src, E.slot, E.total, c.latent, b.cap,
+         b.rank, E.sendback, E.recvback);
+  ep_exchange(s, E.sendback, E.recvback, (size_t)b.cap * c.latent * sizeof(float));
+  launch(s, ep_combine_kernel, dim3(R), dim3(256), 0, s->pair_e, s->pair_w, E.pair_dest, E.pair_slot, c.topk,
+         E.recvback, b.cap, c.latent, s->yq, s->ys);
+}
+
 // Body forward of R rows (src/forward.c:1210-1617): embed, per layer
 // pre-norm -> KDA -> residual -> post-norm -> latent MoE -> residual, then
 // final norm (hidden capture) and the tied lm_head over every row.
 void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
   const LZModel* m = s->m;
   const Cfg& c = m->c;
-  const int d = c.d, kdim = c.key_dim, vdim = c.val_dim, nvk = c.nv * c.kd;
+  const int d = c.d, kdim = c.key_dim, vdim = c.val_dim;
   launch(s, embed_kernel, dim3(R), dim3(256), 0, m->embed.q, m->embed.s, m->embed.gs, d, s->tok, s->x);
   for (int l = 0; l < c.nl; l++) {
     const DLayer& L = m->L[l];
     const InNorm in_ln{s->x, L.in_ln, nullptr, nullptr};
     gemv(s, L.inproj, s->xq, s->xs, R, s->inproj, m->n_in, 0, nullptr, nullptr, nullptr, &in_ln);
-    KdaPreArgs pa{s->inproj, m->n_in, c.conv_dim, L.conv_w, s->seqs,
-                  s->conv + (size_t)l * c.conv_dim * 3, s->conv_seq, s->conv_slot, s->depth, adv, s->conv_out,
-                  m->off_fa, c.rank, L.fb.q, L.fb.s, L.fb.gs, L.a_log, L.dt_bias, c.lb, nvk, c.kd, s->gate,
-                  (c.conv_dim + 255) / 256, (nvk + 255) / 256, nseq};
-    launch(s, kda_pre_kernel, dim3(pa.nconv_x * nseq + pa.nfb_x * R), dim3(256), 0, pa);
+    KdaArgs ka{s->inproj, m->n_in, kdim, m->off_g, m->off_fa, m->off_b, c.rank, L.conv_w,
+               s->conv + (size_t)l * c.conv_dim * 3, s->conv_seq, s->conv_slot, L.fb.q, L.fb.s, L.fb.gs, L.a_log,
+               L.dt_bias, c.lb, s->seqs, s->hi, s->lo, s->sc, s->q_seq, s->q_slot,
+               (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv, s->ssm_scale, L.o_norm, c.eps, vdim, s->oq,
+               s->os};
     // few (head, sequence) blocks (batch 1): 16 warps per block halve the
     // per-token requantisation pass; otherwise 8 warps, 4 blocks per SM
     if (c.nv * nseq <= s->n_sm / 2)
-      launch(s, kda_recur_kernel<2 * kRecurThreads>, dim3(c.nv, nseq), dim3(2 * kRecurThreads), 0,
-             s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
-             s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
-             s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
+      launch(s, kda_recur_kernel<2 * kRecurThreads>, dim3(c.nv, nseq), dim3(2 * kRecurThreads), 0, ka);
     else
-      launch(s, kda_recur_kernel<kRecurThreads>, dim3(c.nv, nseq), dim3(kRecurThreads), 0,
-             s->conv_out, c.conv_dim, kdim, s->inproj, m->n_in, m->off_b, m->off_g, s->gate, nvk, s->seqs,
-             s->hi, s->lo, s->sc, s->q_seq, s->q_slot, (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv,
-             s->ssm_scale, L.o_norm, c.eps, vdim, s->oq, s->os);
+      launch(s, kda_recur_kernel<kRecurThreads>, dim3(c.nv, nseq), dim3(kRecurThreads), 0, ka);
     gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);
     const InNorm post{s->x, L.post_ln, nullptr, nullptr};
     gemv(s, L.moein, s->xq, s->xs, R, s->moein, m->n_moe, 0, nullptr, nullptr, nullptr, &post);
-    launch(s, moe_route_kernel, dim3(R), dim3(512), 0, s->moein, m->n_moe, m->off_router, m->off_down, L.router_bias,
-                                           c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats,
-                                           m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
     const int P = R * c.topk;
-    if (R > kPrologueRows && P <= 2048) {
-      // grouped experts: pairs bucketed by expert into tiles of 8 pairs
-      // (TMA-staged kernels) or 16 (warp-tile kernels)
-      const int trows = moe_tma_fits(c) ? kMoeTileRows : 16;
-      const int tmax = P / trows + std::min(c.ne, P) + 1;
-      launch(s, moe_group_kernel, dim3(1), dim3(1024), 0, s->pair_e, P, c.ne, s->glist, s->gtiles, s->gntiles, trows);
-      if (moe_tma(s, true, L.w13q, L.w13s, L.w13_gs, tmax)) {
-        // launched
-      } else if (L.w13_gs == 32)
-        launch(s, moe_w13_group_kernel<true>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
-               c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
-               s->hs);
-      else
-        launch(s, moe_w13_group_kernel<false>, dim3((c.moe_ffn + 127) / 128, tmax), dim3(128), 0, L.w13q, L.w13s,
-               c.moe_ffn, c.latent, L.w13_gs, s->glist, s->gtiles, s->gntiles, c.topk, s->latq, s->lats, s->hq,
-               s->hs);
-      if (moe_tma(s, false, L.w2q, L.w2s, L.w2_gs, tmax)) {
-        // launched
-      } else if (L.w2_gs == 32)
-        launch(s, moe_w2_group_kernel<true>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, L.w2q, L.w2s,
-               c.moe_ffn, c.latent, L.w2_gs, s->glist, s->gtiles, s->gntiles, s->hq, s->hs, s->h2);
-      else
-        launch(s, moe_w2_group_kernel<false>, dim3((c.latent + 63) / 64, tmax), dim3(128), 0, L.w2q, L.w2s,
-               c.moe_ffn, c.latent, L.w2_gs, s->glist, s->gtiles, s->gntiles, s->hq, s->hs, s->h2);
-      launch(s, moe_combine_kernel, dim3(R), dim3(256), 0, s->pair_e, s->pair_w, c.topk, s->h2, c.latent, s->yq,
-             s->ys);
+    if (R <= kPrologueRows && !s->ep.comm) {
+      // few rows: router fused into the per-pair w1/w3 kernel, then w2 with
+      // the last-block combine
+      launch(s, moe_route_w13_kernel, dim3(c.moe_ffn / 32, P), dim3(256), 0, s->moein, m->n_moe, m->off_router,
+             m->off_down, L.router_bias, c.ne, c.topk, L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e,
+             s->pair_w, s->hq, s->hs, m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
+      launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, P), dim3(256), 0, L.w2q, L.w2s, c.moe_ffn, c.latent,
+             L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2, s->row_counter, s->yq, s->ys);
     } else {
-      launch(s, moe_w13_kernel, dim3(c.moe_ffn / 32, R * c.topk), dim3(256), 0, 
-          L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e, c.topk, s->latq, s->lats, s->hq, s->hs);
-      launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, R * c.topk), dim3(256), 0, 
-          L.w2q, L.w2s, c.moe_ffn, c.latent, L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2,
-          s->row_counter, s->yq, s->ys);
+      launch(s, moe_route_kernel, dim3(R), dim3(512), 0, s->moein, m->n_moe, m->off_router, m->off_down,
+             L.router_bias, c.ne, c.topk, c.latent, s->pair_e, s->pair_w, s->latq, s->lats, m->off_shg, m->off_shu,
+             c.shared_w, s->shq, s->shs);
+      if (s->ep.comm) {
+        moe_ep(s, L, R);
+      } else {
+        const MoeIO io{s->pair_e, P, c.topk, c.ne, 0, s->glist, s->gtiles, s->gntiles, s->latq, s->lats,
+                       s->hq, s->hs, s->h2};
+        grouped_experts(s, L, io);
+        launch(s, moe_combine_kernel, dim3(R), dim3(256), 0, s->pair_e, s->pair_w, c.topk, s->h2, c.latent, s->yq,
+               s->ys);
+      }
     }
     if (c.shared_w) gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1, &L.sh_down, s->shq, s->shs);
     else gemv(s, L.up, s->yq, s->ys, R, s->x, d, 1);
@@ -2560,6 +2719,93 @@ extern "C" int lz_ckpt_restore(const LZStateCkpt* ck, LZRunState* s, const LZMod
     return LZ98_ERR_CKPT_SHAPE;
   }
   return lz_ckpt_restore_seq(ck, s, 0, out_pos, errbuf, errlen);
+}
+
+// ====================================================== expert parallelism
+
+extern "C" int lz_ep_unique_id(uint8_t* out, char* errbuf, int errlen) {
+  if (!out) {
+    set_err(errbuf, errlen, "null argument");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const NcclApi* n = nccl_api();
+  if (!n) {
+    set_err(errbuf, errlen, "NCCL (libnccl.so.2) not loadable");
+    return LZ98_ERR_CUDA;
+  }
+  ncclUniqueId id;
+  const ncclResult_t r = n->get_unique_id(&id);
+  if (r != ncclSuccess) {
+    set_err(errbuf, errlen, "ncclGetUniqueId: %s", n->error_string(r));
+    return LZ98_ERR_CUDA;
+  }
+  memcpy(out, &id, sizeof id);
+  return 0;
+}
+
+extern "C" int lz_ep_init(LZRunState* s, const uint8_t* id, int rank, int world, char* errbuf, int errlen) {
+  if (!s || !id || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world) {
+    set_err(errbuf, errlen, "bad expert-parallel arguments (1 <= world <= 8, 0 <= rank < world)");
+    return LZ98_ERR_NULL_ARG;
+  }
+  const Cfg& c = s->m->c;
+  if (s->ep.comm) {
+    set_err(errbuf, errlen, "expert parallelism is already set up on this state");
+    return LZ98_ERR_NULL_ARG;
+  }
+  if (c.ne % world) {
+    set_err(errbuf, errlen, "the expert count does not split evenly over the ranks");
+    return LZ98_ERR_SIZE;
+  }
+  const int cap = s->Rmax * c.topk;           // pairs of one rank's forward at most
+  if ((long)world * cap > 1024L * kMoeGroupPer) {
+    set_err(errbuf, errlen, "too many pairs per layer for the expert-parallel grouping (world x rows x top-k)");
+    return LZ98_ERR_SIZE;
+  }
+  const NcclApi* n = nccl_api();
+  if (!n) {
+    set_err(errbuf, errlen, "NCCL (libnccl.so.2) not loadable");
+    return LZ98_ERR_CUDA;
+  }
+  EpCtx& E = s->ep;
+  E.world = world;
+  E.rank = rank;
+  E.epr = c.ne / world;
+  E.e0 = rank * E.epr;
+  E.buf.world = world;
+  E.buf.rank = rank;
+  E.buf.cap = cap;
+  E.buf.latent = c.latent;
+  E.buf.slot_bytes = ((size_t)c.latent + (size_t)c.latent / 32 * 4 + 8 + 15) & ~(size_t)15;
+  E.buf.buf_bytes = 16 + (size_t)cap * E.buf.slot_bytes;
+  const size_t W = world, Pr = (size_t)world * cap;
+  bool ok = dmalloc(s, &E.buf.send, W * E.buf.buf_bytes) && dmalloc(s, &E.buf.recv, W * E.buf.buf_bytes) &&
+            dmalloc(s, &E.pair_dest, cap) && dmalloc(s, &E.pair_slot, cap) && dmalloc(s, &E.expert, Pr) &&
+            dmalloc(s, &E.src, Pr) && dmalloc(s, &E.slot, Pr) && dmalloc(s, &E.total, 1) && dmalloc(s, &E.list, Pr) &&
+            dmalloc(s, &E.ntiles, 1) && dmalloc(s, &E.tiles, Pr + E.epr + 1) && dmalloc(s, &E.latq, Pr * c.latent) &&
+            dmalloc(s, &E.lats, Pr * c.latent / 32) && dmalloc(s, &E.hq, Pr * c.moe_ffn) &&
+            dmalloc(s, &E.hs, Pr * c.moe_ffn / 32) && dmalloc(s, &E.h2, Pr * c.latent) &&
+            dmalloc(s, &E.sendback, Pr * c.latent) && dmalloc(s, &E.recvback, Pr * c.latent);
+  if (!ok || cudaDeviceSynchronize() != cudaSuccess) {
+    E = EpCtx{};
+    set_err(errbuf, errlen, "device allocation failed");
+    return LZ98_ERR_ALLOC;
+  }
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof uid);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = n->comm_init_rank(&comm, world, uid, rank);   // every rank calls this together
+  if (r != ncclSuccess) {
+    E = EpCtx{};
+    set_err(errbuf, errlen, "ncclCommInitRank: %s", n->error_string(r));
+    return LZ98_ERR_CUDA;
+  }
+  E.comm = comm;
+  // the exchanges run eagerly (no graph capture)
+  for (auto& kv : s->graph) cudaGraphExecDestroy(kv.second);
+  s->graph.clear();
+  s->graphs = false;
+  return 0;
 }
 
 // ============================================================== prefix cache

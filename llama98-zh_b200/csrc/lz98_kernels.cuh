@@ -1014,101 +1014,43 @@ struct KdaSeq {            // one sequence's rows inside a forward batch
   int row0, nrows, base_slot, seq;
 };
 
-// Both pre-recurrence steps in one grid: blocks [0, nconv) run the conv1d
-// of (sequence, 256-channel slice) and the rest the f_b_proj/decay gate of
-// (token row, 256-output slice).  Same arithmetic as the two kernels above.
-struct KdaPreArgs {
-  const float* inproj; int ldi; int conv_dim; const float* cw; const KdaSeq* seqs;
-  float* conv_state; size_t seq_stride, slot_stride; int depth, adv; float* conv_out;
-  int off_fa, rank; const int8_t* fbq; const float* fbs; int fb_gs; const float* a_log;
-  const float* dt_bias; float lb; int nvk, kd; float* gate; int nconv_x, nfb_x, nseq;
+// Arguments of the KDA layer kernel (one layer, every sequence of the
+// forward batch).
+struct KdaArgs {
+  const float* inproj; int ldi;            // [R][n_in]: q | k | v | g | f_a | b (the fused in-projection)
+  int kdim, off_g, off_fa, off_b, rank;
+  const float* cw;                         // conv1d weights [conv_dim][4]
+  float* conv_state;                       // this layer's [conv_dim][3] of ring slot 0, sequence 0
+  size_t conv_seq_stride, conv_slot_stride;
+  const int8_t* fbq; const float* fbs; int fb_gs;   // f_b [nv 64][rank] Q8_0
+  const float* a_log; const float* dt_bias; float lb;
+  const KdaSeq* seqs;
+  int8_t* st_hi; int8_t* st_lo; float* st_sc;       // two-plane state ring
+  size_t seq_stride_q, slot_stride_q; int layer_off_q;
+  int depth, adv; float ssm_scale;
+  const float* o_norm; float eps; int vdim;
+  int8_t* oq; float* os;                   // quantised gated-norm output [R][vdim]
 };
 
-__global__ void __launch_bounds__(256) kda_pre_kernel(const KdaPreArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ __align__(16) int8_t lq[256];
-  __shared__ float ls[8];
-  const int nconv = a.nconv_x * a.nseq;
-  if ((int)blockIdx.x < nconv) {
-    const KdaSeq sq = a.seqs[blockIdx.x / a.nconv_x];
-    const int c = (blockIdx.x % a.nconv_x) * 256 + threadIdx.x;
-    if (c >= a.conv_dim) return;
-    float* st0 = a.conv_state + (size_t)sq.seq * a.seq_stride + (size_t)c * 3;
-    const float* st = st0 + (size_t)sq.base_slot * a.slot_stride;
-    float h0 = st[0], h1 = st[1], h2 = st[2];
-    const float4 w = __ldg(reinterpret_cast<const float4*>(a.cw) + c);
-    for (int t = 0; t < sq.nrows; t++) {
-      const int r = sq.row0 + t;
-      const float xv = a.inproj[(size_t)r * a.ldi + c];
-      float sum = 0.0f;
-      sum = __fadd_rn(sum, __fmul_rn(w.x, h0));
-      sum = __fadd_rn(sum, __fmul_rn(w.y, h1));
-      sum = __fadd_rn(sum, __fmul_rn(w.z, h2));
-      sum = __fadd_rn(sum, __fmul_rn(w.w, xv));
-      a.conv_out[(size_t)r * a.conv_dim + c] = silu(sum);
-      h0 = h1; h1 = h2; h2 = xv;
-      if (a.adv) {
-        float* d = st0 + (size_t)((sq.base_slot + t + 1) % a.depth) * a.slot_stride;
-        d[0] = h0; d[1] = h1; d[2] = h2;
-      }
-    }
-    if (!a.adv) {
-      float* d = st0 + (size_t)sq.base_slot * a.slot_stride;
-      d[0] = h0; d[1] = h1; d[2] = h2;
-    }
-    return;
-  }
-  const int b2 = blockIdx.x - nconv;
-  const int r = b2 / a.nfb_x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int g = warp; g < a.rank / 32; g += nw) {
-    const float v = a.inproj[(size_t)r * a.ldi + a.off_fa + g * 32 + lane];
-    lq[g * 32 + lane] = warp_quant32(v, &ls[g]);
-  }
-  __syncthreads();
-  const int j = (b2 % a.nfb_x) * 256 + threadIdx.x;
-  if (j >= a.nvk) return;
-  const int nsb = a.rank / 32, rb = a.fb_gs / 32, ng = a.rank / a.fb_gs;
-  __align__(16) float p[8];
-  const int8_t* wr = a.fbq + (size_t)j * a.rank;
-  const float* wsr = a.fbs + (size_t)j * ng;
-  int4 wa[8], wb[8];
-#pragma unroll
-  for (int q = 0; q < 8; q++)
-    if (q < nsb) {
-      wa[q] = __ldg(reinterpret_cast<const int4*>(wr + q * 32));
-      wb[q] = __ldg(reinterpret_cast<const int4*>(wr + q * 32 + 16));
-    }
-  const float dtb = __ldg(a.dt_bias + j), alg = __ldg(a.a_log + j / a.kd);
-#pragma unroll
-  for (int q = 0; q < 8; q++)
-    if (q < nsb) {
-      const int4 xa = *reinterpret_cast<const int4*>(lq + q * 32);
-      const int4 xb = *reinterpret_cast<const int4*>(lq + q * 32 + 16);
-      const float av = (float)dot32(wa[q], wb[q], xa, xb);
-      p[q] = rb > 1 ? __fmul_rn(av, ls[q]) : __fmul_rn(av, __fmul_rn(ls[q], wsr[q]));
-    }
-  const float pre = __fadd_rn(q8_reduce(p, wsr, rb, ng), dtb);
-  const float decay = exp_body(alg);
-  const float g = __fmul_rn(a.lb, sigmoid(__fmul_rn(decay, pre)));
-  a.gate[(size_t)r * a.nvk + j] = exp_body(g);
-}
-
-// The KDA recurrence of one (sequence, head) with the 64x64 two-plane int8
-// state resident in shared memory.  Everything that does not read the
-// state runs for a batch of up to kRecurTB tokens at once: l2norm(q) *
-// kd^-1/2, l2norm(k), beta = sigmoid(b); then per token, serially, pass 1
-// (u = S^T(g.k) and w = S^T(g.q), each a sequential sum over the 64 state
-// rows, one thread per output column forming its products in order; kq =
-// k.q on another thread), the head output w + u*kq with u = (v - u)*beta,
-// and pass 2 (each state row g*S + k*u requantised in two planes, four
-// 32-wide groups per warp at a time); finally the gated RMSNorm and per-32
-// quantisation of every token's output.  src/forward_kda.c:856-936 and
-// 1029-1040, src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340,
-// src/ops_norm.c:749-842.
+// The KDA layer of one (sequence, head): the short conv1d of the head's 192
+// channels (q, k, v) with the conv ring history (src/ops_conv1d.c:26-60),
+// the decay gate of its 64 keys from the f_b projection
+// (src/forward_kda.c:277-404), then the recurrence with the 64x64 two-plane
+// int8 state resident in shared memory.  Everything that does not read the
+// state runs for a batch of up to kRecurTB tokens at once: the conv (one
+// thread per channel, tokens in order, the history in registers), the f_a
+// quantisation and the gate, l2norm(q) * kd^-1/2, l2norm(k), beta =
+// sigmoid(b); then per token, serially, pass 1 (u = S^T(g.k) and w =
+// S^T(g.q), each a sequential sum over the 64 state rows, one thread per
+// output column forming its products in order; kq = k.q on another
+// thread), the head output w + u*kq with u = (v - u)*beta, and pass 2 (each
+// state row g*S + k*u requantised in two planes, four 32-wide groups per
+// warp at a time); finally the gated RMSNorm and per-32 quantisation of
+// every token's output.  src/forward_kda.c:856-936 and 1029-1040,
+// src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
 constexpr int kRecurThreads = 256;
 constexpr int kRecurTB = 4;
+constexpr int kRankMax = 128;
 
 // One two-plane requantisation of a 32-wide state group held one element
 // per lane (src/ops_gdn.c:1191-1340): hi = q8 of buf, residual rounded
@@ -1129,18 +1071,8 @@ LZ_HD void requant_2p(float buf, float iv, int8_t& h8, int8_t& l8, float& e) {
 }
 
 template <int NTH>
-__global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2)
-kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
-                 const float* __restrict__ inproj, int ldi, int off_b, int off_g,
-                 const float* __restrict__ gate, int nvk,
-                 const KdaSeq* __restrict__ seqs,
-                 int8_t* st_hi, int8_t* st_lo, float* st_sc,
-                 size_t seq_stride_q, size_t slot_stride_q, int layer_off_q,
-                 int depth, int adv, float ssm_scale,
-                 const float* __restrict__ o_norm, float eps, int vdim,
-                 int8_t* oq, float* os) {
+__global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(const KdaArgs a) {
   pdl_trigger();
-  pdl_wait();
   constexpr int KD = 64, VD = 64, TB = kRecurTB, NW = NTH / 32;
   __shared__ __align__(16) int8_t hi[KD][VD];
   __shared__ __align__(16) int8_t lo[KD][VD];
@@ -1152,18 +1084,51 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   // each requantisation; per-token scale products of the two passes
   __shared__ __align__(16) float E[KD][VD];
   __shared__ float SCX[2][KD][2], SCG[KD][2];
-  const KdaSeq sq = seqs[blockIdx.y];
+  // the batch's raw conv inputs and f_a rows, and the quantised f_a
+  __shared__ __align__(16) float RAW[TB][3 * KD];
+  __shared__ __align__(16) float FA[TB][kRankMax];
+  __shared__ __align__(16) int8_t LQ[TB][kRankMax];
+  __shared__ float LS[TB][kRankMax / 32];
+  // this head's f_b rows and their scales
+  __shared__ __align__(16) int8_t FB[KD][kRankMax];
+  __shared__ float FBS[KD][kRankMax / 32];
   const int h = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const size_t head_off = (size_t)layer_off_q + (size_t)h * KD * VD;
-  const size_t seq_off = (size_t)sq.seq * seq_stride_q;
+  const int nsb = a.rank / 32, rbf = a.fb_gs / 32, ngf = a.rank / a.fb_gs;
+  // weights do not change during a round: loaded before the wait on the
+  // producing kernel
+  for (int q = tid; q < KD * nsb * 2; q += NTH) {
+    const int j = q / (nsb * 2), c16 = q - j * nsb * 2;
+    reinterpret_cast<int4*>(&FB[j][0])[c16] =
+        __ldg(reinterpret_cast<const int4*>(a.fbq + (size_t)(h * KD + j) * a.rank) + c16);
+  }
+  for (int q = tid; q < KD * ngf; q += NTH) {
+    const int j = q / ngf, u = q - j * ngf;
+    FBS[j][u] = __ldg(a.fbs + (size_t)(h * KD + j) * ngf + u);
+  }
+  const float decay = exp_body(__ldg(a.a_log + h));   // exp(A_log) of the head (src/forward_kda.c:277-404)
+  const float dtb = __ldg(a.dt_bias + h * KD + (tid & 63));
+  const int part = tid >> 6, ci = tid & 63;            // conv channel of threads 0..191: q, k, v of this head
+  const int chan = part == 0 ? h * KD + ci : part == 1 ? a.kdim + h * KD + ci : 2 * a.kdim + h * VD + ci;
+  float4 cwv = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < 3 * KD) cwv = __ldg(reinterpret_cast<const float4*>(a.cw) + chan);
+  pdl_wait();
+  const KdaSeq sq = a.seqs[blockIdx.y];
+  const size_t head_off = (size_t)a.layer_off_q + (size_t)h * KD * VD;
+  const size_t seq_off = (size_t)sq.seq * a.seq_stride_q;
+  float* cst0 = a.conv_state + (size_t)sq.seq * a.conv_seq_stride + (size_t)chan * 3;
+  float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
+  if (tid < 3 * KD) {
+    const float* st = cst0 + (size_t)sq.base_slot * a.conv_slot_stride;
+    c0 = st[0]; c1 = st[1]; c2 = st[2];
+  }
   {
-    const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
+    const size_t off = seq_off + (size_t)sq.base_slot * a.slot_stride_q + head_off;
     if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(st_hi + off)[tid];
-      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(st_lo + off)[tid];
+      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(a.st_hi + off)[tid];
+      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(a.st_lo + off)[tid];
     }
-    if (tid < KD * 2) (&sc[0][0])[tid] = st_sc[off / 32 + tid];
+    if (tid < KD * 2) (&sc[0][0])[tid] = a.st_sc[off / 32 + tid];
   }
   __syncthreads();
   for (int q = tid; q < KD * VD; q += NTH) {
@@ -1172,15 +1137,65 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
   }
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
-    // stage the batch (raw q, k in qn/kn until normalised)
-    for (int q = tid; q < nt * 64; q += NTH) {
+    // stage the batch's raw rows: conv channels, g, f_a
+    for (int q = tid; q < nt * 3 * KD; q += NTH) {
+      const int t = q / (3 * KD), c = q - t * (3 * KD), pp = c >> 6, cc = c & 63;
+      const int ch = pp == 0 ? h * KD + cc : pp == 1 ? a.kdim + h * KD + cc : 2 * a.kdim + h * VD + cc;
+      RAW[t][c] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + ch];
+    }
+    for (int q = tid; q < nt * VD; q += NTH) {
       const int t = q >> 6, i = q & 63;
-      const size_t r = (size_t)(sq.row0 + t0 + t);
-      qn[t][i] = conv_out[r * ldc + h * KD + i];
-      kn[t][i] = conv_out[r * ldc + kdim + h * KD + i];
-      vcs[t][i] = conv_out[r * ldc + 2 * kdim + h * VD + i];
-      zs[t][i] = inproj[r * ldi + off_g + h * VD + i];
-      gv[t][i] = gate[r * nvk + h * KD + i];
+      zs[t][i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_g + h * VD + i];
+    }
+    for (int q = tid; q < nt * a.rank; q += NTH) {
+      const int t = q / a.rank, i = q - t * a.rank;
+      FA[t][i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_fa + i];
+    }
+    __syncthreads();
+    // the conv1d of the batch (src/ops_conv1d.c:26-60), then SiLU
+    if (tid < 3 * KD) {
+      float* dst = part == 0 ? &qn[0][0] : part == 1 ? &kn[0][0] : &vcs[0][0];
+      for (int t = 0; t < nt; t++) {
+        const float xv = RAW[t][tid];
+        float sum = 0.0f;
+        sum = __fadd_rn(sum, __fmul_rn(cwv.x, c0));
+        sum = __fadd_rn(sum, __fmul_rn(cwv.y, c1));
+        sum = __fadd_rn(sum, __fmul_rn(cwv.z, c2));
+        sum = __fadd_rn(sum, __fmul_rn(cwv.w, xv));
+        dst[t * KD + ci] = silu(sum);
+        c0 = c1; c1 = c2; c2 = xv;
+        if (a.adv) {
+          float* d = cst0 + (size_t)((sq.base_slot + t0 + t + 1) % a.depth) * a.conv_slot_stride;
+          d[0] = c0; d[1] = c1; d[2] = c2;
+        }
+      }
+    }
+    // the f_a rows quantised per 32 (src/ops_quant.c:2152-2282), by the
+    // warps above the conv's
+    for (int g = NW - 1 - warp; g < nt * nsb; g += NW) {
+      const int t = g / nsb, gg = g - t * nsb;
+      LQ[t][gg * 32 + lane] = warp_quant32(FA[t][gg * 32 + lane], &LS[t][gg]);
+    }
+    __syncthreads();
+    // the decay gate of this head's 64 keys: exp(lb sigmoid(exp(A) (f_b(f_a) + dt)))
+    static_assert(NTH >= TB * KD, "one gate per thread");
+    if (tid < nt * KD) {
+      const int t = tid >> 6, jj = tid & 63;
+      const float* wsr = FBS[jj];
+      __align__(16) float p[kRankMax / 32];
+#pragma unroll
+      for (int u = 0; u < kRankMax / 32; u++)
+        if (u < nsb) {
+          const int4 wa = *reinterpret_cast<const int4*>(&FB[jj][u * 32]);
+          const int4 wb = *reinterpret_cast<const int4*>(&FB[jj][u * 32 + 16]);
+          const int4 xa = *reinterpret_cast<const int4*>(&LQ[t][u * 32]);
+          const int4 xb = *reinterpret_cast<const int4*>(&LQ[t][u * 32 + 16]);
+          const float av = (float)dot32(wa, wb, xa, xb);
+          p[u] = rbf > 1 ? __fmul_rn(av, LS[t][u]) : __fmul_rn(av, __fmul_rn(LS[t][u], wsr[u]));
+        }
+      const float pre = __fadd_rn(q8_reduce(p, wsr, rbf, ngf), dtb);
+      const float gg = __fmul_rn(a.lb, sigmoid(__fmul_rn(decay, pre)));
+      gv[t][jj] = exp_body(gg);
     }
     __syncthreads();
     {                                          // 3 nt independent chains, two per warp
@@ -1189,14 +1204,14 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
         const int t = c % nt, which = c / nt;
         if (which == 0) inv_q[t] = rsqrt_body(__fadd_rn(seq_sumsq(qn[t], KD), kL2Eps));
         else if (which == 1) inv_k[t] = rsqrt_body(__fadd_rn(seq_sumsq(kn[t], KD), kL2Eps));
-        else beta[t] = sigmoid(inproj[(size_t)(sq.row0 + t0 + t) * ldi + off_b + h]);
+        else beta[t] = sigmoid(a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_b + h]);
       }
     }
     static_assert(2 * (NTH / 32) >= 3 * kRecurTB, "chains per batch exceed the warps");
     __syncthreads();
     for (int q = tid; q < nt * 64; q += NTH) {
       const int t = q >> 6, i = q & 63;
-      qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), ssm_scale);
+      qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), a.ssm_scale);
       kn[t][i] = __fmul_rn(kn[t][i], inv_k[t]);
     }
     __syncthreads();
@@ -1264,45 +1279,99 @@ kda_recur_kernel(const float* __restrict__ conv_out, int ldc, int kdim,
         }
       }
       __syncthreads();
-      if (adv) {
-        const int so = (sq.base_slot + t0 + t + 1) % depth;
-        const size_t off = seq_off + (size_t)so * slot_stride_q + head_off;
+      if (a.adv) {
+        const int so = (sq.base_slot + t0 + t + 1) % a.depth;
+        const size_t off = seq_off + (size_t)so * a.slot_stride_q + head_off;
         if (tid < KD * VD / 16) {
-          reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-          reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+          reinterpret_cast<int4*>(a.st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+          reinterpret_cast<int4*>(a.st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
         }
-        if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+        if (tid < KD * 2) a.st_sc[off / 32 + tid] = (&sc[0][0])[tid];
       }
     }
     // gated RMSNorm of every token's head output, then per-32 quantisation
     if (lane == 0 && warp < nt)
-      inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), eps));
+      inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), a.eps));
     __syncthreads();
     for (int q = tid; q < nt * 64; q += NTH) {
       const int t = q >> 6, i = q & 63;
       const size_t r = (size_t)(sq.row0 + t0 + t);
-      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), o_norm[i]), silu(zs[t][i]));
-      oq[r * vdim + h * VD + i] = warp_quant32(o, &os[r * (vdim / 32) + (h * VD) / 32 + (i >> 5)]);
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), a.o_norm[i]), silu(zs[t][i]));
+      a.oq[r * a.vdim + h * VD + i] = warp_quant32(o, &a.os[r * (a.vdim / 32) + (h * VD) / 32 + (i >> 5)]);
     }
     __syncthreads();
   }
-  if (!adv) {
-    const size_t off = seq_off + (size_t)sq.base_slot * slot_stride_q + head_off;
+  if (!a.adv) {
+    const size_t off = seq_off + (size_t)sq.base_slot * a.slot_stride_q + head_off;
     if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-      reinterpret_cast<int4*>(st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+      reinterpret_cast<int4*>(a.st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
+      reinterpret_cast<int4*>(a.st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
     }
-    if (tid < KD * 2) st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+    if (tid < KD * 2) a.st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+    if (tid < 3 * KD) {
+      float* d = cst0 + (size_t)sq.base_slot * a.conv_slot_stride;
+      d[0] = c0; d[1] = c1; d[2] = c2;
+    }
   }
 }
 
 // ---------------------------------------------------------------- MoE
 
-// Router of one token row: sigmoid scores, key = score + bias, top-k by key
-// (first index on ties), weights = scores renormalised by their sequential
-// sum in selection order (src/ops_moe.c:12-163), by warp 0; then the per-32
-// quantisation of the row's latent (src/forward_moe.c:150) by all warps.
-// E <= 256.
+// Router of one token row, run by one warp (src/ops_moe.c:12-163): sigmoid
+// scores, key = score + bias, top-k by key (first index on ties), weights =
+// the scores renormalised by their sequential sum in selection order.
+// Every lane returns the experts (-1: none left) and weights in sel_e /
+// sel_w[0..topk).  E <= 256, topk <= 16.
+LZ_HD void route_row(const float* __restrict__ logits, const float* __restrict__ bias, int E, int topk,
+                     int* sel_e, float* sel_w) {
+  const int lane = threadIdx.x & 31;
+  float score[8], key[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = lane + 32 * j;
+    if (e < E) {
+      score[j] = sigmoid(logits[e]);
+      key[j] = __fadd_rn(score[j], bias[e]);
+    } else {
+      score[j] = 0.0f;
+      key[j] = -1e30f;
+    }
+  }
+  float wsum = 0.0f;
+  for (int t = 0; t < topk; t++) {
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int e = lane + 32 * j;
+      if (e < E && key[j] > -1e30f) {
+        const unsigned long long kk = ((unsigned long long)fkey(key[j]) << 32) | (0xFFFFFFFFu - (uint32_t)e);
+        best = kk > best ? kk : best;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      best = b2 > best ? b2 : best;
+    }
+    const int bi = best ? argmax_index(best) : -1;
+    float sw = 0.0f;
+    if (bi >= 0 && (bi & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (j == (bi >> 5)) { sw = score[j]; key[j] = -1e30f; }
+    }
+    sw = __shfl_sync(0xffffffffu, sw, bi >= 0 ? (bi & 31) : 0);
+    wsum = __fadd_rn(wsum, bi >= 0 ? sw : 0.0f);
+    sel_e[t] = bi;
+    sel_w[t] = bi >= 0 ? sw : 0.0f;
+  }
+  for (int t = 0; t < topk; t++)
+    if (wsum > 0.0f && sel_e[t] >= 0) sel_w[t] = __fdiv_rn(sel_w[t], wsum);
+}
+
+// Router of one token row (route_row, warp 0) into pair_expert / pair_w;
+// then the per-32 quantisation of the row's latent (src/forward_moe.c:150)
+// and of the shared expert's silu(gate) * up (src/forward_moe.c:484-536)
+// by all warps.  The path for more than 8 token rows.
 __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
                                  const float* __restrict__ bias, int E, int topk, int latent,
                                  int* pair_expert, float* pair_w, int8_t* latq, float* lats,
@@ -1311,53 +1380,17 @@ __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int o
   pdl_wait();
   const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) {
-    float score[8], key[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int e = lane + 32 * j;
-      if (e < E) {
-        score[j] = sigmoid(moein[(size_t)r * ldm + off_router + e]);
-        key[j] = __fadd_rn(score[j], bias[e]);
-      } else {
-        score[j] = 0.0f;
-        key[j] = -1e30f;
-      }
-    }
-    float wsum = 0.0f;
-    for (int t = 0; t < topk; t++) {
-      unsigned long long best = 0ull;
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int e = lane + 32 * j;
-        if (e < E && key[j] > -1e30f) {
-          const unsigned long long kk = ((unsigned long long)fkey(key[j]) << 32) | (0xFFFFFFFFu - (uint32_t)e);
-          best = kk > best ? kk : best;
+    int se[16];
+    float sw_[16];
+    route_row(moein + (size_t)r * ldm + off_router, bias, E, topk, se, sw_);
+    if (lane < topk) {
+      for (int t = 0; t < 16; t++)
+        if (t == lane) {
+          pair_expert[r * topk + t] = se[t];
+          pair_w[r * topk + t] = sw_[t];
         }
-      }
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
-        best = b2 > best ? b2 : best;
-      }
-      const int bi = best ? argmax_index(best) : -1;
-      float sw = 0.0f;
-      if (bi >= 0 && (bi & 31) == lane) {
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-          if (j == (bi >> 5)) { sw = score[j]; key[j] = -1e30f; }
-      }
-      sw = __shfl_sync(0xffffffffu, sw, bi >= 0 ? (bi & 31) : 0);
-      wsum = __fadd_rn(wsum, bi >= 0 ? sw : 0.0f);
-      if (lane == 0) {
-        pair_expert[r * topk + t] = bi;
-        pair_w[r * topk + t] = bi >= 0 ? sw : 0.0f;
-      }
     }
-    __syncwarp();
-    if (lane < topk && wsum > 0.0f && pair_expert[r * topk + lane] >= 0)
-      pair_w[r * topk + lane] = __fdiv_rn(pair_w[r * topk + lane], wsum);
   }
-  // the routed latent, then (when present) the shared expert's
-  // silu(gate)*up (src/forward_moe.c:484-536), both quantised per 32
   const int ng_l = latent / 32, ng_s = sw / 32;
   for (int g = warp; g < ng_l + ng_s; g += blockDim.x >> 5) {
     if (g < ng_l) {
@@ -1371,34 +1404,73 @@ __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int o
   }
 }
 
-// One (token, expert) pair, 32 consecutive FFN outputs of w1 and of w3:
-// int8 GEMV over the pair's quantised latent, silu(w1.x)*(w3.x), and the
-// per-32 quantisation of that group (src/forward_moe.c:189-196).
-// w13 is the expert's [w1 rows; w3 rows] ([2*ffn][latent]), latent <= 1024.
+// Router and w1/w3 of one (token, expert) pair in one kernel, for at most
+// 8 token rows (the pair's expert is known only after the routing, so a
+// separate router launch sat on the critical path of every layer).  Block
+// (chunk, pair p): warp 0 routes the pair's row (route_row) while the other
+// warps quantise the row's latent per 32 into shared memory; blocks of
+// chunk 0 store the row's experts and weights for w2 and the combine;
+// blocks of the row's first pair quantise their share of the shared
+// expert's silu(gate) * up.  Then 32 consecutive FFN outputs of w1 and of
+// w3: int8 GEMV over the latent, silu(w1.x) * (w3.x), the per-32
+// quantisation of that group (src/forward_moe.c:189-196).  w13 is the
+// expert's [w1 rows; w3 rows] ([2 ffn][latent]); latent <= 1024.
 __global__ void __launch_bounds__(256)
-moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent, int gs,
-               const int* __restrict__ pair_expert, int topk,
-               const int8_t* __restrict__ latq, const float* __restrict__ lats,
-               int8_t* hq, float* hs) {
+moe_route_w13_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
+                     const float* __restrict__ bias, int E, int topk,
+                     const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent, int gs,
+                     int* pair_expert, float* pair_w, int8_t* hq, float* hs,
+                     int off_shg, int off_shu, int sw, int8_t* shq, float* shs) {
   pdl_trigger();
   pdl_wait();
   __shared__ __align__(16) float P[8][8][32];
   __shared__ float H[64];
-  const int p = blockIdx.y, r = p / topk;
-  const int e = pair_expert[p];
-  if (e < 0) return;
+  __shared__ __align__(16) int8_t lq[1024];
+  __shared__ float ls[32];
+  __shared__ int s_e[16];
+  __shared__ float s_w[16];
+  const int p = blockIdx.y, r = p / topk, t = p - r * topk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nsb = latent / 32, rb = gs / 32, ng = latent / gs;
-  const int8_t* xr = latq + (size_t)r * latent;
-  const float* xsr = lats + (size_t)r * nsb;
+  const float* row = moein + (size_t)r * ldm;
+  const int nsb = latent / 32;
+  if (warp == 0) {
+    int se[16];
+    float sw_[16];
+    route_row(row + off_router, bias, E, topk, se, sw_);
+    if (lane == 0)
+      for (int i = 0; i < topk; i++) {
+        s_e[i] = se[i];
+        s_w[i] = sw_[i];
+      }
+  } else {
+    for (int g = warp - 1; g < nsb; g += 7) lq[g * 32 + lane] = warp_quant32(row[off_lat + g * 32 + lane], &ls[g]);
+  }
+  if (t == 0 && sw) {
+    // this block's share of the row's shared-expert groups (warp 0, the
+    // router, takes them last)
+    const int ng_s = sw / 32, per = (ng_s + gridDim.x - 1) / gridDim.x;
+    for (int gg = blockIdx.x * per + (7 - warp); gg < min(ng_s, (blockIdx.x + 1) * per); gg += 8) {
+      const int i = gg * 32 + lane;
+      shq[(size_t)r * sw + i] = warp_quant32(__fmul_rn(silu(row[off_shg + i]), row[off_shu + i]),
+                                             &shs[(size_t)r * ng_s + gg]);
+    }
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x < topk && t == 0) {
+    pair_expert[r * topk + threadIdx.x] = s_e[threadIdx.x];
+    pair_w[r * topk + threadIdx.x] = s_w[threadIdx.x];
+  }
+  const int e = s_e[t];
+  if (e < 0) return;
+  const int rb = gs / 32, ng = latent / gs;
   const size_t wbase = (size_t)e * 2 * ffn * latent;
   const size_t sbase = (size_t)e * 2 * ffn * ng;
   int4 xa = make_int4(0, 0, 0, 0), xb = xa;
   float xsv = 0.0f;
   if (lane < nsb) {
-    xa = __ldg(reinterpret_cast<const int4*>(xr + lane * 32));
-    xb = __ldg(reinterpret_cast<const int4*>(xr + lane * 32 + 16));
-    xsv = __ldg(xsr + lane);
+    xa = *reinterpret_cast<const int4*>(lq + lane * 32);
+    xb = *reinterpret_cast<const int4*>(lq + lane * 32 + 16);
+    xsv = ls[lane];
   }
   int4 wa[8], wb[8];
   float wsv[8];
@@ -1433,8 +1505,6 @@ moe_w13_kernel(const int8_t* __restrict__ w13q, const float* __restrict__ w13s, 
   }
 }
 
-// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
-// the last block to finish among a token row's pairs then forms
 // w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
 // the last block to finish among a token row's pairs then forms
 // lat_y = sum over the row's selected experts, in selection order, of
@@ -1499,15 +1569,17 @@ moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int
 // into tiles of at most 16 pair rows; each tile runs the warp-tile
 // tensor-core GEMM over its expert's weights, so every expert's weights
 // are streamed once per 16 rows instead of once per pair.  The arithmetic
-// per pair is that of moe_w13_kernel / moe_w2_kernel.
+// per pair is that of moe_route_w13_kernel / moe_w2_kernel.
 
 struct MoeTile {
   int e, start, count;
 };
 
 // Buckets the P pairs by expert: list holds pair indices grouped by
-// expert, tiles the (expert, start, count) of every 16-row tile, *ntiles
-// their number.  One block; E <= 256.
+// expert, tiles the (expert, start, count) of every tile of at most trows
+// pairs, *ntiles their number.  Pairs with a negative expert are skipped.
+// One block; E <= 256, P <= 1024 kMoeGroupPer.
+constexpr int kMoeGroupPer = 8;
 __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ pair_expert, int P, int E,
                                                          int* list, MoeTile* tiles, int* ntiles, int trows) {
   pdl_trigger();
@@ -1515,9 +1587,12 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
   __shared__ int cnt[256], off[256];
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  int slot[2] = {-1, -1}, ex[2] = {-1, -1};
-  for (int k = 0; k < 2; k++) {
+  int slot[kMoeGroupPer], ex[kMoeGroupPer];
+#pragma unroll
+  for (int k = 0; k < kMoeGroupPer; k++) {
     const int p = threadIdx.x + k * blockDim.x;
+    slot[k] = -1;
+    ex[k] = -1;
     if (p < P) {
       ex[k] = pair_expert[p];
       if (ex[k] >= 0) slot[k] = atomicAdd(&cnt[ex[k]], 1);
@@ -1534,7 +1609,8 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
     *ntiles = nt;
   }
   __syncthreads();
-  for (int k = 0; k < 2; k++)
+#pragma unroll
+  for (int k = 0; k < kMoeGroupPer; k++)
     if (slot[k] >= 0) list[off[ex[k]] + slot[k]] = threadIdx.x + k * blockDim.x;
 }
 

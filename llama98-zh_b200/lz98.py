@@ -102,6 +102,8 @@ def lib():
         "lz_ckpt_restore_seq": (c_int, [c_void_p, c_void_p, c_int, P(c_int), c_char_p, c_int]),
         "lz_debug_seq_sum": (c_int, [c_void_p, c_int, c_int, c_float, P(c_float), P(c_int)]),
         "lz_state_launches": (ctypes.c_longlong, [c_void_p]),
+        "lz_ep_unique_id": (c_int, [c_void_p, c_char_p, c_int]),
+        "lz_ep_init": (c_int, [c_void_p, c_void_p, c_int, c_int, c_char_p, c_int]),
         "lz_generate_resume": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                        ctypes.c_uint64, c_void_p, c_int, P(c_int), c_void_p, c_int, P(c_int),
                                        c_char_p, c_int]),
@@ -132,7 +134,7 @@ EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_debug_inject_wait_
            "lz_state_launches", "lz_state_counters", "lz_profile_round", "lz_profile_launches", "lz_lm_head_static", "lz_debug_seq_sum",
            "lz_ckpt_alloc", "lz_ckpt_free", "lz_ckpt_save", "lz_ckpt_restore", "lz_ckpt_save_seq",
            "lz_ckpt_restore_seq", "lz_generate_resume", "lz_prefix_init", "lz_prefix_free", "lz_prefix_reset",
-           "lz_prefix_match", "lz_prefix_prepare_tokens", "lz_prefix_stats"]
+           "lz_prefix_match", "lz_prefix_prepare_tokens", "lz_prefix_stats", "lz_ep_unique_id", "lz_ep_init"]
 
 
 class LZSampleParams(ctypes.Structure):
@@ -337,6 +339,15 @@ class State:
         if rc:
             raise LzError(f"set sampler failed ({rc})")
 
+    def ep_init(self, uid: bytes, rank: int, world: int):
+        """Expert parallelism over `world` ranks (collective: every rank calls
+        it with the same id)."""
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        err = ctypes.create_string_buffer(256)
+        rc = lib().lz_ep_init(self.h, buf, rank, world, err, 256)
+        if rc:
+            raise LzError(f"ep init failed ({rc}): {err.value.decode()}", rc)
+
     def get_sampler(self, seq=0):
         """(temperature, top-p, generator state) of sequence `seq` on the device."""
         t, p, r = c_float(), c_float(), ctypes.c_uint64()
@@ -462,6 +473,16 @@ class PrefixCache:
         v = [ctypes.c_long() for _ in range(5)]
         lib().lz_prefix_stats(self.h, *[ctypes.byref(x) for x in v])
         return dict(zip(("calls", "hits", "tokens_saved", "mismatch", "unsplittable"), (x.value for x in v)))
+
+
+def ep_unique_id() -> bytes:
+    """A fresh NCCL id for lz_ep_init (made on one rank, shared with all)."""
+    buf = ctypes.create_string_buffer(128)
+    err = ctypes.create_string_buffer(256)
+    rc = lib().lz_ep_unique_id(buf, err, 256)
+    if rc:
+        raise LzError(f"ep unique id failed ({rc}): {err.value.decode()}", rc)
+    return buf.raw
 
 
 def debug_counters():
