@@ -1079,11 +1079,10 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
   __shared__ __align__(16) float sc[KD][2];
   __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], vcs[TB][VD], zs[TB][VD], OUT[TB][VD];
   __shared__ __align__(16) float U[VD];
-  __shared__ float inv_q[TB], inv_k[TB], beta[TB], kqv[TB], inv_o[TB];
+  __shared__ float inv_q[TB], inv_k[TB], beta[TB], inv_o[TB];
   // the state dequantised (hi + lo / 256, unscaled), refreshed right after
-  // each requantisation; per-token scale products of the two passes
+  // each requantisation
   __shared__ __align__(16) float E[KD][VD];
-  __shared__ float SCX[2][KD][2], SCG[KD][2];
   // the batch's raw conv inputs and f_a rows, and the quantised f_a
   __shared__ __align__(16) float RAW[TB][3 * KD];
   __shared__ __align__(16) float FA[TB][kRankMax];
@@ -1216,37 +1215,24 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
     }
     __syncthreads();
     for (int t = 0; t < nt; t++) {
-      // scale products of this token: SCX[k|q][row][group] = sc * (k|q * g)
-      // (pass 1), SCG[row][group] = sc * g (pass 2)
-      {
-        const int kk = tid & 63, grp = (tid >> 6) & 1;
-        if (tid < 2 * VD) {
-          const float g = gv[t][kk];
-          SCX[0][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(kn[t][kk], g));
-          SCX[1][kk][grp] = __fmul_rn(sc[kk][grp], __fmul_rn(qn[t][kk], g));
-        } else if (tid < 4 * VD) {
-          SCG[kk][grp] = __fmul_rn(sc[kk][grp], gv[t][kk]);
-        }
-      }
-      __syncthreads();
-      // pass 1: thread vv (< 64) sums u, thread 64 + vv sums w, each over
-      // the 64 state rows in order; thread 128 forms kq
-      if (tid < 2 * VD) {
-        const int vv = tid & 63, which = tid >> 6, grp = vv >> 5;
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, __fmul_rn(E[kk][vv], SCX[which][kk][grp]));
-        if (tid < VD) U[vv] = acc; else OUT[t][vv] = acc;
-      } else if (tid == 2 * VD) {
-        float kq = 0.0f;
-        for (int kk = 0; kk < KD; kk++) kq = __fadd_rn(kq, __fmul_rn(kn[t][kk], qn[t][kk]));
-        kqv[t] = kq;
-      }
-      __syncthreads();
+      // pass 1 on threads vv < 64, three independent sequential chains over
+      // the 64 state rows, each in the reference's order: u = S^T (g.k)
+      // and w = S^T (g.q) of column vv (their scale products sc * (k|q * g)
+      // formed in place), and kq = k.q; then u = (v - u) * beta and the
+      // head output w + u * kq, all in this thread
       if (tid < VD) {
-        const float u = __fmul_rn(__fsub_rn(vcs[t][tid], U[tid]), beta[t]);
-        U[tid] = u;
-        OUT[t][tid] = __fadd_rn(OUT[t][tid], __fmul_rn(u, kqv[t]));
+        const int vv = tid, grp = vv >> 5;
+        float au = 0.0f, aw = 0.0f, kq = 0.0f;
+#pragma unroll 8
+        for (int kk = 0; kk < KD; kk++) {
+          const float g = gv[t][kk], sck = sc[kk][grp], e = E[kk][vv], k_ = kn[t][kk], q_ = qn[t][kk];
+          au = __fadd_rn(au, __fmul_rn(e, __fmul_rn(sck, __fmul_rn(k_, g))));
+          aw = __fadd_rn(aw, __fmul_rn(e, __fmul_rn(sck, __fmul_rn(q_, g))));
+          kq = __fadd_rn(kq, __fmul_rn(k_, q_));
+        }
+        const float u = __fmul_rn(__fsub_rn(vcs[t][vv], au), beta[t]);
+        U[vv] = u;
+        OUT[t][vv] = __fadd_rn(aw, __fmul_rn(u, kq));
       }
       __syncthreads();
       // pass 2: the 128 (state row, 32-wide group) units, four per warp at
@@ -1257,7 +1243,8 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-          buf[c] = __fadd_rn(__fmul_rn(E[kk][vv], SCG[kk][grp]), __fmul_rn(kn[t][kk], U[vv]));
+          const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);   // sc * g, before this unit's scale is replaced
+          buf[c] = __fadd_rn(__fmul_rn(E[kk][vv], scg), __fmul_rn(kn[t][kk], U[vv]));
           am[c] = abs_bits(buf[c]);
         }
 #pragma unroll
