@@ -85,11 +85,38 @@ def round_bytes(m, R: int, k: int, n_seq: int) -> float:
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the
-    timed region."""
+    """SM clock and clock-event reasons sampled during the timed region:
+    NVML read every 2 ms from a thread (reads only; no setting is
+    changed), else nvidia-smi at its shortest period."""
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu_index: int, uuid: str | None = None):
+        import threading
+        self.sm, self.smax, self.reasons, self.p = [], None, set(), None
+        self.stop_ev = threading.Event()
+        self.thread = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            h = None
+            if uuid:
+                try:
+                    h = nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+                except nv.NVMLError:
+                    h = None
+            self.h = h if h is not None else nv.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nv = None
         self.path = tempfile.mktemp(suffix=".csv")
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -102,7 +129,31 @@ class Clocks:
         except (OSError, ValueError):
             self.p = None
 
+    def _loop(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for n, bit in self.bits.items():
+                    if r & bit:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
     def stop(self):
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+            if not self.sm:
+                return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": [], "source": "nvml"}
+            return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.smax,
+                    "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 2 ms"}
         res = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
         if not self.p:
             return res
@@ -113,7 +164,6 @@ class Clocks:
             self.p.kill()
         self.f.close()
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
@@ -123,14 +173,22 @@ class Clocks:
                 smax = float(f[2])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(self.NAMES, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         os.unlink(self.path)
         if sm:
             res = {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                   "samples": len(sm)}
+                   "samples": len(sm), "source": "nvidia-smi, 50 ms"}
         return res
+
+
+def gpu_uuid(local: int):
+    try:
+        import torch
+        return str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        return None
 
 
 def physical_gpu(local_rank: int) -> int:
@@ -214,6 +272,8 @@ def run_batch32(m, args, rank: int, world: int):
         s.round_batch(K32, fetch=False)
     torch.cuda.synchronize()
     c0 = [s.counters(b) for b in range(B32)]
+    local = torch.cuda.current_device()
+    clocks = Clocks(physical_gpu(local), gpu_uuid(local))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -226,6 +286,7 @@ def run_batch32(m, args, rank: int, world: int):
     if world > 1:
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
     c1 = [s.counters(b) for b in range(B32)]
     emitted = sum(c1[b][1] - c0[b][1] for b in range(B32))
     accepted = sum(c1[b][2] - c0[b][2] for b in range(B32))
@@ -258,6 +319,7 @@ def run_batch32(m, args, rank: int, world: int):
         # one eager round, event-timed one by one on the state's stream
         "roofline": _expert_roofline(prof),
         "gpu_launches": prof["n_kernels"] * steps,
+        "clocks": clk,
     }
 
 
@@ -302,7 +364,7 @@ def run_ours(args):
         s.round_batch(k, fetch=False)
     torch.cuda.synchronize()
     c0 = [s.counters(b) for b in range(n_seq)]
-    clocks = Clocks(physical_gpu(local))
+    clocks = Clocks(physical_gpu(local), gpu_uuid(local))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -353,6 +415,8 @@ def run_ours(args):
     line = None
     if rank == 0:
         cpu = cpu_baseline(args) if (world == 1 and not args.no_cpu) else None
+        if b32 is not None and world == 1 and not args.no_cpu:
+            b32["cpu_baseline"] = b32_cpu_baseline(args.b32_cpu_seconds, *args.b32_prompts)
         per_round_ms = ms / max(1, args.steps)
         rb = round_bytes(m, n_seq * (k + 1), k, n_seq)
         line = {
@@ -395,65 +459,240 @@ def run_ours(args):
     return line
 
 
-def ref_sample(seconds_target: float = 20.0, stock: bool = False):
-    """The reference engine on a bounded sample of the workload: a 16-token
-    prompt then greedy k=2 rounds until about `seconds_target` of decode,
-    in the parity float tier (the faster of the two on x86) or, with
-    `stock`, in the reference's default fixed-point tier.  Returns
-    (tokens/s, detail)."""
+def host_cores() -> int:
+    """Cores this process may use: its affinity mask, bounded by a cgroup
+    CPU quota when one is set."""
+    n = len(os.sched_getaffinity(0))
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            q, per = f.read().split()[:2]
+        if q != "max":
+            n = min(n, max(1, int(q) // int(per)))
+    except (OSError, ValueError):
+        pass
+    return n
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def mem_available_bytes() -> float:
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return float(line.split()[1]) * 1024.0
+    except (OSError, ValueError):
+        pass
+    return 0.0
+
+
+def _reference():
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from oracles import Reference, reference_available
-    import numpy as np
-    if not reference_available():
-        return None, "oracle/_ref/liblz98ref.so not built"
-    d = model_dir()
-    R = Reference(d, 2048, SPEC_K)
-    if stock:
-        R.stock_tier()
-    rng = np.random.default_rng([0, 1000])
-    prompt = rng.integers(0, R.vocab, 16).astype(np.int32)
-    toks, rounds = R.generate(prompt, 8, SPEC_K)
-    per_tok = (R.last_elapsed_ms - R.last_prefill_ms) / max(1, len(toks))
-    n_new = max(8, int(seconds_target * 1000.0 / max(per_tok, 1e-3)))
-    toks, rounds = R.generate(prompt, n_new, SPEC_K)
-    dec_ms = R.last_elapsed_ms - R.last_prefill_ms
-    R.close()
-    tier = "stock tier (--fixed all, --fastfp on)" if stock else "float tier (--fixed off, --fastfp off)"
-    return len(toks) / (dec_ms * 1e-3), f"reference C99 engine, {tier}, 16-token prompt + {len(toks)} greedy k=2 tokens ({len(rounds)} rounds), decode only"
+    return Reference, reference_available
+
+
+def ref_decode_sample(prompt, k: int, temp: float, seed: int, max_new: int, seconds: float, stock: bool = False):
+    """The reference engine (oracle/_ref, one thread) on one sequence of the
+    workload: the prompt prefilled (untimed), a short warm decode, then
+    decode for about `seconds` of wall time.  Returns (tokens/s, tokens,
+    decode seconds, prefill seconds)."""
+    Reference, available = _reference()
+    if not available():
+        return None
+    R = Reference(model_dir(), len(prompt) + max_new + 64, max(1, k))
+    try:
+        if stock:
+            R.stock_tier()
+        pf = R.session_begin(prompt, max_new, k, temp=temp, topp=0.95, seed=seed)
+        R.session_decode(k + 1)
+        toks, _, el = R.session_decode(1 << 30, seconds * 1000.0)
+    finally:
+        if stock:
+            R.L.rd_set_tier(7)
+        R.close()
+    return len(toks) / max(1e-9, el * 1e-3), len(toks), el * 1e-3, pf * 1e-3
 
 
 def cpu_baseline(args):
-    v, sample = ref_sample(args.cpu_seconds)
-    if v is None:
-        return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample}
-    # the reference's default arithmetic too, on a shorter sample: the
-    # baseline above is the faster of the two
-    vs, sample_s = ref_sample(max(2.0, args.cpu_seconds / 3), stock=True)
-    return {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample,
-            "stock_tier": {"value": vs, "sample": sample_s}}
+    """Batch-1 CPU baseline: the reference on the headline workload's own
+    sequence (the 512-token prompt, greedy, k = 2), float tier, then its
+    stock arithmetic on a shorter sample."""
+    p = prompts(1, 0)[0]
+    r = ref_decode_sample(p, SPEC_K, 0.0, 1, MAX_NEW, args.cpu_seconds)
+    if r is None:
+        return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference",
+                "sample": "oracle/_ref/liblz98ref.so not built"}
+    v, n, el, pf = r
+    rs = ref_decode_sample(p, SPEC_K, 0.0, 1, MAX_NEW, max(2.0, args.cpu_seconds / 3), stock=True)
+    return {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "cpu": cpu_model(),
+            "sample": f"reference C99 engine, float tier (--fixed off, --fastfp off), the bench's 512-token "
+                      f"prompt (prefill {pf:.1f} s, untimed), then {n} greedy k=2 tokens in {el:.1f} s of decode",
+            "stock_tier": {"value": rs[0] if rs else None,
+                           "sample": f"stock tier (--fixed all, --fastfp on), same prompt, {rs[1]} tokens in "
+                                     f"{rs[2]:.1f} s" if rs else "not run"}}
+
+
+def _b32_cpu_worker(prompt, seed, seconds, stock, barrier, out):
+    try:
+        Reference, _ = _reference()
+        R = Reference(model_dir(), len(prompt) + NEW32 + 64, K32)
+        if stock:
+            R.stock_tier()
+        R.session_begin(prompt, NEW32, K32, temp=0.8, topp=0.95, seed=seed)
+        R.session_decode(K32 + 1)
+        barrier.wait(timeout=1200)
+        toks, rounds, el = R.session_decode(1 << 30, seconds * 1000.0)
+        R.close()
+        out.put((len(toks), el * 1e-3, len(rounds), None))
+    except Exception as e:          # reported, never hangs the parent
+        try:
+            barrier.abort()
+        except Exception:
+            pass
+        out.put((0, 0.0, 0, repr(e)[:200]))
+
+
+def _collect(procs, q, barrier, n: int, limit_s: float):
+    """Results of the worker processes; a worker that died without one
+    breaks the barrier (the others report an error instead of waiting),
+    and workers still running at the limit are terminated."""
+    import queue
+    outs, aborted, t_end = [], False, time.time() + limit_s
+    while len(outs) < n and time.time() < t_end:
+        try:
+            outs.append(q.get(timeout=1.0))
+            continue
+        except queue.Empty:
+            pass
+        if not aborted and any(pr.exitcode not in (None, 0) for pr in procs):
+            barrier.abort()
+            aborted = True
+        if all(pr.exitcode is not None for pr in procs) and q.empty():
+            break
+    for pr in procs:
+        pr.join(timeout=30)
+        if pr.exitcode is None:
+            pr.terminate()
+            pr.join(timeout=10)
+    return outs
+
+
+def b32_cpu_baseline(seconds: float, lo: int = 256, hi: int = 1024):
+    """Batch-32 CPU baseline: one reference process per usable
+    host core, each on its own sequence of the workload (the GPU arm's 32
+    sequences of rank 0 first, then rank 1's, ...; their seeds), Zipf
+    prompts prefilled untimed, temperature 0.8, top-p 0.95, k = 3.  All
+    processes start decoding together (a barrier) and decode for about
+    `seconds`; the value is the sum of their rates.  Float tier, then
+    stock tier.  The process count is also bounded by host memory (each
+    process holds the model)."""
+    import multiprocessing as mp
+    import lz98_synth
+    Reference, available = _reference()
+    if not available():
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                "sample": "oracle/_ref/liblz98ref.so not built"}
+    cfg = lz98_synth.CONFIGS[MODEL]
+    model_bytes = os.path.getsize(os.path.join(model_dir(), "model.bin")) * 1.1 + 0.3e9
+    n_mem = int(0.5 * mem_available_bytes() // model_bytes)
+    cores = host_cores()
+    n = max(1, min(cores, n_mem, 8 * B32))
+    seqs = []
+    r = 0
+    while len(seqs) < n:
+        for b, p in enumerate(lz98_synth.workload_prompts(cfg, B32, lo, hi, 1.1, seed=r)):
+            seqs.append((p, 1000 + r * B32 + b))
+        r += 1
+    seqs = seqs[:n]
+    ctx = mp.get_context("spawn")
+    res = {}
+    t_all = time.time()
+    for tier, secs in (("float", seconds), ("stock", max(2.0, seconds / 2))):
+        barrier, q = ctx.Barrier(n), ctx.Queue()
+        procs = [ctx.Process(target=_b32_cpu_worker, args=(p, sd, secs, tier == "stock", barrier, q))
+                 for p, sd in seqs]
+        for pr in procs:
+            pr.start()
+        outs = _collect(procs, q, barrier, n, 1800.0)
+        errs = [o[3] for o in outs if o[3]]
+        if len(outs) < n:
+            errs.append(f"{n - len(outs)} processes gave no result")
+        rate = sum(o[0] / o[1] for o in outs if o[1] > 0)
+        res[tier] = {"value": rate if not errs else None, "tokens": sum(o[0] for o in outs),
+                     "decode_s": max(o[1] for o in outs), "errors": errs[:3]}
+    lens = sorted(len(p) for p, _ in seqs)
+    return {"value": res["float"]["value"], "unit": UNIT, "cores": n, "kind": "reference",
+            "cpu": cpu_model(), "host_cores": cores,
+            "sample": f"{n} reference processes (one per core, float tier), one configs[2] sequence each "
+                      f"(prompts {lens[0]}-{lens[-1]} tokens, prefilled untimed), temperature 0.8, top-p 0.95, "
+                      f"k=3, decoding together for {res['float']['decode_s']:.1f} s; "
+                      f"{res['float']['tokens']} tokens; sum of per-process rates",
+            "stock_tier": {"value": res["stock"]["value"], "tokens": res["stock"]["tokens"],
+                           "decode_s": res["stock"]["decode_s"]},
+            "errors": res["float"]["errors"] + res["stock"]["errors"],
+            "wall_s": time.time() - t_all}
 
 
 def run_reference(args):
+    """The reference arm: the reference engine itself on the headline
+    workload (rank 0 only): the bench's 512-token prompt prefilled once
+    (untimed), W warm-up decode slices, then K timed slices; the value is
+    the tokens of the K slices over their decode time."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return None
-    steps_v = []
-    sample = None
-    for _ in range(max(1, args.steps)):
-        v, sample = ref_sample(max(2.0, 60.0 / max(1, args.steps)))
-        if v is None:
-            print(json.dumps({"impl": "reference", "unavailable": sample}), flush=True)
-            return None
-        steps_v.append(v)
-    v = statistics.median(steps_v)
+    Reference, available = _reference()
+    if not available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/liblz98ref.so not built"}), flush=True)
+        return None
+    p = prompts(1, 0)[0]
+    R = Reference(model_dir(), PROMPT + MAX_NEW + 64, SPEC_K)
+    slice_s = min(3.0, max(0.3, 25.0 / max(1, args.steps)))
+    prefill_s = R.session_begin(p, MAX_NEW, SPEC_K) * 1e-3
+    n_prefill = 1
+
+    def one(seconds):
+        nonlocal n_prefill
+        toks, rounds, el = R.session_decode(1 << 30, seconds * 1000.0)
+        if len(toks) == 0:              # the 256-token budget is used up: prefill again
+            R.session_begin(p, MAX_NEW, SPEC_K)
+            n_prefill += 1
+            toks, rounds, el = R.session_decode(1 << 30, seconds * 1000.0)
+        return len(toks), len(rounds), el * 1e-3
+
+    for _ in range(args.warmup):
+        one(min(slice_s, 1.0))
+    steps = [one(slice_s) for _ in range(max(1, args.steps))]
+    R.close()
+    ntok = sum(s_[0] for s_ in steps)
+    nround = sum(s_[1] for s_ in steps)
+    dec_s = sum(s_[2] for s_ in steps)
+    v = ntok / max(1e-9, dec_s)
+    sample = (f"reference C99 engine (oracle/_ref, one thread), float tier (--fixed off, --fastfp off), the "
+              f"bench's 512-token prompt (prefill {prefill_s:.1f} s, untimed, {n_prefill}x), greedy k=2; "
+              f"{args.steps} decode slices of ~{slice_s:.1f} s: {ntok} tokens, {nround} rounds")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec_s * 1e3 / max(1, nround),
+            "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 weights/activations, int32 dot, f32 epilogue (CPU)",
-            "data": "synthetic", "config": {"workload": "configs[1]: ~0.5B KunMoe, batch 1, greedy, k=2",
-                                            "model": "KunMoe-0.5B-synthetic", "global_batch": 1,
-                                            "seq_len": 16, "parallelism": "none (single-threaded C99)"},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "sample": sample},
+            "data": "synthetic: random-init weights N(0,0.02)->bf16->Q8_0, uniform prompt ids",
+            "config": {"workload": "configs[1]: ~0.5B KunMoe, batch 1 per GPU, 512-token prompt, greedy, k=2",
+                       "model": "KunMoe-0.5B-synthetic", "global_batch": 1, "seq_len": PROMPT,
+                       "new_tokens_budget": MAX_NEW, "spec_k": SPEC_K,
+                       "parallelism": "none (the reference is single-threaded C99)"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "cpu": cpu_model(),
+                             "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return line
@@ -466,7 +705,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seqs", type=int, default=1, help="sequences per GPU")
-    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--b32-cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the C-ABI end-to-end pass")
     ap.add_argument("--no-b32", action="store_true", help="skip the batch-32 temperature workload")

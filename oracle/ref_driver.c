@@ -98,9 +98,12 @@ void *rd_open(const char *dir, int seq_len, int spec_k_max, int nt_cap,
     return h;
 }
 
+void rd_session_end_owned(void *vh);
+
 void rd_close(void *vh) {
     RdHandle *h = (RdHandle *)vh;
     if (!h) return;
+    rd_session_end_owned(vh);
     if (h->have_s) lz_state_free(&h->s);
     if (h->have_m) lz_free(&h->m);
     free(h);
@@ -179,49 +182,55 @@ void rd_set_chain(void *vh, const float *chain) {
     memcpy(h->s.mtp_chain, chain, sizeof(float) * (size_t)h->m.config.hidden_size);
 }
 
-/* One whole generation on token ids.  temp <= 0 runs the greedy rounds
-   (lz_spec_round), temp > 0 the coupled rounds (lz_spec_round_temp) with
-   top-p `topp` and the sampler seeded with `seed`.  spec_k = 0 disables
-   speculation (plain per-token decode).
-   out_tok receives every emitted token in order (cap out_cap);
-   rounds receives (k_eff, n_accept) per speculative round (cap round_cap).
-   Returns 0 on success, else a positive LZErr code. */
-int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
-                   int spec_k, float temp, float topp, unsigned long long seed,
-                   float p_min, int n_min,
-                   int *out_tok, int out_cap, int *out_n,
-                   int *rounds, int round_cap, int *n_rounds,
-                   double *elapsed_ms, double *prefill_ms);
+/* A generation on token ids, split so that the decode can run in bounded
+   slices: rd_session_begin resets the state and prefills the prompt,
+   rd_session_decode runs the decode loop until max_tokens more tokens have
+   been emitted, the budget (n_prompt + max_new positions) is used up, or
+   budget_ms of wall time has passed (checked between rounds, 0 = no
+   limit), and can be called again to go on where it stopped;
+   rd_session_end frees the sampler.  rd_generate_pm is begin + one
+   unlimited decode + end.
 
-int rd_generate(void *vh, const int *prompt, int n_prompt, int max_new,
-                int spec_k, float temp, float topp, unsigned long long seed,
-                int *out_tok, int out_cap, int *out_n,
-                int *rounds, int round_cap, int *n_rounds,
-                double *elapsed_ms, double *prefill_ms) {
-    return rd_generate_pm(vh, prompt, n_prompt, max_new, spec_k, temp, topp, seed, 0.0f, 0,
-                          out_tok, out_cap, out_n, rounds, round_cap, n_rounds,
-                          elapsed_ms, prefill_ms);
+   temp <= 0 runs the greedy rounds (lz_spec_round), temp > 0 the coupled
+   rounds (lz_spec_round_temp) with top-p `topp` and the sampler seeded
+   with `seed`.  spec_k = 0 disables speculation (plain per-token decode).
+   A discarded draft (n_emit == 0, p_min / n_min) emits nothing and forces
+   a fresh capture next round (src/generate.c:1972-2080).
+   out_tok receives every emitted token of the call in order (cap
+   out_cap); rounds receives (k_eff, n_accept) per speculative round (cap
+   round_cap).  Return 0 on success, else a positive code. */
+typedef struct {
+    LZSampler samp;
+    void *owner;
+    int active, pos, token, max_pos, have_seed, spec_k, n_min;
+    float temp, p_min;
+} RdSession;
+
+static RdSession rd_sess;   /* one session per process (the tier is process-global too) */
+
+void rd_session_end(void *vh) {
+    (void)vh;
+    if (rd_sess.active) lz_sampler_free(&rd_sess.samp);
+    rd_sess.active = 0;
 }
 
-/* The same loop with the rounds' p_min / n_min: a discarded draft
-   (n_emit == 0) emits nothing and forces a fresh capture next round
-   (src/generate.c:1972-2080). */
-int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
-                   int spec_k, float temp, float topp, unsigned long long seed,
-                   float p_min, int n_min,
-                   int *out_tok, int out_cap, int *out_n,
-                   int *rounds, int round_cap, int *n_rounds,
-                   double *elapsed_ms, double *prefill_ms) {
+/* rd_close's part: the session of this handle, if any, ends with it */
+void rd_session_end_owned(void *vh) {
+    if (rd_sess.active && rd_sess.owner == vh) rd_session_end(vh);
+}
+
+int rd_session_begin(void *vh, const int *prompt, int n_prompt, int max_new,
+                     int spec_k, float temp, float topp, unsigned long long seed,
+                     float p_min, int n_min, double *prefill_ms) {
     RdHandle *h = (RdHandle *)vh;
     const LZModel *m = &h->m;
     LZRunState *s = &h->s;
     const LZModelConfig *c = &m->config;
     LZSampleParams sp;
-    LZSampler samp;
-    int rc = 0, pos, token, max_pos, have_seed = 0, n_out = 0, nr = 0;
-    double t0, t1;
-    char err[256];
+    RdSession *q = &rd_sess;
+    double t0 = rd_now_ms();
 
+    rd_session_end(vh);
     lz_sample_defaults(&sp);
     sp.temperature = temp > 0.0f ? temp : 0.0f;
     sp.topp = topp;
@@ -232,100 +241,149 @@ int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
     sp.repetition_penalty = 1.0f;
     sp.repeat_last_n = 0;
     sp.think_temp_enabled = 0;
-    if (lz_sampler_init(&samp, c->vocab_size, &sp, (lz_u64)seed) != 0) return 1;
+    if (lz_sampler_init(&q->samp, c->vocab_size, &sp, (lz_u64)seed) != 0) return 1;
+    q->active = 1;
+    q->owner = vh;
+    q->spec_k = spec_k;
+    q->temp = temp;
+    q->p_min = p_min;
+    q->n_min = n_min;
+    q->have_seed = 0;
 
     lz_state_reset(s, m);
-    max_pos = n_prompt + max_new;
-    if (max_pos > s->seq_len) max_pos = s->seq_len;
-    if (max_pos < n_prompt + 1) max_pos = n_prompt + 1;
+    q->max_pos = n_prompt + max_new;
+    if (q->max_pos > s->seq_len) q->max_pos = s->seq_len;
+    if (q->max_pos < n_prompt + 1) q->max_pos = n_prompt + 1;
 
-    t0 = rd_now_ms();
     if (n_prompt > 1) {
         if (spec_k > 0) {
             float *hb = (float *)malloc(sizeof(float) * (size_t)(n_prompt - 1) *
                                         (size_t)c->hidden_size);
-            if (!hb) { rc = 1; goto out; }
+            if (!hb) return 1;
             if (!lz_forward_batch_capture(m, s, prompt, n_prompt - 1, 0, hb)) {
-                free(hb); rc = 2; goto out;
+                free(hb); return 2;
             }
             if (lz_mtp_prefill(m, s, hb, prompt + 1, n_prompt - 1, s->mtp_pos) != 0) {
-                free(hb); rc = 3; goto out;
+                free(hb); return 3;
             }
             s->mtp_pos = s->mtp_pos + (n_prompt - 1);
             free(hb);
         } else {
-            if (!lz_forward_batch(m, s, prompt, n_prompt - 1, 0)) { rc = 2; goto out; }
+            if (!lz_forward_batch(m, s, prompt, n_prompt - 1, 0)) return 2;
         }
     }
-    t1 = rd_now_ms();
-    if (prefill_ms) *prefill_ms = t1 - t0;
-    pos = n_prompt - 1;
-    token = prompt[n_prompt - 1];
+    if (prefill_ms) *prefill_ms = rd_now_ms() - t0;
+    q->pos = n_prompt - 1;
+    q->token = prompt[n_prompt - 1];
+    return 0;
+}
 
-    while (pos < max_pos - 1) {
+int rd_session_decode(void *vh, int max_tokens, double budget_ms,
+                      int *out_tok, int out_cap, int *out_n,
+                      int *rounds, int round_cap, int *n_rounds, double *elapsed_ms) {
+    RdHandle *h = (RdHandle *)vh;
+    const LZModel *m = &h->m;
+    LZRunState *s = &h->s;
+    RdSession *q = &rd_sess;
+    int rc = 0, n_out = 0, nr = 0;
+    double t0 = rd_now_ms();
+    char err[256];
+
+    if (!q->active || q->owner != vh) return 1;
+    while (q->pos < q->max_pos - 1 && n_out < max_tokens &&
+           (budget_ms <= 0.0 || rd_now_ms() - t0 < budget_ms)) {
         int round_k = 0;
-        if (spec_k > 0) {
-            round_k = spec_k;
-            if (round_k > max_pos - 3 - pos) round_k = max_pos - 3 - pos;
+        if (q->spec_k > 0) {
+            round_k = q->spec_k;
+            if (round_k > q->max_pos - 3 - q->pos) round_k = q->max_pos - 3 - q->pos;
         }
         if (round_k > 0) {
             int anchor, anchor_pos, n_accept = 0, new_pos = 0, k_eff = 0, n_emit, ei;
             int out[LZ_SPEC_K_MAX + 1];
-            if (have_seed) {
-                anchor = token;
-                anchor_pos = pos - 1;
+            if (q->have_seed) {
+                anchor = q->token;
+                anchor_pos = q->pos - 1;
             } else {
-                float *lg = lz_forward_capture(m, s, token, pos);
+                float *lg = lz_forward_capture(m, s, q->token, q->pos);
                 if (!lg) { rc = 4; goto out; }
-                anchor_pos = pos;
-                anchor = lz_sample_ex(&samp, lg, NULL, 0);
-                lz_sampler_observe(&samp, anchor);
+                anchor_pos = q->pos;
+                anchor = lz_sample_ex(&q->samp, lg, NULL, 0);
+                lz_sampler_observe(&q->samp, anchor);
                 if (n_out < out_cap) out_tok[n_out] = anchor;
                 n_out++;
             }
-            if (temp > 0.0f)
+            if (q->temp > 0.0f)
                 n_emit = lz_spec_round_temp(m, s, anchor, anchor_pos, round_k,
-                                            p_min, n_min, &samp, rd_dbg_break_rollback,
+                                            q->p_min, q->n_min, &q->samp, rd_dbg_break_rollback,
                                             rd_dbg_skip_catchup, out, &n_accept,
                                             &new_pos, &k_eff, err, (int)sizeof err);
             else
                 n_emit = lz_spec_round(m, s, anchor, anchor_pos, round_k,
-                                       p_min, n_min, &samp, rd_dbg_break_rollback,
+                                       q->p_min, q->n_min, &q->samp, rd_dbg_break_rollback,
                                        rd_dbg_skip_catchup, out, &n_accept,
                                        &new_pos, &k_eff, err, (int)sizeof err);
             if (n_emit < 0) { rc = -n_emit; goto out; }
             if (nr < round_cap) { rounds[2 * nr] = k_eff; rounds[2 * nr + 1] = n_accept; }
             nr++;
-            have_seed = (n_emit > 0);
+            q->have_seed = (n_emit > 0);
             if (n_emit > 0) {
                 for (ei = 0; ei <= n_accept; ei++) {
-                    lz_sampler_observe(&samp, out[ei]);
+                    lz_sampler_observe(&q->samp, out[ei]);
                     if (n_out < out_cap) out_tok[n_out] = out[ei];
                     n_out++;
                 }
             }
-            pos = new_pos + 1;
-            token = out[n_accept];
+            q->pos = new_pos + 1;
+            q->token = out[n_accept];
             continue;
         }
         {
-            float *lg = lz_forward(m, s, token, pos);
+            float *lg = lz_forward(m, s, q->token, q->pos);
             int next;
             if (!lg) { rc = 5; goto out; }
-            next = lz_sample_ex(&samp, lg, NULL, 0);
-            lz_sampler_observe(&samp, next);
+            next = lz_sample_ex(&q->samp, lg, NULL, 0);
+            lz_sampler_observe(&q->samp, next);
             if (n_out < out_cap) out_tok[n_out] = next;
             n_out++;
-            token = next;
-            pos++;
+            q->token = next;
+            q->pos++;
         }
     }
 out:
     if (elapsed_ms) *elapsed_ms = rd_now_ms() - t0;
     *out_n = n_out;
     *n_rounds = nr;
-    lz_sampler_free(&samp);
     return rc;
+}
+
+int rd_generate_pm(void *vh, const int *prompt, int n_prompt, int max_new,
+                   int spec_k, float temp, float topp, unsigned long long seed,
+                   float p_min, int n_min,
+                   int *out_tok, int out_cap, int *out_n,
+                   int *rounds, int round_cap, int *n_rounds,
+                   double *elapsed_ms, double *prefill_ms) {
+    double pf = 0.0, dec = 0.0;
+    int rc = rd_session_begin(vh, prompt, n_prompt, max_new, spec_k, temp, topp, seed,
+                              p_min, n_min, &pf);
+    *out_n = 0;
+    *n_rounds = 0;
+    if (rc == 0)
+        rc = rd_session_decode(vh, 1 << 30, 0.0, out_tok, out_cap, out_n,
+                               rounds, round_cap, n_rounds, &dec);
+    rd_session_end(vh);
+    if (prefill_ms) *prefill_ms = pf;
+    if (elapsed_ms) *elapsed_ms = pf + dec;
+    return rc;
+}
+
+int rd_generate(void *vh, const int *prompt, int n_prompt, int max_new,
+                int spec_k, float temp, float topp, unsigned long long seed,
+                int *out_tok, int out_cap, int *out_n,
+                int *rounds, int round_cap, int *n_rounds,
+                double *elapsed_ms, double *prefill_ms) {
+    return rd_generate_pm(vh, prompt, n_prompt, max_new, spec_k, temp, topp, seed, 0.0f, 0,
+                          out_tok, out_cap, out_n, rounds, round_cap, n_rounds,
+                          elapsed_ms, prefill_ms);
 }
 
 /* ---- op-level entry points (plain pointers; the tensor is built here) -- */

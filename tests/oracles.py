@@ -176,6 +176,11 @@ class Reference:
         L.rd_generate_pm.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
                                      ctypes.c_ulonglong, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p,
                                      c_int, P(c_int), P(ctypes.c_double), P(ctypes.c_double)]
+        L.rd_session_begin.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                                       ctypes.c_ulonglong, c_float, c_int, P(ctypes.c_double)]
+        L.rd_session_decode.argtypes = [c_void_p, c_int, ctypes.c_double, c_void_p, c_int, P(c_int), c_void_p,
+                                        c_int, P(c_int), P(ctypes.c_double)]
+        L.rd_session_end.argtypes = [c_void_p]
         L.rd_forward_verify.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
         L.rd_batch_capture.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p]
         L.rd_forward_capture.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p]
@@ -259,6 +264,36 @@ class Reference:
         h = np.ascontiguousarray(hidden, np.float32)
         t = np.ascontiguousarray(nxt, np.int32)
         return self.L.rd_mtp_prefill(c_void_p(self.h), _ptr(h), _ptr(t), len(t), pos0)
+
+    def session_begin(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
+        """Reset and prefill `prompt` for a generation of up to max_new
+        tokens that session_decode then runs in slices; returns the
+        prefill's wall time in ms."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        pf = ctypes.c_double()
+        rc = self.L.rd_session_begin(c_void_p(self.h), _ptr(p), len(p), max_new, spec_k, temp, topp, seed,
+                                     c_float(p_min), int(n_min), ctypes.byref(pf))
+        if rc:
+            raise RuntimeError(f"reference session prefill failed rc={rc}")
+        return pf.value
+
+    def session_decode(self, max_tokens, budget_ms=0.0):
+        """Decode until max_tokens more tokens, the generation's budget or
+        budget_ms of wall time (checked between rounds): (tokens, rounds,
+        elapsed ms)."""
+        out = np.zeros(max_tokens + 16, np.int32)
+        rounds = np.zeros(2 * (max_tokens + 16), np.int32)
+        on, nr, el = c_int(), c_int(), ctypes.c_double()
+        rc = self.L.rd_session_decode(c_void_p(self.h), max_tokens, budget_ms, _ptr(out), len(out),
+                                      ctypes.byref(on), _ptr(rounds), len(rounds) // 2, ctypes.byref(nr),
+                                      ctypes.byref(el))
+        if rc:
+            raise RuntimeError(f"reference session decode failed rc={rc}")
+        n = min(on.value, len(out))
+        return out[:n].copy(), rounds[:2 * min(nr.value, len(rounds) // 2)].reshape(-1, 2).copy(), el.value
+
+    def session_end(self):
+        self.L.rd_session_end(c_void_p(self.h))
 
     def generate(self, prompt, max_new, spec_k, temp=0.0, topp=0.95, seed=1, p_min=0.0, n_min=0):
         p = np.ascontiguousarray(prompt, np.int32)

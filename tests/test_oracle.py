@@ -376,3 +376,30 @@ def test_bench_golden_inputs_regenerate():
     assert max(lens) in [len(g[f"b32_{b}_prompt"]) for b in g["b32_pick"]]
     for b in g["b32_pick"]:
         assert np.array_equal(np.array(prompts[b], np.int32), g[f"b32_{b}_prompt"])
+
+
+@needs_ref
+@pytest.mark.parametrize("temp,k", [(0.0, 2), (0.8, 3)])
+def test_reference_session_slices_match_golden(tiny_dir, temp, k):
+    """The reference driver's resumable generation (prefill once, decode in
+    slices, as the bench's reference arm times it) emits the golden stream
+    and round records of the one-shot generation, whatever the slicing."""
+    g = load_golden("tiny")
+    tag = f"gen_t{int(temp * 10)}_k{k}"
+    R = Reference(tiny_dir, 512, 4)
+    try:
+        for slices in ((40,), (1, 5, 34), (7, 7, 7, 7, 7, 7, 7)):
+            R.session_begin(g["prompt"], 40, k, temp=temp, seed=1234)
+            toks, rounds = [], []
+            for n in slices:
+                t, r, _ = R.session_decode(n)
+                toks.append(t)
+                rounds.append(r)
+            # the budget ends the generation: nothing more comes out
+            t, r, _ = R.session_decode(8)
+            assert len(t) == 0 and len(r) == 0
+            R.session_end()
+            assert np.array_equal(np.concatenate(toks), g[tag + "_tokens"]), slices
+            assert np.array_equal(np.concatenate(rounds), g[tag + "_rounds"]), slices
+    finally:
+        R.close()
