@@ -134,6 +134,27 @@ LZ_HD float random_f32(unsigned long long* st) {
 LZ_HD void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 LZ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Thread-block clusters: this CTA's rank in its cluster, the cluster-wide
+// barrier (every thread of every CTA of the cluster; release / acquire, so
+// shared-memory writes before it are visible to the peers after it), and a
+// float read from the same shared-memory variable of a peer CTA.
+LZ_HD uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+LZ_HD void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+LZ_HD float ld_peer_f32(const float* local, uint32_t peer) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"((uint32_t)__cvta_generic_to_shared(local)),
+               "r"(peer));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 // ------------------------------------------------ TMA, mbarriers, ldmatrix
 
 LZ_HD uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }

@@ -1369,10 +1369,11 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
                L.dt_bias, c.lb, s->seqs, s->hi, s->lo, s->sc, s->q_seq, s->q_slot,
                (int)((size_t)l * c.nv * c.kd * c.vd), s->depth, adv, s->ssm_scale, L.o_norm, c.eps, vdim, s->oq,
                s->os};
-    // few (head, sequence) blocks (batch 1): 16 warps per block halve the
-    // per-token requantisation pass; otherwise 8 warps, 4 blocks per SM
-    if (c.nv * nseq <= s->n_sm / 2)
-      launch(s, kda_recur_kernel<2 * kRecurThreads>, dim3(c.nv, nseq), dim3(2 * kRecurThreads), 0, ka);
+    // few (head, sequence) pairs (batch 1): each head as a cluster of two
+    // 16-warp CTAs, one per value group; otherwise one 8-warp CTA per head,
+    // 4 per SM
+    if (2 * c.nv * nseq <= s->n_sm)
+      launch(s, kda_recur_split_kernel<2 * kRecurThreads>, dim3(2 * c.nv, nseq), dim3(2 * kRecurThreads), 0, ka);
     else
       launch(s, kda_recur_kernel<kRecurThreads>, dim3(c.nv, nseq), dim3(kRecurThreads), 0, ka);
     gemv(s, L.o, s->oq, s->os, R, s->x, d, 1);

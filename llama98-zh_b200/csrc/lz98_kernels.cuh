@@ -1040,14 +1040,24 @@ struct KdaArgs {
 // state runs for a batch of up to kRecurTB tokens at once: the conv (one
 // thread per channel, tokens in order, the history in registers), the f_a
 // quantisation and the gate, l2norm(q) * kd^-1/2, l2norm(k), beta =
-// sigmoid(b); then per token, serially, pass 1 (u = S^T(g.k) and w =
-// S^T(g.q), each a sequential sum over the 64 state rows, one thread per
-// output column forming its products in order; kq = k.q on another
-// thread), the head output w + u*kq with u = (v - u)*beta, and pass 2 (each
-// state row g*S + k*u requantised in two planes, four 32-wide groups per
-// warp at a time); finally the gated RMSNorm and per-32 quantisation of
-// every token's output.  src/forward_kda.c:856-936 and 1029-1040,
-// src/ops_gdn.c:2488-2778, src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
+// sigmoid(b), and the products k*g and q*g; then per token, serially,
+// pass 1 (u = S^T(g.k) and w = S^T(g.q), each a sequential sum over the 64
+// state rows on its own thread per value column, the scale product sc *
+// (k*g) formed in place; k.q on another thread), u = (v - u)*beta, and
+// pass 2 (each state row g*S + k*u requantised in two planes, four 32-wide
+// groups per warp at a time, the head output w + u*kq beside it);
+// finally the gated RMSNorm and per-32 quantisation of every token's
+// output.  src/forward_kda.c:856-936 and 1029-1040, src/ops_gdn.c:2488-2778,
+// src/ops_gdn.c:1191-1340, src/ops_norm.c:749-842.
+//
+// SPLIT = 2 runs a head as a cluster of two CTAs, one per 32-wide value
+// group: the state columns (and their row scales) of the two groups never
+// meet in the recurrence - pass 1 sums down a column, pass 2 requantises a
+// (row, group) - so each CTA holds and updates only its half; the
+// per-key work (conv, gate, norms) is done by both.  The gated RMSNorm
+// needs the whole head output: each CTA reads the peer's 32 columns from
+// its shared memory (cluster barrier, read, cluster barrier).  SPLIT = 1 is
+// one CTA per head.
 constexpr int kRecurThreads = 256;
 constexpr int kRecurTB = 4;
 constexpr int kRankMax = 128;
@@ -1070,28 +1080,32 @@ LZ_HD void requant_2p(float buf, float iv, int8_t& h8, int8_t& l8, float& e) {
   e = __fadd_rn(hf, __fmul_rn((float)lq, 1.0f / kLoScale));
 }
 
-template <int NTH>
-__global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(const KdaArgs a) {
+template <int NTH, int SPLIT>
+LZ_HD void kda_layer(const KdaArgs& a) {
   pdl_trigger();
-  constexpr int KD = 64, VD = 64, TB = kRecurTB, NW = NTH / 32;
-  __shared__ __align__(16) int8_t hi[KD][VD];
-  __shared__ __align__(16) int8_t lo[KD][VD];
-  __shared__ __align__(16) float sc[KD][2];
-  __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], vcs[TB][VD], zs[TB][VD], OUT[TB][VD];
-  __shared__ __align__(16) float U[VD];
-  __shared__ float inv_q[TB], inv_k[TB], beta[TB], inv_o[TB];
+  constexpr int KD = 64, VD = 64, VC = VD / SPLIT, GPC = VC / 32, TB = kRecurTB, NW = NTH / 32;
+  static_assert(NTH >= 3 * KD && NTH >= TB * KD && NTH >= 2 * VC + TB, "thread roles");
+  static_assert(2 * NW >= 3 * TB, "norm chains per batch exceed the warps");
+  // f_a groups a warp stages, and the (g | b) values a thread stages
+  constexpr int FG = (TB * kRankMax / 32 + NW - 1) / NW;
+  constexpr int MI = (TB * (VC + 1) + NTH - 1) / NTH;
+  __shared__ __align__(16) int8_t hi[KD][VC];
+  __shared__ __align__(16) int8_t lo[KD][VC];
   // the state dequantised (hi + lo / 256, unscaled), refreshed right after
   // each requantisation
-  __shared__ __align__(16) float E[KD][VD];
-  // the batch's raw conv inputs and f_a rows, and the quantised f_a
-  __shared__ __align__(16) float RAW[TB][3 * KD];
-  __shared__ __align__(16) float FA[TB][kRankMax];
+  __shared__ __align__(16) float E[KD][VC];
+  __shared__ float sc[KD][GPC];
+  __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], KG[TB][KD], QG[TB][KD];
+  __shared__ __align__(16) float vcs[TB][VC], zs[TB][VC];
+  __shared__ __align__(16) float OUT[TB][VD];
+  __shared__ __align__(16) float U[VC], AW[VC];
+  __shared__ float inv_q[TB], inv_k[TB], beta[TB], braw[TB], kqs[TB], inv_o[TB];
   __shared__ __align__(16) int8_t LQ[TB][kRankMax];
   __shared__ float LS[TB][kRankMax / 32];
   // this head's f_b rows and their scales
   __shared__ __align__(16) int8_t FB[KD][kRankMax];
   __shared__ float FBS[KD][kRankMax / 32];
-  const int h = blockIdx.x;
+  const int h = blockIdx.x / SPLIT, grp = SPLIT == 1 ? 0 : (int)(blockIdx.x % SPLIT), vcol0 = grp * VC;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nsb = a.rank / 32, rbf = a.fb_gs / 32, ngf = a.rank / a.fb_gs;
   // weights do not change during a round: loaded before the wait on the
@@ -1116,68 +1130,106 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
   const size_t head_off = (size_t)a.layer_off_q + (size_t)h * KD * VD;
   const size_t seq_off = (size_t)sq.seq * a.seq_stride_q;
   float* cst0 = a.conv_state + (size_t)sq.seq * a.conv_seq_stride + (size_t)chan * 3;
-  float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
-  if (tid < 3 * KD) {
-    const float* st = cst0 + (size_t)sq.base_slot * a.conv_slot_stride;
-    c0 = st[0]; c1 = st[1]; c2 = st[2];
-  }
+  // a batch's rows, every load issued before the first store: the conv
+  // inputs of this thread's channel, whole 32-wide f_a groups per warp
+  // (quantised from registers), and the z (gate) and b values
+  float xr[TB], fa[FG], mi[MI];
+  auto issue = [&](int t0, int nt) {
+    if (tid < 3 * KD) {
+#pragma unroll
+      for (int t = 0; t < TB; t++)
+        if (t < nt) xr[t] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + chan];
+    }
+#pragma unroll
+    for (int i = 0; i < FG; i++) {
+      const int g = NW - 1 - warp + i * NW;
+      if (g < nt * nsb) {
+        const int t = g / nsb, gg = g - t * nsb;
+        fa[i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_fa + gg * 32 + lane];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < MI; i++) {
+      const int q = tid + i * NTH;
+      if (q < nt * VC) {
+        const int t = q / VC, c = q - t * VC;
+        mi[i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_g + h * VD + vcol0 + c];
+      } else if (q < nt * VC + nt) {
+        mi[i] = a.inproj[(size_t)(sq.row0 + t0 + q - nt * VC) * a.ldi + a.off_b + h];
+      }
+    }
+  };
+  // the state of this CTA's columns and the conv history, in flight with
+  // the first batch's rows
+  constexpr int SQ = KD * VC / 16;       // 16-byte pieces per plane
+  int4 sh = make_int4(0, 0, 0, 0), sl = sh;
+  float ssc = 0.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
   {
     const size_t off = seq_off + (size_t)sq.base_slot * a.slot_stride_q + head_off;
-    if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(&hi[0][0])[tid] = reinterpret_cast<const int4*>(a.st_hi + off)[tid];
-      reinterpret_cast<int4*>(&lo[0][0])[tid] = reinterpret_cast<const int4*>(a.st_lo + off)[tid];
+    if (tid < SQ) {
+      const int row = tid / (VC / 16), c16 = tid - row * (VC / 16);
+      const size_t o = off + (size_t)row * VD + vcol0 + c16 * 16;
+      sh = *reinterpret_cast<const int4*>(a.st_hi + o);
+      sl = *reinterpret_cast<const int4*>(a.st_lo + o);
     }
-    if (tid < KD * 2) (&sc[0][0])[tid] = a.st_sc[off / 32 + tid];
+    if (tid < KD * GPC) ssc = a.st_sc[off / 32 + (tid / GPC) * (VD / 32) + grp * GPC + tid % GPC];
+    if (tid < 3 * KD) {
+      const float* st = cst0 + (size_t)sq.base_slot * a.conv_slot_stride;
+      c0 = st[0]; c1 = st[1]; c2 = st[2];
+    }
   }
-  __syncthreads();
-  for (int q = tid; q < KD * VD; q += NTH) {
-    const int kk = q >> 6, vv = q & 63;
-    E[kk][vv] = __fadd_rn((float)hi[kk][vv], __fmul_rn((float)lo[kk][vv], 1.0f / kLoScale));
+  issue(0, min(TB, sq.nrows));
+  if (tid < SQ) {
+    const int row = tid / (VC / 16), c16 = tid - row * (VC / 16);
+    *reinterpret_cast<int4*>(&hi[row][c16 * 16]) = sh;
+    *reinterpret_cast<int4*>(&lo[row][c16 * 16]) = sl;
+    const int8_t* hb = reinterpret_cast<const int8_t*>(&sh);
+    const int8_t* lb = reinterpret_cast<const int8_t*>(&sl);
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      E[row][c16 * 16 + j] = __fadd_rn((float)hb[j], __fmul_rn((float)lb[j], 1.0f / kLoScale));
   }
+  if (tid < KD * GPC) sc[tid / GPC][tid % GPC] = ssc;
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
-    // stage the batch's raw rows: conv channels, g, f_a
-    for (int q = tid; q < nt * 3 * KD; q += NTH) {
-      const int t = q / (3 * KD), c = q - t * (3 * KD), pp = c >> 6, cc = c & 63;
-      const int ch = pp == 0 ? h * KD + cc : pp == 1 ? a.kdim + h * KD + cc : 2 * a.kdim + h * VD + cc;
-      RAW[t][c] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + ch];
+    if (t0 > 0) issue(t0, nt);
+#pragma unroll
+    for (int i = 0; i < MI; i++) {
+      const int q = tid + i * NTH;
+      if (q < nt * VC) zs[q / VC][q % VC] = mi[i];
+      else if (q < nt * VC + nt) braw[q - nt * VC] = mi[i];
     }
-    for (int q = tid; q < nt * VD; q += NTH) {
-      const int t = q >> 6, i = q & 63;
-      zs[t][i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_g + h * VD + i];
-    }
-    for (int q = tid; q < nt * a.rank; q += NTH) {
-      const int t = q / a.rank, i = q - t * a.rank;
-      FA[t][i] = a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_fa + i];
-    }
-    __syncthreads();
     // the conv1d of the batch (src/ops_conv1d.c:26-60), then SiLU
     if (tid < 3 * KD) {
-      float* dst = part == 0 ? &qn[0][0] : part == 1 ? &kn[0][0] : &vcs[0][0];
       for (int t = 0; t < nt; t++) {
-        const float xv = RAW[t][tid];
+        const float xv = xr[t];
         float sum = 0.0f;
         sum = __fadd_rn(sum, __fmul_rn(cwv.x, c0));
         sum = __fadd_rn(sum, __fmul_rn(cwv.y, c1));
         sum = __fadd_rn(sum, __fmul_rn(cwv.z, c2));
         sum = __fadd_rn(sum, __fmul_rn(cwv.w, xv));
-        dst[t * KD + ci] = silu(sum);
+        const float y = silu(sum);
+        if (part == 0) qn[t][ci] = y;
+        else if (part == 1) kn[t][ci] = y;
+        else if (ci >= vcol0 && ci < vcol0 + VC) vcs[t][ci - vcol0] = y;
         c0 = c1; c1 = c2; c2 = xv;
-        if (a.adv) {
+        if (a.adv && grp == 0) {
           float* d = cst0 + (size_t)((sq.base_slot + t0 + t + 1) % a.depth) * a.conv_slot_stride;
           d[0] = c0; d[1] = c1; d[2] = c2;
         }
       }
     }
-    // the f_a rows quantised per 32 (src/ops_quant.c:2152-2282), by the
-    // warps above the conv's
-    for (int g = NW - 1 - warp; g < nt * nsb; g += NW) {
-      const int t = g / nsb, gg = g - t * nsb;
-      LQ[t][gg * 32 + lane] = warp_quant32(FA[t][gg * 32 + lane], &LS[t][gg]);
+    // the f_a rows quantised per 32 (src/ops_quant.c:2152-2282)
+#pragma unroll
+    for (int i = 0; i < FG; i++) {
+      const int g = NW - 1 - warp + i * NW;
+      if (g < nt * nsb) {
+        const int t = g / nsb, gg = g - t * nsb;
+        LQ[t][gg * 32 + lane] = warp_quant32(fa[i], &LS[t][gg]);
+      }
     }
     __syncthreads();
     // the decay gate of this head's 64 keys: exp(lb sigmoid(exp(A) (f_b(f_a) + dt)))
-    static_assert(NTH >= TB * KD, "one gate per thread");
     if (tid < nt * KD) {
       const int t = tid >> 6, jj = tid & 63;
       const float* wsr = FBS[jj];
@@ -1196,55 +1248,64 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
       const float gg = __fmul_rn(a.lb, sigmoid(__fmul_rn(decay, pre)));
       gv[t][jj] = exp_body(gg);
     }
-    __syncthreads();
-    {                                          // 3 nt independent chains, two per warp
-      const int c = warp * 2 + (lane >> 4);
+    {                                          // 3 nt independent chains, two per warp, after the gate's warps
+      const int c = ((warp + NW - 2 * nt) % NW) * 2 + (lane >> 4);
       if ((lane & 15) == 0 && c < 3 * nt) {
         const int t = c % nt, which = c / nt;
         if (which == 0) inv_q[t] = rsqrt_body(__fadd_rn(seq_sumsq(qn[t], KD), kL2Eps));
         else if (which == 1) inv_k[t] = rsqrt_body(__fadd_rn(seq_sumsq(kn[t], KD), kL2Eps));
-        else beta[t] = sigmoid(a.inproj[(size_t)(sq.row0 + t0 + t) * a.ldi + a.off_b + h]);
+        else beta[t] = sigmoid(braw[t]);
       }
     }
-    static_assert(2 * (NTH / 32) >= 3 * kRecurTB, "chains per batch exceed the warps");
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += NTH) {
+    for (int q = tid; q < nt * KD; q += NTH) {
       const int t = q >> 6, i = q & 63;
-      qn[t][i] = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), a.ssm_scale);
-      kn[t][i] = __fmul_rn(kn[t][i], inv_k[t]);
+      const float qv = __fmul_rn(__fmul_rn(qn[t][i], inv_q[t]), a.ssm_scale);
+      const float kv = __fmul_rn(kn[t][i], inv_k[t]);
+      qn[t][i] = qv;
+      kn[t][i] = kv;
+      KG[t][i] = __fmul_rn(kv, gv[t][i]);
+      QG[t][i] = __fmul_rn(qv, gv[t][i]);
     }
     __syncthreads();
     for (int t = 0; t < nt; t++) {
-      // pass 1 on threads vv < 64, three independent sequential chains over
-      // the 64 state rows, each in the reference's order: u = S^T (g.k)
-      // and w = S^T (g.q) of column vv (their scale products sc * (k|q * g)
-      // formed in place), and kq = k.q; then u = (v - u) * beta and the
-      // head output w + u * kq, all in this thread
-      if (tid < VD) {
-        const int vv = tid, grp = vv >> 5;
-        float au = 0.0f, aw = 0.0f, kq = 0.0f;
+      // pass 1: one sequential chain over the 64 state rows per thread, in
+      // the reference's order: u = S^T (g.k) on threads c < VC, w = S^T
+      // (g.q) on threads VC + c; u = (v - u) * beta.  The batch's k.q
+      // chains run beside the first token's.
+      if (tid < 2 * VC) {
+        const bool isw = tid >= VC;
+        const int c = isw ? tid - VC : tid, gl = c >> 5;
+        const float* G = isw ? QG[t] : KG[t];
+        float acc = 0.0f;
 #pragma unroll 8
-        for (int kk = 0; kk < KD; kk++) {
-          const float g = gv[t][kk], sck = sc[kk][grp], e = E[kk][vv], k_ = kn[t][kk], q_ = qn[t][kk];
-          au = __fadd_rn(au, __fmul_rn(e, __fmul_rn(sck, __fmul_rn(k_, g))));
-          aw = __fadd_rn(aw, __fmul_rn(e, __fmul_rn(sck, __fmul_rn(q_, g))));
-          kq = __fadd_rn(kq, __fmul_rn(k_, q_));
-        }
-        const float u = __fmul_rn(__fsub_rn(vcs[t][vv], au), beta[t]);
-        U[vv] = u;
-        OUT[t][vv] = __fadd_rn(aw, __fmul_rn(u, kq));
+        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, __fmul_rn(E[kk][c], __fmul_rn(sc[kk][gl], G[kk])));
+        if (isw) AW[c] = acc;
+        else U[c] = __fmul_rn(__fsub_rn(vcs[t][c], acc), beta[t]);
+      } else if (t == 0 && tid < 2 * VC + nt) {
+        const int tt = tid - 2 * VC;
+        float kq = 0.0f;
+#pragma unroll 8
+        for (int kk = 0; kk < KD; kk++) kq = __fadd_rn(kq, __fmul_rn(kn[tt][kk], qn[tt][kk]));
+        kqs[tt] = kq;
       }
       __syncthreads();
-      // pass 2: the 128 (state row, 32-wide group) units, four per warp at
-      // a time with their max reductions interleaved
-      for (int u0 = warp * 4; u0 < KD * 2; u0 += NW * 4) {
+      // the head output w + u * kq of this CTA's columns
+      if (tid < VC) OUT[t][vcol0 + tid] = __fadd_rn(AW[tid], __fmul_rn(U[tid], kqs[t]));
+      // pass 2: the (state row, 32-wide group) units, four per warp at a
+      // time with their max reductions interleaved; a verify step writes
+      // its ring slot straight from here
+      const size_t ring = a.adv ? seq_off + (size_t)((sq.base_slot + t0 + t + 1) % a.depth) * a.slot_stride_q +
+                                      head_off
+                                : 0;
+      for (int u0 = warp * 4; u0 < KD * GPC; u0 += NW * 4) {
         float buf[4];
         uint32_t am[4];
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
-          const float scg = __fmul_rn(sc[kk][grp], gv[t][kk]);   // sc * g, before this unit's scale is replaced
-          buf[c] = __fadd_rn(__fmul_rn(E[kk][vv], scg), __fmul_rn(kn[t][kk], U[vv]));
+          const int unit = u0 + c, kk = unit / GPC, gl = unit % GPC, col = gl * 32 + lane;
+          const float scg = __fmul_rn(sc[kk][gl], gv[t][kk]);   // sc * g, before this unit's scale is replaced
+          buf[c] = __fadd_rn(__fmul_rn(E[kk][col], scg), __fmul_rn(kn[t][kk], U[col]));
           am[c] = abs_bits(buf[c]);
         }
 #pragma unroll
@@ -1254,52 +1315,74 @@ __global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(cons
         q8_scale_from_amax(lane == 1 ? am[1] : lane == 2 ? am[2] : lane == 3 ? am[3] : am[0], &sg4, &iv4);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          const int unit = u0 + c, kk = unit >> 1, grp = unit & 1, vv = grp * 32 + lane;
+          const int unit = u0 + c, kk = unit / GPC, gl = unit % GPC, col = gl * 32 + lane;
           const float sg = __shfl_sync(0xffffffffu, sg4, c), iv = __shfl_sync(0xffffffffu, iv4, c);
           int8_t h8, l8;
           float e;
           requant_2p(buf[c], iv, h8, l8, e);
-          hi[kk][vv] = h8;
-          lo[kk][vv] = l8;
-          E[kk][vv] = e;
-          if (lane == 0) sc[kk][grp] = sg;
+          E[kk][col] = e;
+          if (lane == 0) sc[kk][gl] = sg;
+          if (a.adv) {
+            const size_t o = ring + (size_t)kk * VD + vcol0 + col;
+            a.st_hi[o] = h8;
+            a.st_lo[o] = l8;
+            if (lane == 0) a.st_sc[ring / 32 + kk * (VD / 32) + grp * GPC + gl] = sg;
+          } else {
+            hi[kk][col] = h8;
+            lo[kk][col] = l8;
+          }
         }
       }
       __syncthreads();
-      if (a.adv) {
-        const int so = (sq.base_slot + t0 + t + 1) % a.depth;
-        const size_t off = seq_off + (size_t)so * a.slot_stride_q + head_off;
-        if (tid < KD * VD / 16) {
-          reinterpret_cast<int4*>(a.st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-          reinterpret_cast<int4*>(a.st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
-        }
-        if (tid < KD * 2) a.st_sc[off / 32 + tid] = (&sc[0][0])[tid];
+    }
+    // the other CTA's half of every token's head output
+    if (SPLIT > 1) {
+      cluster_barrier();
+      const int pc0 = (grp ^ 1) * VC;
+      for (int q = tid; q < nt * VC; q += NTH) {
+        const int t = q / VC, c = q - t * VC;
+        OUT[t][pc0 + c] = ld_peer_f32(&OUT[t][pc0 + c], (uint32_t)(grp ^ 1));
       }
+      cluster_barrier();
     }
     // gated RMSNorm of every token's head output, then per-32 quantisation
     if (lane == 0 && warp < nt)
       inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), a.eps));
     __syncthreads();
-    for (int q = tid; q < nt * 64; q += NTH) {
-      const int t = q >> 6, i = q & 63;
+    for (int q = tid; q < nt * VC; q += NTH) {
+      const int t = q / VC, c = q - t * VC, i = vcol0 + c;
       const size_t r = (size_t)(sq.row0 + t0 + t);
-      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), a.o_norm[i]), silu(zs[t][i]));
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), a.o_norm[i]), silu(zs[t][c]));
       a.oq[r * a.vdim + h * VD + i] = warp_quant32(o, &a.os[r * (a.vdim / 32) + (h * VD) / 32 + (i >> 5)]);
     }
     __syncthreads();
   }
   if (!a.adv) {
     const size_t off = seq_off + (size_t)sq.base_slot * a.slot_stride_q + head_off;
-    if (tid < KD * VD / 16) {
-      reinterpret_cast<int4*>(a.st_hi + off)[tid] = reinterpret_cast<const int4*>(&hi[0][0])[tid];
-      reinterpret_cast<int4*>(a.st_lo + off)[tid] = reinterpret_cast<const int4*>(&lo[0][0])[tid];
+    if (tid < SQ) {
+      const int row = tid / (VC / 16), c16 = tid - row * (VC / 16);
+      const size_t o = off + (size_t)row * VD + vcol0 + c16 * 16;
+      *reinterpret_cast<int4*>(a.st_hi + o) = *reinterpret_cast<const int4*>(&hi[row][c16 * 16]);
+      *reinterpret_cast<int4*>(a.st_lo + o) = *reinterpret_cast<const int4*>(&lo[row][c16 * 16]);
     }
-    if (tid < KD * 2) a.st_sc[off / 32 + tid] = (&sc[0][0])[tid];
-    if (tid < 3 * KD) {
+    if (tid < KD * GPC) a.st_sc[off / 32 + (tid / GPC) * (VD / 32) + grp * GPC + tid % GPC] = sc[tid / GPC][tid % GPC];
+    if (tid < 3 * KD && grp == 0) {
       float* d = cst0 + (size_t)sq.base_slot * a.conv_slot_stride;
       d[0] = c0; d[1] = c1; d[2] = c2;
     }
   }
+}
+
+// One CTA per (head, sequence).
+template <int NTH>
+__global__ void __launch_bounds__(NTH, NTH == 256 ? 4 : 2) kda_recur_kernel(const KdaArgs a) {
+  kda_layer<NTH, 1>(a);
+}
+
+// Two CTAs per (head, sequence), one per value group (grid x = 2 * heads).
+template <int NTH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTH, 1) kda_recur_split_kernel(const KdaArgs a) {
+  kda_layer<NTH, 2>(a);
 }
 
 // ---------------------------------------------------------------- MoE
