@@ -47,10 +47,10 @@ MAX_NEW = 256
 SPEC_K = 2
 
 
-def model_dir() -> str:
+def model_dir(name: str = MODEL) -> str:
     import lz98_synth
-    d = os.path.join(os.environ.get("LZ98_MODEL_DIR", os.path.join(tempfile.gettempdir(), "lz98_models")), MODEL)
-    lz98_synth.write_model(lz98_synth.CONFIGS[MODEL], d)
+    d = os.path.join(os.environ.get("LZ98_MODEL_DIR", os.path.join(tempfile.gettempdir(), "lz98_models")), name)
+    lz98_synth.write_model(lz98_synth.CONFIGS[name], d)
     return d
 
 
@@ -321,6 +321,115 @@ def run_batch32(m, args, rank: int, world: int):
         "gpu_launches": prof["n_kernels"] * steps,
         "clocks": clk,
     }
+
+
+N3B, P3B, K3B, NEW3B = 8, 8192, 3, 256     # configs[3]: sequences per GPU, prompt, draft depth, new tokens
+
+
+def run_3b(args):
+    """BASELINE configs[3] (--config 3b): the ~3B model, 8 sequences per
+    GPU with 8192-token uniform prompts prefilled in row-capacity chunks
+    (device-timed: prefill tokens/s), then greedy k = 3 rounds of all 8
+    (CUDA graph replay, device-timed), and an end-to-end pass through
+    lz_spec_round_batch that reads the tokens back."""
+    import torch
+    import torch.distributed as dist
+    import lz98
+    import lz98_synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    cfg = lz98_synth.CONFIGS["3b"]
+    if world > 1 and rank != 0:
+        dist.barrier()
+    d = model_dir("3b")
+    if world > 1 and rank == 0:
+        dist.barrier()
+    m = lz98.Model(d)
+    e2e_steps = 4
+    steps = max(1, min(args.steps, NEW3B - args.warmup - e2e_steps - 2))
+    s = lz98.State(m, P3B + (K3B + 1) * (args.warmup + steps + e2e_steps + 2) + 64, K3B, n_seq=N3B)
+    prompts = lz98_synth.uniform_prompts(cfg, N3B, P3B, rank)
+    stream = torch.cuda.ExternalStream(s.stream())
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    t0 = time.time()
+    for b, p in enumerate(prompts):
+        s.seq_prefill(b, p)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_wall = time.time() - t0
+    prefill_ms = p0.elapsed_time(p1)
+    for _ in range(args.warmup):
+        s.round_batch(K3B, fetch=False)
+    torch.cuda.synchronize()
+    c0 = [s.counters(b) for b in range(N3B)]
+    clocks = Clocks(physical_gpu(local), gpu_uuid(local))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        s.round_batch(K3B, fetch=False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    c1 = [s.counters(b) for b in range(N3B)]
+    emitted = sum(c1[b][1] - c0[b][1] for b in range(N3B))
+    accepted = sum(c1[b][2] - c0[b][2] for b in range(N3B))
+    drafted = sum(c1[b][3] - c0[b][3] for b in range(N3B))
+    rounds = sum(c1[b][0] - c0[b][0] for b in range(N3B))
+    torch.cuda.synchronize()
+    t_e = time.perf_counter()
+    n_e = 0
+    for _ in range(e2e_steps):
+        toks, cnt = s.round_batch(K3B, fetch=True)
+        n_e += int(cnt.sum())
+    dt_e = time.perf_counter() - t_e
+    prof = s.profile_round(K3B)
+    rb = round_bytes(m, N3B * (K3B + 1), K3B, N3B)
+    s.close()
+    ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), n_e / dt_e, world, "cuda")
+    pf_max, pf_tok, _ = reduce_over_ranks(prefill_ms, float(N3B * P3B), None, world, "cuda")
+    peak, peak_kind = measured_peak()
+    if rank == 0:
+        gemv_gbs = prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": emitted_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights/activations, int32 dot, f32 epilogue",
+            "data": "synthetic: random-init weights N(0,0.02)->bf16->Q8_0, uniform prompt ids",
+            "config": {"workload": "configs[3]: ~3B KunMoe, 8 sequences per GPU, 8192-token prompts "
+                                   "(chunked prefill), greedy, k=3",
+                       "model": "KunMoe-3B-synthetic", "global_batch": N3B * world, "seq_len": P3B,
+                       "new_tokens_budget": NEW3B, "spec_k": K3B, "parallelism": f"dp{world} (replicas)",
+                       "l2": "no flush: per-round weight stream >> 126 MB L2"},
+            "prefill": {"tokens_per_s": pf_tok / (pf_max * 1e-3), "ms": pf_max, "wall_s": prefill_wall,
+                        "tokens": pf_tok},
+            "mean_accept_len": (accepted + rounds) / max(1, rounds), "alpha": accepted / max(1, drafted),
+            "hbm_gbs_round": rb / (ms / steps * 1e-3) / 1e9,
+            "roofline": _expert_roofline(prof) or {
+                "bound": "hbm", "kernel": "gemv_q8_kernel", "achieved": gemv_gbs, "peak": peak, "unit": "GB/s",
+                "frac": gemv_gbs / peak, "peak_kind": peak_kind, "traffic": None},
+            "e2e": {"value": e2e_all, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": N3B * (K3B + 1) * 4 + N3B * 4,
+                    "api": "lz_spec_round_batch (round state device-resident, tokens and counts read back)"},
+            "gpu_launches": prof["n_kernels"] * steps, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_ours(args):
@@ -704,6 +813,9 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="0p5b", choices=["0p5b", "3b"],
+                    help="0p5b: the headline (configs[1]) with the batch-32 workload (configs[2]); "
+                         "3b: configs[3], 8 x 8192-token chunked prefill then greedy k=3")
     ap.add_argument("--seqs", type=int, default=1, help="sequences per GPU")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--b32-cpu-seconds", type=float, default=10.0)
@@ -719,6 +831,8 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "3b":
+        run_3b(args)
     else:
         run_ours(args)
 

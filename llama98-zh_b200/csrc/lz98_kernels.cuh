@@ -1825,7 +1825,7 @@ struct MoeTma {
   static constexpr int NST = W13 ? 2 : 3;          // w13: two stages let 3 blocks fit per SM (measured faster)
   static constexpr int B = NBOX * BOX * 128;        // swizzled weight tile per stage
   static constexpr int WS = RB1 ? NBOX * BOX * 16 : 0;
-  static constexpr int KMAX = 1024;
+  static constexpr int KMAX = 2048;
   // bytes of dynamic shared memory for inner dimension K
   static size_t smem(int K) { return 1024 + (size_t)NST * (B + WS) + 8 * (size_t)K + 8 * (K / 32) * 4 + 2 * NST * 8; }
 };

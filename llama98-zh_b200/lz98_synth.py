@@ -97,7 +97,8 @@ class KunMoeConfig:
 
 # The BASELINE configurations this path is measured on (weights seed = config
 # index).  "tiny" is the reference's CPU-runnable case; "0p5b" is the ~0.5B
-# model of the batch-1 and batch-32 workloads.
+# model of the batch-1 and batch-32 workloads; "3b" the ~3B model of the
+# 8 x 8192-token chunked-prefill workload.
 CONFIGS = {
     "tiny": KunMoeConfig(name="tiny", hidden=256, n_layers=4, kda_heads=4,
                          vocab=8192, n_experts=8, top_k=2, latent=128,
@@ -107,6 +108,12 @@ CONFIGS = {
                          vocab=64000, n_experts=64, top_k=4, latent=512,
                          moe_ffn=1024, shared_width=1024, seq_len=2048,
                          gs_mode="row", seed=1),
+    # the ~3B model (no shared expert; the context covers the
+    # workload's 8192-token prompts plus the new tokens).
+    "3b": KunMoeConfig(name="3b", hidden=2048, n_layers=32, kda_heads=32,
+                       vocab=128000, n_experts=128, top_k=8, latent=768,
+                       moe_ffn=1536, shared_width=0, seq_len=16384,
+                       gs_mode="row", seed=3),
     # Small shapes of the 0p5b family for fast parity tests.
     "mini": KunMoeConfig(name="mini", hidden=128, n_layers=2, kda_heads=2,
                          vocab=1024, n_experts=8, top_k=4, latent=64,
@@ -376,3 +383,14 @@ def workload_prompts(cfg: KunMoeConfig, n_seq: int, lo: int, hi: int,
             ids = (rng.zipf(zipf, size=n) - 1) % cfg.vocab
         prompts.append([int(x) for x in ids])
     return prompts
+
+
+def uniform_prompts(cfg: KunMoeConfig, n_seq: int, length: int, rank: int = 0):
+    """The configs[3] workload's prompts: n_seq prompts of `length` token
+    ids uniform over the vocabulary, sequence s of rank r drawn from
+    default_rng([cfg.seed, 1000 + 100000 r + s])."""
+    out = []
+    for s in range(n_seq):
+        rng = np.random.default_rng([cfg.seed, 1000 + 100000 * rank + s])
+        out.append(rng.integers(0, cfg.vocab, length).astype(np.int32))
+    return out

@@ -34,7 +34,15 @@ CASES = {
 # max_new, [(k, temperature), ...])
 TOKEN_CASES = {
     "0p5b": (12, 12, [(0, 0.0), (2, 0.0), (2, 0.8), (3, 0.8)]),
+    "3b": (12, 16, [(3, 0.0), (0, 0.0)]),
 }
+
+
+# configs[3] at its own prompt length: the first sequence of the workload
+# (lz98_synth.uniform_prompts(cfg, 8, 8192)), its whole 8192-token prompt
+# through the reference's chunked prefill, then greedy k = 3 rounds.
+LONG_3B_PROMPT = 8192
+LONG_3B_NEW = 16
 
 
 # The benchmarked workloads themselves (bench.py), on the ~0.5B config:
@@ -188,6 +196,23 @@ def make_bench():
     print(path, os.path.getsize(path))
 
 
+def make_3b_long():
+    """tests/golden/3b_long.npz (about an hour of reference prefill)."""
+    d = model_dir("3b")
+    cfg = lz98_synth.CONFIGS["3b"]
+    sha = lz98_synth.write_model(cfg, d)
+    prompt = lz98_synth.uniform_prompts(cfg, 8, LONG_3B_PROMPT)[0]
+    R = Reference(d, LONG_3B_PROMPT + LONG_3B_NEW + 64, 4)
+    toks, rounds = R.generate(prompt, LONG_3B_NEW, 3)
+    out = {"sha256": np.frombuffer(bytes.fromhex(sha), np.uint8), "prompt_len": np.array([LONG_3B_PROMPT], np.int32),
+           "max_new": np.array([LONG_3B_NEW], np.int32), "tokens": toks, "rounds": rounds,
+           "prefill_ms": np.array([R.last_prefill_ms])}
+    R.close()
+    path = os.path.join(HERE, "3b_long.npz")
+    np.savez_compressed(path, **out)
+    print(path, os.path.getsize(path))
+
+
 def make_debug():
     """tests/golden/round_debug.npz: generations of the reference with its
     rounds' debug_break_rollback / debug_skip_catchup switches on (the
@@ -214,6 +239,8 @@ if __name__ == "__main__":
             make_bench()
         elif n == "debug":
             make_debug()
+        elif n == "3b_long":
+            make_3b_long()
         elif n in TOKEN_CASES:
             make_tokens(n)
         else:

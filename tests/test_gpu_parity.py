@@ -322,3 +322,73 @@ def test_umma_and_mma_sync_gemms_agree(gcase):
             streams.append(out)
             s.close()
         assert streams[0] == streams[1], temp
+
+
+def _3b_model():
+    import lz98_synth
+    from conftest import model_dir
+    d = model_dir("3b")
+    sha = lz98_synth.write_model(lz98_synth.CONFIGS["3b"], d)
+    return d, sha
+
+
+def test_3b_config_token_identical():
+    """configs[3], the ~3B model (d 2048, 32 layers, 32 KDA heads, 128
+    experts top-8, latent 768, expert FFN 1536, vocabulary 128000): the
+    device generations reproduce the reference's token streams and round
+    records, greedy k = 3 and plain decode."""
+    import lz98
+    d, sha = _3b_model()
+    g = dict(np.load(os.path.join(GOLDEN, "3b.npz")))
+    assert bytes(g["sha256"]).hex() == sha
+    m = lz98.Model(d)
+    s = lz98.State(m, 512, 4)
+    try:
+        for j, (k, temp) in enumerate(g["runs"]):
+            toks, rounds = s.generate(g["prompt"], int(g["max_new"][0]), int(k), temp=float(temp), topp=0.95,
+                                      seed=1234)
+            assert np.array_equal(toks, g[f"run{j}_tokens"]), (j, k, temp)
+            assert np.array_equal(rounds, g[f"run{j}_rounds"]), (j, k, temp)
+    finally:
+        s.close()
+        m.close()
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(GOLDEN, "3b_long.npz")), reason="3b_long fixture not generated")
+def test_3b_workload_chunked_prefill_token_identical():
+    """configs[3]'s own workload shape: 8 sequences with 8192-token prompts
+    prefilled in row-capacity chunks inside one 8-sequence state, then
+    greedy k = 3 rounds of all 8 together; the first sequence's stream and
+    round records equal the reference's (its whole prompt through the
+    reference's chunked prefill)."""
+    import lz98
+    import lz98_synth
+    d, sha = _3b_model()
+    g = dict(np.load(os.path.join(GOLDEN, "3b_long.npz")))
+    assert bytes(g["sha256"]).hex() == sha
+    cfg = lz98_synth.CONFIGS["3b"]
+    n_prompt, max_new = int(g["prompt_len"][0]), int(g["max_new"][0])
+    prompts = lz98_synth.uniform_prompts(cfg, 8, n_prompt)
+    m = lz98.Model(d)
+    s = lz98.State(m, n_prompt + max_new + 64, 3, n_seq=8)
+    try:
+        emitted = [s.seq_prefill(b, p) for b, p in enumerate(prompts)]
+        emitted = [[int(a)] for a in emitted]
+        recs = []
+        want_t, want_r = g["tokens"], g["rounds"]
+        full = 0
+        while full < len(want_r) and want_r[full][0] == 3:
+            full += 1
+        assert full >= 2, full
+        for _ in range(full):
+            toks, cnt = s.round_batch(3)
+            for b in range(8):
+                emitted[b].extend(toks[b, :cnt[b]].tolist())
+            recs.append((3, int(cnt[0]) - 1))
+        # every round the reference ran at full depth, and the tokens they emitted
+        assert recs == [tuple(r) for r in want_r[:full].tolist()]
+        n_tok = 1 + sum(int(r[1]) + 1 for r in want_r[:full])
+        assert emitted[0][:n_tok] == want_t[:n_tok].tolist()
+    finally:
+        s.close()
+        m.close()
