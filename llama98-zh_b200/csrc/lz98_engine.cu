@@ -1383,9 +1383,16 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
     if (R <= kPrologueRows && !s->ep.comm) {
       // few rows: router fused into the per-pair w1/w3 kernel, then w2 with
       // the last-block combine
-      launch(s, moe_route_w13_kernel, dim3(c.moe_ffn / 32, P), dim3(256), 0, s->moein, m->n_moe, m->off_router,
-             m->off_down, L.router_bias, c.ne, c.topk, L.w13q, L.w13s, c.moe_ffn, c.latent, L.w13_gs, s->pair_e,
-             s->pair_w, s->hq, s->hs, m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
+      // latent <= 512: 16 lanes per weight row, 64 FFN outputs per block
+      // (one wave of blocks at batch 1); else 32 lanes, 32 outputs
+      if (c.latent <= 512 && c.moe_ffn % 64 == 0)
+        launch(s, moe_route_w13_kernel<16>, dim3(c.moe_ffn / 64, P), dim3(256), 0, s->moein, m->n_moe,
+               m->off_router, m->off_down, L.router_bias, c.ne, c.topk, L.w13q, L.w13s, c.moe_ffn, c.latent,
+               L.w13_gs, s->pair_e, s->pair_w, s->hq, s->hs, m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
+      else
+        launch(s, moe_route_w13_kernel<32>, dim3(c.moe_ffn / 32, P), dim3(256), 0, s->moein, m->n_moe,
+               m->off_router, m->off_down, L.router_bias, c.ne, c.topk, L.w13q, L.w13s, c.moe_ffn, c.latent,
+               L.w13_gs, s->pair_e, s->pair_w, s->hq, s->hs, m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
       launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, P), dim3(256), 0, L.w2q, L.w2s, c.moe_ffn, c.latent,
              L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2, s->row_counter, s->yq, s->ys);
     } else {

@@ -1481,20 +1481,26 @@ __global__ void moe_route_kernel(const float* __restrict__ moein, int ldm, int o
 // warps quantise the row's latent per 32 into shared memory; blocks of
 // chunk 0 store the row's experts and weights for w2 and the combine;
 // blocks of the row's first pair quantise their share of the shared
-// expert's silu(gate) * up.  Then 32 consecutive FFN outputs of w1 and of
-// w3: int8 GEMV over the latent, silu(w1.x) * (w3.x), the per-32
-// quantisation of that group (src/forward_moe.c:189-196).  w13 is the
-// expert's [w1 rows; w3 rows] ([2 ffn][latent]); latent <= 1024.
+// expert's silu(gate) * up.  Then FC = 64 * 16 / LPR consecutive FFN
+// outputs of w1 and of w3: int8 GEMV over the latent with LPR lanes per
+// weight row (LPR = 16 for latent <= 512: two rows per warp at a time),
+// silu(w1.x) * (w3.x), the per-32 quantisation of each group
+// (src/forward_moe.c:189-196).  w13 is the expert's [w1 rows; w3 rows]
+// ([2 ffn][latent]); latent <= 32 * LPR.
+template <int LPR>
 __global__ void __launch_bounds__(256)
 moe_route_w13_kernel(const float* __restrict__ moein, int ldm, int off_router, int off_lat,
                      const float* __restrict__ bias, int E, int topk,
                      const int8_t* __restrict__ w13q, const float* __restrict__ w13s, int ffn, int latent, int gs,
                      int* pair_expert, float* pair_w, int8_t* hq, float* hs,
                      int off_shg, int off_shu, int sw, int8_t* shq, float* shs) {
+  constexpr int RPI = 32 / LPR;             // weight rows per warp per step
+  constexpr int RW = 8 * RPI;               // weight rows per warp
+  constexpr int FC = 8 * RW / 2;            // FFN outputs per block
   pdl_trigger();
   pdl_wait();
-  __shared__ __align__(16) float P[8][8][32];
-  __shared__ float H[64];
+  __shared__ __align__(16) float P[8][RW][LPR];
+  __shared__ float H[2 * FC];
   __shared__ __align__(16) int8_t lq[1024];
   __shared__ float ls[32];
   __shared__ int s_e[16];
@@ -1535,43 +1541,44 @@ moe_route_w13_kernel(const float* __restrict__ moein, int ldm, int off_router, i
   const int rb = gs / 32, ng = latent / gs;
   const size_t wbase = (size_t)e * 2 * ffn * latent;
   const size_t sbase = (size_t)e * 2 * ffn * ng;
+  const int sb = lane % LPR, half = lane / LPR;
+  // local weight row lr < FC: w1 row chunk*FC + lr; else w3 row ffn + chunk*FC + lr - FC
+  auto orow_of = [&](int lr) { return lr < FC ? blockIdx.x * FC + lr : ffn + blockIdx.x * FC + (lr - FC); };
   int4 xa = make_int4(0, 0, 0, 0), xb = xa;
   float xsv = 0.0f;
-  if (lane < nsb) {
-    xa = *reinterpret_cast<const int4*>(lq + lane * 32);
-    xb = *reinterpret_cast<const int4*>(lq + lane * 32 + 16);
-    xsv = ls[lane];
+  if (sb < nsb) {
+    xa = *reinterpret_cast<const int4*>(lq + sb * 32);
+    xb = *reinterpret_cast<const int4*>(lq + sb * 32 + 16);
+    xsv = ls[sb];
   }
   int4 wa[8], wb[8];
   float wsv[8];
 #pragma unroll
   for (int k = 0; k < 8; k++) {
-    const int lr = warp * 8 + k;
-    const int orow = (lr < 32) ? blockIdx.x * 32 + lr : ffn + blockIdx.x * 32 + (lr - 32);
-    if (lane < nsb) {
+    const int orow = orow_of(warp * RW + k * RPI + half);
+    if (sb < nsb) {
       const int8_t* wr = w13q + wbase + (size_t)orow * latent;
-      wa[k] = __ldg(reinterpret_cast<const int4*>(wr + lane * 32));
-      wb[k] = __ldg(reinterpret_cast<const int4*>(wr + lane * 32 + 16));
-      wsv[k] = rb == 1 ? __ldg(w13s + sbase + (size_t)orow * ng + lane) : 0.0f;
+      wa[k] = __ldg(reinterpret_cast<const int4*>(wr + sb * 32));
+      wb[k] = __ldg(reinterpret_cast<const int4*>(wr + sb * 32 + 16));
+      wsv[k] = rb == 1 ? __ldg(w13s + sbase + (size_t)orow * ng + sb) : 0.0f;
     }
   }
 #pragma unroll
   for (int k = 0; k < 8; k++)
-    if (lane < nsb) {
+    if (sb < nsb) {
       const float a = (float)dot32(wa[k], wb[k], xa, xb);
-      P[warp][k][lane] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[k]));
+      P[warp][k * RPI + half][sb] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[k]));
     }
   __syncwarp();
-  if (lane < 8) {
-    const int lr = warp * 8 + lane;
-    const int orow = (lr < 32) ? blockIdx.x * 32 + lr : ffn + blockIdx.x * 32 + (lr - 32);
-    H[lr] = q8_reduce(P[warp][lane], w13s + sbase + (size_t)orow * ng, rb, ng);
+  if (lane < RW) {
+    const int lr = warp * RW + lane;
+    H[lr] = q8_reduce(P[warp][lane], w13s + sbase + (size_t)orow_of(lr) * ng, rb, ng);
   }
   __syncthreads();
-  if (warp == 0) {
-    const float a = __fmul_rn(silu(H[lane]), H[32 + lane]);
-    const int i = blockIdx.x * 32 + lane;
-    hq[(size_t)p * ffn + i] = warp_quant32(a, &hs[(size_t)p * (ffn / 32) + blockIdx.x]);
+  if (warp < FC / 32) {
+    const int j = warp * 32 + lane;
+    const float a = __fmul_rn(silu(H[j]), H[FC + j]);
+    hq[(size_t)p * ffn + blockIdx.x * FC + j] = warp_quant32(a, &hs[(size_t)p * (ffn / 32) + blockIdx.x * (FC / 32) + warp]);
   }
 }
 
