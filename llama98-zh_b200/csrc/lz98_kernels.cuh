@@ -96,13 +96,15 @@ LZ_HD float q8_reduce(const float* p, const float* wsr, int rb, int ng) {
   return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
 }
 
+// The exact int32 dot product of a 32-element sub-block: two independent
+// __dp4a chains (its dependent latency is ~13 cycles here) joined by one
+// add; integer sums are exact in any order.
 LZ_HD int dot32(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
-  int acc = 0;
-  acc = __dp4a(wa.x, xa.x, acc); acc = __dp4a(wa.y, xa.y, acc);
-  acc = __dp4a(wa.z, xa.z, acc); acc = __dp4a(wa.w, xa.w, acc);
-  acc = __dp4a(wb.x, xb.x, acc); acc = __dp4a(wb.y, xb.y, acc);
-  acc = __dp4a(wb.z, xb.z, acc); acc = __dp4a(wb.w, xb.w, acc);
-  return acc;
+  int a0 = __dp4a(wa.x, xa.x, 0), a1 = __dp4a(wb.x, xb.x, 0);
+  a0 = __dp4a(wa.y, xa.y, a0); a1 = __dp4a(wb.y, xb.y, a1);
+  a0 = __dp4a(wa.z, xa.z, a0); a1 = __dp4a(wb.z, xb.z, a1);
+  a0 = __dp4a(wa.w, xa.w, a0); a1 = __dp4a(wb.w, xb.w, a1);
+  return a0 + a1;
 }
 
 struct GemvArgs {
@@ -167,18 +169,21 @@ LZ_HD void load_wrow(WRow<JM>& w, const int8_t* __restrict__ wr, const float* __
   }
 }
 
-// Products of one weight row with every token row for the sub-blocks this
-// lane owns; P[rr][s] receives the product fed to the reference reduction.
-// The quantised rows are read from shared memory (SH) or global memory.
-template <int JM, bool SH, int RB>
-LZ_HD void gemv_products(const WRow<JM>& w, int K, int rb, const int8_t* xq, const float* xs, int r0, int nr,
-                         float (*P)[JM * 32], int lane) {
+// Products of NR weight rows (the first nvalid of them) with every token
+// row for this lane's sub-blocks: every activation load and every product
+// comes before the first store to P, so the stores (which may alias the
+// activations in shared memory) never stall the next loads.
+// P[i * nr + rr][s] receives the product of weight row i and token row rr.
+template <int JM, bool SH, int RB, int NR>
+LZ_HD void gemv_products_nr(const WRow<JM> (&w)[NR], int nvalid, int K, int rb, const int8_t* xq, const float* xs,
+                            int nr, float (*P)[JM * 32], int lane) {
   const int nsb = K >> 5;
+  float pr[RB][NR][JM];
 #pragma unroll
   for (int rr = 0; rr < RB; rr++) {
     if (rr < nr) {
-      const int8_t* xr = xq + (size_t)(r0 + rr) * K;
-      const float* xsr = xs + (size_t)(r0 + rr) * nsb;
+      const int8_t* xr = xq + (size_t)rr * K;
+      const float* xsr = xs + (size_t)rr * nsb;
 #pragma unroll
       for (int j = 0; j < JM; j++) {
         const int s = lane + 32 * j;
@@ -194,12 +199,24 @@ LZ_HD void gemv_products(const WRow<JM>& w, int K, int rb, const int8_t* xq, con
             xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
             xsv = __ldg(xsr + s);
           }
-          const float a = (float)dot32(w.a[j], w.b[j], xa, xb);
-          P[rr][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, w.s[j]));
+#pragma unroll
+          for (int i = 0; i < NR; i++) {
+            const float a = (float)dot32(w[i].a[j], w[i].b[j], xa, xb);
+            pr[rr][i][j] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, w[i].s[j]));
+          }
         }
       }
     }
   }
+#pragma unroll
+  for (int rr = 0; rr < RB; rr++)
+#pragma unroll
+    for (int i = 0; i < NR; i++)
+#pragma unroll
+      for (int j = 0; j < JM; j++) {
+        const int s = lane + 32 * j;
+        if (rr < nr && i < nvalid && s < nsb) P[i * nr + rr][s] = pr[rr][i][j];
+      }
 }
 
 // Weight rows a warp takes per step on the multi-row path.
@@ -232,16 +249,28 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
     }
     const float* wsr = a.ws + (size_t)n * ng;
     const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
+    // the output row's scales (one per row) for the reducing lanes
+    const float s1 = (rb > 1 && ng == 1) ? __ldg(wsr) : 0.0f;
+    const float s2 = (a.W2 && rb2 > 1 && ng2 == 1) ? __ldg(wsr2) : 0.0f;
     for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
       const int nr = min(kGemvRB, a.R - r0);
-      gemv_products<JM, SH, kGemvRB>(w1, a.K, rb, xq, xs, r0, nr, P, lane);
-      if (a.W2) gemv_products<JM, false, kGemvRB>(w2, a.K2, rb2, a.xq2, a.xs2, r0, nr, P2, lane);
       float prev = 0.0f;
       if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
+      const WRow<JM> w1a[1] = {w1};
+      gemv_products_nr<JM, SH, kGemvRB, 1>(w1a, 1, a.K, rb, xq + (size_t)r0 * a.K, xs + (size_t)r0 * (a.K >> 5), nr,
+                                          P, lane);
+      if (a.W2) {
+        const WRow<JM> w2a[1] = {w2};
+        gemv_products_nr<JM, false, kGemvRB, 1>(w2a, 1, a.K2, rb2, a.xq2 + (size_t)r0 * a.K2,
+                                               a.xs2 + (size_t)r0 * (a.K2 >> 5), nr, P2, lane);
+      }
       __syncwarp();
       if (lane < nr) {
-        float v = q8_reduce(P[lane], wsr, rb, ng);
-        if (a.W2) v = __fadd_rn(v, q8_reduce(P2[lane], wsr2, rb2, ng2));
+        float v = (rb > 1 && ng == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P[lane], rb), s1))
+                                      : q8_reduce(P[lane], wsr, rb, ng);
+        if (a.W2)
+          v = __fadd_rn(v, (rb2 > 1 && ng2 == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P2[lane], rb2), s2))
+                                                 : q8_reduce(P2[lane], wsr2, rb2, ng2));
         a.y[(size_t)(r0 + lane) * a.ldy + n] = a.mode == 1 ? __fadd_rn(prev, v) : v;
       }
       __syncwarp();
@@ -266,18 +295,22 @@ LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs,
       const int r = nb + i * nstep;
       if (r < a.N) load_wrow<JM>(wn[i], a.W + (size_t)r * a.K, a.ws + (size_t)r * ng, a.K, rb, lane);
     }
-#pragma unroll
-    for (int i = 0; i < NR; i++)
-      if (base + i * nstep < a.N) gemv_products<JM, SH, RB>(wc[i], a.K, rb, xq, xs, 0, R, P + i * R, lane);
+    // the reducing lane's output row scale (one per row) and accumulator
+    // input, loaded before the products
+    const int li = lane / R, lrr = lane - li * R, lr = base + li * nstep;
+    const bool red = lane < NR * R && lr < a.N;
+    float s0 = 0.0f, prev = 0.0f;
+    if (red) {
+      if (rb > 1 && ng == 1) s0 = __ldg(a.ws + lr);
+      if (a.mode == 1) prev = a.y[(size_t)lrr * a.ldy + lr];
+    }
+    const int nvalid = base >= a.N ? 0 : min(NR, (a.N - 1 - base) / nstep + 1);
+    gemv_products_nr<JM, SH, RB, NR>(wc, nvalid, a.K, rb, xq, xs, R, P, lane);
     __syncwarp();
-    if (lane < NR * R) {
-      const int i = lane / R, rr = lane - i * R, r = base + i * nstep;
-      if (r < a.N) {
-        float* yp = a.y + (size_t)rr * a.ldy + r;
-        const float prev = a.mode == 1 ? *yp : 0.0f;
-        const float v = q8_reduce(P[lane], a.ws + (size_t)r * ng, rb, ng);
-        *yp = a.mode == 1 ? __fadd_rn(prev, v) : v;
-      }
+    if (red) {
+      const float v = (rb > 1 && ng == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P[lane], rb), s0))
+                                          : q8_reduce(P[lane], a.ws + (size_t)lr * ng, rb, ng);
+      a.y[(size_t)lrr * a.ldy + lr] = a.mode == 1 ? __fadd_rn(prev, v) : v;
     }
     __syncwarp();
 #pragma unroll
