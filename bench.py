@@ -323,6 +323,54 @@ def run_batch32(m, args, rank: int, world: int):
     }
 
 
+def run_ep(m, args, rank: int, world: int):
+    """Expert parallelism at N > 1 (configs[2]'s batch-32 temperature
+    rounds): each rank's 32 sequences are prefilled with its local experts,
+    then lz_ep_init shards the routed experts over the ranks (rank r owns
+    E/N of them) and every round exchanges each layer's (token, expert)
+    pairs with NCCL send/recv; the rounds run eagerly (no graph).  Same
+    prompts as the batch-32 arm.  Device-timed, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import lz98
+    import lz98_synth
+    cfg = lz98_synth.CONFIGS[MODEL]
+    lo, hi = args.b32_prompts
+    prompts = lz98_synth.workload_prompts(cfg, B32, lo, hi, 1.1, seed=rank)
+    steps = max(1, min(args.steps, 20))
+    s = lz98.State(m, 1024 + (K32 + 1) * (args.warmup + steps + 2) + 64, K32, n_seq=B32)
+    for b, p in enumerate(prompts):
+        s.set_sampler(b, 0.8, 0.95, 1000 + rank * B32 + b)
+        s.seq_prefill(b, p)
+    obj = [lz98.ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    s.ep_init(obj[0], rank, world)
+    stream = torch.cuda.ExternalStream(s.stream())
+    for _ in range(args.warmup):
+        s.round_batch(K32, fetch=False)
+    torch.cuda.synchronize()
+    c0 = [s.counters(b) for b in range(B32)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        s.round_batch(K32, fetch=False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    c1 = [s.counters(b) for b in range(B32)]
+    emitted = sum(c1[b][1] - c0[b][1] for b in range(B32))
+    s.close()
+    ms_max, emitted_all, _ = reduce_over_ranks(ms, float(emitted), None, world, "cuda")
+    return {"workload": "configs[2] rounds (32 sequences per GPU, temperature 0.8, top-p 0.95, k=3) with the "
+                        f"64 routed experts sharded {cfg.n_experts // world} per rank",
+            "value": emitted_all / (ms_max * 1e-3), "unit": UNIT, "steps": steps, "ms_per_step": ms_max / steps,
+            "parallelism": f"ep{world} (NCCL send/recv of each layer's pairs; eager rounds)",
+            "scaling": "weak"}
+
+
 N3B, P3B, K3B, NEW3B = 8, 8192, 3, 256     # configs[3]: sequences per GPU, prompt, draft depth, new tokens
 
 
@@ -519,6 +567,7 @@ def run_ours(args):
         s1.close()
     ms_max, emitted_all, e2e_all = reduce_over_ranks(ms, float(emitted), e2e_val, world, "cuda")
     b32 = None if args.no_b32 else run_batch32(m, args, rank, world)
+    ep = run_ep(m, args, rank, world) if (world > 1 and not args.no_ep) else None
     peak, peak_kind = measured_peak()
     gemv_gbs = prof["gemv_bytes"] / (prof["gemv_ms"] * 1e-3) / 1e9
     line = None
@@ -558,6 +607,7 @@ def run_ours(args):
             "gpu_launches": prof["n_kernels"] * args.steps,
             "clocks": clk,
             "batch32": b32,
+            "expert_parallel": ep,
         }
         print(json.dumps(line), flush=True)
     s.close()
@@ -822,6 +872,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the C-ABI end-to-end pass")
     ap.add_argument("--no-b32", action="store_true", help="skip the batch-32 temperature workload")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel rounds at N > 1")
     ap.add_argument("--b32-only", action="store_true", help="run only the batch-32 workload (profiling)")
     ap.add_argument("--b32-prompts", type=int, nargs=2, default=[256, 1024], metavar=("LO", "HI"),
                     help="prompt length range of the batch-32 workload (default 256 1024, BASELINE configs[2]; "
