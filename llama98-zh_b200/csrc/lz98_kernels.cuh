@@ -29,7 +29,8 @@ constexpr int kRowLoadU = 4;      // loads a thread of a row kernel issues befor
 
 // Sequential sum of squares over a 16-byte aligned array, n % 4 == 0
 // (src/ops_norm.c:718): the adds stay in index order; the loads run ahead
-// in float4 groups.
+// in float4 groups.  (Forming 16 squares ahead of the chain measured
+// faster alone but slower inside the 128-register prologue GEMV.)
 LZ_HD float seq_sumsq(const float* v, int n) {
   float ss = 0.0f;
   const float4* p = reinterpret_cast<const float4*>(v);
@@ -131,13 +132,7 @@ LZ_HD void warp_quant32_x4(const float* v, int8_t* q, float* sg) {
 #pragma unroll
   for (int k = 0; k < 4; k++) m[k] = abs_bits(v[k]);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const uint32_t w = __shfl_xor_sync(0xffffffffu, m[k], o);
-      m[k] = m[k] > w ? m[k] : w;
-    }
-  }
+  for (int k = 0; k < 4; k++) m[k] = __reduce_max_sync(0xffffffffu, m[k]);
 #pragma unroll
   for (int k = 0; k < 4; k++) {
     float inv;
@@ -870,6 +865,7 @@ __global__ void __launch_bounds__(288) gemm_q8_tma_kernel(const __grid_constant_
         ok = false;
         break;
       }
+      fence_proxy_async_smem();
       if (skip0 && it == 0) continue;
       const bool two = it >= it1;
       const int c = two ? it - it1 : it;
@@ -1615,6 +1611,28 @@ moe_route_w13_kernel(const float* __restrict__ moein, int ldm, int off_router, i
   }
 }
 
+// Element i of a token row's latent output: the sum over its selected
+// experts, in selection order, of w * (the pair's w2 row) (src/forward_moe.c:
+// 198-199); unrouted pairs (expert -1) are skipped.  e / w are the row's
+// experts and weights (shared memory); the pair rows are loaded four at a
+// time ahead of their adds (the rows are in bounds whether routed or not).
+// CG reads them through L2 only (rows written by other blocks of the same
+// kernel).
+template <bool CG>
+LZ_HD float combine_elem(const int* e, const float* w, int topk, const float* __restrict__ h2, int latent, int i) {
+  float acc = 0.0f;
+  for (int t0 = 0; t0 < topk; t0 += 4) {
+    float h[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (t0 + u < topk) h[u] = CG ? __ldcg(h2 + (size_t)(t0 + u) * latent + i) : h2[(size_t)(t0 + u) * latent + i];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (t0 + u < topk && e[t0 + u] >= 0) acc = __fadd_rn(acc, __fmul_rn(w[t0 + u], h[u]));
+  }
+  return acc;
+}
+
 // w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
 // the last block to finish among a token row's pairs then forms
 // lat_y = sum over the row's selected experts, in selection order, of
@@ -1660,15 +1678,16 @@ moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  __shared__ int s_pe[16];
+  __shared__ float s_pw[16];
+  if (threadIdx.x < topk) {
+    s_pe[threadIdx.x] = __ldcg(pair_expert + r * topk + threadIdx.x);
+    s_pw[threadIdx.x] = __ldcg(pair_w + r * topk + threadIdx.x);
+  }
+  __syncthreads();
   for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
-    const int i = g * 32 + lane;
-    float acc = 0.0f;
-    for (int t = 0; t < topk; t++) {
-      const int pp = r * topk + t;
-      if (pair_expert[pp] < 0) continue;
-      acc = __fadd_rn(acc, __fmul_rn(pair_w[pp], __ldcg(h2 + (size_t)pp * latent + i)));
-    }
-    yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
+    const float acc = combine_elem<true>(s_pe, s_pw, topk, h2 + (size_t)r * topk * latent, latent, g * 32 + lane);
+    yq[(size_t)r * latent + g * 32 + lane] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
   }
   if (threadIdx.x == 0) row_counter[r] = 0;
 }
@@ -1939,6 +1958,7 @@ __global__ void __launch_bounds__((MoeTma<W13, RB1>::CW + 1) * 32) moe_tma_kerne
         ok = false;
         break;
       }
+      fence_proxy_async_smem();
       issue(it);
     }
     if (!ok) atomicExch(p.err, 1);
@@ -2113,15 +2133,16 @@ __global__ void moe_combine_kernel(const int* __restrict__ pair_expert, const fl
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_pe[16];
+  __shared__ float s_pw[16];
+  if (threadIdx.x < topk) {
+    s_pe[threadIdx.x] = pair_expert[r * topk + threadIdx.x];
+    s_pw[threadIdx.x] = pair_w[r * topk + threadIdx.x];
+  }
+  __syncthreads();
   for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
-    const int i = g * 32 + lane;
-    float acc = 0.0f;
-    for (int t = 0; t < topk; t++) {
-      const int pp = r * topk + t;
-      if (pair_expert[pp] < 0) continue;
-      acc = __fadd_rn(acc, __fmul_rn(pair_w[pp], h2[(size_t)pp * latent + i]));
-    }
-    yq[(size_t)r * latent + i] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
+    const float acc = combine_elem<false>(s_pe, s_pw, topk, h2 + (size_t)r * topk * latent, latent, g * 32 + lane);
+    yq[(size_t)r * latent + g * 32 + lane] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
   }
 }
 

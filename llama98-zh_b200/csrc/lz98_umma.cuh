@@ -203,6 +203,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 2) gemm_q8_umma_kernel(const __g
           ok = false;
           break;
         }
+        fence_proxy_async_smem();
         if (skip0 && it == 0) continue;
         const bool two = it >= it1;
         const int c = two ? it - it1 : it;
