@@ -255,7 +255,10 @@ int lz_generate_resume(const LZModel *m, LZRunState *s, int start_pos, const int
    [r E/world, (r+1) E/world) for the pairs of every rank, each rank keeps
    its own sequences.  Per layer the (token, expert) pairs go to their
    expert's owner and the expert outputs come back (NCCL send/recv over
-   NVLink, the library bound at run time); the combine keeps the
+   NVLink, the library bound at run time: the libnccl.so.2 already loaded
+   in the process, else the path in LZ98_NCCL, else the system's - a
+   process that loads another NCCL itself must do so first); the combine
+   keeps the
    reference's selection order, so results are those of one GPU bit for
    bit.  Rank 0 makes the id with lz_ep_unique_id and the caller hands it
    to every rank; every rank then calls lz_ep_init together (collective).

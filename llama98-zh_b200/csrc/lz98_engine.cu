@@ -448,7 +448,15 @@ const NcclApi* nccl_api() {
   static NcclApi api;
   static bool ok = false;
   std::call_once(once, [] {
+    // the NCCL already in the process (a framework's), else LZ98_NCCL (a
+    // path), else the system's.  A process that loads another NCCL later
+    // must load it first: a second library of the same soname is not
+    // loaded beside this one.
     void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) {
+      const char* path = getenv("LZ98_NCCL");
+      if (path && *path) h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    }
     if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
     if (!h) return;
     auto take = [h](auto& fn, const char* name) {

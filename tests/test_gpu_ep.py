@@ -13,6 +13,7 @@ import os
 
 import numpy as np
 import pytest
+import torch  # noqa: F401  (its NCCL is loaded before the library binds one)
 
 pytestmark = pytest.mark.gpu
 
