@@ -132,7 +132,8 @@ LZ_HD void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Thread-block clusters: this CTA's rank in its cluster, the cluster-wide
 // barrier (every thread of every CTA of the cluster; release / acquire, so
 // shared-memory writes before it are visible to the peers after it), and a
-// float read from the same shared-memory variable of a peer CTA.
+// float written to / read from the same shared-memory variable of a peer
+// CTA.
 LZ_HD uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -140,6 +141,12 @@ LZ_HD uint32_t cluster_rank() {
 }
 LZ_HD void cluster_barrier() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+LZ_HD void st_peer_f32(float* local, uint32_t peer, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"((uint32_t)__cvta_generic_to_shared(local)),
+               "r"(peer));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 LZ_HD float ld_peer_f32(const float* local, uint32_t peer) {
   uint32_t remote;

@@ -508,7 +508,7 @@ struct LZRunState {
   float *xs, *os, *lats, *hs, *ys, *shs, *as;
   int *pair_e, *tok, *catch_tok, *catch_hidx;
   unsigned long long* vmax;
-  int* row_counter;                  // last-block tails (reset by the last block)
+  int* row_counter;                  // last-block tails per (row, 32-group) (reset by the last block)
   // temperature rounds: draft distributions [B][kmax][V], target
   // distributions [Rmax][V], sort scratch [Rmax][npow2], sampled token
   float *qbuf = nullptr, *pbuf = nullptr, *sortbuf = nullptr;
@@ -738,7 +738,7 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->pair_e, P) && dmalloc(s, &s->pair_w, P) && dmalloc(s, &s->tok, R) &&
             dmalloc(s, &s->vmax, R) && dmalloc(s, &s->catch_tok, R) && dmalloc(s, &s->catch_hidx, R) &&
             dmalloc(s, &s->seqs, R) && dmalloc(s, &s->mrows, R) && dmalloc(s, &s->crows, R) &&
-            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R) && dmalloc(s, &s->tok_out, 4) &&
+            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R * (c.latent / 32 + 1)) && dmalloc(s, &s->tok_out, 4) &&
             dmalloc(s, &s->pconf, 4);
   s->npow2 = 2;
   while (s->npow2 < c.vocab) s->npow2 <<= 1;
@@ -1401,7 +1401,8 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
         launch(s, moe_route_w13_kernel<32>, dim3(c.moe_ffn / 32, P), dim3(256), 0, s->moein, m->n_moe,
                m->off_router, m->off_down, L.router_bias, c.ne, c.topk, L.w13q, L.w13s, c.moe_ffn, c.latent,
                L.w13_gs, s->pair_e, s->pair_w, s->hq, s->hs, m->off_shg, m->off_shu, c.shared_w, s->shq, s->shs);
-      launch(s, moe_w2_kernel, dim3((c.latent + 7) / 8, P), dim3(256), 0, L.w2q, L.w2s, c.moe_ffn, c.latent,
+      launch(s, moe_w2_kernel, dim3((c.latent + 8 * kW2Rows - 1) / (8 * kW2Rows), P), dim3(256), 0, L.w2q, L.w2s,
+             c.moe_ffn, c.latent,
              L.w2_gs, s->pair_e, s->pair_w, c.topk, s->hq, s->hs, s->h2, s->row_counter, s->yq, s->ys);
     } else {
       launch(s, moe_route_kernel, dim3(R), dim3(512), 0, s->moein, m->n_moe, m->off_router, m->off_down,

@@ -1084,9 +1084,9 @@ struct KdaArgs {
 // meet in the recurrence - pass 1 sums down a column, pass 2 requantises a
 // (row, group) - so each CTA holds and updates only its half; the
 // per-key work (conv, gate, norms) is done by both.  The gated RMSNorm
-// needs the whole head output: each CTA reads the peer's 32 columns from
-// its shared memory (cluster barrier, read, cluster barrier).  SPLIT = 1 is
-// one CTA per head.
+// needs the whole head output: each CTA writes its 32 columns into the
+// peer's shared memory, then one cluster barrier.  SPLIT = 1 is one CTA
+// per head.
 constexpr int kRecurThreads = 256;
 constexpr int kRecurTB = 4;
 constexpr int kRankMax = 128;
@@ -1126,7 +1126,10 @@ LZ_HD void kda_layer(const KdaArgs& a) {
   __shared__ float sc[KD][GPC];
   __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], KG[TB][KD], QG[TB][KD];
   __shared__ __align__(16) float vcs[TB][VC], zs[TB][VC];
-  __shared__ __align__(16) float OUT[TB][VD];
+  // the head outputs of a batch, both value groups (SPLIT = 2: the peer
+  // writes its group into this copy); two buffers by batch parity, so a
+  // peer one batch ahead never writes the buffer this CTA still reads
+  __shared__ __align__(16) float OUT2[2][TB][VD];
   __shared__ __align__(16) float U[VC], AW[VC];
   __shared__ float inv_q[TB], inv_k[TB], beta[TB], braw[TB], kqs[TB], inv_o[TB];
   __shared__ __align__(16) int8_t LQ[TB][kRankMax];
@@ -1221,6 +1224,7 @@ LZ_HD void kda_layer(const KdaArgs& a) {
   if (tid < KD * GPC) sc[tid / GPC][tid % GPC] = ssc;
   for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
+    float (*OUT)[VD] = OUT2[(t0 / TB) & 1];
     if (t0 > 0) issue(t0, nt);
 #pragma unroll
     for (int i = 0; i < MI; i++) {
@@ -1364,13 +1368,12 @@ LZ_HD void kda_layer(const KdaArgs& a) {
       }
       __syncthreads();
     }
-    // the other CTA's half of every token's head output
+    // this CTA's half of every token's head output into the peer's copy,
+    // then one cluster barrier: both copies whole
     if (SPLIT > 1) {
-      cluster_barrier();
-      const int pc0 = (grp ^ 1) * VC;
       for (int q = tid; q < nt * VC; q += NTH) {
         const int t = q / VC, c = q - t * VC;
-        OUT[t][pc0 + c] = ld_peer_f32(&OUT[t][pc0 + c], (uint32_t)(grp ^ 1));
+        st_peer_f32(&OUT[t][vcol0 + c], (uint32_t)(grp ^ 1), OUT[t][vcol0 + c]);
       }
       cluster_barrier();
     }
@@ -1633,10 +1636,13 @@ LZ_HD float combine_elem(const int* e, const float* w, int topk, const float* __
   return acc;
 }
 
-// w2 (latent x ffn) of every pair, one warp per output row, ffn <= 2048;
-// the last block to finish among a token row's pairs then forms
-// lat_y = sum over the row's selected experts, in selection order, of
-// w * h2 (src/forward_moe.c:198-199) and quantises it per 32.
+// w2 (latent x ffn) of every pair, two output rows per warp (16 outputs
+// per block, so batch 1 runs in one wave of blocks), ffn <= 2048; for each
+// token row and 32-output group, the last of the blocks producing it (2
+// per pair) forms that group of lat_y = sum over the row's selected
+// experts, in selection order, of w * h2 (src/forward_moe.c:198-199) and
+// quantises it per 32.
+constexpr int kW2Rows = 2;   // output rows per warp
 __global__ void __launch_bounds__(256)
 moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int ffn, int latent, int gs,
               const int* __restrict__ pair_expert, const float* __restrict__ pair_w, int topk,
@@ -1644,52 +1650,80 @@ moe_w2_kernel(const int8_t* __restrict__ w2q, const float* __restrict__ w2s, int
               int* row_counter, int8_t* yq, float* ys) {
   pdl_trigger();
   pdl_wait();
-  __shared__ __align__(16) float P[8][64];
+  __shared__ __align__(16) float P[8][kW2Rows][64];
   __shared__ int s_last;
   const int p = blockIdx.y, r = p / topk;
   const int e = pair_expert[p];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
-  if (e >= 0 && n < latent) {
+  const int n0 = (blockIdx.x * 8 + warp) * kW2Rows;
+  if (e >= 0 && n0 < latent) {
     const int nsb = ffn / 32, rb = gs / 32, ng = ffn / gs;
-    const int8_t* wr = w2q + ((size_t)e * latent + n) * ffn;
-    const float* wsr = w2s + ((size_t)e * latent + n) * ng;
     const int8_t* xr = hq + (size_t)p * ffn;
     const float* xsr = hs + (size_t)p * nsb;
+    int4 wa[kW2Rows][2], wb[kW2Rows][2];
+    float wsv[kW2Rows][2];
+#pragma unroll
+    for (int q = 0; q < kW2Rows; q++)
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const int s = lane + 32 * j, n = n0 + q;
+        if (s < nsb && n < latent) {
+          const int8_t* wr = w2q + ((size_t)e * latent + n) * ffn;
+          wa[q][j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
+          wb[q][j] = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
+          wsv[q][j] = rb == 1 ? __ldg(w2s + ((size_t)e * latent + n) * ng + s) : 0.0f;
+        }
+      }
 #pragma unroll
     for (int j = 0; j < 2; j++) {
       const int s = lane + 32 * j;
       if (s < nsb) {
-        const int4 wa = __ldg(reinterpret_cast<const int4*>(wr + s * 32));
-        const int4 wb = __ldg(reinterpret_cast<const int4*>(wr + s * 32 + 16));
         const int4 xa = __ldg(reinterpret_cast<const int4*>(xr + s * 32));
         const int4 xb = __ldg(reinterpret_cast<const int4*>(xr + s * 32 + 16));
-        const float a = (float)dot32(wa, wb, xa, xb);
         const float xsv = __ldg(xsr + s);
-        P[warp][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, __ldg(wsr + s)));
+#pragma unroll
+        for (int q = 0; q < kW2Rows; q++)
+          if (n0 + q < latent) {
+            const float a = (float)dot32(wa[q][j], wb[q][j], xa, xb);
+            P[warp][q][s] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, wsv[q][j]));
+          }
       }
     }
     __syncwarp();
-    if (lane == 0) h2[(size_t)p * latent + n] = q8_reduce(P[warp], wsr, rb, ng);
+    if (lane < kW2Rows && n0 + lane < latent) {
+      const int n = n0 + lane;
+      h2[(size_t)p * latent + n] = q8_reduce(P[warp][lane], w2s + ((size_t)e * latent + n) * ng, rb, ng);
+    }
   }
+  // the last of the blocks that produce 32-output group g of row r (2 per
+  // pair) forms that group's combine (one warp)
+  constexpr int BPG = 32 / (8 * kW2Rows);
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(row_counter + r, 1) == topk * (int)gridDim.x - 1;
+  const int g = blockIdx.x / BPG, cidx = r * (latent / 32) + g;
+  if (threadIdx.x == 0) {
+    const int nb = min(BPG, (int)gridDim.x - BPG * g);
+    s_last = atomicAdd(row_counter + cidx, 1) == topk * nb - 1;
+  }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last || warp != 0) return;
   __threadfence();
+  int pe = -1;
+  float pw = 0.0f;
+  if (lane < topk) {
+    pe = __ldcg(pair_expert + r * topk + lane);
+    pw = __ldcg(pair_w + r * topk + lane);
+  }
   __shared__ int s_pe[16];
   __shared__ float s_pw[16];
-  if (threadIdx.x < topk) {
-    s_pe[threadIdx.x] = __ldcg(pair_expert + r * topk + threadIdx.x);
-    s_pw[threadIdx.x] = __ldcg(pair_w + r * topk + threadIdx.x);
+  if (lane < topk) {
+    s_pe[lane] = pe;
+    s_pw[lane] = pw;
   }
-  __syncthreads();
-  for (int g = warp; g < latent / 32; g += blockDim.x >> 5) {
-    const float acc = combine_elem<true>(s_pe, s_pw, topk, h2 + (size_t)r * topk * latent, latent, g * 32 + lane);
-    yq[(size_t)r * latent + g * 32 + lane] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
-  }
-  if (threadIdx.x == 0) row_counter[r] = 0;
+  __syncwarp();
+  const float acc = combine_elem<true>(s_pe, s_pw, topk, h2 + (size_t)r * topk * latent, latent, g * 32 + lane);
+  yq[(size_t)r * latent + g * 32 + lane] = warp_quant32(acc, &ys[(size_t)r * (latent / 32) + g]);
+  if (lane == 0) row_counter[cidx] = 0;
 }
 
 // ------------------------------------------------ grouped experts (R > 8)
