@@ -660,65 +660,69 @@ def _reference():
     return Reference, reference_available
 
 
-def ref_decode_sample(prompt, k: int, temp: float, seed: int, max_new: int, seconds: float, stock: bool = False):
+def ref_decode_sample(prompt, k: int, temp: float, seed: int, max_new: int, seconds: float, stock_seconds: float = 0.0,
+                      barrier=None):
     """The reference engine (oracle/_ref, one thread) on one sequence of the
     workload: the prompt prefilled (untimed), a short warm decode, then
-    decode for about `seconds` of wall time.  Returns (tokens/s, tokens,
-    decode seconds, prefill seconds)."""
+    decode for about `seconds` in the parity float tier and, when
+    stock_seconds > 0, for about stock_seconds more in the reference's
+    stock tier (the tier is switched between rounds: the decode cost per
+    token is what is timed).  A barrier (multiprocessing) is waited on
+    before each timed phase.  Returns ((tokens/s, tokens, s) float,
+    (tokens/s, tokens, s) stock or None, prefill s)."""
     Reference, available = _reference()
     if not available():
         return None
     R = Reference(model_dir(), len(prompt) + max_new + 64, max(1, k))
     try:
-        if stock:
-            R.stock_tier()
         pf = R.session_begin(prompt, max_new, k, temp=temp, topp=0.95, seed=seed)
         R.session_decode(k + 1)
+        if barrier is not None:
+            barrier.wait(timeout=1200)
         toks, _, el = R.session_decode(1 << 30, seconds * 1000.0)
+        fl = (len(toks) / max(1e-9, el * 1e-3), len(toks), el * 1e-3)
+        st = None
+        if stock_seconds > 0:
+            R.stock_tier()
+            if barrier is not None:
+                barrier.wait(timeout=1200)
+            toks, _, el = R.session_decode(1 << 30, stock_seconds * 1000.0)
+            st = (len(toks) / max(1e-9, el * 1e-3), len(toks), el * 1e-3)
     finally:
-        if stock:
-            R.L.rd_set_tier(7)
+        R.L.rd_set_tier(7)
         R.close()
-    return len(toks) / max(1e-9, el * 1e-3), len(toks), el * 1e-3, pf * 1e-3
+    return fl, st, pf * 1e-3
 
 
 def cpu_baseline(args):
     """Batch-1 CPU baseline: the reference on the headline workload's own
     sequence (the 512-token prompt, greedy, k = 2), float tier, then its
-    stock arithmetic on a shorter sample."""
+    stock arithmetic on a shorter sample of the same decode."""
     p = prompts(1, 0)[0]
-    r = ref_decode_sample(p, SPEC_K, 0.0, 1, MAX_NEW, args.cpu_seconds)
+    r = ref_decode_sample(p, SPEC_K, 0.0, 1, MAX_NEW, args.cpu_seconds, max(2.0, args.cpu_seconds / 3))
     if r is None:
         return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference",
                 "sample": "oracle/_ref/liblz98ref.so not built"}
-    v, n, el, pf = r
-    rs = ref_decode_sample(p, SPEC_K, 0.0, 1, MAX_NEW, max(2.0, args.cpu_seconds / 3), stock=True)
+    (v, n, el), st, pf = r
     return {"value": v, "unit": UNIT, "cores": 1, "kind": "reference", "cpu": cpu_model(),
             "sample": f"reference C99 engine, float tier (--fixed off, --fastfp off), the bench's 512-token "
                       f"prompt (prefill {pf:.1f} s, untimed), then {n} greedy k=2 tokens in {el:.1f} s of decode",
-            "stock_tier": {"value": rs[0] if rs else None,
-                           "sample": f"stock tier (--fixed all, --fastfp on), same prompt, {rs[1]} tokens in "
-                                     f"{rs[2]:.1f} s" if rs else "not run"}}
+            "stock_tier": {"value": st[0] if st else None,
+                           "sample": f"stock tier (--fixed all, --fastfp on), the same decode continued, {st[1]} "
+                                     f"tokens in {st[2]:.1f} s" if st else "not run"}}
 
 
-def _b32_cpu_worker(prompt, seed, seconds, stock, barrier, out):
+def _b32_cpu_worker(prompt, seed, seconds, stock_seconds, barrier, out):
     try:
-        Reference, _ = _reference()
-        R = Reference(model_dir(), len(prompt) + NEW32 + 64, K32)
-        if stock:
-            R.stock_tier()
-        R.session_begin(prompt, NEW32, K32, temp=0.8, topp=0.95, seed=seed)
-        R.session_decode(K32 + 1)
-        barrier.wait(timeout=1200)
-        toks, rounds, el = R.session_decode(1 << 30, seconds * 1000.0)
-        R.close()
-        out.put((len(toks), el * 1e-3, len(rounds), None))
+        r = ref_decode_sample(prompt, K32, 0.8, seed, NEW32, seconds, stock_seconds, barrier)
+        (v, n, el), st, _ = r
+        out.put((n, el, st[1] if st else 0, st[2] if st else 0.0, None))
     except Exception as e:          # reported, never hangs the parent
         try:
             barrier.abort()
         except Exception:
             pass
-        out.put((0, 0.0, 0, repr(e)[:200]))
+        out.put((0, 0.0, 0, 0.0, repr(e)[:200]))
 
 
 def _collect(procs, q, barrier, n: int, limit_s: float):
@@ -774,32 +778,28 @@ def b32_cpu_baseline(seconds: float, lo: int = 256, hi: int = 1024):
         r += 1
     seqs = seqs[:n]
     ctx = mp.get_context("spawn")
-    res = {}
     t_all = time.time()
-    for tier, secs in (("float", seconds), ("stock", max(2.0, seconds / 2))):
-        barrier, q = ctx.Barrier(n), ctx.Queue()
-        procs = [ctx.Process(target=_b32_cpu_worker, args=(p, sd, secs, tier == "stock", barrier, q))
-                 for p, sd in seqs]
-        for pr in procs:
-            pr.start()
-        outs = _collect(procs, q, barrier, n, 1800.0)
-        errs = [o[3] for o in outs if o[3]]
-        if len(outs) < n:
-            errs.append(f"{n - len(outs)} processes gave no result")
-        rate = sum(o[0] / o[1] for o in outs if o[1] > 0)
-        res[tier] = {"value": rate if not errs else None, "tokens": sum(o[0] for o in outs),
-                     "decode_s": max(o[1] for o in outs), "errors": errs[:3]}
+    stock_s = max(2.0, seconds / 2)
+    barrier, q = ctx.Barrier(n), ctx.Queue()
+    procs = [ctx.Process(target=_b32_cpu_worker, args=(p, sd, seconds, stock_s, barrier, q)) for p, sd in seqs]
+    for pr in procs:
+        pr.start()
+    outs = _collect(procs, q, barrier, n, 1800.0)
+    errs = [o[4] for o in outs if o[4]]
+    if len(outs) < n:
+        errs.append(f"{n - len(outs)} processes gave no result")
+    fl = sum(o[0] / o[1] for o in outs if o[1] > 0)
+    st = sum(o[2] / o[3] for o in outs if o[3] > 0)
     lens = sorted(len(p) for p, _ in seqs)
-    return {"value": res["float"]["value"], "unit": UNIT, "cores": n, "kind": "reference",
+    return {"value": fl if not errs else None, "unit": UNIT, "cores": n, "kind": "reference",
             "cpu": cpu_model(), "host_cores": cores,
-            "sample": f"{n} reference processes (one per core, float tier), one configs[2] sequence each "
-                      f"(prompts {lens[0]}-{lens[-1]} tokens, prefilled untimed), temperature 0.8, top-p 0.95, "
-                      f"k=3, decoding together for {res['float']['decode_s']:.1f} s; "
-                      f"{res['float']['tokens']} tokens; sum of per-process rates",
-            "stock_tier": {"value": res["stock"]["value"], "tokens": res["stock"]["tokens"],
-                           "decode_s": res["stock"]["decode_s"]},
-            "errors": res["float"]["errors"] + res["stock"]["errors"],
-            "wall_s": time.time() - t_all}
+            "sample": f"{n} reference processes (one per core), one configs[2] sequence each (prompts "
+                      f"{lens[0]}-{lens[-1]} tokens, prefilled untimed), temperature 0.8, top-p 0.95, k=3, "
+                      f"decoding together (a barrier) for ~{seconds:.0f} s in the float tier: "
+                      f"{sum(o[0] for o in outs)} tokens; sum of per-process rates",
+            "stock_tier": {"value": st if not errs else None, "tokens": sum(o[2] for o in outs),
+                           "sample": f"the same processes continuing for ~{stock_s:.0f} s in the stock tier"},
+            "errors": errs[:3], "wall_s": time.time() - t_all}
 
 
 def run_reference(args):
