@@ -97,6 +97,38 @@ LZ_HD float q8_reduce(const float* p, const float* wsr, int rb, int ng) {
   return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
 }
 
+// q8_reduce over products stored with a stride (p[s * ld], the GEMV's
+// transposed product buffer), the same float operations in the same order;
+// s0 is ws[0], already loaded, for one group per row (rb > 1, ng == 1).
+LZ_HD float q8_reduce_st(const float* p, int ld, const float* wsr, float s0, int rb, int ng) {
+  if (rb > 1) {
+    if (ng == 1) {
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int s = 0; s < rb; s++) sum = __fadd_rn(sum, p[s * ld]);
+      return __fadd_rn(0.0f, __fmul_rn(sum, s0));
+    }
+    float sum = 0.0f;
+    for (int g = 0; g < ng; g++) {
+      float dot = 0.0f;
+      for (int s = 0; s < rb; s++) dot = __fadd_rn(dot, p[(g * rb + s) * ld]);
+      sum = __fadd_rn(sum, __fmul_rn(dot, wsr[g]));
+    }
+    return sum;
+  }
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  int g = 0;
+#pragma unroll 4
+  for (; g + 3 < ng; g += 4) {
+    a0 = __fadd_rn(a0, p[g * ld]);
+    a1 = __fadd_rn(a1, p[(g + 1) * ld]);
+    a2 = __fadd_rn(a2, p[(g + 2) * ld]);
+    a3 = __fadd_rn(a3, p[(g + 3) * ld]);
+  }
+  for (; g < ng; g++) a0 = __fadd_rn(a0, p[g * ld]);
+  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+}
+
 // The exact int32 dot product of a 32-element sub-block: two independent
 // __dp4a chains (its dependent latency is ~13 cycles here) joined by one
 // add; integer sums are exact in any order.
@@ -167,11 +199,13 @@ LZ_HD void load_wrow(WRow<JM>& w, const int8_t* __restrict__ wr, const float* __
 // Products of NR weight rows (the first nvalid of them) with every token
 // row for this lane's sub-blocks: every activation load and every product
 // comes before the first store to P, so the stores (which may alias the
-// activations in shared memory) never stall the next loads.
-// P[i * nr + rr][s] receives the product of weight row i and token row rr.
+// activations in shared memory) never stall the next loads.  P is
+// transposed: P[s * ld + i * nr + rr] receives the product of sub-block s
+// of weight row i with token row rr (ld odd, so both these stores and the
+// reducing lanes' reads along s are free of bank conflicts).
 template <int JM, bool SH, int RB, int NR>
 LZ_HD void gemv_products_nr(const WRow<JM> (&w)[NR], int nvalid, int K, int rb, const int8_t* xq, const float* xs,
-                            int nr, float (*P)[JM * 32], int lane) {
+                            int nr, float* P, int ld, int lane) {
   const int nsb = K >> 5;
   float pr[RB][NR][JM];
 #pragma unroll
@@ -195,10 +229,11 @@ LZ_HD void gemv_products_nr(const WRow<JM> (&w)[NR], int nvalid, int K, int rb, 
             xsv = __ldg(xsr + s);
           }
 #pragma unroll
-          for (int i = 0; i < NR; i++) {
-            const float a = (float)dot32(w[i].a[j], w[i].b[j], xa, xb);
-            pr[rr][i][j] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, w[i].s[j]));
-          }
+          for (int i = 0; i < NR; i++)
+            if (i < nvalid) {
+              const float a = (float)dot32(w[i].a[j], w[i].b[j], xa, xb);
+              pr[rr][i][j] = rb > 1 ? __fmul_rn(a, xsv) : __fmul_rn(a, __fmul_rn(xsv, w[i].s[j]));
+            }
         }
       }
     }
@@ -210,7 +245,7 @@ LZ_HD void gemv_products_nr(const WRow<JM> (&w)[NR], int nvalid, int K, int rb, 
 #pragma unroll
       for (int j = 0; j < JM; j++) {
         const int s = lane + 32 * j;
-        if (rr < nr && i < nvalid && s < nsb) P[i * nr + rr][s] = pr[rr][i][j];
+        if (rr < nr && i < nvalid && s < nsb) P[s * ld + i * nr + rr] = pr[rr][i][j];
       }
 }
 
@@ -219,11 +254,13 @@ template <int JM>
 __host__ __device__ constexpr int gemv_nr() { return 4 / JM; }
 
 // Bytes of dynamic shared memory of one GEMV block: per-warp product
-// buffers (multi-row path: RB x NR rows; single-row path: 8 rows for each
-// of the two weights) and, with the input-norm prologue, the rows, norm
-// weights, quantised rows, scales and inverse norms.
+// buffers, transposed with an odd stride (multi-row path: RB x NR
+// columns + 1; single-row path: 8 + 1 columns for each of the two
+// weights) and, with the input-norm prologue, the rows, norm weights,
+// quantised rows, scales and inverse norms.
 inline size_t gemv_smem_bytes(int JM, int warps, int RB, bool single, bool prologue, int R, int K) {
-  size_t b = single ? (size_t)warps * 2 * kGemvRB * JM * 32 * 4 : (size_t)warps * RB * (4 / JM) * JM * 32 * 4;
+  size_t b = single ? (size_t)warps * 2 * (kGemvRB + 1) * JM * 32 * 4
+                    : (size_t)warps * (RB * (4 / JM) + 1) * JM * 32 * 4;
   if (prologue) b += (size_t)R * K * 4 + (size_t)K * 4 + (size_t)R * K + (size_t)R * (K / 32) * 4 + 64;
   return b;
 }
@@ -232,7 +269,9 @@ inline size_t gemv_smem_bytes(int JM, int warps, int RB, bool single, bool prolo
 // optional second weight over the same outputs.
 template <int JM, int WARPS, bool SH>
 LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM>& wn1, WRow<JM>& wn2,
-                     float (*P)[JM * 32], float (*P2)[JM * 32], int n, int lane) {
+                     float* P, float* P2, int n, int lane, float s1_first, float s2_first) {
+  constexpr int LD = kGemvRB + 1;
+  const int n_first = n;
   const int rb = a.gs >> 5, ng = a.K / a.gs;
   const int rb2 = a.W2 ? a.gs2 >> 5 : 0, ng2 = a.W2 ? a.K2 / a.gs2 : 0;
   const int nstep = gridDim.x * WARPS;
@@ -244,28 +283,26 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
     }
     const float* wsr = a.ws + (size_t)n * ng;
     const float* wsr2 = a.W2 ? a.ws2 + (size_t)n * ng2 : nullptr;
-    // the output row's scales (one per row) for the reducing lanes
-    const float s1 = (rb > 1 && ng == 1) ? __ldg(wsr) : 0.0f;
-    const float s2 = (a.W2 && rb2 > 1 && ng2 == 1) ? __ldg(wsr2) : 0.0f;
+    // the output row's scales (one per row) for the reducing lanes (the
+    // first row's loaded before the dependency wait)
+    const float s1 = n == n_first ? s1_first : (rb > 1 && ng == 1) ? __ldg(wsr) : 0.0f;
+    const float s2 = n == n_first ? s2_first : (a.W2 && rb2 > 1 && ng2 == 1) ? __ldg(wsr2) : 0.0f;
     for (int r0 = 0; r0 < a.R; r0 += kGemvRB) {
       const int nr = min(kGemvRB, a.R - r0);
       float prev = 0.0f;
       if (lane < nr && a.mode == 1) prev = a.y[(size_t)(r0 + lane) * a.ldy + n];
       const WRow<JM> w1a[1] = {w1};
       gemv_products_nr<JM, SH, kGemvRB, 1>(w1a, 1, a.K, rb, xq + (size_t)r0 * a.K, xs + (size_t)r0 * (a.K >> 5), nr,
-                                          P, lane);
+                                          P, LD, lane);
       if (a.W2) {
         const WRow<JM> w2a[1] = {w2};
         gemv_products_nr<JM, false, kGemvRB, 1>(w2a, 1, a.K2, rb2, a.xq2 + (size_t)r0 * a.K2,
-                                               a.xs2 + (size_t)r0 * (a.K2 >> 5), nr, P2, lane);
+                                               a.xs2 + (size_t)r0 * (a.K2 >> 5), nr, P2, LD, lane);
       }
       __syncwarp();
       if (lane < nr) {
-        float v = (rb > 1 && ng == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P[lane], rb), s1))
-                                      : q8_reduce(P[lane], wsr, rb, ng);
-        if (a.W2)
-          v = __fadd_rn(v, (rb2 > 1 && ng2 == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P2[lane], rb2), s2))
-                                                 : q8_reduce(P2[lane], wsr2, rb2, ng2));
+        float v = q8_reduce_st(P + lane, LD, wsr, s1, rb, ng);
+        if (a.W2) v = __fadd_rn(v, q8_reduce_st(P2 + lane, LD, wsr2, s2, rb2, ng2));
         a.y[(size_t)(r0 + lane) * a.ldy + n] = a.mode == 1 ? __fadd_rn(prev, v) : v;
       }
       __syncwarp();
@@ -278,8 +315,8 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
 // (R <= RB <= 8), then their NR * R reductions on as many lanes at once.
 template <int JM, int WARPS, bool SH, int RB>
 LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM> (&wc)[gemv_nr<JM>()],
-                           float (*P)[JM * 32], int n0, int lane) {
-  constexpr int NR = gemv_nr<JM>();
+                           float* P, int n0, int lane, float s0_first) {
+  constexpr int NR = gemv_nr<JM>(), LD = RB * NR + 1;
   const int rb = a.gs >> 5, ng = a.K / a.gs, R = a.R;
   const int nstep = gridDim.x * WARPS;
   WRow<JM> wn[NR];
@@ -296,15 +333,14 @@ LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs,
     const bool red = lane < NR * R && lr < a.N;
     float s0 = 0.0f, prev = 0.0f;
     if (red) {
-      if (rb > 1 && ng == 1) s0 = __ldg(a.ws + lr);
+      if (rb > 1 && ng == 1) s0 = base == n0 ? s0_first : __ldg(a.ws + lr);
       if (a.mode == 1) prev = a.y[(size_t)lrr * a.ldy + lr];
     }
     const int nvalid = base >= a.N ? 0 : min(NR, (a.N - 1 - base) / nstep + 1);
-    gemv_products_nr<JM, SH, RB, NR>(wc, nvalid, a.K, rb, xq, xs, R, P, lane);
+    gemv_products_nr<JM, SH, RB, NR>(wc, nvalid, a.K, rb, xq, xs, R, P, LD, lane);
     __syncwarp();
     if (red) {
-      const float v = (rb > 1 && ng == 1) ? __fadd_rn(0.0f, __fmul_rn(seq_sum(P[lane], rb), s0))
-                                          : q8_reduce(P[lane], a.ws + (size_t)lr * ng, rb, ng);
+      const float v = q8_reduce_st(P + lane, LD, a.ws + (size_t)lr * ng, s0, rb, ng);
       a.y[(size_t)lrr * a.ldy + lr] = a.mode == 1 ? __fadd_rn(prev, v) : v;
     }
     __syncwarp();
@@ -326,10 +362,11 @@ template <int JM, int WARPS, int RB, bool PRO, bool SINGLE>
 __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   constexpr int NR = gemv_nr<JM>();
   extern __shared__ __align__(16) float gsm[];
-  typedef float PRow[JM * 32];
-  PRow* P = reinterpret_cast<PRow*>(gsm) + (size_t)(threadIdx.x >> 5) * (SINGLE ? 2 * kGemvRB : RB * NR);
-  PRow* P2 = P + kGemvRB;
-  float* pro = gsm + (size_t)WARPS * (SINGLE ? 2 * kGemvRB : RB * NR) * JM * 32;
+  // per-warp transposed product buffers (SINGLE: two of kGemvRB + 1 columns)
+  constexpr int PW = (SINGLE ? 2 * (kGemvRB + 1) : RB * NR + 1) * JM * 32;
+  float* P = gsm + (size_t)(threadIdx.x >> 5) * PW;
+  float* P2 = P + (kGemvRB + 1) * JM * 32;
+  float* pro = gsm + (size_t)WARPS * PW;
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * WARPS + (threadIdx.x >> 5);
@@ -350,10 +387,19 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
       if (r < a.N) load_wrow<JM>(wc[i], a.W + (size_t)r * a.K, a.ws + (size_t)r * ng, a.K, rb, lane);
     }
   }
+  // the first step's row scales of the reducing lanes (one per row)
+  float s_first = 0.0f, s2_first = 0.0f;
+  if (SINGLE) {
+    if (n0 < a.N && rb > 1 && ng == 1) s_first = __ldg(a.ws + n0);
+    if (n0 < a.N && a.W2 && (a.gs2 >> 5) > 1 && a.K2 == a.gs2) s2_first = __ldg(a.ws2 + n0);
+  } else {
+    const int li = lane / a.R, lr = n0 + li * nstep;
+    if (lane < NR * a.R && lr < a.N && rb > 1 && ng == 1) s_first = __ldg(a.ws + lr);
+  }
   pdl_wait();
   if (!PRO) {
-    if (SINGLE) gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P, P2, n0, lane);
-    else gemv_rows_multi<JM, WARPS, false, RB>(a, a.xq, a.xs, wc, P, n0, lane);
+    if (SINGLE) gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P, P2, n0, lane, s_first, s2_first);
+    else gemv_rows_multi<JM, WARPS, false, RB>(a, a.xq, a.xs, wc, P, n0, lane, s_first);
     return;
   }
   // input-norm prologue: rows -> shared (every load issued before the
@@ -394,31 +440,17 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   }
   __syncthreads();
   const bool store = a.nout && blockIdx.x == 0;
-  for (int g0 = warp * 4; g0 < R * gpr; g0 += WARPS * 4) {
-    float v[4];
-    int8_t q[4];
-    float sg[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int g = min(g0 + k, R * gpr - 1);
-      const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
-      v[k] = __fmul_rn(__fmul_rn(fx[(size_t)r * K + i], sinv[r]), __fadd_rn(1.0f, fw[i]));
-    }
-    warp_quant32_x4(v, q, sg);
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int g = g0 + k;
-      if (g < R * gpr) {
-        const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
-        sxq[(size_t)r * K + i] = q[k];
-        if (lane == 0) sxs[g] = sg[k];
-        if (store) a.nout[(size_t)r * K + i] = v[k];
-      }
-    }
+  // one 32-group per warp step (with the group max on redux.sync this
+  // measured faster than four interleaved groups)
+  for (int g = warp; g < R * gpr; g += WARPS) {
+    const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
+    const float v = __fmul_rn(__fmul_rn(fx[(size_t)r * K + i], sinv[r]), __fadd_rn(1.0f, fw[i]));
+    sxq[(size_t)r * K + i] = warp_quant32(v, &sxs[g]);
+    if (store) a.nout[(size_t)r * K + i] = v;
   }
   __syncthreads();
-  if (SINGLE) gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P, P2, n0, lane);
-  else gemv_rows_multi<JM, WARPS, true, RB>(a, sxq, sxs, wc, P, n0, lane);
+  if (SINGLE) gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P, P2, n0, lane, s_first, s2_first);
+  else gemv_rows_multi<JM, WARPS, true, RB>(a, sxq, sxs, wc, P, n0, lane, s_first);
 }
 
 // ------------------------------------------------------ tensor-core helpers
