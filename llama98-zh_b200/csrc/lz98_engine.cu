@@ -509,6 +509,7 @@ struct LZRunState {
   int *pair_e, *tok, *catch_tok, *catch_hidx;
   unsigned long long* vmax;
   int* row_counter;                  // last-block tails per (row, 32-group) (reset by the last block)
+  int* accept_counter;               // the fused greedy tail's block count (reset by its last block)
   // temperature rounds: draft distributions [B][kmax][V], target
   // distributions [Rmax][V], sort scratch [Rmax][npow2], sampled token
   float *qbuf = nullptr, *pbuf = nullptr, *sortbuf = nullptr;
@@ -738,7 +739,7 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
             dmalloc(s, &s->pair_e, P) && dmalloc(s, &s->pair_w, P) && dmalloc(s, &s->tok, R) &&
             dmalloc(s, &s->vmax, R) && dmalloc(s, &s->catch_tok, R) && dmalloc(s, &s->catch_hidx, R) &&
             dmalloc(s, &s->seqs, R) && dmalloc(s, &s->mrows, R) && dmalloc(s, &s->crows, R) &&
-            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R * (c.latent / 32 + 1)) && dmalloc(s, &s->tok_out, 4) &&
+            dmalloc(s, &s->sr, B) && dmalloc(s, &s->row_counter, R * (c.latent / 32 + 1)) && dmalloc(s, &s->accept_counter, 1) && dmalloc(s, &s->tok_out, 4) &&
             dmalloc(s, &s->pconf, 4);
   s->npow2 = 2;
   while (s->npow2 < c.vocab) s->npow2 <<= 1;
@@ -1215,13 +1216,18 @@ bool gemm_umma(LZRunState* s, const QW& w, const int8_t* xq, const float* xs, in
 // rmsnorm_quant grid into xq/xs first.
 void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, int ldy,
           int mode = 0, const QW* w2 = nullptr, const int8_t* xq2 = nullptr, const float* xs2 = nullptr,
-          const InNorm* nin = nullptr) {
+          const InNorm* nin = nullptr, const GemvFuse* fz = nullptr) {
   GemvArgs a{w.q, w.s, w.out, w.in, w.gs, xq, xs, R, y, ldy, mode,
              w2 ? w2->q : nullptr, w2 ? w2->s : nullptr, w2 ? w2->in : 0, w2 ? w2->gs : 32, xq2, xs2,
-             nullptr, nullptr, s->m->c.eps, nullptr, nullptr};
+             nullptr, nullptr, s->m->c.eps, nullptr, nullptr, {}};
   const bool prologue = nin && R <= kPrologueRows;
   if (prologue) {
     a.nx = nin->x; a.nw = nin->w; a.nout = nin->out; a.namax = nin->amax;
+    // the fused greedy tail: the slots were cleared by the round's setup kernel
+    if (fz) {
+      a.fz = *fz;
+      a.namax = nullptr;
+    }
   } else if (nin) {
     rmsnorm_quant(s, nin->x, w.in, nin->w, w.in, R, nin->out, w.in, xq, xs, nin->amax);
   }
@@ -1363,7 +1369,7 @@ void moe_ep(LZRunState* s, const DLayer& L, int R) {
 // Body forward of R rows (src/forward.c:1210-1617): embed, per layer
 // pre-norm -> KDA -> residual -> post-norm -> latent MoE -> residual, then
 // final norm (hidden capture) and the tied lm_head over every row.
-void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
+void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits, const GemvFuse* fz = nullptr) {
   const LZModel* m = s->m;
   const Cfg& c = m->c;
   const int d = c.d, kdim = c.key_dim, vdim = c.val_dim;
@@ -1424,7 +1430,7 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
   // final norm: hidden capture, then the tied lm_head
   if (want_logits) {
     const InNorm fin{s->x, m->final_norm, s->hidden, s->vmax};
-    gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin);
+    gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin, fz);
   } else {
     rmsnorm_quant(s, s->x, d, m->final_norm, d, R, s->hidden, d, s->xq, s->xs, s->vmax);
   }
@@ -1435,7 +1441,7 @@ void body_forward(LZRunState* s, int R, int nseq, int adv, bool want_logits) {
 // attention, o_proj, dense SwiGLU FFN, final norm into chain_out and the
 // tied lm_head into s->logits.
 void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const int* hid_idx,
-                 const MtpRow* rows, bool full, float* chain_out) {
+                 const MtpRow* rows, bool full, float* chain_out, const GemvFuse* fz = nullptr) {
   const LZModel* m = s->m;
   const Cfg& c = m->c;
   const DMtp& M = m->mtp;
@@ -1460,7 +1466,7 @@ void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const i
   launch(s, swiglu_quant_kernel, dim3(R), dim3(256), 0, s->inproj, 2 * c.mtp_ffn, 0, c.mtp_ffn, c.mtp_ffn, s->shq, s->shs);
   gemv(s, M.down, s->shq, s->shs, R, s->mtpx, d, 1);
   const InNorm fin{s->mtpx, M.norm, chain_out, s->vmax};
-  gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin);
+  gemv(s, m->embed, s->xq, s->xs, R, s->logits, c.vocab, 0, nullptr, nullptr, nullptr, &fin, fz);
 }
 
 __global__ void set_rows_kernel(MtpRow* rows, int n, int seq, int pos0, int seq_len) {
@@ -1473,11 +1479,14 @@ __global__ void set_rows_kernel(MtpRow* rows, int n, int seq, int pos0, int seq_
 // Rows whose MTP position would fall outside the cache are marked
 // inactive (no cache write, no attention): the memory stays in bounds and
 // the host's budget check (max_pos) keeps such rounds from being asked for.
-__global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_len, int* tok, MtpRow* rows) {
+// Also clears the rows' arg-max slots, which a fused lm_head folds into.
+__global__ void draft_setup_kernel(const SeqRound* sr, int nseq, int i, int seq_len, int* tok, MtpRow* rows,
+                                   unsigned long long* amax) {
   pdl_trigger();
   pdl_wait();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= nseq) return;
+  amax[b] = 0ull;
   tok[b] = i == 0 ? sr[b].anchor : sr[b].draft[i - 1];
   const int pos = sr[b].mtp_pos + i;
   rows[b] = MtpRow{b, pos, pos >= 0 && pos < seq_len};
@@ -1492,14 +1501,18 @@ __global__ void draft_store_kernel(SeqRound* sr, int nseq, int i, int k, const u
   sr[b].k = k;
 }
 
-__global__ void verify_setup_kernel(const SeqRound* sr, int nseq, int k, int* tok, KdaSeq* seqs) {
+// Also clears the verify rows' arg-max slots, which a fused lm_head folds into.
+__global__ void verify_setup_kernel(const SeqRound* sr, int nseq, int k, int* tok, KdaSeq* seqs,
+                                    unsigned long long* amax) {
   pdl_trigger();
   pdl_wait();
   int b = blockIdx.x;
   if (b >= nseq) return;
   if (threadIdx.x == 0) seqs[b] = KdaSeq{b * (k + 1), k + 1, sr[b].ssm_slot, b};
-  for (int j = threadIdx.x; j <= k; j += blockDim.x)
+  for (int j = threadIdx.x; j <= k; j += blockDim.x) {
     tok[b * (k + 1) + j] = j == 0 ? sr[b].anchor : sr[b].draft[j - 1];
+    amax[b * (k + 1) + j] = 0ull;
+  }
 }
 
 int upload_seqs(LZRunState* s, const std::vector<KdaSeq>& v) {
@@ -1520,11 +1533,19 @@ void dbg_mark(LZRunState* s, int i) {
 void verify_greedy(LZRunState* s, int k) {
   const Cfg& c = s->m->c;
   const int B = s->B, R = B * (k + 1);
-  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
-  body_forward(s, R, B, 1, true);
-  argmax(s, s->logits, R, 0);
-  launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain, s->depth,
-                                                  s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs, s->vmax);
+  if (R <= kPrologueRows) {
+    // logits to acceptance in the lm_head's own launch: arg-max folded into
+    // its reductions, the acceptance by its last block
+    const GemvFuse fz{s->vmax, 0, s->sr, B, k, s->hidden, c.d, s->chain, s->depth, s->seq_len, s->crows,
+                      s->catch_tok, s->catch_hidx, s->accept_counter};
+    body_forward(s, R, B, 1, true, &fz);
+  } else {
+    body_forward(s, R, B, 1, true);
+    argmax(s, s->logits, R, 0);
+    launch(s, spec_accept_greedy_kernel, dim3(B), dim3(256), 0, s->sr, B, k, s->vmax, s->hidden, c.d, s->chain,
+           s->depth, s->seq_len, s->crows, s->catch_tok, s->catch_hidx);
+  }
   dbg_mark(s, 2);
   if (k > 1)
     mtp_forward(s, B * (k - 1), s->catch_tok, s->hidden, s->catch_hidx, s->crows, false, nullptr);
@@ -1535,7 +1556,7 @@ void verify_greedy(LZRunState* s, int k) {
 void verify_temp(LZRunState* s, int k) {
   const Cfg& c = s->m->c;
   const int B = s->B, V = c.vocab, R = B * (k + 1);
-  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs);
+  launch(s, verify_setup_kernel, dim3(B), dim3(32), 0, s->sr, B, k, s->tok, s->seqs, s->vmax);
   body_forward(s, R, B, 1, true);
   launch(s, temp_target_kernel, dim3(R), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, k, s->pbuf,
          s->sortbuf, s->npow2);
@@ -1553,9 +1574,15 @@ void round_greedy(LZRunState* s, int k) {
   const int tb = (B + 127) / 128;
   dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
-    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
-    mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
-    argmax(s, s->logits, B, 1);
+    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows, s->vmax);
+    if (B <= kPrologueRows) {
+      // the draft arg-max folded into the lm_head's reductions
+      const GemvFuse fz{s->vmax, 1, nullptr, 0, 0, nullptr, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr};
+      mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain, &fz);
+    } else {
+      mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
+      argmax(s, s->logits, B, 1);
+    }
     launch(s, draft_store_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, k, s->vmax);
   }
   dbg_mark(s, 1);
@@ -1573,7 +1600,7 @@ void round_temp(LZRunState* s, int k) {
   const int tb = (B + 127) / 128;
   dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
-    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows);
+    launch(s, draft_setup_kernel, dim3(tb), dim3(128), 0, s->sr, B, i, s->seq_len, s->tok, s->mrows, s->vmax);
     mtp_forward(s, B, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
     launch(s, temp_draft_kernel, dim3(B), dim3(kSampThreads), kSampSmem, s->logits, V, s->sr, i, k, s->kmax,
            s->qbuf);
@@ -1604,7 +1631,7 @@ int draft_pmin(LZRunState* s, int k, bool temp, float p_min) {
   int k_eff = 0;
   dbg_mark(s, 0);
   for (int i = 0; i < k; i++) {
-    launch(s, draft_setup_kernel, dim3(1), dim3(128), 0, s->sr, 1, i, s->seq_len, s->tok, s->mrows);
+    launch(s, draft_setup_kernel, dim3(1), dim3(128), 0, s->sr, 1, i, s->seq_len, s->tok, s->mrows, s->vmax);
     mtp_forward(s, 1, s->tok, s->chain, nullptr, s->mrows, true, s->chain);
     float conf = 0.0f;
     if (temp) {

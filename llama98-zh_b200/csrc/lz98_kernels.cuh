@@ -140,6 +140,26 @@ LZ_HD int dot32(const int4 wa, const int4 wb, const int4 xa, const int4 xb) {
   return a0 + a1;
 }
 
+struct SeqRound;
+struct MtpRow;
+
+// The fused greedy tail of an lm_head GEMV of at most 8 token rows (the
+// logits-to-acceptance path of a greedy round): every block folds the
+// arg-max of its outputs per token row into amax (the packed order key of
+// argmax_kernel, one atomic per block and row; the slots are cleared by
+// an earlier kernel of the round), and, when sr is set, the last block to
+// finish runs the round's acceptance (spec_accept_greedy_kernel's work)
+// for every sequence.
+struct GemvFuse {
+  unsigned long long* amax;   // nullptr: off
+  int p1;                     // -0 compares equal to +0 (the draft steps)
+  SeqRound* sr; int nseq, kmax;
+  const float* vhid; int d; float* chain; int depth, seq_len;
+  MtpRow* catch_rows; int* catch_tok; int* catch_hidx;
+  int* counter;
+};
+LZ_HD void greedy_accept_all(const GemvFuse& f);
+
 struct GemvArgs {
   const int8_t* W; const float* ws; int N, K, gs;
   const int8_t* xq; const float* xs; int R;      // quantised input rows
@@ -154,6 +174,7 @@ struct GemvArgs {
   // per 32 into shared memory; block 0 also stores the normalised rows to
   // nout and clears the arg-max slots namax.
   const float* nx; const float* nw; float eps; float* nout; unsigned long long* namax;
+  GemvFuse fz;               // fused arg-max / acceptance (input-norm path only)
 };
 
 // Four 32-element groups at once (one element of each per lane): the
@@ -315,7 +336,7 @@ LZ_HD void gemv_rows(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<
 // (R <= RB <= 8), then their NR * R reductions on as many lanes at once.
 template <int JM, int WARPS, bool SH, int RB>
 LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs, WRow<JM> (&wc)[gemv_nr<JM>()],
-                           float* P, int n0, int lane, float s0_first) {
+                           float* P, int n0, int lane, float s0_first, unsigned long long& kbest) {
   constexpr int NR = gemv_nr<JM>(), LD = RB * NR + 1;
   const int rb = a.gs >> 5, ng = a.K / a.gs, R = a.R;
   const int nstep = gridDim.x * WARPS;
@@ -342,6 +363,11 @@ LZ_HD void gemv_rows_multi(const GemvArgs& a, const int8_t* xq, const float* xs,
     if (red) {
       const float v = q8_reduce_st(P + lane, LD, a.ws + (size_t)lr * ng, s0, rb, ng);
       a.y[(size_t)lrr * a.ldy + lr] = a.mode == 1 ? __fadd_rn(prev, v) : v;
+      if (a.fz.amax) {
+        const float vk = (a.fz.p1 && v == 0.0f) ? 0.0f : v;
+        const unsigned long long key = ((unsigned long long)fkey(vk) << 32) | (0xFFFFFFFFu - (uint32_t)lr);
+        kbest = key > kbest ? key : kbest;
+      }
     }
     __syncwarp();
 #pragma unroll
@@ -398,8 +424,9 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   }
   pdl_wait();
   if (!PRO) {
+    unsigned long long kb = 0ull;
     if (SINGLE) gemv_rows<JM, WARPS, false>(a, a.xq, a.xs, w1, w2, P, P2, n0, lane, s_first, s2_first);
-    else gemv_rows_multi<JM, WARPS, false, RB>(a, a.xq, a.xs, wc, P, n0, lane, s_first);
+    else gemv_rows_multi<JM, WARPS, false, RB>(a, a.xq, a.xs, wc, P, n0, lane, s_first, kb);
     return;
   }
   // input-norm prologue: rows -> shared (every load issued before the
@@ -449,8 +476,43 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
     if (store) a.nout[(size_t)r * K + i] = v;
   }
   __syncthreads();
+  unsigned long long kb = 0ull;
   if (SINGLE) gemv_rows<JM, WARPS, true>(a, sxq, sxs, w1, w2, P, P2, n0, lane, s_first, s2_first);
-  else gemv_rows_multi<JM, WARPS, true, RB>(a, sxq, sxs, wc, P, n0, lane, s_first);
+  else gemv_rows_multi<JM, WARPS, true, RB>(a, sxq, sxs, wc, P, n0, lane, s_first, kb);
+  if (!SINGLE && a.fz.amax) {
+    // the block's arg-max per token row, one atomic per row
+    __shared__ unsigned long long wbest[WARPS][kGemvRB];
+    const int li = lane / R, lrr = lane - li * R;
+    for (int rr = 0; rr < R; rr++) {
+      unsigned long long v = (lane < NR * R && lrr == rr) ? kb : 0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+      }
+      if (lane == 0) wbest[warp][rr] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < R) {
+      unsigned long long m = 0ull;
+      for (int w = 0; w < WARPS; w++) m = wbest[w][threadIdx.x] > m ? wbest[w][threadIdx.x] : m;
+      atomicMax(a.fz.amax + threadIdx.x, m);
+    }
+    if (a.fz.sr) {
+      // the last block: every row's arg-max is final, the hidden rows
+      // (block 0's prologue) are written; the round's acceptance
+      __shared__ int s_lastblk;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) s_lastblk = atomicAdd(a.fz.counter, 1) == (int)gridDim.x - 1;
+      __syncthreads();
+      if (s_lastblk) {
+        __threadfence();
+        greedy_accept_all(a.fz);
+        if (threadIdx.x == 0) *a.fz.counter = 0;
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------ tensor-core helpers
@@ -2475,6 +2537,36 @@ LZ_HD void round_bookkeeping(SeqRound& s, int b, int n_accept, int k, int kmax, 
 // the state ring at the accepted slot, reseed the draft chain from the
 // verify hidden row n_accept, set up the catch-up rows and advance the
 // MTP position.
+// One sequence's acceptance, by every thread of the calling block.
+LZ_HD void greedy_accept_seq(SeqRound* sr, int b, int kmax, const unsigned long long* vmax, const float* vhid, int d,
+                             float* chain, int depth, int seq_len, MtpRow* catch_rows, int* catch_tok,
+                             int* catch_hidx) {
+  SeqRound& s = sr[b];
+  const int row0 = b * (kmax + 1);
+  __shared__ int n_acc_s;
+  if (threadIdx.x == 0) {
+    const int k = s.k;
+    int n_accept = k;
+    for (int i = 0; i < k; i++) {
+      s.out[i] = argmax_index(__ldcg(vmax + row0 + i));
+      if (s.draft[i] != s.out[i]) { n_accept = i; break; }
+    }
+    if (n_accept == k) s.out[k] = argmax_index(__ldcg(vmax + row0 + k));
+    round_bookkeeping(s, b, n_accept, k, kmax, row0, depth, seq_len, catch_rows, catch_tok, catch_hidx);
+    n_acc_s = n_accept;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    chain[(size_t)b * d + i] = __ldcg(vhid + (size_t)(row0 + n_acc_s) * d + i);
+  __syncthreads();
+}
+
+LZ_HD void greedy_accept_all(const GemvFuse& f) {
+  for (int b = 0; b < f.nseq; b++)
+    greedy_accept_seq(f.sr, b, f.kmax, f.amax, f.vhid, f.d, f.chain, f.depth, f.seq_len, f.catch_rows, f.catch_tok,
+                      f.catch_hidx);
+}
+
 __global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax,
                                           const unsigned long long* __restrict__ vmax,
                                           const float* __restrict__ vhid, int d, float* chain,
@@ -2484,23 +2576,7 @@ __global__ void spec_accept_greedy_kernel(SeqRound* sr, int nseq, int kmax,
   pdl_wait();
   const int b = blockIdx.x;
   if (b >= nseq) return;
-  SeqRound& s = sr[b];
-  const int k = s.k;
-  const int row0 = b * (kmax + 1);
-  __shared__ int n_acc_s;
-  if (threadIdx.x == 0) {
-    int n_accept = k;
-    for (int i = 0; i < k; i++) {
-      s.out[i] = argmax_index(vmax[row0 + i]);
-      if (s.draft[i] != s.out[i]) { n_accept = i; break; }
-    }
-    if (n_accept == k) s.out[k] = argmax_index(vmax[row0 + k]);
-    round_bookkeeping(s, b, n_accept, k, kmax, row0, depth, seq_len, catch_rows, catch_tok, catch_hidx);
-    n_acc_s = n_accept;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x)
-    chain[(size_t)b * d + i] = vhid[(size_t)(row0 + n_acc_s) * d + i];
+  greedy_accept_seq(sr, b, kmax, vmax, vhid, d, chain, depth, seq_len, catch_rows, catch_tok, catch_hidx);
 }
 
 }  // namespace lz98
