@@ -1192,11 +1192,15 @@ constexpr int kRankMax = 128;
 // it (hi as a float is exact, so it is adjusted with hq).
 LZ_HD void requant_2p(float buf, float iv, int8_t& h8, int8_t& l8, float& e) {
   const float f = __fmul_rn(buf, iv);
-  int hq = q8_clamp(q8_round(f));
-  float hf = (float)hq;
-  float res = __fsub_rn(f, hf);
-  if (res >= 0.5f) { if (hq < 127) { hq += 1; hf = __fadd_rn(hf, 1.0f); res = __fsub_rn(res, 1.0f); } }
-  else if (res < -0.5f) { if (hq > -127) { hq -= 1; hf = __fsub_rn(hf, 1.0f); res = __fadd_rn(res, 1.0f); } }
+  const int hq0 = q8_clamp(q8_round(f));
+  const float hf0 = (float)hq0;
+  const float res0 = __fsub_rn(f, hf0);
+  // the residual's half-up correction, by selects (the two cases exclude
+  // each other)
+  const bool up = res0 >= 0.5f && hq0 < 127, dn = res0 < -0.5f && hq0 > -127;
+  const int hq = hq0 + (up ? 1 : 0) - (dn ? 1 : 0);
+  const float hf = up ? __fadd_rn(hf0, 1.0f) : (dn ? __fsub_rn(hf0, 1.0f) : hf0);
+  const float res = up ? __fsub_rn(res0, 1.0f) : (dn ? __fadd_rn(res0, 1.0f) : res0);
   h8 = (int8_t)hq;
   const int lq = q8_clamp(q8_round(__fmul_rn(res, kLoScale)));
   l8 = (int8_t)lq;
@@ -1219,6 +1223,8 @@ LZ_HD void kda_layer(const KdaArgs& a) {
   __shared__ __align__(16) float E[KD][VC];
   __shared__ float sc[KD][GPC];
   __shared__ __align__(16) float qn[TB][KD], kn[TB][KD], gv[TB][KD], KG[TB][KD], QG[TB][KD];
+  // the current token's scale products sc * (k*g) and sc * (q*g) of pass 1
+  __shared__ float SCK[KD][GPC], SCQ[KD][GPC];
   __shared__ __align__(16) float vcs[TB][VC], zs[TB][VC];
   // the head outputs of a batch, both value groups (SPLIT = 2: the peer
   // writes its group into this copy); two buffers by batch parity, so a
@@ -1316,7 +1322,25 @@ LZ_HD void kda_layer(const KdaArgs& a) {
       E[row][c16 * 16 + j] = __fadd_rn((float)hb[j], __fmul_rn((float)lb[j], 1.0f / kLoScale));
   }
   if (tid < KD * GPC) sc[tid / GPC][tid % GPC] = ssc;
-  for (int t0 = 0; t0 < sq.nrows; t0 += TB) {
+  int t0 = 0;
+  // ring slot of batch token t (verify steps): this CTA's state planes and
+  // row scales, copied from shared memory in 16-byte pieces by threads
+  // i0, i0 + step, ...
+  auto ring_copy = [&](int t, int i0, int step) {
+    const size_t ring = seq_off + (size_t)((sq.base_slot + t0 + t + 1) % a.depth) * a.slot_stride_q + head_off;
+    for (int q = i0; q < 2 * SQ + KD * GPC; q += step) {
+      if (q < 2 * SQ) {
+        const int pl = q / SQ, qq = q - pl * SQ, row = qq / (VC / 16), c16 = qq - row * (VC / 16);
+        const size_t o = ring + (size_t)row * VD + vcol0 + c16 * 16;
+        if (pl == 0) *reinterpret_cast<int4*>(a.st_hi + o) = *reinterpret_cast<const int4*>(&hi[row][c16 * 16]);
+        else *reinterpret_cast<int4*>(a.st_lo + o) = *reinterpret_cast<const int4*>(&lo[row][c16 * 16]);
+      } else {
+        const int u = q - 2 * SQ, kk = u / GPC, gl = u - kk * GPC;
+        a.st_sc[ring / 32 + kk * (VD / 32) + grp * GPC + gl] = sc[kk][gl];
+      }
+    }
+  };
+  for (; t0 < sq.nrows; t0 += TB) {
     const int nt = min(TB, sq.nrows - t0);
     float (*OUT)[VD] = OUT2[(t0 / TB) & 1];
     if (t0 > 0) issue(t0, nt);
@@ -1393,6 +1417,12 @@ LZ_HD void kda_layer(const KdaArgs& a) {
       kn[t][i] = kv;
       KG[t][i] = __fmul_rn(kv, gv[t][i]);
       QG[t][i] = __fmul_rn(qv, gv[t][i]);
+      if (t == 0)
+#pragma unroll
+        for (int gl = 0; gl < GPC; gl++) {
+          SCK[i][gl] = __fmul_rn(sc[i][gl], KG[0][i]);
+          SCQ[i][gl] = __fmul_rn(sc[i][gl], QG[0][i]);
+        }
     }
     __syncthreads();
     for (int t = 0; t < nt; t++) {
@@ -1403,10 +1433,17 @@ LZ_HD void kda_layer(const KdaArgs& a) {
       if (tid < 2 * VC) {
         const bool isw = tid >= VC;
         const int c = isw ? tid - VC : tid, gl = c >> 5;
-        const float* G = isw ? QG[t] : KG[t];
+        const float* Sx = isw ? &SCQ[0][gl] : &SCK[0][gl];
         float acc = 0.0f;
-#pragma unroll 8
-        for (int kk = 0; kk < KD; kk++) acc = __fadd_rn(acc, __fmul_rn(E[kk][c], __fmul_rn(sc[kk][gl], G[kk])));
+        // 16 products formed ahead of their adds (the adds stay in order)
+#pragma unroll
+        for (int k0 = 0; k0 < KD; k0 += 16) {
+          float pr[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) pr[j] = __fmul_rn(E[k0 + j][c], Sx[(k0 + j) * GPC]);
+#pragma unroll
+          for (int j = 0; j < 16; j++) acc = __fadd_rn(acc, pr[j]);
+        }
         if (isw) AW[c] = acc;
         else U[c] = __fmul_rn(__fsub_rn(vcs[t][c], acc), beta[t]);
       } else if (t == 0 && tid < 2 * VC + nt) {
@@ -1415,16 +1452,17 @@ LZ_HD void kda_layer(const KdaArgs& a) {
 #pragma unroll 8
         for (int kk = 0; kk < KD; kk++) kq = __fadd_rn(kq, __fmul_rn(kn[tt][kk], qn[tt][kk]));
         kqs[tt] = kq;
+      } else if (a.adv && t > 0 && tid >= 2 * VC + TB) {
+        // the previous token's ring slot, from the shared state, by the
+        // threads pass 1 leaves idle
+        ring_copy(t - 1, tid - (2 * VC + TB), NTH - (2 * VC + TB));
       }
       __syncthreads();
       // the head output w + u * kq of this CTA's columns
       if (tid < VC) OUT[t][vcol0 + tid] = __fadd_rn(AW[tid], __fmul_rn(U[tid], kqs[t]));
       // pass 2: the (state row, 32-wide group) units, four per warp at a
-      // time with their max reductions interleaved; a verify step writes
-      // its ring slot straight from here
-      const size_t ring = a.adv ? seq_off + (size_t)((sq.base_slot + t0 + t + 1) % a.depth) * a.slot_stride_q +
-                                      head_off
-                                : 0;
+      // time with their max reductions interleaved; the new row scales
+      // also give the next token's pass-1 products
       for (int u0 = warp * 4; u0 < KD * GPC; u0 += NW * 4) {
         float buf[4];
         uint32_t am[4];
@@ -1448,20 +1486,21 @@ LZ_HD void kda_layer(const KdaArgs& a) {
           float e;
           requant_2p(buf[c], iv, h8, l8, e);
           E[kk][col] = e;
-          if (lane == 0) sc[kk][gl] = sg;
-          if (a.adv) {
-            const size_t o = ring + (size_t)kk * VD + vcol0 + col;
-            a.st_hi[o] = h8;
-            a.st_lo[o] = l8;
-            if (lane == 0) a.st_sc[ring / 32 + kk * (VD / 32) + grp * GPC + gl] = sg;
-          } else {
-            hi[kk][col] = h8;
-            lo[kk][col] = l8;
+          hi[kk][col] = h8;
+          lo[kk][col] = l8;
+          if (lane == 0) {
+            sc[kk][gl] = sg;
+            if (t + 1 < nt) {
+              SCK[kk][gl] = __fmul_rn(sg, KG[t + 1][kk]);
+              SCQ[kk][gl] = __fmul_rn(sg, QG[t + 1][kk]);
+            }
           }
         }
       }
       __syncthreads();
     }
+    // the batch's last ring slot
+    if (a.adv) ring_copy(nt - 1, tid, NTH);
     // this CTA's half of every token's head output into the peer's copy,
     // then one cluster barrier: both copies whole
     if (SPLIT > 1) {
