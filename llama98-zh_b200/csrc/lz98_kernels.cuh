@@ -2454,27 +2454,50 @@ mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
   __syncthreads();
   head_norm_rope(qh, q_norm, eps, hd, rot, rope_cs + (size_t)pos * rot, &s_red[0]);
   const size_t cb = (size_t)row.seq * cache_seq_stride;
-  uint32_t bk = 0;
-  for (int t = i; t <= pos; t += blockDim.x) {
-    const int8_t* kt = kq + cb + (size_t)t * kvd + kvh * hd;
-    const float* kts = ks + (cb + (size_t)t * kvd + kvh * hd) / 32;
-    int4 k4[4];
+  // the query in registers; two positions per step, their K rows loaded
+  // together and their score chains interleaved (each in the reference's
+  // order)
+  float qr[64];
 #pragma unroll
-    for (int c = 0; c < 4; c++) k4[c] = __ldg(reinterpret_cast<const int4*>(kt) + c);
-    const float s0 = __ldg(kts), s1 = __ldg(kts + 1);
-    const int8_t* kb = reinterpret_cast<const int8_t*>(k4);
-    float sum = 0.0f;
+  for (int e = 0; e < 64; e++) qr[e] = qh[e];
+  uint32_t bk = 0;
+  for (int t = i; t <= pos; t += 2 * blockDim.x) {
+    const int tb = t + blockDim.x;
+    const bool two = tb <= pos;
+    int4 k4[2][4];
+    float sc2[2][2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int tu = u ? (two ? tb : t) : t;
+      const int8_t* kt = kq + cb + (size_t)tu * kvd + kvh * hd;
+      const float* kts = ks + (cb + (size_t)tu * kvd + kvh * hd) / 32;
+#pragma unroll
+      for (int c = 0; c < 4; c++) k4[u][c] = __ldg(reinterpret_cast<const int4*>(kt) + c);
+      sc2[u][0] = __ldg(kts);
+      sc2[u][1] = __ldg(kts + 1);
+    }
+    float sum[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int dd = 0; dd < 64; dd += 32) {
-      float acc = 0.0f;
+      float acc[2] = {0.0f, 0.0f};
 #pragma unroll
-      for (int e = 0; e < 32; e++) acc = __fadd_rn(acc, __fmul_rn(qh[dd + e], (float)kb[dd + e]));
-      sum = __fadd_rn(sum, __fmul_rn(acc, dd ? s1 : s0));
+      for (int e = 0; e < 32; e++)
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const int8_t kv = reinterpret_cast<const int8_t*>(k4[u])[dd + e];
+          acc[u] = __fadd_rn(acc[u], __fmul_rn(qr[dd + e], (float)kv));
+        }
+#pragma unroll
+      for (int u = 0; u < 2; u++) sum[u] = __fadd_rn(sum[u], __fmul_rn(acc[u], sc2[u][dd ? 1 : 0]));
     }
-    const float a = __fmul_rn(sum, scale);
-    att[t] = a;
-    const uint32_t k = fkey(a);
-    bk = k > bk ? k : bk;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      if (u == 1 && !two) break;
+      const float a = __fmul_rn(sum[u], scale);
+      att[u ? tb : t] = a;
+      const uint32_t k = fkey(a);
+      bk = k > bk ? k : bk;
+    }
   }
   bk = warp_max_u32(bk);
   if ((i & 31) == 0) wk[i >> 5] = bk;
@@ -2500,21 +2523,47 @@ mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
   for (int t0 = 0; t0 <= pos; t0 += kAttnChunk) {
     const int nt = min(kAttnChunk, pos + 1 - t0);
     __syncthreads();
-    for (int q = i; q < nt * 4; q += blockDim.x) {
-      const int tt = q >> 2, c = q & 3;
-      reinterpret_cast<int4*>(&vch[tt][0])[c] =
-          __ldg(reinterpret_cast<const int4*>(vq + cb + (size_t)(t0 + tt) * kvd + kvh * hd) + c);
-    }
-    for (int q = i; q < nt * 2; q += blockDim.x) {
-      const int tt = q >> 1, c = q & 1;
-      vsc[tt][c] = __ldg(vs + (cb + (size_t)(t0 + tt) * kvd + kvh * hd) / 32 + c);
+    {
+      // the chunk's V rows and scales: every load in flight before the
+      // first store
+      constexpr int LV = kAttnChunk * 4 / kAttnThreads, LS = kAttnChunk * 2 / kAttnThreads;
+      int4 v4[LV];
+      float s4[LS];
+#pragma unroll
+      for (int u = 0; u < LV; u++) {
+        const int q = i + u * kAttnThreads, tt = q >> 2, c = q & 3;
+        if (tt < nt) v4[u] = __ldg(reinterpret_cast<const int4*>(vq + cb + (size_t)(t0 + tt) * kvd + kvh * hd) + c);
+      }
+#pragma unroll
+      for (int u = 0; u < LS; u++) {
+        const int q = i + u * kAttnThreads, tt = q >> 1, c = q & 1;
+        if (tt < nt) s4[u] = __ldg(vs + (cb + (size_t)(t0 + tt) * kvd + kvh * hd) / 32 + c);
+      }
+#pragma unroll
+      for (int u = 0; u < LV; u++) {
+        const int q = i + u * kAttnThreads, tt = q >> 2, c = q & 3;
+        if (tt < nt) reinterpret_cast<int4*>(&vch[tt][0])[c] = v4[u];
+      }
+#pragma unroll
+      for (int u = 0; u < LS; u++) {
+        const int q = i + u * kAttnThreads, tt = q >> 1, c = q & 1;
+        if (tt < nt) vsc[tt][c] = s4[u];
+      }
     }
     __syncthreads();
     if (i < hd) {
       const int g = i >> 5;
-#pragma unroll 8
-      for (int tt = 0; tt < nt; tt++)
-        out = __fadd_rn(out, __fmul_rn(__fmul_rn(att[t0 + tt], (float)vch[tt][i]), vsc[tt][g]));
+      int tt = 0;
+      // 16 products formed ahead of their adds (the adds stay in order)
+      for (; tt + 16 <= nt; tt += 16) {
+        float pr[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          pr[j] = __fmul_rn(__fmul_rn(att[t0 + tt + j], (float)vch[tt + j][i]), vsc[tt + j][g]);
+#pragma unroll
+        for (int j = 0; j < 16; j++) out = __fadd_rn(out, pr[j]);
+      }
+      for (; tt < nt; tt++) out = __fadd_rn(out, __fmul_rn(__fmul_rn(att[t0 + tt], (float)vch[tt][i]), vsc[tt][g]));
     }
   }
   if (i < hd) {
