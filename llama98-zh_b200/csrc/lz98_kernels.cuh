@@ -2426,7 +2426,7 @@ __global__ void mtp_kv_write_kernel(const float* __restrict__ qkv, int ldq, int 
 // V staged through shared memory in chunks), times sigmoid(gate), then
 // per-32 quantisation for o_proj.  hd = 64.
 // src/forward_attn.c:17-41, 206-640, src/ops_norm.c:903-985.
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kAttnChunk = 256;
 __global__ void __launch_bounds__(kAttnThreads)
 mtp_attn_kernel(const float* __restrict__ qkv, int ldq, int qd,
