@@ -789,6 +789,14 @@ static int state_alloc(LZRunState** out, const LZModel* m, int n_seq, int seq_le
       lz_state_free(s);
       return LZ98_ERR_ALLOC;
     }
+    // the MTP front keeps its two rows and their squares: 4 d + 32 floats
+    const int front = (4 * m->c.d + 32) * (int)sizeof(float);
+    if (front > 48 * 1024 &&
+        cudaFuncSetAttribute(mtp_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, front) != cudaSuccess) {
+      set_err(errbuf, errlen, "hidden size too large for the MTP front kernel's shared memory");
+      lz_state_free(s);
+      return LZ98_ERR_ALLOC;
+    }
   }
   std::vector<float> rope;
   build_rope(c, seq_len, rope);
@@ -1446,7 +1454,7 @@ void mtp_forward(LZRunState* s, int R, const int* tok, const float* hid, const i
   const Cfg& c = m->c;
   const DMtp& M = m->mtp;
   const int d = c.d;
-  launch(s, mtp_front_kernel, dim3(R), dim3(256), 2 * d * sizeof(float), m->embed.q, m->embed.s, m->embed.gs, d, tok,
+  launch(s, mtp_front_kernel, dim3(R), dim3(256), (4 * d + 32) * sizeof(float), m->embed.q, m->embed.s, m->embed.gs, d, tok,
                                                              hid, hid_idx, M.pre_e, M.pre_h, c.eps, s->xq,
                                                              s->xs);
   gemv(s, M.fc, s->xq, s->xs, R, s->mtpx, d);

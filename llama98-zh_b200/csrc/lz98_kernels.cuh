@@ -45,6 +45,110 @@ LZ_HD float seq_sumsq(const float* v, int n) {
   return ss;
 }
 
+// The same sequential sum of squares over a row of K floats (K % 512 == 0)
+// by a group of 128 threads, in about half the chain's time.  The row
+// splits into four segments.  The group squares the row into `sq` (one
+// segment per warp, each segment padded by 16 bytes so the segments sit on
+// different banks) and sums each segment's squares as a float tree.  Two
+// warps of the group then run the chains, two per lane on each loaded
+// square: lane 0 the first segment's chain from zero, the other lanes the
+// later segments' chains from candidate starts - the consecutive floats
+// around the segment's prefix of tree sums (32, 32 and 62 of them).  The
+// sequential prefix departs from that estimate by a few units in the last
+// place (under half an ulp per add, a random walk), so one candidate
+// almost always starts exactly from it.  Lane 0 walks the segments: the
+// candidate whose start equals the prefix reached so far is found by
+// index, and a segment with no such candidate is chained by lane 0 itself.
+// The result is the sequential sum bit for bit (src/ops_norm.c:718).
+// (Shared-memory bandwidth bounds the chains: each lane reads its whole
+// segment, so two chains per lane halve the bytes of one.)
+//   x: the row in shared memory (16-byte aligned); sq: shared scratch of
+//   K + 16 floats; u: the thread's index in the group; cw: the first of
+//   the two chain warps (0 or 2); r: the group (0-3), which names its
+//   barriers.  Returns the sum in lane 0 of warp cw (0 elsewhere).
+constexpr int kSplitGroup = 128;
+struct SplitSumShared {
+  float part[4];
+  float end[128];
+};
+
+// named barriers with immediate ids: the group's 128 threads (ids 1-4),
+// then its two chain warps (ids 5-8)
+LZ_HD void group_bar(int r) {
+  switch (r) {
+    case 0: asm volatile("bar.sync 1, 128;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
+  }
+}
+LZ_HD void chain_bar(int r) {
+  switch (r) {
+    case 0: asm volatile("bar.sync 5, 64;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 6, 64;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 7, 64;" ::: "memory"); break;
+    default: asm volatile("bar.sync 8, 64;" ::: "memory"); break;
+  }
+}
+
+LZ_HD float seq_sumsq_split(const float* x, float* sq, int K, int u, int cw, int r, SplitSumShared& sh) {
+  const int L = K / 4, LP = L + 4, per = K / kSplitGroup, su = u >> 5;
+  float acc = 0.0f;
+  for (int i = u * per; i < (u + 1) * per; i += 4) {
+    const float4 q = *reinterpret_cast<const float4*>(x + i);
+    const float4 p = make_float4(__fmul_rn(q.x, q.x), __fmul_rn(q.y, q.y), __fmul_rn(q.z, q.z), __fmul_rn(q.w, q.w));
+    *reinterpret_cast<float4*>(sq + su * LP + (i - su * L)) = p;
+    acc = __fadd_rn(acc, __fadd_rn(__fadd_rn(p.x, p.y), __fadd_rn(p.z, p.w)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if ((u & 31) == 0) sh.part[su] = acc;
+  group_bar(r);
+  const int t = u - 32 * cw;            // chain lane, 0-63
+  if (t < 0 || t >= 64) return 0.0f;
+  const float g1 = sh.part[0], g2 = __fadd_rn(g1, sh.part[1]), g3 = __fadd_rn(g2, sh.part[2]);
+  int seg = 0, o = 0;
+  float g = 0.0f;
+  if (t >= 33) seg = 3, g = g3, o = 2 * (t - 33) - 31;
+  else if (t >= 17) seg = 2, g = g2, o = 2 * (t - 17) - 16;
+  else if (t >= 1) seg = 1, g = g1, o = 2 * (t - 1) - 16;
+  float c0 = 0.0f, c1 = 0.0f;
+  if (t > 0) {
+    c0 = __int_as_float(__float_as_int(g) + o);
+    c1 = __int_as_float(__float_as_int(g) + o + 1);
+  }
+  const float4* p = reinterpret_cast<const float4*>(sq + seg * LP);
+#pragma unroll 4
+  for (int i = 0; i < L / 4; i++) {
+    const float4 q = p[i];
+    c0 = __fadd_rn(c0, q.x);
+    c1 = __fadd_rn(c1, q.x);
+    c0 = __fadd_rn(c0, q.y);
+    c1 = __fadd_rn(c1, q.y);
+    c0 = __fadd_rn(c0, q.z);
+    c1 = __fadd_rn(c1, q.z);
+    c0 = __fadd_rn(c0, q.w);
+    c1 = __fadd_rn(c1, q.w);
+  }
+  *reinterpret_cast<float2*>(&sh.end[2 * t]) = make_float2(c0, c1);
+  chain_bar(r);
+  if (t != 0) return 0.0f;
+  float v = c0;
+  const float gs[3] = {g1, g2, g3};
+  const int first[3] = {2, 34, 66}, ctr[3] = {16, 16, 31}, nc[3] = {32, 32, 62};
+#pragma unroll
+  for (int s = 0; s < 3; s++) {
+    const int d = __float_as_int(v) - __float_as_int(gs[s]) + ctr[s];
+    if ((unsigned)d < (unsigned)nc[s]) {
+      v = sh.end[first[s] + d];
+    } else {   // no candidate started from the prefix: chain the segment here
+      const float* ps = sq + (s + 1) * LP;
+      for (int i = 0; i < L; i++) v = __fadd_rn(v, ps[i]);
+    }
+  }
+  return v;
+}
+
 // Sequential sum (index order) of a 16-byte aligned array, any n.
 LZ_HD float seq_sum(const float* v, int n) {
   float s = 0.0f;
@@ -461,7 +565,17 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   }
   if (a.namax && blockIdx.x == 0 && threadIdx.x < R) a.namax[threadIdx.x] = 0ull;
   __syncthreads();
-  {
+  if (R * 4 <= WARPS && K % 512 == 0 && R * (K + 16) <= WARPS * PW) {
+    // four warps per row split the chain, the chain warps of rows 0-3 on
+    // schedulers (0,1), (2,3), (0,1), (2,3); the squares go to the product
+    // buffers, unused until the contraction
+    __shared__ SplitSumShared split[WARPS / 4];
+    if (warp < 4 * R) {
+      const int r = warp >> 2, u = threadIdx.x - r * kSplitGroup, cw = 2 * (r & 1);
+      const float ss = seq_sumsq_split(fx + (size_t)r * K, gsm + (size_t)r * (K + 16), K, u, cw, r, split[r]);
+      if (u == 32 * cw) sinv[r] = rsqrt_body(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps));
+    }
+  } else {
     const int r = warp + WARPS * lane;
     if (r < R) sinv[r] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(fx + (size_t)r * K, K), (float)K), a.eps));
   }
@@ -2324,7 +2438,7 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
                                  int8_t* xq, float* xs) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ __align__(16) float sm[];           // [2][d]
+  extern __shared__ __align__(16) float sm[];           // [2][d] rows, [2][d + 16] squares
   __shared__ float s_inv[2];
   const int r = blockIdx.x;
   const int hr = hid_idx ? hid_idx[r] : r;
@@ -2350,8 +2464,17 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) s_inv[0] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, d), (float)d), eps));
-  if (threadIdx.x == 32) s_inv[1] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm + d, d), (float)d), eps));
+  if (blockDim.x == 2 * kSplitGroup && d % 512 == 0) {
+    // one 128-thread group per half (chain warps 0-1 and 6-7), squares
+    // into sm[2d..4d+32)
+    __shared__ SplitSumShared split[2];
+    const int g = threadIdx.x / kSplitGroup, u = threadIdx.x - g * kSplitGroup;
+    const float ss = seq_sumsq_split(sm + (size_t)g * d, sm + 2 * (size_t)d + (size_t)g * (d + 16), d, u, 2 * g, g, split[g]);
+    if (u == 64 * g) s_inv[g] = rsqrt_body(__fadd_rn(__fdiv_rn(ss, (float)d), eps));
+  } else {
+    if (threadIdx.x == 0) s_inv[0] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, d), (float)d), eps));
+    if (threadIdx.x == 32) s_inv[1] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm + d, d), (float)d), eps));
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int g = warp; g < 2 * d / 32; g += nw) {
