@@ -344,6 +344,12 @@ int lz_lm_head_static(const LZModel *m, const float *hidden, int n, float *logit
    *out_hit = the index or -1. */
 int lz_debug_seq_sum(const float *vals, int n, int mode, float target, float *out_value,
                      int *out_hit);
+/* Test hook: the split sequential sum of squares of the input norms
+   (src/ops_norm.c:718, the sum the RMSNorm scale divides) over nrows
+   (1-4) host rows of n floats (n a multiple of 512, at most 4096), one
+   128-thread group per row; out[r] = row r's sum, which must equal the
+   sequential float32 sum of the float32 squares bit for bit. */
+int lz_debug_sumsq_split(const float *rows, int nrows, int n, float *out);
 /* Test hook: lz_argmax_p1 (src/sampler.c:279-295) of n host values on the
    device - the arg-max and the online-softmax probability the greedy
    p_min compares. */

@@ -2593,6 +2593,30 @@ extern "C" int lz_debug_seq_sum(const float* vals, int n, int mode, float target
   return 0;
 }
 
+extern "C" int lz_debug_sumsq_split(const float* rows, int nrows, int n, float* out) {
+  if (!rows || !out) return LZ98_ERR_NULL_ARG;
+  if (nrows < 1 || nrows > 4 || n < 512 || n > 4096 || n % 512) return LZ98_ERR_SIZE;
+  const int smem = nrows * (2 * n + 16) * (int)sizeof(float);
+  if (cudaFuncSetAttribute(sumsq_split_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return LZ98_ERR_CUDA;
+  float* dv = nullptr;
+  float* dout = nullptr;
+  if (cudaMalloc(&dv, (size_t)nrows * n * 4) != cudaSuccess) return LZ98_ERR_ALLOC;
+  if (cudaMalloc(&dout, 16) != cudaSuccess) {
+    cudaFree(dv);
+    return LZ98_ERR_ALLOC;
+  }
+  int rc = 0;
+  if (cudaMemcpy(dv, rows, (size_t)nrows * n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  if (!rc) {
+    sumsq_split_probe_kernel<<<1, nrows * kSplitGroup, smem>>>(dv, nrows, n, dout);
+    if (cudaMemcpy(out, dout, (size_t)nrows * 4, cudaMemcpyDeviceToHost) != cudaSuccess) rc = LZ98_ERR_CUDA;
+  }
+  cudaFree(dv);
+  cudaFree(dout);
+  return rc;
+}
+
 extern "C" int lz_debug_wait_timeout(int* out_err, double* out_ms) {
   if (!out_err) return LZ98_ERR_NULL_ARG;
   int* h = nullptr;

@@ -149,6 +149,20 @@ LZ_HD float seq_sumsq_split(const float* x, float* sq, int K, int u, int cw, int
   return v;
 }
 
+// Test probe of seq_sumsq_split: one 128-thread group per row (up to 4
+// rows of n floats), the rows and their squares in dynamic shared memory.
+__global__ void sumsq_split_probe_kernel(const float* __restrict__ rows, int nrows, int n, float* out) {
+  extern __shared__ __align__(16) float psm[];
+  __shared__ SplitSumShared sh[4];
+  float* x = psm;
+  float* sq = psm + (size_t)nrows * n;
+  for (int i = threadIdx.x; i < nrows * n; i += blockDim.x) x[i] = rows[i];
+  __syncthreads();
+  const int r = threadIdx.x / kSplitGroup, u = threadIdx.x - r * kSplitGroup, cw = 2 * (r & 1);
+  const float v = seq_sumsq_split(x + (size_t)r * n, sq + (size_t)r * (n + 16), n, u, cw, r, sh[r]);
+  if (u == 32 * cw) out[r] = v;
+}
+
 // Sequential sum (index order) of a 16-byte aligned array, any n.
 LZ_HD float seq_sum(const float* v, int n) {
   float s = 0.0f;
@@ -581,13 +595,17 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
   }
   __syncthreads();
   const bool store = a.nout && blockIdx.x == 0;
-  // one 32-group per warp step (with the group max on redux.sync this
-  // measured faster than four interleaved groups)
-  for (int g = warp; g < R * gpr; g += WARPS) {
-    const int r = g / gpr, i = (g - r * gpr) * 32 + lane;
-    const float v = __fmul_rn(__fmul_rn(fx[(size_t)r * K + i], sinv[r]), __fadd_rn(1.0f, fw[i]));
-    sxq[(size_t)r * K + i] = warp_quant32(v, &sxs[g]);
-    if (store) a.nout[(size_t)r * K + i] = v;
+  // one 32-group per warp step, row by row (no index division); a row's
+  // groups of one warp are independent, so two of them overlap
+  for (int r = 0; r < R; r++) {
+    const float sr = sinv[r];
+#pragma unroll 2
+    for (int gg = warp; gg < gpr; gg += WARPS) {
+      const int i = gg * 32 + lane;
+      const float v = __fmul_rn(__fmul_rn(fx[(size_t)r * K + i], sr), __fadd_rn(1.0f, fw[i]));
+      sxq[(size_t)r * K + i] = warp_quant32(v, &sxs[r * gpr + gg]);
+      if (store) a.nout[(size_t)r * K + i] = v;
+    }
   }
   __syncthreads();
   unsigned long long kb = 0ull;

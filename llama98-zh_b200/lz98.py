@@ -83,6 +83,7 @@ def lib():
                                    ctypes.c_uint64, c_float, c_int, c_void_p, c_int, P(c_int), c_void_p, c_int,
                                    P(c_int), c_char_p, c_int]),
         "lz_debug_argmax_p1": (c_int, [c_void_p, c_int, P(c_int), P(c_float)]),
+        "lz_debug_sumsq_split": (c_int, [c_void_p, c_int, c_int, c_void_p]),
         "lz_read_weights": (c_int, [c_void_p, c_char_p, c_int]),
         "lz_profile_experts": (c_int, [c_void_p, P(ctypes.c_double), P(ctypes.c_double), P(c_int)]),
         "lz_debug_wait_timeout": (c_int, [P(c_int), P(ctypes.c_double)]),
@@ -124,7 +125,7 @@ def lib():
     return L
 
 
-EXPORTS = ["lz_profile_experts", "lz_debug_wait_timeout", "lz_debug_inject_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
+EXPORTS = ["lz_profile_experts", "lz_debug_sumsq_split", "lz_debug_wait_timeout", "lz_debug_inject_wait_timeout", "lz_generate_ex", "lz_debug_argmax_p1", "lz_read_weights", "lz_set_debug_timing", "lz_open", "lz_free", "lz_model_info", "lz_model_weight_bytes", "lz_state_alloc",
            "lz_state_alloc_batch", "lz_state_reset", "lz_state_free", "lz_state_get", "lz_state_set",
            "lz_state_get_chain", "lz_state_set_chain", "lz_forward", "lz_forward_capture",
            "lz_forward_batch_capture", "lz_forward_verify", "lz_state_mtp_logits",
@@ -508,6 +509,18 @@ def debug_seq_sum(vals, mode=0, target=0.0):
     if rc:
         raise LzError(f"debug_seq_sum failed ({rc})")
     return out.value, hit.value
+
+
+def debug_sumsq_split(rows):
+    """The input norms' split sum of squares over 1-4 host rows: float32 [nrows]."""
+    v = np.ascontiguousarray(rows, np.float32)
+    if v.ndim == 1:
+        v = v[None]
+    out = np.zeros(v.shape[0], np.float32)
+    rc = lib().lz_debug_sumsq_split(_ptr(v), v.shape[0], v.shape[1], _ptr(out))
+    if rc:
+        raise LzError(f"lz_debug_sumsq_split failed ({rc})")
+    return out
 
 
 def spec_accept(draft, targ, bonus):

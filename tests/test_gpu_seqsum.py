@@ -88,3 +88,55 @@ def test_bounded_wait_reports_and_context_survives():
     v, hit = lz98.debug_seq_sum(np.ones(100, np.float32))
     assert v == 100.0
 
+
+
+def _seq_sumsq(row):
+    s = np.float32(0)
+    with np.errstate(over="ignore"):
+        for x in row:
+            s = np.float32(s + np.float32(x * x))
+    return s
+
+
+def sumsq_rows(rng, n):
+    """Rows for the input norms' split sum of squares: ordinary activations,
+    rows whose sequential sum drifts far from the tree estimate (a few huge
+    entries early, then values the accumulator absorbs), zeros, subnormal
+    squares, squares that overflow, and constant rows."""
+    yield "normal", rng.standard_normal(n).astype(np.float32)
+    yield "scaled", (rng.standard_normal(n) * np.exp(rng.standard_normal(n) * 2)).astype(np.float32)
+    r = (rng.standard_normal(n) * 0.05).astype(np.float32)
+    r[rng.integers(0, 64, 3)] = rng.standard_normal(3).astype(np.float32) * 300
+    yield "early outliers", r
+    r = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+    r[0] = 4096.0
+    yield "absorbed tail", r
+    r = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+    r[n // 2] = 4096.0
+    yield "mid jump", r
+    r = rng.standard_normal(n).astype(np.float32)
+    r[rng.random(n) < 0.7] = 0
+    yield "sparse", r
+    yield "zeros", np.zeros(n, np.float32)
+    yield "subnormal squares", (rng.standard_normal(n) * 1e-22).astype(np.float32)
+    r = rng.standard_normal(n).astype(np.float32)
+    r[n - 5] = 3e19
+    yield "overflow", r
+    yield "constant", np.full(n, 0.1, np.float32)
+
+
+def test_sumsq_split_bit_exact():
+    """The segment-split sum of squares of the input norms equals the
+    sequential float32 sum (src/ops_norm.c:718) bit for bit, including rows
+    where no candidate start matches and a segment is chained again."""
+    import lz98
+    rng = np.random.default_rng(7)
+    for n in (512, 1024, 2048, 4096):
+        rows = list(sumsq_rows(rng, n))
+        want = [_seq_sumsq(v) for _, v in rows]
+        for nr in (1, 3, 4):
+            for i in range(0, len(rows), nr):
+                got = lz98.debug_sumsq_split(np.stack([v for _, v in rows[i:i + nr]]))
+                for j, g in enumerate(got):
+                    name = rows[i + j][0]
+                    assert np.float32(g).view(np.uint32) == want[i + j].view(np.uint32), (n, nr, name, g, want[i + j])
