@@ -1198,6 +1198,8 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
   __syncthreads();
   const float inv = s_inv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // a warp's groups are independent: four in flight
+#pragma unroll 4
   for (int g = warp; g < n / 32; g += nw) {
     const int i = g * 32 + lane;
     const float o = __fmul_rn(__fmul_rn(sm[i], inv), __fadd_rn(1.0f, sm[n + i]));
@@ -1226,10 +1228,25 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ src, int lds, int 
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const float* row = src + (size_t)r * lds;
-  for (int g = warp; g < n / 32; g += nw) {
-    const int i = g * 32 + lane;
-    const float a = __fmul_rn(silu(row[g0 + i]), row[u0 + i]);
-    xq[(size_t)r * n + i] = warp_quant32(a, &xs[(size_t)r * (n / 32) + g]);
+  // four of a warp's groups at a time, their loads issued together
+  constexpr int U = 4;
+  const int ng = n / 32;
+  for (int gb = warp; gb < ng; gb += U * nw) {
+    float gv[U], uv[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = (gb + u * nw) * 32 + lane;
+      gv[u] = gb + u * nw < ng ? row[g0 + i] : 0.0f;
+      uv[u] = gb + u * nw < ng ? row[u0 + i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int g = gb + u * nw;
+      if (g < ng) {
+        const float a = __fmul_rn(silu(gv[u]), uv[u]);
+        xq[(size_t)r * n + g * 32 + lane] = warp_quant32(a, &xs[(size_t)r * ng + g]);
+      }
+    }
   }
 }
 
@@ -2495,6 +2512,8 @@ __global__ void mtp_front_kernel(const int8_t* __restrict__ eq, const float* __r
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // a warp's groups are independent: four in flight
+#pragma unroll 4
   for (int g = warp; g < 2 * d / 32; g += nw) {
     const int i = g * 32 + lane;
     const int half = i >= d;
