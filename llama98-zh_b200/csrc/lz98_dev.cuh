@@ -94,6 +94,15 @@ LZ_HD uint32_t abs_bits(float x) { return __float_as_uint(x) & 0x7FFFFFFFu; }
 // (~22 cycles here, against ~130 for five shuffle steps).
 LZ_HD uint32_t warp_max_u32(uint32_t v) { return __reduce_max_sync(0xffffffffu, v); }
 
+// Max of a 64-bit value over the 32 lanes (every lane gets it): the max of
+// the high words, then of the low words among the lanes holding that high
+// word - two redux.sync instead of five two-word shuffle steps.
+LZ_HD unsigned long long warp_max_u64(unsigned long long v) {
+  const uint32_t hi = (uint32_t)(v >> 32), mh = __reduce_max_sync(0xffffffffu, hi);
+  const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? (uint32_t)v : 0u);
+  return ((unsigned long long)mh << 32) | ml;
+}
+
 // One 32-element activation group held one element per lane: the
 // reference quantiser (src/ops_quant.c:2152-2282). Returns the code; the
 // group scale is written by lane 0 when `scale_out` is non-null.

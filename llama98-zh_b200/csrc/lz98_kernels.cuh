@@ -616,12 +616,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_q8_kernel(const GemvArgs a) {
     __shared__ unsigned long long wbest[WARPS][kGemvRB];
     const int li = lane / R, lrr = lane - li * R;
     for (int rr = 0; rr < R; rr++) {
-      unsigned long long v = (lane < NR * R && lrr == rr) ? kb : 0ull;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
-        v = w > v ? w : v;
-      }
+      const unsigned long long v = warp_max_u64((lane < NR * R && lrr == rr) ? kb : 0ull);
       if (lane == 0) wbest[warp][rr] = v;
     }
     __syncthreads();
@@ -1271,10 +1266,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int V, int p1_mo
     const unsigned long long key = ((unsigned long long)fkey(v) << 32) | (0xFFFFFFFFu - (uint32_t)i);
     best = key > best ? key : best;
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
-    best = b2 > best ? b2 : best;
-  }
+  best = warp_max_u64(best);
   if ((threadIdx.x & 31) == 0) atomicMax(slot + r, best);
 }
 
@@ -1659,14 +1651,23 @@ LZ_HD void kda_layer(const KdaArgs& a) {
       }
       cluster_barrier();
     }
-    // gated RMSNorm of every token's head output, then per-32 quantisation
+    // gated RMSNorm of every token's head output, then per-32 quantisation;
+    // each thread's first output's norm weight and gate are formed while
+    // the sums of squares run
+    float pw = 0.0f, pz = 0.0f;
+    if (tid < nt * VC) {
+      const int t = tid / VC, c = tid - t * VC;
+      pw = a.o_norm[vcol0 + c];
+      pz = silu(zs[t][c]);
+    }
     if (lane == 0 && warp < nt)
       inv_o[warp] = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(OUT[warp], VD), (float)VD), a.eps));
     __syncthreads();
     for (int q = tid; q < nt * VC; q += NTH) {
       const int t = q / VC, c = q - t * VC, i = vcol0 + c;
       const size_t r = (size_t)(sq.row0 + t0 + t);
-      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), a.o_norm[i]), silu(zs[t][c]));
+      const float w = q == tid ? pw : a.o_norm[i], z = q == tid ? pz : silu(zs[t][c]);
+      const float o = __fmul_rn(__fmul_rn(__fmul_rn(OUT[t][i], inv_o[t]), w), z);
       a.oq[r * a.vdim + h * VD + i] = warp_quant32(o, &a.os[r * (a.vdim / 32) + (h * VD) / 32 + (i >> 5)]);
     }
     __syncthreads();
@@ -1732,10 +1733,7 @@ LZ_HD void route_row(const float* __restrict__ logits, const float* __restrict__
         best = kk > best ? kk : best;
       }
     }
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
-      best = b2 > best ? b2 : best;
-    }
+    best = warp_max_u64(best);
     const int bi = best ? argmax_index(best) : -1;
     float sw = 0.0f;
     if (bi >= 0 && (bi & 31) == lane) {

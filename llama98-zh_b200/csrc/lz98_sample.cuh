@@ -603,10 +603,7 @@ __device__ int block_argmax(const float* v, int n, SampShared& sh) {
     best = k > best ? k : best;
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long w = __shfl_xor_sync(0xffffffffu, best, o);
-    best = w > best ? w : best;
-  }
+  best = warp_max_u64(best);
   __shared__ unsigned long long red[kSampWarps];
   __syncthreads();
   if (lane == 0) red[warp] = best;
