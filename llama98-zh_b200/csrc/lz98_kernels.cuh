@@ -1493,7 +1493,11 @@ LZ_HD void kda_layer(const KdaArgs& a) {
     }
     // the conv1d of the batch (src/ops_conv1d.c:26-60), then SiLU
     if (tid < 3 * KD) {
-      for (int t = 0; t < nt; t++) {
+      // unrolled over the batch: the tokens' convolutions read only the raw
+      // inputs and the shifted history, so their SiLUs overlap
+#pragma unroll
+      for (int t = 0; t < TB; t++) {
+        if (t >= nt) break;
         const float xv = xr[t];
         float sum = 0.0f;
         sum = __fadd_rn(sum, __fmul_rn(cwv.x, c0));
