@@ -1293,7 +1293,8 @@ void gemv(LZRunState* s, const QW& w, int8_t* xq, float* xs, int R, float* y, in
 
 void rmsnorm_quant(LZRunState* s, const float* x, int ldx, const float* w, int n, int R, float* out,
                    int ldo, int8_t* xq, float* xs, unsigned long long* amax_clear) {
-  launch(s, rmsnorm_quant_kernel, dim3(R), dim3(256), 2 * n * sizeof(float), x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs,
+  // the row, its weights, and the squares of the split sum of squares
+  launch(s, rmsnorm_quant_kernel, dim3(R), dim3(256), (3 * n + 16) * sizeof(float), x, ldx, w, n, s->m->c.eps, out, ldo, xq, xs,
                                                                  amax_clear);
 }
 

@@ -67,7 +67,8 @@ LZ_HD float seq_sumsq(const float* v, int n) {
 //   the two chain warps (0 or 2); r: the group (0-3), which names its
 //   barriers.  Returns the sum in lane 0 of warp cw (0 elsewhere).
 constexpr int kSplitGroup = 128;
-struct SplitSumShared {
+// 16-byte aligned: the chain lanes store their two ends as one float2
+struct __align__(16) SplitSumShared {
   float part[4];
   float end[128];
 };
@@ -1189,7 +1190,16 @@ __global__ void rmsnorm_quant_kernel(const float* __restrict__ x, int ldx,
   }
   if (amax_clear && threadIdx.x == 0) amax_clear[r] = 0ull;
   __syncthreads();
-  if (threadIdx.x == 0) s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, n), (float)n), eps));
+  if (n % 512 == 0 && blockDim.x >= kSplitGroup) {
+    // the first four warps split the chain, squares into sm[2n..3n+16)
+    __shared__ SplitSumShared split;
+    if (threadIdx.x < kSplitGroup) {
+      const float ss = seq_sumsq_split(sm, sm + 2 * (size_t)n, n, threadIdx.x, 0, 0, split);
+      if (threadIdx.x == 0) s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+    }
+  } else if (threadIdx.x == 0) {
+    s_inv = rsqrt_body(__fadd_rn(__fdiv_rn(seq_sumsq(sm, n), (float)n), eps));
+  }
   __syncthreads();
   const float inv = s_inv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
